@@ -1,0 +1,29 @@
+// Test infrastructure: the model restatements of the CPU oracle.
+#pragma once
+
+#include "engine.h"
+
+namespace ref {
+
+// crates/realesrgan-native/src/network.rs + lib.rs (see realesrgan.cpp).
+class RealEsrgan {
+ public:
+  static constexpr size_t SCALE = 4, FEATURES = 64, BODY = 32, STEPS = BODY + 2;
+  explicit RealEsrgan(const std::string& path);
+  static void check_size(size_t len, size_t width, size_t height);
+  // network.rs:80-112: whole image, `step` after each layer (false = cancel).
+  std::vector<float> run(const float* image, size_t width, size_t height,
+                         const std::function<bool()>& step) const;
+  // lib.rs:241-289 with identity load/store.
+  std::vector<float> run_tiled(const float* image, size_t width, size_t height, size_t tile,
+                               size_t margin, const std::function<bool(float)>& progress) const;
+
+ private:
+  struct Layer {
+    Matrix conv;
+    std::vector<float> slope;
+  };
+  std::vector<Layer> layers_;
+};
+
+}  // namespace ref
