@@ -1,0 +1,352 @@
+#!/usr/bin/env python3
+"""Benchmark of the CUDA backend: output megapixels/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (BASELINE config 5a): a batch of 256 independent 3 x 256 x 384
+Real-ESRGAN inputs (seeded, uniform in [0, 1)), seeded random-init weights,
+split evenly across the N ranks (one process per GPU, no collective on the
+data path: the batch shards by image). One step = the whole batch once.
+value = 256 x 1.5729 output MP / step time (device time, max over ranks).
+
+Printed as one JSON line by rank 0:
+  value      inputs resident in HBM (302 MB in, 4.8 GB out: larger than L2),
+             CUDA events on the stream the kernels run on;
+  e2e        the same through the C ABI's host-buffer entry point from
+             page-locked memory, the H2D and D2H copies inside the timed region;
+  roofline   the dominant kernel (conv3x3 64->64, 32 of 34 layers): its
+             algorithmic FLOPs per launch over its mean launch time, both
+             measured by events around each launch during the timed steps;
+  cpu_baseline  the CPU oracle (a restatement of the reference's CPU f32
+             path) on the host's cores, rank 0 at N = 1, a bounded sample.
+`--impl reference` times that CPU path alone (rank 0; the others exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "image-engine-native_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+BATCH, WIDTH, HEIGHT = 256, 384, 256
+OUT_MP = WIDTH * HEIGHT * 16 / 1e6  # 1.572864 output MP per image
+# Algorithmic work of one 64 -> 64 3x3 convolution per pixel (2 FLOP / MAC).
+CONV64_FLOP_PER_PX = 2 * 9 * 64 * 64
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+def traffic_per_px():
+    """DRAM bytes per output pixel of the 64->64 conv from the committed ncu
+    summary (profiles/conv3x3_64x64_realesrgan.txt), or None."""
+    path = os.path.join(ROOT, "profiles", "conv3x3_64x64_realesrgan.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_pixel:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = max((num(r[2]) or 0) for r in rows)
+        power = [num(r[3]) or 0 for r in rows]
+        loaded = [s for s, p in zip(sm, power) if p > 0.4 * max(power)] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(power)}
+
+
+def cpu_sample(weights_path, seconds=12.0, cap=30.0):
+    """The CPU oracle on whole 3x256x384 images until `seconds` have passed."""
+    from iec import weights as W
+    from oracle import refcpu
+
+    model = refcpu.RealEsrgan(weights_path)
+    image = W.realesrgan_input(WIDTH, HEIGHT, 0)
+    model.run_float(image[:32, :32])  # warm-up of the threads
+    n, t0 = 0, time.perf_counter()
+    while True:
+        model.run_float(image)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or el + el / n > cap:
+            break
+    cores = refcpu.threads()
+    return {"value": n * OUT_MP / el, "unit": "MP/s", "cores": cores, "kind": "port",
+            "sample": f"{n} whole 3x256x384 images of the batch, {el:.1f} s, oracle/refcpu (restated reference CPU f32 path: Winograd F(4x4) + FMA products), {cores} threads"}
+
+
+def reference_arm(args, weights_path):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from iec import weights as W
+    from oracle import refcpu
+
+    model = refcpu.RealEsrgan(weights_path)
+    image = W.realesrgan_input(WIDTH, HEIGHT, 0)
+    for _ in range(args.warmup):
+        model.run_float(image)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.run_float(image)
+    el = time.perf_counter() - t0
+    value = args.steps * OUT_MP / el
+    cores = refcpu.threads()
+    line = {
+        "impl": "reference", "metric": "output megapixels/s", "value": value, "unit": "MP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config(args, 0),
+        "cpu_baseline": {"value": value, "unit": "MP/s", "cores": cores, "kind": "port",
+                         "sample": f"one 3x256x384 image of the batch per step, oracle/refcpu (the reference CPU f32 path restated; the Rust reference cannot be built here), {cores} threads"},
+        "e2e": {"value": value, "unit": "MP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config(args, chunk):
+    return {"workload": "realesrgan_x4v3 batch of 256 x 3x256x384 (BASELINE config 5a), split by image",
+            "model": "Real-ESRGAN general-x4v3 (SRVGGNetCompact, 34 conv3x3), seeded random-init weights",
+            "global_batch": BATCH, "image": f"{WIDTH}x{HEIGHT}", "images_per_launch": chunk,
+            "parallelism": f"dp{args.gpus} (by image, no collective)",
+            "l2": "inputs 302 MB and outputs 4.8 GB exceed the 126 MB L2; no flush"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--chunk", type=int, default=8, help="images per launch")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+
+    from iec import weights as W
+
+    wdir = tempfile.mkdtemp()
+    weights_path = os.path.join(wdir, "realesrgan.weights")
+    W.write_realesrgan(weights_path, 0)
+
+    if args.impl == "reference":
+        reference_arm(args, weights_path)
+        return
+
+    import numpy as np
+    import torch
+
+    import iec
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    assert BATCH % world == 0
+    count = BATCH // world
+
+    model = iec.RealEsrgan(weights_path, device=local, batch_chunk=args.chunk)
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    d_in = torch.rand((count, HEIGHT, WIDTH, 3), generator=gen, device="cuda", dtype=torch.float32)
+    d_out = torch.empty((count, HEIGHT * 4, WIDTH * 4, 3), device="cuda", dtype=torch.float32)
+    stream = torch.cuda.Stream()
+    sptr = stream.cuda_stream
+
+    def step():
+        model.run_device(d_in.data_ptr(), count, WIDTH, HEIGHT, d_out.data_ptr(), sptr)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches_per_step = model.launches(count, WIDTH, HEIGHT)
+    model.set_timing(args.steps * launches_per_step * 2 + 64)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks([local] if world == 1 else list(range(world))) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = max_over_ranks(start.elapsed_time(end) / 1e3)
+    kinds, ms = model.timing(args.steps * launches_per_step * 2 + 64)
+    model.set_timing(0)
+    conv_ms = float(ms[kinds == 2].mean()) if (kinds == 2).any() else None
+    step_s = elapsed / args.steps
+    value = BATCH * OUT_MP / step_s
+
+    # End to end through the host-buffer entry point, page-locked buffers.
+    h_in = torch.empty((count, HEIGHT, WIDTH, 3), dtype=torch.float32, pin_memory=True)
+    h_in.copy_(d_in)
+    h_out = torch.empty((count, HEIGHT * 4, WIDTH * 4, 3), dtype=torch.float32, pin_memory=True)
+    e2e_steps = max(2, args.steps // 2)
+    model.run_batch(h_in, h_out, sptr)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        model.run_batch(h_in, h_out, sptr)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3) / e2e_steps
+    # The host path gives the device path's numbers bit for bit.
+    same = bool(torch.equal(h_out[:2].cuda(), d_out[:2]))
+
+    # One image on one GPU, device-resident.
+    single = None
+    if rank == 0 and world == 1:
+        s_out = torch.empty((1, HEIGHT * 4, WIDTH * 4, 3), device="cuda", dtype=torch.float32)
+        for _ in range(3):
+            model.run_device(d_in.data_ptr(), 1, WIDTH, HEIGHT, s_out.data_ptr(), sptr)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(20):
+            model.run_device(d_in.data_ptr(), 1, WIDTH, HEIGHT, s_out.data_ptr(), sptr)
+        b.record(stream)
+        torch.cuda.synchronize()
+        t1 = a.elapsed_time(b) / 1e3 / 20
+        single = {"workload": "realesrgan_x4v3 one 3x256x384 image (BASELINE config 1)", "value": OUT_MP / t1,
+                  "unit": "MP/s", "ms": t1 * 1e3}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(weights_path)
+
+    if rank == 0:
+        pk, src = peaks()
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        px_per_launch = args.chunk * WIDTH * HEIGHT
+        achieved = CONV64_FLOP_PER_PX * px_per_launch / (conv_ms / 1e3) / 1e12 if conv_ms else None
+        tpp = traffic_per_px()
+        clocks = clk.summary()
+        line = {
+            "metric": "output megapixels/s", "value": value, "unit": "MP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
+            "data": "synthetic (seeded uniform images, seeded He-normal weights)",
+            "config": config(args, args.chunk),
+            "e2e": {"value": BATCH * OUT_MP / e2e_s, "unit": "MP/s",
+                    "h2d_bytes_per_step": BATCH * WIDTH * HEIGHT * 3 * 4,
+                    "d2h_bytes_per_step": BATCH * WIDTH * HEIGHT * 3 * 4 * 16,
+                    "api": "iec_realesrgan_run_batch (host buffers)", "matches_device_path": same},
+            "roofline": {"kernel": "conv3x3_sm100<64,64,PRELU>", "bound": "tensor", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if achieved else None,
+                         "peak_source": f"{src} bf16 dense (sustained; f16 rate is the same)",
+                         "mean_launch_ms": conv_ms, "flop_per_launch": CONV64_FLOP_PER_PX * px_per_launch,
+                         "traffic": tpp * px_per_launch if tpp else None,
+                         "algorithmic_bytes_per_launch": px_per_launch * 64 * 2 * 2},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_step * args.steps * world,
+            "clocks": clocks,
+            "per_model": {"realesrgan_single_image": single},
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

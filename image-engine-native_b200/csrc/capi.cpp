@@ -1,0 +1,191 @@
+// The C ABI of include/iec_cuda.h: argument checks with the reference's
+// messages, C++ exceptions turned into status codes, host <-> device copies
+// of the host-buffer entry points.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <string>
+
+#include "../../include/iec_cuda.h"
+#include "realesrgan.h"
+
+using namespace iec;
+
+namespace {
+
+thread_local std::string g_error;
+
+template <class F>
+iec_status guard(F&& f) {
+  try {
+    f();
+    g_error.clear();
+    return IEC_OK;
+  } catch (const Error& e) {
+    g_error = e.what();
+    return (iec_status)e.code;
+  } catch (const std::bad_alloc&) {
+    g_error = "out of host memory";
+    return IEC_ERR_GPU;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return IEC_ERR_INPUT;
+  }
+}
+
+Options to_options(const iec_options* o) {
+  Options opt;
+  if (o) {
+    opt.device = o->device;
+    opt.timeout_ms = o->timeout_ms;
+    opt.batch_chunk = o->batch_chunk;
+  }
+  return opt;
+}
+
+// crates/realesrgan-native/src/lib.rs:302-316 (check_size): a nonempty image
+// whose 16x larger output still has a size.
+void check_realesrgan_size(size_t width, size_t height) {
+  if (width == 0 || height == 0)
+    throw Error(ERR_INPUT, "empty " + std::to_string(width) + " x " + std::to_string(height) + " image");
+  const size_t max = std::numeric_limits<size_t>::max();
+  if (width > max / height || width * height > max / (3 * 16) || width > (size_t)INT32_MAX / 4 ||
+      height > (size_t)INT32_MAX / 4)
+    throw Error(ERR_INPUT, "a " + std::to_string(width) + " x " + std::to_string(height) + " image is too large");
+}
+
+void need(const void* p, const char* what) {
+  if (!p) throw Error(ERR_INPUT, std::string(what) + " is null");
+}
+
+}  // namespace
+
+struct iec_realesrgan {
+  std::unique_ptr<RealEsrgan> model;
+};
+
+extern "C" {
+
+const char* iec_last_error(void) { return g_error.c_str(); }
+
+int iec_device_count(void) { return device_count(); }
+
+iec_status iec_realesrgan_load(const char* weights_path, const iec_options* options, iec_realesrgan** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    need(weights_path, "weights_path");
+    auto h = std::make_unique<iec_realesrgan>();
+    h->model = std::make_unique<RealEsrgan>(weights_path, to_options(options));
+    *out = h.release();
+  });
+}
+
+void iec_realesrgan_free(iec_realesrgan* model) { delete model; }
+
+const char* iec_realesrgan_device_name(const iec_realesrgan* model) {
+  return model ? model->model->device().name().c_str() : "";
+}
+
+static iec_status run_host(iec_realesrgan* model, const void* image, bool u8, size_t width, size_t height,
+                           size_t tile, size_t margin, void* out, iec_progress_fn progress, void* user) {
+  return guard([&] {
+    need(model, "model");
+    need(image, "image");
+    need(out, "out");
+    check_realesrgan_size(width, height);
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    const size_t elem = u8 ? 1 : 4;
+    const size_t in_bytes = width * height * 3 * elem, out_bytes = in_bytes * 16;
+    m.host_in.reserve(in_bytes);
+    m.host_out.reserve(out_bytes);
+    cudaStream_t s = m.device().stream();
+    IEC_CUDA(cudaMemcpyAsync(m.host_in.get(), image, in_bytes, cudaMemcpyHostToDevice, s));
+    std::function<bool(float)> cb;
+    if (progress) cb = [progress, user](float f) { return progress(f, user) == 0; };
+    m.run_tiled_device(m.host_in.get(), u8, m.host_out.get(), u8, 1, width, height, tile, margin, cb, s);
+    IEC_CUDA(cudaMemcpyAsync(out, m.host_out.get(), out_bytes, cudaMemcpyDeviceToHost, s));
+    m.device().sync(s);
+  });
+}
+
+iec_status iec_realesrgan_run_float(iec_realesrgan* model, const float* image, size_t width, size_t height,
+                                    float* out) {
+  return run_host(model, image, false, width, height, RealEsrgan::GPU_TILE, RealEsrgan::MARGIN, out, nullptr,
+                  nullptr);
+}
+
+iec_status iec_realesrgan_run_float_tiled(iec_realesrgan* model, const float* image, size_t width, size_t height,
+                                          size_t tile, size_t margin, float* out, iec_progress_fn progress,
+                                          void* user) {
+  if (tile == 0) {
+    g_error = "input: tile size 0";
+    return IEC_ERR_INPUT;
+  }
+  return run_host(model, image, false, width, height, tile, margin, out, progress, user);
+}
+
+iec_status iec_realesrgan_run(iec_realesrgan* model, const uint8_t* rgb, size_t width, size_t height,
+                              uint8_t* out, iec_progress_fn progress, void* user) {
+  return run_host(model, rgb, true, width, height, RealEsrgan::GPU_TILE, RealEsrgan::MARGIN, out, progress, user);
+}
+
+iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, size_t count, size_t width,
+                                    size_t height, float* out, void* stream) {
+  return guard([&] {
+    need(model, "model");
+    need(images, "images");
+    need(out, "out");
+    if (count == 0) return;
+    check_realesrgan_size(width, height);
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run_batch_host(images, out, count, width, height, s);
+  });
+}
+
+iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images, size_t count, size_t width,
+                                     size_t height, float* out, void* stream) {
+  return guard([&] {
+    need(model, "model");
+    need(images, "images");
+    need(out, "out");
+    if (count == 0) return;
+    check_realesrgan_size(width, height);
+    if (reinterpret_cast<uintptr_t>(out) % 16 != 0) throw Error(ERR_INPUT, "out must be 16-byte aligned");
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run_device(images, out, count, width, height, s);
+  });
+}
+
+size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width, size_t height) {
+  return model ? model->model->launches(count, width, height) : 0;
+}
+
+iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity) {
+  return guard([&] {
+    need(model, "model");
+    DeviceScope scope(model->model->device());
+    model->model->set_timing(capacity);
+  });
+}
+
+size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n) {
+  size_t written = 0;
+  iec_status st = guard([&] {
+    need(model, "model");
+    need(kinds, "kinds");
+    need(ms, "ms");
+    DeviceScope scope(model->model->device());
+    written = model->model->timing(kinds, ms, n);
+  });
+  return st == IEC_OK ? written : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,372 @@
+// Real-ESRGAN general-x4v3 on the CUDA backend (see realesrgan.h).
+//
+// Network (crates/realesrgan-native/src/network.rs:22-140): conv3x3 3 -> 64
+// + PReLU, 32 x [conv3x3 64 -> 64 + PReLU], conv3x3 64 -> 48, pixel shuffle
+// x4, plus the input repeated. Tiling (lib.rs:241-289): equal grid tiles,
+// each run with `margin` pixels of context, only its own output kept.
+#include "realesrgan.h"
+
+#include <algorithm>
+#include <cstring>
+
+#include "conv3x3_sm100.cuh"
+
+namespace iec {
+
+// The network's input, a region of the source image (f32 or 8-bit, whose
+// value v means v / 255 as lib.rs:293-295 to_float), as the first layer's
+// f16 channel-group planes: group 0 holds R, G, B and five zeros, group 1
+// zeros (the first convolution runs with 16 input channels).
+__global__ void realesrgan_prep(const void* __restrict__ src, int src_u8, int src_w, int src_h, int rx0, int ry0,
+                                int rw, int rh, int mw, int mh, int count, __half* __restrict__ dst) {
+  const size_t total = (size_t)count * rw * rh;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t per = (size_t)rw * rh;
+    const int img = (int)(i / per);
+    const int rem = (int)(i - (size_t)img * per);
+    const int y = rem / rw, x = rem - y * rw;
+    const size_t spix = ((size_t)img * src_h + ry0 + y) * src_w + rx0 + x;
+    float c[3];
+    if (src_u8) {
+      const uint8_t* s = static_cast<const uint8_t*>(src) + spix * 3;
+      for (int k = 0; k < 3; k++) c[k] = (float)s[k] / 255.0f;
+    } else {
+      const float* s = static_cast<const float*>(src) + spix * 3;
+      for (int k = 0; k < 3; k++) c[k] = s[k];
+    }
+    __half2 rg = __floats2half2_rn(c[0], c[1]);
+    __half2 b0 = __floats2half2_rn(c[2], 0.0f);
+    const size_t plane = (size_t)mw * mh;
+    uint4* g0 = reinterpret_cast<uint4*>(dst + ((size_t)img * 2 * plane + (size_t)y * mw + x) * 8);
+    *g0 = make_uint4(*reinterpret_cast<uint32_t*>(&rg), *reinterpret_cast<uint32_t*>(&b0), 0u, 0u);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(g0) + plane * 8) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+namespace {
+
+template <int CIN, int COUT, int MODE>
+void launch_conv(Device& dev, const void* in_maps, int count, int mw, int mh, ConvParams p, cudaStream_t s) {
+  using L = ConvSmem<CIN, COUT>;
+  constexpr int KCH = CIN / 8;
+  CUtensorMap map;
+  const uint64_t dims[5] = {8, (uint64_t)mw, (uint64_t)mh, (uint64_t)KCH, (uint64_t)count};
+  const uint64_t plane = (uint64_t)mw * mh * 16;
+  const uint64_t strides[4] = {16, (uint64_t)mw * 16, plane, plane * KCH};
+  const uint32_t box[5] = {8, CONV_HALO_W, CONV_HALO_H, (uint32_t)KCH, 1};
+  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, in_maps, dims, strides, box);
+  auto kernel = conv3x3_sm100<CIN, COUT, MODE>;
+  // Every variant takes the whole opt-in shared memory: one CTA per SM (so
+  // the TMEM columns never run short) and room past every operand it reads.
+  static int smem_bytes[64] = {};
+  int& bytes = smem_bytes[dev.ordinal() & 63];
+  if (bytes == 0) {
+    int optin = 0;
+    IEC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev.ordinal()));
+    if (optin < L::DYN_BYTES) throw Error(ERR_GPU, "not enough shared memory per block");
+    IEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+    bytes = optin;
+  }
+  const int grid = std::min(p.tiles, dev.sms());
+  kernel<<<grid, CONV_THREADS, bytes, s>>>(map, p);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+RealEsrgan::RealEsrgan(const std::string& path, const Options& opt) : dev_(opt) {
+  WeightFile file = WeightFile::read(path, "REALESRG");
+  DeviceScope scope(dev_);
+  // network.rs:54-74: body.{2i}.weight [9 cin, cout], body.{2i}.bias, and
+  // the PReLU slopes body.{2i+1}.weight of every layer but the last.
+  for (int i = 0; i < STEPS; i++) {
+    const int cin = i == 0 ? 3 : FEATURES;
+    const bool last = i == STEPS - 1;
+    const int cout = last ? 3 * SCALE * SCALE : FEATURES;
+    const std::string name = "body." + std::to_string(2 * i);
+    HostTensor w = file.take_tensor(name + ".weight", {(size_t)(9 * cin), (size_t)cout});
+    std::vector<float> b = file.take(name + ".bias", {(size_t)cout});
+    std::vector<float> slope;
+    if (!last) slope = file.take("body." + std::to_string(2 * i + 1) + ".weight", {(size_t)FEATURES});
+    Layer layer;
+    layer.cin = i == 0 ? 16 : FEATURES;
+    layer.cout = cout;
+    // The K-major core-matrix image of B: [tap][cin / 8][cout][8] halves.
+    const int kch = layer.cin / 8;
+    std::vector<uint16_t> packed((size_t)9 * kch * cout * 8, 0);
+    for (int tap = 0; tap < 9; tap++)
+      for (int c = 0; c < cin; c++)
+        for (int o = 0; o < cout; o++)
+          packed[(((size_t)tap * kch + c / 8) * cout + o) * 8 + c % 8] =
+              f32_to_half(w.values[((size_t)tap * cin + c) * cout + o]);
+    layer.w.reserve(packed.size() * 2);
+    IEC_CUDA(cudaMemcpy(layer.w.get(), packed.data(), packed.size() * 2, cudaMemcpyHostToDevice));
+    layer.b.reserve(cout * 4);
+    IEC_CUDA(cudaMemcpy(layer.b.get(), b.data(), cout * 4, cudaMemcpyHostToDevice));
+    if (!last) {
+      layer.s.reserve(FEATURES * 4);
+      IEC_CUDA(cudaMemcpy(layer.s.get(), slope.data(), FEATURES * 4, cudaMemcpyHostToDevice));
+    }
+    layers_.push_back(std::move(layer));
+  }
+  file.finish();
+  layer_events_.resize(STEPS);
+  for (auto& e : layer_events_) IEC_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  IEC_CUDA(cudaStreamCreateWithFlags(&h2d_, cudaStreamNonBlocking));
+  IEC_CUDA(cudaStreamCreateWithFlags(&d2h_, cudaStreamNonBlocking));
+  for (int i = 0; i < 2; i++) {
+    IEC_CUDA(cudaEventCreateWithFlags(&ev_h2d_[i], cudaEventDisableTiming));
+    IEC_CUDA(cudaEventCreateWithFlags(&ev_done_[i], cudaEventDisableTiming));
+    IEC_CUDA(cudaEventCreateWithFlags(&ev_d2h_[i], cudaEventDisableTiming));
+  }
+  IEC_CUDA(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming));
+  IEC_CUDA(cudaDeviceSynchronize());
+}
+
+RealEsrgan::~RealEsrgan() {
+  if (dev_.poisoned()) {
+    // A device that failed a wait may still be running this model's work:
+    // its memory is leaked rather than freed under it.
+    for (auto& L : layers_) {
+      L.w.leak();
+      L.b.leak();
+      L.s.leak();
+    }
+    for (DeviceBuffer* b : {&prep_, &map_a_, &map_b_, &host_in, &host_out, &batch_in_[0], &batch_in_[1],
+                            &batch_out_[0], &batch_out_[1]})
+      b->leak();
+    return;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(dev_.ordinal());
+  for (auto& e : layer_events_) cudaEventDestroy(e);
+  for (auto& e : t_events_) cudaEventDestroy(e);
+  for (int i = 0; i < 2; i++) {
+    cudaEventDestroy(ev_h2d_[i]);
+    cudaEventDestroy(ev_done_[i]);
+    cudaEventDestroy(ev_d2h_[i]);
+  }
+  if (ev_start_) cudaEventDestroy(ev_start_);
+  if (h2d_) cudaStreamDestroy(h2d_);
+  if (d2h_) cudaStreamDestroy(d2h_);
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+void RealEsrgan::ensure_maps(size_t count, int w, int h, cudaStream_t stream) {
+  // A region narrower or shorter than the TMA box is kept in zero-filled
+  // maps of the box's size, so the box never outgrows the tensor.
+  const int mw = std::max(w, CONV_HALO_W), mh = std::max(h, CONV_HALO_H);
+  const size_t pixels = count * (size_t)mw * mh;
+  prep_.reserve(pixels * 2 * 16);
+  map_a_.reserve(pixels * 8 * 16);
+  map_b_.reserve(pixels * 8 * 16);
+  if (mw != w || mh != h) {
+    IEC_CUDA(cudaMemsetAsync(prep_.get(), 0, pixels * 2 * 16, stream));
+    IEC_CUDA(cudaMemsetAsync(map_a_.get(), 0, pixels * 8 * 16, stream));
+    IEC_CUDA(cudaMemsetAsync(map_b_.get(), 0, pixels * 8 * 16, stream));
+  }
+}
+
+void RealEsrgan::set_timing(size_t capacity) {
+  for (auto& e : t_events_) cudaEventDestroy(e);
+  t_events_.clear();
+  t_kinds_.clear();
+  t_used_ = 0;
+  for (size_t i = 0; i < capacity; i++) {
+    cudaEvent_t e;
+    IEC_CUDA(cudaEventCreate(&e));
+    t_events_.push_back(e);
+  }
+  t_kinds_.resize(capacity);
+}
+
+void RealEsrgan::mark(int kind, cudaStream_t s) {
+  if (t_used_ >= t_events_.size()) return;
+  IEC_CUDA(cudaEventRecord(t_events_[t_used_], s));
+  t_kinds_[t_used_++] = kind;
+}
+
+size_t RealEsrgan::timing(int* kinds, float* ms, size_t n) {
+  size_t w = 0;
+  for (size_t i = 0; i + 1 < t_used_ && w < n; i++) {
+    if (t_kinds_[i] < 0) continue;
+    dev_.wait_event(t_events_[i + 1]);
+    float t = 0;
+    IEC_CUDA(cudaEventElapsedTime(&t, t_events_[i], t_events_[i + 1]));
+    kinds[w] = t_kinds_[i];
+    ms[w] = t;
+    w++;
+  }
+  t_used_ = 0;
+  return w;
+}
+
+bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u8, int count, int src_w, int src_h,
+                             const Region& r, const std::function<bool()>& step, cudaStream_t s) {
+  ensure_maps(count, r.rw, r.rh, s);
+  const int mw = std::max(r.rw, CONV_HALO_W), mh = std::max(r.rh, CONV_HALO_H);
+  mark(0, s);
+  {
+    const size_t total = (size_t)count * r.rw * r.rh;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)dev_.sms() * 16);
+    realesrgan_prep<<<blocks, 256, 0, s>>>(src, src_u8, src_w, src_h, r.rx0, r.ry0, r.rw, r.rh, mw, mh, count,
+                                           prep_.as<__half>());
+    IEC_CUDA(cudaGetLastError());
+  }
+  ConvParams p{};
+  p.H = r.rh;
+  p.W = r.rw;
+  p.MW = mw;
+  p.MH = mh;
+  p.tiles_x = (r.rw + CONV_TILE_W - 1) / CONV_TILE_W;
+  p.tiles_y = (r.rh + CONV_TILE_H - 1) / CONV_TILE_H;
+  p.tiles = p.tiles_x * p.tiles_y * count;
+  p.dev_err = dev_.dev_err();
+  const void* in = prep_.get();
+  bool cancelled = false;
+  for (int i = 0; i < STEPS; i++) {
+    const Layer& L = layers_[i];
+    p.weights = L.w.as<uint16_t>();
+    p.bias = L.b.as<float>();
+    p.slope = L.s.get() ? L.s.as<float>() : nullptr;
+    __half* out = (i % 2 == 0 ? map_a_ : map_b_).as<__half>();
+    p.out = out;
+    mark(i == 0 ? 1 : i < STEPS - 1 ? 2 : 3, s);
+    if (i == 0) {
+      launch_conv<16, 64, CONV_PRELU>(dev_, in, count, mw, mh, p, s);
+    } else if (i < STEPS - 1) {
+      launch_conv<64, 64, CONV_PRELU>(dev_, in, count, mw, mh, p, s);
+    } else {
+      ShuffleOut& so = p.shuffle;
+      so.src = src;
+      so.dst = dst;
+      so.src_w = src_w;
+      so.src_h = src_h;
+      so.rx0 = r.rx0;
+      so.ry0 = r.ry0;
+      so.kx0 = r.kx0;
+      so.ky0 = r.ky0;
+      so.kx1 = r.kx1;
+      so.ky1 = r.ky1;
+      so.src_u8 = src_u8;
+      so.dst_u8 = dst_u8;
+      launch_conv<64, 48, CONV_SHUFFLE>(dev_, in, count, mw, mh, p, s);
+      mark(-1, s);
+    }
+    in = out;
+    if (step) {
+      // Two slots, as the reference's Steps (native-vulkan lib.rs:521-572):
+      // layer i is queued before layer i - 1 is waited for and reported, so
+      // the progress reports cost the GPU no idle time.
+      IEC_CUDA(cudaEventRecord(layer_events_[i], s));
+      if (i >= 1) {
+        dev_.wait_event(layer_events_[i - 1]);
+        if (!step()) {
+          cancelled = true;
+          break;
+        }
+      }
+    }
+  }
+  if (step && !cancelled) {
+    dev_.wait_event(layer_events_[STEPS - 1]);
+    if (!step()) cancelled = true;
+  }
+  if (cancelled) dev_.sync(s);  // nothing may still use the buffers
+  return !cancelled;
+}
+
+void RealEsrgan::run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_u8, size_t count, size_t width,
+                                  size_t height, size_t tile, size_t margin,
+                                  const std::function<bool(float)>& progress, cudaStream_t s) {
+  if (tile == 0) throw Error(ERR_INPUT, "tile size 0");
+  const size_t cols = (width + tile - 1) / tile, rows = (height + tile - 1) / tile;
+  const float steps = (float)(cols * rows * STEPS);
+  size_t done = 0;
+  std::function<bool()> step;
+  if (progress) step = [&] { return progress((float)(++done) / steps); };
+  for (size_t j = 0; j < rows; j++) {
+    const size_t y0 = j * height / rows, y1 = (j + 1) * height / rows;
+    for (size_t i = 0; i < cols; i++) {
+      const size_t x0 = i * width / cols, x1 = (i + 1) * width / cols;
+      const size_t rx0 = x0 > margin ? x0 - margin : 0, ry0 = y0 > margin ? y0 - margin : 0;
+      const size_t rx1 = margin > width - x1 ? width : x1 + margin;
+      const size_t ry1 = margin > height - y1 ? height : y1 + margin;
+      Region r;
+      r.rx0 = (int)rx0;
+      r.ry0 = (int)ry0;
+      r.rw = (int)(rx1 - rx0);
+      r.rh = (int)(ry1 - ry0);
+      r.kx0 = (int)(x0 - rx0);
+      r.ky0 = (int)(y0 - ry0);
+      r.kx1 = (int)(x1 - rx0);
+      r.ky1 = (int)(y1 - ry0);
+      if (!run_network(src, src_u8, dst, dst_u8, (int)count, (int)width, (int)height, r, step, s))
+        throw Error(CANCELLED, "cancelled");
+    }
+  }
+}
+
+size_t RealEsrgan::chunk_for(size_t width, size_t height) const {
+  if (dev_.batch_chunk() > 0) return (size_t)dev_.batch_chunk();
+  // About a million pixels per pass: the two 64-channel maps (256 MB) stay
+  // near the 126 MB L2 while each layer still fills the GPU many times over.
+  const size_t px = std::max<size_t>(1, width * height);
+  return std::max<size_t>(1, ((size_t)1 << 20) / px);
+}
+
+size_t RealEsrgan::launches(size_t count, size_t width, size_t height) const {
+  const size_t chunk = chunk_for(width, height);
+  return (count + chunk - 1) / chunk * (STEPS + 1);
+}
+
+void RealEsrgan::run_device(const float* src, float* dst, size_t count, size_t width, size_t height,
+                            cudaStream_t s) {
+  const size_t chunk = chunk_for(width, height);
+  Region r{0, 0, (int)width, (int)height, 0, 0, (int)width, (int)height};
+  for (size_t c0 = 0; c0 < count; c0 += chunk) {
+    const size_t n = std::min(chunk, count - c0);
+    run_network(src + c0 * width * height * 3, false, dst + c0 * width * height * 3 * SCALE * SCALE, false, (int)n,
+                (int)width, (int)height, r, nullptr, s);
+  }
+}
+
+void RealEsrgan::run_batch_host(const float* src, float* dst, size_t count, size_t width, size_t height,
+                                cudaStream_t s) {
+  // Three streams: H2D of chunk c + 1 and D2H of chunk c - 1 run while chunk
+  // c computes; two device buffers of each kind alternate.
+  const size_t chunk = chunk_for(width, height);
+  const size_t in_bytes = chunk * width * height * 3 * 4, out_bytes = in_bytes * SCALE * SCALE;
+  for (int b = 0; b < 2; b++) {
+    batch_in_[b].reserve(in_bytes);
+    batch_out_[b].reserve(out_bytes);
+  }
+  Region r{0, 0, (int)width, (int)height, 0, 0, (int)width, (int)height};
+  IEC_CUDA(cudaEventRecord(ev_start_, s));
+  IEC_CUDA(cudaStreamWaitEvent(h2d_, ev_start_, 0));
+  IEC_CUDA(cudaStreamWaitEvent(d2h_, ev_start_, 0));
+  size_t k = 0;
+  for (size_t c0 = 0; c0 < count; c0 += chunk, k++) {
+    const int b = (int)(k & 1);
+    const size_t n = std::min(chunk, count - c0);
+    const size_t ib = n * width * height * 3 * 4, ob = ib * SCALE * SCALE;
+    if (k >= 2) IEC_CUDA(cudaStreamWaitEvent(h2d_, ev_done_[b], 0));  // chunk k - 2 has read batch_in_[b]
+    IEC_CUDA(cudaMemcpyAsync(batch_in_[b].get(), src + c0 * width * height * 3, ib, cudaMemcpyHostToDevice, h2d_));
+    IEC_CUDA(cudaEventRecord(ev_h2d_[b], h2d_));
+    IEC_CUDA(cudaStreamWaitEvent(s, ev_h2d_[b], 0));
+    if (k >= 2) IEC_CUDA(cudaStreamWaitEvent(s, ev_d2h_[b], 0));  // chunk k - 2's output is copied out
+    run_network(batch_in_[b].get(), false, batch_out_[b].get(), false, (int)n, (int)width, (int)height, r, nullptr,
+                s);
+    IEC_CUDA(cudaEventRecord(ev_done_[b], s));
+    IEC_CUDA(cudaStreamWaitEvent(d2h_, ev_done_[b], 0));
+    IEC_CUDA(cudaMemcpyAsync(dst + c0 * width * height * 3 * SCALE * SCALE, batch_out_[b].get(), ob,
+                             cudaMemcpyDeviceToHost, d2h_));
+    IEC_CUDA(cudaEventRecord(ev_d2h_[b], d2h_));
+  }
+  // The caller's stream completes only once every output is in host memory.
+  for (int b = 0; b < 2 && (size_t)b < k; b++) IEC_CUDA(cudaStreamWaitEvent(s, ev_d2h_[b], 0));
+  dev_.sync(s);
+}
+
+}  // namespace iec

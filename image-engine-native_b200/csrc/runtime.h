@@ -1,0 +1,188 @@
+// Host runtime of the CUDA backend: errors, the device a model runs on, its
+// streams, device and page-locked buffers, bounded waits, TMA descriptors and
+// the weights-file reader.
+//
+// It takes the slot of the reference's Vulkan runtime
+// (crates/native-vulkan/src/lib.rs:122-1021: Gpu, Buffer, Steps): one device
+// per model, buffers grown on demand with the smaller ones freed first
+// (crates/realesrgan-native/src/gpu.rs:132-136), and a failed or timed-out
+// wait that poisons the device for every later call (lib.rs:443-480, usable).
+// Unlike the reference every wait here is bounded.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace iec {
+
+enum Status { OK = 0, ERR_IO = 1, ERR_WEIGHTS = 2, ERR_INPUT = 3, CANCELLED = 4, ERR_GPU = 5, ERR_TIMEOUT = 6 };
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define IEC_CUDA(call)                                                                      \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess)                                                                  \
+      throw ::iec::Error(::iec::ERR_GPU, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+uint16_t f32_to_half(float v);
+float half_to_f32(uint16_t h);
+
+// ------------------------------------------------------------- weights file
+// crates/native-engine/src/weight_file.rs:28-145: magic, u32 version 1, u32
+// count, then per tensor u16 name length, name, u8 type (0 f32 / 1 f16), u8
+// rank, u32 dims, values. Every length is checked against what is left of
+// the file before it is used; a tensor the model does not take is an error.
+struct HostTensor {
+  std::vector<size_t> shape;
+  bool half = false;
+  std::vector<float> values;  // halves widened exactly
+};
+
+class WeightFile {
+ public:
+  static WeightFile read(const std::string& path, const char magic[8]);
+  static WeightFile parse(const uint8_t* data, size_t len, const char magic[8]);
+  HostTensor take_tensor(const std::string& name, const std::vector<size_t>& shape);
+  std::vector<float> take(const std::string& name, const std::vector<size_t>& shape) {
+    return take_tensor(name, shape).values;
+  }
+  void finish() const;
+
+ private:
+  std::map<std::string, HostTensor> tensors_;
+};
+
+// ------------------------------------------------------------------ device
+struct Options {
+  int device = -1;
+  int timeout_ms = 0;
+  int batch_chunk = 0;
+};
+
+class DeviceBuffer {
+ public:
+  DeviceBuffer() = default;
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+  DeviceBuffer(DeviceBuffer&& o) noexcept : ptr_(o.ptr_), bytes_(o.bytes_) {
+    o.ptr_ = nullptr;
+    o.bytes_ = 0;
+  }
+  DeviceBuffer& operator=(DeviceBuffer&& o) noexcept {
+    if (this != &o) {
+      release();
+      ptr_ = o.ptr_;
+      bytes_ = o.bytes_;
+      o.ptr_ = nullptr;
+      o.bytes_ = 0;
+    }
+    return *this;
+  }
+  // Forget the memory without freeing it (a poisoned device may still use it).
+  void leak() {
+    ptr_ = nullptr;
+    bytes_ = 0;
+  }
+  ~DeviceBuffer() { release(); }
+  // Grow to at least `bytes` (contents not kept); frees the old one first.
+  void reserve(size_t bytes);
+  void release();
+  void* get() const { return ptr_; }
+  size_t size() const { return bytes_; }
+  template <class T>
+  T* as() const { return static_cast<T*>(ptr_); }
+
+ private:
+  void* ptr_ = nullptr;
+  size_t bytes_ = 0;
+};
+
+class PinnedBuffer {
+ public:
+  PinnedBuffer() = default;
+  PinnedBuffer(const PinnedBuffer&) = delete;
+  PinnedBuffer& operator=(const PinnedBuffer&) = delete;
+  ~PinnedBuffer() { release(); }
+  void reserve(size_t bytes);
+  void release();
+  void* get() const { return ptr_; }
+  template <class T>
+  T* as() const { return static_cast<T*>(ptr_); }
+
+ private:
+  void* ptr_ = nullptr;
+  size_t bytes_ = 0;
+};
+
+class Device {
+ public:
+  explicit Device(const Options& opt);
+  ~Device();
+  Device(const Device&) = delete;
+  Device& operator=(const Device&) = delete;
+
+  int ordinal() const { return ordinal_; }
+  const std::string& name() const { return name_; }
+  int sms() const { return sms_; }
+  cudaStream_t stream() const { return stream_; }
+  cudaStream_t copy_stream() const { return copy_stream_; }
+  int* dev_err() const { return dev_err_.as<int>(); }
+  int timeout_ms() const { return timeout_ms_; }
+  int batch_chunk() const { return batch_chunk_; }
+
+  // Make this device current on the calling thread; throws if poisoned.
+  void enter();
+  // Wait for `stream` to drain, polling at most timeout_ms; a timeout or a
+  // CUDA error poisons the device. Then checks the kernels' error word.
+  void sync(cudaStream_t stream);
+  // Wait (bounded) for one recorded event.
+  void wait_event(cudaEvent_t ev);
+  // Throw (and poison) on a sticky CUDA error or a nonzero kernel error word
+  // as last copied back by sync().
+  void check_device_errors();
+  void poison(const std::string& why) { poisoned_ = why.empty() ? "GPU failure" : why; }
+  bool poisoned() const { return !poisoned_.empty(); }
+
+ private:
+  int ordinal_ = 0;
+  std::string name_;
+  int sms_ = 0;
+  int timeout_ms_ = 120000;
+  int batch_chunk_ = 0;
+  cudaStream_t stream_ = nullptr;
+  cudaStream_t copy_stream_ = nullptr;
+  DeviceBuffer dev_err_;
+  PinnedBuffer host_err_;
+  std::string poisoned_;
+};
+
+// RAII: make the device current for a call and restore the caller's.
+class DeviceScope {
+ public:
+  explicit DeviceScope(Device& d);
+  ~DeviceScope();
+
+ private:
+  int prev_ = -1;
+};
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (so the
+// library does not link libcuda and still loads on a machine without it).
+void encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base,
+                       const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box);
+
+int device_count();
+
+}  // namespace iec

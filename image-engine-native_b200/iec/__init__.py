@@ -1,0 +1,187 @@
+"""Python mirror of the reference models' public API over the CUDA backend.
+
+The C ABI (include/iec_cuda.h, implemented by libiec_cuda.so next to this
+file) is the product's boundary; this module is a thin ctypes binding with
+the reference's method names and error kinds (crates/<model>-native/src/
+lib.rs, crates/native-engine/src/lib.rs:62-85), used by the tests and the
+benchmark. There is no CPU fallback: without the library or a B200 every
+call fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libiec_cuda.so")
+
+OK, ERR_IO, ERR_WEIGHTS, ERR_INPUT, CANCELLED, ERR_GPU, ERR_TIMEOUT = range(7)
+_KIND = {ERR_IO: "io", ERR_WEIGHTS: "weights", ERR_INPUT: "input", CANCELLED: "cancelled",
+         ERR_GPU: "gpu", ERR_TIMEOUT: "timeout"}
+
+PROGRESS = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_float, ctypes.c_void_p)
+
+
+class IecError(RuntimeError):
+    """A failed call: `code` is the iec_status, `kind` its Error variant."""
+
+    def __init__(self, code: int, message: str):
+        self.code = code
+        self.kind = _KIND.get(code, "unknown")
+        super().__init__(f"{self.kind}: {message}")
+
+
+class Cancelled(IecError):
+    pass
+
+
+class Options(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("timeout_ms", ctypes.c_int), ("batch_chunk", ctypes.c_int)]
+
+
+_lib = None
+
+
+def lib():
+    """The backend library, loaded once; raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        sz, vp, f32p = ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        L.iec_last_error.restype = ctypes.c_char_p
+        L.iec_device_count.restype = ctypes.c_int
+        L.iec_realesrgan_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
+        L.iec_realesrgan_free.argtypes = [vp]
+        L.iec_realesrgan_device_name.argtypes = [vp]
+        L.iec_realesrgan_device_name.restype = ctypes.c_char_p
+        L.iec_realesrgan_run_float.argtypes = [vp, f32p, sz, sz, f32p]
+        L.iec_realesrgan_run_float_tiled.argtypes = [vp, f32p, sz, sz, sz, sz, f32p, PROGRESS, vp]
+        L.iec_realesrgan_run.argtypes = [vp, u8p, sz, sz, u8p, PROGRESS, vp]
+        L.iec_realesrgan_run_batch.argtypes = [vp, vp, sz, sz, sz, vp, vp]
+        L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
+        L.iec_realesrgan_launches.argtypes = [vp, sz, sz, sz]
+        L.iec_realesrgan_launches.restype = sz
+        L.iec_realesrgan_set_timing.argtypes = [vp, sz]
+        L.iec_realesrgan_timing.argtypes = [vp, ctypes.POINTER(ctypes.c_int), f32p, sz]
+        L.iec_realesrgan_timing.restype = sz
+        _lib = L
+    return _lib
+
+
+def _check(status: int):
+    if status != OK:
+        msg = lib().iec_last_error().decode(errors="replace")
+        raise (Cancelled if status == CANCELLED else IecError)(status, msg)
+
+
+def device_count() -> int:
+    return lib().iec_device_count()
+
+
+def _progress(progress):
+    """The reference's progress closure (returns ControlFlow::Break to stop)
+    as a C callback: `progress(done)` returning True stops the run."""
+    if progress is None:
+        return PROGRESS()
+    return PROGRESS(lambda done, _user: 1 if progress(done) else 0)
+
+
+def _f32(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+class RealEsrgan:
+    """crates/realesrgan-native/src/lib.rs Model, on the CUDA backend."""
+
+    SCALE = 4
+    GPU_TILE = 768
+    MARGIN = 34
+    STEPS = 34
+
+    def __init__(self, path, device: int = -1, timeout_ms: int = 0, batch_chunk: int = 0):
+        self._h = ctypes.c_void_p()
+        opt = Options(device, timeout_ms, batch_chunk)
+        _check(lib().iec_realesrgan_load(os.fsencode(path), ctypes.byref(opt), ctypes.byref(self._h)))
+
+    load = classmethod(lambda cls, path, **kw: cls(path, **kw))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().iec_realesrgan_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def gpu(self) -> str:
+        """Model::gpu: the device's name."""
+        return lib().iec_realesrgan_device_name(self._h).decode()
+
+    def run_float(self, image: np.ndarray) -> np.ndarray:
+        """Model::run_float: HxWx3 floats in 0..=1 to 4Hx4Wx3, unclamped."""
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, c = image.shape
+        assert c == 3
+        out = np.empty((4 * h, 4 * w, 3), np.float32)
+        _check(lib().iec_realesrgan_run_float(self._h, _f32(image), w, h, _f32(out)))
+        return out
+
+    def run_float_tiled(self, image: np.ndarray, tile: int, margin: int, progress=None) -> np.ndarray:
+        """Model::run_float_tiled; `progress(done)` returning True cancels."""
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, _ = image.shape
+        out = np.empty((4 * h, 4 * w, 3), np.float32)
+        cb = _progress(progress)
+        margin = min(margin, 2**64 - 1)
+        _check(lib().iec_realesrgan_run_float_tiled(self._h, _f32(image), w, h, tile, margin, _f32(out), cb, None))
+        return out
+
+    def run(self, rgb: np.ndarray, progress=None) -> np.ndarray:
+        """Model::run / run_with_progress: 8-bit RGB in and out."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        h, w, _ = rgb.shape
+        out = np.empty((4 * h, 4 * w, 3), np.uint8)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        _check(lib().iec_realesrgan_run(self._h, rgb.ctypes.data_as(u8p), w, h, out.ctypes.data_as(u8p),
+                                        _progress(progress), None))
+        return out
+
+    run_with_progress = run
+
+    def run_batch(self, images, out=None, stream: int = 0):
+        """Batched run_float on host arrays (N x H x W x 3). `images` and
+        `out` may be page-locked torch tensors or numpy arrays."""
+        n, h, w, _ = images.shape
+        if out is None:
+            out = np.empty((n, 4 * h, 4 * w, 3), np.float32)
+        _check(lib().iec_realesrgan_run_batch(self._h, _addr(images), n, w, h, _addr(out), stream or None))
+        return out
+
+    def run_device(self, images_ptr: int, count: int, width: int, height: int, out_ptr: int, stream: int = 0):
+        """Batched run_float on device pointers; queued on `stream`, no wait."""
+        _check(lib().iec_realesrgan_run_device(self._h, images_ptr, count, width, height, out_ptr, stream or None))
+
+    def launches(self, count: int, width: int, height: int) -> int:
+        return lib().iec_realesrgan_launches(self._h, count, width, height)
+
+    # Measurement hooks (see iec_cuda.h): kinds 0 prep, 1 conv 16->64,
+    # 2 conv 64->64, 3 conv 64->48 + pixel shuffle.
+    def set_timing(self, capacity: int):
+        _check(lib().iec_realesrgan_set_timing(self._h, capacity))
+
+    def timing(self, n: int):
+        kinds = (ctypes.c_int * n)()
+        ms = np.zeros(n, np.float32)
+        k = lib().iec_realesrgan_timing(self._h, kinds, _f32(ms), n)
+        return np.array(kinds[:k], np.int32), ms[:k]
+
+
+def _addr(a) -> int:
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data

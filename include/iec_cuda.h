@@ -1,0 +1,127 @@
+/*
+ * iec_cuda.h - C ABI of the B200 (sm_100a) CUDA backend for the image models
+ * of image-engine-native.
+ *
+ * Each entry point replaces one call of a reference model crate's public API
+ * (crates/<model>-native/src/lib.rs), with the same argument meaning and
+ * errors, so that a native-cuda backend crate binds it with plain `extern
+ * "C"` declarations. Images are NHWC (row by row, channels interleaved), as
+ * everywhere in the reference.
+ *
+ * Errors (crates/native-engine/src/lib.rs:62-85, Error): every call returns
+ * an iec_status; the message of the last failure on the calling thread is
+ * iec_last_error(). A GPU failure or a wait that timed out poisons the
+ * handle, as the reference's Vulkan backend refuses work after a failed
+ * wait (crates/native-vulkan/src/lib.rs:443-480, usable): every later call
+ * on it returns IEC_ERR_GPU. Handles are not thread-safe: one handle per
+ * host thread (the reference's Model takes &mut self).
+ */
+#ifndef IEC_CUDA_H
+#define IEC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum iec_status {
+  IEC_OK = 0,
+  IEC_ERR_IO = 1,       /* Error::Io: a file could not be read */
+  IEC_ERR_WEIGHTS = 2,  /* Error::Weights: the weights file is not this model's */
+  IEC_ERR_INPUT = 3,    /* Error::Input: bad sizes or arguments */
+  IEC_CANCELLED = 4,    /* Error::Cancelled: the progress callback asked to stop */
+  IEC_ERR_GPU = 5,      /* Error::Gpu: no usable GPU, or a CUDA failure */
+  IEC_ERR_TIMEOUT = 6   /* a bounded wait on the GPU ran out (also poisons) */
+} iec_status;
+
+/* Load options; a NULL pointer means all defaults. */
+typedef struct iec_options {
+  int device;       /* CUDA device ordinal; -1: $IEC_CUDA_DEVICE, else 0 */
+  int timeout_ms;   /* bound on every host wait; 0: $IEC_TIMEOUT_MS, else 120000 */
+  int batch_chunk;  /* images per launch in batched runs; 0: chosen by the backend */
+} iec_options;
+
+/* Called with the share of the work done (0..1] after each layer; a nonzero
+ * return stops the run with IEC_CANCELLED (the reference's progress closure
+ * returning ControlFlow::Break, crates/realesrgan-native/src/lib.rs:181-191). */
+typedef int (*iec_progress_fn)(float done, void* user);
+
+/* Message of the last failure on this thread ("" when none). */
+const char* iec_last_error(void);
+
+/* Number of CUDA devices the backend can use (0 without a GPU). */
+int iec_device_count(void);
+
+/* ------------------------------------------------------------------ Real-ESRGAN
+ * crates/realesrgan-native/src/lib.rs: realesr-general-x4v3 (SRVGGNetCompact),
+ * output 4x larger on each side. */
+typedef struct iec_realesrgan iec_realesrgan;
+
+/* Model::load (lib.rs:120-137) with IMAGE_ENGINE_NATIVE_GPU=1 semantics: a
+ * missing or unsuitable GPU is IEC_ERR_GPU, never a CPU fallback. Reads the
+ * "REALESRG" weights file export_weights.py writes (f32 or f16 matrices). */
+iec_status iec_realesrgan_load(const char* weights_path, const iec_options* options,
+                               iec_realesrgan** out);
+
+/* Drop a model (frees its device memory). NULL is ignored. */
+void iec_realesrgan_free(iec_realesrgan* model);
+
+/* Model::gpu (lib.rs:153-159): the device's name. */
+const char* iec_realesrgan_device_name(const iec_realesrgan* model);
+
+/* Model::run_float (lib.rs:197-219): width x height x 3 floats in 0..=1 to
+ * (4 width) x (4 height) x 3 floats, neither clamped nor rounded. Runs in
+ * tiles of 768 with a 34-pixel margin, which give the whole image's result
+ * bit for bit (each output pixel is computed the same way wherever its tile
+ * is). */
+iec_status iec_realesrgan_run_float(iec_realesrgan* model, const float* image, size_t width,
+                                    size_t height, float* out);
+
+/* Model::run_float_tiled (lib.rs:221-232): a grid of equal tiles at most
+ * `tile` input pixels on a side, each run with up to `margin` pixels of its
+ * surroundings (SIZE_MAX: unbounded). `progress` (may be NULL) is called 34
+ * times per tile. */
+iec_status iec_realesrgan_run_float_tiled(iec_realesrgan* model, const float* image, size_t width,
+                                          size_t height, size_t tile, size_t margin, float* out,
+                                          iec_progress_fn progress, void* user);
+
+/* Model::run / run_with_progress (lib.rs:161-191): 8-bit RGB in and out
+ * (v / 255 in, clamp(0, 1) * 255 rounded out), tiles of 768 with margin 34. */
+iec_status iec_realesrgan_run(iec_realesrgan* model, const uint8_t* rgb, size_t width,
+                              size_t height, uint8_t* out, iec_progress_fn progress, void* user);
+
+/* Batched Model::run_float over `count` images of one size, HOST buffers
+ * (count x height x width x 3 in, count x 4 height x 4 width x 3 out). The
+ * copies and kernels are queued on `stream` (a cudaStream_t; NULL: the
+ * model's own stream) and the call returns when the outputs are in `out`.
+ * Page-locked host buffers let the copies overlap the kernels. */
+iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, size_t count,
+                                    size_t width, size_t height, float* out, void* stream);
+
+/* As iec_realesrgan_run_batch on DEVICE pointers of the model's device; the
+ * work is queued on `stream` and the call returns without waiting for it. */
+iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images, size_t count,
+                                     size_t width, size_t height, float* out, void* stream);
+
+/* Kernel launches one run_device call of this size makes (for accounting). */
+size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width,
+                               size_t height);
+
+/* Measurement hooks (no counterpart in the reference, which has no GPU
+ * timestamps). iec_realesrgan_set_timing(model, capacity) makes every later
+ * run record a CUDA event before each kernel launch and after the last one,
+ * on the stream the kernel runs on, for up to `capacity` launches (0 turns
+ * it off). iec_realesrgan_timing then waits for those events, writes each
+ * launch's kind (0 input prep, 1 conv 16->64, 2 conv 64->64, 3 conv 64->48
+ * with the pixel-shuffle store) and duration in ms, returns how many it
+ * wrote (at most `n`) and starts a new record. */
+iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity);
+size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IEC_CUDA_H */
