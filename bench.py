@@ -183,9 +183,9 @@ def reference_arm(args, weights_path):
 
 
 def config(args, chunk):
-    return {"workload": "realesrgan_x4v3 batch of 256 x 3x256x384 (BASELINE config 5a), split by image",
+    return {"workload": f"realesrgan_x4v3 batch of {args.batch} x 3x256x384 (BASELINE config 5a), split by image",
             "model": "Real-ESRGAN general-x4v3 (SRVGGNetCompact, 34 conv3x3), seeded random-init weights",
-            "global_batch": BATCH, "image": f"{WIDTH}x{HEIGHT}", "images_per_launch": chunk,
+            "global_batch": args.batch, "image": f"{WIDTH}x{HEIGHT}", "images_per_launch": chunk,
             "parallelism": f"dp{args.gpus} (by image, no collective)",
             "l2": "inputs 302 MB and outputs 4.8 GB exceed the 126 MB L2; no flush"}
 
@@ -197,7 +197,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--chunk", type=int, default=8, help="images per launch")
-    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 
@@ -227,8 +230,9 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    assert BATCH % world == 0
-    count = BATCH // world
+    batch = args.batch
+    assert batch % world == 0
+    count = batch // world
 
     model = iec.RealEsrgan(weights_path, device=local, batch_chunk=args.chunk)
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
@@ -271,26 +275,32 @@ def main():
     model.set_timing(0)
     conv_ms = float(ms[kinds == 2].mean()) if (kinds == 2).any() else None
     step_s = elapsed / args.steps
-    value = BATCH * OUT_MP / step_s
+    value = batch * OUT_MP / step_s
 
-    # End to end through the host-buffer entry point, page-locked buffers.
-    h_in = torch.empty((count, HEIGHT, WIDTH, 3), dtype=torch.float32, pin_memory=True)
-    h_in.copy_(d_in)
-    h_out = torch.empty((count, HEIGHT * 4, WIDTH * 4, 3), dtype=torch.float32, pin_memory=True)
-    e2e_steps = max(2, args.steps // 2)
-    model.run_batch(h_in, h_out, sptr)
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
+    e2e = None
+    if not args.no_e2e:
+        # End to end through the host-buffer entry point, page-locked buffers.
+        h_in = torch.empty((count, HEIGHT, WIDTH, 3), dtype=torch.float32, pin_memory=True)
+        h_in.copy_(d_in)
+        h_out = torch.empty((count, HEIGHT * 4, WIDTH * 4, 3), dtype=torch.float32, pin_memory=True)
+        e2e_steps = max(2, args.steps // 2)
         model.run_batch(h_in, h_out, sptr)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3) / e2e_steps
-    # The host path gives the device path's numbers bit for bit.
-    same = bool(torch.equal(h_out[:2].cuda(), d_out[:2]))
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            model.run_batch(h_in, h_out, sptr)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3) / e2e_steps
+        # The host path gives the device path's numbers bit for bit.
+        same = bool(torch.equal(h_out[:2].cuda(), d_out[:2]))
+        e2e = {"value": batch * OUT_MP / e2e_s, "unit": "MP/s",
+               "h2d_bytes_per_step": batch * WIDTH * HEIGHT * 3 * 4,
+               "d2h_bytes_per_step": batch * WIDTH * HEIGHT * 3 * 4 * 16,
+               "api": "iec_realesrgan_run_batch (host buffers, page-locked)", "matches_device_path": same}
 
     # One image on one GPU, device-resident.
     single = None
@@ -326,10 +336,7 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
             "data": "synthetic (seeded uniform images, seeded He-normal weights)",
             "config": config(args, args.chunk),
-            "e2e": {"value": BATCH * OUT_MP / e2e_s, "unit": "MP/s",
-                    "h2d_bytes_per_step": BATCH * WIDTH * HEIGHT * 3 * 4,
-                    "d2h_bytes_per_step": BATCH * WIDTH * HEIGHT * 3 * 4 * 16,
-                    "api": "iec_realesrgan_run_batch (host buffers)", "matches_device_path": same},
+            "e2e": e2e,
             "roofline": {"kernel": "conv3x3_sm100<64,64,PRELU>", "bound": "tensor", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if achieved else None,
                          "peak_source": f"{src} bf16 dense (sustained; f16 rate is the same)",
