@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Workload (BASELINE config 5a): a batch of 256 independent 3 x 256 x 384
+Workload (the sharded-batch configuration): a batch of 256 independent 3 x 256 x 384
 Real-ESRGAN inputs (seeded, uniform in [0, 1)), seeded random-init weights,
 split evenly across the N ranks (one process per GPU, no collective on the
 data path: the batch shards by image). One step = the whole batch once.
@@ -183,7 +183,7 @@ def reference_arm(args, weights_path):
 
 
 def config(args, chunk):
-    return {"workload": f"realesrgan_x4v3 batch of {args.batch} x 3x256x384 (BASELINE config 5a), split by image",
+    return {"workload": f"realesrgan_x4v3 batch of {args.batch} x 3x256x384 (sharded batch), split by image",
             "model": "Real-ESRGAN general-x4v3 (SRVGGNetCompact, 34 conv3x3), seeded random-init weights",
             "global_batch": args.batch, "image": f"{WIDTH}x{HEIGHT}", "images_per_launch": chunk,
             "parallelism": f"dp{args.gpus} (by image, no collective)",
@@ -302,7 +302,7 @@ def main():
                "d2h_bytes_per_step": batch * WIDTH * HEIGHT * 3 * 4 * 16,
                "api": "iec_realesrgan_run_batch (host buffers, page-locked)", "matches_device_path": same}
 
-    # One image on one GPU, device-resident.
+    # One image (the single-image configuration) on one GPU, device-resident.
     single = None
     if rank == 0 and world == 1:
         s_out = torch.empty((1, HEIGHT * 4, WIDTH * 4, 3), device="cuda", dtype=torch.float32)
@@ -316,7 +316,7 @@ def main():
         b.record(stream)
         torch.cuda.synchronize()
         t1 = a.elapsed_time(b) / 1e3 / 20
-        single = {"workload": "realesrgan_x4v3 one 3x256x384 image (BASELINE config 1)", "value": OUT_MP / t1,
+        single = {"workload": "realesrgan_x4v3 one 3x256x384 image (single-image configuration)", "value": OUT_MP / t1,
                   "unit": "MP/s", "ms": t1 * 1e3}
 
     cpu = None

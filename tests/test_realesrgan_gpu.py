@@ -1,6 +1,6 @@
 """Real-ESRGAN on the CUDA backend against the CPU oracle (GPU tests).
 
-Tolerance (the north star's, for RGB outputs): max abs <= 2e-2 on raw
+Tolerance (the project's parity bar for RGB outputs): max abs <= 2e-2 on raw
 outputs and PSNR >= 45 dB on outputs clamped to [0, 1]. The behaviour tests
 follow crates/realesrgan-native/tests/gpu.rs:49-72 (tiles of 64 with MARGIN
 are bit for bit the whole image) and tests/reference.rs:85-152 (progress,
@@ -70,7 +70,7 @@ def test_matches_oracle(gpu_model, cpu_model, w, h, seed):
 
 
 def test_full_config_matches_oracle(gpu_model, cpu_model):
-    # 3 x 256 x 384.
+    # The single-image benchmark configuration: 3 x 256 x 384.
     image = W.realesrgan_input(384, 256, 0)
     err, p = within(gpu_model.run_float(image), cpu_model.run_float(image))
     print(f"384x256: max abs {err:.3g}, PSNR {p:.1f} dB")
