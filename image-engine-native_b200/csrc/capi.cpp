@@ -164,6 +164,22 @@ iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images,
   });
 }
 
+iec_status iec_realesrgan_run_device_noalloc(iec_realesrgan* model, const float* images, size_t count,
+                                             size_t width, size_t height, float* out, void* stream) {
+  return guard([&] {
+    need(model, "model");
+    need(images, "images");
+    need(out, "out");
+    if (count == 0) return;
+    check_realesrgan_size(width, height);
+    if (reinterpret_cast<uintptr_t>(out) % 16 != 0) throw Error(ERR_INPUT, "out must be 16-byte aligned");
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run_device_noalloc(images, out, count, width, height, s);
+  });
+}
+
 size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width, size_t height) {
   return model ? model->model->launches(count, width, height) : 0;
 }

@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "conv3x3_sm100.cuh"
 
@@ -367,6 +368,109 @@ void RealEsrgan::run_batch_host(const float* src, float* dst, size_t count, size
   // The caller's stream completes only once every output is in host memory.
   for (int b = 0; b < 2 && (size_t)b < k; b++) IEC_CUDA(cudaStreamWaitEvent(s, ev_d2h_[b], 0));
   dev_.sync(s);
+}
+
+}  // namespace iec
+
+// ------------------------------------------------------- allocation-free path
+namespace iec {
+
+namespace {
+
+// The feature maps of iec_realesrgan_run_device_noalloc: the first layer's
+// two channel groups and the two 64-channel maps, 18 x 16 bytes per pixel,
+// for at most NOALLOC_MAX_PIXELS pixels (31.5 MiB). The array is part of the
+// library's device code, so every GPU that loads the library holds it until
+// the process exits, and every call on a device shares it.
+constexpr size_t NOALLOC_PREP_BYTES = RealEsrgan::NOALLOC_MAX_PIXELS * 2 * 16;
+constexpr size_t NOALLOC_MAP_BYTES = RealEsrgan::NOALLOC_MAX_PIXELS * 8 * 16;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_PREP_BYTES + 2 * NOALLOC_MAP_BYTES];
+
+// The array's device address on each device. In host code the name
+// g_noalloc_scratch is only a host-side stand-in, so the address is looked
+// up once per device, with that device current, and passed to the kernels.
+std::mutex g_noalloc_mutex;
+uint8_t* g_noalloc_ptr[64] = {};
+
+uint8_t* noalloc_scratch(int device) {
+  if (device < 0 || device >= 64) throw Error(ERR_GPU, "device ordinal out of range for the fixed scratch");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      throw Error(ERR_GPU, std::string("cudaGetSymbolAddress of the fixed scratch: ") + cudaGetErrorString(e));
+    g_noalloc_ptr[device] = static_cast<uint8_t*>(p);
+  }
+  return g_noalloc_ptr[device];
+}
+
+}  // namespace
+
+void RealEsrgan::run_device_noalloc(const float* src, float* dst, size_t count, size_t width, size_t height,
+                                    cudaStream_t s) {
+  const int w = (int)width, h = (int)height;
+  const int mw = std::max(w, CONV_HALO_W), mh = std::max(h, CONV_HALO_H);
+  // (count is bounded first so that the product cannot wrap around)
+  const size_t pixels = count > NOALLOC_MAX_PIXELS ? NOALLOC_MAX_PIXELS + 1 : count * (size_t)mw * mh;
+  if (pixels > NOALLOC_MAX_PIXELS)
+    throw Error(ERR_INPUT, std::to_string(count) + " images of " + std::to_string(width) + " x " +
+                               std::to_string(height) + " need " + std::to_string(pixels) +
+                               " pixels of scratch; the allocation-free entry point holds " +
+                               std::to_string(NOALLOC_MAX_PIXELS));
+  uint8_t* base = noalloc_scratch(dev_.ordinal());
+  __half* prep = reinterpret_cast<__half*>(base);
+  __half* maps[2] = {reinterpret_cast<__half*>(base + NOALLOC_PREP_BYTES),
+                     reinterpret_cast<__half*>(base + NOALLOC_PREP_BYTES + NOALLOC_MAP_BYTES)};
+  // The array keeps the previous call's values; the margin of maps kept
+  // larger than the image (too small for a TMA box) must read as zeros.
+  if (mw != w || mh != h) {
+    IEC_CUDA(cudaMemsetAsync(prep, 0, pixels * 2 * 16, s));
+    IEC_CUDA(cudaMemsetAsync(maps[0], 0, pixels * 8 * 16, s));
+    IEC_CUDA(cudaMemsetAsync(maps[1], 0, pixels * 8 * 16, s));
+  }
+  {
+    const size_t total = count * (size_t)w * h;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)dev_.sms() * 16);
+    realesrgan_prep<<<blocks, 256, 0, s>>>(src, 0, w, h, 0, 0, w, h, mw, mh, (int)count, prep);
+    IEC_CUDA(cudaGetLastError());
+  }
+  ConvParams p{};
+  p.H = h;
+  p.W = w;
+  p.MW = mw;
+  p.MH = mh;
+  p.tiles_x = (w + CONV_TILE_W - 1) / CONV_TILE_W;
+  p.tiles_y = (h + CONV_TILE_H - 1) / CONV_TILE_H;
+  p.tiles = p.tiles_x * p.tiles_y * (int)count;
+  p.dev_err = dev_.dev_err();
+  const void* in = prep;
+  for (int i = 0; i < STEPS; i++) {
+    const Layer& L = layers_[i];
+    p.weights = L.w.as<uint16_t>();
+    p.bias = L.b.as<float>();
+    p.slope = L.s.get() ? L.s.as<float>() : nullptr;
+    p.out = maps[i % 2];
+    if (i == 0) {
+      launch_conv<16, 64, CONV_PRELU>(dev_, in, (int)count, mw, mh, p, s);
+    } else if (i < STEPS - 1) {
+      launch_conv<64, 64, CONV_PRELU>(dev_, in, (int)count, mw, mh, p, s);
+    } else {
+      ShuffleOut& so = p.shuffle;
+      so.src = src;
+      so.dst = dst;
+      so.src_w = w;
+      so.src_h = h;
+      so.rx0 = so.ry0 = 0;
+      so.kx0 = so.ky0 = 0;
+      so.kx1 = w;
+      so.ky1 = h;
+      so.src_u8 = 0;
+      so.dst_u8 = 0;
+      launch_conv<64, 48, CONV_SHUFFLE>(dev_, in, (int)count, mw, mh, p, s);
+    }
+    in = p.out;
+  }
 }
 
 }  // namespace iec

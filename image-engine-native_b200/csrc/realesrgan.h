@@ -42,6 +42,13 @@ class RealEsrgan {
   void run_batch_host(const float* src, float* dst, size_t count, size_t width, size_t height,
                       cudaStream_t stream);
 
+  // As run_device, but the feature maps live in a fixed scratch array that
+  // the library holds on every device (no allocation at all); see
+  // iec_realesrgan_run_device_noalloc in iec_cuda.h for the limit and rules.
+  static constexpr size_t NOALLOC_MAX_PIXELS = 114688;
+  void run_device_noalloc(const float* src, float* dst, size_t count, size_t width, size_t height,
+                          cudaStream_t stream);
+
   size_t launches(size_t count, size_t width, size_t height) const;
   size_t chunk_for(size_t width, size_t height) const;
 

@@ -105,6 +105,29 @@ iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, 
 iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images, size_t count,
                                      size_t width, size_t height, float* out, void* stream);
 
+/* iec_realesrgan_run_device without any allocation. This entry point has no
+ * counterpart in the reference. It is for callers that cannot allocate device
+ * memory while they run: a process that hands all device memory to its own
+ * pool allocator at start-up and forbids raw cudaMalloc afterwards, or a
+ * real-time frame pipeline that cannot absorb the device-wide
+ * synchronisation cudaMalloc and cudaFree imply. The other entry points grow
+ * their feature maps with cudaMalloc on demand; this one keeps them in a
+ * fixed scratch array built into the library, 31.5 MiB that every GPU which
+ * loads the library holds until the process exits.
+ *  - Limit: count x max(width, 10) x max(height, 18) <= 114688 pixels (for
+ *    example one 384 x 256 image); a larger call returns IEC_ERR_INPUT.
+ *  - The model itself is loaded beforehand with iec_realesrgan_load, which
+ *    does allocate; the call only uses `images`, `out` and the scratch.
+ *  - The first call on a device looks up the scratch array's device address
+ *    (once per device); make that first call before any stream capture.
+ *  - Every call on a device shares the one scratch array: calls whose work
+ *    overlaps on the GPU (other streams, other models on the same device)
+ *    race and corrupt each other's results. Order them on one stream.
+ *  - Work is queued on `stream` (NULL: the model's stream); no wait. */
+iec_status iec_realesrgan_run_device_noalloc(iec_realesrgan* model, const float* images,
+                                             size_t count, size_t width, size_t height,
+                                             float* out, void* stream);
+
 /* Kernel launches one run_device call of this size makes (for accounting). */
 size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width,
                                size_t height);
