@@ -7,25 +7,39 @@
 // network.rs:118-140 (pixel shuffle x4 plus the input repeated).
 //
 // Layout. Feature maps are f16 and "channel-group planar": [image][cin / 8]
-// [height][width][8]. One tile is 16 rows x 8 columns of output pixels (the
-// M = 128 rows of one UMMA). A single 5-D TMA box brings the tile's 18 x 10
-// pixel halo of every channel group into shared memory as [group][18][10][8],
-// which is exactly the no-swizzle K-major core-matrix layout tcgen05 reads:
-// 8 consecutive pixels of a halo row are one 8 x 16-byte core matrix, the
-// next tile row is 160 bytes on (SBO), the next channel group 2880 bytes on
-// (LBO). Each of the 9 taps is therefore just a start-address offset of
-// (ky * 10 + kx) * 16 bytes into the same halo: no im2col, one TMA load per
-// tile, out-of-image pixels zero-filled by TMA itself.
+// [height][width][8], so a row of one plane is contiguous. One tile is 8 rows
+// x 14 columns of output pixels. Its MMA rows (M = 128) are the 8 x 16
+// positions x0 - 1 .. x0 + 14 of those rows, and its MMA columns are the
+// three horizontal taps side by side (N = 3 * cout): row (r, c), column
+// kx * cout + o accumulates Q_kx(r, c)[o] = sum over ky and channels of
+// in(r + ky - 1, c - 1) * w[ky][kx][.][o]. Output pixel (r, c) (c = 1..14)
+// is then Q_0(r, c - 1) + Q_1(r, c) + Q_2(r, c + 1): its neighbours' partial
+// sums sit in the adjacent TMEM lanes, one warp shuffle away. Three MMAs of
+// N = 192 fetch as many shared-memory operand bytes as three of N = 64 but
+// do three times the math, which is what bounds this convolution (its
+// narrow N otherwise leaves the tensor core waiting on operand fetches).
 //
-// The weights of the layer, pre-arranged on the host as [tap][cin / 8][cout]
-// [8] (the K-major core-matrix image of B), stay in shared memory for the
-// whole persistent kernel (72 KB for 64 -> 64).
+// A single 4-D TMA box (inner row 16 pixels x 8 channels = 256 bytes) brings
+// the tile's 10 x 16 pixel halo of every channel group into shared memory as
+// [group][10][16][8]: the no-swizzle K-major core-matrix layout tcgen05
+// reads, 8 consecutive positions of a row per core matrix (SBO 128 bytes),
+// the next channel group 2560 bytes on (LBO). Tap row ky is a start offset
+// of ky * 256 bytes into the same halo; out-of-image pixels are TMA's zero
+// fill.
 //
-// Roles (192 threads): warp 0 one thread issues TMA loads into a ring of
-// NSTAGE halo stages; warp 1 one thread issues 9 * cin / 16 UMMAs
-// (M 128, N cout, K 16) per tile into one of two TMEM accumulators; warps
-// 2..5 (one per TMEM lane quarter) drain an accumulator while the next
-// tile's MMAs run, apply the epilogue and store.
+// The weights of the layer, pre-arranged on the host as [ky][cin / 8]
+// [kx][cout][8] (the K-major core-matrix image of B), stay in shared memory
+// for the whole persistent kernel (72 KB for 64 -> 64).
+//
+// Roles (576 threads): warp 0 one thread issues TMA loads into a ring of
+// NSTAGE halo stages; warp 1 one thread issues 3 * cin / 16 UMMAs
+// (M 128, N 3 cout, K 16) per tile into one of two TMEM accumulators; warps
+// 2..17 (four per TMEM lane quarter, each with a quarter of the channels, or
+// one output row of the pixel shuffle) drain an accumulator while the next
+// tile's MMAs run, combine the taps, apply the epilogue and store. Per tile
+// the epilogue issues several times the MMA warp's instructions and waits on
+// TMEM loads and shuffles, so it gets four warps per SM sub-partition to
+// hide those latencies.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -36,14 +50,16 @@
 
 namespace iec {
 
-constexpr int CONV_TILE_H = 16;
-constexpr int CONV_TILE_W = 8;
-constexpr int CONV_HALO_H = CONV_TILE_H + 2;
-constexpr int CONV_HALO_W = CONV_TILE_W + 2;
-constexpr int CONV_CHUNK_BYTES = CONV_HALO_H * CONV_HALO_W * 16;  // 2880
-constexpr int CONV_NSTAGE = 4;
-constexpr int CONV_THREADS = 192;
-constexpr int CONV_TMEM_COLS = 128;  // two accumulators of up to 64 columns
+constexpr int CONV_TILE_H = 8;                    // output rows of a tile
+constexpr int CONV_TILE_W = 14;                   // output columns of a tile
+constexpr int CONV_HALO_H = CONV_TILE_H + 2;      // 10
+constexpr int CONV_HALO_W = CONV_TILE_W + 2;      // 16: also the partial-sum positions of a row
+constexpr int CONV_CHUNK_BYTES = CONV_HALO_H * CONV_HALO_W * 16;  // 2560: one channel group
+constexpr int CONV_NSTAGE = 6;
+constexpr int CONV_EPI_WARPS = 16;                // four per TMEM lane quarter
+constexpr int CONV_THREADS = 64 + 32 * CONV_EPI_WARPS;
+constexpr int CONV_ACC_COLS = 256;                // TMEM columns between the two accumulators
+constexpr int CONV_TMEM_COLS = 2 * CONV_ACC_COLS;
 
 enum ConvMode { CONV_PRELU = 0, CONV_SHUFFLE = 1 };
 
@@ -62,11 +78,13 @@ struct ShuffleOut {
 struct ConvParams {
   int H, W;                    // valid size of the maps (the region)
   int MH, MW;                  // allocated size of the maps (>= H, W; the excess stays zero)
-  int tiles_x, tiles_y, tiles;  // tile grid over all images
-  const uint16_t* weights;     // [9][cin / 8][cout][8] f16
+  int tiles_x, tiles_y, tiles;  // tile grid over all images (tiles < 2^24, sides < 2^16)
+  FastDiv div_tiles_x, div_tiles_y;
+  int slope_unit;              // every PReLU slope is in [0, 1]: max(v, s v) is PReLU
+  const uint16_t* weights;     // [3 ky][cin / 8][3 kx][cout][8] f16
   const float* bias;           // [cout]
   const float* slope;          // [cout] PReLU slopes, or null
-  __half* out;                 // CONV_PRELU: [image][cout / 8][H][W][8]
+  __half* out;                 // CONV_PRELU: [image][cout / 8][MH][MW][8]
   ShuffleOut shuffle;          // CONV_SHUFFLE
   int* dev_err;
 };
@@ -117,7 +135,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], CONV_EPI_WARPS);
     }
     mbar_init(wbar, 1);
     *abort_flag = 0;
@@ -135,7 +153,6 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int tiles_per_img = p.tiles_x * p.tiles_y;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -152,11 +169,12 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       for (int i = 0; i < CONV_NSTAGE; i++) issued[i] = -1;
       for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
         if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) break;
-        const int img = tile / tiles_per_img;
-        const int rem = tile - img * tiles_per_img;
-        const int ty = rem / p.tiles_x, tx = rem - ty * p.tiles_x;
+        const int row_id = (int)p.div_tiles_x.div((uint32_t)tile);  // image * tiles_y + ty
+        const int tx = tile - row_id * p.tiles_x;
+        const int img = (int)p.div_tiles_y.div((uint32_t)row_id), ty = row_id - img * p.tiles_y;
         mbar_arrive_expect_tx(&full[s], KCH * CONV_CHUNK_BYTES);
-        tma_load_5d(a_smem + s * L::STAGE_BYTES, &in_map, &full[s], 0, tx * CONV_TILE_W - 1,
+        // x in elements of a plane row: (x0 - 1) * 8 halves, 16-byte aligned.
+        tma_load_4d(a_smem + s * L::STAGE_BYTES, &in_map, &full[s], (tx * CONV_TILE_W - 1) * 8,
                     ty * CONV_TILE_H - 1, 0, img);
         issued[s] = (int)phase;
         if (++s == CONV_NSTAGE) {
@@ -172,7 +190,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc = idesc_f16_f32(128, COUT);
+      constexpr int N = 3 * COUT;
+      constexpr uint32_t idesc = idesc_f16_f32(128, N);
       const uint32_t abase0 = smem_u32(a_smem), wbase = smem_u32(w_smem);
       int last_acc = -1;
       uint32_t last_parity = 0;
@@ -185,18 +204,18 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           if (!mbar_wait(&acc_empty[a], acc_phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_EMPTY)) break;
           if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) break;
           tc_fence_after();
-          const uint32_t d = tmem_base + (uint32_t)(a * 64);
+          const uint32_t d = tmem_base + (uint32_t)(a * CONV_ACC_COLS);
           const uint32_t abase = abase0 + (uint32_t)(s * L::STAGE_BYTES);
 #pragma unroll
-          for (int tap = 0; tap < 9; tap++) {
-            const uint32_t off = (uint32_t)(((tap / 3) * CONV_HALO_W + (tap % 3)) * 16);
+          for (int ky = 0; ky < 3; ky++) {
 #pragma unroll
             for (int ks = 0; ks < KCH / 2; ks++) {
-              const uint64_t adesc =
-                  smem_desc(abase + (uint32_t)(2 * ks * CONV_CHUNK_BYTES) + off, CONV_CHUNK_BYTES, CONV_HALO_W * 16);
-              const uint64_t bdesc =
-                  smem_desc(wbase + (uint32_t)((tap * KCH + 2 * ks) * COUT * 16), COUT * 16, 128);
-              umma_f16(d, adesc, bdesc, idesc, (tap | ks) != 0);
+              // A: positions (r, c) of the tile read halo pixel (r + ky, c);
+              // B: the three kx taps' weights of row ky, N = 3 cout.
+              const uint64_t adesc = smem_desc(abase + (uint32_t)(2 * ks * CONV_CHUNK_BYTES + ky * CONV_HALO_W * 16),
+                                               CONV_CHUNK_BYTES, 128);
+              const uint64_t bdesc = smem_desc(wbase + (uint32_t)((ky * KCH + 2 * ks) * N * 16), N * 16, 128);
+              umma_f16(d, adesc, bdesc, idesc, (ky | ks) != 0);
             }
           }
           umma_commit(&empty[s]);
@@ -215,46 +234,100 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   } else {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp & 3;            // TMEM lanes 32 q .. 32 q + 31
-    const int row = quarter * 32 + lane;     // M row = pixel of the tile
-    const int my = row >> 3, mx = row & 7;
+    const int part = (warp - 2) >> 2;        // which quarter of the channels (0..3)
+    const int row = quarter * 32 + lane;     // M row = partial-sum position (r, c) of the tile
+    const int pr = row >> 4, pc = row & 15;
+    // This warp's channels' bias and PReLU slope, kept in registers.
+    constexpr int NB = MODE == CONV_PRELU ? COUT / 4 : 12;
+    float r_bias[NB], r_slope[NB];
+#pragma unroll
+    for (int e = 0; e < NB; e++) {
+      const int k = MODE == CONV_PRELU ? part * NB + e : 16 * (e / 4) + 4 * part + (e % 4);
+      r_bias[e] = s_bias[k];
+      r_slope[e] = s_slope[k];
+    }
+    const bool slope_unit = p.slope_unit != 0;
     int i = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
       const int a = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
       if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
       tc_fence_after();
-      uint32_t v[COUT];
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * 64);
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * CONV_ACC_COLS);
+      // out(r, c) = Q_0(r, c - 1) + Q_1(r, c) + Q_2(r, c + 1): the left and
+      // right partial sums come from the neighbouring lanes (same tile row:
+      // a row is 16 lanes, a warp holds two whole rows).
+      constexpr int NV = MODE == CONV_PRELU ? COUT / 4 : 12;
+      float v[NV];
+      if constexpr (MODE == CONV_PRELU) {
+        // channels 16 part .. 16 part + 15
+        static_assert(COUT == 64, "four parts of 16 channels");
+        uint32_t q0[16], q1[16], q2[16];
+        const uint32_t col = (uint32_t)(part * 16);
+        tmem_ld16(taddr + col, q0);
+        tmem_ld16(taddr + (uint32_t)COUT + col, q1);
+        tmem_ld16(taddr + (uint32_t)(2 * COUT) + col, q2);
+        tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < COUT; c += 16) tmem_ld16(taddr + (uint32_t)c, v + c);
-      tmem_wait_ld();
+        for (int e = 0; e < 16; e++) {
+          const float left = __shfl_up_sync(0xffffffffu, __uint_as_float(q0[e]), 1);
+          const float right = __shfl_down_sync(0xffffffffu, __uint_as_float(q2[e]), 1);
+          v[e] = (left + __uint_as_float(q1[e])) + right;
+        }
+      } else {
+        // output row i = part of the pixel shuffle needs channels
+        // 16 c + 4 part .. + 3 of each colour c
+        static_assert(COUT == 48, "three colours of 16 channels");
+        uint32_t q0[12], q1[12], q2[12];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+          const uint32_t col = (uint32_t)(16 * c + 4 * part);
+          tmem_ld4(taddr + col, q0 + 4 * c);
+          tmem_ld4(taddr + (uint32_t)COUT + col, q1 + 4 * c);
+          tmem_ld4(taddr + (uint32_t)(2 * COUT) + col, q2 + 4 * c);
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 12; e++) {
+          const float left = __shfl_up_sync(0xffffffffu, __uint_as_float(q0[e]), 1);
+          const float right = __shfl_down_sync(0xffffffffu, __uint_as_float(q2[e]), 1);
+          v[e] = (left + __uint_as_float(q1[e])) + right;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
 
-      const int img = tile / tiles_per_img;
-      const int rem = tile - img * tiles_per_img;
-      const int ty = rem / p.tiles_x, tx = rem - ty * p.tiles_x;
-      const int y = ty * CONV_TILE_H + my, x = tx * CONV_TILE_W + mx;
-      if (y >= p.H || x >= p.W) continue;
+      const int row_id = (int)p.div_tiles_x.div((uint32_t)tile);
+      const int tx = tile - row_id * p.tiles_x;
+      const int img = (int)p.div_tiles_y.div((uint32_t)row_id), ty = row_id - img * p.tiles_y;
+      const int y = ty * CONV_TILE_H + pr, x = tx * CONV_TILE_W + pc - 1;
+      if (pc < 1 || pc > CONV_TILE_W || y >= p.H || x >= p.W) continue;
 
       if constexpr (MODE == CONV_PRELU) {
         const size_t plane = (size_t)p.MH * p.MW;
         __half* base = p.out + ((size_t)img * (COUT / 8) * plane + (size_t)y * p.MW + x) * 8;
 #pragma unroll
-        for (int g = 0; g < COUT / 8; g++) {
+        for (int g = 0; g < NV / 8; g++) {
+          const int c0 = part * NV + g * 8;  // first channel of the group
           uint32_t packed[4];
 #pragma unroll
           for (int e = 0; e < 4; e++) {
-            const int c = g * 8 + 2 * e;
-            float v0 = __uint_as_float(v[c]) + s_bias[c];
-            float v1 = __uint_as_float(v[c + 1]) + s_bias[c + 1];
-            v0 = v0 < 0.0f ? v0 * s_slope[c] : v0;
-            v1 = v1 < 0.0f ? v1 * s_slope[c + 1] : v1;
+            const int k = g * 8 + 2 * e;
+            float v0 = v[k] + r_bias[k];
+            float v1 = v[k + 1] + r_bias[k + 1];
+            if (slope_unit) {
+              v0 = fmaxf(v0, v0 * r_slope[k]);
+              v1 = fmaxf(v1, v1 * r_slope[k + 1]);
+            } else {
+              v0 = v0 < 0.0f ? v0 * r_slope[k] : v0;
+              v1 = v1 < 0.0f ? v1 * r_slope[k + 1] : v1;
+            }
             __half2 h = __floats2half2_rn(v0, v1);
             packed[e] = *reinterpret_cast<uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(base + (size_t)g * plane * 8) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint4*>(base + (size_t)(c0 / 8) * plane * 8) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
       } else {
         // Pixel shuffle x4 plus the input repeated (network.rs:118-140):
@@ -269,24 +342,18 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           in[c] = so.src_u8 ? (float)reinterpret_cast<const uint8_t*>(so.src)[spix * 3 + c] / 255.0f
                             : reinterpret_cast<const float*>(so.src)[spix * 3 + c];
         const size_t ow = (size_t)so.src_w * 4;
-#pragma unroll
-        for (int ii = 0; ii < 4; ii++) {
+        {
+          const int ii = part;
           float o[12];
 #pragma unroll
           for (int j = 0; j < 4; j++)
 #pragma unroll
-            for (int c = 0; c < 3; c++) {
-              const int k = 16 * c + 4 * ii + j;
-              o[j * 3 + c] = (__uint_as_float(v[k]) + s_bias[k]) + in[c];
-            }
+            for (int c = 0; c < 3; c++) o[j * 3 + c] = (v[4 * c + j] + r_bias[4 * c + j]) + in[c];
           const size_t opix = ((size_t)img * so.src_h * 4 + (size_t)gy * 4 + ii) * ow + (size_t)gx * 4;
           if (so.dst_u8) {
-            uint8_t b[12];
-#pragma unroll
-            for (int e = 0; e < 12; e++) b[e] = (uint8_t)roundf(fminf(fmaxf(o[e], 0.0f), 1.0f) * 255.0f);
             uint8_t* d = reinterpret_cast<uint8_t*>(so.dst) + opix * 3;
 #pragma unroll
-            for (int e = 0; e < 12; e++) d[e] = b[e];
+            for (int e = 0; e < 12; e++) d[e] = (uint8_t)roundf(fminf(fmaxf(o[e], 0.0f), 1.0f) * 255.0f);
           } else {
             float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(so.dst) + opix * 3);
             d[0] = make_float4(o[0], o[1], o[2], o[3]);

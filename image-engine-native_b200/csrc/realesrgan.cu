@@ -50,12 +50,15 @@ template <int CIN, int COUT, int MODE>
 void launch_conv(Device& dev, const void* in_maps, int count, int mw, int mh, ConvParams p, cudaStream_t s) {
   using L = ConvSmem<CIN, COUT>;
   constexpr int KCH = CIN / 8;
+  // The maps as 4-D tensors: a plane row of mw pixels x 8 channels (one
+  // contiguous run), rows, channel groups, images. A box is one tile's halo:
+  // 16 pixels of 10 rows of every channel group.
   CUtensorMap map;
-  const uint64_t dims[5] = {8, (uint64_t)mw, (uint64_t)mh, (uint64_t)KCH, (uint64_t)count};
+  const uint64_t dims[4] = {(uint64_t)mw * 8, (uint64_t)mh, (uint64_t)KCH, (uint64_t)count};
   const uint64_t plane = (uint64_t)mw * mh * 16;
-  const uint64_t strides[4] = {16, (uint64_t)mw * 16, plane, plane * KCH};
-  const uint32_t box[5] = {8, CONV_HALO_W, CONV_HALO_H, (uint32_t)KCH, 1};
-  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, in_maps, dims, strides, box);
+  const uint64_t strides[3] = {(uint64_t)mw * 16, plane, plane * KCH};
+  const uint32_t box[4] = {CONV_HALO_W * 8, CONV_HALO_H, (uint32_t)KCH, 1};
+  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, in_maps, dims, strides, box);
   auto kernel = conv3x3_sm100<CIN, COUT, MODE>;
   // Every variant takes the whole opt-in shared memory: one CTA per SM (so
   // the TMEM columns never run short) and room past every operand it reads.
@@ -92,18 +95,24 @@ RealEsrgan::RealEsrgan(const std::string& path, const Options& opt) : dev_(opt) 
     Layer layer;
     layer.cin = i == 0 ? 16 : FEATURES;
     layer.cout = cout;
-    // The K-major core-matrix image of B: [tap][cin / 8][cout][8] halves.
+    // The K-major core-matrix image of B: [ky][cin / 8][kx][cout][8] halves
+    // (a tap row's three taps side by side as the MMA's N = 3 cout).
     const int kch = layer.cin / 8;
     std::vector<uint16_t> packed((size_t)9 * kch * cout * 8, 0);
-    for (int tap = 0; tap < 9; tap++)
-      for (int c = 0; c < cin; c++)
-        for (int o = 0; o < cout; o++)
-          packed[(((size_t)tap * kch + c / 8) * cout + o) * 8 + c % 8] =
-              f32_to_half(w.values[((size_t)tap * cin + c) * cout + o]);
+    for (int ky = 0; ky < 3; ky++)
+      for (int kx = 0; kx < 3; kx++)
+        for (int c = 0; c < cin; c++)
+          for (int o = 0; o < cout; o++)
+            packed[((((size_t)ky * kch + c / 8) * 3 + kx) * cout + o) * 8 + c % 8] =
+                f32_to_half(w.values[((size_t)(ky * 3 + kx) * cin + c) * cout + o]);
     layer.w.reserve(packed.size() * 2);
     IEC_CUDA(cudaMemcpy(layer.w.get(), packed.data(), packed.size() * 2, cudaMemcpyHostToDevice));
     layer.b.reserve(cout * 4);
     IEC_CUDA(cudaMemcpy(layer.b.get(), b.data(), cout * 4, cudaMemcpyHostToDevice));
+    // Slopes in [0, 1] (0.25 at initialisation) let the epilogue take
+    // max(v, s v), which equals v < 0 ? s v : v for them.
+    layer.slope_unit = 1;
+    for (float v : slope) layer.slope_unit &= (v >= 0.0f && v <= 1.0f) ? 1 : 0;
     if (!last) {
       layer.s.reserve(FEATURES * 4);
       IEC_CUDA(cudaMemcpy(layer.s.get(), slope.data(), FEATURES * 4, cudaMemcpyHostToDevice));
@@ -223,6 +232,10 @@ bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u
   p.tiles_x = (r.rw + CONV_TILE_W - 1) / CONV_TILE_W;
   p.tiles_y = (r.rh + CONV_TILE_H - 1) / CONV_TILE_H;
   p.tiles = p.tiles_x * p.tiles_y * count;
+  if ((size_t)p.tiles_x * p.tiles_y * count >= (1u << 24) || p.tiles_x >= (1 << 16) || p.tiles_y >= (1 << 16))
+    throw Error(ERR_INPUT, "too many tiles for one pass");
+  p.div_tiles_x = FastDiv((uint32_t)p.tiles_x);
+  p.div_tiles_y = FastDiv((uint32_t)p.tiles_y);
   p.dev_err = dev_.dev_err();
   const void* in = prep_.get();
   bool cancelled = false;
@@ -231,6 +244,7 @@ bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u
     p.weights = L.w.as<uint16_t>();
     p.bias = L.b.as<float>();
     p.slope = L.s.get() ? L.s.as<float>() : nullptr;
+    p.slope_unit = L.slope_unit;
     __half* out = (i % 2 == 0 ? map_a_ : map_b_).as<__half>();
     p.out = out;
     mark(i == 0 ? 1 : i < STEPS - 1 ? 2 : 3, s);
@@ -443,6 +457,10 @@ void RealEsrgan::run_device_noalloc(const float* src, float* dst, size_t count, 
   p.tiles_x = (w + CONV_TILE_W - 1) / CONV_TILE_W;
   p.tiles_y = (h + CONV_TILE_H - 1) / CONV_TILE_H;
   p.tiles = p.tiles_x * p.tiles_y * (int)count;
+  if ((size_t)p.tiles_x * p.tiles_y * count >= (1u << 24) || p.tiles_x >= (1 << 16) || p.tiles_y >= (1 << 16))
+    throw Error(ERR_INPUT, "too many tiles for one pass");
+  p.div_tiles_x = FastDiv((uint32_t)p.tiles_x);
+  p.div_tiles_y = FastDiv((uint32_t)p.tiles_y);
   p.dev_err = dev_.dev_err();
   const void* in = prep;
   for (int i = 0; i < STEPS; i++) {
@@ -450,6 +468,7 @@ void RealEsrgan::run_device_noalloc(const float* src, float* dst, size_t count, 
     p.weights = L.w.as<uint16_t>();
     p.bias = L.b.as<float>();
     p.slope = L.s.get() ? L.s.as<float>() : nullptr;
+    p.slope_unit = L.slope_unit;
     p.out = maps[i % 2];
     if (i == 0) {
       launch_conv<16, 64, CONV_PRELU>(dev_, in, (int)count, mw, mh, p, s);

@@ -62,6 +62,7 @@ class RealEsrgan {
  private:
   struct Layer {
     int cin = 0, cout = 0;  // cin as the kernel sees it (3 -> 16)
+    int slope_unit = 0;     // all PReLU slopes in [0, 1]
     DeviceBuffer w, b, s;
   };
   struct Region {

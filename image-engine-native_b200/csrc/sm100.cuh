@@ -67,21 +67,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase of `bar` with `parity` to complete, at most IEC_WAIT_NS.
-// Gives up early when another role of the CTA has aborted.
+// Gives up early when another role of the CTA has aborted. try_wait itself
+// blocks for a while before it fails; the clock and the abort flag are only
+// looked at every 64 failed tries, so waiting warps take few issue slots
+// from the ones doing work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* dev_err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
-  while (true) {
+  for (uint32_t n = 1;; n++) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (global_ns() - start > IEC_WAIT_NS) {
-      *abort_flag = 1;
-      atomicOr(dev_err, code);
-      return false;
+    if ((n & 63) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - start > IEC_WAIT_NS) {
+        *abort_flag = 1;
+        atomicOr(dev_err, code);
+        return false;
+      }
     }
   }
 }
+
+// n / d for n < 2^24 and 0 < d < 2^16 by one 64-bit multiply: m = ceil(2^40
+// / d) makes n * m / 2^40 exceed n / d by less than 2^-16 < 1 / d.
+struct FastDiv {
+  uint32_t d;
+  uint64_t m;
+  __host__ FastDiv() : d(1), m(1ull << 40) {}
+  __host__ explicit FastDiv(uint32_t div) : d(div), m(((1ull << 40) + div - 1) / div) {}
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (uint32_t)(((uint64_t)n * m) >> 40); }
+};
 
 // ---------------------------------------------------------------------- TMA
 // 1-D bulk copy global -> shared, completing on `bar` (16-byte aligned
@@ -103,6 +118,17 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+// Tiled 4-D tensor load (no multicast). The caller keeps c0 * element size a
+// multiple of 16 bytes; negative or past-the-end coordinates read zeros.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 
@@ -163,6 +189,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+
+// 32 lanes x 4 columns of 32 bits.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
+// 32 lanes x 8 columns of 32 bits.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 
 // Shared-memory matrix descriptor, no swizzle, K-major: core matrices of

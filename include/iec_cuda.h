@@ -114,7 +114,7 @@ iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images,
  * their feature maps with cudaMalloc on demand; this one keeps them in a
  * fixed scratch array built into the library, 31.5 MiB that every GPU which
  * loads the library holds until the process exits.
- *  - Limit: count x max(width, 10) x max(height, 18) <= 114688 pixels (for
+ *  - Limit: count x max(width, 16) x max(height, 10) <= 114688 pixels (for
  *    example one 384 x 256 image); a larger call returns IEC_ERR_INPUT.
  *  - The model itself is loaded beforehand with iec_realesrgan_load, which
  *    does allocate; the call only uses `images`, `out` and the scratch.
