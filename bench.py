@@ -199,6 +199,7 @@ def main():
     ap.add_argument("--chunk", type=int, default=8, help="images per launch")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
+    ap.add_argument("--no-tiles", action="store_true", help="skip the large-image tiles leg")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()
@@ -302,6 +303,42 @@ def main():
                "d2h_bytes_per_step": batch * WIDTH * HEIGHT * 3 * 4 * 16,
                "api": "iec_realesrgan_run_batch (host buffers, page-locked)", "matches_device_path": same}
 
+    # The other sharded workload: one 3x4096x4096 image cut into 512 x 512
+    # tiles with a 34-pixel margin; each rank runs its cost-balanced range of
+    # the 64 tiles (device-resident input and output, no gather in the timed
+    # region). Same max-over-ranks device timing.
+    tiles_leg = None
+    if not args.no_tiles:
+        from iec import shard
+
+        TW, TILE, MARGIN = 4096, 512, 34
+        grid = shard.tile_grid(TW, TW, TILE, MARGIN)
+        first, last = shard.split_ranges([t.cost for t in grid], world)[rank]
+        g2 = torch.Generator(device="cuda").manual_seed(4321)
+        big_in = torch.rand((TW, TW, 3), generator=g2, device="cuda", dtype=torch.float32)
+        big_out = torch.empty((4 * TW, 4 * TW, 3), device="cuda", dtype=torch.float32)
+
+        def tiles_step():
+            model.run_tiles_device(big_in.data_ptr(), TW, TW, TILE, MARGIN, first, last, big_out.data_ptr(), sptr)
+
+        tiles_step()
+        torch.cuda.synchronize()
+        barrier()
+        t_a, t_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tiles_steps = max(2, args.steps // 2)
+        t_a.record(stream)
+        for _ in range(tiles_steps):
+            tiles_step()
+        t_b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t_s = max_over_ranks(t_a.elapsed_time(t_b) / 1e3) / tiles_steps
+        tiles_leg = {"workload": "realesrgan_x4v3 one 3x4096x4096 image, 64 tiles of 512 + 34 margin, split by tile",
+                     "value": TW * TW * 16 / 1e6 / t_s, "unit": "MP/s", "ms_per_step": t_s * 1e3,
+                     "steps": tiles_steps, "tiles_rank0": [first, last],
+                     "computed_over_algorithmic_px": sum(t.cost for t in grid) / (TW * TW)}
+        del big_in, big_out
+
     # One image (the single-image configuration) on one GPU, device-resident.
     single = None
     if rank == 0 and world == 1:
@@ -346,6 +383,7 @@ def main():
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps * world,
             "clocks": clocks,
+            "sharded_tiles": tiles_leg,
             "per_model": {"realesrgan_single_image": single},
         }
         print(json.dumps(line), flush=True)

@@ -133,6 +133,51 @@ iec_status iec_realesrgan_run(iec_realesrgan* model, const uint8_t* rgb, size_t 
   return run_host(model, rgb, true, width, height, RealEsrgan::GPU_TILE, RealEsrgan::MARGIN, out, progress, user);
 }
 
+iec_status iec_realesrgan_run_float_tiles(iec_realesrgan* model, const float* image, size_t width, size_t height,
+                                          size_t tile, size_t margin, size_t first, size_t last, float* out) {
+  return guard([&] {
+    need(model, "model");
+    need(image, "image");
+    need(out, "out");
+    check_realesrgan_size(width, height);
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    const auto windows = RealEsrgan::tile_windows(width, height, tile, first, last);
+    const size_t in_bytes = width * height * 3 * 4;
+    m.host_in.reserve(in_bytes);
+    m.host_out.reserve(in_bytes * 16);
+    cudaStream_t s = m.device().stream();
+    IEC_CUDA(cudaMemcpyAsync(m.host_in.get(), image, in_bytes, cudaMemcpyHostToDevice, s));
+    m.run_tiled_device(m.host_in.get(), false, m.host_out.get(), false, 1, width, height, tile, margin, nullptr, s,
+                       first, last);
+    // Only the tiles' own windows come back; the rest of `out` is untouched.
+    const size_t pitch = width * 4 * 3 * sizeof(float);
+    for (const auto& w : windows) {
+      const size_t off = (w[1] * 4 * width * 4 + w[0] * 4) * 3;
+      IEC_CUDA(cudaMemcpy2DAsync(out + off, pitch, m.host_out.as<float>() + off, pitch,
+                                 (w[2] - w[0]) * 4 * 3 * sizeof(float), (w[3] - w[1]) * 4, cudaMemcpyDeviceToHost,
+                                 s));
+    }
+    m.device().sync(s);
+  });
+}
+
+iec_status iec_realesrgan_run_tiles_device(iec_realesrgan* model, const float* image, size_t width, size_t height,
+                                           size_t tile, size_t margin, size_t first, size_t last, float* out,
+                                           void* stream) {
+  return guard([&] {
+    need(model, "model");
+    need(image, "image");
+    need(out, "out");
+    check_realesrgan_size(width, height);
+    if (reinterpret_cast<uintptr_t>(out) % 16 != 0) throw Error(ERR_INPUT, "out must be 16-byte aligned");
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run_tiled_device(image, false, out, false, 1, width, height, tile, margin, nullptr, s, first, last);
+  });
+}
+
 iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, size_t count, size_t width,
                                     size_t height, float* out, void* stream) {
   return guard([&] {

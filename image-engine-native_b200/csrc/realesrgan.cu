@@ -292,34 +292,43 @@ bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u
   return !cancelled;
 }
 
-void RealEsrgan::run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_u8, size_t count, size_t width,
-                                  size_t height, size_t tile, size_t margin,
-                                  const std::function<bool(float)>& progress, cudaStream_t s) {
+std::vector<std::array<size_t, 4>> RealEsrgan::tile_windows(size_t width, size_t height, size_t tile, size_t first,
+                                                            size_t last) {
   if (tile == 0) throw Error(ERR_INPUT, "tile size 0");
   const size_t cols = (width + tile - 1) / tile, rows = (height + tile - 1) / tile;
-  const float steps = (float)(cols * rows * STEPS);
+  std::vector<std::array<size_t, 4>> out;
+  for (size_t t = first; t < std::min(last, cols * rows); t++) {
+    const size_t j = t / cols, i = t % cols;
+    out.push_back({i * width / cols, j * height / rows, (i + 1) * width / cols, (j + 1) * height / rows});
+  }
+  return out;
+}
+
+void RealEsrgan::run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_u8, size_t count, size_t width,
+                                  size_t height, size_t tile, size_t margin,
+                                  const std::function<bool(float)>& progress, cudaStream_t s, size_t first,
+                                  size_t last) {
+  const std::vector<std::array<size_t, 4>> windows = tile_windows(width, height, tile, first, last);
+  const float steps = (float)(windows.size() * STEPS);
   size_t done = 0;
   std::function<bool()> step;
   if (progress) step = [&] { return progress((float)(++done) / steps); };
-  for (size_t j = 0; j < rows; j++) {
-    const size_t y0 = j * height / rows, y1 = (j + 1) * height / rows;
-    for (size_t i = 0; i < cols; i++) {
-      const size_t x0 = i * width / cols, x1 = (i + 1) * width / cols;
-      const size_t rx0 = x0 > margin ? x0 - margin : 0, ry0 = y0 > margin ? y0 - margin : 0;
-      const size_t rx1 = margin > width - x1 ? width : x1 + margin;
-      const size_t ry1 = margin > height - y1 ? height : y1 + margin;
-      Region r;
-      r.rx0 = (int)rx0;
-      r.ry0 = (int)ry0;
-      r.rw = (int)(rx1 - rx0);
-      r.rh = (int)(ry1 - ry0);
-      r.kx0 = (int)(x0 - rx0);
-      r.ky0 = (int)(y0 - ry0);
-      r.kx1 = (int)(x1 - rx0);
-      r.ky1 = (int)(y1 - ry0);
-      if (!run_network(src, src_u8, dst, dst_u8, (int)count, (int)width, (int)height, r, step, s))
-        throw Error(CANCELLED, "cancelled");
-    }
+  for (const auto& wnd : windows) {
+    const size_t x0 = wnd[0], y0 = wnd[1], x1 = wnd[2], y1 = wnd[3];
+    const size_t rx0 = x0 > margin ? x0 - margin : 0, ry0 = y0 > margin ? y0 - margin : 0;
+    const size_t rx1 = margin > width - x1 ? width : x1 + margin;
+    const size_t ry1 = margin > height - y1 ? height : y1 + margin;
+    Region r;
+    r.rx0 = (int)rx0;
+    r.ry0 = (int)ry0;
+    r.rw = (int)(rx1 - rx0);
+    r.rh = (int)(ry1 - ry0);
+    r.kx0 = (int)(x0 - rx0);
+    r.ky0 = (int)(y0 - ry0);
+    r.kx1 = (int)(x1 - rx0);
+    r.ky1 = (int)(y1 - ry0);
+    if (!run_network(src, src_u8, dst, dst_u8, (int)count, (int)width, (int)height, r, step, s))
+      throw Error(CANCELLED, "cancelled");
   }
 }
 

@@ -9,6 +9,8 @@
 
 #include <cuda_fp16.h>
 
+#include <array>
+#include <cstdint>
 #include <functional>
 #include <memory>
 #include <string>
@@ -31,9 +33,16 @@ class RealEsrgan {
   // width x height x 3 (f32 or u8), `dst` their 4x outputs (f32 or u8).
   // Runs tile by tile; `progress` (may be empty) gets the share done after
   // each layer and returns false to cancel.
+  // Only tiles first .. last - 1 of the grid (row-major) run when a range is
+  // given; each writes just its own window of `dst`.
   void run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_u8, size_t count, size_t width,
                         size_t height, size_t tile, size_t margin, const std::function<bool(float)>& progress,
-                        cudaStream_t stream);
+                        cudaStream_t stream, size_t first = 0, size_t last = SIZE_MAX);
+
+  // lib.rs:241-289's grid: the kept window {x0, y0, x1, y1} (input pixels)
+  // of each tile first .. last - 1.
+  static std::vector<std::array<size_t, 4>> tile_windows(size_t width, size_t height, size_t tile, size_t first,
+                                                         size_t last);
 
   // Whole images (one region each), `count` at a time in chunks; no waits.
   void run_device(const float* src, float* dst, size_t count, size_t width, size_t height, cudaStream_t stream);

@@ -63,6 +63,8 @@ def lib():
         L.iec_realesrgan_run_float.argtypes = [vp, f32p, sz, sz, f32p]
         L.iec_realesrgan_run_float_tiled.argtypes = [vp, f32p, sz, sz, sz, sz, f32p, PROGRESS, vp]
         L.iec_realesrgan_run.argtypes = [vp, u8p, sz, sz, u8p, PROGRESS, vp]
+        L.iec_realesrgan_run_float_tiles.argtypes = [vp, f32p, sz, sz, sz, sz, sz, sz, f32p]
+        L.iec_realesrgan_run_tiles_device.argtypes = [vp, vp, sz, sz, sz, sz, sz, sz, vp, vp]
         L.iec_realesrgan_run_batch.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_launches.argtypes = [vp, sz, sz, sz]
@@ -152,6 +154,24 @@ class RealEsrgan:
         return out
 
     run_with_progress = run
+
+    def run_float_tiles(self, image: np.ndarray, tile: int, margin: int, first: int, last: int, out=None):
+        """Tiles first .. last - 1 of run_float_tiled's grid into `out` (the
+        whole 4x output; the other tiles' windows are left untouched)."""
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, _ = image.shape
+        if out is None:
+            out = np.zeros((4 * h, 4 * w, 3), np.float32)
+        assert out.flags.c_contiguous and out.dtype == np.float32
+        _check(lib().iec_realesrgan_run_float_tiles(self._h, _f32(image), w, h, tile, min(margin, 2**64 - 1),
+                                                    first, last, _f32(out)))
+        return out
+
+    def run_tiles_device(self, image_ptr: int, width: int, height: int, tile: int, margin: int, first: int,
+                         last: int, out_ptr: int, stream: int = 0):
+        """run_float_tiles on device pointers, queued on `stream`."""
+        _check(lib().iec_realesrgan_run_tiles_device(self._h, image_ptr, width, height, tile, margin, first, last,
+                                                     out_ptr, stream or None))
 
     def run_batch(self, images, out=None, stream: int = 0):
         """Batched run_float on host arrays (N x H x W x 3). `images` and

@@ -100,6 +100,24 @@ iec_status iec_realesrgan_run(iec_realesrgan* model, const uint8_t* rgb, size_t 
 iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, size_t count,
                                     size_t width, size_t height, float* out, void* stream);
 
+/* Part of Model::run_float_tiled for sharding one large image over GPUs: of
+ * the grid of tiles run_float_tiled would cut (row-major order), only tiles
+ * first .. last - 1 run, and only their own output windows of `out` (the
+ * whole 4x image, width x height x 48 floats) are written; the rest of `out`
+ * is left as it was. Host buffers; returns when the windows are in `out`.
+ * Every tile's pixels come out exactly as in run_float_tiled. */
+iec_status iec_realesrgan_run_float_tiles(iec_realesrgan* model, const float* image,
+                                          size_t width, size_t height, size_t tile,
+                                          size_t margin, size_t first, size_t last, float* out);
+
+/* As iec_realesrgan_run_float_tiles on DEVICE pointers of the model's
+ * device (the whole image in, the whole 4x output); queued on `stream`
+ * (NULL: the model's stream), no wait. */
+iec_status iec_realesrgan_run_tiles_device(iec_realesrgan* model, const float* image,
+                                           size_t width, size_t height, size_t tile,
+                                           size_t margin, size_t first, size_t last, float* out,
+                                           void* stream);
+
 /* As iec_realesrgan_run_batch on DEVICE pointers of the model's device; the
  * work is queued on `stream` and the call returns without waiting for it. */
 iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images, size_t count,

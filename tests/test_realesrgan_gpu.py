@@ -180,3 +180,17 @@ def test_weight_file_errors(workdir):
     with pytest.raises(iec.IecError) as e:
         iec.RealEsrgan(str(workdir / "does-not-exist.weights"))
     assert e.value.code == iec.ERR_IO
+
+
+def test_tile_ranges_stitch_to_the_tiled_run(gpu_model):
+    # The sharded large-image path: each rank runs a contiguous range of
+    # tiles; the ranges here run one after another on one GPU.
+    from iec import shard
+
+    image = W.realesrgan_input(200, 130, 13)
+    tiles = shard.tile_grid(200, 130, 64, 34)
+    want = gpu_model.run_float_tiled(image, 64, 34)
+    out = np.full((520, 800, 3), np.nan, np.float32)
+    for first, last in shard.split_ranges([t.cost for t in tiles], 3):
+        gpu_model.run_float_tiles(image, 64, 34, first, last, out)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
