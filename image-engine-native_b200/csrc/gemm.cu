@@ -1,0 +1,279 @@
+// Host side of the general implicit GEMM and the bandwidth kernels around it
+// (see gemm.h).
+#include "gemm.h"
+
+#include <algorithm>
+
+#include "igemm_sm100.cuh"
+
+namespace iec {
+
+namespace {
+
+int choose_bn(int n) {
+  const int cands[] = {256, 192, 128, 96, 64, 32};
+  for (int bn : cands)
+    if (n % bn == 0) return bn;
+  return 32;  // n padded to a multiple of 32 with zero columns
+}
+
+int choose_kb(int k) {
+  if (k % 64 == 0) return 64;
+  if (k % 32 == 0) return 32;
+  if (k % 16 == 0) return 16;
+  throw Error(ERR_INPUT, "GEMM reduction of " + std::to_string(k) + " channels: not a multiple of 16");
+}
+
+template <int BN, int KB, int AMODE>
+void launch(Device& dev, const CUtensorMap& map, const GemmParams& p, cudaStream_t s) {
+  auto kernel = igemm_sm100<BN, KB, AMODE>;
+  static int smem_bytes[64] = {};
+  int& bytes = smem_bytes[dev.ordinal() & 63];
+  if (bytes == 0) {
+    int optin = 0;
+    IEC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev.ordinal()));
+    if (optin < GemmSmem<BN, KB>::DYN_BYTES) throw Error(ERR_GPU, "not enough shared memory per block");
+    IEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+    bytes = optin;  // one CTA per SM: its TMEM columns are always free
+  }
+  const int grid = std::min(p.tiles, dev.sms());
+  kernel<<<grid, GEMM_THREADS, bytes, s>>>(map, p);
+  IEC_CUDA(cudaGetLastError());
+}
+
+template <int AMODE>
+void dispatch(Device& dev, int bn, int kb, const CUtensorMap& map, const GemmParams& p, cudaStream_t s) {
+#define IEC_GEMM_CASE(BN_, KB_) \
+  if (bn == BN_ && kb == KB_) return launch<BN_, KB_, AMODE>(dev, map, p, s);
+#define IEC_GEMM_BN(KB_)  \
+  IEC_GEMM_CASE(32, KB_)  \
+  IEC_GEMM_CASE(64, KB_)  \
+  IEC_GEMM_CASE(96, KB_)  \
+  IEC_GEMM_CASE(128, KB_) \
+  IEC_GEMM_CASE(192, KB_) \
+  IEC_GEMM_CASE(256, KB_)
+  IEC_GEMM_BN(64)
+  IEC_GEMM_BN(32)
+  if (AMODE == A_CONV3) {
+    IEC_GEMM_BN(16)
+  }
+#undef IEC_GEMM_BN
+#undef IEC_GEMM_CASE
+  throw Error(ERR_GPU, "no GEMM kernel for this tile shape");
+}
+
+void fill_out(GemmParams& p, const GemmOutSpec& o) {
+  p.out_mode = o.mode;
+  p.out = o.out;
+  p.out_plane_elems = o.plane_elems;
+  p.out_plane0 = o.plane0;
+  p.map_h = o.map_h;
+  p.map_w = o.map_w;
+  p.shift = o.shift;
+  p.dbl_w = o.dbl_w;
+  p.dbl_cout = o.dbl_cout;
+}
+
+}  // namespace
+
+void pack_weights(PackedWeights& pw, const std::vector<float>& w, int taps, int k, int n, const float* bias) {
+  pw.n = n;
+  pw.k = k;
+  pw.taps = taps;
+  pw.ktot = taps * k;
+  pw.bn = choose_bn(n);
+  pw.kb = choose_kb(k);
+  const int n_pad = (n + pw.bn - 1) / pw.bn * pw.bn;
+  pw.n_tiles = n_pad / pw.bn;
+  pw.ksteps = pw.ktot / pw.kb;
+  if ((size_t)pw.ktot * n != w.size()) throw Error(ERR_WEIGHTS, "weight matrix size does not match");
+  // [n tile][k step][kb / 8 groups][bn][8]
+  std::vector<uint16_t> packed((size_t)n_pad * pw.ktot, 0);
+  const int kg = pw.kb / 8;
+  for (int nt = 0; nt < pw.n_tiles; nt++)
+    for (int ks = 0; ks < pw.ksteps; ks++)
+      for (int g = 0; g < kg; g++)
+        for (int j = 0; j < pw.bn; j++)
+          for (int e = 0; e < 8; e++) {
+            const int kk = ks * pw.kb + g * 8 + e, nn = nt * pw.bn + j;
+            const size_t at = ((((size_t)nt * pw.ksteps + ks) * kg + g) * pw.bn + j) * 8 + e;
+            packed[at] = nn < n ? f32_to_half(w[(size_t)kk * n + nn]) : 0;
+          }
+  pw.w.reserve(packed.size() * 2);
+  IEC_CUDA(cudaMemcpy(pw.w.get(), packed.data(), packed.size() * 2, cudaMemcpyHostToDevice));
+  pw.has_bias = bias != nullptr;
+  if (bias) {
+    pw.bias.reserve((size_t)n * 4);
+    IEC_CUDA(cudaMemcpy(pw.bias.get(), bias, (size_t)n * 4, cudaMemcpyHostToDevice));
+  }
+}
+
+void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long a_plane_elems, int m, int act,
+               const GemmOutSpec& out, cudaStream_t s) {
+  if (pw.taps != 1) throw Error(ERR_INPUT, "gemm_rows needs a 1x1 weight matrix");
+  if (m % 16 != 0) throw Error(ERR_INPUT, "GEMM rows must be a multiple of 16");
+  const int kg = pw.kb / 8;
+  CUtensorMap map;
+  const uint64_t dims[3] = {128, (uint64_t)m / 16, (uint64_t)pw.k / 8};
+  const uint64_t strides[2] = {256, (uint64_t)a_plane_elems * 2};
+  const uint32_t box[3] = {128, 8, (uint32_t)kg};
+  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, a, dims, strides, box);
+  GemmParams p{};
+  p.M = m;
+  p.N = pw.n;
+  p.K = pw.k;
+  p.tiles_m = (m + 127) / 128;
+  p.tiles_n = pw.n_tiles;
+  p.tiles = p.tiles_m * p.tiles_n;
+  p.div_tiles_n = FastDiv((uint32_t)p.tiles_n);
+  p.ksteps = pw.ksteps;
+  p.b = pw.w.as<uint16_t>();
+  p.bias = pw.has_bias ? pw.bias.as<float>() : nullptr;
+  p.act = act;
+  fill_out(p, out);
+  p.dev_err = dev.dev_err();
+  if (p.tiles >= (1 << 24)) throw Error(ERR_INPUT, "GEMM too large for one launch");
+  dispatch<A_ROWS>(dev, pw.bn, pw.kb, map, p, s);
+}
+
+void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map_ptr, long long map_plane_elems, int h, int w,
+                int act, const GemmOutSpec& out, cudaStream_t s) {
+  if (pw.taps != 9) throw Error(ERR_INPUT, "gemm_conv3 needs 3x3 weights");
+  if (w % 8 != 0 || w < 8 || h < 8) throw Error(ERR_INPUT, "3x3 GEMM maps must be at least 8 x 8, width a multiple of 8");
+  const int kg = pw.kb / 8;
+  const int tw = w >= 16 ? 16 : 8;
+  CUtensorMap map;
+  const uint64_t dims[4] = {(uint64_t)w * 8, (uint64_t)h, (uint64_t)pw.k / 8, 1};
+  const uint64_t strides[3] = {(uint64_t)w * 16, (uint64_t)map_plane_elems * 2, (uint64_t)map_plane_elems * 2 * (pw.k / 8)};
+  const uint32_t box[4] = {(uint32_t)tw * 8, 8, (uint32_t)kg, 1};
+  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, map_ptr, dims, strides, box);
+  GemmParams p{};
+  p.M = h * w;
+  p.N = pw.n;
+  p.K = pw.k;
+  p.H = h;
+  p.W = w;
+  p.TW = tw;
+  p.tiles_w = (w + tw - 1) / tw;
+  p.tiles_m = p.tiles_w * ((h + 7) / 8);
+  p.tiles_n = pw.n_tiles;
+  p.tiles = p.tiles_m * p.tiles_n;
+  p.div_tiles_n = FastDiv((uint32_t)p.tiles_n);
+  p.div_tiles_w = FastDiv((uint32_t)p.tiles_w);
+  p.ksteps = pw.ksteps;
+  p.b = pw.w.as<uint16_t>();
+  p.bias = pw.has_bias ? pw.bias.as<float>() : nullptr;
+  p.act = act;
+  fill_out(p, out);
+  p.dev_err = dev.dev_err();
+  if (p.tiles >= (1 << 24) || p.tiles_w >= (1 << 16)) throw Error(ERR_INPUT, "GEMM too large for one launch");
+  dispatch<A_CONV3>(dev, pw.bn, pw.kb, map, p, s);
+}
+
+// ---------------------------------------------------------- bandwidth kernels
+__global__ void rows_to_planar_kernel(const float* __restrict__ src, int rows, int c, __half* __restrict__ dst,
+                                      long long plane) {
+  const int groups = c / 8;
+  const long long total = (long long)rows * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int g = (int)(i % groups);
+    const long long r = i / groups;
+    const float4* s4 = reinterpret_cast<const float4*>(src + r * c + g * 8);
+    const float4 a = s4[0], b = s4[1];
+    __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+    __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+    *reinterpret_cast<uint4*>(dst + g * plane + r * 8) =
+        make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                   *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+  }
+}
+
+__global__ void planar_to_rows_kernel(const __half* __restrict__ src, long long plane, int rows, int c,
+                                      float* __restrict__ dst) {
+  const long long total = (long long)rows * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int ch = (int)(i % c);
+    const long long r = i / c;
+    dst[i] = __half2float(src[(ch / 8) * plane + r * 8 + ch % 8]);
+  }
+}
+
+static int grid_for(long long n, int block, int sms) {
+  return (int)std::max<long long>(1, std::min<long long>((n + block - 1) / block, (long long)sms * 32));
+}
+
+void rows_to_planar(const float* src, int rows, int c, __half* dst, long long dst_plane_elems, cudaStream_t s) {
+  if (c % 8 != 0) throw Error(ERR_INPUT, "channels must be a multiple of 8");
+  rows_to_planar_kernel<<<grid_for((long long)rows * c / 8, 256, 148), 256, 0, s>>>(src, rows, c, dst, dst_plane_elems);
+  IEC_CUDA(cudaGetLastError());
+}
+
+void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int c, float* dst, cudaStream_t s) {
+  planar_to_rows_kernel<<<grid_for((long long)rows * c, 256, 148), 256, 0, s>>>(src, src_plane_elems, rows, c, dst);
+  IEC_CUDA(cudaGetLastError());
+}
+
+// One thread per output row (token or pixel): two passes over its channel
+// groups for the mean and the variance, a third to normalise and store.
+__global__ void layer_norm_planar_kernel(const __half* __restrict__ src, long long src_plane, int plane0, int rows,
+                                         int c, const float* __restrict__ gamma, const float* __restrict__ beta,
+                                         __half* __restrict__ dst, long long dst_plane, int window, int map_h,
+                                         int map_w, int shift) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rows) return;
+  long long pix = t;
+  if (window) {
+    const int win = t >> 6, i = t & 63, cols = map_w >> 3;
+    const int wy = win / cols, wx = win - wy * cols;
+    pix = (long long)((wy * 8 + (i >> 3) + shift) % map_h) * map_w + (wx * 8 + (i & 7) + shift) % map_w;
+  }
+  const int groups = c / 8;
+  const __half* base = src + (long long)plane0 * src_plane + pix * 8;
+  float sum = 0.0f;
+  for (int g = 0; g < groups; g++) {
+    const uint4 u = *reinterpret_cast<const uint4*>(base + g * src_plane);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float2 f = __half22float2(h[e]);
+      sum += f.x + f.y;
+    }
+  }
+  const float mean = sum / (float)c;
+  float var = 0.0f;
+  for (int g = 0; g < groups; g++) {
+    const uint4 u = *reinterpret_cast<const uint4*>(base + g * src_plane);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float2 f = __half22float2(h[e]);
+      var += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
+    }
+  }
+  const float inv = 1.0f / sqrtf(var / (float)c + 1e-5f);
+  for (int g = 0; g < groups; g++) {
+    const uint4 u = *reinterpret_cast<const uint4*>(base + g * src_plane);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    uint32_t packed[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float2 f = __half22float2(h[e]);
+      const int ch = g * 8 + 2 * e;
+      const float a = (f.x - mean) * inv * gamma[ch] + beta[ch];
+      const float b = (f.y - mean) * inv * gamma[ch + 1] + beta[ch + 1];
+      __half2 o = __floats2half2_rn(a, b);
+      packed[e] = *reinterpret_cast<uint32_t*>(&o);
+    }
+    *reinterpret_cast<uint4*>(dst + g * dst_plane + (long long)t * 8) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+}
+
+void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c, const float* gamma,
+                       const float* beta, __half* dst, long long dst_plane_elems, bool window, int map_h, int map_w,
+                       int shift, cudaStream_t s) {
+  layer_norm_planar_kernel<<<(rows + 127) / 128, 128, 0, s>>>(src, src_plane_elems, plane0, rows, c, gamma, beta, dst,
+                                                              dst_plane_elems, window ? 1 : 0, map_h, map_w, shift);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace iec

@@ -1,0 +1,60 @@
+// Host side of the general implicit GEMM (igemm_sm100.cuh): weight packing,
+// tile-shape choice, tensor maps and launches, and the small bandwidth
+// kernels around it (layout conversions, layer norm, window partition).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <vector>
+
+#include "runtime.h"
+
+namespace iec {
+
+// A layer's weights as the GEMM reads them: `ktot` x `n` (row-major, k =
+// tap * cin + channel for a 3x3 convolution) re-packed per (N tile, K step)
+// into the tensor-core core-matrix image, f16; bias (f32) kept beside.
+struct PackedWeights {
+  int n = 0, k = 0, ktot = 0, taps = 1, bn = 0, kb = 0, n_tiles = 0, ksteps = 0;
+  DeviceBuffer w, bias;
+  bool has_bias = false;
+};
+
+// `w` is ktot x n row-major (ktot = taps * k), `bias` n floats or null.
+void pack_weights(PackedWeights& pw, const std::vector<float>& w, int taps, int k, int n, const float* bias);
+
+// Where a GEMM writes: planar f16 [planes][rows][8].
+struct GemmOutSpec {
+  int mode = 0;                // GemmOut
+  __half* out = nullptr;
+  long long plane_elems = 0;   // rows of the destination * 8
+  int plane0 = 0;              // destination plane of column 0
+  int map_h = 0, map_w = 0, shift = 0;  // OUT_WINDOW_ACCUM
+  int dbl_w = 0, dbl_cout = 0;          // OUT_DOUBLE
+};
+
+// out = act(A x W + bias) over `m` rows of the planar input `a` (k / 8
+// planes of a_rows_alloc rows each; m a multiple of 16).
+void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long a_plane_elems, int m, int act,
+               const GemmOutSpec& out, cudaStream_t s);
+
+// out = act(conv3x3(map) + bias): `map` is planar f16 with k / 8 planes of
+// h x w pixels (plane stride map_plane_elems), zero padding.
+void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map, long long map_plane_elems, int h, int w,
+                int act, const GemmOutSpec& out, cudaStream_t s);
+
+// ---------------------------------------------------------- bandwidth kernels
+// f32 rows [rows][c] <-> planar f16 [c / 8][rows][8] (c a multiple of 8).
+void rows_to_planar(const float* src, int rows, int c, __half* dst, long long dst_plane_elems, cudaStream_t s);
+void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int c, float* dst, cudaStream_t s);
+
+// Layer norm (eps 1e-5) of the c channels starting at plane `plane0` of
+// `src` for every row, written as c / 8 planes of `dst`. With `window`, the
+// rows are the map's pixels and are written in (shifted) 8 x 8 window order:
+// token t of window w comes from pixel ((wy 8 + t / 8 + shift) % h,
+// (wx 8 + t % 8 + shift) % w) (crates/scunet-native/src/swin.rs:170-181).
+void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c,
+                       const float* gamma, const float* beta, __half* dst, long long dst_plane_elems, bool window,
+                       int map_h, int map_w, int shift, cudaStream_t s);
+
+}  // namespace iec

@@ -1,0 +1,314 @@
+// General implicit GEMM on sm_100a tensor cores: every 1x1 convolution,
+// linear layer, 2x2 stride-2 (transposed) convolution and wide 3x3
+// convolution of the networks. f16 inputs, f32 accumulators in TMEM.
+//
+// Semantics: crates/native-engine/src/gemm.rs:514-667 (multiply): out[r] =
+// act(input[r] * w + bias), or accumulated onto out[r], over Input::Rows or a
+// centred 3x3 stride-1 zero-padded convolution (Taps::Conv), with the GELU of
+// math.rs:63-75 (exact, through erf) or ReLU applied after the sum.
+//
+// Layout. Every activation is f16 "channel-group planar": [channels / 8]
+// [rows][8] with rows = pixels (or tokens) row-major, so the 8 channels of
+// one row form one 16-byte K-unit of a tensor-core core matrix, and a plane
+// is one contiguous run. A-tiles come in by TMA in the no-swizzle K-major
+// core-matrix layout [k-group][128 rows][8] that tcgen05 reads directly:
+//   A_ROWS   128 consecutive rows: a 3-D box {16 rows x 8 channels, 8 blocks of
+//            16 rows, KB/8 groups} (256-byte inner runs).
+//   A_CONV3  a tile of 8 map rows x TW pixels (TW = 16, or the map width when
+//            it is 8): per tap (ky, kx) a 4-D box of the map shifted by
+//            (ky - 1, kx - 1) (zero fill outside the map), K = 9 taps x cin.
+// B-tiles (weights) are pre-arranged on the host per (N tile, K step) as the
+// core-matrix image [KB/8][BN][8] and brought in by one cp.async.bulk.
+//
+// Persistent CTAs walk (M tile, N tile) pairs; 320 threads: warp 0 issues
+// the TMA / bulk loads into a ring of stages, warp 1 the MMAs (M 128, N BN,
+// K 16) into one of two TMEM accumulators, warps 2..9 (two per TMEM lane
+// quarter, half the columns each) run the epilogue while the next tile's
+// MMAs proceed:
+//   OUT_STORE        act(acc + bias) -> f16 planes (at a channel offset)
+//   OUT_ACCUM        out += act(acc + bias)                (residual adds)
+//   OUT_WINDOW_ACCUM out[pixel(token)] += acc + bias, the token's pixel from
+//                    the (shifted) window partition: swin.rs:174-178,212-219
+//   OUT_DOUBLE       2x2 stride-2 transposed convolution: column q cout + o of
+//                    input pixel (y, x) -> output pixel (2y + q / 2, 2x + q % 2),
+//                    channel o (crates/scunet-native/src/network.rs:446-478)
+// All waits are bounded as in conv3x3_sm100.cuh.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace iec {
+
+enum GemmA { A_ROWS = 0, A_CONV3 = 1 };
+enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3 };
+enum GemmAct { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
+
+constexpr int GEMM_EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
+
+struct GemmParams {
+  int M;                    // output rows (A_ROWS) or map pixels H * W (A_CONV3)
+  int N, K;                 // output columns; reduction per tap (channels)
+  int H, W, TW;             // A_CONV3: map size, tile width (16, or 8 for 8-wide maps)
+  int tiles_m, tiles_n, tiles, tiles_w;
+  FastDiv div_tiles_n, div_tiles_w;
+  int ksteps;               // K steps of KB channels (A_CONV3: 9 taps x K / KB)
+  const uint16_t* b;        // [n tile][k step][KB / 8][BN][8] f16
+  const float* bias;        // [N] or null
+  int act;
+  int out_mode;
+  __half* out;              // planar f16: plane p at out + p * out_plane_elems
+  long long out_plane_elems;  // elements per plane (rows * 8)
+  int out_plane0;           // plane of output column 0
+  int map_h, map_w, shift;  // OUT_WINDOW_ACCUM: the map the tokens came from
+  int dbl_w, dbl_cout;      // OUT_DOUBLE: input width, output channels
+  int* dev_err;
+};
+
+template <int BN, int KB>
+struct GemmSmem {
+  static constexpr int A_BYTES = (KB / 8) * 128 * 16;
+  static constexpr int B_BYTES = (KB / 8) * BN * 16;
+  static constexpr int STAGE = ((A_BYTES + B_BYTES) + 1023) / 1024 * 1024;
+  static constexpr int NSTAGE = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+  static constexpr int BAR_OFF = NSTAGE * STAGE;
+  static constexpr int NBARS = 2 * NSTAGE + 4;
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int TOTAL = MISC_OFF + 16;
+  static constexpr int DYN_BYTES = TOTAL + 1024;
+  static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
+};
+
+__device__ __forceinline__ float gemm_act(float v, int act) {
+  if (act == ACT_RELU) return v > 0.0f ? v : 0.0f;
+  if (act == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  return v;
+}
+
+template <int BN, int KB, int AMODE>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    igemm_sm100(const __grid_constant__ CUtensorMap a_map, const GemmParams p) {
+  static_assert(BN % 16 == 0 && BN <= 256 && (KB == 16 || KB == 32 || KB == 64), "tile shape");
+  using L = GemmSmem<BN, KB>;
+  constexpr int KG = KB / 8;  // channel groups per K step
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + L::NSTAGE;
+  uint64_t* acc_full = bars + 2 * L::NSTAGE;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // A tile: rows of the box, and the A-side bytes one TMA load delivers.
+  const int a_rows = AMODE == A_ROWS ? 128 : 8 * p.TW;
+  const uint32_t a_bytes = (uint32_t)(KG * a_rows * 16);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::NSTAGE; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], GEMM_EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      prefetch_tensor_map(&a_map);
+      int s = 0;
+      uint32_t phase = 0;
+      int issued[L::NSTAGE];
+      for (int i = 0; i < L::NSTAGE; i++) issued[i] = -1;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+        const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
+        int x0 = 0, y0 = 0;
+        if (AMODE == A_CONV3) {
+          y0 = (int)p.div_tiles_w.div((uint32_t)mt);
+          x0 = (mt - y0 * p.tiles_w) * p.TW;
+          y0 *= 8;
+        }
+        const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
+        for (int ks = 0; ks < p.ksteps; ks++) {
+          if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * L::STAGE;
+          mbar_arrive_expect_tx(&full[s], a_bytes + (uint32_t)L::B_BYTES);
+          if (AMODE == A_ROWS) {
+            tma_load_3d(st, &a_map, &full[s], 0, mt * 8, ks * KG);
+          } else {
+            const int per_tap = p.K / KB;
+            const int tap = ks / per_tap, kb = ks - tap * per_tap;
+            tma_load_4d(st, &a_map, &full[s], (x0 + tap % 3 - 1) * 8, y0 + tap / 3 - 1, kb * KG, 0);
+          }
+          bulk_load(st + L::A_BYTES, bsrc + (size_t)ks * L::B_BYTES, L::B_BYTES, &full[s]);
+          issued[s] = (int)phase;
+          if (++s == L::NSTAGE) {
+            s = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int i = 0; i < L::NSTAGE; i++)
+        if (issued[i] >= 0) mbar_wait(&full[i], (uint32_t)issued[i], abort_flag, p.dev_err, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      const uint32_t lbo_a = (uint32_t)(a_rows * 16);
+      int s = 0, i = 0, last_acc = -1;
+      uint32_t phase = 0, last_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
+        const int a = i & 1;
+        const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
+        if (!mbar_wait(&acc_empty[a], acc_phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_EMPTY)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(a * L::ACC_COLS);
+        for (int ks = 0; ks < p.ksteps; ks++) {
+          if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t abase = smem_u32(smem + s * L::STAGE), bbase = abase + (uint32_t)L::A_BYTES;
+#pragma unroll
+          for (int j = 0; j < KB / 16; j++) {
+            const uint64_t adesc = smem_desc(abase + (uint32_t)(2 * j) * lbo_a, lbo_a, 128);
+            const uint64_t bdesc = smem_desc(bbase + (uint32_t)(2 * j * BN * 16), BN * 16, 128);
+            umma_f16(d, adesc, bdesc, idesc, (ks | j) != 0);
+          }
+          umma_commit(&empty[s]);
+          if (++s == L::NSTAGE) {
+            s = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[a]);
+        last_acc = a;
+        last_parity = acc_phase;
+      }
+      if (last_acc >= 0) mbar_wait(&acc_full[last_acc], last_parity, abort_flag, p.dev_err, 0);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int part = (warp - 2) >> 2;  // which half of the columns
+    const int row = quarter * 32 + lane;
+    constexpr int HALF = (BN + 31) / 32 * 16;  // columns per part, a multiple of 16
+    int i = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
+      const int a = i & 1;
+      const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
+      if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
+      tc_fence_after();
+      const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
+      // This thread's output row.
+      int m = -1;
+      if (AMODE == A_ROWS) {
+        m = mt * 128 + row;
+        if (m >= p.M) m = -1;
+      } else {
+        const int ty = (int)p.div_tiles_w.div((uint32_t)mt);
+        const int x0 = (mt - ty * p.tiles_w) * p.TW, y0 = ty * 8;
+        const int py = y0 + row / p.TW, px = x0 + row % p.TW;
+        if (row < a_rows && py < p.H && px < p.W) m = py * p.W + px;
+      }
+      // Destination pixel of the row for the scattering epilogues.
+      long long dest = m;
+      if (m >= 0 && p.out_mode == OUT_WINDOW_ACCUM) {
+        const int win = m >> 6, t = m & 63, cols = p.map_w >> 3;
+        const int wy = win / cols, wx = win - wy * cols;
+        const int py = (wy * 8 + (t >> 3) + p.shift) % p.map_h, px = (wx * 8 + (t & 7) + p.shift) % p.map_w;
+        dest = (long long)py * p.map_w + px;
+      }
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * L::ACC_COLS);
+#pragma unroll 1
+      for (int c0 = part * HALF; c0 < part * HALF + HALF && c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + (uint32_t)c0, r);
+        tmem_wait_ld();
+        const int n0 = nt * BN + c0;
+        if (m < 0 || n0 >= p.N) continue;
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          float x = __uint_as_float(r[e]);
+          if (p.bias) x += p.bias[n0 + e < p.N ? n0 + e : 0];
+          v[e] = gemm_act(x, p.act);
+        }
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+          const int n = n0 + 8 * g;
+          if (n >= p.N) break;
+          __half* dst;
+          if (p.out_mode == OUT_DOUBLE) {
+            const int q = n / p.dbl_cout, o = n - q * p.dbl_cout;
+            const int iy = m / p.dbl_w, ix = m - iy * p.dbl_w;
+            const long long op = (long long)(2 * iy + (q >> 1)) * (2 * p.dbl_w) + 2 * ix + (q & 1);
+            dst = p.out + (long long)(p.out_plane0 + o / 8) * p.out_plane_elems + op * 8;
+          } else {
+            dst = p.out + (long long)(p.out_plane0 + n / 8) * p.out_plane_elems + dest * 8;
+          }
+          float w8[8];
+#pragma unroll
+          for (int e = 0; e < 8; e++) w8[e] = v[8 * g + e];
+          if (p.out_mode == OUT_ACCUM || p.out_mode == OUT_WINDOW_ACCUM) {
+            const uint4 old = *reinterpret_cast<const uint4*>(dst);
+            const __half2* oh = reinterpret_cast<const __half2*>(&old);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const float2 f = __half22float2(oh[e]);
+              w8[2 * e] += f.x;
+              w8[2 * e + 1] += f.y;
+            }
+          }
+          uint32_t packed[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            __half2 h2 = __floats2half2_rn(w8[2 * e], w8[2 * e + 1]);
+            packed[e] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+}  // namespace iec

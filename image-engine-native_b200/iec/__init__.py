@@ -69,6 +69,8 @@ def lib():
         L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_launches.argtypes = [vp, sz, sz, sz]
         L.iec_realesrgan_launches.restype = sz
+        i32 = ctypes.c_int
+        L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
         L.iec_realesrgan_set_timing.argtypes = [vp, sz]
         L.iec_realesrgan_timing.argtypes = [vp, ctypes.POINTER(ctypes.c_int), f32p, sz]
         L.iec_realesrgan_timing.restype = sz
@@ -205,3 +207,26 @@ def _addr(a) -> int:
     if hasattr(a, "data_ptr"):
         return a.data_ptr()
     return a.ctypes.data
+
+
+def selftest_gemm(a, w, bias=None, *, conv=False, shape=None, act=0, accumulate_onto=None, device=0):
+    """Diagnostics: one general-GEMM launch on host arrays. Rows: `a` is
+    rows x k, `w` k x n. conv: `a` is h x w x k (shape=(h, w)), `w` 9k x n,
+    3x3 zero padding. act 0 none, 1 ReLU, 2 GELU. Returns rows x n float32."""
+    a = np.ascontiguousarray(a, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    n = w.shape[1]
+    if conv:
+        h, wd = shape
+        k = a.shape[-1]
+        rows_or_h, width, rows = h, wd, h * wd
+    else:
+        rows, k = a.shape
+        rows_or_h, width = rows, 0
+    out = (np.zeros((rows, n), np.float32) if accumulate_onto is None
+           else np.ascontiguousarray(accumulate_onto, np.float32).copy())
+    b = np.ascontiguousarray(bias, np.float32) if bias is not None else None
+    st = lib().iec_selftest_gemm(device, int(conv), rows_or_h, width, k, n, _f32(a), _f32(w),
+                                 _f32(b) if b is not None else None, act, int(accumulate_onto is not None), _f32(out))
+    _check(st)
+    return out

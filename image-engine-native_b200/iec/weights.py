@@ -80,3 +80,75 @@ def realesrgan_input(width: int, height: int, seed: int = 0) -> np.ndarray:
     """A seeded RGB image, NHWC float32 uniform in [0, 1)."""
     rng = np.random.default_rng(seed)
     return rng.random((height, width, 3), dtype=np.float32)
+
+
+def scunet_tensors(seed: int = 0, branch_gain: float = 0.25, tail_gain: float = 0.1):
+    """SCUNet tensors as crates/scunet-native/src/network.rs:113-260 and
+    swin.rs:101-119 load them, 2-D matrices in f16 (export --half), biases,
+    norms and position biases f32. Convolutions He-normal, linear layers
+    LeCun-normal; the last layer of each residual branch (conv_block.2,
+    msa.linear, mlp.2, conv1_2) is scaled by `branch_gain` and the tail by
+    `tail_gain`, so that the 28 residual blocks keep activations of order one
+    and the output stays within a few units, as a trained denoiser's does
+    (plain He/LeCun init compounds to outputs of several hundred). Position
+    bias N(0, 0.02^2),
+    LayerNorm weight 1 + N(0, 0.05^2), bias N(0, 0.02^2), biases U(+-0.05)."""
+    rng = np.random.default_rng(seed)
+    tensors = []
+    half = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+
+    def conv3(name, cin, cout, gain=1.0):
+        w = rng.standard_normal((9 * cin, cout)) * np.sqrt(2.0 / (9 * cin)) * gain
+        tensors.append((f"{name}.weight", half(w), True))
+
+    def lin(name, k, n, bias=True, gain=1.0):
+        w = rng.standard_normal((k, n)) * np.sqrt(1.0 / k) * gain
+        tensors.append((f"{name}.weight", half(w), True))
+        if bias:
+            tensors.append((f"{name}.bias", rng.uniform(-0.05, 0.05, n).astype(np.float32), False))
+
+    def ln(name, c):
+        tensors.append((f"{name}.weight", (1 + 0.05 * rng.standard_normal(c)).astype(np.float32), False))
+        tensors.append((f"{name}.bias", (0.02 * rng.standard_normal(c)).astype(np.float32), False))
+
+    def block(name, c):
+        h = c // 2
+        lin(f"{name}.conv1_1", c, c)
+        conv3(f"{name}.conv_block.0", h, h)
+        conv3(f"{name}.conv_block.2", h, h, branch_gain)
+        t = f"{name}.trans_block"
+        ln(f"{t}.ln1", h)
+        lin(f"{t}.msa.embedding_layer", h, 3 * h)
+        tensors.append((f"{t}.msa.position_bias", (0.02 * rng.standard_normal((h // 32, 64, 64))).astype(np.float32),
+                        False))
+        lin(f"{t}.msa.linear", h, h, gain=branch_gain)
+        ln(f"{t}.ln2", h)
+        lin(f"{t}.mlp.0", h, 4 * h)
+        lin(f"{t}.mlp.2", 4 * h, h, gain=branch_gain)
+        lin(f"{name}.conv1_2", c, c, gain=branch_gain)
+
+    conv3("m_head.0", 3, 64)
+    for i, c in [(1, 64), (2, 128), (3, 256)]:
+        for b in range(4):
+            block(f"m_down{i}.{b}", c)
+        lin(f"m_down{i}.4", 4 * c, 2 * c, bias=False)
+    for b in range(4):
+        block(f"m_body.{b}", 512)
+    for i, c in [(3, 256), (2, 128), (1, 64)]:
+        lin(f"m_up{i}.0", 2 * c, 4 * c, bias=False)
+        for b in range(1, 5):
+            block(f"m_up{i}.{b}", c)
+    conv3("m_tail.0", 64, 3, tail_gain)
+    return tensors
+
+
+def write_scunet(path, seed: int = 0) -> str:
+    return write(path, MAGIC["scunet"], scunet_tensors(seed))
+
+
+def scunet_input(width: int, height: int, seed: int = 0) -> np.ndarray:
+    """A seeded noisy RGB image: uniform [0, 1) plus N(0, (25/255)^2), clamped."""
+    rng = np.random.default_rng(seed)
+    base = rng.random((height, width, 3))
+    noisy = base + rng.standard_normal((height, width, 3)) * (25.0 / 255.0)
+    return np.clip(noisy, 0.0, 1.0).astype(np.float32)

@@ -60,6 +60,14 @@ def lib():
         L.refcpu_realesrgan_run_tiled.argtypes = [
             ctypes.c_void_p, _f32p, sz, sz, sz, sz, _f32p, PROGRESS, ctypes.c_void_p,
         ]
+        L.refcpu_scunet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        L.refcpu_scunet_free.argtypes = [ctypes.c_void_p]
+        L.refcpu_scunet_run_float.argtypes = [ctypes.c_void_p, _f32p, sz, sz, _f32p]
+        L.refcpu_scunet_run_tiled.argtypes = [
+            ctypes.c_void_p, _f32p, sz, sz, sz, sz, _f32p, PROGRESS, ctypes.c_void_p,
+        ]
+        L.refcpu_attention.argtypes = [_f32p, sz, sz, _f32p, sz, _f32p]
+        L.refcpu_layer_norm.argtypes = [_f32p, sz, sz, _f32p, _f32p]
         L.refcpu_set_threads.argtypes = [ctypes.c_int]
         L.refcpu_set_direct.argtypes = [ctypes.c_int]
         _lib = L
@@ -178,3 +186,47 @@ class RealEsrgan:
         _check(lib().refcpu_realesrgan_run_tiled(self._h, _ptr(image), w, h, tile, margin,
                                                  _ptr(out), cb, None))
         return out
+
+
+class Scunet:
+    """The reference's CPU SCUNet (Model::load_cpu) as restated."""
+
+    def __init__(self, path):
+        self._h = ctypes.c_void_p()
+        _check(lib().refcpu_scunet_load(os.fsencode(path), ctypes.byref(self._h)))
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.refcpu_scunet_free(self._h)
+            self._h = None
+
+    def run_float(self, image: np.ndarray) -> np.ndarray:
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, _ = image.shape
+        out = np.empty((h, w, 3), np.float32)
+        _check(lib().refcpu_scunet_run_float(self._h, _ptr(image), w, h, _ptr(out)))
+        return out
+
+    def run_float_tiled(self, image: np.ndarray, tile: int, margin: int, progress=None):
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, _ = image.shape
+        out = np.empty((h, w, 3), np.float32)
+        cb = PROGRESS(lambda f, _u: int(bool(progress(f)))) if progress else PROGRESS()
+        _check(lib().refcpu_scunet_run_tiled(self._h, _ptr(image), w, h, tile, margin, _ptr(out), cb, None))
+        return out
+
+
+def attention(qkv, c, head, bias, tokens):
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    bias = np.ascontiguousarray(bias, np.float32)
+    out = np.zeros((tokens, c), np.float32)
+    _check(lib().refcpu_attention(_ptr(qkv), c, head, _ptr(bias), tokens, _ptr(out)))
+    return out
+
+
+def layer_norm(x, gamma, beta):
+    x = np.array(x, np.float32, copy=True, order="C")
+    g = np.ascontiguousarray(gamma, np.float32)
+    b = np.ascontiguousarray(beta, np.float32)
+    _check(lib().refcpu_layer_norm(_ptr(x), x.shape[0], x.shape[1], _ptr(g), _ptr(b)))
+    return x

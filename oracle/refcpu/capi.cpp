@@ -120,4 +120,39 @@ int refcpu_realesrgan_run_tiled(void* h, const float* image, size_t width, size_
   });
 }
 
+// ---------------------------------------------------------------------- SCUNet
+int refcpu_scunet_load(const char* path, void** out) {
+  return guard([&] { *out = new Scunet(path); });
+}
+void refcpu_scunet_free(void* h) { delete static_cast<Scunet*>(h); }
+
+// Model::run_float on the CPU engine: the whole image (padded to 64).
+int refcpu_scunet_run_float(void* h, const float* image, size_t width, size_t height, float* out) {
+  return guard([&] {
+    if (width == 0 || height == 0) throw Error(ERR_INPUT, "empty image");
+    std::vector<float> r = static_cast<Scunet*>(h)->run(image, width, height, nullptr);
+    std::memcpy(out, r.data(), r.size() * sizeof(float));
+  });
+}
+
+int refcpu_scunet_run_tiled(void* h, const float* image, size_t width, size_t height, size_t tile, size_t margin,
+                            float* out, refcpu_progress_fn cb, void* user) {
+  return guard([&] {
+    std::function<bool(float)> progress;
+    if (cb) progress = [cb, user](float f) { return cb(f, user) == 0; };
+    std::vector<float> r = static_cast<Scunet*>(h)->run_tiled(image, width, height, tile, margin, progress);
+    std::memcpy(out, r.data(), r.size() * sizeof(float));
+  });
+}
+
+// The engine's window attention and layer norm, for the kernels' unit tests.
+int refcpu_attention(const float* qkv, size_t c, size_t head, const float* bias, size_t tokens, float* out) {
+  return guard([&] { attention(qkv, c, head, bias, tokens, out); });
+}
+int refcpu_layer_norm(float* x, size_t rows, size_t n, const float* gamma, const float* beta) {
+  return guard([&] {
+    for (size_t r = 0; r < rows; r++) layer_norm_row(x + r * n, n, gamma, beta);
+  });
+}
+
 }  // extern "C"

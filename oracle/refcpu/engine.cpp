@@ -246,42 +246,67 @@ const float* Input::at(size_t r, size_t t) const {
 // then one fused multiply-add per reduction element in tap-major, channel-
 // minor order; blocks of the reduction store and reload the partial sum in
 // f32, which changes nothing. ReLU applies at the last store, GELU after.
-void multiply(const Input& input, size_t r0, size_t r1, const Matrix& w, float* out, size_t stride,
-              Act act, bool accumulate) {
-  if (r1 <= r0) return;
-  size_t taps = input.tap_count();
-  size_t channels = input.kind == Input::Rows ? w.k : input.channels;
-  if (taps * channels != w.k) throw Error(ERR_INPUT, "input does not match the weights");
+namespace {
+void multiply_rows(const Input& input, size_t r0, size_t r1, long first, long last, const Matrix& w, float* out,
+                   size_t stride, Act act, bool accumulate, std::vector<float>& acc, std::vector<const float*>& ptrs) {
+  const size_t taps = input.tap_count();
+  const size_t channels = input.kind == Input::Rows ? w.k : input.channels;
   const size_t n = w.n;
   const float* W = w.w.data();
   const float* B = w.bias.data();
+  acc.resize(n);
+  ptrs.resize(taps);
+  for (long r = first; r < last; r++) {
+    float* o = out + (size_t)(r - (long)r0) * stride;
+    for (size_t j = 0; j < n; j++) acc[j] = (accumulate ? o[j] : 0.0f) + B[j];
+    for (size_t t = 0; t < taps; t++) ptrs[t] = input.at((size_t)r, t);
+    float* a_ = acc.data();
+    for (size_t t = 0; t < taps; t++) {
+      const float* p = ptrs[t];
+      const float* wt = W + t * channels * n;
+      for (size_t c = 0; c < channels; c++) {
+        float a = p ? p[c] : 0.0f;
+        const float* wr = wt + c * n;
+        for (size_t j = 0; j < n; j++) a_[j] = std::fma(a, wr[j], a_[j]);
+      }
+    }
+    if (act == Act::Relu)
+      for (size_t j = 0; j < n; j++) o[j] = acc[j] > 0.0f ? acc[j] : 0.0f;
+    else
+      for (size_t j = 0; j < n; j++) o[j] = acc[j];
+    if (act == Act::Gelu)
+      for (size_t j = 0; j < n; j++) o[j] = gelu_one(o[j]);
+  }
+}
+
+void check_multiply(const Input& input, const Matrix& w) {
+  const size_t taps = input.tap_count();
+  const size_t channels = input.kind == Input::Rows ? w.k : input.channels;
+  if (taps * channels != w.k) throw Error(ERR_INPUT, "input does not match the weights");
+}
+}  // namespace
+
+void multiply(const Input& input, size_t r0, size_t r1, const Matrix& w, float* out, size_t stride,
+              Act act, bool accumulate) {
+  if (r1 <= r0) return;
+  check_multiply(input, w);
 #pragma omp parallel
   {
-    std::vector<float> acc(n);
-    std::vector<const float*> ptrs(taps);
+    std::vector<float> acc;
+    std::vector<const float*> ptrs;
 #pragma omp for schedule(dynamic, 16)
-    for (long r = (long)r0; r < (long)r1; r++) {
-      float* o = out + (size_t)(r - (long)r0) * stride;
-      for (size_t j = 0; j < n; j++) acc[j] = (accumulate ? o[j] : 0.0f) + B[j];
-      for (size_t t = 0; t < taps; t++) ptrs[t] = input.at((size_t)r, t);
-      float* a_ = acc.data();
-      for (size_t t = 0; t < taps; t++) {
-        const float* p = ptrs[t];
-        const float* wt = W + t * channels * n;
-        for (size_t c = 0; c < channels; c++) {
-          float a = p ? p[c] : 0.0f;
-          const float* wr = wt + c * n;
-          for (size_t j = 0; j < n; j++) a_[j] = std::fma(a, wr[j], a_[j]);
-        }
-      }
-      if (act == Act::Relu)
-        for (size_t j = 0; j < n; j++) o[j] = acc[j] > 0.0f ? acc[j] : 0.0f;
-      else
-        for (size_t j = 0; j < n; j++) o[j] = acc[j];
-      if (act == Act::Gelu)
-        for (size_t j = 0; j < n; j++) o[j] = gelu_one(o[j]);
-    }
+    for (long r = (long)r0; r < (long)r1; r++)
+      multiply_rows(input, r0, r1, r, r + 1, w, out, stride, act, accumulate, acc, ptrs);
   }
+}
+
+void multiply_serial(const Input& input, size_t r0, size_t r1, const Matrix& w, float* out, size_t stride,
+                     Act act, bool accumulate) {
+  if (r1 <= r0) return;
+  check_multiply(input, w);
+  std::vector<float> acc;
+  std::vector<const float*> ptrs;
+  multiply_rows(input, r0, r1, (long)r0, (long)r1, w, out, stride, act, accumulate, acc, ptrs);
 }
 
 // -------------------------------------------------------- winograd.rs:53-773
@@ -533,5 +558,72 @@ float sigmoid_one(float x) {
   return x > 0.0f ? 1.0f - s : s;
 }
 float gelu_one(float x) { return 0.5f * x * (1.0f + std::erf(x * 0.70710678118654752f)); }
+
+}  // namespace ref
+
+namespace ref {
+
+static float lane_sum(const float* v, size_t n) {
+  float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  size_t whole = n / 8 * 8;
+  for (size_t i = 0; i < whole; i += 8)
+    for (int l = 0; l < 8; l++) lanes[l] += v[i + l];
+  float total = ((lanes[0] + lanes[4]) + (lanes[1] + lanes[5])) + ((lanes[2] + lanes[6]) + (lanes[3] + lanes[7]));
+  for (size_t i = whole; i < n; i++) total += v[i];
+  return total;
+}
+
+void layer_norm_row(float* x, size_t n, const float* gamma, const float* beta) {
+  const float fn = (float)n;
+  const float mean = lane_sum(x, n) / fn;
+  float sq[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  size_t whole = n / 8 * 8;
+  for (size_t i = 0; i < whole; i += 8)
+    for (int l = 0; l < 8; l++) {
+      float d = x[i + l] - mean;
+      sq[l] += d * d;
+    }
+  float var = lane_sum(sq, 8);
+  for (size_t i = whole; i < n; i++) {
+    float d = x[i] - mean;
+    var += d * d;
+  }
+  const float inv = 1.0f / std::sqrt(var / fn + 1e-5f);
+  for (size_t i = 0; i < n; i++) x[i] = (x[i] - mean) * inv * gamma[i] + beta[i];
+}
+
+void softmax_from(float* x, size_t n, float max) {
+  for (size_t i = 0; i < n; i++) x[i] = exp_neg(x[i] - max);
+  const float inv = 1.0f / lane_sum(x, n);
+  for (size_t i = 0; i < n; i++) x[i] *= inv;
+}
+
+void attention(const float* qkv, size_t c, size_t head, const float* bias, size_t tokens, float* out) {
+  constexpr size_t D = 32;
+  const float scale = 1.0f / std::sqrt((float)D);
+  const size_t q0 = head * D, k0 = c + head * D, v0 = 2 * c + head * D;
+  std::vector<float> s(tokens);
+  for (size_t i = 0; i < tokens; i++) {
+    const float* q = qkv + i * 3 * c + q0;
+    for (size_t j = 0; j < tokens; j++) s[j] = 0.0f;
+    for (size_t d = 0; d < D; d++) {
+      const float a = q[d] * scale;
+      for (size_t j = 0; j < tokens; j++) s[j] = std::fma(a, qkv[j * 3 * c + k0 + d], s[j]);
+    }
+    float max = -INFINITY;
+    for (size_t j = 0; j < tokens; j++) {
+      s[j] += bias[i * tokens + j];
+      max = s[j] > max ? s[j] : max;
+    }
+    softmax_from(s.data(), tokens, max);
+    float acc[D];
+    for (size_t d = 0; d < D; d++) acc[d] = 0.0f;
+    for (size_t j = 0; j < tokens; j++) {
+      const float* v = qkv + j * 3 * c + v0;
+      for (size_t d = 0; d < D; d++) acc[d] = std::fma(s[j], v[d], acc[d]);
+    }
+    for (size_t d = 0; d < D; d++) out[i * c + head * D + d] = acc[d];
+  }
+}
 
 }  // namespace ref

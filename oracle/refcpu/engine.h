@@ -113,6 +113,9 @@ inline size_t reflect(long i, size_t n) {
 // out[(r - r0) * stride].
 void multiply(const Input& input, size_t r0, size_t r1, const Matrix& w, float* out, size_t stride,
               Act act, bool accumulate);
+// The same on the calling thread alone (for use inside a parallel region).
+void multiply_serial(const Input& input, size_t r0, size_t r1, const Matrix& w, float* out, size_t stride,
+                     Act act, bool accumulate);
 
 // winograd.rs:612-672: the 3x3 stride-1 convolution of an image input with
 // `w`, plus bias, stored to (or with `accumulate` added to) out pixels
@@ -130,5 +133,20 @@ int threads();
 float gelu_one(float x);
 float sigmoid_one(float x);
 float exp_neg(float x);
+
+}  // namespace ref
+
+namespace ref {
+
+// math.rs:78-116: layer normalisation of one row in place (sums in eight
+// interleaved lanes), epsilon 1e-5.
+void layer_norm_row(float* x, size_t n, const float* gamma, const float* beta);
+// math.rs:119-134: softmax of a row in place, given its largest value.
+void softmax_from(float* x, size_t n, float max);
+// attention.rs:25-209 at the AVX2 tier: head `head` (32 channels) of one
+// window of `tokens` tokens; qkv rows of 3c (q | k | v); bias [tokens][tokens]
+// (masks included); writes the head's 32 columns of `tokens` rows of `out`,
+// `c` apart.
+void attention(const float* qkv, size_t c, size_t head, const float* bias, size_t tokens, float* out);
 
 }  // namespace ref

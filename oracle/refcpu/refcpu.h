@@ -26,4 +26,23 @@ class RealEsrgan {
   std::vector<Layer> layers_;
 };
 
+// crates/scunet-native/src/network.rs + swin.rs + lib.rs (see scunet.cpp).
+class Scunet {
+ public:
+  static constexpr size_t DIM = 64, BLOCKS = 4, STEPS = 7 * BLOCKS, MULTIPLE = 64, WINDOW = 8;
+  static constexpr size_t TILE = 896, MARGIN = 64;
+  explicit Scunet(const std::string& path);
+  ~Scunet();
+  // network.rs:265-353: whole image, `step` after each block (false = cancel).
+  std::vector<float> run(const float* image, size_t width, size_t height,
+                         const std::function<bool()>& step) const;
+  // lib.rs:160-247 with identity load/store.
+  std::vector<float> run_tiled(const float* image, size_t width, size_t height, size_t tile,
+                               size_t margin, const std::function<bool(float)>& progress) const;
+  struct Impl;
+
+ private:
+  Impl* impl_;
+};
+
 }  // namespace ref

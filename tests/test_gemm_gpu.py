@@ -1,0 +1,68 @@
+"""The general tcgen05 implicit GEMM (igemm_sm100) against the CPU oracle's
+gemm::multiply (crates/native-engine/src/gemm.rs:514-667) on the same
+f16-rounded inputs: rows and 3x3 convolutions, every tile shape the models
+use, bias, ReLU / GELU, and accumulation onto an existing output. The GPU
+rounds its result to f16; the tolerance is 2e-3 (1 + |v|)."""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def f16(a):
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+def close(got, want, tol=2e-3):
+    err = np.abs(got - want) / (1 + np.abs(want))
+    assert np.isfinite(got).all()
+    assert err.max() <= tol, (err.max(), np.unravel_index(err.argmax(), err.shape))
+
+
+@pytest.mark.parametrize("m,k,n,act", [
+    (256, 32, 96, 0), (128, 64, 64, 1), (384, 256, 768, 0), (512, 128, 32, 2), (256, 64, 192, 2),
+    (1024, 512, 256, 0), (128, 1024, 512, 1), (256, 64, 3, 0),
+])
+def test_rows_match_oracle(m, k, n, act):
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(m + k + n)
+    a = f16(rng.standard_normal((m, k)))
+    w = f16(rng.standard_normal((k, n)) / np.sqrt(k))
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    want = refcpu.multiply(a.ravel(), w, bias, kind="rows", act=act).reshape(m, n)
+    got = iec.selftest_gemm(a, w, bias, act=act)
+    close(got, want)
+
+
+def test_rows_accumulate_onto_output():
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(5)
+    m, k, n = 256, 128, 64
+    a = f16(rng.standard_normal((m, k)))
+    w = f16(rng.standard_normal((k, n)) / np.sqrt(k))
+    old = f16(rng.standard_normal((m, n)))
+    want = refcpu.multiply(a.ravel(), w, None, kind="rows", out=old.ravel().copy(), accumulate=True).reshape(m, n)
+    got = iec.selftest_gemm(a, w, None, accumulate_onto=old)
+    close(got, want)
+
+
+@pytest.mark.parametrize("h,w,k,n,act", [
+    (16, 24, 32, 32, 1), (8, 8, 256, 256, 0), (24, 40, 64, 128, 0), (16, 16, 128, 128, 1), (32, 48, 16, 64, 0),
+    (8, 16, 64, 3, 0),
+])
+def test_conv3_matches_oracle(h, w, k, n, act):
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(h * w + k + n)
+    img = f16(rng.standard_normal((h, w, k)))
+    wt = f16(rng.standard_normal((9 * k, n)) / np.sqrt(9 * k))
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    want = refcpu.multiply(img.ravel(), wt, bias, kind="conv", shape=(h, w, k), size=3, act=act).reshape(h * w, n)
+    got = iec.selftest_gemm(img, wt, bias, conv=True, shape=(h, w), act=act)
+    close(got, want)
