@@ -1,0 +1,173 @@
+// Fused window attention: one CTA per (window, head), softmax(Q K^T / sqrt(32)
+// + bias) V over the 64 tokens of an 8 x 8 window, head dimension 32.
+//
+// Semantics: crates/native-engine/src/attention.rs:25-111 (one head over one
+// window: scores = (q / sqrt 32) . k + bias, the bias already holding the
+// relative-position bias and the shift mask, -inf where tokens may not
+// attend; softmax; weighted sum of values), with the tables of
+// crates/scunet-native/src/swin.rs:26-50.
+//
+// Layout: qkv is the QKV GEMM's output, planar f16 [3c / 8][tokens][8]
+// (queries, then keys, then values, head h at channels 32 h .. 32 h + 31 of
+// each); the output is planar f16 [c / 8][tokens][8], ready as the
+// projection GEMM's A operand. Four warps each own 16 query rows: Q K^T and
+// P V run on mma.sync m16n8k16 (f16 in, f32 accumulate), the scores stay in
+// registers between the two (the accumulator fragment of S is the A fragment
+// of P), and the softmax uses quad shuffles for the row max and sum.
+#include <cuda_fp16.h>
+
+#include "gemm.h"
+
+namespace iec {
+
+namespace {
+
+constexpr int TOK = 64, HD = 32, PITCH = HD + 8;  // smem row pitch in halves (80 bytes)
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(128) window_attention_kernel(const __half* __restrict__ qkv, long long qkv_plane,
+                                                               int c, const float* __restrict__ bias, int shifted,
+                                                               int rows_w, int cols_w, __half* __restrict__ out,
+                                                               long long out_plane) {
+  __shared__ __align__(16) __half sq[TOK * PITCH], sk[TOK * PITCH], sv[TOK * PITCH];
+  const int win = blockIdx.x, head = blockIdx.y, heads = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row0 = (long long)win * TOK;
+  // Q, K, V of this head: 64 tokens x 4 channel groups each.
+  for (int i = threadIdx.x; i < 3 * TOK * 4; i += 128) {
+    const int which = i / (TOK * 4), r = i % (TOK * 4);
+    const int t = r >> 2, g = r & 3;
+    const int plane = which * (c / 8) + head * 4 + g;
+    const uint4 v = *reinterpret_cast<const uint4*>(qkv + plane * qkv_plane + (row0 + t) * 8);
+    __half* dst = (which == 0 ? sq : which == 1 ? sk : sv) + t * PITCH + g * 8;
+    *reinterpret_cast<uint4*>(dst) = v;
+  }
+  __syncthreads();
+
+  // The bias table of this window's class (swin.rs:154-159).
+  int cls = 0;
+  if (shifted) cls = (win % cols_w == cols_w - 1 ? 1 : 0) + 2 * (win / cols_w == rows_w - 1 ? 1 : 0);
+  const float* tb = bias + ((long long)cls * heads + head) * TOK * TOK;
+
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = warp * 16;
+  // S = Q K^T for this warp's 16 rows: 8 key tiles of 8.
+  float s[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 2; kk++) {
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + (q0 + (lane & 15)) * PITCH + kk * 16 + (lane >> 4) * 8), a0, a1,
+            a2, a3);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      // keys 8j .. 8j + 15, dims 16 kk .. 16 kk + 15: two B fragments
+      uint32_t b0, b1, b2, b3;
+      const int key = 8 * j + (lane & 7) + ((lane >> 4) << 3);
+      const int dim = kk * 16 + ((lane >> 3) & 1) * 8;
+      ldsm_x4((uint32_t)__cvta_generic_to_shared(sk + key * PITCH + dim), b0, b1, b2, b3);
+      mma16816(s[j], a0, a1, a2, a3, b0, b1);
+      mma16816(s[j + 1], a0, a1, a2, a3, b2, b3);
+    }
+  }
+  // Scale, bias, softmax (rows g and g + 8 of the warp's 16).
+  const float scale = 0.17677669529663688f;  // 1 / sqrt(32)
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int r = q0 + g + (e >> 1) * 8, col = 8 * j + 2 * t + (e & 1);
+      s[j][e] = s[j][e] * scale + tb[r * TOK + col];
+      mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
+    }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+  }
+  float sum[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      s[j][e] = __expf(s[j][e] - mx[e >> 1]);
+      sum[e >> 1] += s[j][e];
+    }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+  }
+  // O = P V: tokens are the reduction, 4 dim tiles of 8.
+  float o[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    const uint32_t a0 = pack_half2(s[2 * kk][0], s[2 * kk][1]);
+    const uint32_t a1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
+    const uint32_t a2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    const uint32_t a3 = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      // tokens 16 kk .. 16 kk + 15, dims 8 j .. 8 j + 15, transposed
+      uint32_t b0, b1, b2, b3;
+      const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int dim = 8 * j + (lane >> 4) * 8;
+      ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv + tok * PITCH + dim), b0, b1, b2, b3);
+      mma16816(o[j], a0, a1, a2, a3, b0, b1);
+      mma16816(o[j + 1], a0, a1, a2, a3, b2, b3);
+    }
+  }
+  const float inv[2] = {1.0f / sum[0], 1.0f / sum[1]};
+#pragma unroll
+  for (int j = 0; j < 4; j++)
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const long long tok = row0 + q0 + g + 8 * h;
+      const int plane = head * 4 + j;
+      *reinterpret_cast<uint32_t*>(out + plane * out_plane + tok * 8 + 2 * t) =
+          pack_half2(o[j][2 * h] * inv[h], o[j][2 * h + 1] * inv[h]);
+    }
+}
+
+}  // namespace
+
+void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int windows, const float* bias,
+                      bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems,
+                      cudaStream_t s) {
+  if (c % 32 != 0) throw Error(ERR_INPUT, "attention channels must be a multiple of 32");
+  dim3 grid(windows, c / 32);
+  window_attention_kernel<<<grid, 128, 0, s>>>(qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w, out,
+                                               out_plane_elems);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace iec

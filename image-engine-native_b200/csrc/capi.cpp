@@ -10,6 +10,7 @@
 
 #include "../../include/iec_cuda.h"
 #include "realesrgan.h"
+#include "scunet.h"
 
 using namespace iec;
 
@@ -64,6 +65,10 @@ void need(const void* p, const char* what) {
 
 struct iec_realesrgan {
   std::unique_ptr<RealEsrgan> model;
+};
+
+struct iec_scunet {
+  std::unique_ptr<Scunet> model;
 };
 
 extern "C" {
@@ -223,6 +228,77 @@ iec_status iec_realesrgan_run_device_noalloc(iec_realesrgan* model, const float*
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
     m.run_device_noalloc(images, out, count, width, height, s);
   });
+}
+
+// ---------------------------------------------------------------------- SCUNet
+iec_status iec_scunet_load(const char* weights_path, const iec_options* options, iec_scunet** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    need(weights_path, "weights_path");
+    auto h = std::make_unique<iec_scunet>();
+    h->model = std::make_unique<Scunet>(weights_path, to_options(options));
+    *out = h.release();
+  });
+}
+
+void iec_scunet_free(iec_scunet* model) { delete model; }
+
+const char* iec_scunet_device_name(const iec_scunet* model) {
+  return model ? model->model->device().name().c_str() : "";
+}
+
+// crates/scunet-native/src/lib.rs:256-267 (check_size).
+static void check_scunet_size(size_t width, size_t height) {
+  if (width == 0 || height == 0)
+    throw Error(ERR_INPUT, "empty " + std::to_string(width) + " x " + std::to_string(height) + " image");
+  if (width > (size_t)1 << 20 || height > (size_t)1 << 20 || width * height > ((size_t)1 << 31) / 64)
+    throw Error(ERR_INPUT, "a " + std::to_string(width) + " x " + std::to_string(height) + " image is too large");
+}
+
+static iec_status scunet_host(iec_scunet* model, const void* image, bool u8, size_t width, size_t height, bool whole,
+                              size_t tile, size_t margin, void* out, iec_progress_fn progress, void* user) {
+  return guard([&] {
+    need(model, "model");
+    need(image, "image");
+    need(out, "out");
+    check_scunet_size(width, height);
+    Scunet& m = *model->model;
+    DeviceScope scope(m.device());
+    const size_t elem = u8 ? 1 : 4, bytes = width * height * 3 * elem;
+    m.host_in.reserve(bytes);
+    m.host_out.reserve(bytes);
+    cudaStream_t s = m.device().stream();
+    IEC_CUDA(cudaMemcpyAsync(m.host_in.get(), image, bytes, cudaMemcpyHostToDevice, s));
+    std::function<bool(float)> cb;
+    if (progress) cb = [progress, user](float f) { return progress(f, user) == 0; };
+    if (whole) {
+      m.run_region(m.host_in.get(), u8, m.host_out.get(), u8, (int)width, (int)height, 0, 0, (int)width, (int)height, 0,
+                   0, (int)width, (int)height, nullptr, s);
+    } else {
+      m.run_tiled_device(m.host_in.get(), u8, m.host_out.get(), u8, width, height, tile, margin, cb, s);
+    }
+    IEC_CUDA(cudaMemcpyAsync(out, m.host_out.get(), bytes, cudaMemcpyDeviceToHost, s));
+    m.device().sync(s);
+  });
+}
+
+iec_status iec_scunet_run_float(iec_scunet* model, const float* image, size_t width, size_t height, float* out) {
+  return scunet_host(model, image, false, width, height, true, 0, 0, out, nullptr, nullptr);
+}
+
+iec_status iec_scunet_run_float_tiled(iec_scunet* model, const float* image, size_t width, size_t height, size_t tile,
+                                      size_t margin, float* out, iec_progress_fn progress, void* user) {
+  if (tile == 0) {
+    g_error = "input: tile size 0";
+    return IEC_ERR_INPUT;
+  }
+  return scunet_host(model, image, false, width, height, false, tile, margin, out, progress, user);
+}
+
+iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, size_t height, uint8_t* out,
+                          iec_progress_fn progress, void* user) {
+  return scunet_host(model, rgb, true, width, height, false, Scunet::TILE, Scunet::MARGIN, out, progress, user);
 }
 
 size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width, size_t height) {

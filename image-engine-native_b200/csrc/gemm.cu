@@ -112,9 +112,11 @@ void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long 
                const GemmOutSpec& out, cudaStream_t s) {
   if (pw.taps != 1) throw Error(ERR_INPUT, "gemm_rows needs a 1x1 weight matrix");
   if (m % 16 != 0) throw Error(ERR_INPUT, "GEMM rows must be a multiple of 16");
+  if (a_plane_elems < (long long)std::max(m, 128) * 8) throw Error(ERR_INPUT, "GEMM input planes must hold 128 rows");
   const int kg = pw.kb / 8;
   CUtensorMap map;
-  const uint64_t dims[3] = {128, (uint64_t)m / 16, (uint64_t)pw.k / 8};
+  // Planes hold at least 128 rows, so the 128-row box never outgrows them.
+  const uint64_t dims[3] = {128, (uint64_t)std::max(m, 128) / 16, (uint64_t)pw.k / 8};
   const uint64_t strides[2] = {256, (uint64_t)a_plane_elems * 2};
   const uint32_t box[3] = {128, 8, (uint32_t)kg};
   encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, a, dims, strides, box);

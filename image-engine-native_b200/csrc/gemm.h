@@ -34,7 +34,7 @@ struct GemmOutSpec {
 };
 
 // out = act(A x W + bias) over `m` rows of the planar input `a` (k / 8
-// planes of a_rows_alloc rows each; m a multiple of 16).
+// planes of a_plane_elems / 8 >= max(m, 128) rows each; m a multiple of 16).
 void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long a_plane_elems, int m, int act,
                const GemmOutSpec& out, cudaStream_t s);
 
@@ -56,5 +56,11 @@ void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int 
 void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c,
                        const float* gamma, const float* beta, __half* dst, long long dst_plane_elems, bool window,
                        int map_h, int map_w, int shift, cudaStream_t s);
+
+// Fused attention over 8 x 8 windows (attention.cu): `qkv` planar [3c / 8]
+// [windows * 64][8], `bias` [classes][c / 32][64][64] f32 (classes 4 when
+// `shifted`, else 1), output planar [c / 8][windows * 64][8].
+void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int windows, const float* bias,
+                      bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems, cudaStream_t s);
 
 }  // namespace iec

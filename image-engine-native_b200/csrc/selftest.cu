@@ -3,6 +3,7 @@
 // CPU oracle in isolation.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <memory>
 #include <string>
 
@@ -52,6 +53,36 @@ extern "C" iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int
     planar_to_rows(d_o16.as<__half>(), out_plane, rows, out_groups * 8, d_o32.as<float>(), s);
     IEC_CUDA(cudaMemcpy2DAsync(out, (size_t)n * 4, d_o32.get(), (size_t)out_groups * 8 * 4, (size_t)n * 4, rows,
                                cudaMemcpyDeviceToHost, s));
+    dev.sync(s);
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
+extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int windows, int c, const float* bias,
+                                             int shifted, int rows_w, int cols_w, float* out) {
+  try {
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    const int rows = windows * 64, classes = shifted ? 4 : 1;
+    const long long plane = (long long)std::max(rows, 128) * 8;
+    DeviceBuffer d32, dq, db, dout, do32;
+    d32.reserve((size_t)rows * 3 * c * 4);
+    dq.reserve((size_t)plane * (3 * c / 8) * 2);
+    db.reserve((size_t)classes * (c / 32) * 64 * 64 * 4);
+    dout.reserve((size_t)plane * (c / 8) * 2);
+    do32.reserve((size_t)rows * c * 4);
+    cudaStream_t s = dev.stream();
+    IEC_CUDA(cudaMemcpyAsync(d32.get(), qkv, (size_t)rows * 3 * c * 4, cudaMemcpyHostToDevice, s));
+    IEC_CUDA(cudaMemcpyAsync(db.get(), bias, (size_t)classes * (c / 32) * 64 * 64 * 4, cudaMemcpyHostToDevice, s));
+    rows_to_planar(d32.as<float>(), rows, 3 * c, dq.as<__half>(), plane, s);
+    window_attention(dq.as<__half>(), plane, c, windows, db.as<float>(), shifted != 0, rows_w, cols_w,
+                     dout.as<__half>(), plane, s);
+    planar_to_rows(dout.as<__half>(), plane, rows, c, do32.as<float>(), s);
+    IEC_CUDA(cudaMemcpyAsync(out, do32.get(), (size_t)rows * c * 4, cudaMemcpyDeviceToHost, s));
     dev.sync(s);
     return IEC_OK;
   } catch (const Error& e) {

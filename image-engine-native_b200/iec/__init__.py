@@ -71,6 +71,14 @@ def lib():
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
+        L.iec_selftest_attention.argtypes = [i32, f32p, i32, i32, f32p, i32, i32, i32, f32p]
+        L.iec_scunet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
+        L.iec_scunet_free.argtypes = [vp]
+        L.iec_scunet_device_name.argtypes = [vp]
+        L.iec_scunet_device_name.restype = ctypes.c_char_p
+        L.iec_scunet_run_float.argtypes = [vp, f32p, sz, sz, f32p]
+        L.iec_scunet_run_float_tiled.argtypes = [vp, f32p, sz, sz, sz, sz, f32p, PROGRESS, vp]
+        L.iec_scunet_run.argtypes = [vp, u8p, sz, sz, u8p, PROGRESS, vp]
         L.iec_realesrgan_set_timing.argtypes = [vp, sz]
         L.iec_realesrgan_timing.argtypes = [vp, ctypes.POINTER(ctypes.c_int), f32p, sz]
         L.iec_realesrgan_timing.restype = sz
@@ -230,3 +238,64 @@ def selftest_gemm(a, w, bias=None, *, conv=False, shape=None, act=0, accumulate_
                                  _f32(b) if b is not None else None, act, int(accumulate_onto is not None), _f32(out))
     _check(st)
     return out
+
+
+def selftest_attention(qkv, windows, c, bias, shifted, rows_w, cols_w, device=0):
+    """Diagnostics: the fused window attention on host arrays (see
+    iec_selftest_attention)."""
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    bias = np.ascontiguousarray(bias, np.float32)
+    out = np.zeros((windows * 64, c), np.float32)
+    _check(lib().iec_selftest_attention(device, _f32(qkv), windows, c, _f32(bias), int(shifted), rows_w, cols_w,
+                                        _f32(out)))
+    return out
+
+
+class Scunet:
+    """crates/scunet-native/src/lib.rs Model, on the CUDA backend."""
+
+    TILE = 896
+    MARGIN = 64
+    STEPS = 28
+
+    def __init__(self, path, device: int = -1, timeout_ms: int = 0):
+        self._h = ctypes.c_void_p()
+        opt = Options(device, timeout_ms, 0)
+        _check(lib().iec_scunet_load(os.fsencode(path), ctypes.byref(opt), ctypes.byref(self._h)))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().iec_scunet_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def gpu(self) -> str:
+        return lib().iec_scunet_device_name(self._h).decode()
+
+    def run_float(self, image: np.ndarray) -> np.ndarray:
+        """Model::run_float: HxWx3 floats to HxWx3, the whole image at once."""
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, _ = image.shape
+        out = np.empty_like(image)
+        _check(lib().iec_scunet_run_float(self._h, _f32(image), w, h, _f32(out)))
+        return out
+
+    def run_float_tiled(self, image: np.ndarray, tile: int, margin: int, progress=None) -> np.ndarray:
+        image = np.ascontiguousarray(image, np.float32)
+        h, w, _ = image.shape
+        out = np.empty_like(image)
+        _check(lib().iec_scunet_run_float_tiled(self._h, _f32(image), w, h, tile, min(margin, 2**64 - 1), _f32(out),
+                                                _progress(progress), None))
+        return out
+
+    def run(self, rgb: np.ndarray, progress=None) -> np.ndarray:
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        h, w, _ = rgb.shape
+        out = np.empty_like(rgb)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        _check(lib().iec_scunet_run(self._h, rgb.ctypes.data_as(u8p), w, h, out.ctypes.data_as(u8p),
+                                    _progress(progress), None))
+        return out
+
+    run_with_progress = run

@@ -161,6 +161,47 @@ size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t
 iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity);
 size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n);
 
+/* ------------------------------------------------------------------ SCUNet
+ * crates/scunet-native/src/lib.rs: SCUNet denoising, output the size of the
+ * input. */
+typedef struct iec_scunet iec_scunet;
+
+/* Model::load (lib.rs:82-100) with IMAGE_ENGINE_NATIVE_GPU=1 semantics; the
+ * "SCUNET\0\0" weights file of export_weights.py (f16 matrices). */
+iec_status iec_scunet_load(const char* weights_path, const iec_options* options, iec_scunet** out);
+void iec_scunet_free(iec_scunet* model);
+const char* iec_scunet_device_name(const iec_scunet* model);
+
+/* Model::run_float (lib.rs:148-162): the whole image at once (padded to a
+ * multiple of 64 inside), neither clamped nor rounded. */
+iec_status iec_scunet_run_float(iec_scunet* model, const float* image, size_t width, size_t height,
+                                float* out);
+
+/* Model::run_float_tiled (lib.rs:164-183); `progress` called 28 times per
+ * tile. */
+iec_status iec_scunet_run_float_tiled(iec_scunet* model, const float* image, size_t width,
+                                      size_t height, size_t tile, size_t margin, float* out,
+                                      iec_progress_fn progress, void* user);
+
+/* Model::run / run_with_progress (lib.rs:121-146): 8-bit RGB in and out,
+ * tiles of 896 with a 64-pixel margin. */
+iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, size_t height,
+                          uint8_t* out, iec_progress_fn progress, void* user);
+
+/* Diagnostics (no counterpart in the reference): one launch of the general
+ * GEMM on host arrays. conv = 0: `a` rows_or_h x k, `weights` k x n; conv = 1:
+ * `a` rows_or_h x w x k, `weights` 9k x n (3x3, zero padding). act 0 none,
+ * 1 ReLU, 2 GELU; accumulate adds onto `out` (rows x n). */
+iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int w, int k, int n,
+                             const float* a, const float* weights, const float* bias, int act,
+                             int accumulate, float* out);
+
+/* Diagnostics: the fused window attention on host arrays: `qkv` windows * 64
+ * rows of 3c (q | k | v), `bias` classes x (c / 32) x 64 x 64, `out` windows *
+ * 64 rows of c. */
+iec_status iec_selftest_attention(int device, const float* qkv, int windows, int c, const float* bias,
+                                  int shifted, int rows_w, int cols_w, float* out);
+
 #ifdef __cplusplus
 }
 #endif
