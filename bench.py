@@ -182,6 +182,43 @@ def reference_arm(args, weights_path):
     print(json.dumps(line), flush=True)
 
 
+def time_device(fn, stream, warmup=3, iters=10):
+    """Mean seconds per call of `fn` (queued on `stream`), by CUDA events."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(iters):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / 1e3 / iters
+
+
+def other_models(wdir, stream, sptr, args):
+    """SCUNet 3x512x768 (seeded f16 weights), device-resident."""
+    import torch
+
+    import iec
+    from iec import weights as W
+
+    out = {}
+    path = os.path.join(wdir, "scunet.weights")
+    W.write_scunet(path, 0)
+    m = iec.Scunet(path, device=torch.cuda.current_device())
+    img = torch.from_numpy(W.scunet_input(768, 512, 0)).cuda()
+    res = torch.empty_like(img)
+    t = time_device(lambda: m.run_device(img.data_ptr(), 768, 512, res.data_ptr(), sptr), stream)
+    out["scunet_768x512"] = {"workload": "SCUNet 3x512x768 (single-image configuration)", "value": 768 * 512 / 1e6 / t,
+                             "unit": "MP/s", "ms": t * 1e3, "gflop": 899.58,
+                             "tflops_achieved": 899.58e9 / t / 1e12}
+    m.close()
+    return out
+
+
 def config(args, chunk):
     return {"workload": f"realesrgan_x4v3 batch of {args.batch} x 3x256x384 (sharded batch), split by image",
             "model": "Real-ESRGAN general-x4v3 (SRVGGNetCompact, 34 conv3x3), seeded random-init weights",
@@ -200,6 +237,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     ap.add_argument("--no-tiles", action="store_true", help="skip the large-image tiles leg")
+    ap.add_argument("--no-models", action="store_true", help="skip the other models' single-image legs")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()
@@ -356,6 +394,12 @@ def main():
         single = {"workload": "realesrgan_x4v3 one 3x256x384 image (single-image configuration)", "value": OUT_MP / t1,
                   "unit": "MP/s", "ms": t1 * 1e3}
 
+    # The other models' single-image configurations on one GPU (rank 0 at
+    # N = 1), device-resident, CUDA events on the launch stream.
+    per_model_extra = {}
+    if rank == 0 and world == 1 and not args.no_models:
+        per_model_extra.update(other_models(wdir, stream, sptr, args))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_sample(weights_path)
@@ -384,7 +428,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps * world,
             "clocks": clocks,
             "sharded_tiles": tiles_leg,
-            "per_model": {"realesrgan_single_image": single},
+            "per_model": {"realesrgan_single_image": single, **per_model_extra},
         }
         print(json.dumps(line), flush=True)
     model.close()

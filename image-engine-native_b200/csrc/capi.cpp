@@ -296,6 +296,21 @@ iec_status iec_scunet_run_float_tiled(iec_scunet* model, const float* image, siz
   return scunet_host(model, image, false, width, height, false, tile, margin, out, progress, user);
 }
 
+iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t width, size_t height, float* out,
+                                 void* stream) {
+  return guard([&] {
+    need(model, "model");
+    need(image, "image");
+    need(out, "out");
+    check_scunet_size(width, height);
+    Scunet& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run_region(image, false, out, false, (int)width, (int)height, 0, 0, (int)width, (int)height, 0, 0, (int)width,
+                 (int)height, nullptr, s);
+  });
+}
+
 iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, size_t height, uint8_t* out,
                           iec_progress_fn progress, void* user) {
   return scunet_host(model, rgb, true, width, height, false, Scunet::TILE, Scunet::MARGIN, out, progress, user);

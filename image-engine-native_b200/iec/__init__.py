@@ -79,6 +79,7 @@ def lib():
         L.iec_scunet_run_float.argtypes = [vp, f32p, sz, sz, f32p]
         L.iec_scunet_run_float_tiled.argtypes = [vp, f32p, sz, sz, sz, sz, f32p, PROGRESS, vp]
         L.iec_scunet_run.argtypes = [vp, u8p, sz, sz, u8p, PROGRESS, vp]
+        L.iec_scunet_run_device.argtypes = [vp, vp, sz, sz, vp, vp]
         L.iec_realesrgan_set_timing.argtypes = [vp, sz]
         L.iec_realesrgan_timing.argtypes = [vp, ctypes.POINTER(ctypes.c_int), f32p, sz]
         L.iec_realesrgan_timing.restype = sz
@@ -288,6 +289,10 @@ class Scunet:
         _check(lib().iec_scunet_run_float_tiled(self._h, _f32(image), w, h, tile, min(margin, 2**64 - 1), _f32(out),
                                                 _progress(progress), None))
         return out
+
+    def run_device(self, image_ptr: int, width: int, height: int, out_ptr: int, stream: int = 0):
+        """run_float on device pointers, queued on `stream`."""
+        _check(lib().iec_scunet_run_device(self._h, image_ptr, width, height, out_ptr, stream or None))
 
     def run(self, rgb: np.ndarray, progress=None) -> np.ndarray:
         rgb = np.ascontiguousarray(rgb, np.uint8)

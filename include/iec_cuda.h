@@ -188,6 +188,12 @@ iec_status iec_scunet_run_float_tiled(iec_scunet* model, const float* image, siz
 iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, size_t height,
                           uint8_t* out, iec_progress_fn progress, void* user);
 
+/* Model::run_float on DEVICE pointers of the model's device (width x height
+ * x 3 floats in and out); queued on `stream` (NULL: the model's stream), no
+ * wait. */
+iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t width, size_t height,
+                                 float* out, void* stream);
+
 /* Diagnostics (no counterpart in the reference): one launch of the general
  * GEMM on host arrays. conv = 0: `a` rows_or_h x k, `weights` k x n; conv = 1:
  * `a` rows_or_h x w x k, `weights` 9k x n (3x3, zero padding). act 0 none,

@@ -68,6 +68,8 @@ def lib():
         ]
         L.refcpu_attention.argtypes = [_f32p, sz, sz, _f32p, sz, _f32p]
         L.refcpu_layer_norm.argtypes = [_f32p, sz, sz, _f32p, _f32p]
+        L.refcpu_gelu.argtypes = [_f32p, sz]
+        L.refcpu_sigmoid.argtypes = [_f32p, sz]
         L.refcpu_set_threads.argtypes = [ctypes.c_int]
         L.refcpu_set_direct.argtypes = [ctypes.c_int]
         _lib = L
@@ -229,4 +231,16 @@ def layer_norm(x, gamma, beta):
     g = np.ascontiguousarray(gamma, np.float32)
     b = np.ascontiguousarray(beta, np.float32)
     _check(lib().refcpu_layer_norm(_ptr(x), x.shape[0], x.shape[1], _ptr(g), _ptr(b)))
+    return x
+
+
+def gelu(x):
+    x = np.array(x, np.float32, copy=True)
+    lib().refcpu_gelu(_ptr(x), x.size)
+    return x
+
+
+def sigmoid(x):
+    x = np.array(x, np.float32, copy=True)
+    lib().refcpu_sigmoid(_ptr(x), x.size)
     return x

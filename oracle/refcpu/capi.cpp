@@ -149,6 +149,12 @@ int refcpu_scunet_run_tiled(void* h, const float* image, size_t width, size_t he
 int refcpu_attention(const float* qkv, size_t c, size_t head, const float* bias, size_t tokens, float* out) {
   return guard([&] { attention(qkv, c, head, bias, tokens, out); });
 }
+void refcpu_gelu(float* x, size_t n) {
+  for (size_t i = 0; i < n; i++) x[i] = gelu_one(x[i]);
+}
+void refcpu_sigmoid(float* x, size_t n) {
+  for (size_t i = 0; i < n; i++) x[i] = sigmoid_one(x[i]);
+}
 int refcpu_layer_norm(float* x, size_t rows, size_t n, const float* gamma, const float* beta) {
   return guard([&] {
     for (size_t r = 0; r < rows; r++) layer_norm_row(x + r * n, n, gamma, beta);
