@@ -238,6 +238,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     ap.add_argument("--no-tiles", action="store_true", help="skip the large-image tiles leg")
     ap.add_argument("--no-models", action="store_true", help="skip the other models' single-image legs")
+    ap.add_argument("--profile-models", action="store_true",
+                    help="run only the other models' single-image legs (for profiler launch lists)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()
@@ -272,6 +274,11 @@ def main():
     batch = args.batch
     assert batch % world == 0
     count = batch // world
+
+    if args.profile_models:
+        stream = torch.cuda.Stream()
+        print(json.dumps(other_models(wdir, stream, stream.cuda_stream, args)), flush=True)
+        return
 
     model = iec.RealEsrgan(weights_path, device=local, batch_chunk=args.chunk)
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)

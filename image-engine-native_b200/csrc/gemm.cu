@@ -54,7 +54,7 @@ void dispatch(Device& dev, int bn, int kb, const CUtensorMap& map, const GemmPar
   IEC_GEMM_CASE(256, KB_)
   IEC_GEMM_BN(64)
   IEC_GEMM_BN(32)
-  if (AMODE == A_CONV3) {
+  if (AMODE == A_TAPS) {
     IEC_GEMM_BN(16)
   }
 #undef IEC_GEMM_BN
@@ -72,6 +72,8 @@ void fill_out(GemmParams& p, const GemmOutSpec& o) {
   p.shift = o.shift;
   p.dbl_w = o.dbl_w;
   p.dbl_cout = o.dbl_cout;
+  p.phase_y = o.phase_y;
+  p.phase_x = o.phase_x;
 }
 
 }  // namespace
@@ -140,16 +142,36 @@ void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long 
 
 void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map_ptr, long long map_plane_elems, int h, int w,
                 int act, const GemmOutSpec& out, cudaStream_t s) {
-  if (pw.taps != 9) throw Error(ERR_INPUT, "gemm_conv3 needs 3x3 weights");
-  if (w % 8 != 0 || w < 8 || h < 8) throw Error(ERR_INPUT, "3x3 GEMM maps must be at least 8 x 8, width a multiple of 8");
-  const int kg = pw.kb / 8;
+  std::vector<Tap> taps;
+  for (int t = 0; t < 9; t++) taps.push_back({t / 3 - 1, t % 3 - 1, 0});
+  TapSource src{map_ptr, map_plane_elems, w, h, 1};
+  gemm_taps(dev, pw, src, taps, h, w, act, out, s);
+}
+
+void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const std::vector<Tap>& taps, int h, int w,
+               int act, const GemmOutSpec& out, cudaStream_t s) {
+  if (pw.taps != (int)taps.size() || taps.size() > (size_t)GEMM_MAX_TAPS)
+    throw Error(ERR_INPUT, "tap table does not match the weights");
+  if (w % 8 != 0 || w < 8 || h < 8) throw Error(ERR_INPUT, "convolution outputs must be at least 8 x 8, width a multiple of 8");
   const int tw = w >= 16 ? 16 : 8;
+  if (src.w < tw || src.h < 8) throw Error(ERR_INPUT, "convolution source smaller than a tile");
+  const int kg = pw.kb / 8;
   CUtensorMap map;
-  const uint64_t dims[4] = {(uint64_t)w * 8, (uint64_t)h, (uint64_t)pw.k / 8, 1};
-  const uint64_t strides[3] = {(uint64_t)w * 16, (uint64_t)map_plane_elems * 2, (uint64_t)map_plane_elems * 2 * (pw.k / 8)};
-  const uint32_t box[4] = {(uint32_t)tw * 8, 8, (uint32_t)kg, 1};
-  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, map_ptr, dims, strides, box);
+  const uint64_t phase_bytes = (uint64_t)src.w * src.h * 16;
+  const uint64_t dims[5] = {(uint64_t)src.w * 8, (uint64_t)src.h, (uint64_t)src.phases, (uint64_t)pw.k / 8, 1};
+  const uint64_t strides[4] = {(uint64_t)src.w * 16, phase_bytes, (uint64_t)src.plane_elems * 2,
+                               (uint64_t)src.plane_elems * 2 * (pw.k / 8)};
+  const uint32_t box[5] = {(uint32_t)tw * 8, 8, 1, (uint32_t)kg, 1};
+  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, src.ptr, dims, strides, box);
   GemmParams p{};
+  p.taps = (int)taps.size();
+  for (size_t t = 0; t < taps.size(); t++) {
+    p.dy[t] = (signed char)taps[t].dy;
+    p.dx[t] = (signed char)taps[t].dx;
+    p.phase[t] = (signed char)taps[t].phase;
+  }
+  p.phase_y = out.phase_y;
+  p.phase_x = out.phase_x;
   p.M = h * w;
   p.N = pw.n;
   p.K = pw.k;
@@ -169,7 +191,7 @@ void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map_ptr, lon
   fill_out(p, out);
   p.dev_err = dev.dev_err();
   if (p.tiles >= (1 << 24) || p.tiles_w >= (1 << 16)) throw Error(ERR_INPUT, "GEMM too large for one launch");
-  dispatch<A_CONV3>(dev, pw.bn, pw.kb, map, p, s);
+  dispatch<A_TAPS>(dev, pw.bn, pw.kb, map, p, s);
 }
 
 // ---------------------------------------------------------- bandwidth kernels

@@ -31,7 +31,27 @@ struct GemmOutSpec {
   int plane0 = 0;              // destination plane of column 0
   int map_h = 0, map_w = 0, shift = 0;  // OUT_WINDOW_ACCUM
   int dbl_w = 0, dbl_cout = 0;          // OUT_DOUBLE
+  int phase_y = 0, phase_x = 0;         // OUT_PHASE
 };
+
+// One tap of a convolution: the source pixel (y + dy, x + dx) of phase
+// `phase` for output pixel (y, x).
+struct Tap {
+  int dy, dx, phase;
+};
+
+// A convolution's source: planar f16, `phases` images of w x h pixels one
+// after another in every plane ([k / 8][phases][h][w][8]).
+struct TapSource {
+  const __half* ptr;
+  long long plane_elems;  // elements between channel-group planes
+  int w, h, phases;
+};
+
+// out (h x w pixels) = act(sum over taps and channels + bias), the taps'
+// weights row-major in tap order (pw packed with taps = taps.size()).
+void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const std::vector<Tap>& taps, int h, int w,
+               int act, const GemmOutSpec& out, cudaStream_t s);
 
 // out = act(A x W + bias) over `m` rows of the planar input `a` (k / 8
 // planes of a_plane_elems / 8 >= max(m, 128) rows each; m a multiple of 16).

@@ -14,9 +14,15 @@
 // core-matrix layout [k-group][128 rows][8] that tcgen05 reads directly:
 //   A_ROWS   128 consecutive rows: a 3-D box {16 rows x 8 channels, 8 blocks of
 //            16 rows, KB/8 groups} (256-byte inner runs).
-//   A_CONV3  a tile of 8 map rows x TW pixels (TW = 16, or the map width when
-//            it is 8): per tap (ky, kx) a 4-D box of the map shifted by
-//            (ky - 1, kx - 1) (zero fill outside the map), K = 9 taps x cin.
+//   A_TAPS   a tile of 8 output rows x TW pixels (TW = 16, or 8 for 8-wide
+//            outputs): per tap t a 5-D box of the source map, phase
+//            phase[t], shifted by (dy[t], dx[t]) from the tile (zero fill
+//            outside the map), K = taps x cin. A 3x3 zero-padded convolution
+//            is 9 taps of offsets -1..1 over the map itself; a reflect-padded
+//            one reads a map padded beforehand with offsets 0..k-1; a stride-2
+//            one reads the four space-to-depth phases of the (padded) map;
+//            one output phase of a stride-2 transposed convolution reads
+//            offsets 0..1 (gemm.rs:274-286 Taps, lama network.rs:271-333).
 // B-tiles (weights) are pre-arranged on the host per (N tile, K step) as the
 // core-matrix image [KB/8][BN][8] and brought in by one cp.async.bulk.
 //
@@ -32,6 +38,9 @@
 //   OUT_DOUBLE       2x2 stride-2 transposed convolution: column q cout + o of
 //                    input pixel (y, x) -> output pixel (2y + q / 2, 2x + q % 2),
 //                    channel o (crates/scunet-native/src/network.rs:446-478)
+//   OUT_PHASE        one output phase (py, px) of a stride-2 transposed
+//                    convolution: row (y, x) -> output pixel (2y + py, 2x + px)
+// When accumulating, the activation applies after the add, as multiply does.
 // All waits are bounded as in conv3x3_sm100.cuh.
 #pragma once
 
@@ -43,20 +52,24 @@
 
 namespace iec {
 
-enum GemmA { A_ROWS = 0, A_CONV3 = 1 };
-enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3 };
-enum GemmAct { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2 };
+enum GemmA { A_ROWS = 0, A_TAPS = 1 };
+enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3, OUT_PHASE = 4 };
+enum GemmAct { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_SIGMOID = 3 };
 
 constexpr int GEMM_EPI_WARPS = 8;
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
+constexpr int GEMM_MAX_TAPS = 49;
 
 struct GemmParams {
-  int M;                    // output rows (A_ROWS) or map pixels H * W (A_CONV3)
+  int M;                    // output rows (A_ROWS) or output pixels H * W (A_TAPS)
   int N, K;                 // output columns; reduction per tap (channels)
-  int H, W, TW;             // A_CONV3: map size, tile width (16, or 8 for 8-wide maps)
+  int H, W, TW;             // A_TAPS: output size, tile width (16, or 8 for 8-wide outputs)
   int tiles_m, tiles_n, tiles, tiles_w;
   FastDiv div_tiles_n, div_tiles_w;
-  int ksteps;               // K steps of KB channels (A_CONV3: 9 taps x K / KB)
+  int ksteps;               // K steps of KB channels (A_TAPS: taps x K / KB)
+  int taps;
+  signed char dy[GEMM_MAX_TAPS], dx[GEMM_MAX_TAPS], phase[GEMM_MAX_TAPS];
+  int phase_y, phase_x;     // OUT_PHASE
   const uint16_t* b;        // [n tile][k step][KB / 8][BN][8] f16
   const float* bias;        // [N] or null
   int act;
@@ -87,6 +100,11 @@ struct GemmSmem {
 __device__ __forceinline__ float gemm_act(float v, int act) {
   if (act == ACT_RELU) return v > 0.0f ? v : 0.0f;
   if (act == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  if (act == ACT_SIGMOID) {
+    // math.rs:33-39: from exp(-|x|), so that neither tail cancels.
+    const float e = expf(-fabsf(v)), s = e / (e + 1.0f);
+    return v > 0.0f ? 1.0f - s : s;
+  }
   return v;
 }
 
@@ -144,7 +162,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
         const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
         int x0 = 0, y0 = 0;
-        if (AMODE == A_CONV3) {
+        if (AMODE == A_TAPS) {
           y0 = (int)p.div_tiles_w.div((uint32_t)mt);
           x0 = (mt - y0 * p.tiles_w) * p.TW;
           y0 *= 8;
@@ -162,7 +180,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           } else {
             const int per_tap = p.K / KB;
             const int tap = ks / per_tap, kb = ks - tap * per_tap;
-            tma_load_4d(st, &a_map, &full[s], (x0 + tap % 3 - 1) * 8, y0 + tap / 3 - 1, kb * KG, 0);
+            tma_load_5d(st, &a_map, &full[s], (x0 + p.dx[tap]) * 8, y0 + p.dy[tap], p.phase[tap], kb * KG, 0);
           }
           bulk_load(st + L::A_BYTES, bsrc + (size_t)ks * L::B_BYTES, L::B_BYTES, &full[s]);
           issued[s] = (int)phase;
@@ -260,7 +278,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int e = 0; e < 16; e++) {
           float x = __uint_as_float(r[e]);
           if (p.bias) x += p.bias[n0 + e < p.N ? n0 + e : 0];
-          v[e] = gemm_act(x, p.act);
+          v[e] = x;
         }
 #pragma unroll
         for (int g = 0; g < 2; g++) {
@@ -272,6 +290,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int iy = m / p.dbl_w, ix = m - iy * p.dbl_w;
             const long long op = (long long)(2 * iy + (q >> 1)) * (2 * p.dbl_w) + 2 * ix + (q & 1);
             dst = p.out + (long long)(p.out_plane0 + o / 8) * p.out_plane_elems + op * 8;
+          } else if (p.out_mode == OUT_PHASE) {
+            const int iy = m / p.W, ix = m - iy * p.W;
+            const long long op = (long long)(2 * iy + p.phase_y) * (2 * p.W) + 2 * ix + p.phase_x;
+            dst = p.out + (long long)(p.out_plane0 + n / 8) * p.out_plane_elems + op * 8;
           } else {
             dst = p.out + (long long)(p.out_plane0 + n / 8) * p.out_plane_elems + dest * 8;
           }
@@ -288,6 +310,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               w8[2 * e + 1] += f.y;
             }
           }
+#pragma unroll
+          for (int e = 0; e < 8; e++) w8[e] = gemm_act(w8[e], p.act);
           uint32_t packed[4];
 #pragma unroll
           for (int e = 0; e < 4; e++) {
