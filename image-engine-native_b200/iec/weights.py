@@ -152,3 +152,84 @@ def scunet_input(width: int, height: int, seed: int = 0) -> np.ndarray:
     base = rng.random((height, width, 3))
     noisy = base + rng.standard_normal((height, width, 3)) * (25.0 / 255.0)
     return np.clip(noisy, 0.0, 1.0).astype(np.float32)
+
+
+# crates/lama-native/src/network.rs:271 PHASE_TAPS: the (input offset, kernel
+# tap) pairs one output phase of a 3x3 stride-2 transposed convolution reads
+# along an axis.
+LAMA_PHASE_TAPS = [[(0, 1)], [(0, 2), (1, 0)]]
+
+
+def lama_phase_matrices(weight: np.ndarray):
+    """A ConvTranspose2d weight [cin, cout, 3, 3] as the four phase matrices
+    of tools/lama/export_weights.py:146-152: phase 2 py + px stacks the cin x
+    cout slices of its taps, y-major."""
+    out = []
+    for phase in range(4):
+        ys, xs = LAMA_PHASE_TAPS[phase // 2], LAMA_PHASE_TAPS[phase % 2]
+        out.append(np.concatenate([weight[:, :, ky, kx] for _, ky in ys for _, kx in xs]))
+    return out
+
+
+def lama_tensors(seed: int = 0, branch_gain: float = 0.1, tail_gain: float = 0.3):
+    """Big LaMa tensors as crates/lama-native/src/network.rs:151-171,280-297,
+    381-403 load them: matrices f16 (export --half), biases f32. Batch norms
+    are folded in the exported file, so the generator draws the folded
+    matrices directly: convolutions He-normal (std sqrt(2 / fan_in)), biases
+    U(+-0.05); the three layers that end the second convolution of each
+    residual block (ffc1 local, cross, spectral_out) are scaled by
+    `branch_gain` so that 18 residual additions of ReLU outputs stay of order
+    one, and the last layer by `tail_gain` so that the sigmoid stays off its
+    tails. The transposed convolutions are drawn as [cin, cout, 3, 3]
+    weights and split into their phases with one shared bias."""
+    rng = np.random.default_rng(seed)
+    tensors = []
+    half = lambda a: a.astype(np.float16).astype(np.float32)  # noqa: E731
+
+    def mat(name, k, n, fan_in=None, bias=True, gain=1.0):
+        w = rng.standard_normal((k, n)) * np.sqrt(2.0 / (fan_in or k)) * gain
+        tensors.append((f"{name}.weight", half(w), True))
+        if bias:
+            tensors.append((f"{name}.bias", rng.uniform(-0.05, 0.05, n).astype(np.float32), False))
+
+    mat("first", 49 * 4, 64)
+    for i, (cin, cout) in enumerate([(64, 128), (128, 256), (256, 512)]):
+        mat(f"down{i}", 9 * cin, cout)
+    for b in range(18):
+        for f in range(2):
+            g = branch_gain if f == 1 else 1.0
+            name = f"block{b}.ffc{f}"
+            mat(f"{name}.local", 9 * 512, 128, gain=g)
+            mat(f"{name}.cross", 9 * 128, 384, gain=g)
+            mat(f"{name}.spectral_in", 384, 192)
+            mat(f"{name}.fourier", 384, 384)
+            mat(f"{name}.spectral_out", 192, 384, bias=False, gain=g)
+    for i, (cin, cout) in enumerate([(512, 256), (256, 128), (128, 64)]):
+        w = rng.standard_normal((cin, cout, 3, 3)) * np.sqrt(2.0 / (cin * 9 / 4))
+        bias = rng.uniform(-0.05, 0.05, cout).astype(np.float32)
+        for p, m in enumerate(lama_phase_matrices(w)):
+            tensors.append((f"up{i}.phase{p}.weight", half(m), True))
+            tensors.append((f"up{i}.phase{p}.bias", bias, False))
+    mat("last", 49 * 64, 3, gain=tail_gain)
+    return tensors
+
+
+def write_lama(path, seed: int = 0) -> str:
+    return write(path, MAGIC["lama"], lama_tensors(seed))
+
+
+def lama_input(width: int, height: int, seed: int = 0, cover: float = 0.3):
+    """A seeded inpainting input: RGB uniform [0, 1) (height x width x 3,
+    float32) and a binary mask (height x width, 1 = fill) of random
+    rectangles, each up to a quarter of each side, added until they cover
+    `cover` of the image."""
+    rng = np.random.default_rng(seed)
+    image = rng.random((height, width, 3), dtype=np.float32)
+    mask = np.zeros((height, width), np.float32)
+    while mask.mean() < cover:
+        rh = int(rng.integers(1, max(2, height // 4 + 1)))
+        rw = int(rng.integers(1, max(2, width // 4 + 1)))
+        y = int(rng.integers(0, height - rh + 1))
+        x = int(rng.integers(0, width - rw + 1))
+        mask[y:y + rh, x:x + rw] = 1.0
+    return image, mask

@@ -66,6 +66,13 @@ def lib():
         L.refcpu_scunet_run_tiled.argtypes = [
             ctypes.c_void_p, _f32p, sz, sz, sz, sz, _f32p, PROGRESS, ctypes.c_void_p,
         ]
+        L.refcpu_lama_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        L.refcpu_lama_free.argtypes = [ctypes.c_void_p]
+        L.refcpu_lama_run_float.argtypes = [
+            ctypes.c_void_p, _f32p, _f32p, sz, sz, _f32p, PROGRESS, ctypes.c_void_p,
+        ]
+        L.refcpu_rfft2.argtypes = [_f32p, sz, sz, sz, _f32p]
+        L.refcpu_irfft2_add.argtypes = [_f32p, sz, sz, sz, _f32p]
         L.refcpu_attention.argtypes = [_f32p, sz, sz, _f32p, sz, _f32p]
         L.refcpu_layer_norm.argtypes = [_f32p, sz, sz, _f32p, _f32p]
         L.refcpu_gelu.argtypes = [_f32p, sz]
@@ -216,6 +223,63 @@ class Scunet:
         cb = PROGRESS(lambda f, _u: int(bool(progress(f)))) if progress else PROGRESS()
         _check(lib().refcpu_scunet_run_tiled(self._h, _ptr(image), w, h, tile, margin, _ptr(out), cb, None))
         return out
+
+
+class Lama:
+    """The reference's CPU Big LaMa (Model::load_cpu) as restated."""
+
+    MIN_SIDE = 9
+    STEPS = 26
+
+    def __init__(self, path):
+        self._h = ctypes.c_void_p()
+        _check(lib().refcpu_lama_load(os.fsencode(path), ctypes.byref(self._h)))
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.refcpu_lama_free(self._h)
+            self._h = None
+
+    def run_float(self, image: np.ndarray, mask: np.ndarray, progress=None) -> np.ndarray:
+        """lib.rs:163-172: the prediction for every pixel (image h x w x 3,
+        mask h x w, both in 0..=1)."""
+        image = np.ascontiguousarray(image, np.float32)
+        mask = np.ascontiguousarray(mask, np.float32)
+        h, w, _ = image.shape
+        if mask.shape != (h, w):
+            raise ValueError("mask shape")
+        out = np.empty((h, w, 3), np.float32)
+        cb = PROGRESS(lambda f, _u: int(bool(progress(f)))) if progress else PROGRESS()
+        _check(lib().refcpu_lama_run_float(self._h, _ptr(image), _ptr(mask), w, h, _ptr(out), cb, None))
+        return out
+
+    def run(self, rgb: np.ndarray, mask: np.ndarray) -> np.ndarray:
+        """lib.rs:128-160: 8-bit image with the pixels where `mask` (u8) is
+        non-zero filled from the prediction."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        mask = np.ascontiguousarray(mask, np.uint8)
+        pred = self.run_float(rgb.astype(np.float32) / np.float32(255.0), (mask != 0).astype(np.float32))
+        v = (np.clip(pred, np.float32(0.0), np.float32(1.0)) * np.float32(255.0)).astype(np.float64)
+        fill = np.floor(v + 0.5).astype(np.uint8)  # f32::round: half away from zero
+        out = rgb.copy()
+        out[mask != 0] = fill[mask != 0]
+        return out
+
+
+def rfft2(x, h, w, c):
+    """fourier.rs forward: ortho rfft2 of an h x w x c map; h x (w/2+1) x 2c."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty((h, w // 2 + 1, 2 * c), np.float32)
+    _check(lib().refcpu_rfft2(_ptr(x), h, w, c, _ptr(out)))
+    return out
+
+
+def irfft2_add(spec, h, w, c, out):
+    """fourier.rs inverse: adds the ortho inverse of `spec` onto `out`."""
+    spec = np.ascontiguousarray(spec, np.float32)
+    out = np.array(out, np.float32, copy=True, order="C")
+    _check(lib().refcpu_irfft2_add(_ptr(spec), h, w, c, _ptr(out)))
+    return out
 
 
 def attention(qkv, c, head, bias, tokens):

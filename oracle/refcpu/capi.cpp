@@ -145,6 +145,40 @@ int refcpu_scunet_run_tiled(void* h, const float* image, size_t width, size_t he
   });
 }
 
+// ------------------------------------------------------------------------ LaMa
+int refcpu_lama_load(const char* path, void** out) {
+  return guard([&] { *out = new Lama(path); });
+}
+void refcpu_lama_free(void* h) { delete static_cast<Lama*>(h); }
+
+// Model::run_float: the prediction for every pixel (`out` width x height x 3).
+int refcpu_lama_run_float(void* h, const float* image, const float* mask, size_t width, size_t height, float* out,
+                          refcpu_progress_fn cb, void* user) {
+  return guard([&] {
+    Lama::check_size(width * height * 3, width * height, width, height);
+    size_t done = 0;
+    std::function<bool()> step;
+    if (cb) step = [&] { return cb((float)++done / (float)Lama::STEPS, user) == 0; };
+    std::vector<float> r = static_cast<Lama*>(h)->run(image, mask, width, height, step);
+    std::memcpy(out, r.data(), r.size() * sizeof(float));
+  });
+}
+
+// fourier.rs forward / inverse (the inverse adds onto `out`).
+int refcpu_rfft2(const float* x, size_t h, size_t w, size_t c, float* out) {
+  return guard([&] {
+    std::vector<float> s;
+    rfft2(x, c, h, w, c, s);
+    std::memcpy(out, s.data(), s.size() * sizeof(float));
+  });
+}
+int refcpu_irfft2_add(const float* spec, size_t h, size_t w, size_t c, float* out) {
+  return guard([&] {
+    std::vector<float> s(spec, spec + h * (w / 2 + 1) * 2 * c);
+    irfft2_add(s, h, w, c, out, c);
+  });
+}
+
 // The engine's window attention and layer norm, for the kernels' unit tests.
 int refcpu_attention(const float* qkv, size_t c, size_t head, const float* bias, size_t tokens, float* out) {
   return guard([&] { attention(qkv, c, head, bias, tokens, out); });

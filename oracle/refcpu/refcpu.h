@@ -45,4 +45,28 @@ class Scunet {
   Impl* impl_;
 };
 
+// crates/lama-native/src/network.rs + fourier.rs + lib.rs (see lama.cpp).
+class Lama {
+ public:
+  static constexpr size_t MIN_SIDE = 9, STEPS = 26;
+  explicit Lama(const std::string& path);
+  ~Lama();
+  // lib.rs:174-194 check_size.
+  static void check_size(size_t image, size_t mask, size_t width, size_t height);
+  // network.rs:405-488: the prediction for every pixel, `step` after each of
+  // the 26 steps (false = cancel).
+  std::vector<float> run(const float* image, const float* mask, size_t width, size_t height,
+                         const std::function<bool()>& step) const;
+  struct Impl;
+
+ private:
+  Impl* impl_;
+};
+
+// fourier.rs: the ortho rfft2 of an h x w map of c channels (pixel p at
+// x[p * stride]) into rows of h x (w / 2 + 1) pixels [re(c) | im(c)], and
+// the ortho inverse added onto `out`.
+void rfft2(const float* x, size_t stride, size_t h, size_t w, size_t c, std::vector<float>& out);
+void irfft2_add(const std::vector<float>& spec, size_t h, size_t w, size_t c, float* out, size_t stride);
+
 }  // namespace ref
