@@ -199,7 +199,18 @@ def time_device(fn, stream, warmup=3, iters=10):
 
 
 def other_models(wdir, stream, sptr, args):
-    """SCUNet 3x512x768 (seeded f16 weights), device-resident."""
+    """SCUNet 3x512x768 and Big LaMa 4x512x512 (seeded f16 weights),
+    device-resident; LaMa also through the host entry point."""
+    out = {}
+    only = set(args.models.split(","))
+    if "scunet" in only:
+        out.update(scunet_leg(wdir, stream, sptr))
+    if "lama" in only:
+        out.update(lama_leg(wdir, stream, sptr))
+    return out
+
+
+def scunet_leg(wdir, stream, sptr):
     import torch
 
     import iec
@@ -215,6 +226,34 @@ def other_models(wdir, stream, sptr, args):
     out["scunet_768x512"] = {"workload": "SCUNet 3x512x768 (single-image configuration)", "value": 768 * 512 / 1e6 / t,
                              "unit": "MP/s", "ms": t * 1e3, "gflop": 899.58,
                              "tflops_achieved": 899.58e9 / t / 1e12}
+    m.close()
+    return out
+
+
+def lama_leg(wdir, stream, sptr):
+    """Big LaMa 512 x 512, about 30 % masked (seeded f16 weights and rectangles)."""
+    import torch
+
+    import iec
+    from iec import weights as W
+
+    out = {}
+    path = os.path.join(wdir, "lama.weights")
+    W.write_lama(path, 0)
+    m = iec.Lama(path, device=torch.cuda.current_device())
+    image, mask = W.lama_input(512, 512, 0)
+    img = torch.from_numpy(image).cuda()
+    msk = torch.from_numpy(mask).cuda()
+    res = torch.empty_like(img)
+    t = time_device(lambda: m.run_device(img.data_ptr(), msk.data_ptr(), 512, 512, res.data_ptr(), sptr), stream)
+    m.run_float(image, mask)
+    t0 = time.perf_counter()
+    for _ in range(5):
+        m.run_float(image, mask)
+    te = (time.perf_counter() - t0) / 5
+    out["lama_512x512"] = {"workload": "Big LaMa 4x512x512 (single-image configuration)", "value": 512 * 512 / 1e6 / t,
+                           "unit": "MP/s", "ms": t * 1e3, "gflop": 439.8, "tflops_achieved": 439.8e9 / t / 1e12,
+                           "e2e_ms": te * 1e3, "e2e_value": 512 * 512 / 1e6 / te}
     m.close()
     return out
 
@@ -240,6 +279,7 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the other models' single-image legs")
     ap.add_argument("--profile-models", action="store_true",
                     help="run only the other models' single-image legs (for profiler launch lists)")
+    ap.add_argument("--models", default="scunet,lama", help="which single-image legs run (comma list)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()

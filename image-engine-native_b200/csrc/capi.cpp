@@ -10,6 +10,7 @@
 
 #include "../../include/iec_cuda.h"
 #include "realesrgan.h"
+#include "lama.h"
 #include "scunet.h"
 
 using namespace iec;
@@ -63,13 +64,40 @@ void need(const void* p, const char* what) {
 
 }  // namespace
 
+// Each handle carries a tag, so that a handle of one model passed where
+// another's is expected fails with IEC_ERR_INPUT instead of being used.
 struct iec_realesrgan {
+  static constexpr uint32_t TAG = 0x52455347;  // "RESG"
+  uint32_t tag = TAG;
   std::unique_ptr<RealEsrgan> model;
+  ~iec_realesrgan() { tag = 0; }
 };
 
 struct iec_scunet {
+  static constexpr uint32_t TAG = 0x53434e54;  // "SCNT"
+  uint32_t tag = TAG;
   std::unique_ptr<Scunet> model;
+  ~iec_scunet() { tag = 0; }
 };
+
+struct iec_lama {
+  static constexpr uint32_t TAG = 0x4c414d41;  // "LAMA"
+  uint32_t tag = TAG;
+  std::unique_ptr<Lama> model;
+  ~iec_lama() { tag = 0; }
+};
+
+namespace {
+template <class H>
+bool valid(const H* h) {
+  return h && h->tag == H::TAG && h->model;
+}
+template <class H>
+void need_model(const H* h) {
+  if (!h) throw Error(ERR_INPUT, "model is null");
+  if (!valid(h)) throw Error(ERR_INPUT, "model is not a handle of this model type");
+}
+}  // namespace
 
 extern "C" {
 
@@ -88,16 +116,18 @@ iec_status iec_realesrgan_load(const char* weights_path, const iec_options* opti
   });
 }
 
-void iec_realesrgan_free(iec_realesrgan* model) { delete model; }
+void iec_realesrgan_free(iec_realesrgan* model) {
+  if (valid(model)) delete model;
+}
 
 const char* iec_realesrgan_device_name(const iec_realesrgan* model) {
-  return model ? model->model->device().name().c_str() : "";
+  return valid(model) ? model->model->device().name().c_str() : "";
 }
 
 static iec_status run_host(iec_realesrgan* model, const void* image, bool u8, size_t width, size_t height,
                            size_t tile, size_t margin, void* out, iec_progress_fn progress, void* user) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(image, "image");
     need(out, "out");
     check_realesrgan_size(width, height);
@@ -141,7 +171,7 @@ iec_status iec_realesrgan_run(iec_realesrgan* model, const uint8_t* rgb, size_t 
 iec_status iec_realesrgan_run_float_tiles(iec_realesrgan* model, const float* image, size_t width, size_t height,
                                           size_t tile, size_t margin, size_t first, size_t last, float* out) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(image, "image");
     need(out, "out");
     check_realesrgan_size(width, height);
@@ -171,7 +201,7 @@ iec_status iec_realesrgan_run_tiles_device(iec_realesrgan* model, const float* i
                                            size_t tile, size_t margin, size_t first, size_t last, float* out,
                                            void* stream) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(image, "image");
     need(out, "out");
     check_realesrgan_size(width, height);
@@ -186,7 +216,7 @@ iec_status iec_realesrgan_run_tiles_device(iec_realesrgan* model, const float* i
 iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, size_t count, size_t width,
                                     size_t height, float* out, void* stream) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(images, "images");
     need(out, "out");
     if (count == 0) return;
@@ -201,7 +231,7 @@ iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, 
 iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images, size_t count, size_t width,
                                      size_t height, float* out, void* stream) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(images, "images");
     need(out, "out");
     if (count == 0) return;
@@ -217,7 +247,7 @@ iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images,
 iec_status iec_realesrgan_run_device_noalloc(iec_realesrgan* model, const float* images, size_t count,
                                              size_t width, size_t height, float* out, void* stream) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(images, "images");
     need(out, "out");
     if (count == 0) return;
@@ -242,10 +272,12 @@ iec_status iec_scunet_load(const char* weights_path, const iec_options* options,
   });
 }
 
-void iec_scunet_free(iec_scunet* model) { delete model; }
+void iec_scunet_free(iec_scunet* model) {
+  if (valid(model)) delete model;
+}
 
 const char* iec_scunet_device_name(const iec_scunet* model) {
-  return model ? model->model->device().name().c_str() : "";
+  return valid(model) ? model->model->device().name().c_str() : "";
 }
 
 // crates/scunet-native/src/lib.rs:256-267 (check_size).
@@ -259,7 +291,7 @@ static void check_scunet_size(size_t width, size_t height) {
 static iec_status scunet_host(iec_scunet* model, const void* image, bool u8, size_t width, size_t height, bool whole,
                               size_t tile, size_t margin, void* out, iec_progress_fn progress, void* user) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(image, "image");
     need(out, "out");
     check_scunet_size(width, height);
@@ -299,7 +331,7 @@ iec_status iec_scunet_run_float_tiled(iec_scunet* model, const float* image, siz
 iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t width, size_t height, float* out,
                                  void* stream) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     need(image, "image");
     need(out, "out");
     check_scunet_size(width, height);
@@ -316,13 +348,94 @@ iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, s
   return scunet_host(model, rgb, true, width, height, false, Scunet::TILE, Scunet::MARGIN, out, progress, user);
 }
 
+// ------------------------------------------------------------------------ LaMa
+iec_status iec_lama_load(const char* weights_path, const iec_options* options, iec_lama** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    need(weights_path, "weights_path");
+    auto h = std::make_unique<iec_lama>();
+    h->model = std::make_unique<Lama>(weights_path, to_options(options));
+    *out = h.release();
+  });
+}
+
+void iec_lama_free(iec_lama* model) {
+  if (valid(model)) delete model;
+}
+
+const char* iec_lama_device_name(const iec_lama* model) { return valid(model) ? model->model->device().name().c_str() : ""; }
+
+// crates/lama-native/src/lib.rs:180-194 (check_size), with a bound on the
+// side the Fourier transforms take.
+static void check_lama_size(size_t width, size_t height) {
+  if (width < (size_t)Lama::MIN_SIDE || height < (size_t)Lama::MIN_SIDE)
+    throw Error(ERR_INPUT, std::to_string(width) + " x " + std::to_string(height) +
+                               " image: sides of at least " + std::to_string(Lama::MIN_SIDE) + " pixels");
+  if (width > 12288 || height > 12288)
+    throw Error(ERR_INPUT, "a " + std::to_string(width) + " x " + std::to_string(height) + " image is too large");
+}
+
+static iec_status lama_host(iec_lama* model, const void* image, const void* mask, bool u8, size_t width, size_t height,
+                            void* out, iec_progress_fn progress, void* user) {
+  return guard([&] {
+    need_model(model);
+    need(image, "image");
+    need(mask, "mask");
+    need(out, "out");
+    check_lama_size(width, height);
+    Lama& m = *model->model;
+    DeviceScope scope(m.device());
+    const size_t elem = u8 ? 1 : 4, bytes = width * height * 3 * elem, mbytes = width * height * elem;
+    m.host_in.reserve(bytes);
+    m.host_mask.reserve(mbytes);
+    m.host_out.reserve(bytes);
+    cudaStream_t s = m.device().stream();
+    IEC_CUDA(cudaMemcpyAsync(m.host_in.get(), image, bytes, cudaMemcpyHostToDevice, s));
+    IEC_CUDA(cudaMemcpyAsync(m.host_mask.get(), mask, mbytes, cudaMemcpyHostToDevice, s));
+    size_t done = 0;
+    std::function<bool()> step;
+    if (progress)
+      step = [&] { return progress((float)(++done) / (float)Lama::STEPS, user) == 0; };
+    if (!m.run(m.host_in.get(), u8, m.host_mask.get(), u8, m.host_out.get(), u8, (int)width, (int)height, step, s))
+      throw Error(CANCELLED, "cancelled");
+    IEC_CUDA(cudaMemcpyAsync(out, m.host_out.get(), bytes, cudaMemcpyDeviceToHost, s));
+    m.device().sync(s);
+  });
+}
+
+iec_status iec_lama_run_float(iec_lama* model, const float* image, const float* mask, size_t width, size_t height,
+                              float* out) {
+  return lama_host(model, image, mask, false, width, height, out, nullptr, nullptr);
+}
+
+iec_status iec_lama_run(iec_lama* model, const uint8_t* rgb, const uint8_t* mask, size_t width, size_t height,
+                        uint8_t* out, iec_progress_fn progress, void* user) {
+  return lama_host(model, rgb, mask, true, width, height, out, progress, user);
+}
+
+iec_status iec_lama_run_device(iec_lama* model, const float* image, const float* mask, size_t width, size_t height,
+                               float* out, void* stream) {
+  return guard([&] {
+    need_model(model);
+    need(image, "image");
+    need(mask, "mask");
+    need(out, "out");
+    check_lama_size(width, height);
+    Lama& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run(image, false, mask, false, out, false, (int)width, (int)height, nullptr, s);
+  });
+}
+
 size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width, size_t height) {
-  return model ? model->model->launches(count, width, height) : 0;
+  return valid(model) ? model->model->launches(count, width, height) : 0;
 }
 
 iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity) {
   return guard([&] {
-    need(model, "model");
+    need_model(model);
     DeviceScope scope(model->model->device());
     model->model->set_timing(capacity);
   });
@@ -331,7 +444,7 @@ iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity) {
 size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n) {
   size_t written = 0;
   iec_status st = guard([&] {
-    need(model, "model");
+    need_model(model);
     need(kinds, "kinds");
     need(ms, "ms");
     DeviceScope scope(model->model->device());

@@ -1,0 +1,336 @@
+// LaMa's 2-D real Fourier transforms on planar f16 maps (see fft.h).
+//
+// A transform runs as two passes through an f32 scratch of row spectra, each
+// pass a batch of 1-D transforms of "lines": n points of one channel group
+// (8 channels, the 16 bytes a pixel holds in one plane), so every load and
+// store moves whole 16-byte pixel groups. A CTA holds up to 512 points
+// (several short lines, or one long one) in shared memory and transforms them
+// in place of fourier.rs's recursive mixed-radix FFT (fourier.rs:16-139):
+// radix-2 Stockham passes when n is a power of two, else the direct sum of
+// the transform's definition. Twiddles are cos / sin of 2 pi j / n computed
+// in double and rounded to f32, as fourier.rs:45-52 makes them.
+//   forward: rows  real -> complex (all n outputs, the first w/2 + 1 kept)
+//            cols  complex, times 1 / sqrt(h w), to the f16 spectrum
+//   inverse: cols  complex from the f16 spectrum
+//            rows  the Hermitian row (imaginary parts of columns 0 and w/2
+//                  dropped) -> real part, times 1 / sqrt(h w), added on x
+#include "fft.h"
+
+#include <cmath>
+#include <vector>
+
+namespace iec {
+
+namespace {
+
+constexpr int FFT_THREADS = 256;
+constexpr int FFT_POINTS = 512;   // points per CTA when lines are short
+constexpr int FFT_MAX_N = 1536;   // longest line (shared memory: 2 x 64 n bytes)
+
+struct Line {
+  int n, log2n;  // log2n < 0: not a power of two
+  const float* cos_t;
+  const float* sin_t;
+};
+
+__device__ __forceinline__ float2 cmul(float2 a, float wr, float wi) {
+  return make_float2(a.x * wr - a.y * wi, a.x * wi + a.y * wr);
+}
+
+// Transforms `lines` lines of f.n points x 8 channels held in `a`
+// ([line][n][8] complex) with `b` as the other buffer, sign -1 forward or +1
+// inverse (no scaling); returns the buffer that holds the result.
+__device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, float sign) {
+  const int n = f.n;
+  if (f.log2n >= 0) {
+    const int half = n >> 1;
+    for (int st = 0; st < f.log2n; st++) {
+      const int m = 1 << st;
+      const int total = lines * half * 8;
+      for (int t = threadIdx.x; t < total; t += blockDim.x) {
+        const int c = t & 7, r = t >> 3;
+        const int line = r / half, bf = r - line * half;
+        const int j = bf >> st;
+        const float2* src = a + (size_t)line * n * 8;
+        float2* dst = b + (size_t)line * n * 8;
+        const float2 c0 = src[bf * 8 + c], c1 = src[(bf + half) * 8 + c];
+        const float wr = __ldg(f.cos_t + j * m), wi = sign * __ldg(f.sin_t + j * m);
+        dst[(bf + j * m) * 8 + c] = make_float2(c0.x + c1.x, c0.y + c1.y);
+        dst[(bf + j * m + m) * 8 + c] = cmul(make_float2(c0.x - c1.x, c0.y - c1.y), wr, wi);
+      }
+      __syncthreads();
+      float2* tmp = a;
+      a = b;
+      b = tmp;
+    }
+    return a;
+  }
+  const int total = lines * n * 8;
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int c = t & 7, r = t >> 3;
+    const int line = r / n, k = r - line * n;
+    const float2* src = a + (size_t)line * n * 8;
+    float re = 0.0f, im = 0.0f;
+    int idx = 0;
+    for (int j = 0; j < n; j++) {
+      const float2 x = src[j * 8 + c];
+      const float wr = __ldg(f.cos_t + idx), wi = sign * __ldg(f.sin_t + idx);
+      re += x.x * wr - x.y * wi;
+      im += x.x * wi + x.y * wr;
+      idx += k;
+      if (idx >= n) idx -= n;
+    }
+    b[((size_t)line * n + k) * 8 + c] = make_float2(re, im);
+  }
+  __syncthreads();
+  return b;
+}
+
+struct Dims {
+  int h, w, half, groups, lines_rows, lines_cols;
+  float scale;
+};
+
+// One thread moves one point of a line: the 8 channels of a pixel group,
+// 16 bytes of f16 or 64 bytes of complex f32, in vector loads and stores.
+__device__ __forceinline__ void load_half8(const __half* src, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const float2 f = __half22float2(h[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store_half8(__half* dst, const float* v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    __half2 h2 = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void copy_point(float2* dst, const float2* src) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  float4 r[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) r[e] = s4[e];
+#pragma unroll
+  for (int e = 0; e < 4; e++) d4[e] = r[e];
+}
+
+// Forward rows: x (real) -> scratch row spectra.
+__global__ void __launch_bounds__(FFT_THREADS) fft_rows_fwd(const __half* __restrict__ x, long long x_plane,
+                                                           float2* __restrict__ T, Dims d, Line f) {
+  extern __shared__ float4 fft_smem4[];
+  float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
+  const int g = blockIdx.y, y0 = blockIdx.x * d.lines_rows;
+  const int lines = min(d.lines_rows, d.h - y0), n = d.w;
+  float2* a = fft_smem;
+  float2* b = fft_smem + (size_t)d.lines_rows * n * 8;
+  const __half* src = x + g * x_plane + (size_t)y0 * n * 8;
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    float v[8];
+    load_half8(src + (size_t)t * 8, v);
+#pragma unroll
+    for (int c = 0; c < 8; c++) a[(size_t)t * 8 + c] = make_float2(v[c], 0.0f);
+  }
+  __syncthreads();
+  const float2* r = fft_lines(a, b, lines, f, -1.0f);
+  for (int t = threadIdx.x; t < lines * d.half; t += blockDim.x) {
+    const int line = t / d.half, k = t - line * d.half;
+    copy_point(T + (((size_t)g * d.h + y0 + line) * d.half + k) * 8, r + ((size_t)line * n + k) * 8);
+  }
+}
+
+// Forward columns: scratch -> f16 spectrum (real planes, then imaginary).
+__global__ void __launch_bounds__(FFT_THREADS) fft_cols_fwd(const float2* __restrict__ T, __half* __restrict__ spec,
+                                                           long long spec_plane, Dims d, Line f) {
+  extern __shared__ float4 fft_smem4[];
+  float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
+  const int g = blockIdx.y, k0 = blockIdx.x * d.lines_cols;
+  const int lines = min(d.lines_cols, d.half - k0), n = d.h;
+  float2* a = fft_smem;
+  float2* b = fft_smem + (size_t)d.lines_cols * n * 8;
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    const int line = t % lines, y = t / lines;
+    copy_point(a + ((size_t)line * n + y) * 8, T + (((size_t)g * d.h + y) * d.half + k0 + line) * 8);
+  }
+  __syncthreads();
+  const float2* r = fft_lines(a, b, lines, f, -1.0f);
+  __half* re = spec + g * spec_plane;
+  __half* im = spec + (g + d.groups) * spec_plane;
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    const int line = t % lines, ky = t / lines;
+    const float2* v = r + ((size_t)line * n + ky) * 8;
+    float vr[8], vi[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      vr[c] = v[c].x * d.scale;
+      vi[c] = v[c].y * d.scale;
+    }
+    const size_t at = ((size_t)ky * d.half + k0 + line) * 8;
+    store_half8(re + at, vr);
+    store_half8(im + at, vi);
+  }
+}
+
+// Inverse columns: f16 spectrum -> scratch.
+__global__ void __launch_bounds__(FFT_THREADS) fft_cols_inv(const __half* __restrict__ spec, long long spec_plane,
+                                                           float2* __restrict__ T, Dims d, Line f) {
+  extern __shared__ float4 fft_smem4[];
+  float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
+  const int g = blockIdx.y, k0 = blockIdx.x * d.lines_cols;
+  const int lines = min(d.lines_cols, d.half - k0), n = d.h;
+  float2* a = fft_smem;
+  float2* b = fft_smem + (size_t)d.lines_cols * n * 8;
+  const __half* re = spec + g * spec_plane;
+  const __half* im = spec + (g + d.groups) * spec_plane;
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    const int line = t % lines, ky = t / lines;
+    const size_t at = ((size_t)ky * d.half + k0 + line) * 8;
+    float vr[8], vi[8];
+    load_half8(re + at, vr);
+    load_half8(im + at, vi);
+    float2* dst = a + ((size_t)line * n + ky) * 8;
+#pragma unroll
+    for (int c = 0; c < 8; c++) dst[c] = make_float2(vr[c], vi[c]);
+  }
+  __syncthreads();
+  const float2* r = fft_lines(a, b, lines, f, 1.0f);
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    const int line = t % lines, y = t / lines;
+    copy_point(T + (((size_t)g * d.h + y) * d.half + k0 + line) * 8, r + ((size_t)line * n + y) * 8);
+  }
+}
+
+// Inverse rows: scratch -> the Hermitian row -> real part, added on x.
+__global__ void __launch_bounds__(FFT_THREADS) fft_rows_inv(const float2* __restrict__ T, __half* __restrict__ x,
+                                                           long long x_plane, Dims d, Line f) {
+  extern __shared__ float4 fft_smem4[];
+  float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
+  const int g = blockIdx.y, y0 = blockIdx.x * d.lines_rows;
+  const int lines = min(d.lines_rows, d.h - y0), n = d.w;
+  float2* a = fft_smem;
+  float2* b = fft_smem + (size_t)d.lines_rows * n * 8;
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    const int line = t / n, j = t - line * n;
+    const float2* row = T + (((size_t)g * d.h + y0 + line) * d.half) * 8;
+    float2* dst = a + (size_t)t * 8;
+    if (j < d.half) {
+      copy_point(dst, row + (size_t)j * 8);
+      if (j == 0 || 2 * j == n) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) dst[c].y = 0.0f;
+      }
+    } else {
+      copy_point(dst, row + (size_t)(n - j) * 8);
+#pragma unroll
+      for (int c = 0; c < 8; c++) dst[c].y = -dst[c].y;
+    }
+  }
+  __syncthreads();
+  const float2* r = fft_lines(a, b, lines, f, 1.0f);
+  __half* dst = x + g * x_plane + (size_t)y0 * n * 8;
+  for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
+    float v[8];
+    load_half8(dst + (size_t)t * 8, v);
+#pragma unroll
+    for (int c = 0; c < 8; c++) v[c] += r[(size_t)t * 8 + c].x * d.scale;
+    store_half8(dst + (size_t)t * 8, v);
+  }
+}
+
+int log2_exact(int n) {
+  int l = 0;
+  while ((1 << l) < n) l++;
+  return (1 << l) == n ? l : -1;
+}
+
+Dims dims_of(const FourierPlan& p) {
+  Dims d;
+  d.h = p.h;
+  d.w = p.w;
+  d.half = p.half;
+  d.groups = p.channels / 8;
+  d.lines_rows = std::max(1, FFT_POINTS / p.w);
+  d.lines_cols = std::max(1, FFT_POINTS / p.h);
+  d.scale = (float)(1.0 / std::sqrt((double)p.h * (double)p.w));
+  return d;
+}
+
+Line line_of(const FourierPlan& p, bool rows) {
+  const float* t = p.twiddles.as<float>();
+  if (rows) return Line{p.w, log2_exact(p.w), t, t + p.w};
+  return Line{p.h, log2_exact(p.h), t + 2 * p.w, t + 2 * p.w + p.h};
+}
+
+size_t smem_for(int lines, int n) { return (size_t)2 * lines * n * 8 * sizeof(float2); }
+
+template <class K>
+void prepare(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) IEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
+}  // namespace
+
+void fourier_plan(FourierPlan& plan, int h, int w, int channels) {
+  if (h < 1 || w < 1 || h > FFT_MAX_N || w > FFT_MAX_N || channels % 8 != 0)
+    throw Error(ERR_INPUT, "Fourier transform of " + std::to_string(h) + " x " + std::to_string(w) +
+                               ": sides up to " + std::to_string(FFT_MAX_N));
+  plan.h = h;
+  plan.w = w;
+  plan.half = w / 2 + 1;
+  plan.channels = channels;
+  std::vector<float> t(2 * (size_t)w + 2 * (size_t)h);
+  for (int j = 0; j < w; j++) {
+    const double a = 2.0 * M_PI * j / w;
+    t[j] = (float)std::cos(a);
+    t[w + j] = (float)std::sin(a);
+  }
+  for (int j = 0; j < h; j++) {
+    const double a = 2.0 * M_PI * j / h;
+    t[2 * w + j] = (float)std::cos(a);
+    t[2 * w + h + j] = (float)std::sin(a);
+  }
+  plan.twiddles.reserve(t.size() * sizeof(float));
+  IEC_CUDA(cudaMemcpy(plan.twiddles.get(), t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
+  plan.scratch.reserve((size_t)channels / 8 * h * plan.half * 8 * sizeof(float2));
+}
+
+void rfft2_planar(const FourierPlan& plan, const __half* x, long long x_plane_elems, __half* spec,
+                  long long spec_plane_elems, cudaStream_t s) {
+  const Dims d = dims_of(plan);
+  float2* T = plan.scratch.as<float2>();
+  const size_t sr = smem_for(d.lines_rows, d.w), sc = smem_for(d.lines_cols, d.h);
+  prepare(fft_rows_fwd, sr);
+  prepare(fft_cols_fwd, sc);
+  fft_rows_fwd<<<dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s>>>(
+      x, x_plane_elems, T, d, line_of(plan, true));
+  IEC_CUDA(cudaGetLastError());
+  fft_cols_fwd<<<dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s>>>(
+      T, spec, spec_plane_elems, d, line_of(plan, false));
+  IEC_CUDA(cudaGetLastError());
+}
+
+void irfft2_add_planar(const FourierPlan& plan, const __half* spec, long long spec_plane_elems, __half* x,
+                       long long x_plane_elems, cudaStream_t s) {
+  const Dims d = dims_of(plan);
+  float2* T = plan.scratch.as<float2>();
+  const size_t sr = smem_for(d.lines_rows, d.w), sc = smem_for(d.lines_cols, d.h);
+  prepare(fft_cols_inv, sc);
+  prepare(fft_rows_inv, sr);
+  fft_cols_inv<<<dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s>>>(
+      spec, spec_plane_elems, T, d, line_of(plan, false));
+  IEC_CUDA(cudaGetLastError());
+  fft_rows_inv<<<dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s>>>(
+      T, x, x_plane_elems, d, line_of(plan, true));
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace iec

@@ -74,9 +74,41 @@ void fill_out(GemmParams& p, const GemmOutSpec& o) {
   p.dbl_cout = o.dbl_cout;
   p.phase_y = o.phase_y;
   p.phase_x = o.phase_x;
+  p.ostep = o.ostep;
+  p.dst_h = o.dst_h;
+  p.dst_w = o.dst_w;
+  p.dst_pad = o.dst_pad;
+  p.dst_split = o.dst_split;
+  p.dst_pw = o.dst_pw;
+  p.dst_ph = o.dst_ph;
+  p.acc_src = o.acc_src;
+  p.resid = o.resid;
+  if (o.mode == OUT_MAP) {
+    const MapGeom g{o.dst_h, o.dst_w, o.dst_pad, o.dst_split};
+    if (o.ostep < 1 || o.ostep > 2 || o.phase_y < 0 || o.phase_y >= o.ostep || o.phase_x < 0 ||
+        o.phase_x >= o.ostep || o.dst_pad < 0 || o.dst_pad >= o.dst_h || o.dst_pad >= o.dst_w ||
+        (o.dst_split != 1 && o.dst_split != 2) || o.dst_pw != g.pw() || o.dst_ph != g.ph() ||
+        o.plane_elems < g.plane_elems() || o.dst_w % o.ostep != 0 || o.dst_h % o.ostep != 0)
+      throw Error(ERR_INPUT, "GEMM output map geometry is inconsistent");
+  }
 }
 
 }  // namespace
+
+GemmOutSpec map_out(const MapGeom& g, __half* out, int plane0) {
+  GemmOutSpec o;
+  o.mode = OUT_MAP;
+  o.out = out;
+  o.plane_elems = g.plane_elems();
+  o.plane0 = plane0;
+  o.dst_h = g.h;
+  o.dst_w = g.w;
+  o.dst_pad = g.pad;
+  o.dst_split = g.split;
+  o.dst_pw = g.pw();
+  o.dst_ph = g.ph();
+  return o;
+}
 
 void pack_weights(PackedWeights& pw, const std::vector<float>& w, int taps, int k, int n, const float* bias) {
   pw.n = n;
@@ -113,12 +145,15 @@ void pack_weights(PackedWeights& pw, const std::vector<float>& w, int taps, int 
 void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long a_plane_elems, int m, int act,
                const GemmOutSpec& out, cudaStream_t s) {
   if (pw.taps != 1) throw Error(ERR_INPUT, "gemm_rows needs a 1x1 weight matrix");
-  if (m % 16 != 0) throw Error(ERR_INPUT, "GEMM rows must be a multiple of 16");
-  if (a_plane_elems < (long long)std::max(m, 128) * 8) throw Error(ERR_INPUT, "GEMM input planes must hold 128 rows");
+  if (m <= 0) throw Error(ERR_INPUT, "GEMM without rows");
+  const int rows = gemm_rows_alloc(m);
+  if (a_plane_elems < (long long)rows * 8) throw Error(ERR_INPUT, "GEMM input planes too short");
+  if (out.mode == OUT_MAP && (m % (out.dst_w / out.ostep) != 0 || m / (out.dst_w / out.ostep) != out.dst_h / out.ostep))
+    throw Error(ERR_INPUT, "GEMM rows do not match the output map");
   const int kg = pw.kb / 8;
   CUtensorMap map;
   // Planes hold at least 128 rows, so the 128-row box never outgrows them.
-  const uint64_t dims[3] = {128, (uint64_t)std::max(m, 128) / 16, (uint64_t)pw.k / 8};
+  const uint64_t dims[3] = {128, (uint64_t)rows / 16, (uint64_t)pw.k / 8};
   const uint64_t strides[2] = {256, (uint64_t)a_plane_elems * 2};
   const uint32_t box[3] = {128, 8, (uint32_t)kg};
   encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, a, dims, strides, box);
@@ -135,6 +170,10 @@ void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long 
   p.bias = pw.has_bias ? pw.bias.as<float>() : nullptr;
   p.act = act;
   fill_out(p, out);
+  if (out.mode == OUT_MAP) {
+    p.W = out.dst_w / out.ostep;
+    p.H = out.dst_h / out.ostep;
+  }
   p.dev_err = dev.dev_err();
   if (p.tiles >= (1 << 24)) throw Error(ERR_INPUT, "GEMM too large for one launch");
   dispatch<A_ROWS>(dev, pw.bn, pw.kb, map, p, s);
@@ -152,9 +191,12 @@ void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const
                int act, const GemmOutSpec& out, cudaStream_t s) {
   if (pw.taps != (int)taps.size() || taps.size() > (size_t)GEMM_MAX_TAPS)
     throw Error(ERR_INPUT, "tap table does not match the weights");
-  if (w % 8 != 0 || w < 8 || h < 8) throw Error(ERR_INPUT, "convolution outputs must be at least 8 x 8, width a multiple of 8");
-  const int tw = w >= 16 ? 16 : 8;
-  if (src.w < tw || src.h < 8) throw Error(ERR_INPUT, "convolution source smaller than a tile");
+  if (w < 1 || h < 1) throw Error(ERR_INPUT, "empty convolution output");
+  if (out.mode == OUT_MAP && (out.dst_w != w * out.ostep || out.dst_h != h * out.ostep))
+    throw Error(ERR_INPUT, "convolution output does not match the output map");
+  // Tiles of 8 rows x 16 (or, for narrow outputs, 8) columns; boxes that
+  // reach past the source read TMA's zero fill.
+  const int tw = w > 8 ? 16 : 8;
   const int kg = pw.kb / 8;
   CUtensorMap map;
   const uint64_t phase_bytes = (uint64_t)src.w * src.h * 16;

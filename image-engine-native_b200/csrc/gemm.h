@@ -5,6 +5,7 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "runtime.h"
@@ -31,7 +32,12 @@ struct GemmOutSpec {
   int plane0 = 0;              // destination plane of column 0
   int map_h = 0, map_w = 0, shift = 0;  // OUT_WINDOW_ACCUM
   int dbl_w = 0, dbl_cout = 0;          // OUT_DOUBLE
-  int phase_y = 0, phase_x = 0;         // OUT_PHASE
+  int phase_y = 0, phase_x = 0;         // OUT_PHASE, OUT_MAP
+  // OUT_MAP (set by map_out): the stored map's geometry, output step, and
+  // the optional sources added before / after the activation.
+  int ostep = 1, dst_h = 0, dst_w = 0, dst_pad = 0, dst_split = 1, dst_pw = 0, dst_ph = 0;
+  const __half* acc_src = nullptr;
+  const __half* resid = nullptr;
 };
 
 // One tap of a convolution: the source pixel (y + dy, x + dx) of phase
@@ -48,15 +54,35 @@ struct TapSource {
   int w, h, phases;
 };
 
+// A map as LaMa's layers store it: h x w pixels reflect-padded by `pad`
+// and, with split 2, stored as the four space-to-depth phases of the padded
+// map ([k / 8][phase (py, px)][ph][pw][8]), which a stride-2 convolution
+// reads as taps of stride 1.
+struct MapGeom {
+  int h = 0, w = 0, pad = 0, split = 1;
+  int ph() const { return (h + 2 * pad + split - 1) / split; }
+  int pw() const { return (w + 2 * pad + split - 1) / split; }
+  long long plane_elems() const { return (long long)split * split * ph() * pw() * 8; }
+  TapSource source(const __half* ptr, int plane0 = 0) const {
+    return TapSource{ptr + (long long)plane0 * plane_elems(), plane_elems(), pw(), ph(), split * split};
+  }
+};
+
+// An OUT_MAP destination: channel planes from `plane0` of `out` stored as `g`.
+GemmOutSpec map_out(const MapGeom& g, __half* out, int plane0 = 0);
+
 // out (h x w pixels) = act(sum over taps and channels + bias), the taps'
 // weights row-major in tap order (pw packed with taps = taps.size()).
 void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const std::vector<Tap>& taps, int h, int w,
                int act, const GemmOutSpec& out, cudaStream_t s);
 
 // out = act(A x W + bias) over `m` rows of the planar input `a` (k / 8
-// planes of a_plane_elems / 8 >= max(m, 128) rows each; m a multiple of 16).
+// planes of a_plane_elems / 8 >= gemm_rows_alloc(m) rows each; the rows past
+// m are read but their results dropped). With OUT_MAP, row m is pixel
+// (m / w, m % w) of the output map (w = dst_w / ostep).
 void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long a_plane_elems, int m, int act,
                const GemmOutSpec& out, cudaStream_t s);
+inline int gemm_rows_alloc(int m) { return (std::max(m, 128) + 15) / 16 * 16; }
 
 // out = act(conv3x3(map) + bias): `map` is planar f16 with k / 8 planes of
 // h x w pixels (plane stride map_plane_elems), zero padding.

@@ -40,6 +40,13 @@
 //                    channel o (crates/scunet-native/src/network.rs:446-478)
 //   OUT_PHASE        one output phase (py, px) of a stride-2 transposed
 //                    convolution: row (y, x) -> output pixel (2y + py, 2x + px)
+//   OUT_MAP          row (y, x) -> pixel (ostep y + phase_y, ostep x + phase_x)
+//                    of a map stored reflect-padded by dst_pad (every pixel
+//                    also written where the padding mirrors it: gemm.rs:408-441
+//                    reflect) and, with dst_split 2, as the four space-to-depth
+//                    phases a stride-2 convolution reads; the value is
+//                    act(acc + bias [+ acc_src]) [+ resid], the two optional
+//                    sources read at the pixel in the same geometry
 // When accumulating, the activation applies after the add, as multiply does.
 // All waits are bounded as in conv3x3_sm100.cuh.
 #pragma once
@@ -53,7 +60,7 @@
 namespace iec {
 
 enum GemmA { A_ROWS = 0, A_TAPS = 1 };
-enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3, OUT_PHASE = 4 };
+enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3, OUT_PHASE = 4, OUT_MAP = 5 };
 enum GemmAct { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_SIGMOID = 3 };
 
 constexpr int GEMM_EPI_WARPS = 8;
@@ -79,8 +86,31 @@ struct GemmParams {
   int out_plane0;           // plane of output column 0
   int map_h, map_w, shift;  // OUT_WINDOW_ACCUM: the map the tokens came from
   int dbl_w, dbl_cout;      // OUT_DOUBLE: input width, output channels
+  // OUT_MAP: logical map size, reflect padding, phase split (1 or 2), pitch
+  // and rows of one stored phase image, output step (1, or 2 for one phase
+  // of a transposed convolution); A_ROWS reads the pixel (m / W, m % W).
+  int dst_h, dst_w, dst_pad, dst_split, dst_pw, dst_ph, ostep;
+  const __half* acc_src;    // added before the activation, or null
+  const __half* resid;      // added after the activation, or null
   int* dev_err;
 };
+
+// OUT_MAP: the stored rows (or columns) that hold logical row `y` of a map of
+// `n` rows reflect-padded by `pad` (pad < n): its own, and where the padding
+// mirrors it, reflect(i) = min(|i|, 2 (n - 1) - i).
+__device__ __forceinline__ int map_mirrors(int y, int n, int pad, int* r) {
+  int k = 0;
+  r[k++] = y + pad;
+  if (y >= 1 && y <= pad) r[k++] = pad - y;
+  if (y >= n - 1 - pad && y <= n - 2) r[k++] = pad + 2 * (n - 1) - y;
+  return k;
+}
+
+__device__ __forceinline__ long long map_offset(const GemmParams& p, int r, int c) {
+  if (p.dst_split == 2)
+    return ((long long)(((r & 1) * 2 + (c & 1)) * p.dst_ph + (r >> 1))) * p.dst_pw + (c >> 1);
+  return (long long)r * p.dst_pw + c;
+}
 
 template <int BN, int KB>
 struct GemmSmem {
@@ -91,21 +121,105 @@ struct GemmSmem {
   static constexpr int BAR_OFF = NSTAGE * STAGE;
   static constexpr int NBARS = 2 * NSTAGE + 4;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int TOTAL = MISC_OFF + 16;
+  // The bias, staged once per CTA for the epilogue (when N fits).
+  static constexpr int BIAS_FLOATS = 4096;
+  static constexpr int BIAS_OFF = (MISC_OFF + 16 + 15) / 16 * 16;
+  static constexpr int TOTAL = BIAS_OFF + BIAS_FLOATS * 4;
   static constexpr int DYN_BYTES = TOTAL + 1024;
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
 };
 
+// w[e] += the 8 halves of `old`.
+__device__ __forceinline__ void add_half8(float* w, const uint4 old) {
+  const __half2* oh = reinterpret_cast<const __half2*>(&old);
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const float2 f = __half22float2(oh[e]);
+    w[2 * e] += f.x;
+    w[2 * e + 1] += f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack_half8(const float* w) {
+  uint32_t packed[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    __half2 h2 = __floats2half2_rn(w[2 * e], w[2 * e + 1]);
+    packed[e] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  return make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+// GELU and sigmoid stay out of line: inlined into every element of the
+// unrolled epilogue they made its loop body too large for the instruction
+// cache, and the common ReLU / identity path would pay for them.
+static __device__ __noinline__ float gemm_gelu(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+
+static __device__ __noinline__ float gemm_sigmoid(float v) {
+  // math.rs:33-39: from exp(-|x|), so that neither tail cancels.
+  const float e = expf(-fabsf(v)), s = e / (e + 1.0f);
+  return v > 0.0f ? 1.0f - s : s;
+}
+
 __device__ __forceinline__ float gemm_act(float v, int act) {
   if (act == ACT_RELU) return v > 0.0f ? v : 0.0f;
-  if (act == ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-  if (act == ACT_SIGMOID) {
-    // math.rs:33-39: from exp(-|x|), so that neither tail cancels.
-    const float e = expf(-fabsf(v)), s = e / (e + 1.0f);
-    return v > 0.0f ? 1.0f - s : s;
-  }
+  if (act == ACT_GELU) return gemm_gelu(v);
+  if (act == ACT_SIGMOID) return gemm_sigmoid(v);
   return v;
+}
+
+// The OUT_MAP epilogue of one thread's row over columns [c_begin, c_end) of
+// its tile: in batches of 32 columns (two TMEM loads), the old values of the
+// batch's four 8-column groups are loaded together ahead of the
+// accumulators, so that their latencies overlap.
+template <int BN>
+__device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* bias, uint32_t taddr, int c_begin,
+                                             int c_end, int nt, int m, const int* ry, const int* rx, int nry, int nrx) {
+  const bool live = m >= 0;
+  const long long pix = live ? map_offset(p, ry[0], rx[0]) * 8 : 0;
+#pragma unroll 1
+  for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+    const bool two = c0 + 16 < c_end;  // uniform across the warp
+    uint4 oa[4], orr[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int n = nt * BN + c0 + 8 * q;
+      oa[q] = make_uint4(0u, 0u, 0u, 0u);
+      orr[q] = oa[q];
+      if (live && (q < 2 || two) && n < p.N) {
+        const long long at = (long long)(p.out_plane0 + n / 8) * p.out_plane_elems + pix;
+        if (p.acc_src) oa[q] = *reinterpret_cast<const uint4*>(p.acc_src + at);
+        if (p.resid) orr[q] = *reinterpret_cast<const uint4*>(p.resid + at);
+      }
+    }
+    uint32_t r[32];
+    tmem_ld16(taddr + (uint32_t)c0, r);
+    if (two) tmem_ld16(taddr + (uint32_t)c0 + 16, r + 16);
+    tmem_wait_ld();
+    if (!live) continue;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int n = nt * BN + c0 + 8 * q;
+      if ((q >= 2 && !two) || n >= p.N) continue;
+      float w[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        float x = __uint_as_float(r[8 * q + e]);
+        if (bias) x += bias[n + e < p.N ? n + e : 0];
+        w[e] = x;
+      }
+      if (p.acc_src) add_half8(w, oa[q]);
+#pragma unroll
+      for (int e = 0; e < 8; e++) w[e] = gemm_act(w[e], p.act);
+      if (p.resid) add_half8(w, orr[q]);
+      const uint4 val = pack_half8(w);
+      __half* plane = p.out + (long long)(p.out_plane0 + n / 8) * p.out_plane_elems;
+      for (int iy = 0; iy < nry; iy++)
+        for (int ix = 0; ix < nrx; ix++)
+          *reinterpret_cast<uint4*>(plane + map_offset(p, ry[iy], rx[ix]) * 8) = val;
+    }
+  }
 }
 
 template <int BN, int KB, int AMODE>
@@ -239,6 +353,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int part = (warp - 2) >> 2;  // which half of the columns
     const int row = quarter * 32 + lane;
     constexpr int HALF = (BN + 31) / 32 * 16;  // columns per part, a multiple of 16
+    // Stage the bias in shared memory: the epilogue then reads it at shared
+    // memory latency instead of a round trip to L2 per column chunk.
+    float* sbias = reinterpret_cast<float*>(smem + L::BIAS_OFF);
+    const bool bias_staged = p.bias && p.N <= L::BIAS_FLOATS;
+    if (bias_staged)
+      for (int j = (int)threadIdx.x - 64; j < p.N; j += 32 * GEMM_EPI_WARPS) sbias[j] = p.bias[j];
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * GEMM_EPI_WARPS) : "memory");
+    const float* bias = bias_staged ? sbias : p.bias;
     int i = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
       const int a = i & 1;
@@ -246,16 +368,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
       tc_fence_after();
       const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
-      // This thread's output row.
-      int m = -1;
+      // This thread's output row, and for A_TAPS its pixel.
+      int m = -1, oy = 0, ox = 0;
       if (AMODE == A_ROWS) {
         m = mt * 128 + row;
         if (m >= p.M) m = -1;
       } else {
         const int ty = (int)p.div_tiles_w.div((uint32_t)mt);
         const int x0 = (mt - ty * p.tiles_w) * p.TW, y0 = ty * 8;
-        const int py = y0 + row / p.TW, px = x0 + row % p.TW;
-        if (row < a_rows && py < p.H && px < p.W) m = py * p.W + px;
+        oy = y0 + row / p.TW;
+        ox = x0 + row % p.TW;
+        if (row < a_rows && oy < p.H && ox < p.W) m = oy * p.W + ox;
+      }
+      // OUT_MAP: the stored pixels that hold this row's output.
+      int ry[3], rx[3], nry = 0, nrx = 0;
+      if (p.out_mode == OUT_MAP && m >= 0) {
+        if (AMODE == A_ROWS) {
+          oy = m / p.W;
+          ox = m - oy * p.W;
+        }
+        nry = map_mirrors(oy * p.ostep + p.phase_y, p.dst_h, p.dst_pad, ry);
+        nrx = map_mirrors(ox * p.ostep + p.phase_x, p.dst_w, p.dst_pad, rx);
       }
       // Destination pixel of the row for the scattering epilogues.
       long long dest = m;
@@ -266,8 +399,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         dest = (long long)py * p.map_w + px;
       }
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * L::ACC_COLS);
+      if (p.out_mode == OUT_MAP)
+        map_epilogue<BN>(p, bias, taddr, part * HALF, min(part * HALF + HALF, BN), nt, m, ry, rx, nry, nrx);
 #pragma unroll 1
-      for (int c0 = part * HALF; c0 < part * HALF + HALF && c0 < BN; c0 += 16) {
+      for (int c0 = part * HALF; p.out_mode != OUT_MAP && c0 < part * HALF + HALF && c0 < BN; c0 += 16) {
         uint32_t r[16];
         tmem_ld16(taddr + (uint32_t)c0, r);
         tmem_wait_ld();
@@ -277,7 +412,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 16; e++) {
           float x = __uint_as_float(r[e]);
-          if (p.bias) x += p.bias[n0 + e < p.N ? n0 + e : 0];
+          if (bias) x += bias[n0 + e < p.N ? n0 + e : 0];
           v[e] = x;
         }
 #pragma unroll

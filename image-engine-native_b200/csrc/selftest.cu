@@ -4,10 +4,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <memory>
 #include <string>
 
 #include "../../include/iec_cuda.h"
+#include "fft.h"
 #include "gemm.h"
 #include "igemm_sm100.cuh"
 
@@ -84,6 +86,134 @@ extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int w
     planar_to_rows(dout.as<__half>(), plane, rows, c, do32.as<float>(), s);
     IEC_CUDA(cudaMemcpyAsync(out, do32.get(), (size_t)rows * c * 4, cudaMemcpyDeviceToHost, s));
     dev.sync(s);
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
+extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, float* spec, float* back) {
+  try {
+    if (c % 8 != 0 || h < 1 || w < 1) throw Error(ERR_INPUT, "rfft2 self-test: c a multiple of 8");
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    FourierPlan plan;
+    fourier_plan(plan, h, w, c);
+    const int half = w / 2 + 1, rows = h * w, frows = h * half;
+    const long long xp = (long long)rows * 8, fp = (long long)frows * 8;
+    DeviceBuffer d32, dx, dspec, dout;
+    d32.reserve((size_t)std::max(rows * c, frows * 2 * c) * 4);
+    dx.reserve((size_t)xp * (c / 8) * 2);
+    dspec.reserve((size_t)fp * (2 * c / 8) * 2);
+    cudaStream_t s = dev.stream();
+    IEC_CUDA(cudaMemcpyAsync(d32.get(), x, (size_t)rows * c * 4, cudaMemcpyHostToDevice, s));
+    rows_to_planar(d32.as<float>(), rows, c, dx.as<__half>(), xp, s);
+    rfft2_planar(plan, dx.as<__half>(), xp, dspec.as<__half>(), fp, s);
+    planar_to_rows(dspec.as<__half>(), fp, frows, 2 * c, d32.as<float>(), s);
+    IEC_CUDA(cudaMemcpyAsync(spec, d32.get(), (size_t)frows * 2 * c * 4, cudaMemcpyDeviceToHost, s));
+    IEC_CUDA(cudaMemsetAsync(dx.get(), 0, (size_t)xp * (c / 8) * 2, s));
+    irfft2_add_planar(plan, dspec.as<__half>(), fp, dx.as<__half>(), xp, s);
+    planar_to_rows(dx.as<__half>(), xp, rows, c, d32.as<float>(), s);
+    IEC_CUDA(cudaMemcpyAsync(back, d32.get(), (size_t)rows * c * 4, cudaMemcpyDeviceToHost, s));
+    dev.sync(s);
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
+// Diagnostics: per launch of the general GEMM on zero-filled device buffers,
+// `iters` launches back to back after 3 warm-up ones: us[0] device
+// microseconds, us[1] host microseconds to enqueue, us[2] device microseconds
+// when the launches replay from a CUDA graph. mode 0: rows (m x k); mode 1: 3x3 taps over an h x w map (K = k per
+// tap); mode 2: one tap over an h x w map. out_map: store through OUT_MAP
+// (unpadded map) with `sources` old-value sources (0..2) instead of OUT_STORE.
+extern "C" iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, int w, int k, int n, int out_map,
+                                             int sources, int iters, float* us) {
+  try {
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    const int taps = mode == 1 ? 9 : 1;
+    // rows stored through the map epilogue: a map of rows / 64 x 64 pixels
+    const int h = mode == 0 ? (out_map ? m_or_h / 64 : 1) : m_or_h, width = mode == 0 ? (out_map ? 64 : 1) : w;
+    const int rows = mode == 0 ? m_or_h : h * width;
+    if (mode == 0 && out_map && m_or_h % 64 != 0) throw Error(ERR_INPUT, "map rows: a multiple of 64");
+    std::vector<float> wv((size_t)taps * k * n, 0.0f);
+    std::vector<float> bias(n, 0.0f);
+    PackedWeights pw;
+    pack_weights(pw, wv, taps, k, n, bias.data());
+    const MapGeom src_geom{h, width, 1, 1};
+    const long long in_plane = mode == 0 ? (long long)gemm_rows_alloc(rows) * 8 : src_geom.plane_elems();
+    const long long out_plane = out_map ? (long long)h * width * 8 : (long long)gemm_rows_alloc(rows) * 8;
+    DeviceBuffer a, o, s1, s2;
+    const size_t abytes = (size_t)in_plane * (k / 8) * 2, obytes = (size_t)out_plane * ((n + 7) / 8) * 2;
+    a.reserve(abytes);
+    o.reserve(obytes);
+    s1.reserve(obytes);
+    s2.reserve(obytes);
+    cudaStream_t s = dev.stream();
+    IEC_CUDA(cudaMemsetAsync(a.get(), 0, abytes, s));
+    IEC_CUDA(cudaMemsetAsync(o.get(), 0, obytes, s));
+    IEC_CUDA(cudaMemsetAsync(s1.get(), 0, obytes, s));
+    IEC_CUDA(cudaMemsetAsync(s2.get(), 0, obytes, s));
+    GemmOutSpec spec;
+    if (out_map) {
+      spec = map_out(MapGeom{h, width, 0, 1}, o.as<__half>());
+      if (sources >= 1) spec.acc_src = s1.as<__half>();
+      if (sources >= 2) spec.resid = s2.as<__half>();
+    } else {
+      spec.mode = OUT_STORE;
+      spec.out = o.as<__half>();
+      spec.plane_elems = out_plane;
+    }
+    std::vector<Tap> tl;
+    if (mode == 1)
+      for (int t = 0; t < 9; t++) tl.push_back({t / 3, t % 3, 0});
+    else
+      tl.push_back({1, 1, 0});
+    auto launch = [&]() {
+      if (mode == 0)
+        gemm_rows(dev, pw, a.as<__half>(), in_plane, rows, ACT_RELU, spec, s);
+      else
+        gemm_taps(dev, pw, src_geom.source(a.as<__half>()), tl, h, width, ACT_RELU, spec, s);
+    };
+    for (int i = 0; i < 3; i++) launch();
+    cudaEvent_t e0, e1;
+    IEC_CUDA(cudaEventCreate(&e0));
+    IEC_CUDA(cudaEventCreate(&e1));
+    dev.sync(s);
+    const auto h0 = std::chrono::steady_clock::now();
+    IEC_CUDA(cudaEventRecord(e0, s));
+    for (int i = 0; i < iters; i++) launch();
+    IEC_CUDA(cudaEventRecord(e1, s));
+    const auto h1 = std::chrono::steady_clock::now();
+    dev.sync(s);
+    float ms = 0;
+    IEC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    us[0] = ms * 1000.0f / (float)iters;
+    us[1] = (float)std::chrono::duration<double, std::micro>(h1 - h0).count() / (float)iters;
+    // The same launches replayed from a CUDA graph: no host work between them.
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    IEC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    for (int i = 0; i < iters; i++) launch();
+    IEC_CUDA(cudaStreamEndCapture(s, &graph));
+    IEC_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+    IEC_CUDA(cudaGraphLaunch(exec, s));
+    IEC_CUDA(cudaEventRecord(e0, s));
+    IEC_CUDA(cudaGraphLaunch(exec, s));
+    IEC_CUDA(cudaEventRecord(e1, s));
+    dev.sync(s);
+    IEC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    us[2] = ms * 1000.0f / (float)iters;
+    cudaGraphExecDestroy(exec);
+    cudaGraphDestroy(graph);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
     return IEC_OK;
   } catch (const Error& e) {
     return (iec_status)e.code;

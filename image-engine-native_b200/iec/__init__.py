@@ -71,6 +71,8 @@ def lib():
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
+        L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, f32p, f32p]
+        L.iec_selftest_gemm_time.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)]
         L.iec_selftest_attention.argtypes = [i32, f32p, i32, i32, f32p, i32, i32, i32, f32p]
         L.iec_scunet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
         L.iec_scunet_free.argtypes = [vp]
@@ -80,6 +82,13 @@ def lib():
         L.iec_scunet_run_float_tiled.argtypes = [vp, f32p, sz, sz, sz, sz, f32p, PROGRESS, vp]
         L.iec_scunet_run.argtypes = [vp, u8p, sz, sz, u8p, PROGRESS, vp]
         L.iec_scunet_run_device.argtypes = [vp, vp, sz, sz, vp, vp]
+        L.iec_lama_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
+        L.iec_lama_free.argtypes = [vp]
+        L.iec_lama_device_name.argtypes = [vp]
+        L.iec_lama_device_name.restype = ctypes.c_char_p
+        L.iec_lama_run_float.argtypes = [vp, f32p, f32p, sz, sz, f32p]
+        L.iec_lama_run.argtypes = [vp, u8p, u8p, sz, sz, u8p, PROGRESS, vp]
+        L.iec_lama_run_device.argtypes = [vp, vp, vp, sz, sz, vp, vp]
         L.iec_realesrgan_set_timing.argtypes = [vp, sz]
         L.iec_realesrgan_timing.argtypes = [vp, ctypes.POINTER(ctypes.c_int), f32p, sz]
         L.iec_realesrgan_timing.restype = sz
@@ -165,6 +174,7 @@ class RealEsrgan:
         return out
 
     run_with_progress = run
+
 
     def run_float_tiles(self, image: np.ndarray, tile: int, margin: int, first: int, last: int, out=None):
         """Tiles first .. last - 1 of run_float_tiled's grid into `out` (the
@@ -304,3 +314,77 @@ class Scunet:
         return out
 
     run_with_progress = run
+
+
+class Lama:
+    """crates/lama-native/src/lib.rs Model, on the CUDA backend."""
+
+    MIN_SIDE = 9
+    STEPS = 26
+
+    def __init__(self, path, device: int = -1, timeout_ms: int = 0):
+        self._h = ctypes.c_void_p()
+        opt = Options(device, timeout_ms, 0)
+        _check(lib().iec_lama_load(os.fsencode(path), ctypes.byref(opt), ctypes.byref(self._h)))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().iec_lama_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def gpu(self) -> str:
+        return lib().iec_lama_device_name(self._h).decode()
+
+    def run_float(self, image: np.ndarray, mask: np.ndarray) -> np.ndarray:
+        """Model::run_float: the prediction (HxWx3) for an HxWx3 image in
+        0..=1 and an HxW mask (1 fills)."""
+        image = np.ascontiguousarray(image, np.float32)
+        mask = np.ascontiguousarray(mask, np.float32)
+        h, w, _ = image.shape
+        if mask.shape != (h, w):
+            raise ValueError("mask must be height x width")
+        out = np.empty_like(image)
+        _check(lib().iec_lama_run_float(self._h, _f32(image), _f32(mask), w, h, _f32(out)))
+        return out
+
+    def run(self, rgb: np.ndarray, mask: np.ndarray, progress=None) -> np.ndarray:
+        """Model::run: 8-bit RGB with the pixels where `mask` (u8) is not
+        zero filled in."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        mask = np.ascontiguousarray(mask, np.uint8)
+        h, w, _ = rgb.shape
+        if mask.shape != (h, w):
+            raise ValueError("mask must be height x width")
+        out = np.empty_like(rgb)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        _check(lib().iec_lama_run(self._h, rgb.ctypes.data_as(u8p), mask.ctypes.data_as(u8p), w, h,
+                                  out.ctypes.data_as(u8p), _progress(progress), None))
+        return out
+
+    run_with_progress = run
+
+    def run_device(self, image_ptr: int, mask_ptr: int, width: int, height: int, out_ptr: int, stream: int = 0):
+        """run_float on device pointers, queued on `stream`."""
+        _check(lib().iec_lama_run_device(self._h, image_ptr, mask_ptr, width, height, out_ptr, stream or None))
+
+
+def selftest_rfft2(x: np.ndarray, device: int = -1):
+    """LaMa's planar rfft2 / irfft2 on an h x w x c array (c % 8 == 0):
+    returns (spectrum h x (w/2+1) x 2c, irfft2 of it h x w x c)."""
+    x = np.ascontiguousarray(x, np.float32)
+    h, w, c = x.shape
+    spec = np.empty((h, w // 2 + 1, 2 * c), np.float32)
+    back = np.empty_like(x)
+    _check(lib().iec_selftest_rfft2(device, _f32(x), h, w, c, _f32(spec), _f32(back)))
+    return spec, back
+
+
+def selftest_gemm_time(mode: int, m_or_h: int, w: int, k: int, n: int, out_map: bool = False, sources: int = 0,
+                       iters: int = 50, device: int = -1):
+    """(device us, host enqueue us, graph-replay device us) per launch of
+    one GEMM shape (iec_selftest_gemm_time)."""
+    us = (ctypes.c_float * 3)()
+    _check(lib().iec_selftest_gemm_time(device, mode, m_or_h, w, k, n, int(out_map), sources, iters, us))
+    return tuple(us)

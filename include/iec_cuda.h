@@ -194,6 +194,34 @@ iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, s
 iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t width, size_t height,
                                  float* out, void* stream);
 
+/* -------------------------------------------------------------------- LaMa
+ * crates/lama-native/src/lib.rs: Big LaMa inpainting, output the size of the
+ * input. Sides of at least 9 pixels (lib.rs:180-194); at most 12288 here. */
+typedef struct iec_lama iec_lama;
+
+/* Model::load (lib.rs:76-94) with IMAGE_ENGINE_NATIVE_GPU=1 semantics; the
+ * "LAMA\0\0\0\0" weights file of tools/lama/export_weights.py. */
+iec_status iec_lama_load(const char* weights_path, const iec_options* options, iec_lama** out);
+void iec_lama_free(iec_lama* model);
+const char* iec_lama_device_name(const iec_lama* model);
+
+/* Model::run_float (lib.rs:163-172): the network's prediction for every
+ * pixel, width x height x 3 floats, given the image (values in 0..=1) and a
+ * mask of width x height floats (1 to fill, 0 to keep). */
+iec_status iec_lama_run_float(iec_lama* model, const float* image, const float* mask, size_t width,
+                              size_t height, float* out);
+
+/* Model::run / run_with_progress (lib.rs:118-156): 8-bit RGB with the pixels
+ * whose mask byte is not zero filled in; `progress` after each of the 26
+ * steps, non-zero cancels (IEC_CANCELLED). */
+iec_status iec_lama_run(iec_lama* model, const uint8_t* rgb, const uint8_t* mask, size_t width,
+                        size_t height, uint8_t* out, iec_progress_fn progress, void* user);
+
+/* Model::run_float on DEVICE pointers of the model's device; queued on
+ * `stream` (NULL: the model's stream), no wait. */
+iec_status iec_lama_run_device(iec_lama* model, const float* image, const float* mask, size_t width,
+                               size_t height, float* out, void* stream);
+
 /* Diagnostics (no counterpart in the reference): one launch of the general
  * GEMM on host arrays. conv = 0: `a` rows_or_h x k, `weights` k x n; conv = 1:
  * `a` rows_or_h x w x k, `weights` 9k x n (3x3, zero padding). act 0 none,
@@ -201,6 +229,21 @@ iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t w
 iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int w, int k, int n,
                              const float* a, const float* weights, const float* bias, int act,
                              int accumulate, float* out);
+
+/* Diagnostics: LaMa's planar Fourier transforms on host arrays: `x` h x w x c
+ * floats (c a multiple of 8, rounded to f16 on the way in); `spec` gets
+ * rfft2(x) as h x (w / 2 + 1) x 2c floats (real parts of the c channels, then
+ * imaginary), `back` gets irfft2 of that spectrum (h x w x c). */
+iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, float* spec, float* back);
+
+/* Diagnostics: per launch of the general GEMM on zero-filled buffers (mode
+ * 0: m x k rows; 1: 3x3 taps over an h x w map; 2: one tap over an h x w
+ * map), `iters` launches back to back; out_map stores through the map
+ * epilogue with `sources` (0..2) old-value sources. us[0] device
+ * microseconds, us[1] host microseconds to enqueue, us[2] device
+ * microseconds replayed from a CUDA graph. */
+iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, int w, int k, int n, int out_map,
+                                  int sources, int iters, float* us);
 
 /* Diagnostics: the fused window attention on host arrays: `qkv` windows * 64
  * rows of 3c (q | k | v), `bias` classes x (c / 32) x 64 x 64, `out` windows *

@@ -1,0 +1,172 @@
+"""Big LaMa on the CUDA backend against the CPU oracle and the float64 torch
+fixture (GPU tests), and the planar Fourier transforms alone.
+
+Tolerance (the project's parity bar for RGB outputs): max abs <= 2e-2 on raw
+outputs and PSNR >= 45 dB on outputs clamped to [0, 1]. The behaviour tests
+follow crates/lama-native/src/lib.rs: 26 progress calls, cancel, the size
+check, and the 8-bit run keeping every unmasked pixel.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from iec import weights as W
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MIN_PSNR = 45.0
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "lama_torch.npz")
+
+
+def psnr(a, b):
+    mse = np.mean((np.clip(a, 0, 1).astype(np.float64) - np.clip(b, 0, 1)) ** 2)
+    return float("inf") if mse == 0 else 10 * np.log10(1.0 / mse)
+
+
+def within(got, want, max_abs=MAX_ABS):
+    assert got.shape == want.shape
+    assert np.isfinite(got).all()
+    err = float(np.abs(got - want).max())
+    p = psnr(got, want)
+    assert err <= max_abs and p >= MIN_PSNR, (err, p)
+    return err, p
+
+
+@pytest.fixture(scope="module")
+def lama_weights(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("lama") / "lama.weights")
+    W.write_lama(path, 0)
+    return path
+
+
+@pytest.fixture(scope="module")
+def gpu_model(lama_weights):
+    import iec
+
+    m = iec.Lama(lama_weights)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def cpu_model(lama_weights):
+    from oracle import refcpu
+
+    return refcpu.Lama(lama_weights)
+
+
+def test_matches_torch_fixture(gpu_model):
+    g = np.load(GOLDEN)
+    for i in range(3):
+        within(gpu_model.run_float(g[f"case{i}_image"], g[f"case{i}_mask"]), g[f"case{i}_out"])
+
+
+@pytest.mark.parametrize("width,height,seed", [(64, 64, 1), (40, 24, 2), (27, 35, 3), (136, 72, 4), (9, 9, 5)])
+def test_matches_oracle(gpu_model, cpu_model, width, height, seed):
+    image, mask = W.lama_input(width, height, seed)
+    within(gpu_model.run_float(image, mask), cpu_model.run_float(image, mask))
+
+
+def test_matches_oracle_at_config_size(gpu_model, cpu_model):
+    """The benchmark's 512 x 512 input with about 30 % masked."""
+    image, mask = W.lama_input(512, 512, 0)
+    within(gpu_model.run_float(image, mask), cpu_model.run_float(image, mask))
+
+
+def test_repeatable_and_size_changes(gpu_model):
+    a_img, a_mask = W.lama_input(48, 40, 7)
+    b_img, b_mask = W.lama_input(96, 64, 8)
+    first = gpu_model.run_float(a_img, a_mask)
+    gpu_model.run_float(b_img, b_mask)
+    assert np.array_equal(gpu_model.run_float(a_img, a_mask), first)
+
+
+def test_run_u8_composites_holes(gpu_model, cpu_model):
+    image, mask = W.lama_input(72, 56, 9)
+    rgb = np.round(image * 255).astype(np.uint8)
+    m8 = (mask * 255).astype(np.uint8)
+    got = gpu_model.run(rgb, m8)
+    want = cpu_model.run(rgb, m8)
+    keep = m8 == 0
+    assert np.array_equal(got[keep], rgb[keep])
+    diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+    assert diff.max() <= 6
+    assert psnr(got / 255.0, want / 255.0) > 48
+
+
+def test_progress_and_cancel(gpu_model):
+    import iec
+
+    image, mask = W.lama_input(32, 24, 3)
+    rgb = np.round(image * 255).astype(np.uint8)
+    m8 = (mask * 255).astype(np.uint8)
+    seen = []
+    gpu_model.run(rgb, m8, progress=lambda f: seen.append(f) and False)
+    assert len(seen) == 26 and abs(seen[-1] - 1.0) < 1e-6
+    calls = []
+    with pytest.raises(iec.Cancelled):
+        gpu_model.run(rgb, m8, progress=lambda f: calls.append(f) or len(calls) >= 3)
+    assert len(calls) == 3
+    # the model still works after a cancelled run
+    assert gpu_model.run(rgb, m8).shape == rgb.shape
+
+
+def test_size_check(gpu_model):
+    import iec
+
+    image, mask = W.lama_input(16, 16, 0)
+    with pytest.raises(iec.IecError):
+        gpu_model.run_float(image[:8], mask[:8])
+    with pytest.raises(iec.IecError):
+        gpu_model.run_float(image[:, :8], mask[:, :8])
+
+
+def test_run_device(gpu_model, cpu_model):
+    import torch
+
+    image, mask = W.lama_input(80, 48, 11)
+    ti = torch.from_numpy(image).cuda()
+    tm = torch.from_numpy(mask).cuda()
+    out = torch.empty_like(ti)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    gpu_model.run_device(ti.data_ptr(), tm.data_ptr(), 80, 48, out.data_ptr(), s.cuda_stream)
+    s.synchronize()
+    within(out.cpu().numpy(), cpu_model.run_float(image, mask))
+
+
+@pytest.mark.parametrize("h,w,c", [(64, 64, 16), (5, 7, 8), (16, 12, 8), (9, 10, 8), (1, 8, 8), (2, 2, 8),
+                                   (32, 128, 8)])
+def test_planar_rfft2_matches_numpy(h, w, c):
+    """fft.cu against numpy's ortho rfft2 / irfft2 of the same f16-rounded
+    input; the spectrum is stored in f16, hence the relative bound."""
+    import iec
+
+    rng = np.random.default_rng(h * 1000 + w)
+    x = rng.random((h, w, c), dtype=np.float32).astype(np.float16).astype(np.float32)
+    spec, back = iec.selftest_rfft2(x)
+    want = np.fft.rfft2(x.astype(np.float64), axes=(0, 1), norm="ortho")
+    scale = 1.0 + np.abs(want).max()
+    assert np.abs(spec[:, :, :c] - want.real).max() <= 2e-3 * scale
+    assert np.abs(spec[:, :, c:] - want.imag).max() <= 2e-3 * scale
+    z = (spec[:, :, :c] + 1j * spec[:, :, c:]).astype(np.complex128)
+    want_back = np.fft.irfft2(z, s=(h, w), axes=(0, 1), norm="ortho")
+    assert np.abs(back - want_back).max() <= 2e-3 * (1.0 + np.abs(want_back).max())
+    assert np.abs(back - x).max() <= 1e-2
+
+
+def test_handle_of_another_model_is_refused(gpu_model):
+    """A LaMa handle passed to a SCUNet entry point fails cleanly."""
+    import ctypes
+
+    import iec
+
+    image = np.zeros((16, 16, 3), np.float32)
+    out = np.empty_like(image)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    st = iec.lib().iec_scunet_run_float(gpu_model._h, image.ctypes.data_as(f32p), 16, 16, out.ctypes.data_as(f32p))
+    assert st == 3  # IEC_ERR_INPUT
+    assert gpu_model.run_float(*W.lama_input(16, 16, 0)).shape == (16, 16, 3)
