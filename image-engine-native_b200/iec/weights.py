@@ -233,3 +233,101 @@ def lama_input(width: int, height: int, seed: int = 0, cover: float = 0.3):
         x = int(rng.integers(0, width - rw + 1))
         mask[y:y + rh, x:x + rw] = 1.0
     return image, mask
+
+
+BIREFNET_STAGES = [(96, 2), (192, 2), (384, 6), (768, 2)]
+BIREFNET_SIZES = [1, 1, 3, 7]
+BIREFNET_LEVELS = [(1728, 768), (960, 384), (480, 192), (240, 96)]
+BIREFNET_MEAN = (0.485, 0.456, 0.406)
+BIREFNET_STD = (0.229, 0.224, 0.225)
+
+
+def birefnet_tensors(seed: int = 0, branch_gain: float = 0.3, offset_scale: float = 0.5, head_gain: float = 1.0):
+    """BiRefNet-lite tensors as crates/birefnet-native/src/swin.rs:115-158 and
+    decoder.rs:106-135,316-340,538-545,605-633,753-786 load them. As
+    tools/birefnet/export_weights.py:248-259 writes them with --half: 2-D
+    `.weight` tensors f16, everything else f32. Batch norms are folded in the
+    exported file, so the generator draws the folded matrices directly:
+    convolutions before a ReLU He-normal, other layers LeCun-normal, biases
+    U(+-0.05), LayerNorm weight 1 + N(0, 0.05^2) and bias N(0, 0.02^2),
+    position bias N(0, 0.02^2). The residual branches' last layers (proj,
+    fc2) are scaled by `branch_gain`; the deformable offsets and modulator
+    logits are drawn so that the offsets are of order `offset_scale` pixels."""
+    rng = np.random.default_rng(seed)
+    tensors = []
+
+    def half(a):
+        return a.astype(np.float16).astype(np.float32)
+
+    def mat(name, k, n, bias=True, he=False, gain=1.0, bias_scale=0.05):
+        w = rng.standard_normal((k, n)) * np.sqrt((2.0 if he else 1.0) / k) * gain
+        tensors.append((f"{name}.weight", half(w), True))
+        if bias:
+            tensors.append((f"{name}.bias", rng.uniform(-bias_scale, bias_scale, n).astype(np.float32), False))
+
+    def ln(name, c):
+        tensors.append((f"{name}.weight", (1 + 0.05 * rng.standard_normal(c)).astype(np.float32), False))
+        tensors.append((f"{name}.bias", (0.02 * rng.standard_normal(c)).astype(np.float32), False))
+
+    mat("patch_embed", 48, 96)
+    ln("patch_embed.norm", 96)
+    for s, (c, depth) in enumerate(BIREFNET_STAGES):
+        for b in range(depth):
+            p = f"stage{s}.block{b}"
+            ln(f"{p}.norm1", c)
+            mat(f"{p}.qkv", c, 3 * c)
+            tensors.append((f"{p}.position_bias",
+                            (0.02 * rng.standard_normal((c // 32, 49, 49))).astype(np.float32), False))
+            mat(f"{p}.proj", c, c, gain=branch_gain)
+            ln(f"{p}.norm2", c)
+            mat(f"{p}.fc1", c, 4 * c)
+            mat(f"{p}.fc2", 4 * c, c, gain=branch_gain)
+        if s < 3:
+            ln(f"stage{s}.merge.norm", 4 * c)
+            mat(f"stage{s}.merge", 4 * c, 2 * c, bias=False)
+        ln(f"stage{s}.norm", c)
+
+    def block(p, cin, cout, gate):
+        mat(f"{p}.conv_in", 9 * cin, 64, he=True)
+        mat(f"{p}.conv_out", 9 * 64, cout)
+        if gate:
+            mat(f"{p}.gdt", 9 * cout, 16, he=True)
+            mat(f"{p}.gdt_attn", 16, 1)
+        for i, k in enumerate(BIREFNET_SIZES):
+            taps = k * k
+            mat(f"{p}.aspp.branch{i}.offset", taps * 64, 3 * taps, gain=offset_scale, bias_scale=offset_scale)
+            mat(f"{p}.aspp.branch{i}", taps * 64, 256, he=True)
+        mat(f"{p}.aspp.pool", 64, 256, he=True)
+        mat(f"{p}.aspp.conv1", 5 * 256, 64, he=True)
+
+    block("squeeze", 2880, 1536, False)
+    for i, (cin, cout) in enumerate(BIREFNET_LEVELS):
+        block(f"block{4 - i}", cin, cout, i < 3)
+    for n, c in [(4, 768), (3, 384), (2, 192)]:
+        mat(f"lateral{n}", c, c)
+    for n, cin, cout in [(5, 3072, 192), (4, 768, 192), (3, 192, 96), (2, 48, 48)]:
+        mat(f"patches{n}.conv1", 9 * cin, 64)
+        mat(f"patches{n}.conv_out", 9 * 64, cout)
+    mat("head", 96, 1, gain=head_gain)
+    mat("patches1.conv1", 27, 64)
+    mat("patches1.conv_out", 9 * 64, 1)
+    return tensors
+
+
+def write_birefnet(path, seed: int = 0) -> str:
+    return write(path, MAGIC["birefnet"], birefnet_tensors(seed))
+
+
+def birefnet_input(side: int, seed: int = 0) -> np.ndarray:
+    """A seeded 8-bit RGB image, side x side x 3, uniform over 0..255."""
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 256, (side, side, 3), dtype=np.uint8)
+
+
+def birefnet_normalize(rgb: np.ndarray) -> np.ndarray:
+    """lib.rs:116-133: (v / 255 - mean) / std per colour, in f32."""
+    table = np.empty((256, 3), np.float32)
+    v = np.arange(256, dtype=np.float32) / np.float32(255.0)
+    for c in range(3):
+        table[:, c] = (v - np.float32(BIREFNET_MEAN[c])) / np.float32(BIREFNET_STD[c])
+    return table[rgb, np.arange(3)].astype(np.float32)

@@ -73,6 +73,11 @@ def lib():
         ]
         L.refcpu_rfft2.argtypes = [_f32p, sz, sz, sz, _f32p]
         L.refcpu_irfft2_add.argtypes = [_f32p, sz, sz, sz, _f32p]
+        L.refcpu_birefnet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        L.refcpu_birefnet_free.argtypes = [ctypes.c_void_p]
+        L.refcpu_birefnet_run_normalized.argtypes = [ctypes.c_void_p, _f32p, sz, _f32p]
+        L.refcpu_birefnet_run.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint8), sz, _f32p]
+        L.refcpu_resize.argtypes = [_f32p, sz, sz, sz, _f32p, sz, sz, ctypes.c_int]
         L.refcpu_attention.argtypes = [_f32p, sz, sz, _f32p, sz, _f32p]
         L.refcpu_layer_norm.argtypes = [_f32p, sz, sz, _f32p, _f32p]
         L.refcpu_gelu.argtypes = [_f32p, sz]
@@ -264,6 +269,45 @@ class Lama:
         out = rgb.copy()
         out[mask != 0] = fill[mask != 0]
         return out
+
+
+class Birefnet:
+    """The reference's CPU BiRefNet-lite (Model::load_cpu) as restated."""
+
+    def __init__(self, path):
+        self._h = ctypes.c_void_p()
+        _check(lib().refcpu_birefnet_load(os.fsencode(path), ctypes.byref(self._h)))
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.refcpu_birefnet_free(self._h)
+            self._h = None
+
+    def run_normalized(self, image: np.ndarray) -> np.ndarray:
+        """lib.rs:134-172: side x side logits of a normalised NHWC image."""
+        image = np.ascontiguousarray(image, np.float32)
+        side = image.shape[0]
+        out = np.empty((side, side), np.float32)
+        _check(lib().refcpu_birefnet_run_normalized(self._h, _ptr(image), side, _ptr(out)))
+        return out
+
+    def run(self, rgb: np.ndarray) -> np.ndarray:
+        """lib.rs:116-133: logits of an 8-bit side x side image."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        side = rgb.shape[0]
+        out = np.empty((side, side), np.float32)
+        _check(lib().refcpu_birefnet_run(self._h, rgb.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), side,
+                                         _ptr(out)))
+        return out
+
+
+def resize(src, dh, dw, out=None, add=False):
+    """decoder.rs:443-521: aligned-corner bilinear resize of an h x w x c map."""
+    src = np.ascontiguousarray(src, np.float32)
+    sh, sw, c = src.shape
+    dst = np.zeros((dh, dw, c), np.float32) if out is None else np.array(out, np.float32, copy=True, order="C")
+    _check(lib().refcpu_resize(_ptr(src), sh, sw, c, _ptr(dst), dh, dw, int(add)))
+    return dst
 
 
 def rfft2(x, h, w, c):

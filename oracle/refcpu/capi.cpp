@@ -179,6 +179,35 @@ int refcpu_irfft2_add(const float* spec, size_t h, size_t w, size_t c, float* ou
   });
 }
 
+// -------------------------------------------------------------------- BiRefNet
+int refcpu_birefnet_load(const char* path, void** out) {
+  return guard([&] { *out = new Birefnet(path); });
+}
+void refcpu_birefnet_free(void* h) { delete static_cast<Birefnet*>(h); }
+
+// Model::run_normalized: side x side logits.
+int refcpu_birefnet_run_normalized(void* h, const float* image, size_t side, float* out) {
+  return guard([&] {
+    Birefnet::check_size(side * side * 3, side);
+    std::vector<float> r = static_cast<Birefnet*>(h)->run_normalized(image, side);
+    std::memcpy(out, r.data(), r.size() * sizeof(float));
+  });
+}
+
+// Model::run: the 8-bit image normalised, then run_normalized.
+int refcpu_birefnet_run(void* h, const uint8_t* rgb, size_t side, float* out) {
+  return guard([&] {
+    Birefnet::check_size(side * side * 3, side);
+    std::vector<float> img = Birefnet::normalize(rgb, side * side);
+    std::vector<float> r = static_cast<Birefnet*>(h)->run_normalized(img.data(), side);
+    std::memcpy(out, r.data(), r.size() * sizeof(float));
+  });
+}
+
+int refcpu_resize(const float* src, size_t sh, size_t sw, size_t c, float* dst, size_t dh, size_t dw, int add) {
+  return guard([&] { resize(src, sh, sw, c, dst, dh, dw, c, add != 0); });
+}
+
 // The engine's window attention and layer norm, for the kernels' unit tests.
 int refcpu_attention(const float* qkv, size_t c, size_t head, const float* bias, size_t tokens, float* out) {
   return guard([&] { attention(qkv, c, head, bias, tokens, out); });

@@ -63,6 +63,27 @@ class Lama {
   Impl* impl_;
 };
 
+// crates/birefnet-native/src/lib.rs + swin.rs + decoder.rs (see birefnet.cpp).
+class Birefnet {
+ public:
+  explicit Birefnet(const std::string& path);
+  ~Birefnet();
+  // lib.rs:175-187 check_size.
+  static void check_size(size_t len, size_t side);
+  // lib.rs:134-172: the logit of every pixel of a normalised side x side image.
+  std::vector<float> run_normalized(const float* image, size_t side) const;
+  // lib.rs:116-133: an 8-bit image through the ImageNet normalisation table.
+  static std::vector<float> normalize(const uint8_t* rgb, size_t pixels);
+  struct Impl;
+
+ private:
+  Impl* impl_;
+};
+
+// decoder.rs:443-521: aligned-corner bilinear resize (ONNX Runtime's rule).
+void resize(const float* src, size_t sh, size_t sw, size_t c, float* dst, size_t dh, size_t dw, size_t stride,
+            bool add);
+
 // fourier.rs: the ortho rfft2 of an h x w map of c channels (pixel p at
 // x[p * stride]) into rows of h x (w / 2 + 1) pixels [re(c) | im(c)], and
 // the ortho inverse added onto `out`.
