@@ -1,0 +1,918 @@
+// BiRefNet-lite on the CUDA backend (see birefnet.h).
+//
+// lib.rs:134-172: the normalised image and its aligned-corner half-size copy
+// go through the Swin-T backbone (swin.rs:162-215); the decoder
+// (decoder.rs:790-926) concatenates each level's two runs (the half-size one
+// resized), squeezes the four levels at 1/32, and runs blocks 4..1 upwards,
+// each fed the previous output (resized and added onto the level's lateral
+// 1x1 convolution) and the image cut into patches; the head ends in f32.
+//
+// Planar f16 maps `[C/8][pixels][8]` throughout (rows y * w + x); every
+// concatenation is a plane offset. A Swin block: LayerNorm + window gather
+// into 64-row slots (49 tokens, the rest zero rows), qkv GEMM, fused window
+// attention (the 64 x 64 bias tables carry the reference's 49 x 49 tables,
+// its -100 shift masks, and -inf for the slots' padding keys), projection
+// GEMM scattered back onto the tokens, LayerNorm, fc1 + GELU, fc2 added on.
+#include "birefnet.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "igemm_sm100.cuh"
+
+namespace iec {
+
+namespace {
+
+constexpr int WS = 7, SHIFT = 3, NTOK = 49, INTER = 64, BRANCH = 256;
+constexpr int STAGE_C[4] = {96, 192, 384, 768}, STAGE_D[4] = {2, 2, 6, 2};
+constexpr int SIZES[4] = {1, 1, 3, 7};
+constexpr int LEVELS[4][2] = {{1728, 768}, {960, 384}, {480, 192}, {240, 96}};
+constexpr int PATCH_C[4] = {3072, 768, 192, 48};   // patches5..2 input channels
+constexpr int PATCH_OUT[4] = {192, 192, 96, 48};
+__constant__ float MEAN[3] = {0.485f, 0.456f, 0.406f}, STDV[3] = {0.229f, 0.224f, 0.225f};
+// Full-resolution tables: composed 5x5 [75], conv1 [27 * 64], bias1 [64],
+// conv_out [9 * 64], then bias_out and the composed bias.
+constexpr int FR_COMPOSED = 0, FR_CONV1 = 75, FR_BIAS1 = FR_CONV1 + 27 * 64, FR_OUT = FR_BIAS1 + 64,
+              FR_SCALARS = FR_OUT + 9 * 64, FR_TOTAL = FR_SCALARS + 2;
+
+int blocks_for(long long n, int sms) {
+  return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sms * 16));
+}
+
+long long pe(long long pixels) { return (long long)gemm_rows_alloc((int)pixels) * 8; }
+
+__device__ __forceinline__ void load8(const __half* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const float2 f = __half22float2(h[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__half* p, const float* v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    __half2 h2 = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ float sigmoid_f(float v) {
+  // math.rs:33-39: from exp(-|x|), so that neither tail cancels.
+  const float e = expf(-fabsf(v)), s = e / (e + 1.0f);
+  return v > 0.0f ? 1.0f - s : s;
+}
+
+// decoder.rs:462-476: source pixels and weights of output coordinate `out`.
+__device__ __forceinline__ void axis(int out, int len_in, int len_out, int& i0, int& i1, float& w0, float& w1) {
+  float pos = len_out == 1 ? 0.0f : (float)out * (float)(len_in - 1) / (float)(len_out - 1);
+  pos = fminf(fmaxf(pos, 0.0f), (float)(len_in - 1));
+  i0 = (int)pos;
+  i1 = min(i0 + 1, len_in - 1);
+  if (i0 == i1) {
+    w0 = 0.5f;
+    w1 = 0.5f;
+  } else {
+    w0 = fabsf(pos - (float)i0);
+    w1 = fabsf(pos - (float)i1);
+  }
+}
+
+// lib.rs:116-133: 8-bit RGB through the ImageNet normalisation (or a copy of
+// an already normalised image).
+__global__ void bir_prep(const void* __restrict__ src, int u8, long long n, float* __restrict__ dst) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    if (u8) {
+      const int c = (int)(i % 3);
+      dst[i] = ((float)static_cast<const uint8_t*>(src)[i] / 255.0f - MEAN[c]) / STDV[c];
+    } else {
+      dst[i] = static_cast<const float*>(src)[i];
+    }
+  }
+}
+
+// decoder.rs:443-521 on an f32 NHWC map (the half-size image).
+__global__ void bir_resize_f32(const float* __restrict__ src, int sh, int sw, int c, float* __restrict__ dst, int dh,
+                               int dw) {
+  const long long n = (long long)dh * dw;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int y = (int)(i / dw), x = (int)(i % dw);
+    int y1, y2, x1, x2;
+    float dy1, dy2, dx1, dx2;
+    axis(y, sh, dh, y1, y2, dy1, dy2);
+    axis(x, sw, dw, x1, x2, dx1, dx2);
+    for (int j = 0; j < c; j++) {
+      const float p11 = src[((long long)y1 * sw + x1) * c + j], p21 = src[((long long)y1 * sw + x2) * c + j];
+      const float p12 = src[((long long)y2 * sw + x1) * c + j], p22 = src[((long long)y2 * sw + x2) * c + j];
+      dst[i * c + j] = dx2 * dy2 * p11 + dx1 * dy2 * p21 + dx2 * dy1 * p12 + dx1 * dy1 * p22;
+    }
+  }
+}
+
+// The same resize on planar f16 maps, `planes` channel groups, optionally
+// added onto the destination (decoder.rs:500-519).
+__global__ void bir_resize_planar(const __half* __restrict__ src, long long src_plane, int sh, int sw,
+                                  __half* __restrict__ dst, long long dst_plane, int dh, int dw, int planes, int add) {
+  const long long n = (long long)dh * dw * planes;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int q = (int)(i / ((long long)dh * dw));
+    const long long p = i - (long long)q * dh * dw;
+    const int y = (int)(p / dw), x = (int)(p % dw);
+    int y1, y2, x1, x2;
+    float dy1, dy2, dx1, dx2;
+    axis(y, sh, dh, y1, y2, dy1, dy2);
+    axis(x, sw, dw, x1, x2, dx1, dx2);
+    const __half* s = src + q * src_plane;
+    float p11[8], p21[8], p12[8], p22[8], v[8];
+    load8(s + ((long long)y1 * sw + x1) * 8, p11);
+    load8(s + ((long long)y1 * sw + x2) * 8, p21);
+    load8(s + ((long long)y2 * sw + x1) * 8, p12);
+    load8(s + ((long long)y2 * sw + x2) * 8, p22);
+    __half* d = dst + q * dst_plane + p * 8;
+    float old[8];
+    if (add) load8(d, old);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float r = dx2 * dy2 * p11[j] + dx1 * dy2 * p21[j] + dx2 * dy1 * p12[j] + dx1 * dy1 * p22[j];
+      v[j] = add ? old[j] + r : r;
+    }
+    store8(d, v);
+  }
+}
+
+// swin.rs:188-204: each 4 x 4 patch's 48 values, (ky, kx, c) order.
+__global__ void bir_embed_gather(const float* __restrict__ img, int side, __half* __restrict__ dst, long long plane) {
+  const int grid = side / 4;
+  const long long n = (long long)grid * grid * 6;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int g = (int)(i % 6);
+    const long long t = i / 6;
+    const int ty = (int)(t / grid), tx = (int)(t % grid);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int j = 8 * g + e, ky = j / 12, kx = (j % 12) / 3, c = j % 3;
+      v[e] = img[(((long long)ty * 4 + ky) * side + tx * 4 + kx) * 3 + c];
+    }
+    store8(dst + g * plane + t * 8, v);
+  }
+}
+
+// swin.rs:366-404: merge each 2 x 2 group in the order (0,0), (1,0), (0,1),
+// (1,1) and normalise the 4c values.
+__global__ void bir_merge_ln(const __half* __restrict__ x, long long x_plane, int grid, int c,
+                             const float* __restrict__ gamma, const float* __restrict__ beta,
+                             __half* __restrict__ dst, long long dst_plane) {
+  const int half = grid / 2, tokens = half * half;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= tokens) return;
+  const int y = 2 * (r / half), xx = 2 * (r % half), groups = c / 8;
+  const int dy[4] = {0, 1, 0, 1}, dx[4] = {0, 0, 1, 1};
+  float sum = 0.0f;
+  for (int q = 0; q < 4; q++) {
+    const __half* base = x + ((long long)(y + dy[q]) * grid + xx + dx[q]) * 8;
+    for (int g = 0; g < groups; g++) {
+      float v[8];
+      load8(base + g * x_plane, v);
+#pragma unroll
+      for (int e = 0; e < 8; e++) sum += v[e];
+    }
+  }
+  const float mean = sum / (float)(4 * c);
+  float var = 0.0f;
+  for (int q = 0; q < 4; q++) {
+    const __half* base = x + ((long long)(y + dy[q]) * grid + xx + dx[q]) * 8;
+    for (int g = 0; g < groups; g++) {
+      float v[8];
+      load8(base + g * x_plane, v);
+#pragma unroll
+      for (int e = 0; e < 8; e++) var += (v[e] - mean) * (v[e] - mean);
+    }
+  }
+  const float inv = 1.0f / sqrtf(var / (float)(4 * c) + 1e-5f);
+  for (int q = 0; q < 4; q++) {
+    const __half* base = x + ((long long)(y + dy[q]) * grid + xx + dx[q]) * 8;
+    for (int g = 0; g < groups; g++) {
+      float v[8];
+      load8(base + g * x_plane, v);
+      const int ch0 = q * c + g * 8;
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = (v[e] - mean) * inv * gamma[ch0 + e] + beta[ch0 + e];
+      store8(dst + (long long)(q * groups + g) * dst_plane + (long long)r * 8, v);
+    }
+  }
+}
+
+// decoder.rs:144-150: per-channel sums of a 64-channel map (f32 partials,
+// f64 totals).
+__global__ void bir_channel_sums(const __half* __restrict__ t, long long plane, long long pixels,
+                                 double* __restrict__ sums) {
+  const int q = blockIdx.y;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
+       p += (long long)gridDim.x * blockDim.x) {
+    float v[8];
+    load8(t + q * plane + p * 8, v);
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[e] += v[e];
+  }
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    float v = acc[e];
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&sums[q * 8 + e], (double)v);
+  }
+}
+
+// decoder.rs:141-165: the pooling branch (mean, 1x1 to 256, ReLU) and its
+// share of conv1, as the bias of conv1 for this map.
+__global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, const float* __restrict__ pool_w,
+                              const float* __restrict__ pool_b, const float* __restrict__ conv1_pool,
+                              const float* __restrict__ conv1_bias, float* __restrict__ bias) {
+  __shared__ float mean[INTER], pooled[BRANCH];
+  const int t = threadIdx.x;
+  if (t < INTER) mean[t] = (float)(sums[t] / pixels);
+  __syncthreads();
+  if (t < BRANCH) {
+    float p = pool_b[t];
+    for (int c = 0; c < INTER; c++) p += mean[c] * pool_w[c * BRANCH + t];
+    pooled[t] = p > 0.0f ? p : 0.0f;
+  }
+  __syncthreads();
+  if (t < INTER) {
+    float b = conv1_bias[t];
+    for (int j = 0; j < BRANCH; j++) b += pooled[j] * conv1_pool[j * INTER + t];
+    bias[t] = b;
+  }
+}
+
+// decoder.rs:243-313: the deformable convolution's input: for pixel p and
+// tap k of a size x size kernel, the 64 channels of `t` sampled bilinearly
+// at the tap moved by its offset, times 2 sigmoid(modulator). `offs` holds
+// the offset convolution's 3 taps channels (y, x per tap, then the logits).
+__global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plane, int height, int width, int size,
+                                  const __half* __restrict__ offs, long long offs_plane, __half* __restrict__ out,
+                                  long long out_plane) {
+  const int taps = size * size;
+  const long long n = (long long)height * width * taps;
+  const float hs = (float)(size / 2), hf = (float)height, wf = (float)width;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int tap = (int)(i % taps);
+    const long long p = i / taps;
+    const int y = (int)(p / width), x = (int)(p % width);
+    auto ch = [&](int c) { return __half2float(offs[(long long)(c / 8) * offs_plane + p * 8 + (c % 8)]); };
+    const float py = ((float)y - hs + (float)(tap / size)) + ch(2 * tap);
+    const float px = ((float)x - hs + (float)(tap % size)) + ch(2 * tap + 1);
+    const float m = 2.0f * sigmoid_f(ch(2 * taps + tap));
+    float acc[64];
+#pragma unroll
+    for (int j = 0; j < 64; j++) acc[j] = 0.0f;
+    if (!(py <= -1.0f || py >= hf || px <= -1.0f || px >= wf)) {
+      const float y0f = floorf(py), x0f = floorf(px);
+      const float ly = py - y0f, lx = px - x0f, hy = 1.0f - ly, hx = 1.0f - lx;
+      const int y0 = (int)y0f, x0 = (int)x0f;
+      const int cy[4] = {y0, y0, y0 + 1, y0 + 1}, cx[4] = {x0, x0 + 1, x0, x0 + 1};
+      const float cw[4] = {hy * hx, hy * lx, ly * hx, ly * lx};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        if (cy[k] < 0 || cx[k] < 0 || cy[k] >= height || cx[k] >= width) continue;
+        const __half* src = t + ((long long)cy[k] * width + cx[k]) * 8;
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+          float v[8];
+          load8(src + g * t_plane, v);
+#pragma unroll
+          for (int e = 0; e < 8; e++) acc[g * 8 + e] += cw[k] * v[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = acc[g * 8 + e] * m;
+      store8(out + (long long)(tap * 8 + g) * out_plane + p * 8, v);
+    }
+  }
+}
+
+// decoder.rs:382-404: the gate sigmoid(b + w . g16) multiplied onto the
+// block's output (`planes` channel groups).
+__global__ void bir_gate(const __half* __restrict__ g16, long long g_plane, const float* __restrict__ w, float b,
+                         __half* __restrict__ out, long long out_plane, int planes, long long pixels) {
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
+       p += (long long)gridDim.x * blockDim.x) {
+    float v[16];
+    load8(g16 + p * 8, v);
+    load8(g16 + g_plane + p * 8, v + 8);
+    float s = b;
+    for (int k = 0; k < 16; k++) s = s + v[k] * w[k];
+    const float gate = sigmoid_f(s);
+    for (int q = 0; q < planes; q++) {
+      float o[8];
+      __half* d = out + q * out_plane + p * 8;
+      load8(d, o);
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[e] *= gate;
+      store8(d, o);
+    }
+  }
+}
+
+// decoder.rs:564-583: the image cut into g x g patches of size x size
+// pixels, patch (gy, gx) of colour c as channel (c g + gy) g + gx.
+__global__ void bir_patches(const float* __restrict__ img, int side, int size, __half* __restrict__ dst,
+                            long long plane) {
+  const int g = side / size, groups = 3 * g * g / 8;
+  const long long n = (long long)size * size * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int q = (int)(i % groups);
+    const long long p = i / groups;
+    const int y = (int)(p / size), x = (int)(p % size);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int ch = 8 * q + e, c = ch / (g * g), rem = ch % (g * g), gy = rem / g, gx = rem % g;
+      v[e] = img[(((long long)gy * size + y) * side + gx * size + x) * 3 + c];
+    }
+    store8(dst + q * plane + p * 8, v);
+  }
+}
+
+// decoder.rs:882-898: the head's 1x1 convolution to one channel, in f32.
+__global__ void bir_head(const __half* __restrict__ x, long long plane, const float* __restrict__ w, long long pixels,
+                         float* __restrict__ low) {
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
+       p += (long long)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int q = 0; q < 12; q++) {
+      float v[8];
+      load8(x + q * plane + p * 8, v);
+#pragma unroll
+      for (int e = 0; e < 8; e++) s = fmaf(v[e], w[q * 8 + e], s);
+    }
+    low[p] = s;
+  }
+}
+
+// decoder.rs:899-925 and 637-752: logits = head bias + the low-resolution
+// logits resized to the image + the full-resolution branch, as the composed
+// 5x5 convolution inside and the two 3x3 convolutions at the border.
+__global__ void bir_logits(const float* __restrict__ low, int lg, const float* __restrict__ img, int side,
+                           const float* __restrict__ fr, float head_b, float* __restrict__ logits) {
+  const long long n = (long long)side * side;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int y = (int)(i / side), x = (int)(i % side);
+    int y1, y2, x1, x2;
+    float dy1, dy2, dx1, dx2;
+    axis(y, lg, side, y1, y2, dy1, dy2);
+    axis(x, lg, side, x1, x2, dx1, dx2);
+    const float v = dx2 * dy2 * low[y1 * lg + x1] + dx1 * dy2 * low[y1 * lg + x2] + dx2 * dy1 * low[y2 * lg + x1] +
+                    dx1 * dy1 * low[y2 * lg + x2];
+    float d = head_b + v;
+    auto pix = [&](int yy, int xx, int c) {
+      return (yy >= 0 && xx >= 0 && yy < side && xx < side) ? img[((long long)yy * side + xx) * 3 + c] : 0.0f;
+    };
+    float s;
+    if (y == 0 || x == 0 || y == side - 1 || x == side - 1) {
+      s = fr[FR_SCALARS];
+      for (int dd = 0; dd < 9; dd++) {
+        const int qy = y + dd / 3 - 1, qx = x + dd % 3 - 1;
+        if (qy < 0 || qx < 0 || qy >= side || qx >= side) continue;
+        float dot = 0.0f;
+        for (int k = 0; k < INTER; k++) {
+          float mid = fr[FR_BIAS1 + k];
+          for (int e = 0; e < 9; e++) {
+            const int py = qy + e / 3 - 1, px = qx + e % 3 - 1;
+            if (py < 0 || px < 0 || py >= side || px >= side) continue;
+            for (int c = 0; c < 3; c++) mid += pix(py, px, c) * fr[FR_CONV1 + (e * 3 + c) * INTER + k];
+          }
+          dot += mid * fr[FR_OUT + dd * INTER + k];
+        }
+        s += dot;
+      }
+    } else {
+      s = fr[FR_SCALARS + 1];
+      for (int e = 0; e < 25; e++) {
+        const int py = y + e / 5 - 2, px = x + e % 5 - 2;
+        s += fr[FR_COMPOSED + e * 3] * pix(py, px, 0) + fr[FR_COMPOSED + e * 3 + 1] * pix(py, px, 1) +
+             fr[FR_COMPOSED + e * 3 + 2] * pix(py, px, 2);
+      }
+    }
+    logits[i] = d + s;
+  }
+}
+
+void pack(WeightFile& f, PackedWeights& pw, const std::string& name, int taps, int k, int n, bool bias) {
+  HostTensor w = f.take_tensor(name + ".weight", {(size_t)taps * k, (size_t)n});
+  std::vector<float> b;
+  if (bias) b = f.take(name + ".bias", {(size_t)n});
+  pack_weights(pw, w.values, taps, k, n, bias ? b.data() : nullptr);
+}
+
+void upload(DeviceBuffer& b, const std::vector<float>& v) {
+  b.reserve(v.size() * 4);
+  IEC_CUDA(cudaMemcpy(b.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+}
+
+// swin.rs:31-51 tables widened to the 64-row window slots: the reference's
+// 49 x 49 position bias (plus its -100 masks between the regions a shift
+// brought together, per window class), -inf towards the slots' 15 padding
+// keys, and zeros in the padding queries' rows (their outputs are dropped).
+std::vector<float> slot_tables(const std::vector<float>& position, int heads, bool shifted) {
+  const int classes = shifted ? 4 : 1;
+  std::vector<float> t((size_t)classes * heads * 64 * 64);
+  auto region = [](int v, bool last) { return (last && v >= WS - SHIFT) ? 1 : 0; };
+  for (int cls = 0; cls < classes; cls++) {
+    const bool last_col = cls & 1, last_row = cls & 2;
+    auto id = [&](int i) { return region(i / WS, last_row) * 2 + region(i % WS, last_col); };
+    for (int h = 0; h < heads; h++)
+      for (int i = 0; i < 64; i++)
+        for (int j = 0; j < 64; j++) {
+          float v;
+          if (j >= NTOK)
+            v = -INFINITY;
+          else if (i >= NTOK)
+            v = 0.0f;
+          else
+            v = position[((size_t)h * NTOK + i) * NTOK + j] + (shifted && id(i) != id(j) ? -100.0f : 0.0f);
+          t[(((size_t)cls * heads + h) * 64 + i) * 64 + j] = v;
+        }
+  }
+  return t;
+}
+
+}  // namespace
+
+struct Birefnet::SwinBlock {
+  int c = 0, heads = 0;
+  bool shifted = false;
+  DeviceBuffer n1g, n1b, n2g, n2b, bias;
+  PackedWeights qkv, proj, fc1, fc2;
+};
+
+struct Birefnet::Stage {
+  int c = 0;
+  std::vector<SwinBlock> blocks;
+  DeviceBuffer ng, nb, mg, mb;
+  PackedWeights merge;
+  bool has_merge = false;
+};
+
+struct Birefnet::DBlock {
+  int cin = 0, cout = 0;
+  PackedWeights conv_in, conv_out, gdt, offsets[4], branch[4], conv1;
+  bool gated = false;
+  DeviceBuffer gw, pool_w, pool_b, conv1_pool, conv1_bias;
+  float gb = 0.0f;
+};
+
+struct Birefnet::Patches {
+  PackedWeights conv1, conv_out;
+};
+
+Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
+  WeightFile f = WeightFile::read(path, "BIREFNET");
+  DeviceScope scope(dev_);
+  pack(f, embed_, "patch_embed", 1, 48, 96, true);
+  upload(embed_g_, f.take("patch_embed.norm.weight", {96}));
+  upload(embed_b_, f.take("patch_embed.norm.bias", {96}));
+  for (int s = 0; s < 4; s++) {
+    auto st = std::make_unique<Stage>();
+    const int c = STAGE_C[s], heads = c / 32;
+    st->c = c;
+    for (int b = 0; b < STAGE_D[s]; b++) {
+      const std::string p = "stage" + std::to_string(s) + ".block" + std::to_string(b);
+      SwinBlock blk;
+      blk.c = c;
+      blk.heads = heads;
+      blk.shifted = b % 2 == 1;
+      upload(blk.n1g, f.take(p + ".norm1.weight", {(size_t)c}));
+      upload(blk.n1b, f.take(p + ".norm1.bias", {(size_t)c}));
+      pack(f, blk.qkv, p + ".qkv", 1, c, 3 * c, true);
+      upload(blk.bias, slot_tables(f.take(p + ".position_bias", {(size_t)heads, NTOK, NTOK}), heads, blk.shifted));
+      pack(f, blk.proj, p + ".proj", 1, c, c, true);
+      upload(blk.n2g, f.take(p + ".norm2.weight", {(size_t)c}));
+      upload(blk.n2b, f.take(p + ".norm2.bias", {(size_t)c}));
+      pack(f, blk.fc1, p + ".fc1", 1, c, 4 * c, true);
+      pack(f, blk.fc2, p + ".fc2", 1, 4 * c, c, true);
+      st->blocks.push_back(std::move(blk));
+    }
+    const std::string sn = "stage" + std::to_string(s);
+    if (s < 3) {
+      st->has_merge = true;
+      upload(st->mg, f.take(sn + ".merge.norm.weight", {(size_t)4 * c}));
+      upload(st->mb, f.take(sn + ".merge.norm.bias", {(size_t)4 * c}));
+      pack(f, st->merge, sn + ".merge", 1, 4 * c, 2 * c, false);
+    }
+    upload(st->ng, f.take(sn + ".norm.weight", {(size_t)c}));
+    upload(st->nb, f.take(sn + ".norm.bias", {(size_t)c}));
+    stages_.push_back(std::move(st));
+  }
+  auto load_block = [&](const std::string& p, int cin, int cout, bool gate) {
+    auto b = std::make_unique<DBlock>();
+    b->cin = cin;
+    b->cout = cout;
+    pack(f, b->conv_in, p + ".conv_in", 9, cin, INTER, true);
+    pack(f, b->conv_out, p + ".conv_out", 9, INTER, cout, true);
+    if (gate) {
+      b->gated = true;
+      pack(f, b->gdt, p + ".gdt", 9, cout, 16, true);
+      upload(b->gw, f.take(p + ".gdt_attn.weight", {16, 1}));
+      b->gb = f.take(p + ".gdt_attn.bias", {1})[0];
+    }
+    for (int i = 0; i < 4; i++) {
+      const int taps = SIZES[i] * SIZES[i];
+      const std::string br = p + ".aspp.branch" + std::to_string(i);
+      pack(f, b->offsets[i], br + ".offset", taps, INTER, 3 * taps, true);
+      pack(f, b->branch[i], br, 1, taps * INTER, BRANCH, true);
+    }
+    upload(b->pool_w, f.take(p + ".aspp.pool.weight", {INTER, BRANCH}));
+    upload(b->pool_b, f.take(p + ".aspp.pool.bias", {BRANCH}));
+    HostTensor c1 = f.take_tensor(p + ".aspp.conv1.weight", {5 * BRANCH, INTER});
+    upload(b->conv1_bias, f.take(p + ".aspp.conv1.bias", {INTER}));
+    std::vector<float> rows(c1.values.begin(), c1.values.begin() + 4 * BRANCH * INTER);
+    std::vector<float> zero(INTER, 0.0f);
+    // conv1's bias is written per run (the pooling branch's share).
+    pack_weights(b->conv1, rows, 1, 4 * BRANCH, INTER, zero.data());
+    upload(b->conv1_pool, std::vector<float>(c1.values.begin() + 4 * BRANCH * INTER, c1.values.end()));
+    return b;
+  };
+  squeeze_ = load_block("squeeze", 2880, 1536, false);
+  for (int i = 0; i < 4; i++)
+    blocks_.push_back(load_block("block" + std::to_string(4 - i), LEVELS[i][0], LEVELS[i][1], i < 3));
+  const int lat[3][2] = {{4, 768}, {3, 384}, {2, 192}};
+  for (int i = 0; i < 3; i++) pack(f, laterals_[i], "lateral" + std::to_string(lat[i][0]), 1, lat[i][1], lat[i][1], true);
+  for (int i = 0; i < 4; i++) {
+    auto pt = std::make_unique<Patches>();
+    const std::string p = "patches" + std::to_string(5 - i);
+    pack(f, pt->conv1, p + ".conv1", 9, PATCH_C[i], INTER, true);
+    pack(f, pt->conv_out, p + ".conv_out", 9, INTER, PATCH_OUT[i], true);
+    patches_.push_back(std::move(pt));
+  }
+  upload(head_w_, f.take("head.weight", {96, 1}));
+  head_b_ = f.take("head.bias", {1})[0];
+  {
+    // decoder.rs:605-633: the composed 5x5 convolution, in double.
+    const std::vector<float> conv1 = f.take("patches1.conv1.weight", {27, INTER});
+    const std::vector<float> bias1 = f.take("patches1.conv1.bias", {INTER});
+    const std::vector<float> conv_out = f.take("patches1.conv_out.weight", {9 * INTER, 1});
+    const float bias_out = f.take("patches1.conv_out.bias", {1})[0];
+    std::vector<double> comp(75, 0.0);
+    double cb = bias_out;
+    for (int d = 0; d < 9; d++)
+      for (int k = 0; k < INTER; k++) {
+        const double w2 = conv_out[d * INTER + k];
+        cb += w2 * (double)bias1[k];
+        for (int e = 0; e < 9; e++) {
+          const int ey = d / 3 + e / 3, ex = d % 3 + e % 3;
+          for (int c = 0; c < 3; c++) comp[(ey * 5 + ex) * 3 + c] += w2 * (double)conv1[(e * 3 + c) * INTER + k];
+        }
+      }
+    std::vector<float> fr(FR_TOTAL);
+    for (int i = 0; i < 75; i++) fr[FR_COMPOSED + i] = (float)comp[i];
+    std::copy(conv1.begin(), conv1.end(), fr.begin() + FR_CONV1);
+    std::copy(bias1.begin(), bias1.end(), fr.begin() + FR_BIAS1);
+    std::copy(conv_out.begin(), conv_out.end(), fr.begin() + FR_OUT);
+    fr[FR_SCALARS] = bias_out;
+    fr[FR_SCALARS + 1] = (float)cb;
+    upload(full_, fr);
+  }
+  f.finish();
+  sums_.reserve(INTER * sizeof(double));
+  IEC_CUDA(cudaDeviceSynchronize());
+}
+
+Birefnet::~Birefnet() {
+  if (dev_.poisoned()) {
+    for (DeviceBuffer* b : {&img_, &himg_, &patch_rows_, &x_, &tok_, &qkv_, &att_, &ln_, &hid_, &mrg_, &lev_[0],
+                            &lev_[1], &lev_[2], &hf_[0], &hf_[1], &hf_[2], &hf_[3], &x4_, &in_[0], &in_[1], &in_[2],
+                            &in_[3], &outb_[0], &outb_[1], &outb_[2], &out1_, &t_, &t2_, &offs_, &samp_, &cat_, &g16_,
+                            &sums_, &low_, &stack_, &pmid_, &host_in, &host_out})
+      b->leak();
+  }
+}
+
+void Birefnet::ensure(int side) {
+  if (side == alloc_side_) return;
+  const long long g0 = side / 4, P0 = g0 * g0;
+  auto bytes = [](long long planes, long long elems) { return (size_t)(planes * elems * 2); };
+  img_.reserve((size_t)side * side * 3 * 4);
+  himg_.reserve((size_t)(side / 2) * (side / 2) * 3 * 4);
+  patch_rows_.reserve(bytes(6, pe(P0)));
+  size_t bx = 0, btok = 0, bqkv = 0, bln = 0, bhid = 0, bmrg = 0;
+  long long g = g0;
+  for (int s = 0; s < 4; s++, g /= 2) {
+    const long long c = STAGE_C[s], tokens = g * g, pad = (g + WS - 1) / WS * WS, slots = (pad / WS) * (pad / WS) * 64;
+    bx = std::max(bx, bytes(c / 8, pe(tokens)));
+    btok = std::max(btok, bytes(c / 8, pe(slots)));
+    bqkv = std::max(bqkv, bytes(3 * c / 8, pe(slots)));
+    bln = std::max(bln, bytes(c / 8, pe(tokens)));
+    bhid = std::max(bhid, bytes(4 * c / 8, pe(tokens)));
+    if (s < 3) bmrg = std::max(bmrg, bytes(4 * c / 8, pe(tokens / 4)));
+  }
+  x_.reserve(bx);
+  tok_.reserve(btok);
+  att_.reserve(btok);
+  qkv_.reserve(bqkv);
+  ln_.reserve(bln);
+  hid_.reserve(bhid);
+  mrg_.reserve(bmrg);
+  for (int i = 0; i < 3; i++) {
+    const long long gi = g0 >> i;
+    lev_[i].reserve(bytes(2 * STAGE_C[i] / 8, pe(gi * gi)));
+  }
+  for (int i = 0; i < 4; i++) {
+    const long long hg = (g0 >> i) / 2;
+    hf_[i].reserve(bytes(STAGE_C[i] / 8, pe(hg * hg)));
+  }
+  const long long g3 = g0 >> 3;
+  x4_.reserve(bytes(360, pe(g3 * g3)));
+  for (int i = 0; i < 4; i++) {
+    const long long gi = g0 >> (3 - i);
+    in_[i].reserve(bytes(LEVELS[i][0] / 8, pe(gi * gi)));
+    if (i < 3)
+      outb_[i].reserve(bytes(LEVELS[i][1] / 8, pe(gi * gi)));
+    else
+      out1_.reserve(bytes(12, pe(gi * gi)));
+  }
+  t_.reserve(bytes(8, pe(P0)));
+  t2_.reserve(bytes(8, pe(P0)));
+  offs_.reserve(bytes(19, pe(P0)));
+  samp_.reserve(bytes(49 * 8, pe(P0)));
+  cat_.reserve(bytes(128, pe(P0)));
+  g16_.reserve(bytes(2, pe(P0)));
+  low_.reserve((size_t)P0 * 4);
+  size_t bstack = 0;
+  for (int i = 0; i < 4; i++) {
+    const long long gi = g0 >> (3 - i);
+    bstack = std::max(bstack, bytes(PATCH_C[i] / 8, pe(gi * gi)));
+  }
+  stack_.reserve(bstack);
+  pmid_.reserve(bytes(8, pe(P0)));
+  alloc_side_ = side;
+}
+
+void Birefnet::backbone(const float* img, int side, __half* const dst[4], const long long dst_plane[4],
+                        const int plane0[4], cudaStream_t s) {
+  const int sms = dev_.sms();
+  int grid = side / 4;
+  long long tokens = (long long)grid * grid;
+  bir_embed_gather<<<blocks_for(tokens * 6, sms), 256, 0, s>>>(img, side, patch_rows_.as<__half>(), pe(tokens));
+  IEC_CUDA(cudaGetLastError());
+  __half* x = x_.as<__half>();
+  {
+    GemmOutSpec o;
+    o.mode = OUT_STORE;
+    o.out = x;
+    o.plane_elems = pe(tokens);
+    gemm_rows(dev_, embed_, patch_rows_.as<__half>(), pe(tokens), (int)tokens, ACT_NONE, o, s);
+    layer_norm_planar(x, pe(tokens), 0, (int)tokens, 96, embed_g_.as<float>(), embed_b_.as<float>(), x, pe(tokens),
+                      nullptr, s);
+  }
+  for (int si = 0; si < 4; si++) {
+    const Stage& st = *stages_[si];
+    const int c = st.c;
+    const long long xp = pe(tokens);
+    const int pad = (grid + WS - 1) / WS * WS, wins = pad / WS;
+    const long long slots = (long long)wins * wins * 64, sp = pe(slots);
+    for (const SwinBlock& B : st.blocks) {
+      const int shift = B.shifted ? SHIFT : 0;
+      // attention: x += proj(attn(window(LN1(x))))
+      const WindowMap wm{WS, pad, pad, grid, grid, shift};
+      layer_norm_planar(x, xp, 0, (int)slots, c, B.n1g.as<float>(), B.n1b.as<float>(), tok_.as<__half>(), sp, &wm, s);
+      GemmOutSpec o;
+      o.mode = OUT_STORE;
+      o.out = qkv_.as<__half>();
+      o.plane_elems = sp;
+      gemm_rows(dev_, B.qkv, tok_.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
+      window_attention(qkv_.as<__half>(), sp, c, (int)(slots / 64), B.bias.as<float>(), B.shifted, wins, wins,
+                       att_.as<__half>(), sp, s);
+      o.mode = OUT_WINDOW_ACCUM;
+      o.out = x;
+      o.plane_elems = xp;
+      o.map_h = grid;
+      o.map_w = grid;
+      o.shift = shift;
+      o.win_ws = WS;
+      o.pad_h = pad;
+      o.pad_w = pad;
+      gemm_rows(dev_, B.proj, att_.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
+      // MLP: x += fc2(GELU(fc1(LN2(x))))
+      layer_norm_planar(x, xp, 0, (int)tokens, c, B.n2g.as<float>(), B.n2b.as<float>(), ln_.as<__half>(), xp, nullptr,
+                        s);
+      GemmOutSpec h;
+      h.mode = OUT_STORE;
+      h.out = hid_.as<__half>();
+      h.plane_elems = xp;
+      gemm_rows(dev_, B.fc1, ln_.as<__half>(), xp, (int)tokens, ACT_GELU, h, s);
+      GemmOutSpec a;
+      a.mode = OUT_ACCUM;
+      a.out = x;
+      a.plane_elems = xp;
+      gemm_rows(dev_, B.fc2, hid_.as<__half>(), xp, (int)tokens, ACT_NONE, a, s);
+    }
+    // the stage's normalised output
+    layer_norm_planar(x, xp, 0, (int)tokens, c, st.ng.as<float>(), st.nb.as<float>(),
+                      dst[si] + (long long)plane0[si] * dst_plane[si], dst_plane[si], nullptr, s);
+    if (st.has_merge) {
+      const long long mt = tokens / 4, mp = pe(mt);
+      bir_merge_ln<<<(int)((mt + 127) / 128), 128, 0, s>>>(x, xp, grid, c, st.mg.as<float>(), st.mb.as<float>(),
+                                                           mrg_.as<__half>(), mp);
+      IEC_CUDA(cudaGetLastError());
+      GemmOutSpec o;
+      o.mode = OUT_STORE;
+      o.out = x;
+      o.plane_elems = mp;
+      gemm_rows(dev_, st.merge, mrg_.as<__half>(), mp, (int)mt, ACT_NONE, o, s);
+      grid /= 2;
+      tokens = mt;
+    }
+  }
+}
+
+void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int cin, int g, __half* out,
+                     long long out_plane, int plane0, cudaStream_t s) {
+  const int sms = dev_.sms();
+  const long long P = (long long)g * g, pp = pe(P);
+  (void)cin;
+  __half* t = t_.as<__half>();
+  // t = ReLU(conv_in(x))
+  {
+    GemmOutSpec o;
+    o.mode = OUT_STORE;
+    o.out = t;
+    o.plane_elems = pp;
+    gemm_conv3(dev_, b.conv_in, x, x_plane, g, g, ACT_RELU, o, s);
+  }
+  // ASPP (decoder.rs:138-236): the pooled bias, four deformable branches
+  // into `cat`, conv1 + bias + ReLU.
+  IEC_CUDA(cudaMemsetAsync(sums_.get(), 0, INTER * sizeof(double), s));
+  bir_channel_sums<<<dim3(std::max(1, std::min(64, (int)((P + 255) / 256))), 8), 256, 0, s>>>(t, pp, P,
+                                                                                              sums_.as<double>());
+  IEC_CUDA(cudaGetLastError());
+  bir_aspp_bias<<<1, 256, 0, s>>>(sums_.as<double>(), (double)P, b.pool_w.as<float>(), b.pool_b.as<float>(),
+                                  b.conv1_pool.as<float>(), b.conv1_bias.as<float>(), b.conv1.bias.as<float>());
+  IEC_CUDA(cudaGetLastError());
+  for (int i = 0; i < 4; i++) {
+    const int k = SIZES[i], taps = k * k;
+    std::vector<Tap> tl;
+    for (int ky = 0; ky < k; ky++)
+      for (int kx = 0; kx < k; kx++) tl.push_back({ky - k / 2, kx - k / 2, 0});
+    GemmOutSpec o;
+    o.mode = OUT_STORE;
+    o.out = offs_.as<__half>();
+    o.plane_elems = pp;
+    gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, s);
+    bir_deform_sample<<<blocks_for(P * taps, sms), 256, 0, s>>>(t, pp, g, g, k, offs_.as<__half>(), pp,
+                                                                samp_.as<__half>(), pp);
+    IEC_CUDA(cudaGetLastError());
+    GemmOutSpec c;
+    c.mode = OUT_STORE;
+    c.out = cat_.as<__half>();
+    c.plane_elems = pp;
+    c.plane0 = i * (BRANCH / 8);
+    gemm_rows(dev_, b.branch[i], samp_.as<__half>(), pp, (int)P, ACT_RELU, c, s);
+  }
+  __half* t2 = t2_.as<__half>();
+  {
+    GemmOutSpec o;
+    o.mode = OUT_STORE;
+    o.out = t2;
+    o.plane_elems = pp;
+    gemm_rows(dev_, b.conv1, cat_.as<__half>(), pp, (int)P, ACT_RELU, o, s);
+  }
+  // out = conv_out(t2) [* gate]
+  GemmOutSpec o;
+  o.mode = OUT_STORE;
+  o.out = out;
+  o.plane_elems = out_plane;
+  o.plane0 = plane0;
+  gemm_conv3(dev_, b.conv_out, t2, pp, g, g, ACT_NONE, o, s);
+  if (b.gated) {
+    __half* base = out + (long long)plane0 * out_plane;
+    GemmOutSpec go;
+    go.mode = OUT_STORE;
+    go.out = g16_.as<__half>();
+    go.plane_elems = pp;
+    gemm_conv3(dev_, b.gdt, base, out_plane, g, g, ACT_RELU, go, s);
+    bir_gate<<<blocks_for(P, sms), 256, 0, s>>>(g16_.as<__half>(), pp, b.gw.as<float>(), b.gb, base, out_plane,
+                                                 b.cout / 8, P);
+    IEC_CUDA(cudaGetLastError());
+  }
+}
+
+void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStream_t s) {
+  if (side <= 0 || side % 64 != 0)
+    throw Error(ERR_INPUT, "side " + std::to_string(side) + " is not a positive multiple of 64");
+  ensure(side);
+  const int sms = dev_.sms();
+  const long long n = (long long)side * side * 3;
+  float* img = img_.as<float>();
+  bir_prep<<<blocks_for(n, sms), 256, 0, s>>>(image, u8 ? 1 : 0, n, img);
+  IEC_CUDA(cudaGetLastError());
+  const int hs = side / 2;
+  bir_resize_f32<<<blocks_for((long long)hs * hs, sms), 256, 0, s>>>(img, side, side, 3, himg_.as<float>(), hs, hs);
+  IEC_CUDA(cudaGetLastError());
+
+  const int g0 = side / 4, g[4] = {g0, g0 / 2, g0 / 4, g0 / 8};
+  // Full-size features straight into their levels (level 3 into x4, after
+  // the three resized levels' 168 planes); half-size ones into hf.
+  {
+    __half* dst[4] = {lev_[0].as<__half>(), lev_[1].as<__half>(), lev_[2].as<__half>(), x4_.as<__half>()};
+    const long long dp[4] = {pe((long long)g[0] * g[0]), pe((long long)g[1] * g[1]), pe((long long)g[2] * g[2]),
+                             pe((long long)g[3] * g[3])};
+    const int p0[4] = {0, 0, 0, 168};
+    backbone(img, side, dst, dp, p0, s);
+  }
+  {
+    __half* dst[4] = {hf_[0].as<__half>(), hf_[1].as<__half>(), hf_[2].as<__half>(), hf_[3].as<__half>()};
+    long long dp[4];
+    for (int i = 0; i < 4; i++) dp[i] = pe((long long)(g[i] / 2) * (g[i] / 2));
+    const int p0[4] = {0, 0, 0, 0};
+    backbone(himg_.as<float>(), hs, dst, dp, p0, s);
+  }
+  // Each level's second half: the half-size run resized to the level's grid.
+  for (int i = 0; i < 4; i++) {
+    const int c8 = STAGE_C[i] / 8, hg = g[i] / 2;
+    __half* dst = i < 3 ? lev_[i].as<__half>() : x4_.as<__half>();
+    const int plane = i < 3 ? c8 : 168 + c8;
+    const long long dp = pe((long long)g[i] * g[i]);
+    bir_resize_planar<<<blocks_for((long long)g[i] * g[i] * c8, sms), 256, 0, s>>>(
+        hf_[i].as<__half>(), pe((long long)hg * hg), hg, hg, dst + plane * dp, dp, g[i], g[i], c8, 0);
+    IEC_CUDA(cudaGetLastError());
+  }
+  // x4: levels 1-3 resized to 1/32 (planes 0..167), level 4 after them.
+  {
+    const long long p3 = pe((long long)g[3] * g[3]);
+    int plane = 0;
+    for (int i = 0; i < 3; i++) {
+      const int c8 = 2 * STAGE_C[i] / 8;
+      bir_resize_planar<<<blocks_for((long long)g[3] * g[3] * c8, sms), 256, 0, s>>>(
+          lev_[i].as<__half>(), pe((long long)g[i] * g[i]), g[i], g[i], x4_.as<__half>() + plane * p3, p3, g[3], g[3],
+          c8, 0);
+      IEC_CUDA(cudaGetLastError());
+      plane += c8;
+    }
+  }
+  // squeeze -> block 4's input planes 0..191
+  block(*squeeze_, x4_.as<__half>(), pe((long long)g[3] * g[3]), 2880, g[3], in_[0].as<__half>(),
+        pe((long long)g[3] * g[3]), 0, s);
+  const int main_c[4] = {1536, 768, 384, 192};
+  for (int i = 0; i < 4; i++) {
+    const int level = 3 - i, gi = g[level], cin = LEVELS[i][0];
+    const long long ip = pe((long long)gi * gi);
+    __half* in = in_[i].as<__half>();
+    if (i > 0) {
+      // lateral(level features) + previous output resized
+      GemmOutSpec o;
+      o.mode = OUT_STORE;
+      o.out = in;
+      o.plane_elems = ip;
+      gemm_rows(dev_, laterals_[i - 1], lev_[level].as<__half>(), ip, gi * gi, ACT_NONE, o, s);
+      const int pg = g[level + 1];
+      const __half* prev = outb_[i - 1].as<__half>();
+      bir_resize_planar<<<blocks_for((long long)gi * gi * (main_c[i] / 8), sms), 256, 0, s>>>(
+          prev, pe((long long)pg * pg), pg, pg, in, ip, gi, gi, main_c[i] / 8, 1);
+      IEC_CUDA(cudaGetLastError());
+    }
+    // patches of the image, through two convolutions, after the main planes
+    {
+      const Patches& pt = *patches_[i];
+      const int groups = PATCH_C[i] / 8;
+      const long long sp = pe((long long)gi * gi);
+      bir_patches<<<blocks_for((long long)gi * gi * groups, sms), 256, 0, s>>>(img, side, gi, stack_.as<__half>(), sp);
+      IEC_CUDA(cudaGetLastError());
+      GemmOutSpec o;
+      o.mode = OUT_STORE;
+      o.out = pmid_.as<__half>();
+      o.plane_elems = sp;
+      gemm_conv3(dev_, pt.conv1, stack_.as<__half>(), sp, gi, gi, ACT_NONE, o, s);
+      o.out = in;
+      o.plane_elems = ip;
+      o.plane0 = main_c[i] / 8;
+      gemm_conv3(dev_, pt.conv_out, pmid_.as<__half>(), sp, gi, gi, ACT_NONE, o, s);
+    }
+    __half* out = i < 3 ? outb_[i].as<__half>() : out1_.as<__half>();
+    block(*blocks_[i], in, ip, cin, gi, out, ip, 0, s);
+  }
+  // head
+  {
+    const long long P0 = (long long)g0 * g0;
+    bir_head<<<blocks_for(P0, sms), 256, 0, s>>>(out1_.as<__half>(), pe(P0), head_w_.as<float>(), P0,
+                                                  low_.as<float>());
+    IEC_CUDA(cudaGetLastError());
+    bir_logits<<<blocks_for((long long)side * side, sms), 256, 0, s>>>(low_.as<float>(), g0, img, side,
+                                                                        full_.as<float>(), head_b_, logits);
+    IEC_CUDA(cudaGetLastError());
+  }
+}
+
+}  // namespace iec

@@ -1,0 +1,73 @@
+// BiRefNet-lite (background removal) on the CUDA backend.
+//
+// Replaces crates/birefnet-native/src/gpu.rs (the Vulkan network) behind the
+// model's public API (lib.rs): the Swin-T backbone of swin.rs (patch
+// embedding, 7 x 7 shifted-window attention in 64-row window slots, MLPs,
+// patch merges) on the general tcgen05 GEMM and the fused window attention,
+// run on the image and on its half-size copy; and the decoder of decoder.rs
+// (3x3 convolutions, deformable ASPPs as a bilinear-sample kernel feeding
+// GEMMs, aligned-corner resizes, image patches, gates), ending in an f32
+// head: the decoder's low-resolution logits resized and the full-resolution
+// patch branch's composed 5x5 convolution added per pixel. Concatenations
+// cost nothing: every map is planar, and each producer writes its channel
+// planes straight into the consumer's input.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gemm.h"
+#include "runtime.h"
+
+namespace iec {
+
+class Birefnet {
+ public:
+  Birefnet(const std::string& path, const Options& opt);
+  ~Birefnet();
+  Device& device() { return dev_; }
+
+  // lib.rs:116-172 on device buffers: `image` side x side x 3, 8-bit RGB
+  // (`u8`) or already normalised f32; `logits` side x side f32.
+  void run(const void* image, bool u8, int side, float* logits, cudaStream_t s);
+
+  DeviceBuffer host_in, host_out;  // staging of the host entry points
+
+  struct SwinBlock;
+  struct Stage;
+  struct DBlock;
+  struct Patches;
+
+ private:
+  void ensure(int side);
+  // swin.rs:162-215 on `img` (f32 NHWC, side x side); stage i's normalised
+  // output goes to planes from plane0[i] of dst[i] (dst_plane[i] elements per
+  // plane).
+  void backbone(const float* img, int side, __half* const dst[4], const long long dst_plane[4], const int plane0[4],
+                cudaStream_t s);
+  // decoder.rs:343-406: `x` (cin channels, g x g) -> out planes from `plane0`
+  // of `out` (cout channels).
+  void block(const DBlock& b, const __half* x, long long x_plane, int cin, int g, __half* out, long long out_plane,
+             int plane0, cudaStream_t s);
+
+  Device dev_;
+  PackedWeights embed_;
+  DeviceBuffer embed_g_, embed_b_;
+  std::vector<std::unique_ptr<Stage>> stages_;
+  std::unique_ptr<DBlock> squeeze_;
+  std::vector<std::unique_ptr<DBlock>> blocks_;
+  PackedWeights laterals_[3];
+  std::vector<std::unique_ptr<Patches>> patches_;
+  DeviceBuffer head_w_, full_;  // head [96]; full-resolution branch tables
+  float head_b_ = 0.0f;
+  int alloc_side_ = 0;
+  // working buffers
+  DeviceBuffer img_, himg_, patch_rows_, x_, tok_, qkv_, att_, ln_, hid_, mrg_;
+  DeviceBuffer lev_[3], hf_[4], x4_, in_[4], outb_[3], out1_, t_, t2_, offs_, samp_, cat_, g16_, sums_, low_, stack_,
+      pmid_;
+};
+
+}  // namespace iec

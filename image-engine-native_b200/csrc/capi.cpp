@@ -10,6 +10,7 @@
 
 #include "../../include/iec_cuda.h"
 #include "realesrgan.h"
+#include "birefnet.h"
 #include "lama.h"
 #include "scunet.h"
 
@@ -85,6 +86,13 @@ struct iec_lama {
   uint32_t tag = TAG;
   std::unique_ptr<Lama> model;
   ~iec_lama() { tag = 0; }
+};
+
+struct iec_birefnet {
+  static constexpr uint32_t TAG = 0x42524e54;  // "BRNT"
+  uint32_t tag = TAG;
+  std::unique_ptr<Birefnet> model;
+  ~iec_birefnet() { tag = 0; }
 };
 
 namespace {
@@ -426,6 +434,75 @@ iec_status iec_lama_run_device(iec_lama* model, const float* image, const float*
     DeviceScope scope(m.device());
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
     m.run(image, false, mask, false, out, false, (int)width, (int)height, nullptr, s);
+  });
+}
+
+// -------------------------------------------------------------------- BiRefNet
+iec_status iec_birefnet_load(const char* weights_path, const iec_options* options, iec_birefnet** out) {
+  return guard([&] {
+    need(out, "out");
+    *out = nullptr;
+    need(weights_path, "weights_path");
+    auto h = std::make_unique<iec_birefnet>();
+    h->model = std::make_unique<Birefnet>(weights_path, to_options(options));
+    *out = h.release();
+  });
+}
+
+void iec_birefnet_free(iec_birefnet* model) {
+  if (valid(model)) delete model;
+}
+
+const char* iec_birefnet_device_name(const iec_birefnet* model) {
+  return valid(model) ? model->model->device().name().c_str() : "";
+}
+
+// crates/birefnet-native/src/lib.rs:175-187 (check_size), with a bound on
+// the side.
+static void check_birefnet_size(size_t side) {
+  if (side == 0 || side % 64 != 0)
+    throw Error(ERR_INPUT, "side " + std::to_string(side) + " is not a positive multiple of 64");
+  if (side > 8192) throw Error(ERR_INPUT, "side " + std::to_string(side) + " is too large");
+}
+
+static iec_status birefnet_host(iec_birefnet* model, const void* image, bool u8, size_t side, float* logits) {
+  return guard([&] {
+    need_model(model);
+    need(image, "image");
+    need(logits, "logits");
+    check_birefnet_size(side);
+    Birefnet& m = *model->model;
+    DeviceScope scope(m.device());
+    const size_t bytes = side * side * 3 * (u8 ? 1 : 4), obytes = side * side * 4;
+    m.host_in.reserve(bytes);
+    m.host_out.reserve(obytes);
+    cudaStream_t s = m.device().stream();
+    IEC_CUDA(cudaMemcpyAsync(m.host_in.get(), image, bytes, cudaMemcpyHostToDevice, s));
+    m.run(m.host_in.get(), u8, (int)side, m.host_out.as<float>(), s);
+    IEC_CUDA(cudaMemcpyAsync(logits, m.host_out.get(), obytes, cudaMemcpyDeviceToHost, s));
+    m.device().sync(s);
+  });
+}
+
+iec_status iec_birefnet_run(iec_birefnet* model, const uint8_t* rgb, size_t side, float* logits) {
+  return birefnet_host(model, rgb, true, side, logits);
+}
+
+iec_status iec_birefnet_run_normalized(iec_birefnet* model, const float* image, size_t side, float* logits) {
+  return birefnet_host(model, image, false, side, logits);
+}
+
+iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int image_u8, size_t side, float* logits,
+                                   void* stream) {
+  return guard([&] {
+    need_model(model);
+    need(image, "image");
+    need(logits, "logits");
+    check_birefnet_size(side);
+    Birefnet& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run(image, image_u8 != 0, (int)side, logits, s);
   });
 }
 

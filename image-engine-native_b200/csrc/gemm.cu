@@ -54,9 +54,7 @@ void dispatch(Device& dev, int bn, int kb, const CUtensorMap& map, const GemmPar
   IEC_GEMM_CASE(256, KB_)
   IEC_GEMM_BN(64)
   IEC_GEMM_BN(32)
-  if (AMODE == A_TAPS) {
-    IEC_GEMM_BN(16)
-  }
+  IEC_GEMM_BN(16)
 #undef IEC_GEMM_BN
 #undef IEC_GEMM_CASE
   throw Error(ERR_GPU, "no GEMM kernel for this tile shape");
@@ -70,6 +68,12 @@ void fill_out(GemmParams& p, const GemmOutSpec& o) {
   p.map_h = o.map_h;
   p.map_w = o.map_w;
   p.shift = o.shift;
+  p.win_ws = o.win_ws ? o.win_ws : 8;
+  p.pad_h = o.pad_h ? o.pad_h : o.map_h;
+  p.pad_w = o.pad_w ? o.pad_w : o.map_w;
+  if (o.mode == OUT_WINDOW_ACCUM && (p.win_ws < 1 || p.win_ws > 8 || p.pad_h % p.win_ws || p.pad_w % p.win_ws ||
+                                     p.pad_h < o.map_h || p.pad_w < o.map_w))
+    throw Error(ERR_INPUT, "window partition geometry is inconsistent");
   p.dbl_w = o.dbl_w;
   p.dbl_cout = o.dbl_cout;
   p.phase_y = o.phase_y;
@@ -283,17 +287,23 @@ void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int 
 // groups for the mean and the variance, a third to normalise and store.
 __global__ void layer_norm_planar_kernel(const __half* __restrict__ src, long long src_plane, int plane0, int rows,
                                          int c, const float* __restrict__ gamma, const float* __restrict__ beta,
-                                         __half* __restrict__ dst, long long dst_plane, int window, int map_h,
-                                         int map_w, int shift) {
+                                         __half* __restrict__ dst, long long dst_plane, int window,
+                                         WindowMap wm) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= rows) return;
+  const int groups = c / 8;
   long long pix = t;
   if (window) {
-    const int win = t >> 6, i = t & 63, cols = map_w >> 3;
+    const int win = t >> 6, i = t & 63, ws = wm.ws, cols = wm.pad_w / ws;
     const int wy = win / cols, wx = win - wy * cols;
-    pix = (long long)((wy * 8 + (i >> 3) + shift) % map_h) * map_w + (wx * 8 + (i & 7) + shift) % map_w;
+    const int y = (wy * ws + i / ws + wm.shift) % wm.pad_h, x = (wx * ws + i % ws + wm.shift) % wm.pad_w;
+    if (i >= ws * ws || y >= wm.map_h || x >= wm.map_w) {
+      for (int g = 0; g < groups; g++)
+        *reinterpret_cast<uint4*>(dst + g * dst_plane + (long long)t * 8) = make_uint4(0u, 0u, 0u, 0u);
+      return;
+    }
+    pix = (long long)y * wm.map_w + x;
   }
-  const int groups = c / 8;
   const __half* base = src + (long long)plane0 * src_plane + pix * 8;
   float sum = 0.0f;
   for (int g = 0; g < groups; g++) {
@@ -335,10 +345,16 @@ __global__ void layer_norm_planar_kernel(const __half* __restrict__ src, long lo
 }
 
 void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c, const float* gamma,
-                       const float* beta, __half* dst, long long dst_plane_elems, bool window, int map_h, int map_w,
-                       int shift, cudaStream_t s) {
+                       const float* beta, __half* dst, long long dst_plane_elems, const WindowMap* window,
+                       cudaStream_t s) {
+  WindowMap wm;
+  if (window) {
+    wm = *window;
+    if (wm.ws < 1 || wm.ws > 8 || wm.pad_h % wm.ws || wm.pad_w % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w)
+      throw Error(ERR_INPUT, "window partition geometry is inconsistent");
+  }
   layer_norm_planar_kernel<<<(rows + 127) / 128, 128, 0, s>>>(src, src_plane_elems, plane0, rows, c, gamma, beta, dst,
-                                                              dst_plane_elems, window ? 1 : 0, map_h, map_w, shift);
+                                                              dst_plane_elems, window ? 1 : 0, wm);
   IEC_CUDA(cudaGetLastError());
 }
 

@@ -31,6 +31,7 @@ struct GemmOutSpec {
   long long plane_elems = 0;   // rows of the destination * 8
   int plane0 = 0;              // destination plane of column 0
   int map_h = 0, map_w = 0, shift = 0;  // OUT_WINDOW_ACCUM
+  int win_ws = 0, pad_h = 0, pad_w = 0;  // window side (0: 8), padded map (0: the map)
   int dbl_w = 0, dbl_cout = 0;          // OUT_DOUBLE
   int phase_y = 0, phase_x = 0;         // OUT_PHASE, OUT_MAP
   // OUT_MAP (set by map_out): the stored map's geometry, output step, and
@@ -94,14 +95,22 @@ void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map, long lo
 void rows_to_planar(const float* src, int rows, int c, __half* dst, long long dst_plane_elems, cudaStream_t s);
 void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int c, float* dst, cudaStream_t s);
 
+// A shifted-window partition: windows of ws x ws tokens tiling the map
+// padded to pad_h x pad_w, each stored as a slot of 64 rows; token t of
+// window (wy, wx) is pixel ((wy ws + t / ws + shift) % pad_h, (wx ws + t % ws
+// + shift) % pad_w) (crates/scunet-native/src/swin.rs:170-181, 8 x 8;
+// crates/birefnet-native/src/swin.rs:219-251, 7 x 7).
+struct WindowMap {
+  int ws = 8, pad_h = 0, pad_w = 0, map_h = 0, map_w = 0, shift = 0;
+};
+
 // Layer norm (eps 1e-5) of the c channels starting at plane `plane0` of
 // `src` for every row, written as c / 8 planes of `dst`. With `window`, the
-// rows are the map's pixels and are written in (shifted) 8 x 8 window order:
-// token t of window w comes from pixel ((wy 8 + t / 8 + shift) % h,
-// (wx 8 + t % 8 + shift) % w) (crates/scunet-native/src/swin.rs:170-181).
+// rows are written in window order; slot rows past ws * ws and tokens past
+// the map's edge are zero rows, not normalised (birefnet swin.rs:236-248).
 void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c,
-                       const float* gamma, const float* beta, __half* dst, long long dst_plane_elems, bool window,
-                       int map_h, int map_w, int shift, cudaStream_t s);
+                       const float* gamma, const float* beta, __half* dst, long long dst_plane_elems,
+                       const WindowMap* window, cudaStream_t s);
 
 // Fused attention over 8 x 8 windows (attention.cu): `qkv` planar [3c / 8]
 // [windows * 64][8], `bias` [classes][c / 32][64][64] f32 (classes 4 when

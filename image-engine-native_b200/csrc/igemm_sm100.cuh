@@ -34,7 +34,9 @@
 //   OUT_STORE        act(acc + bias) -> f16 planes (at a channel offset)
 //   OUT_ACCUM        out += act(acc + bias)                (residual adds)
 //   OUT_WINDOW_ACCUM out[pixel(token)] += acc + bias, the token's pixel from
-//                    the (shifted) window partition: swin.rs:174-178,212-219
+//                    the (shifted) window partition: scunet swin.rs:174-178,
+//                    212-219 (8 x 8), birefnet swin.rs:219-306 (7 x 7 windows
+//                    of a map padded to a multiple of 7, in 64-row slots)
 //   OUT_DOUBLE       2x2 stride-2 transposed convolution: column q cout + o of
 //                    input pixel (y, x) -> output pixel (2y + q / 2, 2x + q % 2),
 //                    channel o (crates/scunet-native/src/network.rs:446-478)
@@ -84,7 +86,8 @@ struct GemmParams {
   __half* out;              // planar f16: plane p at out + p * out_plane_elems
   long long out_plane_elems;  // elements per plane (rows * 8)
   int out_plane0;           // plane of output column 0
-  int map_h, map_w, shift;  // OUT_WINDOW_ACCUM: the map the tokens came from
+  int map_h, map_w, shift;  // OUT_WINDOW_ACCUM: the map the tokens came from,
+  int win_ws, pad_h, pad_w; // its window side and the padded size the windows tile
   int dbl_w, dbl_cout;      // OUT_DOUBLE: input width, output channels
   // OUT_MAP: logical map size, reflect padding, phase split (1 or 2), pitch
   // and rows of one stored phase image, output step (1, or 2 for one phase
@@ -393,10 +396,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // Destination pixel of the row for the scattering epilogues.
       long long dest = m;
       if (m >= 0 && p.out_mode == OUT_WINDOW_ACCUM) {
-        const int win = m >> 6, t = m & 63, cols = p.map_w >> 3;
+        // Window slots of 64 rows: rows past ws * ws tokens, and tokens of
+        // the padding past the map's edge, are dropped.
+        const int win = m >> 6, t = m & 63, ws = p.win_ws, cols = p.pad_w / ws;
         const int wy = win / cols, wx = win - wy * cols;
-        const int py = (wy * 8 + (t >> 3) + p.shift) % p.map_h, px = (wx * 8 + (t & 7) + p.shift) % p.map_w;
-        dest = (long long)py * p.map_w + px;
+        const int py = (wy * ws + t / ws + p.shift) % p.pad_h, px = (wx * ws + t % ws + p.shift) % p.pad_w;
+        if (t >= ws * ws || py >= p.map_h || px >= p.map_w)
+          m = -1;
+        else
+          dest = (long long)py * p.map_w + px;
       }
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * L::ACC_COLS);
       if (p.out_mode == OUT_MAP)

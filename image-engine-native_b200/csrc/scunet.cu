@@ -324,7 +324,8 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       gemm_conv3(dev_, B.conv2, t, pl, H, W, ACT_NONE, o, s);
       // Attention (swin.rs:124-220) on y[h:]: LN1 + window partition, qkv,
       // attention, projection added back at the tokens' pixels.
-      layer_norm_planar(y, pl, h / 8, Pl, h, B.ln1g.as<float>(), B.ln1b.as<float>(), tok, pl, true, H, W, shift, s);
+      const WindowMap wm{8, H, W, H, W, shift};
+      layer_norm_planar(y, pl, h / 8, Pl, h, B.ln1g.as<float>(), B.ln1b.as<float>(), tok, pl, &wm, s);
       o.mode = OUT_STORE;
       o.out = qkv;
       o.plane0 = 0;
@@ -338,7 +339,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       o.shift = shift;
       gemm_rows(dev_, B.proj, att, pl, Pl, ACT_NONE, o, s);
       // MLP (swin.rs:222-254): y[h:] += fc2(gelu(fc1(LN2(y[h:])))).
-      layer_norm_planar(y, pl, h / 8, Pl, h, B.ln2g.as<float>(), B.ln2b.as<float>(), ln2, pl, false, H, W, 0, s);
+      layer_norm_planar(y, pl, h / 8, Pl, h, B.ln2g.as<float>(), B.ln2b.as<float>(), ln2, pl, nullptr, s);
       o.mode = OUT_STORE;
       o.out = hid;
       o.plane0 = 0;

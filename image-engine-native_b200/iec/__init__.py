@@ -89,6 +89,13 @@ def lib():
         L.iec_lama_run_float.argtypes = [vp, f32p, f32p, sz, sz, f32p]
         L.iec_lama_run.argtypes = [vp, u8p, u8p, sz, sz, u8p, PROGRESS, vp]
         L.iec_lama_run_device.argtypes = [vp, vp, vp, sz, sz, vp, vp]
+        L.iec_birefnet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
+        L.iec_birefnet_free.argtypes = [vp]
+        L.iec_birefnet_device_name.argtypes = [vp]
+        L.iec_birefnet_device_name.restype = ctypes.c_char_p
+        L.iec_birefnet_run.argtypes = [vp, u8p, sz, f32p]
+        L.iec_birefnet_run_normalized.argtypes = [vp, f32p, sz, f32p]
+        L.iec_birefnet_run_device.argtypes = [vp, vp, i32, sz, vp, vp]
         L.iec_realesrgan_set_timing.argtypes = [vp, sz]
         L.iec_realesrgan_timing.argtypes = [vp, ctypes.POINTER(ctypes.c_int), f32p, sz]
         L.iec_realesrgan_timing.restype = sz
@@ -368,6 +375,46 @@ class Lama:
     def run_device(self, image_ptr: int, mask_ptr: int, width: int, height: int, out_ptr: int, stream: int = 0):
         """run_float on device pointers, queued on `stream`."""
         _check(lib().iec_lama_run_device(self._h, image_ptr, mask_ptr, width, height, out_ptr, stream or None))
+
+
+class Birefnet:
+    """crates/birefnet-native/src/lib.rs Model, on the CUDA backend."""
+
+    def __init__(self, path, device: int = -1, timeout_ms: int = 0):
+        self._h = ctypes.c_void_p()
+        opt = Options(device, timeout_ms, 0)
+        _check(lib().iec_birefnet_load(os.fsencode(path), ctypes.byref(opt), ctypes.byref(self._h)))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().iec_birefnet_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def gpu(self) -> str:
+        return lib().iec_birefnet_device_name(self._h).decode()
+
+    def run(self, rgb: np.ndarray) -> np.ndarray:
+        """Model::run: side x side logits of a side x side x 3 8-bit image."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        side = rgb.shape[0]
+        out = np.empty((side, side), np.float32)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        _check(lib().iec_birefnet_run(self._h, rgb.ctypes.data_as(u8p), side, _f32(out)))
+        return out
+
+    def run_normalized(self, image: np.ndarray) -> np.ndarray:
+        """Model::run_normalized: logits of an ImageNet-normalised image."""
+        image = np.ascontiguousarray(image, np.float32)
+        side = image.shape[0]
+        out = np.empty((side, side), np.float32)
+        _check(lib().iec_birefnet_run_normalized(self._h, _f32(image), side, _f32(out)))
+        return out
+
+    def run_device(self, image_ptr: int, image_u8: bool, side: int, logits_ptr: int, stream: int = 0):
+        """run / run_normalized on device pointers, queued on `stream`."""
+        _check(lib().iec_birefnet_run_device(self._h, image_ptr, int(image_u8), side, logits_ptr, stream or None))
 
 
 def selftest_rfft2(x: np.ndarray, device: int = -1):

@@ -222,6 +222,32 @@ iec_status iec_lama_run(iec_lama* model, const uint8_t* rgb, const uint8_t* mask
 iec_status iec_lama_run_device(iec_lama* model, const float* image, const float* mask, size_t width,
                                size_t height, float* out, void* stream);
 
+/* ---------------------------------------------------------------- BiRefNet
+ * crates/birefnet-native/src/lib.rs: BiRefNet-lite background removal. The
+ * side must be a positive multiple of 64 (lib.rs:175-187); at most 8192 here. */
+typedef struct iec_birefnet iec_birefnet;
+
+/* Model::load (lib.rs:62-80) with IMAGE_ENGINE_NATIVE_GPU=1 semantics; the
+ * "BIREFNET" weights file of tools/birefnet/export_weights.py (f16 matrices). */
+iec_status iec_birefnet_load(const char* weights_path, const iec_options* options, iec_birefnet** out);
+void iec_birefnet_free(iec_birefnet* model);
+const char* iec_birefnet_device_name(const iec_birefnet* model);
+
+/* Model::run (lib.rs:116-133): the foreground logit of every pixel of a
+ * side x side 8-bit RGB image (side * side floats); the sigmoid of a logit is
+ * the pixel's opacity. */
+iec_status iec_birefnet_run(iec_birefnet* model, const uint8_t* rgb, size_t side, float* logits);
+
+/* Model::run_normalized (lib.rs:134-172): the same for an image already
+ * normalised with the ImageNet mean and deviation (side x side x 3 floats). */
+iec_status iec_birefnet_run_normalized(iec_birefnet* model, const float* image, size_t side, float* logits);
+
+/* run / run_normalized on DEVICE pointers of the model's device (`image_u8`
+ * selects 8-bit RGB or normalised floats); queued on `stream` (NULL: the
+ * model's stream), no wait. */
+iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int image_u8, size_t side,
+                                   float* logits, void* stream);
+
 /* Diagnostics (no counterpart in the reference): one launch of the general
  * GEMM on host arrays. conv = 0: `a` rows_or_h x k, `weights` k x n; conv = 1:
  * `a` rows_or_h x w x k, `weights` 9k x n (3x3, zero padding). act 0 none,
