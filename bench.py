@@ -199,18 +199,34 @@ def time_device(fn, stream, warmup=3, iters=10):
 
 
 def other_models(wdir, stream, sptr, args):
-    """SCUNet 3x512x768 and Big LaMa 4x512x512 (seeded f16 weights),
-    device-resident; LaMa also through the host entry point."""
+    """SCUNet 3x512x768, Big LaMa 4x512x512 and BiRefNet-lite 3x1024x1024
+    (seeded weights), device-resident; LaMa and BiRefNet also through their
+    host entry points; with the CPU oracle's time for one run beside each."""
     out = {}
     only = set(args.models.split(","))
+    cpu = not args.no_cpu and not args.profile_models
     if "scunet" in only:
-        out.update(scunet_leg(wdir, stream, sptr))
+        out.update(scunet_leg(wdir, stream, sptr, cpu))
     if "lama" in only:
-        out.update(lama_leg(wdir, stream, sptr))
+        out.update(lama_leg(wdir, stream, sptr, cpu))
+    if "birefnet" in only:
+        out.update(birefnet_leg(wdir, stream, sptr, cpu))
     return out
 
 
-def scunet_leg(wdir, stream, sptr):
+def cpu_once(fn, mp):
+    """The CPU oracle's time for one run of a model's configuration (after a
+    small warm-up of its threads): the per-model CPU baseline."""
+    from oracle import refcpu
+
+    t0 = time.perf_counter()
+    fn()
+    el = time.perf_counter() - t0
+    cores = refcpu.threads()
+    return {"value": mp / el, "unit": "MP/s", "seconds": el, "cores": cores, "kind": "port"}
+
+
+def scunet_leg(wdir, stream, sptr, cpu):
     import torch
 
     import iec
@@ -227,10 +243,17 @@ def scunet_leg(wdir, stream, sptr):
                              "unit": "MP/s", "ms": t * 1e3, "gflop": 899.58,
                              "tflops_achieved": 899.58e9 / t / 1e12}
     m.close()
+    if cpu:
+        from oracle import refcpu
+
+        ref = refcpu.Scunet(path)
+        image = W.scunet_input(768, 512, 0)
+        ref.run_float(image[:64, :64])
+        out["scunet_768x512"]["cpu_baseline"] = cpu_once(lambda: ref.run_float(image), 768 * 512 / 1e6)
     return out
 
 
-def lama_leg(wdir, stream, sptr):
+def lama_leg(wdir, stream, sptr, cpu):
     """Big LaMa 512 x 512, about 30 % masked (seeded f16 weights and rectangles)."""
     import torch
 
@@ -255,6 +278,47 @@ def lama_leg(wdir, stream, sptr):
                            "unit": "MP/s", "ms": t * 1e3, "gflop": 439.8, "tflops_achieved": 439.8e9 / t / 1e12,
                            "e2e_ms": te * 1e3, "e2e_value": 512 * 512 / 1e6 / te}
     m.close()
+    if cpu:
+        from oracle import refcpu
+
+        ref = refcpu.Lama(path)
+        ref.run_float(image[:16, :16], mask[:16, :16])
+        out["lama_512x512"]["cpu_baseline"] = cpu_once(lambda: ref.run_float(image, mask), 512 * 512 / 1e6)
+    return out
+
+
+def birefnet_leg(wdir, stream, sptr, cpu):
+    """BiRefNet-lite at side 1024 (seeded f16 weights, uniform 8-bit image):
+    device-resident, and through the host entry point."""
+    import torch
+
+    import iec
+    from iec import weights as W
+
+    out = {}
+    path = os.path.join(wdir, "birefnet.weights")
+    W.write_birefnet(path, 0)
+    m = iec.Birefnet(path, device=torch.cuda.current_device())
+    rgb = W.birefnet_input(1024, 0)
+    img = torch.from_numpy(rgb).cuda()
+    res = torch.empty((1024, 1024), dtype=torch.float32, device="cuda")
+    t = time_device(lambda: m.run_device(img.data_ptr(), True, 1024, res.data_ptr(), sptr), stream)
+    m.run(rgb)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        m.run(rgb)
+    te = (time.perf_counter() - t0) / 3
+    out["birefnet_1024"] = {"workload": "BiRefNet-lite 3x1024x1024 (single-image configuration)",
+                            "value": 1024 * 1024 / 1e6 / t, "unit": "MP/s", "ms": t * 1e3, "gflop": 606.36,
+                            "tflops_achieved": 606.36e9 / t / 1e12, "e2e_ms": te * 1e3,
+                            "e2e_value": 1024 * 1024 / 1e6 / te}
+    m.close()
+    if cpu:
+        from oracle import refcpu
+
+        ref = refcpu.Birefnet(path)
+        ref.run(rgb[:64, :64])
+        out["birefnet_1024"]["cpu_baseline"] = cpu_once(lambda: ref.run(rgb), 1024 * 1024 / 1e6)
     return out
 
 
@@ -279,7 +343,7 @@ def main():
     ap.add_argument("--no-models", action="store_true", help="skip the other models' single-image legs")
     ap.add_argument("--profile-models", action="store_true",
                     help="run only the other models' single-image legs (for profiler launch lists)")
-    ap.add_argument("--models", default="scunet,lama", help="which single-image legs run (comma list)")
+    ap.add_argument("--models", default="scunet,lama,birefnet", help="which single-image legs run (comma list)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()
