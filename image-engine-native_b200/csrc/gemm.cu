@@ -11,10 +11,16 @@ namespace iec {
 namespace {
 
 int choose_bn(int n) {
+  // Up to 256 columns: one tile, the narrowest that covers them (its
+  // padding columns are zero weights); above: the widest tile that divides.
+  const int up[] = {32, 64, 96, 128, 192, 256};
+  if (n <= 256)
+    for (int bn : up)
+      if (bn >= n) return bn;
   const int cands[] = {256, 192, 128, 96, 64, 32};
   for (int bn : cands)
     if (n % bn == 0) return bn;
-  return 32;  // n padded to a multiple of 32 with zero columns
+  return 128;  // n padded to a multiple of 128 with zero columns
 }
 
 int choose_kb(int k) {
@@ -283,65 +289,117 @@ void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int 
   IEC_CUDA(cudaGetLastError());
 }
 
-// One thread per output row (token or pixel): two passes over its channel
-// groups for the mean and the variance, a third to normalise and store.
-__global__ void layer_norm_planar_kernel(const __half* __restrict__ src, long long src_plane, int plane0, int rows,
-                                         int c, const float* __restrict__ gamma, const float* __restrict__ beta,
-                                         __half* __restrict__ dst, long long dst_plane, int window,
-                                         WindowMap wm) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= rows) return;
+// S threads per output row (token or pixel), each holding up to G of the
+// row's channel groups in registers: one read of the row, the mean and the
+// variance by shuffles within the S threads (two passes, as math.rs:78-116
+// computes them), then the normalised groups. mode 0: row r is pixel r;
+// mode 1: window order (zero rows where WindowMap says so); mode 2: patch
+// merge, row r of the (grid / 2)^2 map gathering its 2 x 2 pixels in the
+// order (0,0), (1,0), (0,1), (1,1) (birefnet swin.rs:366-404).
+template <int S, int G>
+__global__ void __launch_bounds__(256) layer_norm_rows(const __half* __restrict__ src, long long src_plane, int plane0,
+                                                       int rows, int c, const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta, __half* __restrict__ dst,
+                                                       long long dst_plane, int mode, WindowMap wm, int grid) {
+  const int lane = threadIdx.x % S, sub = threadIdx.x / S;
+  const int r = blockIdx.x * (256 / S) + sub;
+  const bool valid = r < rows;
   const int groups = c / 8;
-  long long pix = t;
-  if (window) {
-    const int win = t >> 6, i = t & 63, ws = wm.ws, cols = wm.pad_w / ws;
+  bool zero = false;
+  long long pix = r;
+  int src_groups = groups;
+  if (valid && mode == 1) {
+    const int win = r >> 6, i = r & 63, ws = wm.ws, cols = wm.pad_w / ws;
     const int wy = win / cols, wx = win - wy * cols;
     const int y = (wy * ws + i / ws + wm.shift) % wm.pad_h, x = (wx * ws + i % ws + wm.shift) % wm.pad_w;
-    if (i >= ws * ws || y >= wm.map_h || x >= wm.map_w) {
-      for (int g = 0; g < groups; g++)
-        *reinterpret_cast<uint4*>(dst + g * dst_plane + (long long)t * 8) = make_uint4(0u, 0u, 0u, 0u);
-      return;
-    }
-    pix = (long long)y * wm.map_w + x;
+    if (i >= ws * ws || y >= wm.map_h || x >= wm.map_w)
+      zero = true;
+    else
+      pix = (long long)y * wm.map_w + x;
   }
-  const __half* base = src + (long long)plane0 * src_plane + pix * 8;
+  if (mode == 2) src_groups = groups / 4;
+  float v[G][8];
   float sum = 0.0f;
-  for (int g = 0; g < groups; g++) {
-    const uint4 u = *reinterpret_cast<const uint4*>(base + g * src_plane);
+#pragma unroll
+  for (int k = 0; k < G; k++) {
+    const int g = lane + k * S;
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[k][e] = 0.0f;
+    if (!valid || zero || g >= groups) continue;
+    const __half* at;
+    if (mode == 2) {
+      const int q = g / src_groups, gs = g - q * src_groups, half = grid / 2;
+      const long long p2 = (long long)(2 * (r / half) + (q & 1)) * grid + 2 * (r % half) + (q >> 1);
+      at = src + (long long)gs * src_plane + p2 * 8;
+    } else {
+      at = src + (long long)(plane0 + g) * src_plane + pix * 8;
+    }
+    const uint4 u = *reinterpret_cast<const uint4*>(at);
     const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
     for (int e = 0; e < 4; e++) {
       const float2 f = __half22float2(h[e]);
+      v[k][2 * e] = f.x;
+      v[k][2 * e + 1] = f.y;
       sum += f.x + f.y;
     }
   }
+#pragma unroll
+  for (int o = S / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o, S);
   const float mean = sum / (float)c;
   float var = 0.0f;
-  for (int g = 0; g < groups; g++) {
-    const uint4 u = *reinterpret_cast<const uint4*>(base + g * src_plane);
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const float2 f = __half22float2(h[e]);
-      var += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
-    }
+  for (int k = 0; k < G; k++) {
+    if (lane + k * S >= groups) continue;
+#pragma unroll
+    for (int e = 0; e < 8; e++) var += (v[k][e] - mean) * (v[k][e] - mean);
   }
+#pragma unroll
+  for (int o = S / 2; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o, S);
+  if (!valid) return;
   const float inv = 1.0f / sqrtf(var / (float)c + 1e-5f);
-  for (int g = 0; g < groups; g++) {
-    const uint4 u = *reinterpret_cast<const uint4*>(base + g * src_plane);
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < G; k++) {
+    const int g = lane + k * S;
+    if (g >= groups) continue;
     uint32_t packed[4];
 #pragma unroll
     for (int e = 0; e < 4; e++) {
-      const float2 f = __half22float2(h[e]);
-      const int ch = g * 8 + 2 * e;
-      const float a = (f.x - mean) * inv * gamma[ch] + beta[ch];
-      const float b = (f.y - mean) * inv * gamma[ch + 1] + beta[ch + 1];
+      float a = 0.0f, b = 0.0f;
+      if (!zero) {
+        const int ch = g * 8 + 2 * e;
+        a = (v[k][2 * e] - mean) * inv * gamma[ch] + beta[ch];
+        b = (v[k][2 * e + 1] - mean) * inv * gamma[ch + 1] + beta[ch + 1];
+      }
       __half2 o = __floats2half2_rn(a, b);
       packed[e] = *reinterpret_cast<uint32_t*>(&o);
     }
-    *reinterpret_cast<uint4*>(dst + g * dst_plane + (long long)t * 8) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    *reinterpret_cast<uint4*>(dst + g * dst_plane + (long long)r * 8) =
+        make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
+}
+
+static void launch_ln(const __half* src, long long src_plane, int plane0, int rows, int c, const float* gamma,
+                      const float* beta, __half* dst, long long dst_plane, int mode, const WindowMap& wm, int grid,
+                      cudaStream_t s) {
+  const int groups = c / 8;
+  if (c % 8 != 0 || groups < 1) throw Error(ERR_INPUT, "layer norm over a channel count not a multiple of 8");
+  if (groups <= 8) {
+    layer_norm_rows<2, 4><<<(rows + 127) / 128, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+                                                             dst_plane, mode, wm, grid);
+  } else if (groups <= 16) {
+    layer_norm_rows<4, 4><<<(rows + 63) / 64, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+                                                           dst_plane, mode, wm, grid);
+  } else if (groups <= 48) {
+    layer_norm_rows<8, 6><<<(rows + 31) / 32, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+                                                           dst_plane, mode, wm, grid);
+  } else if (groups <= 384) {
+    layer_norm_rows<32, 12><<<(rows + 7) / 8, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+                                                           dst_plane, mode, wm, grid);
+  } else {
+    throw Error(ERR_INPUT, "layer norm over more than 3072 channels");
+  }
+  IEC_CUDA(cudaGetLastError());
 }
 
 void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c, const float* gamma,
@@ -353,9 +411,14 @@ void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0,
     if (wm.ws < 1 || wm.ws > 8 || wm.pad_h % wm.ws || wm.pad_w % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w)
       throw Error(ERR_INPUT, "window partition geometry is inconsistent");
   }
-  layer_norm_planar_kernel<<<(rows + 127) / 128, 128, 0, s>>>(src, src_plane_elems, plane0, rows, c, gamma, beta, dst,
-                                                              dst_plane_elems, window ? 1 : 0, wm);
-  IEC_CUDA(cudaGetLastError());
+  launch_ln(src, src_plane_elems, plane0, rows, c, gamma, beta, dst, dst_plane_elems, window ? 1 : 0, wm, 0, s);
+}
+
+void merge_layer_norm_planar(const __half* src, long long src_plane_elems, int grid, int c, const float* gamma,
+                             const float* beta, __half* dst, long long dst_plane_elems, cudaStream_t s) {
+  if (grid % 2 != 0) throw Error(ERR_INPUT, "patch merge of an odd grid");
+  const int rows = (grid / 2) * (grid / 2);
+  launch_ln(src, src_plane_elems, 0, rows, 4 * c, gamma, beta, dst, dst_plane_elems, 2, WindowMap{}, grid, s);
 }
 
 }  // namespace iec
