@@ -165,51 +165,6 @@ __global__ void bir_embed_gather(const float* __restrict__ img, int side, __half
   }
 }
 
-// swin.rs:366-404: merge each 2 x 2 group in the order (0,0), (1,0), (0,1),
-// (1,1) and normalise the 4c values.
-__global__ void bir_merge_ln(const __half* __restrict__ x, long long x_plane, int grid, int c,
-                             const float* __restrict__ gamma, const float* __restrict__ beta,
-                             __half* __restrict__ dst, long long dst_plane) {
-  const int half = grid / 2, tokens = half * half;
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= tokens) return;
-  const int y = 2 * (r / half), xx = 2 * (r % half), groups = c / 8;
-  const int dy[4] = {0, 1, 0, 1}, dx[4] = {0, 0, 1, 1};
-  float sum = 0.0f;
-  for (int q = 0; q < 4; q++) {
-    const __half* base = x + ((long long)(y + dy[q]) * grid + xx + dx[q]) * 8;
-    for (int g = 0; g < groups; g++) {
-      float v[8];
-      load8(base + g * x_plane, v);
-#pragma unroll
-      for (int e = 0; e < 8; e++) sum += v[e];
-    }
-  }
-  const float mean = sum / (float)(4 * c);
-  float var = 0.0f;
-  for (int q = 0; q < 4; q++) {
-    const __half* base = x + ((long long)(y + dy[q]) * grid + xx + dx[q]) * 8;
-    for (int g = 0; g < groups; g++) {
-      float v[8];
-      load8(base + g * x_plane, v);
-#pragma unroll
-      for (int e = 0; e < 8; e++) var += (v[e] - mean) * (v[e] - mean);
-    }
-  }
-  const float inv = 1.0f / sqrtf(var / (float)(4 * c) + 1e-5f);
-  for (int q = 0; q < 4; q++) {
-    const __half* base = x + ((long long)(y + dy[q]) * grid + xx + dx[q]) * 8;
-    for (int g = 0; g < groups; g++) {
-      float v[8];
-      load8(base + g * x_plane, v);
-      const int ch0 = q * c + g * 8;
-#pragma unroll
-      for (int e = 0; e < 8; e++) v[e] = (v[e] - mean) * inv * gamma[ch0 + e] + beta[ch0 + e];
-      store8(dst + (long long)(q * groups + g) * dst_plane + (long long)r * 8, v);
-    }
-  }
-}
-
 // decoder.rs:144-150: per-channel sums of a 64-channel map (f32 partials,
 // f64 totals).
 __global__ void bir_channel_sums(const __half* __restrict__ t, long long plane, long long pixels,
@@ -257,49 +212,43 @@ __global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, co
 // tap k of a size x size kernel, the 64 channels of `t` sampled bilinearly
 // at the tap moved by its offset, times 2 sigmoid(modulator). `offs` holds
 // the offset convolution's 3 taps channels (y, x per tap, then the logits).
+// One thread per (pixel, tap, channel group).
 __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plane, int height, int width, int size,
                                   const __half* __restrict__ offs, long long offs_plane, __half* __restrict__ out,
                                   long long out_plane) {
   const int taps = size * size;
-  const long long n = (long long)height * width * taps;
+  const long long n = (long long)height * width * taps * 8;
   const float hs = (float)(size / 2), hf = (float)height, wf = (float)width;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int tap = (int)(i % taps);
-    const long long p = i / taps;
+    const int g = (int)(i & 7);
+    const long long pt = i >> 3;
+    const int tap = (int)(pt % taps);
+    const long long p = pt / taps;
     const int y = (int)(p / width), x = (int)(p % width);
     auto ch = [&](int c) { return __half2float(offs[(long long)(c / 8) * offs_plane + p * 8 + (c % 8)]); };
     const float py = ((float)y - hs + (float)(tap / size)) + ch(2 * tap);
     const float px = ((float)x - hs + (float)(tap % size)) + ch(2 * tap + 1);
     const float m = 2.0f * sigmoid_f(ch(2 * taps + tap));
-    float acc[64];
-#pragma unroll
-    for (int j = 0; j < 64; j++) acc[j] = 0.0f;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (!(py <= -1.0f || py >= hf || px <= -1.0f || px >= wf)) {
       const float y0f = floorf(py), x0f = floorf(px);
       const float ly = py - y0f, lx = px - x0f, hy = 1.0f - ly, hx = 1.0f - lx;
       const int y0 = (int)y0f, x0 = (int)x0f;
       const int cy[4] = {y0, y0, y0 + 1, y0 + 1}, cx[4] = {x0, x0 + 1, x0, x0 + 1};
       const float cw[4] = {hy * hx, hy * lx, ly * hx, ly * lx};
+      const __half* src = t + g * t_plane;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         if (cy[k] < 0 || cx[k] < 0 || cy[k] >= height || cx[k] >= width) continue;
-        const __half* src = t + ((long long)cy[k] * width + cx[k]) * 8;
+        float v[8];
+        load8(src + ((long long)cy[k] * width + cx[k]) * 8, v);
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
-          float v[8];
-          load8(src + g * t_plane, v);
-#pragma unroll
-          for (int e = 0; e < 8; e++) acc[g * 8 + e] += cw[k] * v[e];
-        }
+        for (int e = 0; e < 8; e++) acc[e] += cw[k] * v[e];
       }
     }
 #pragma unroll
-    for (int g = 0; g < 8; g++) {
-      float v[8];
-#pragma unroll
-      for (int e = 0; e < 8; e++) v[e] = acc[g * 8 + e] * m;
-      store8(out + (long long)(tap * 8 + g) * out_plane + p * 8, v);
-    }
+    for (int e = 0; e < 8; e++) acc[e] *= m;
+    store8(out + (long long)(tap * 8 + g) * out_plane + p * 8, acc);
   }
 }
 
@@ -329,18 +278,18 @@ __global__ void bir_gate(const __half* __restrict__ g16, long long g_plane, cons
 // decoder.rs:564-583: the image cut into g x g patches of size x size
 // pixels, patch (gy, gx) of colour c as channel (c g + gy) g + gx.
 __global__ void bir_patches(const float* __restrict__ img, int side, int size, __half* __restrict__ dst,
-                            long long plane) {
+                            long long plane, int out_groups) {
   const int g = side / size, groups = 3 * g * g / 8;
-  const long long n = (long long)size * size * groups;
+  const long long n = (long long)size * size * out_groups;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int q = (int)(i % groups);
-    const long long p = i / groups;
+    const int q = (int)(i % out_groups);
+    const long long p = i / out_groups;
     const int y = (int)(p / size), x = (int)(p % size);
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) {
       const int ch = 8 * q + e, c = ch / (g * g), rem = ch % (g * g), gy = rem / g, gx = rem % g;
-      v[e] = img[(((long long)gy * size + y) * side + gx * size + x) * 3 + c];
+      v[e] = q < groups ? img[(((long long)gy * size + y) * side + gx * size + x) * 3 + c] : 0.0f;
     }
     store8(dst + q * plane + p * 8, v);
   }
@@ -363,8 +312,8 @@ __global__ void bir_head(const __half* __restrict__ x, long long plane, const fl
 }
 
 // decoder.rs:899-925 and 637-752: logits = head bias + the low-resolution
-// logits resized to the image + the full-resolution branch, as the composed
-// 5x5 convolution inside and the two 3x3 convolutions at the border.
+// logits resized to the image + the full-resolution branch, here as the
+// composed 5x5 convolution; border pixels get the branch from bir_edges.
 __global__ void bir_logits(const float* __restrict__ low, int lg, const float* __restrict__ img, int side,
                            const float* __restrict__ fr, float head_b, float* __restrict__ logits) {
   const long long n = (long long)side * side;
@@ -376,46 +325,86 @@ __global__ void bir_logits(const float* __restrict__ low, int lg, const float* _
     axis(x, lg, side, x1, x2, dx1, dx2);
     const float v = dx2 * dy2 * low[y1 * lg + x1] + dx1 * dy2 * low[y1 * lg + x2] + dx2 * dy1 * low[y2 * lg + x1] +
                     dx1 * dy1 * low[y2 * lg + x2];
-    float d = head_b + v;
-    auto pix = [&](int yy, int xx, int c) {
-      return (yy >= 0 && xx >= 0 && yy < side && xx < side) ? img[((long long)yy * side + xx) * 3 + c] : 0.0f;
-    };
-    float s;
+    const float d = head_b + v;
     if (y == 0 || x == 0 || y == side - 1 || x == side - 1) {
-      s = fr[FR_SCALARS];
-      for (int dd = 0; dd < 9; dd++) {
-        const int qy = y + dd / 3 - 1, qx = x + dd % 3 - 1;
-        if (qy < 0 || qx < 0 || qy >= side || qx >= side) continue;
-        float dot = 0.0f;
-        for (int k = 0; k < INTER; k++) {
-          float mid = fr[FR_BIAS1 + k];
-          for (int e = 0; e < 9; e++) {
-            const int py = qy + e / 3 - 1, px = qx + e % 3 - 1;
-            if (py < 0 || px < 0 || py >= side || px >= side) continue;
-            for (int c = 0; c < 3; c++) mid += pix(py, px, c) * fr[FR_CONV1 + (e * 3 + c) * INTER + k];
-          }
-          dot += mid * fr[FR_OUT + dd * INTER + k];
-        }
-        s += dot;
-      }
-    } else {
-      s = fr[FR_SCALARS + 1];
-      for (int e = 0; e < 25; e++) {
-        const int py = y + e / 5 - 2, px = x + e % 5 - 2;
-        s += fr[FR_COMPOSED + e * 3] * pix(py, px, 0) + fr[FR_COMPOSED + e * 3 + 1] * pix(py, px, 1) +
-             fr[FR_COMPOSED + e * 3 + 2] * pix(py, px, 2);
-      }
+      logits[i] = d;
+      continue;
+    }
+    float s = fr[FR_SCALARS + 1];
+    for (int e = 0; e < 25; e++) {
+      const int py = y + e / 5 - 2, px = x + e % 5 - 2;
+      const bool in = py >= 0 && px >= 0 && py < side && px < side;
+      const float* q = img + ((long long)py * side + px) * 3;
+      const float p0 = in ? q[0] : 0.0f, p1 = in ? q[1] : 0.0f, p2 = in ? q[2] : 0.0f;
+      s += fr[FR_COMPOSED + e * 3] * p0 + fr[FR_COMPOSED + e * 3 + 1] * p1 + fr[FR_COMPOSED + e * 3 + 2] * p2;
     }
     logits[i] = d + s;
   }
 }
 
-void pack(WeightFile& f, PackedWeights& pw, const std::string& name, int taps, int k, int n, bool bias) {
+// decoder.rs:684-722: at the border the two 3x3 convolutions run as they are
+// (the intermediate map's zero padding is reached). One warp per border
+// pixel, two of the 64 intermediate channels per lane.
+__global__ void bir_edges(const float* __restrict__ img, int side, const float* __restrict__ fr,
+                          float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int e_count = 4 * side - 4;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < e_count; w += (gridDim.x * blockDim.x) >> 5) {
+    int y, x;
+    if (w < side) {
+      y = 0;
+      x = w;
+    } else if (w < 2 * side) {
+      y = side - 1;
+      x = w - side;
+    } else {
+      const int j = w - 2 * side;
+      y = 1 + j / 2;
+      x = (j & 1) ? side - 1 : 0;
+    }
+    float s = fr[FR_SCALARS];
+    for (int dd = 0; dd < 9; dd++) {
+      const int qy = y + dd / 3 - 1, qx = x + dd % 3 - 1;
+      if (qy < 0 || qx < 0 || qy >= side || qx >= side) continue;
+      float part = 0.0f;
+      for (int kk = 0; kk < 2; kk++) {
+        const int k = lane + 32 * kk;
+        float mid = fr[FR_BIAS1 + k];
+        for (int e = 0; e < 9; e++) {
+          const int py = qy + e / 3 - 1, px = qx + e % 3 - 1;
+          if (py < 0 || px < 0 || py >= side || px >= side) continue;
+          const float* q = img + ((long long)py * side + px) * 3;
+          for (int c = 0; c < 3; c++) mid += q[c] * fr[FR_CONV1 + (e * 3 + c) * INTER + k];
+        }
+        part += mid * fr[FR_OUT + dd * INTER + k];
+      }
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      s += part;
+    }
+    if (lane == 0) logits[(long long)y * side + x] += s;
+  }
+}
+
+// A [taps * k, n] matrix packed with its input channels padded to k_pad per
+// tap (zero rows), so that the GEMM's K steps are 64 channels wide.
+void pack(WeightFile& f, PackedWeights& pw, const std::string& name, int taps, int k, int n, bool bias,
+          int k_pad = 0) {
   HostTensor w = f.take_tensor(name + ".weight", {(size_t)taps * k, (size_t)n});
   std::vector<float> b;
   if (bias) b = f.take(name + ".bias", {(size_t)n});
-  pack_weights(pw, w.values, taps, k, n, bias ? b.data() : nullptr);
+  if (k_pad <= k) {
+    pack_weights(pw, w.values, taps, k, n, bias ? b.data() : nullptr);
+    return;
+  }
+  std::vector<float> padded((size_t)taps * k_pad * n, 0.0f);
+  for (int t = 0; t < taps; t++)
+    for (int c = 0; c < k; c++)
+      std::copy(w.values.begin() + ((size_t)t * k + c) * n, w.values.begin() + ((size_t)t * k + c + 1) * n,
+                padded.begin() + ((size_t)t * k_pad + c) * n);
+  pack_weights(pw, padded, taps, k_pad, n, bias ? b.data() : nullptr);
 }
+
+int pad64(int c) { return (c + 63) / 64 * 64; }
 
 void upload(DeviceBuffer& b, const std::vector<float>& v) {
   b.reserve(v.size() * 4);
@@ -520,7 +509,7 @@ Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
     auto b = std::make_unique<DBlock>();
     b->cin = cin;
     b->cout = cout;
-    pack(f, b->conv_in, p + ".conv_in", 9, cin, INTER, true);
+    pack(f, b->conv_in, p + ".conv_in", 9, cin, INTER, true, pad64(cin));
     pack(f, b->conv_out, p + ".conv_out", 9, INTER, cout, true);
     if (gate) {
       b->gated = true;
@@ -553,7 +542,7 @@ Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
   for (int i = 0; i < 4; i++) {
     auto pt = std::make_unique<Patches>();
     const std::string p = "patches" + std::to_string(5 - i);
-    pack(f, pt->conv1, p + ".conv1", 9, PATCH_C[i], INTER, true);
+    pack(f, pt->conv1, p + ".conv1", 9, PATCH_C[i], INTER, true, pad64(PATCH_C[i]));
     pack(f, pt->conv_out, p + ".conv_out", 9, INTER, PATCH_OUT[i], true);
     patches_.push_back(std::move(pt));
   }
@@ -637,7 +626,9 @@ void Birefnet::ensure(int side) {
   x4_.reserve(bytes(360, pe(g3 * g3)));
   for (int i = 0; i < 4; i++) {
     const long long gi = g0 >> (3 - i);
-    in_[i].reserve(bytes(LEVELS[i][0] / 8, pe(gi * gi)));
+    // the planes past cin stay zero: conv_in's padded input channels
+    in_[i].reserve(bytes(pad64(LEVELS[i][0]) / 8, pe(gi * gi)));
+    IEC_CUDA(cudaMemset(in_[i].get(), 0, bytes(pad64(LEVELS[i][0]) / 8, pe(gi * gi))));
     if (i < 3)
       outb_[i].reserve(bytes(LEVELS[i][1] / 8, pe(gi * gi)));
     else
@@ -653,7 +644,7 @@ void Birefnet::ensure(int side) {
   size_t bstack = 0;
   for (int i = 0; i < 4; i++) {
     const long long gi = g0 >> (3 - i);
-    bstack = std::max(bstack, bytes(PATCH_C[i] / 8, pe(gi * gi)));
+    bstack = std::max(bstack, bytes(pad64(PATCH_C[i]) / 8, pe(gi * gi)));
   }
   stack_.reserve(bstack);
   pmid_.reserve(bytes(8, pe(P0)));
@@ -724,9 +715,7 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
                       dst[si] + (long long)plane0[si] * dst_plane[si], dst_plane[si], nullptr, s);
     if (st.has_merge) {
       const long long mt = tokens / 4, mp = pe(mt);
-      bir_merge_ln<<<(int)((mt + 127) / 128), 128, 0, s>>>(x, xp, grid, c, st.mg.as<float>(), st.mb.as<float>(),
-                                                           mrg_.as<__half>(), mp);
-      IEC_CUDA(cudaGetLastError());
+      merge_layer_norm_planar(x, xp, grid, c, st.mg.as<float>(), st.mb.as<float>(), mrg_.as<__half>(), mp, s);
       GemmOutSpec o;
       o.mode = OUT_STORE;
       o.out = x;
@@ -771,7 +760,7 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     o.out = offs_.as<__half>();
     o.plane_elems = pp;
     gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, s);
-    bir_deform_sample<<<blocks_for(P * taps, sms), 256, 0, s>>>(t, pp, g, g, k, offs_.as<__half>(), pp,
+    bir_deform_sample<<<blocks_for(P * taps * 8, sms), 256, 0, s>>>(t, pp, g, g, k, offs_.as<__half>(), pp,
                                                                 samp_.as<__half>(), pp);
     IEC_CUDA(cudaGetLastError());
     GemmOutSpec c;
@@ -886,9 +875,10 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
     // patches of the image, through two convolutions, after the main planes
     {
       const Patches& pt = *patches_[i];
-      const int groups = PATCH_C[i] / 8;
+      const int groups = pad64(PATCH_C[i]) / 8;  // zero channels past the stack's
       const long long sp = pe((long long)gi * gi);
-      bir_patches<<<blocks_for((long long)gi * gi * groups, sms), 256, 0, s>>>(img, side, gi, stack_.as<__half>(), sp);
+      bir_patches<<<blocks_for((long long)gi * gi * groups, sms), 256, 0, s>>>(img, side, gi, stack_.as<__half>(), sp,
+                                                                                groups);
       IEC_CUDA(cudaGetLastError());
       GemmOutSpec o;
       o.mode = OUT_STORE;
@@ -911,6 +901,8 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
     IEC_CUDA(cudaGetLastError());
     bir_logits<<<blocks_for((long long)side * side, sms), 256, 0, s>>>(low_.as<float>(), g0, img, side,
                                                                         full_.as<float>(), head_b_, logits);
+    IEC_CUDA(cudaGetLastError());
+    bir_edges<<<blocks_for((long long)(4 * side - 4) * 32, sms), 256, 0, s>>>(img, side, full_.as<float>(), logits);
     IEC_CUDA(cudaGetLastError());
   }
 }

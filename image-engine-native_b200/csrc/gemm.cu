@@ -43,7 +43,19 @@ void launch(Device& dev, const CUtensorMap& map, const GemmParams& p, cudaStream
     bytes = optin;  // one CTA per SM: its TMEM columns are always free
   }
   const int grid = std::min(p.tiles, dev.sms());
-  kernel<<<grid, GEMM_THREADS, bytes, s>>>(map, p);
+  // Programmatic dependent launch (the kernel waits for its predecessor's
+  // completion before touching global memory; see igemm_sm100).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = (size_t)bytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  IEC_CUDA(cudaLaunchKernelEx(&cfg, kernel, map, p));
   IEC_CUDA(cudaGetLastError());
 }
 
@@ -64,6 +76,38 @@ void dispatch(Device& dev, int bn, int kb, const CUtensorMap& map, const GemmPar
 #undef IEC_GEMM_BN
 #undef IEC_GEMM_CASE
   throw Error(ERR_GPU, "no GEMM kernel for this tile shape");
+}
+
+// Launch the GEMM of `p` (tiles set, split-K not yet): launches whose tiles
+// fill less than half the GPU and that have at least 16 K steps run their K
+// steps in slices of at least 8 steps on more CTAs, and a reduce kernel adds
+// the slices in order and applies the epilogue.
+template <int AMODE>
+void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, GemmParams& p, cudaStream_t s) {
+  p.tiles_mn = p.tiles;
+  p.ksplit = 1;
+  p.kslice = p.ksteps;
+  p.ws = nullptr;
+  p.ws_n = p.tiles_n * pw.bn;
+  const bool splittable = p.out_mode == OUT_STORE || p.out_mode == OUT_ACCUM || p.out_mode == OUT_MAP;
+  if (splittable && p.tiles_mn * 2 <= dev.sms() && p.ksteps >= 16) {
+    const int want = std::min(dev.sms() / p.tiles_mn, p.ksteps / 8);  // one wave of tiles
+    if (want >= 2) {
+      p.kslice = (p.ksteps + want - 1) / want;
+      p.ksplit = (p.ksteps + p.kslice - 1) / p.kslice;
+    }
+  }
+  if (p.ksplit > 1) {
+    p.ws = static_cast<float*>(dev.scratch((size_t)p.ksplit * p.M * p.ws_n * sizeof(float)));
+    p.tiles = p.tiles_mn * p.ksplit;
+  }
+  dispatch<AMODE>(dev, pw.bn, pw.kb, map, p, s);
+  if (p.ksplit > 1) {
+    const long long total = (long long)p.M * ((p.N + 7) / 8);
+    const int grid = (int)std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)dev.sms() * 16));
+    gemm_splitk_reduce<<<grid, 256, 0, s>>>(p);
+    IEC_CUDA(cudaGetLastError());
+  }
 }
 
 void fill_out(GemmParams& p, const GemmOutSpec& o) {
@@ -186,7 +230,7 @@ void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long 
   }
   p.dev_err = dev.dev_err();
   if (p.tiles >= (1 << 24)) throw Error(ERR_INPUT, "GEMM too large for one launch");
-  dispatch<A_ROWS>(dev, pw.bn, pw.kb, map, p, s);
+  run_gemm<A_ROWS>(dev, pw, map, p, s);
 }
 
 void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map_ptr, long long map_plane_elems, int h, int w,
@@ -243,7 +287,7 @@ void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const
   fill_out(p, out);
   p.dev_err = dev.dev_err();
   if (p.tiles >= (1 << 24) || p.tiles_w >= (1 << 16)) throw Error(ERR_INPUT, "GEMM too large for one launch");
-  dispatch<A_TAPS>(dev, pw.bn, pw.kb, map, p, s);
+  run_gemm<A_TAPS>(dev, pw, map, p, s);
 }
 
 // ---------------------------------------------------------- bandwidth kernels

@@ -112,6 +112,13 @@ void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0,
                        const float* gamma, const float* beta, __half* dst, long long dst_plane_elems,
                        const WindowMap* window, cudaStream_t s);
 
+// Patch merging (crates/birefnet-native/src/swin.rs:366-404): each 2 x 2
+// group of the grid x grid map `src` (c channels) concatenated in the order
+// (0,0), (1,0), (0,1), (1,1) by (row, column) and layer-normalised over its
+// 4c values, as (grid / 2)^2 rows of 4c / 8 planes of `dst`.
+void merge_layer_norm_planar(const __half* src, long long src_plane_elems, int grid, int c, const float* gamma,
+                             const float* beta, __half* dst, long long dst_plane_elems, cudaStream_t s);
+
 // Fused attention over 8 x 8 windows (attention.cu): `qkv` planar [3c / 8]
 // [windows * 64][8], `bias` [classes][c / 32][64][64] f32 (classes 4 when
 // `shifted`, else 1), output planar [c / 8][windows * 64][8].

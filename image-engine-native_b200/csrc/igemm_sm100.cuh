@@ -95,6 +95,11 @@ struct GemmParams {
   int dst_h, dst_w, dst_pad, dst_split, dst_pw, dst_ph, ostep;
   const __half* acc_src;    // added before the activation, or null
   const __half* resid;      // added after the activation, or null
+  // Split-K: the K steps of each output tile in `ksplit` slices of `kslice`,
+  // one tile per (slice, M tile, N tile); each writes its f32 partial sums
+  // to ws[slice][row][ws_n], summed by gemm_splitk_reduce.
+  int ksplit, kslice, tiles_mn, ws_n;
+  float* ws;
   int* dev_err;
 };
 
@@ -266,6 +271,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: let the next kernel's CTAs start their
+  // own set-up as SMs free up, and wait for the previous kernel's results
+  // (and for its reads of what this one overwrites) before any global
+  // memory access. Without the launch attribute both are no-ops.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -277,7 +288,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int i = 0; i < L::NSTAGE; i++) issued[i] = -1;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
-        const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
+        const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
+        const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
+        const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
         int x0 = 0, y0 = 0;
         if (AMODE == A_TAPS) {
           y0 = (int)p.div_tiles_w.div((uint32_t)mt);
@@ -285,7 +298,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           y0 *= 8;
         }
         const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
-        for (int ks = 0; ks < p.ksteps; ks++) {
+        for (int ks = ks0; ks < ks1; ks++) {
           if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
             ok = false;
             break;
@@ -324,7 +337,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&acc_empty[a], acc_phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_EMPTY)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(a * L::ACC_COLS);
-        for (int ks = 0; ks < p.ksteps; ks++) {
+        const int split = tile / p.tiles_mn;
+        const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
+        for (int ks = ks0; ks < ks1; ks++) {
           if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
             ok = false;
             break;
@@ -335,7 +350,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int j = 0; j < KB / 16; j++) {
             const uint64_t adesc = smem_desc(abase + (uint32_t)(2 * j) * lbo_a, lbo_a, 128);
             const uint64_t bdesc = smem_desc(bbase + (uint32_t)(2 * j * BN * 16), BN * 16, 128);
-            umma_f16(d, adesc, bdesc, idesc, (ks | j) != 0);
+            umma_f16(d, adesc, bdesc, idesc, (ks != ks0) || (j != 0));
           }
           umma_commit(&empty[s]);
           if (++s == L::NSTAGE) {
@@ -370,7 +385,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
       if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
       tc_fence_after();
-      const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
+      const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
+      const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
       // This thread's output row, and for A_TAPS its pixel.
       int m = -1, oy = 0, ox = 0;
       if (AMODE == A_ROWS) {
@@ -407,10 +423,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           dest = (long long)py * p.map_w + px;
       }
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * L::ACC_COLS);
-      if (p.out_mode == OUT_MAP)
+      if (p.ksplit > 1) {
+        // the slice's raw partial sums, f32
+#pragma unroll 1
+        for (int c0 = part * HALF; c0 < part * HALF + HALF && c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + (uint32_t)c0, r);
+          tmem_wait_ld();
+          if (m < 0) continue;
+          float4* w = reinterpret_cast<float4*>(p.ws + ((size_t)split * p.M + m) * p.ws_n + nt * BN + c0);
+#pragma unroll
+          for (int q = 0; q < 4; q++)
+            w[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                               __uint_as_float(r[4 * q + 3]));
+        }
+      } else if (p.out_mode == OUT_MAP)
         map_epilogue<BN>(p, bias, taddr, part * HALF, min(part * HALF + HALF, BN), nt, m, ry, rx, nry, nrx);
 #pragma unroll 1
-      for (int c0 = part * HALF; p.out_mode != OUT_MAP && c0 < part * HALF + HALF && c0 < BN; c0 += 16) {
+      for (int c0 = part * HALF; p.ksplit == 1 && p.out_mode != OUT_MAP && c0 < part * HALF + HALF && c0 < BN;
+           c0 += 16) {
         uint32_t r[16];
         tmem_ld16(taddr + (uint32_t)c0, r);
         tmem_wait_ld();
@@ -475,6 +506,58 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+
+// Split-K: out = the slices' partial sums added in slice order, then the
+// tile epilogue's bias, activation and store (OUT_STORE, OUT_ACCUM, OUT_MAP).
+// One thread per (row, 8-column group).
+static __global__ void __launch_bounds__(256) gemm_splitk_reduce(const GemmParams p) {
+  const int groups = (p.N + 7) / 8;
+  const long long total = (long long)p.M * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / groups), g = (int)(i - (long long)m * groups), n0 = 8 * g;
+    float w[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) w[e] = 0.0f;
+    for (int sp = 0; sp < p.ksplit; sp++) {
+      const float4* src = reinterpret_cast<const float4*>(p.ws + ((size_t)sp * p.M + m) * p.ws_n + n0);
+      const float4 a = src[0], b = src[1];
+      w[0] += a.x;
+      w[1] += a.y;
+      w[2] += a.z;
+      w[3] += a.w;
+      w[4] += b.x;
+      w[5] += b.y;
+      w[6] += b.z;
+      w[7] += b.w;
+    }
+    if (p.bias)
+#pragma unroll
+      for (int e = 0; e < 8; e++) w[e] += p.bias[n0 + e < p.N ? n0 + e : 0];
+    __half* plane = p.out + (long long)(p.out_plane0 + g) * p.out_plane_elems;
+    if (p.out_mode == OUT_MAP) {
+      const int oy = m / p.W, ox = m - oy * p.W;
+      int ry[3], rx[3];
+      const int nry = map_mirrors(oy * p.ostep + p.phase_y, p.dst_h, p.dst_pad, ry);
+      const int nrx = map_mirrors(ox * p.ostep + p.phase_x, p.dst_w, p.dst_pad, rx);
+      const long long at = (long long)(p.out_plane0 + g) * p.out_plane_elems + map_offset(p, ry[0], rx[0]) * 8;
+      if (p.acc_src) add_half8(w, *reinterpret_cast<const uint4*>(p.acc_src + at));
+#pragma unroll
+      for (int e = 0; e < 8; e++) w[e] = gemm_act(w[e], p.act);
+      if (p.resid) add_half8(w, *reinterpret_cast<const uint4*>(p.resid + at));
+      const uint4 val = pack_half8(w);
+      for (int iy = 0; iy < nry; iy++)
+        for (int ix = 0; ix < nrx; ix++) *reinterpret_cast<uint4*>(plane + map_offset(p, ry[iy], rx[ix]) * 8) = val;
+      continue;
+    }
+    __half* dst = plane + (long long)m * 8;
+    if (p.out_mode == OUT_ACCUM) add_half8(w, *reinterpret_cast<const uint4*>(dst));
+#pragma unroll
+    for (int e = 0; e < 8; e++) w[e] = gemm_act(w[e], p.act);
+    *reinterpret_cast<uint4*>(dst) = pack_half8(w);
   }
 }
 

@@ -246,7 +246,10 @@ Device::~Device() {
   }
   // A poisoned device may still run work; its buffers and streams are leaked
   // rather than freed under it (as the reference's busy flag does).
-  if (poisoned()) dev_err_.leak();
+  if (poisoned()) {
+    dev_err_.leak();
+    scratch_.leak();
+  }
   if (prev >= 0) cudaSetDevice(prev);
 }
 

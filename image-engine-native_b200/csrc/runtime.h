@@ -154,6 +154,12 @@ class Device {
   void check_device_errors();
   void poison(const std::string& why) { poisoned_ = why.empty() ? "GPU failure" : why; }
   bool poisoned() const { return !poisoned_.empty(); }
+  // Scratch of at least `bytes` for the work of one launch sequence on the
+  // device's streams (the GEMM's split-K partial sums); grows on demand.
+  void* scratch(size_t bytes) {
+    if (scratch_.size() < bytes) scratch_.reserve(bytes);
+    return scratch_.get();
+  }
 
  private:
   int ordinal_ = 0;
@@ -164,6 +170,7 @@ class Device {
   cudaStream_t stream_ = nullptr;
   cudaStream_t copy_stream_ = nullptr;
   DeviceBuffer dev_err_;
+  DeviceBuffer scratch_;
   PinnedBuffer host_err_;
   std::string poisoned_;
 };
