@@ -37,26 +37,64 @@ __device__ __forceinline__ float2 cmul(float2 a, float wr, float wi) {
   return make_float2(a.x * wr - a.y * wi, a.x * wi + a.y * wr);
 }
 
+__device__ __forceinline__ float4 cmul2(float4 v, float wr, float wi) {
+  return make_float4(v.x * wr - v.y * wi, v.x * wi + v.y * wr, v.z * wr - v.w * wi, v.z * wi + v.w * wr);
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float4 sub4(float4 a, float4 b) { return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w); }
+// v times (s i): (x + i y)(s i) = -s y + i s x, for both complex values of v.
+__device__ __forceinline__ float4 mul_si(float4 v, float s) { return make_float4(-s * v.y, s * v.x, -s * v.w, s * v.z); }
+
 // Transforms `lines` lines of f.n points x 8 channels held in `a`
 // ([line][n][8] complex) with `b` as the other buffer, sign -1 forward or +1
-// inverse (no scaling); returns the buffer that holds the result.
-__device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, float sign) {
+// inverse (no scaling); returns the buffer that holds the result. Powers of
+// two run Stockham stages of radix 4 (and one of radix 2 for odd log2 n):
+// for span m and l m = n / 4, the four points k + j m + q l m of sub-
+// transform (j, k) go through a 4-point DFT and out to k + (4 j + q) m
+// turned by w^(q j m), w = exp(sign 2 pi i / n). One thread per (line,
+// butterfly, channel pair). Other lengths take the direct sum. `ct` / `st`
+// are the cos / sin tables in shared memory.
+__device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, const float* ct, const float* st,
+                             float sign) {
   const int n = f.n;
   if (f.log2n >= 0) {
-    const int half = n >> 1;
-    for (int st = 0; st < f.log2n; st++) {
-      const int m = 1 << st;
-      const int total = lines * half * 8;
-      for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        const int c = t & 7, r = t >> 3;
-        const int line = r / half, bf = r - line * half;
-        const int j = bf >> st;
-        const float2* src = a + (size_t)line * n * 8;
-        float2* dst = b + (size_t)line * n * 8;
-        const float2 c0 = src[bf * 8 + c], c1 = src[(bf + half) * 8 + c];
-        const float wr = __ldg(f.cos_t + j * m), wi = sign * __ldg(f.sin_t + j * m);
-        dst[(bf + j * m) * 8 + c] = make_float2(c0.x + c1.x, c0.y + c1.y);
-        dst[(bf + j * m + m) * 8 + c] = cmul(make_float2(c0.x - c1.x, c0.y - c1.y), wr, wi);
+    int sm = 0, rem = f.log2n;
+    while (rem > 0) {
+      const int m = 1 << sm;
+      const float4* src4 = reinterpret_cast<const float4*>(a);
+      float4* dst4 = reinterpret_cast<float4*>(b);
+      if (rem >= 2) {
+        const int lq = f.log2n - 2, quarter = n >> 2;
+        const int total = (lines << lq) << 2;
+        for (int t = threadIdx.x; t < total; t += blockDim.x) {
+          const int cc = t & 3, rest = t >> 2, line = rest >> lq, r = rest & (quarter - 1);
+          const int j = r >> sm, k = r & (m - 1);
+          const int base = (line * n) * 4 + cc;
+          const float4 c0 = src4[base + r * 4], c1 = src4[base + (r + quarter) * 4];
+          const float4 c2 = src4[base + (r + 2 * quarter) * 4], c3 = src4[base + (r + 3 * quarter) * 4];
+          const float4 t0 = add4(c0, c2), t1 = sub4(c0, c2), t2 = add4(c1, c3), t3 = mul_si(sub4(c1, c3), sign);
+          const int o = base + (k + 4 * j * m) * 4, jm = j * m;
+          dst4[o] = add4(t0, t2);
+          dst4[o + m * 4] = cmul2(add4(t1, t3), ct[jm], sign * st[jm]);
+          dst4[o + 2 * m * 4] = cmul2(sub4(t0, t2), ct[2 * jm], sign * st[2 * jm]);
+          dst4[o + 3 * m * 4] = cmul2(sub4(t1, t3), ct[3 * jm], sign * st[3 * jm]);
+        }
+        sm += 2;
+        rem -= 2;
+      } else {
+        const int lh = f.log2n - 1, half = n >> 1;
+        const int total = (lines << lh) << 2;
+        for (int t = threadIdx.x; t < total; t += blockDim.x) {
+          const int cc = t & 3, rest = t >> 2, line = rest >> lh, r = rest & (half - 1);
+          const int j = r >> sm, k = r & (m - 1);
+          const int base = (line * n) * 4 + cc;
+          const float4 c0 = src4[base + r * 4], c1 = src4[base + (r + half) * 4];
+          const int o = base + (k + 2 * j * m) * 4, jm = j * m;
+          dst4[o] = add4(c0, c1);
+          dst4[o + m * 4] = cmul2(sub4(c0, c1), ct[jm], sign * st[jm]);
+        }
+        sm += 1;
+        rem -= 1;
       }
       __syncthreads();
       float2* tmp = a;
@@ -74,7 +112,7 @@ __device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, floa
     int idx = 0;
     for (int j = 0; j < n; j++) {
       const float2 x = src[j * 8 + c];
-      const float wr = __ldg(f.cos_t + idx), wi = sign * __ldg(f.sin_t + idx);
+      const float wr = ct[idx], wi = sign * st[idx];
       re += x.x * wr - x.y * wi;
       im += x.x * wi + x.y * wr;
       idx += k;
@@ -84,6 +122,14 @@ __device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, floa
   }
   __syncthreads();
   return b;
+}
+
+// The twiddle table of `f` copied into shared memory after the two buffers.
+__device__ __forceinline__ void load_twiddles(const Line f, float* ct, float* st) {
+  for (int j = threadIdx.x; j < f.n; j += blockDim.x) {
+    ct[j] = f.cos_t[j];
+    st[j] = f.sin_t[j];
+  }
 }
 
 struct Dims {
@@ -133,6 +179,9 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_rows_fwd(const __half* __rest
   const int lines = min(d.lines_rows, d.h - y0), n = d.w;
   float2* a = fft_smem;
   float2* b = fft_smem + (size_t)d.lines_rows * n * 8;
+  float* ct = reinterpret_cast<float*>(b + (size_t)d.lines_rows * n * 8);
+  float* st = ct + n;
+  load_twiddles(f, ct, st);
   const __half* src = x + g * x_plane + (size_t)y0 * n * 8;
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
     float v[8];
@@ -141,7 +190,7 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_rows_fwd(const __half* __rest
     for (int c = 0; c < 8; c++) a[(size_t)t * 8 + c] = make_float2(v[c], 0.0f);
   }
   __syncthreads();
-  const float2* r = fft_lines(a, b, lines, f, -1.0f);
+  const float2* r = fft_lines(a, b, lines, f, ct, st, -1.0f);
   for (int t = threadIdx.x; t < lines * d.half; t += blockDim.x) {
     const int line = t / d.half, k = t - line * d.half;
     copy_point(T + (((size_t)g * d.h + y0 + line) * d.half + k) * 8, r + ((size_t)line * n + k) * 8);
@@ -157,12 +206,15 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_cols_fwd(const float2* __rest
   const int lines = min(d.lines_cols, d.half - k0), n = d.h;
   float2* a = fft_smem;
   float2* b = fft_smem + (size_t)d.lines_cols * n * 8;
+  float* ct = reinterpret_cast<float*>(b + (size_t)d.lines_cols * n * 8);
+  float* st = ct + n;
+  load_twiddles(f, ct, st);
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
     const int line = t % lines, y = t / lines;
     copy_point(a + ((size_t)line * n + y) * 8, T + (((size_t)g * d.h + y) * d.half + k0 + line) * 8);
   }
   __syncthreads();
-  const float2* r = fft_lines(a, b, lines, f, -1.0f);
+  const float2* r = fft_lines(a, b, lines, f, ct, st, -1.0f);
   __half* re = spec + g * spec_plane;
   __half* im = spec + (g + d.groups) * spec_plane;
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
@@ -189,6 +241,9 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_cols_inv(const __half* __rest
   const int lines = min(d.lines_cols, d.half - k0), n = d.h;
   float2* a = fft_smem;
   float2* b = fft_smem + (size_t)d.lines_cols * n * 8;
+  float* ct = reinterpret_cast<float*>(b + (size_t)d.lines_cols * n * 8);
+  float* st = ct + n;
+  load_twiddles(f, ct, st);
   const __half* re = spec + g * spec_plane;
   const __half* im = spec + (g + d.groups) * spec_plane;
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
@@ -202,7 +257,7 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_cols_inv(const __half* __rest
     for (int c = 0; c < 8; c++) dst[c] = make_float2(vr[c], vi[c]);
   }
   __syncthreads();
-  const float2* r = fft_lines(a, b, lines, f, 1.0f);
+  const float2* r = fft_lines(a, b, lines, f, ct, st, 1.0f);
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
     const int line = t % lines, y = t / lines;
     copy_point(T + (((size_t)g * d.h + y) * d.half + k0 + line) * 8, r + ((size_t)line * n + y) * 8);
@@ -218,6 +273,9 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_rows_inv(const float2* __rest
   const int lines = min(d.lines_rows, d.h - y0), n = d.w;
   float2* a = fft_smem;
   float2* b = fft_smem + (size_t)d.lines_rows * n * 8;
+  float* ct = reinterpret_cast<float*>(b + (size_t)d.lines_rows * n * 8);
+  float* st = ct + n;
+  load_twiddles(f, ct, st);
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
     const int line = t / n, j = t - line * n;
     const float2* row = T + (((size_t)g * d.h + y0 + line) * d.half) * 8;
@@ -235,7 +293,7 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_rows_inv(const float2* __rest
     }
   }
   __syncthreads();
-  const float2* r = fft_lines(a, b, lines, f, 1.0f);
+  const float2* r = fft_lines(a, b, lines, f, ct, st, 1.0f);
   __half* dst = x + g * x_plane + (size_t)y0 * n * 8;
   for (int t = threadIdx.x; t < lines * n; t += blockDim.x) {
     float v[8];
@@ -270,7 +328,7 @@ Line line_of(const FourierPlan& p, bool rows) {
   return Line{p.h, log2_exact(p.h), t + 2 * p.w, t + 2 * p.w + p.h};
 }
 
-size_t smem_for(int lines, int n) { return (size_t)2 * lines * n * 8 * sizeof(float2); }
+size_t smem_for(int lines, int n) { return (size_t)2 * lines * n * 8 * sizeof(float2) + (size_t)2 * n * sizeof(float); }
 
 template <class K>
 void prepare(K kernel, size_t bytes) {

@@ -79,9 +79,9 @@ void dispatch(Device& dev, int bn, int kb, const CUtensorMap& map, const GemmPar
 }
 
 // Launch the GEMM of `p` (tiles set, split-K not yet): launches whose tiles
-// fill less than half the GPU and that have at least 16 K steps run their K
-// steps in slices of at least 8 steps on more CTAs, and a reduce kernel adds
-// the slices in order and applies the epilogue.
+// fill less than half the GPU and that have at least 32 K steps run their K
+// steps in slices of at least 16 steps on more CTAs (one wave), and a reduce
+// kernel adds the slices in order and applies the epilogue.
 template <int AMODE>
 void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, GemmParams& p, cudaStream_t s) {
   p.tiles_mn = p.tiles;
@@ -90,8 +90,8 @@ void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, Gemm
   p.ws = nullptr;
   p.ws_n = p.tiles_n * pw.bn;
   const bool splittable = p.out_mode == OUT_STORE || p.out_mode == OUT_ACCUM || p.out_mode == OUT_MAP;
-  if (splittable && p.tiles_mn * 2 <= dev.sms() && p.ksteps >= 16) {
-    const int want = std::min(dev.sms() / p.tiles_mn, p.ksteps / 8);  // one wave of tiles
+  if (splittable && p.tiles_mn * 2 <= dev.sms() && p.ksteps >= 32) {
+    const int want = std::min(dev.sms() / p.tiles_mn, p.ksteps / 16);  // one wave of tiles
     if (want >= 2) {
       p.kslice = (p.ksteps + want - 1) / want;
       p.ksplit = (p.ksteps + p.kslice - 1) / p.kslice;
@@ -105,7 +105,17 @@ void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, Gemm
   if (p.ksplit > 1) {
     const long long total = (long long)p.M * ((p.N + 7) / 8);
     const int grid = (int)std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)dev.sms() * 16));
-    gemm_splitk_reduce<<<grid, 256, 0, s>>>(p);
+    // programmatic dependent of the GEMM: it waits for the partial sums
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    IEC_CUDA(cudaLaunchKernelEx(&cfg, gemm_splitk_reduce, p));
     IEC_CUDA(cudaGetLastError());
   }
 }

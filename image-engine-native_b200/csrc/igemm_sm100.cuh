@@ -514,6 +514,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // tile epilogue's bias, activation and store (OUT_STORE, OUT_ACCUM, OUT_MAP).
 // One thread per (row, 8-column group).
 static __global__ void __launch_bounds__(256) gemm_splitk_reduce(const GemmParams p) {
+  griddep_wait();  // launched as a programmatic dependent of the GEMM
   const int groups = (p.N + 7) / 8;
   const long long total = (long long)p.M * groups;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
