@@ -33,9 +33,6 @@ struct Line {
   const float* sin_t;
 };
 
-__device__ __forceinline__ float2 cmul(float2 a, float wr, float wi) {
-  return make_float2(a.x * wr - a.y * wi, a.x * wi + a.y * wr);
-}
 
 __device__ __forceinline__ float4 cmul2(float4 v, float wr, float wi) {
   return make_float4(v.x * wr - v.y * wi, v.x * wi + v.y * wr, v.z * wr - v.w * wi, v.z * wi + v.w * wr);

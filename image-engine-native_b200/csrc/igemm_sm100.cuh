@@ -65,7 +65,7 @@ enum GemmA { A_ROWS = 0, A_TAPS = 1 };
 enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3, OUT_PHASE = 4, OUT_MAP = 5 };
 enum GemmAct { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_SIGMOID = 3 };
 
-constexpr int GEMM_EPI_WARPS = 8;
+constexpr int GEMM_EPI_WARPS = 16;
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_MAX_TAPS = 49;
 
@@ -159,15 +159,37 @@ __device__ __forceinline__ uint4 pack_half8(const float* w) {
   return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
-// GELU and sigmoid stay out of line: inlined into every element of the
-// unrolled epilogue they made its loop body too large for the instruction
-// cache, and the common ReLU / identity path would pay for them.
-static __device__ __noinline__ float gemm_gelu(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+// Sigmoid stays out of line (and GELU compact): inlined into every element of
+// the unrolled epilogue they made its loop body too large for the
+// instruction cache, and the common ReLU / identity path would pay for them.
+// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7; __expf adds about
+// 1e-7 relative): compact enough to stay inline in the epilogue.
+__device__ __forceinline__ float gemm_erf(float x) {
+  const float a = fabsf(x), t = 1.0f / fmaf(0.3275911f, a, 1.0f);
+  const float poly =
+      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+  return copysignf(1.0f - poly * __expf(-a * a), x);
+}
+__device__ __forceinline__ float gemm_gelu(float v) { return 0.5f * v * (1.0f + gemm_erf(v * 0.70710678118654752f)); }
 
 static __device__ __noinline__ float gemm_sigmoid(float v) {
   // math.rs:33-39: from exp(-|x|), so that neither tail cancels.
   const float e = expf(-fabsf(v)), s = e / (e + 1.0f);
   return v > 0.0f ? 1.0f - s : s;
+}
+
+// The activation of 16 values, one branch for all of them.
+__device__ __forceinline__ void act16(float* v, int act) {
+  if (act == ACT_RELU) {
+#pragma unroll
+    for (int e = 0; e < 16; e++) v[e] = v[e] > 0.0f ? v[e] : 0.0f;
+  } else if (act == ACT_GELU) {
+#pragma unroll
+    for (int e = 0; e < 16; e++) v[e] = gemm_gelu(v[e]);
+  } else if (act == ACT_SIGMOID) {
+#pragma unroll
+    for (int e = 0; e < 16; e++) v[e] = gemm_sigmoid(v[e]);
+  }
 }
 
 __device__ __forceinline__ float gemm_act(float v, int act) {
@@ -368,15 +390,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp & 3;
-    const int part = (warp - 2) >> 2;  // which half of the columns
+    const int part = (warp - 2) >> 2;  // which quarter of the columns
     const int row = quarter * 32 + lane;
-    constexpr int HALF = (BN + 31) / 32 * 16;  // columns per part, a multiple of 16
+    constexpr int HALF = (BN + 63) / 64 * 16;  // columns per part, a multiple of 16
     // Stage the bias in shared memory: the epilogue then reads it at shared
     // memory latency instead of a round trip to L2 per column chunk.
     float* sbias = reinterpret_cast<float*>(smem + L::BIAS_OFF);
-    const bool bias_staged = p.bias && p.N <= L::BIAS_FLOATS;
+    const int n_pad = p.tiles_n * BN;
+    const bool bias_staged = p.bias && n_pad <= L::BIAS_FLOATS;
     if (bias_staged)
-      for (int j = (int)threadIdx.x - 64; j < p.N; j += 32 * GEMM_EPI_WARPS) sbias[j] = p.bias[j];
+      for (int j = (int)threadIdx.x - 64; j < n_pad; j += 32 * GEMM_EPI_WARPS) sbias[j] = j < p.N ? p.bias[j] : 0.0f;
     asm volatile("bar.sync 1, %0;" ::"n"(32 * GEMM_EPI_WARPS) : "memory");
     const float* bias = bias_staged ? sbias : p.bias;
     int i = 0;
@@ -448,11 +471,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int n0 = nt * BN + c0;
         if (m < 0 || n0 >= p.N) continue;
         float v[16];
+        if (bias_staged) {
+          const float4* b4 = reinterpret_cast<const float4*>(sbias + n0);
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-          float x = __uint_as_float(r[e]);
-          if (bias) x += bias[n0 + e < p.N ? n0 + e : 0];
-          v[e] = x;
+          for (int q = 0; q < 4; q++) {
+            const float4 b = b4[q];
+            v[4 * q] = __uint_as_float(r[4 * q]) + b.x;
+            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + b.y;
+            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + b.z;
+            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + b.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; e++) {
+            float x = __uint_as_float(r[e]);
+            if (bias) x += bias[n0 + e < p.N ? n0 + e : 0];
+            v[e] = x;
+          }
+        }
+        if (p.out_mode == OUT_STORE) {
+          // the common case without per-group branches
+          act16(v, p.act);
+          __half* dst = p.out + (long long)(p.out_plane0 + n0 / 8) * p.out_plane_elems + dest * 8;
+          *reinterpret_cast<uint4*>(dst) = pack_half8(v);
+          if (n0 + 8 < p.N) *reinterpret_cast<uint4*>(dst + p.out_plane_elems) = pack_half8(v + 8);
+          continue;
         }
 #pragma unroll
         for (int g = 0; g < 2; g++) {

@@ -131,7 +131,7 @@ extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int 
 // tap); mode 2: one tap over an h x w map. out_map: store through OUT_MAP
 // (unpadded map) with `sources` old-value sources (0..2) instead of OUT_STORE.
 extern "C" iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, int w, int k, int n, int out_map,
-                                             int sources, int iters, float* us) {
+                                             int sources, int act, int iters, float* us) {
   try {
     Options opt;
     opt.device = device;
@@ -177,9 +177,9 @@ extern "C" iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, i
       tl.push_back({1, 1, 0});
     auto launch = [&]() {
       if (mode == 0)
-        gemm_rows(dev, pw, a.as<__half>(), in_plane, rows, ACT_RELU, spec, s);
+        gemm_rows(dev, pw, a.as<__half>(), in_plane, rows, act, spec, s);
       else
-        gemm_taps(dev, pw, src_geom.source(a.as<__half>()), tl, h, width, ACT_RELU, spec, s);
+        gemm_taps(dev, pw, src_geom.source(a.as<__half>()), tl, h, width, act, spec, s);
     };
     for (int i = 0; i < 3; i++) launch();
     cudaEvent_t e0, e1;

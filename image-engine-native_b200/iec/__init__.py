@@ -72,7 +72,7 @@ def lib():
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
         L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, f32p, f32p]
-        L.iec_selftest_gemm_time.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)]
+        L.iec_selftest_gemm_time.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)]
         L.iec_selftest_attention.argtypes = [i32, f32p, i32, i32, f32p, i32, i32, i32, f32p]
         L.iec_scunet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
         L.iec_scunet_free.argtypes = [vp]
@@ -429,9 +429,9 @@ def selftest_rfft2(x: np.ndarray, device: int = -1):
 
 
 def selftest_gemm_time(mode: int, m_or_h: int, w: int, k: int, n: int, out_map: bool = False, sources: int = 0,
-                       iters: int = 50, device: int = -1):
+                       iters: int = 50, device: int = -1, act: int = 1):
     """(device us, host enqueue us, graph-replay device us) per launch of
     one GEMM shape (iec_selftest_gemm_time)."""
     us = (ctypes.c_float * 3)()
-    _check(lib().iec_selftest_gemm_time(device, mode, m_or_h, w, k, n, int(out_map), sources, iters, us))
+    _check(lib().iec_selftest_gemm_time(device, mode, m_or_h, w, k, n, int(out_map), sources, act, iters, us))
     return tuple(us)

@@ -265,11 +265,12 @@ iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, f
 /* Diagnostics: per launch of the general GEMM on zero-filled buffers (mode
  * 0: m x k rows; 1: 3x3 taps over an h x w map; 2: one tap over an h x w
  * map), `iters` launches back to back; out_map stores through the map
- * epilogue with `sources` (0..2) old-value sources. us[0] device
+ * epilogue with `sources` (0..2) old-value sources; act 0 none, 1 ReLU, 2 GELU,
+ * 3 sigmoid. us[0] device
  * microseconds, us[1] host microseconds to enqueue, us[2] device
  * microseconds replayed from a CUDA graph. */
 iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, int w, int k, int n, int out_map,
-                                  int sources, int iters, float* us);
+                                  int sources, int act, int iters, float* us);
 
 /* Diagnostics: the fused window attention on host arrays: `qkv` windows * 64
  * rows of 3c (q | k | v), `bias` classes x (c / 32) x 64 x 64, `out` windows *
