@@ -17,6 +17,7 @@
 #include <cuda_fp16.h>
 
 #include "gemm.h"
+#include "sm100.cuh"
 
 namespace iec {
 
@@ -54,6 +55,8 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
                                                                int c, const float* __restrict__ bias, int shifted,
                                                                int rows_w, int cols_w, __half* __restrict__ out,
                                                                long long out_plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ __align__(16) __half sq[TOK * PITCH], sk[TOK * PITCH], sv[TOK * PITCH];
   const int win = blockIdx.x, head = blockIdx.y, heads = gridDim.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -165,7 +168,7 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
                       cudaStream_t s) {
   if (c % 32 != 0) throw Error(ERR_INPUT, "attention channels must be a multiple of 32");
   dim3 grid(windows, c / 32);
-  window_attention_kernel<<<grid, 128, 0, s>>>(qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w, out,
+  launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w, out,
                                                out_plane_elems);
   IEC_CUDA(cudaGetLastError());
 }

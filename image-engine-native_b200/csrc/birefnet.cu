@@ -88,6 +88,8 @@ __device__ __forceinline__ void axis(int out, int len_in, int len_out, int& i0, 
 // lib.rs:116-133: 8-bit RGB through the ImageNet normalisation (or a copy of
 // an already normalised image).
 __global__ void bir_prep(const void* __restrict__ src, int u8, long long n, float* __restrict__ dst) {
+  griddep_wait();
+  griddep_launch_dependents();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     if (u8) {
       const int c = (int)(i % 3);
@@ -101,6 +103,8 @@ __global__ void bir_prep(const void* __restrict__ src, int u8, long long n, floa
 // decoder.rs:443-521 on an f32 NHWC map (the half-size image).
 __global__ void bir_resize_f32(const float* __restrict__ src, int sh, int sw, int c, float* __restrict__ dst, int dh,
                                int dw) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long n = (long long)dh * dw;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int y = (int)(i / dw), x = (int)(i % dw);
@@ -120,6 +124,8 @@ __global__ void bir_resize_f32(const float* __restrict__ src, int sh, int sw, in
 // added onto the destination (decoder.rs:500-519).
 __global__ void bir_resize_planar(const __half* __restrict__ src, long long src_plane, int sh, int sw,
                                   __half* __restrict__ dst, long long dst_plane, int dh, int dw, int planes, int add) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long n = (long long)dh * dw * planes;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int q = (int)(i / ((long long)dh * dw));
@@ -149,6 +155,8 @@ __global__ void bir_resize_planar(const __half* __restrict__ src, long long src_
 
 // swin.rs:188-204: each 4 x 4 patch's 48 values, (ky, kx, c) order.
 __global__ void bir_embed_gather(const float* __restrict__ img, int side, __half* __restrict__ dst, long long plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int grid = side / 4;
   const long long n = (long long)grid * grid * 6;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -169,6 +177,8 @@ __global__ void bir_embed_gather(const float* __restrict__ img, int side, __half
 // f64 totals).
 __global__ void bir_channel_sums(const __half* __restrict__ t, long long plane, long long pixels,
                                  double* __restrict__ sums) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int q = blockIdx.y;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
@@ -191,6 +201,8 @@ __global__ void bir_channel_sums(const __half* __restrict__ t, long long plane, 
 __global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, const float* __restrict__ pool_w,
                               const float* __restrict__ pool_b, const float* __restrict__ conv1_pool,
                               const float* __restrict__ conv1_bias, float* __restrict__ bias) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float mean[INTER], pooled[BRANCH];
   const int t = threadIdx.x;
   if (t < INTER) mean[t] = (float)(sums[t] / pixels);
@@ -216,6 +228,8 @@ __global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, co
 __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plane, int height, int width, int size,
                                   const __half* __restrict__ offs, long long offs_plane, __half* __restrict__ out,
                                   long long out_plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int taps = size * size;
   const long long n = (long long)height * width * taps * 8;
   const float hs = (float)(size / 2), hf = (float)height, wf = (float)width;
@@ -256,6 +270,8 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
 // block's output (`planes` channel groups).
 __global__ void bir_gate(const __half* __restrict__ g16, long long g_plane, const float* __restrict__ w, float b,
                          __half* __restrict__ out, long long out_plane, int planes, long long pixels) {
+  griddep_wait();
+  griddep_launch_dependents();
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
        p += (long long)gridDim.x * blockDim.x) {
     float v[16];
@@ -279,6 +295,8 @@ __global__ void bir_gate(const __half* __restrict__ g16, long long g_plane, cons
 // pixels, patch (gy, gx) of colour c as channel (c g + gy) g + gx.
 __global__ void bir_patches(const float* __restrict__ img, int side, int size, __half* __restrict__ dst,
                             long long plane, int out_groups) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int g = side / size, groups = 3 * g * g / 8;
   const long long n = (long long)size * size * out_groups;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -298,6 +316,8 @@ __global__ void bir_patches(const float* __restrict__ img, int side, int size, _
 // decoder.rs:882-898: the head's 1x1 convolution to one channel, in f32.
 __global__ void bir_head(const __half* __restrict__ x, long long plane, const float* __restrict__ w, long long pixels,
                          float* __restrict__ low) {
+  griddep_wait();
+  griddep_launch_dependents();
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
        p += (long long)gridDim.x * blockDim.x) {
     float s = 0.0f;
@@ -316,6 +336,8 @@ __global__ void bir_head(const __half* __restrict__ x, long long plane, const fl
 // composed 5x5 convolution; border pixels get the branch from bir_edges.
 __global__ void bir_logits(const float* __restrict__ low, int lg, const float* __restrict__ img, int side,
                            const float* __restrict__ fr, float head_b, float* __restrict__ logits) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long n = (long long)side * side;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const int y = (int)(i / side), x = (int)(i % side);
@@ -347,6 +369,8 @@ __global__ void bir_logits(const float* __restrict__ low, int lg, const float* _
 // pixel, two of the 64 intermediate channels per lane.
 __global__ void bir_edges(const float* __restrict__ img, int side, const float* __restrict__ fr,
                           float* __restrict__ logits) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int e_count = 4 * side - 4;
   for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < e_count; w += (gridDim.x * blockDim.x) >> 5) {
@@ -656,7 +680,7 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
   const int sms = dev_.sms();
   int grid = side / 4;
   long long tokens = (long long)grid * grid;
-  bir_embed_gather<<<blocks_for(tokens * 6, sms), 256, 0, s>>>(img, side, patch_rows_.as<__half>(), pe(tokens));
+  launch_pdl(bir_embed_gather, blocks_for(tokens * 6, sms), 256, 0, s, img, side, patch_rows_.as<__half>(), pe(tokens));
   IEC_CUDA(cudaGetLastError());
   __half* x = x_.as<__half>();
   {
@@ -744,10 +768,10 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
   // ASPP (decoder.rs:138-236): the pooled bias, four deformable branches
   // into `cat`, conv1 + bias + ReLU.
   IEC_CUDA(cudaMemsetAsync(sums_.get(), 0, INTER * sizeof(double), s));
-  bir_channel_sums<<<dim3(std::max(1, std::min(64, (int)((P + 255) / 256))), 8), 256, 0, s>>>(t, pp, P,
+  launch_pdl(bir_channel_sums, dim3(std::max(1, std::min(64, (int)((P + 255) / 256))), 8), 256, 0, s, t, pp, P,
                                                                                               sums_.as<double>());
   IEC_CUDA(cudaGetLastError());
-  bir_aspp_bias<<<1, 256, 0, s>>>(sums_.as<double>(), (double)P, b.pool_w.as<float>(), b.pool_b.as<float>(),
+  launch_pdl(bir_aspp_bias, 1, 256, 0, s, sums_.as<double>(), (double)P, b.pool_w.as<float>(), b.pool_b.as<float>(),
                                   b.conv1_pool.as<float>(), b.conv1_bias.as<float>(), b.conv1.bias.as<float>());
   IEC_CUDA(cudaGetLastError());
   for (int i = 0; i < 4; i++) {
@@ -760,7 +784,7 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     o.out = offs_.as<__half>();
     o.plane_elems = pp;
     gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, s);
-    bir_deform_sample<<<blocks_for(P * taps * 8, sms), 256, 0, s>>>(t, pp, g, g, k, offs_.as<__half>(), pp,
+    launch_pdl(bir_deform_sample, blocks_for(P * taps * 8, sms), 256, 0, s, t, pp, g, g, k, offs_.as<__half>(), pp,
                                                                 samp_.as<__half>(), pp);
     IEC_CUDA(cudaGetLastError());
     GemmOutSpec c;
@@ -792,7 +816,7 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     go.out = g16_.as<__half>();
     go.plane_elems = pp;
     gemm_conv3(dev_, b.gdt, base, out_plane, g, g, ACT_RELU, go, s);
-    bir_gate<<<blocks_for(P, sms), 256, 0, s>>>(g16_.as<__half>(), pp, b.gw.as<float>(), b.gb, base, out_plane,
+    launch_pdl(bir_gate, blocks_for(P, sms), 256, 0, s, g16_.as<__half>(), pp, b.gw.as<float>(), b.gb, base, out_plane,
                                                  b.cout / 8, P);
     IEC_CUDA(cudaGetLastError());
   }
@@ -805,10 +829,10 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
   const int sms = dev_.sms();
   const long long n = (long long)side * side * 3;
   float* img = img_.as<float>();
-  bir_prep<<<blocks_for(n, sms), 256, 0, s>>>(image, u8 ? 1 : 0, n, img);
+  launch_pdl(bir_prep, blocks_for(n, sms), 256, 0, s, image, u8 ? 1 : 0, n, img);
   IEC_CUDA(cudaGetLastError());
   const int hs = side / 2;
-  bir_resize_f32<<<blocks_for((long long)hs * hs, sms), 256, 0, s>>>(img, side, side, 3, himg_.as<float>(), hs, hs);
+  launch_pdl(bir_resize_f32, blocks_for((long long)hs * hs, sms), 256, 0, s, img, side, side, 3, himg_.as<float>(), hs, hs);
   IEC_CUDA(cudaGetLastError());
 
   const int g0 = side / 4, g[4] = {g0, g0 / 2, g0 / 4, g0 / 8};
@@ -834,7 +858,7 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
     __half* dst = i < 3 ? lev_[i].as<__half>() : x4_.as<__half>();
     const int plane = i < 3 ? c8 : 168 + c8;
     const long long dp = pe((long long)g[i] * g[i]);
-    bir_resize_planar<<<blocks_for((long long)g[i] * g[i] * c8, sms), 256, 0, s>>>(
+    launch_pdl(bir_resize_planar, blocks_for((long long)g[i] * g[i] * c8, sms), 256, 0, s, 
         hf_[i].as<__half>(), pe((long long)hg * hg), hg, hg, dst + plane * dp, dp, g[i], g[i], c8, 0);
     IEC_CUDA(cudaGetLastError());
   }
@@ -844,7 +868,7 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
     int plane = 0;
     for (int i = 0; i < 3; i++) {
       const int c8 = 2 * STAGE_C[i] / 8;
-      bir_resize_planar<<<blocks_for((long long)g[3] * g[3] * c8, sms), 256, 0, s>>>(
+      launch_pdl(bir_resize_planar, blocks_for((long long)g[3] * g[3] * c8, sms), 256, 0, s, 
           lev_[i].as<__half>(), pe((long long)g[i] * g[i]), g[i], g[i], x4_.as<__half>() + plane * p3, p3, g[3], g[3],
           c8, 0);
       IEC_CUDA(cudaGetLastError());
@@ -868,7 +892,7 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
       gemm_rows(dev_, laterals_[i - 1], lev_[level].as<__half>(), ip, gi * gi, ACT_NONE, o, s);
       const int pg = g[level + 1];
       const __half* prev = outb_[i - 1].as<__half>();
-      bir_resize_planar<<<blocks_for((long long)gi * gi * (main_c[i] / 8), sms), 256, 0, s>>>(
+      launch_pdl(bir_resize_planar, blocks_for((long long)gi * gi * (main_c[i] / 8), sms), 256, 0, s, 
           prev, pe((long long)pg * pg), pg, pg, in, ip, gi, gi, main_c[i] / 8, 1);
       IEC_CUDA(cudaGetLastError());
     }
@@ -877,7 +901,7 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
       const Patches& pt = *patches_[i];
       const int groups = pad64(PATCH_C[i]) / 8;  // zero channels past the stack's
       const long long sp = pe((long long)gi * gi);
-      bir_patches<<<blocks_for((long long)gi * gi * groups, sms), 256, 0, s>>>(img, side, gi, stack_.as<__half>(), sp,
+      launch_pdl(bir_patches, blocks_for((long long)gi * gi * groups, sms), 256, 0, s, img, side, gi, stack_.as<__half>(), sp,
                                                                                 groups);
       IEC_CUDA(cudaGetLastError());
       GemmOutSpec o;
@@ -896,13 +920,13 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
   // head
   {
     const long long P0 = (long long)g0 * g0;
-    bir_head<<<blocks_for(P0, sms), 256, 0, s>>>(out1_.as<__half>(), pe(P0), head_w_.as<float>(), P0,
+    launch_pdl(bir_head, blocks_for(P0, sms), 256, 0, s, out1_.as<__half>(), pe(P0), head_w_.as<float>(), P0,
                                                   low_.as<float>());
     IEC_CUDA(cudaGetLastError());
-    bir_logits<<<blocks_for((long long)side * side, sms), 256, 0, s>>>(low_.as<float>(), g0, img, side,
+    launch_pdl(bir_logits, blocks_for((long long)side * side, sms), 256, 0, s, low_.as<float>(), g0, img, side,
                                                                         full_.as<float>(), head_b_, logits);
     IEC_CUDA(cudaGetLastError());
-    bir_edges<<<blocks_for((long long)(4 * side - 4) * 32, sms), 256, 0, s>>>(img, side, full_.as<float>(), logits);
+    launch_pdl(bir_edges, blocks_for((long long)(4 * side - 4) * 32, sms), 256, 0, s, img, side, full_.as<float>(), logits);
     IEC_CUDA(cudaGetLastError());
   }
 }

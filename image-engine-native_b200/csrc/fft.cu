@@ -15,8 +15,10 @@
 //            rows  the Hermitian row (imaginary parts of columns 0 and w/2
 //                  dropped) -> real part, times 1 / sqrt(h w), added on x
 #include "fft.h"
+#include "sm100.cuh"
 
 #include <cmath>
+
 #include <vector>
 
 namespace iec {
@@ -170,6 +172,8 @@ __device__ __forceinline__ void copy_point(float2* dst, const float2* src) {
 // Forward rows: x (real) -> scratch row spectra.
 __global__ void __launch_bounds__(FFT_THREADS) fft_rows_fwd(const __half* __restrict__ x, long long x_plane,
                                                            float2* __restrict__ T, Dims d, Line f) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ float4 fft_smem4[];
   float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
   const int g = blockIdx.y, y0 = blockIdx.x * d.lines_rows;
@@ -197,6 +201,8 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_rows_fwd(const __half* __rest
 // Forward columns: scratch -> f16 spectrum (real planes, then imaginary).
 __global__ void __launch_bounds__(FFT_THREADS) fft_cols_fwd(const float2* __restrict__ T, __half* __restrict__ spec,
                                                            long long spec_plane, Dims d, Line f) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ float4 fft_smem4[];
   float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
   const int g = blockIdx.y, k0 = blockIdx.x * d.lines_cols;
@@ -232,6 +238,8 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_cols_fwd(const float2* __rest
 // Inverse columns: f16 spectrum -> scratch.
 __global__ void __launch_bounds__(FFT_THREADS) fft_cols_inv(const __half* __restrict__ spec, long long spec_plane,
                                                            float2* __restrict__ T, Dims d, Line f) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ float4 fft_smem4[];
   float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
   const int g = blockIdx.y, k0 = blockIdx.x * d.lines_cols;
@@ -264,6 +272,8 @@ __global__ void __launch_bounds__(FFT_THREADS) fft_cols_inv(const __half* __rest
 // Inverse rows: scratch -> the Hermitian row -> real part, added on x.
 __global__ void __launch_bounds__(FFT_THREADS) fft_rows_inv(const float2* __restrict__ T, __half* __restrict__ x,
                                                            long long x_plane, Dims d, Line f) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ float4 fft_smem4[];
   float2* fft_smem = reinterpret_cast<float2*>(fft_smem4);
   const int g = blockIdx.y, y0 = blockIdx.x * d.lines_rows;
@@ -365,10 +375,10 @@ void rfft2_planar(const FourierPlan& plan, const __half* x, long long x_plane_el
   const size_t sr = smem_for(d.lines_rows, d.w), sc = smem_for(d.lines_cols, d.h);
   prepare(fft_rows_fwd, sr);
   prepare(fft_cols_fwd, sc);
-  fft_rows_fwd<<<dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s>>>(
+  launch_pdl(fft_rows_fwd, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, 
       x, x_plane_elems, T, d, line_of(plan, true));
   IEC_CUDA(cudaGetLastError());
-  fft_cols_fwd<<<dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s>>>(
+  launch_pdl(fft_cols_fwd, dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s, 
       T, spec, spec_plane_elems, d, line_of(plan, false));
   IEC_CUDA(cudaGetLastError());
 }
@@ -380,10 +390,10 @@ void irfft2_add_planar(const FourierPlan& plan, const __half* spec, long long sp
   const size_t sr = smem_for(d.lines_rows, d.w), sc = smem_for(d.lines_cols, d.h);
   prepare(fft_cols_inv, sc);
   prepare(fft_rows_inv, sr);
-  fft_cols_inv<<<dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s>>>(
+  launch_pdl(fft_cols_inv, dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s, 
       spec, spec_plane_elems, T, d, line_of(plan, false));
   IEC_CUDA(cudaGetLastError());
-  fft_rows_inv<<<dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s>>>(
+  launch_pdl(fft_rows_inv, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, 
       T, x, x_plane_elems, d, line_of(plan, true));
   IEC_CUDA(cudaGetLastError());
 }

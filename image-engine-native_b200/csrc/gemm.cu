@@ -303,6 +303,8 @@ void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const
 // ---------------------------------------------------------- bandwidth kernels
 __global__ void rows_to_planar_kernel(const float* __restrict__ src, int rows, int c, __half* __restrict__ dst,
                                       long long plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int groups = c / 8;
   const long long total = (long long)rows * groups;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -320,6 +322,8 @@ __global__ void rows_to_planar_kernel(const float* __restrict__ src, int rows, i
 
 __global__ void planar_to_rows_kernel(const __half* __restrict__ src, long long plane, int rows, int c,
                                       float* __restrict__ dst) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long total = (long long)rows * c;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const int ch = (int)(i % c);
@@ -334,12 +338,12 @@ static int grid_for(long long n, int block, int sms) {
 
 void rows_to_planar(const float* src, int rows, int c, __half* dst, long long dst_plane_elems, cudaStream_t s) {
   if (c % 8 != 0) throw Error(ERR_INPUT, "channels must be a multiple of 8");
-  rows_to_planar_kernel<<<grid_for((long long)rows * c / 8, 256, 148), 256, 0, s>>>(src, rows, c, dst, dst_plane_elems);
+  launch_pdl(rows_to_planar_kernel, grid_for((long long)rows * c / 8, 256, 148), 256, 0, s, src, rows, c, dst, dst_plane_elems);
   IEC_CUDA(cudaGetLastError());
 }
 
 void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int c, float* dst, cudaStream_t s) {
-  planar_to_rows_kernel<<<grid_for((long long)rows * c, 256, 148), 256, 0, s>>>(src, src_plane_elems, rows, c, dst);
+  launch_pdl(planar_to_rows_kernel, grid_for((long long)rows * c, 256, 148), 256, 0, s, src, src_plane_elems, rows, c, dst);
   IEC_CUDA(cudaGetLastError());
 }
 
@@ -355,6 +359,8 @@ __global__ void __launch_bounds__(256) layer_norm_rows(const __half* __restrict_
                                                        int rows, int c, const float* __restrict__ gamma,
                                                        const float* __restrict__ beta, __half* __restrict__ dst,
                                                        long long dst_plane, int mode, WindowMap wm, int grid) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x % S, sub = threadIdx.x / S;
   const int r = blockIdx.x * (256 / S) + sub;
   const bool valid = r < rows;
@@ -439,16 +445,16 @@ static void launch_ln(const __half* src, long long src_plane, int plane0, int ro
   const int groups = c / 8;
   if (c % 8 != 0 || groups < 1) throw Error(ERR_INPUT, "layer norm over a channel count not a multiple of 8");
   if (groups <= 8) {
-    layer_norm_rows<2, 4><<<(rows + 127) / 128, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<2, 4>, (rows + 127) / 128, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                              dst_plane, mode, wm, grid);
   } else if (groups <= 16) {
-    layer_norm_rows<4, 4><<<(rows + 63) / 64, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<4, 4>, (rows + 63) / 64, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                            dst_plane, mode, wm, grid);
   } else if (groups <= 48) {
-    layer_norm_rows<8, 6><<<(rows + 31) / 32, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<8, 6>, (rows + 31) / 32, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                            dst_plane, mode, wm, grid);
   } else if (groups <= 384) {
-    layer_norm_rows<32, 12><<<(rows + 7) / 8, 256, 0, s>>>(src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<32, 12>, (rows + 7) / 8, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                            dst_plane, mode, wm, grid);
   } else {
     throw Error(ERR_INPUT, "layer norm over more than 3072 channels");

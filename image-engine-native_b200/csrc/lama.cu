@@ -52,6 +52,8 @@ __device__ __forceinline__ int reflect_index(int i, int n) {
 // the hp x wp map mirroring the image past its bottom and right edges.
 __global__ void lama_prep(const void* __restrict__ image, int image_u8, const void* __restrict__ mask, int mask_u8,
                           int width, int height, int hp, int wp, __half* __restrict__ dst, long long plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long total = (long long)(hp + 6) * wp;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -92,6 +94,8 @@ __global__ void lama_prep(const void* __restrict__ image, int image_u8, const vo
 // Zero the one-pixel border of a map reflect-padded by 1 (h x w inside), so
 // that the transposed convolution's phase taps read zeros past the edge.
 __global__ void lama_zero_border(__half* __restrict__ x, long long plane, int planes, int h, int w) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int ring = 2 * (w + 2) + 2 * h;
   const long long total = (long long)ring * planes;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -118,6 +122,8 @@ __global__ void lama_zero_border(__half* __restrict__ x, long long plane, int pl
 __global__ void lama_output(const __half* __restrict__ pred, int wp, int width, int height, void* __restrict__ dst,
                             int dst_u8, const uint8_t* __restrict__ rgb, const void* __restrict__ mask,
                             int mask_u8) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long total = (long long)width * height;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -302,7 +308,7 @@ bool Lama::run(const void* image, bool image_u8, const void* mask, bool mask_u8,
   // first: conv7 over the folded input, into down0's phases.
   {
     const long long plane = (long long)(hp + 6) * wp * 8;
-    lama_prep<<<blocks_for((long long)(hp + 6) * wp, sms), 256, 0, s>>>(image, image_u8 ? 1 : 0, mask,
+    launch_pdl(lama_prep, blocks_for((long long)(hp + 6) * wp, sms), 256, 0, s, image, image_u8 ? 1 : 0, mask,
                                                                          mask_u8 ? 1 : 0, width, height, hp, wp,
                                                                          in0_.as<__half>(), plane);
     IEC_CUDA(cudaGetLastError());
@@ -344,7 +350,7 @@ bool Lama::run(const void* image, bool image_u8, const void* mask, bool mask_u8,
   {
     const int h8 = hp / 8, w8 = wp / 8;
     const MapGeom g8{h8, w8, 1, 1};
-    lama_zero_border<<<blocks_for((long long)(2 * (w8 + 2) + 2 * h8) * 64, sms), 256, 0, s>>>(
+    launch_pdl(lama_zero_border, blocks_for((long long)(2 * (w8 + 2) + 2 * h8) * 64, sms), 256, 0, s, 
         x_.as<__half>(), g8.plane_elems(), 64, h8, w8);
     IEC_CUDA(cudaGetLastError());
     int h = h8, w = w8;
@@ -386,7 +392,7 @@ bool Lama::run(const void* image, bool image_u8, const void* mask, bool mask_u8,
     o.out = out_.as<__half>();
     o.plane_elems = (long long)gemm_rows_alloc(hp * wp) * 8;
     gemm_taps(dev_, last_, MapGeom{hp, wp, 3, 1}.source(u2_.as<__half>()), taps7, hp, wp, ACT_SIGMOID, o, s);
-    lama_output<<<blocks_for((long long)width * height, sms), 256, 0, s>>>(
+    launch_pdl(lama_output, blocks_for((long long)width * height, sms), 256, 0, s, 
         out_.as<__half>(), wp, width, height, dst, dst_u8 ? 1 : 0, static_cast<const uint8_t*>(image), mask,
         mask_u8 ? 1 : 0);
     IEC_CUDA(cudaGetLastError());

@@ -18,6 +18,7 @@
 #include <map>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace iec {
@@ -184,6 +185,25 @@ class DeviceScope {
  private:
   int prev_ = -1;
 };
+
+// Launch `kernel` as a programmatic dependent of the work before it on `s`:
+// it may start while its predecessor drains, so it must execute
+// griddepcontrol.wait (griddep_wait in sm100.cuh) before touching global
+// memory.
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  IEC_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (so the
 // library does not link libcuda and still loads on a machine without it).

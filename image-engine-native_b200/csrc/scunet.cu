@@ -81,6 +81,8 @@ std::vector<float> bias_tables(const std::vector<float>& position, bool shifted)
 // planes (R, G, B and zeros; zeros) for the 16-channel head convolution.
 __global__ void scunet_prep(const void* __restrict__ src, int src_u8, int src_w, int rx0, int ry0, int rw, int rh,
                             int ph, int pw, __half* __restrict__ dst, long long plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long total = (long long)ph * pw;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const int y = (int)(i / pw), x = (int)(i % pw);
@@ -100,6 +102,8 @@ __global__ void scunet_prep(const void* __restrict__ src, int src_u8, int src_w,
 // input pixels (y, x), (y, x + 1), (y + 1, x), (y + 1, x + 1) in turn.
 __global__ void scunet_halve_gather(const __half* __restrict__ x, long long x_plane, int groups, int h, int w,
                                     __half* __restrict__ out, long long out_plane) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int oh = h / 2, ow = w / 2;
   const long long total = (long long)oh * ow * 4 * groups;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -115,6 +119,8 @@ __global__ void scunet_halve_gather(const __half* __restrict__ x, long long x_pl
 // x += s over `planes` planes of `rows` rows (network.rs:382-393).
 __global__ void scunet_add(__half* __restrict__ x, const __half* __restrict__ s, long long plane, int planes,
                            long long rows) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long total = (long long)planes * rows;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long at = (i / rows) * plane + (i % rows) * 8;
@@ -134,6 +140,8 @@ __global__ void scunet_add(__half* __restrict__ x, const __half* __restrict__ s,
 // image (f32 or 8-bit, lib.rs:264-270 to_byte).
 __global__ void scunet_store(const __half* __restrict__ y, int pw, int kx0, int ky0, int kx1, int ky1, int rx0,
                              int ry0, void* __restrict__ dst, int dst_u8, int dst_w) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int kw = kx1 - kx0;
   const long long total = (long long)kw * (ky1 - ky0);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -270,7 +278,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
   const long long P = (long long)ph * pw;
   __half* img = img_.as<__half>();
   const long long img_plane = rows_alloc(P) * 8;
-  scunet_prep<<<blocks_for(P, sms), 256, 0, s>>>(src, src_u8, src_w, rx0, ry0, rw, rh, ph, pw, img, img_plane);
+  launch_pdl(scunet_prep, blocks_for(P, sms), 256, 0, s, src, src_u8, src_w, rx0, ry0, rw, rh, ph, pw, img, img_plane);
   IEC_CUDA(cudaGetLastError());
 
   int done = 0;
@@ -371,7 +379,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       const int si = 2 - (level_index - 4);  // up levels 3, 2, 1 use skips 2, 1, 0
       const int cin = 2 * L.c;
       const long long pin = plane((long long)H * W);
-      scunet_add<<<blocks_for((long long)(cin / 8) * H * W, sms), 256, 0, s>>>(x, skip_[si].as<__half>(), pin,
+      launch_pdl(scunet_add, blocks_for((long long)(cin / 8) * H * W, sms), 256, 0, s, x, skip_[si].as<__half>(), pin,
                                                                                cin / 8, (long long)H * W);
       IEC_CUDA(cudaGetLastError());
       // The doubled map goes to y's buffer first, then becomes x.
@@ -391,7 +399,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       // halved(x) -> skip and the next level's x (network.rs:310-318).
       const int c = L.c;
       const long long pin = plane((long long)H * W), pout = plane((long long)H * W / 4);
-      scunet_halve_gather<<<blocks_for((long long)H * W / 4 * 4 * (c / 8), sms), 256, 0, s>>>(
+      launch_pdl(scunet_halve_gather, blocks_for((long long)H * W / 4 * 4 * (c / 8), sms), 256, 0, s, 
           x, pin, c / 8, H, W, gat_.as<__half>(), pout);
       IEC_CUDA(cudaGetLastError());
       GemmOutSpec o;
@@ -422,7 +430,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
   o.mode = OUT_STORE;
   o.out = out_.as<__half>();
   gemm_conv3(dev_, tail_, x, plane(P), H, W, ACT_NONE, o, s);
-  scunet_store<<<blocks_for((long long)(kx1 - kx0) * (ky1 - ky0), sms), 256, 0, s>>>(
+  launch_pdl(scunet_store, blocks_for((long long)(kx1 - kx0) * (ky1 - ky0), sms), 256, 0, s, 
       out_.as<__half>(), pw, kx0, ky0, kx1, ky1, rx0, ry0, dst, dst_u8 ? 1 : 0, src_w);
   IEC_CUDA(cudaGetLastError());
   return true;
