@@ -225,7 +225,7 @@ void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long 
   p.M = m;
   p.N = pw.n;
   p.K = pw.k;
-  p.tiles_m = (m + 127) / 128;
+  p.tiles_m = ((m + 127) / 128 + gemm_msub(pw.bn) - 1) / gemm_msub(pw.bn);
   p.tiles_n = pw.n_tiles;
   p.tiles = p.tiles_m * p.tiles_n;
   p.div_tiles_n = FastDiv((uint32_t)p.tiles_n);
@@ -285,7 +285,8 @@ void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const
   p.W = w;
   p.TW = tw;
   p.tiles_w = (w + tw - 1) / tw;
-  p.tiles_m = p.tiles_w * ((h + 7) / 8);
+  // groups of gemm_msub consecutive 8 x tw blocks, row-major
+  p.tiles_m = (p.tiles_w * ((h + 7) / 8) + gemm_msub(pw.bn) - 1) / gemm_msub(pw.bn);
   p.tiles_n = pw.n_tiles;
   p.tiles = p.tiles_m * p.tiles_n;
   p.div_tiles_n = FastDiv((uint32_t)p.tiles_n);

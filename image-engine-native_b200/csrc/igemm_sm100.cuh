@@ -120,9 +120,16 @@ __device__ __forceinline__ long long map_offset(const GemmParams& p, int r, int 
   return (long long)r * p.dst_pw + c;
 }
 
+// M blocks of 128 rows per tile: narrow tiles (N <= 64) take several, so that
+// each tile's pipeline hand-offs and weight loads serve more rows and all
+// four epilogue column parts have work.
+__host__ __device__ constexpr int gemm_msub(int bn) { return bn <= 32 ? 4 : bn <= 64 ? 2 : 1; }
+
 template <int BN, int KB>
 struct GemmSmem {
-  static constexpr int A_BYTES = (KB / 8) * 128 * 16;
+  static constexpr int MSUB = gemm_msub(BN);
+  static constexpr int A_ONE = (KB / 8) * 128 * 16;  // one M block
+  static constexpr int A_BYTES = MSUB * A_ONE;
   static constexpr int B_BYTES = (KB / 8) * BN * 16;
   static constexpr int STAGE = ((A_BYTES + B_BYTES) + 1023) / 1024 * 1024;
   static constexpr int NSTAGE = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
@@ -134,7 +141,7 @@ struct GemmSmem {
   static constexpr int BIAS_OFF = (MISC_OFF + 16 + 15) / 16 * 16;
   static constexpr int TOTAL = BIAS_OFF + BIAS_FLOATS * 4;
   static constexpr int DYN_BYTES = TOTAL + 1024;
-  static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int ACC_COLS = MSUB * (BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256);
   static constexpr int TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
 };
 
@@ -199,13 +206,14 @@ __device__ __forceinline__ float gemm_act(float v, int act) {
   return v;
 }
 
-// The OUT_MAP epilogue of one thread's row over columns [c_begin, c_end) of
-// its tile: in batches of 32 columns (two TMEM loads), the old values of the
+// The OUT_MAP epilogue of one thread's row over accumulator columns
+// [c_begin, c_end) of its tile (output column = that - cb + the N tile's): in batches of 32 columns (two TMEM loads), the old values of the
 // batch's four 8-column groups are loaded together ahead of the
 // accumulators, so that their latencies overlap.
 template <int BN>
 __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* bias, uint32_t taddr, int c_begin,
-                                             int c_end, int nt, int m, const int* ry, const int* rx, int nry, int nrx) {
+                                             int c_end, int cb, int nt, int m, const int* ry, const int* rx, int nry,
+                                             int nrx) {
   const bool live = m >= 0;
   const long long pix = live ? map_offset(p, ry[0], rx[0]) * 8 : 0;
 #pragma unroll 1
@@ -214,7 +222,7 @@ __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* b
     uint4 oa[4], orr[4];
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-      const int n = nt * BN + c0 + 8 * q;
+      const int n = nt * BN + (c0 - cb) + 8 * q;
       oa[q] = make_uint4(0u, 0u, 0u, 0u);
       orr[q] = oa[q];
       if (live && (q < 2 || two) && n < p.N) {
@@ -230,7 +238,7 @@ __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* b
     if (!live) continue;
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-      const int n = nt * BN + c0 + 8 * q;
+      const int n = nt * BN + (c0 - cb) + 8 * q;
       if ((q >= 2 && !two) || n >= p.N) continue;
       float w[8];
 #pragma unroll
@@ -313,12 +321,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
         const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
         const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
-        int x0 = 0, y0 = 0;
-        if (AMODE == A_TAPS) {
-          y0 = (int)p.div_tiles_w.div((uint32_t)mt);
-          x0 = (mt - y0 * p.tiles_w) * p.TW;
-          y0 *= 8;
-        }
         const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
         for (int ks = ks0; ks < ks1; ks++) {
           if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
@@ -326,13 +328,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           uint8_t* st = smem + s * L::STAGE;
-          mbar_arrive_expect_tx(&full[s], a_bytes + (uint32_t)L::B_BYTES);
-          if (AMODE == A_ROWS) {
-            tma_load_3d(st, &a_map, &full[s], 0, mt * 8, ks * KG);
-          } else {
-            const int per_tap = p.K / KB;
-            const int tap = ks / per_tap, kb = ks - tap * per_tap;
-            tma_load_5d(st, &a_map, &full[s], (x0 + p.dx[tap]) * 8, y0 + p.dy[tap], p.phase[tap], kb * KG, 0);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)L::MSUB * a_bytes + (uint32_t)L::B_BYTES);
+#pragma unroll
+          for (int sb = 0; sb < L::MSUB; sb++) {
+            const int blk = mt * L::MSUB + sb;
+            uint8_t* sa = st + sb * L::A_ONE;
+            if (AMODE == A_ROWS) {
+              tma_load_3d(sa, &a_map, &full[s], 0, blk * 8, ks * KG);
+            } else {
+              const int by = (int)p.div_tiles_w.div((uint32_t)blk);
+              const int bx0 = (blk - by * p.tiles_w) * p.TW, by0 = by * 8;
+              const int per_tap = p.K / KB;
+              const int tap = ks / per_tap, kb = ks - tap * per_tap;
+              tma_load_5d(sa, &a_map, &full[s], (bx0 + p.dx[tap]) * 8, by0 + p.dy[tap], p.phase[tap], kb * KG, 0);
+            }
           }
           bulk_load(st + L::A_BYTES, bsrc + (size_t)ks * L::B_BYTES, L::B_BYTES, &full[s]);
           issued[s] = (int)phase;
@@ -369,11 +378,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_after();
           const uint32_t abase = smem_u32(smem + s * L::STAGE), bbase = abase + (uint32_t)L::A_BYTES;
 #pragma unroll
-          for (int j = 0; j < KB / 16; j++) {
-            const uint64_t adesc = smem_desc(abase + (uint32_t)(2 * j) * lbo_a, lbo_a, 128);
-            const uint64_t bdesc = smem_desc(bbase + (uint32_t)(2 * j * BN * 16), BN * 16, 128);
-            umma_f16(d, adesc, bdesc, idesc, (ks != ks0) || (j != 0));
-          }
+          for (int sb = 0; sb < L::MSUB; sb++)
+#pragma unroll
+            for (int j = 0; j < KB / 16; j++) {
+              const uint64_t adesc = smem_desc(abase + (uint32_t)(sb * L::A_ONE + 2 * j * lbo_a), lbo_a, 128);
+              const uint64_t bdesc = smem_desc(bbase + (uint32_t)(2 * j * BN * 16), BN * 16, 128);
+              umma_f16(d + (uint32_t)(sb * BN), adesc, bdesc, idesc, (ks != ks0) || (j != 0));
+            }
           umma_commit(&empty[s]);
           if (++s == L::NSTAGE) {
             s = 0;
@@ -392,7 +403,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;  // which quarter of the columns
     const int row = quarter * 32 + lane;
-    constexpr int HALF = (BN + 63) / 64 * 16;  // columns per part, a multiple of 16
+    // columns per part (a multiple of 16); with several M blocks a part's
+    // columns lie in one block's accumulator
+    constexpr int HALF = (L::MSUB * BN + 63) / 64 * 16;
+    constexpr int ACC_USED = L::MSUB * BN;
+    const int sb = (part * HALF) / BN;  // this part's M block within the tile
+    const int cb = sb * BN;             // its first accumulator column
     // Stage the bias in shared memory: the epilogue then reads it at shared
     // memory latency instead of a round trip to L2 per column chunk.
     float* sbias = reinterpret_cast<float*>(smem + L::BIAS_OFF);
@@ -412,12 +428,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
       // This thread's output row, and for A_TAPS its pixel.
       int m = -1, oy = 0, ox = 0;
+      const int blk = mt * L::MSUB + sb;
       if (AMODE == A_ROWS) {
-        m = mt * 128 + row;
+        m = blk * 128 + row;
         if (m >= p.M) m = -1;
       } else {
-        const int ty = (int)p.div_tiles_w.div((uint32_t)mt);
-        const int x0 = (mt - ty * p.tiles_w) * p.TW, y0 = ty * 8;
+        const int ty = (int)p.div_tiles_w.div((uint32_t)blk);
+        const int x0 = (blk - ty * p.tiles_w) * p.TW, y0 = ty * 8;
         oy = y0 + row / p.TW;
         ox = x0 + row % p.TW;
         if (row < a_rows && oy < p.H && ox < p.W) m = oy * p.W + ox;
@@ -449,26 +466,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (p.ksplit > 1) {
         // the slice's raw partial sums, f32
 #pragma unroll 1
-        for (int c0 = part * HALF; c0 < part * HALF + HALF && c0 < BN; c0 += 16) {
+        for (int c0 = part * HALF; c0 < part * HALF + HALF && c0 < ACC_USED; c0 += 16) {
           uint32_t r[16];
           tmem_ld16(taddr + (uint32_t)c0, r);
           tmem_wait_ld();
           if (m < 0) continue;
-          float4* w = reinterpret_cast<float4*>(p.ws + ((size_t)split * p.M + m) * p.ws_n + nt * BN + c0);
+          float4* w = reinterpret_cast<float4*>(p.ws + ((size_t)split * p.M + m) * p.ws_n + nt * BN + (c0 - cb));
 #pragma unroll
           for (int q = 0; q < 4; q++)
             w[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
                                __uint_as_float(r[4 * q + 3]));
         }
       } else if (p.out_mode == OUT_MAP)
-        map_epilogue<BN>(p, bias, taddr, part * HALF, min(part * HALF + HALF, BN), nt, m, ry, rx, nry, nrx);
+        map_epilogue<BN>(p, bias, taddr, part * HALF, min(part * HALF + HALF, ACC_USED), cb, nt, m, ry, rx, nry, nrx);
 #pragma unroll 1
-      for (int c0 = part * HALF; p.ksplit == 1 && p.out_mode != OUT_MAP && c0 < part * HALF + HALF && c0 < BN;
+      for (int c0 = part * HALF; p.ksplit == 1 && p.out_mode != OUT_MAP && c0 < part * HALF + HALF && c0 < ACC_USED;
            c0 += 16) {
         uint32_t r[16];
         tmem_ld16(taddr + (uint32_t)c0, r);
         tmem_wait_ld();
-        const int n0 = nt * BN + c0;
+        const int n0 = nt * BN + (c0 - cb);
         if (m < 0 || n0 >= p.N) continue;
         float v[16];
         if (bias_staged) {
