@@ -98,7 +98,7 @@ void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, Gemm
     }
   }
   if (p.ksplit > 1) {
-    p.ws = static_cast<float*>(dev.scratch((size_t)p.ksplit * p.M * p.ws_n * sizeof(float)));
+    p.ws = static_cast<float*>(dev.scratch((size_t)p.ksplit * p.M * p.ws_n * sizeof(float), s));
     p.tiles = p.tiles_mn * p.ksplit;
   }
   dispatch<AMODE>(dev, pw.bn, pw.kb, map, p, s);

@@ -204,6 +204,9 @@ Lama::Lama(const std::string& path, const Options& opt) : dev_(opt) {
   f.finish();
   step_events_.resize(STEPS);
   for (auto& e : step_events_) IEC_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  IEC_CUDA(cudaStreamCreateWithFlags(&s_local_, cudaStreamNonBlocking));
+  IEC_CUDA(cudaStreamCreateWithFlags(&s_spec_, cudaStreamNonBlocking));
+  for (cudaEvent_t* e : {&ev_in_, &ev_local_, &ev_spec_}) IEC_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
   IEC_CUDA(cudaDeviceSynchronize());
 }
 
@@ -218,6 +221,10 @@ Lama::~Lama() {
   cudaGetDevice(&prev);
   cudaSetDevice(dev_.ordinal());
   for (auto& e : step_events_) cudaEventDestroy(e);
+  for (cudaEvent_t e : {ev_in_, ev_local_, ev_spec_})
+    if (e) cudaEventDestroy(e);
+  for (cudaStream_t st : {s_local_, s_spec_})
+    if (st) cudaStreamDestroy(st);
   if (prev >= 0) cudaSetDevice(prev);
 }
 
@@ -247,17 +254,24 @@ void Lama::ensure(int hp, int wp) {
 
 // network.rs:174-248. `out` = ffc(`in`); with `residual`, `out` (the block's
 // input) gets ffc(`in`) added instead, its global part staged in `tmp`.
+// Three independent chains run on three streams: the local convolution
+// (writes the local planes of `out`), the spectral chain (spectral_in,
+// rfft2, the Fourier 1x1, irfft2: its own buffers) and the cross
+// convolution (the global planes of `out` or `tmp`); spectral_out joins the
+// last two, and `s` waits for all before the next layer.
 void Lama::ffc(const Ffc& F, const __half* in, __half* out, __half* tmp, bool residual, cudaStream_t s) {
   const int h8 = alloc_h_ / 8, w8 = alloc_w_ / 8, half = w8 / 2 + 1;
   const MapGeom g{h8, w8, 1, 1};
   static const std::vector<Tap> taps3 = conv_taps(3);
+  IEC_CUDA(cudaEventRecord(ev_in_, s));
+  IEC_CUDA(cudaStreamWaitEvent(s_local_, ev_in_, 0));
+  IEC_CUDA(cudaStreamWaitEvent(s_spec_, ev_in_, 0));
   // local = relu(conv3(all 512 channels)) [+ out]
   GemmOutSpec o = map_out(g, out, 0);
   if (residual) o.resid = out;
-  gemm_taps(dev_, F.local, g.source(in), taps3, h8, w8, ACT_RELU, o, s);
-  // global = cross(local part) + spectral_out(spectral + irfft2(...)), then ReLU
-  __half* global = residual ? tmp : out;
-  gemm_taps(dev_, F.cross, g.source(in), taps3, h8, w8, ACT_NONE, map_out(g, global, LOCAL / 8), s);
+  gemm_taps(dev_, F.local, g.source(in), taps3, h8, w8, ACT_RELU, o, s_local_);
+  IEC_CUDA(cudaEventRecord(ev_local_, s_local_));
+  // the spectral chain
   const long long spec_plane = (long long)gemm_rows_alloc(h8 * w8) * 8;
   const long long freq_plane = (long long)gemm_rows_alloc(h8 * half) * 8;
   __half* spectral = spectral_.as<__half>();
@@ -266,21 +280,27 @@ void Lama::ffc(const Ffc& F, const __half* in, __half* out, __half* tmp, bool re
     so.mode = OUT_STORE;
     so.out = spectral;
     so.plane_elems = spec_plane;
-    gemm_taps(dev_, F.spectral_in, g.source(in, LOCAL / 8), {{1, 1, 0}}, h8, w8, ACT_RELU, so, s);
+    gemm_taps(dev_, F.spectral_in, g.source(in, LOCAL / 8), {{1, 1, 0}}, h8, w8, ACT_RELU, so, s_spec_);
   }
-  rfft2_planar(plan_, spectral, spec_plane, spectrum_.as<__half>(), freq_plane, s);
+  rfft2_planar(plan_, spectral, spec_plane, spectrum_.as<__half>(), freq_plane, s_spec_);
   {
     GemmOutSpec fo;
     fo.mode = OUT_STORE;
     fo.out = filtered_.as<__half>();
     fo.plane_elems = freq_plane;
-    gemm_rows(dev_, F.fourier, spectrum_.as<__half>(), freq_plane, h8 * half, ACT_RELU, fo, s);
+    gemm_rows(dev_, F.fourier, spectrum_.as<__half>(), freq_plane, h8 * half, ACT_RELU, fo, s_spec_);
   }
-  irfft2_add_planar(plan_, filtered_.as<__half>(), freq_plane, spectral, spec_plane, s);
+  irfft2_add_planar(plan_, filtered_.as<__half>(), freq_plane, spectral, spec_plane, s_spec_);
+  IEC_CUDA(cudaEventRecord(ev_spec_, s_spec_));
+  // global = cross(local part) + spectral_out(spectral + irfft2(...)), then ReLU
+  __half* global = residual ? tmp : out;
+  gemm_taps(dev_, F.cross, g.source(in), taps3, h8, w8, ACT_NONE, map_out(g, global, LOCAL / 8), s);
+  IEC_CUDA(cudaStreamWaitEvent(s, ev_spec_, 0));
   GemmOutSpec go = map_out(g, out, LOCAL / 8);
   go.acc_src = global;
   if (residual) go.resid = out;
   gemm_rows(dev_, F.spectral_out, spectral, spec_plane, h8 * w8, ACT_RELU, go, s);
+  IEC_CUDA(cudaStreamWaitEvent(s, ev_local_, 0));
 }
 
 bool Lama::run(const void* image, bool image_u8, const void* mask, bool mask_u8, void* dst, bool dst_u8, int width,

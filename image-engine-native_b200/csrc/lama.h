@@ -59,6 +59,10 @@ class Lama {
   // device working buffers (planar f16)
   DeviceBuffer in0_, d0_, d1_, d2_, x_, mid_, tmp_, spectral_, spectrum_, filtered_, u0_, u1_, u2_, out_;
   std::vector<cudaEvent_t> step_events_;
+  // Side streams of an FFC: its local convolution and its spectral chain run
+  // beside the cross convolution (each alone fills a fraction of the GPU).
+  cudaStream_t s_local_ = nullptr, s_spec_ = nullptr;
+  cudaEvent_t ev_in_ = nullptr, ev_local_ = nullptr, ev_spec_ = nullptr;
 };
 
 }  // namespace iec

@@ -248,7 +248,7 @@ Device::~Device() {
   // rather than freed under it (as the reference's busy flag does).
   if (poisoned()) {
     dev_err_.leak();
-    scratch_.leak();
+    for (auto& e : scratch_) e.second.leak();
   }
   if (prev >= 0) cudaSetDevice(prev);
 }

@@ -155,11 +155,18 @@ class Device {
   void check_device_errors();
   void poison(const std::string& why) { poisoned_ = why.empty() ? "GPU failure" : why; }
   bool poisoned() const { return !poisoned_.empty(); }
-  // Scratch of at least `bytes` for the work of one launch sequence on the
-  // device's streams (the GEMM's split-K partial sums); grows on demand.
-  void* scratch(size_t bytes) {
-    if (scratch_.size() < bytes) scratch_.reserve(bytes);
-    return scratch_.get();
+  // Scratch of at least `bytes` for the launches queued on `stream` (the
+  // GEMM's split-K partial sums): one buffer per stream, so that work on
+  // concurrent streams never shares it; grows on demand.
+  void* scratch(size_t bytes, cudaStream_t stream) {
+    for (auto& e : scratch_)
+      if (e.first == stream) {
+        if (e.second.size() < bytes) e.second.reserve(bytes);
+        return e.second.get();
+      }
+    scratch_.emplace_back(stream, DeviceBuffer());
+    scratch_.back().second.reserve(bytes);
+    return scratch_.back().second.get();
   }
 
  private:
@@ -171,7 +178,7 @@ class Device {
   cudaStream_t stream_ = nullptr;
   cudaStream_t copy_stream_ = nullptr;
   DeviceBuffer dev_err_;
-  DeviceBuffer scratch_;
+  std::vector<std::pair<cudaStream_t, DeviceBuffer>> scratch_;
   PinnedBuffer host_err_;
   std::string poisoned_;
 };
