@@ -600,12 +600,32 @@ Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
   }
   f.finish();
   sums_.reserve(INTER * sizeof(double));
+  for (cudaStream_t* st : {&s_half_, &s_patch_, &s_aspp_}) IEC_CUDA(cudaStreamCreateWithFlags(st, cudaStreamNonBlocking));
+  for (cudaEvent_t* e : {&ev_prep_, &ev_half_, &ev_t_, &ev_aspp_, &ev_patch_[0], &ev_patch_[1], &ev_patch_[2],
+                         &ev_patch_[3]})
+    IEC_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
   IEC_CUDA(cudaDeviceSynchronize());
 }
 
 Birefnet::~Birefnet() {
+  if (!dev_.poisoned()) {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev_.ordinal());
+    for (cudaEvent_t e : {ev_prep_, ev_half_, ev_t_, ev_aspp_, ev_patch_[0], ev_patch_[1], ev_patch_[2], ev_patch_[3]})
+      if (e) cudaEventDestroy(e);
+    for (cudaStream_t st : {s_half_, s_patch_, s_aspp_})
+      if (st) cudaStreamDestroy(st);
+    if (prev >= 0) cudaSetDevice(prev);
+  }
   if (dev_.poisoned()) {
-    for (DeviceBuffer* b : {&img_, &himg_, &patch_rows_, &x_, &tok_, &qkv_, &att_, &ln_, &hid_, &mrg_, &lev_[0],
+    for (BackboneBuffers& bb : bb_)
+      for (DeviceBuffer* b : {&bb.patch_rows, &bb.x, &bb.tok, &bb.qkv, &bb.att, &bb.ln, &bb.hid, &bb.mrg}) b->leak();
+    for (int i = 0; i < 3; i++) {
+      offs_b_[i].leak();
+      samp_b_[i].leak();
+    }
+    for (DeviceBuffer* b : {&img_, &himg_, &lev_[0],
                             &lev_[1], &lev_[2], &hf_[0], &hf_[1], &hf_[2], &hf_[3], &x4_, &in_[0], &in_[1], &in_[2],
                             &in_[3], &outb_[0], &outb_[1], &outb_[2], &out1_, &t_, &t2_, &offs_, &samp_, &cat_, &g16_,
                             &sums_, &low_, &stack_, &pmid_, &host_in, &host_out})
@@ -619,25 +639,8 @@ void Birefnet::ensure(int side) {
   auto bytes = [](long long planes, long long elems) { return (size_t)(planes * elems * 2); };
   img_.reserve((size_t)side * side * 3 * 4);
   himg_.reserve((size_t)(side / 2) * (side / 2) * 3 * 4);
-  patch_rows_.reserve(bytes(6, pe(P0)));
-  size_t bx = 0, btok = 0, bqkv = 0, bln = 0, bhid = 0, bmrg = 0;
-  long long g = g0;
-  for (int s = 0; s < 4; s++, g /= 2) {
-    const long long c = STAGE_C[s], tokens = g * g, pad = (g + WS - 1) / WS * WS, slots = (pad / WS) * (pad / WS) * 64;
-    bx = std::max(bx, bytes(c / 8, pe(tokens)));
-    btok = std::max(btok, bytes(c / 8, pe(slots)));
-    bqkv = std::max(bqkv, bytes(3 * c / 8, pe(slots)));
-    bln = std::max(bln, bytes(c / 8, pe(tokens)));
-    bhid = std::max(bhid, bytes(4 * c / 8, pe(tokens)));
-    if (s < 3) bmrg = std::max(bmrg, bytes(4 * c / 8, pe(tokens / 4)));
-  }
-  x_.reserve(bx);
-  tok_.reserve(btok);
-  att_.reserve(btok);
-  qkv_.reserve(bqkv);
-  ln_.reserve(bln);
-  hid_.reserve(bhid);
-  mrg_.reserve(bmrg);
+  ensure_backbone(bb_[0], side);
+  ensure_backbone(bb_[1], side / 2);
   for (int i = 0; i < 3; i++) {
     const long long gi = g0 >> i;
     lev_[i].reserve(bytes(2 * STAGE_C[i] / 8, pe(gi * gi)));
@@ -662,6 +665,10 @@ void Birefnet::ensure(int side) {
   t2_.reserve(bytes(8, pe(P0)));
   offs_.reserve(bytes(19, pe(P0)));
   samp_.reserve(bytes(49 * 8, pe(P0)));
+  for (int i = 0; i < 3; i++) {
+    offs_b_[i].reserve(bytes(19, pe(P0)));
+    samp_b_[i].reserve(bytes(SIZES[i] * SIZES[i] * 8, pe(P0)));
+  }
   cat_.reserve(bytes(128, pe(P0)));
   g16_.reserve(bytes(2, pe(P0)));
   low_.reserve((size_t)P0 * 4);
@@ -675,20 +682,44 @@ void Birefnet::ensure(int side) {
   alloc_side_ = side;
 }
 
+void Birefnet::ensure_backbone(BackboneBuffers& bb, int side) {
+  const long long g0 = side / 4, P0 = g0 * g0;
+  auto bytes = [](long long planes, long long elems) { return (size_t)(planes * elems * 2); };
+  bb.patch_rows.reserve(bytes(6, pe(P0)));
+  size_t bx = 0, btok = 0, bqkv = 0, bln = 0, bhid = 0, bmrg = 0;
+  long long g = g0;
+  for (int s = 0; s < 4; s++, g /= 2) {
+    const long long c = STAGE_C[s], tokens = g * g, pad = (g + WS - 1) / WS * WS, slots = (pad / WS) * (pad / WS) * 64;
+    bx = std::max(bx, bytes(c / 8, pe(tokens)));
+    btok = std::max(btok, bytes(c / 8, pe(slots)));
+    bqkv = std::max(bqkv, bytes(3 * c / 8, pe(slots)));
+    bln = std::max(bln, bytes(c / 8, pe(tokens)));
+    bhid = std::max(bhid, bytes(4 * c / 8, pe(tokens)));
+    if (s < 3) bmrg = std::max(bmrg, bytes(4 * c / 8, pe(tokens / 4)));
+  }
+  bb.x.reserve(bx);
+  bb.tok.reserve(btok);
+  bb.att.reserve(btok);
+  bb.qkv.reserve(bqkv);
+  bb.ln.reserve(bln);
+  bb.hid.reserve(bhid);
+  bb.mrg.reserve(bmrg);
+}
+
 void Birefnet::backbone(const float* img, int side, __half* const dst[4], const long long dst_plane[4],
-                        const int plane0[4], cudaStream_t s) {
+                        const int plane0[4], BackboneBuffers& bb, cudaStream_t s) {
   const int sms = dev_.sms();
   int grid = side / 4;
   long long tokens = (long long)grid * grid;
-  launch_pdl(bir_embed_gather, blocks_for(tokens * 6, sms), 256, 0, s, img, side, patch_rows_.as<__half>(), pe(tokens));
+  launch_pdl(bir_embed_gather, blocks_for(tokens * 6, sms), 256, 0, s, img, side, bb.patch_rows.as<__half>(), pe(tokens));
   IEC_CUDA(cudaGetLastError());
-  __half* x = x_.as<__half>();
+  __half* x = bb.x.as<__half>();
   {
     GemmOutSpec o;
     o.mode = OUT_STORE;
     o.out = x;
     o.plane_elems = pe(tokens);
-    gemm_rows(dev_, embed_, patch_rows_.as<__half>(), pe(tokens), (int)tokens, ACT_NONE, o, s);
+    gemm_rows(dev_, embed_, bb.patch_rows.as<__half>(), pe(tokens), (int)tokens, ACT_NONE, o, s);
     layer_norm_planar(x, pe(tokens), 0, (int)tokens, 96, embed_g_.as<float>(), embed_b_.as<float>(), x, pe(tokens),
                       nullptr, s);
   }
@@ -702,14 +733,14 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
       const int shift = B.shifted ? SHIFT : 0;
       // attention: x += proj(attn(window(LN1(x))))
       const WindowMap wm{WS, pad, pad, grid, grid, shift};
-      layer_norm_planar(x, xp, 0, (int)slots, c, B.n1g.as<float>(), B.n1b.as<float>(), tok_.as<__half>(), sp, &wm, s);
+      layer_norm_planar(x, xp, 0, (int)slots, c, B.n1g.as<float>(), B.n1b.as<float>(), bb.tok.as<__half>(), sp, &wm, s);
       GemmOutSpec o;
       o.mode = OUT_STORE;
-      o.out = qkv_.as<__half>();
+      o.out = bb.qkv.as<__half>();
       o.plane_elems = sp;
-      gemm_rows(dev_, B.qkv, tok_.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
-      window_attention(qkv_.as<__half>(), sp, c, (int)(slots / 64), B.bias.as<float>(), B.shifted, wins, wins,
-                       att_.as<__half>(), sp, s);
+      gemm_rows(dev_, B.qkv, bb.tok.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
+      window_attention(bb.qkv.as<__half>(), sp, c, (int)(slots / 64), B.bias.as<float>(), B.shifted, wins, wins,
+                       bb.att.as<__half>(), sp, s);
       o.mode = OUT_WINDOW_ACCUM;
       o.out = x;
       o.plane_elems = xp;
@@ -719,32 +750,32 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
       o.win_ws = WS;
       o.pad_h = pad;
       o.pad_w = pad;
-      gemm_rows(dev_, B.proj, att_.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
+      gemm_rows(dev_, B.proj, bb.att.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
       // MLP: x += fc2(GELU(fc1(LN2(x))))
-      layer_norm_planar(x, xp, 0, (int)tokens, c, B.n2g.as<float>(), B.n2b.as<float>(), ln_.as<__half>(), xp, nullptr,
+      layer_norm_planar(x, xp, 0, (int)tokens, c, B.n2g.as<float>(), B.n2b.as<float>(), bb.ln.as<__half>(), xp, nullptr,
                         s);
       GemmOutSpec h;
       h.mode = OUT_STORE;
-      h.out = hid_.as<__half>();
+      h.out = bb.hid.as<__half>();
       h.plane_elems = xp;
-      gemm_rows(dev_, B.fc1, ln_.as<__half>(), xp, (int)tokens, ACT_GELU, h, s);
+      gemm_rows(dev_, B.fc1, bb.ln.as<__half>(), xp, (int)tokens, ACT_GELU, h, s);
       GemmOutSpec a;
       a.mode = OUT_ACCUM;
       a.out = x;
       a.plane_elems = xp;
-      gemm_rows(dev_, B.fc2, hid_.as<__half>(), xp, (int)tokens, ACT_NONE, a, s);
+      gemm_rows(dev_, B.fc2, bb.hid.as<__half>(), xp, (int)tokens, ACT_NONE, a, s);
     }
     // the stage's normalised output
     layer_norm_planar(x, xp, 0, (int)tokens, c, st.ng.as<float>(), st.nb.as<float>(),
                       dst[si] + (long long)plane0[si] * dst_plane[si], dst_plane[si], nullptr, s);
     if (st.has_merge) {
       const long long mt = tokens / 4, mp = pe(mt);
-      merge_layer_norm_planar(x, xp, grid, c, st.mg.as<float>(), st.mb.as<float>(), mrg_.as<__half>(), mp, s);
+      merge_layer_norm_planar(x, xp, grid, c, st.mg.as<float>(), st.mb.as<float>(), bb.mrg.as<__half>(), mp, s);
       GemmOutSpec o;
       o.mode = OUT_STORE;
       o.out = x;
       o.plane_elems = mp;
-      gemm_rows(dev_, st.merge, mrg_.as<__half>(), mp, (int)mt, ACT_NONE, o, s);
+      gemm_rows(dev_, st.merge, bb.mrg.as<__half>(), mp, (int)mt, ACT_NONE, o, s);
       grid /= 2;
       tokens = mt;
     }
@@ -774,26 +805,34 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
   launch_pdl(bir_aspp_bias, 1, 256, 0, s, sums_.as<double>(), (double)P, b.pool_w.as<float>(), b.pool_b.as<float>(),
                                   b.conv1_pool.as<float>(), b.conv1_bias.as<float>(), b.conv1.bias.as<float>());
   IEC_CUDA(cudaGetLastError());
+  // Branches 0-2 on the side stream (their own offset and sample buffers),
+  // beside the 7x7 branch; each writes its 256 planes of `cat`.
+  IEC_CUDA(cudaEventRecord(ev_t_, s));
+  IEC_CUDA(cudaStreamWaitEvent(s_aspp_, ev_t_, 0));
   for (int i = 0; i < 4; i++) {
     const int k = SIZES[i], taps = k * k;
+    cudaStream_t bs = i < 3 ? s_aspp_ : s;
+    __half* offs = i < 3 ? offs_b_[i].as<__half>() : offs_.as<__half>();
+    __half* samp = i < 3 ? samp_b_[i].as<__half>() : samp_.as<__half>();
     std::vector<Tap> tl;
     for (int ky = 0; ky < k; ky++)
       for (int kx = 0; kx < k; kx++) tl.push_back({ky - k / 2, kx - k / 2, 0});
     GemmOutSpec o;
     o.mode = OUT_STORE;
-    o.out = offs_.as<__half>();
+    o.out = offs;
     o.plane_elems = pp;
-    gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, s);
-    launch_pdl(bir_deform_sample, blocks_for(P * taps * 8, sms), 256, 0, s, t, pp, g, g, k, offs_.as<__half>(), pp,
-                                                                samp_.as<__half>(), pp);
+    gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, bs);
+    launch_pdl(bir_deform_sample, blocks_for(P * taps * 8, sms), 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
     IEC_CUDA(cudaGetLastError());
     GemmOutSpec c;
     c.mode = OUT_STORE;
     c.out = cat_.as<__half>();
     c.plane_elems = pp;
     c.plane0 = i * (BRANCH / 8);
-    gemm_rows(dev_, b.branch[i], samp_.as<__half>(), pp, (int)P, ACT_RELU, c, s);
+    gemm_rows(dev_, b.branch[i], samp, pp, (int)P, ACT_RELU, c, bs);
+    if (i == 2) IEC_CUDA(cudaEventRecord(ev_aspp_, s_aspp_));
   }
+  IEC_CUDA(cudaStreamWaitEvent(s, ev_aspp_, 0));
   __half* t2 = t2_.as<__half>();
   {
     GemmOutSpec o;
@@ -836,22 +875,51 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
   IEC_CUDA(cudaGetLastError());
 
   const int g0 = side / 4, g[4] = {g0, g0 / 2, g0 / 4, g0 / 8};
-  // Full-size features straight into their levels (level 3 into x4, after
-  // the three resized levels' 168 planes); half-size ones into hf.
-  {
-    __half* dst[4] = {lev_[0].as<__half>(), lev_[1].as<__half>(), lev_[2].as<__half>(), x4_.as<__half>()};
-    const long long dp[4] = {pe((long long)g[0] * g[0]), pe((long long)g[1] * g[1]), pe((long long)g[2] * g[2]),
-                             pe((long long)g[3] * g[3])};
-    const int p0[4] = {0, 0, 0, 168};
-    backbone(img, side, dst, dp, p0, s);
+  const int main_c[4] = {1536, 768, 384, 192};
+  // Three concurrent chains from here: the image patches of the four levels
+  // (they read only the image; each writes its level's input planes after
+  // the main ones), the half-size backbone pass, and the full-size pass.
+  IEC_CUDA(cudaEventRecord(ev_prep_, s));
+  IEC_CUDA(cudaStreamWaitEvent(s_patch_, ev_prep_, 0));
+  IEC_CUDA(cudaStreamWaitEvent(s_half_, ev_prep_, 0));
+  for (int i = 0; i < 4; i++) {
+    const int level = 3 - i, gi = g[level];
+    const Patches& pt = *patches_[i];
+    const int groups = pad64(PATCH_C[i]) / 8;  // zero channels past the stack's
+    const long long sp = pe((long long)gi * gi), ip = pe((long long)gi * gi);
+    launch_pdl(bir_patches, blocks_for((long long)gi * gi * groups, sms), 256, 0, s_patch_, img, side, gi,
+               stack_.as<__half>(), sp, groups);
+    IEC_CUDA(cudaGetLastError());
+    GemmOutSpec o;
+    o.mode = OUT_STORE;
+    o.out = pmid_.as<__half>();
+    o.plane_elems = sp;
+    gemm_conv3(dev_, pt.conv1, stack_.as<__half>(), sp, gi, gi, ACT_NONE, o, s_patch_);
+    o.out = in_[i].as<__half>();
+    o.plane_elems = ip;
+    o.plane0 = main_c[i] / 8;
+    gemm_conv3(dev_, pt.conv_out, pmid_.as<__half>(), sp, gi, gi, ACT_NONE, o, s_patch_);
+    IEC_CUDA(cudaEventRecord(ev_patch_[i], s_patch_));
   }
+  // Half-size features into hf (side stream); full-size features straight
+  // into their levels (level 3 into x4, after the three resized levels' 168
+  // planes).
   {
     __half* dst[4] = {hf_[0].as<__half>(), hf_[1].as<__half>(), hf_[2].as<__half>(), hf_[3].as<__half>()};
     long long dp[4];
     for (int i = 0; i < 4; i++) dp[i] = pe((long long)(g[i] / 2) * (g[i] / 2));
     const int p0[4] = {0, 0, 0, 0};
-    backbone(himg_.as<float>(), hs, dst, dp, p0, s);
+    backbone(himg_.as<float>(), hs, dst, dp, p0, bb_[1], s_half_);
+    IEC_CUDA(cudaEventRecord(ev_half_, s_half_));
   }
+  {
+    __half* dst[4] = {lev_[0].as<__half>(), lev_[1].as<__half>(), lev_[2].as<__half>(), x4_.as<__half>()};
+    const long long dp[4] = {pe((long long)g[0] * g[0]), pe((long long)g[1] * g[1]), pe((long long)g[2] * g[2]),
+                             pe((long long)g[3] * g[3])};
+    const int p0[4] = {0, 0, 0, 168};
+    backbone(img, side, dst, dp, p0, bb_[0], s);
+  }
+  IEC_CUDA(cudaStreamWaitEvent(s, ev_half_, 0));
   // Each level's second half: the half-size run resized to the level's grid.
   for (int i = 0; i < 4; i++) {
     const int c8 = STAGE_C[i] / 8, hg = g[i] / 2;
@@ -878,7 +946,6 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
   // squeeze -> block 4's input planes 0..191
   block(*squeeze_, x4_.as<__half>(), pe((long long)g[3] * g[3]), 2880, g[3], in_[0].as<__half>(),
         pe((long long)g[3] * g[3]), 0, s);
-  const int main_c[4] = {1536, 768, 384, 192};
   for (int i = 0; i < 4; i++) {
     const int level = 3 - i, gi = g[level], cin = LEVELS[i][0];
     const long long ip = pe((long long)gi * gi);
@@ -896,24 +963,8 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
           prev, pe((long long)pg * pg), pg, pg, in, ip, gi, gi, main_c[i] / 8, 1);
       IEC_CUDA(cudaGetLastError());
     }
-    // patches of the image, through two convolutions, after the main planes
-    {
-      const Patches& pt = *patches_[i];
-      const int groups = pad64(PATCH_C[i]) / 8;  // zero channels past the stack's
-      const long long sp = pe((long long)gi * gi);
-      launch_pdl(bir_patches, blocks_for((long long)gi * gi * groups, sms), 256, 0, s, img, side, gi, stack_.as<__half>(), sp,
-                                                                                groups);
-      IEC_CUDA(cudaGetLastError());
-      GemmOutSpec o;
-      o.mode = OUT_STORE;
-      o.out = pmid_.as<__half>();
-      o.plane_elems = sp;
-      gemm_conv3(dev_, pt.conv1, stack_.as<__half>(), sp, gi, gi, ACT_NONE, o, s);
-      o.out = in;
-      o.plane_elems = ip;
-      o.plane0 = main_c[i] / 8;
-      gemm_conv3(dev_, pt.conv_out, pmid_.as<__half>(), sp, gi, gi, ACT_NONE, o, s);
-    }
+    // the level's image patches, through two convolutions (side stream)
+    IEC_CUDA(cudaStreamWaitEvent(s, ev_patch_[i], 0));
     __half* out = i < 3 ? outb_[i].as<__half>() : out1_.as<__half>();
     block(*blocks_[i], in, ip, cin, gi, out, ip, 0, s);
   }

@@ -43,11 +43,16 @@ class Birefnet {
 
  private:
   void ensure(int side);
+  // The backbone's working buffers (one set per concurrent pass).
+  struct BackboneBuffers {
+    DeviceBuffer patch_rows, x, tok, qkv, att, ln, hid, mrg;
+  };
+  void ensure_backbone(BackboneBuffers& b, int side);
   // swin.rs:162-215 on `img` (f32 NHWC, side x side); stage i's normalised
   // output goes to planes from plane0[i] of dst[i] (dst_plane[i] elements per
   // plane).
   void backbone(const float* img, int side, __half* const dst[4], const long long dst_plane[4], const int plane0[4],
-                cudaStream_t s);
+                BackboneBuffers& bb, cudaStream_t s);
   // decoder.rs:343-406: `x` (cin channels, g x g) -> out planes from `plane0`
   // of `out` (cout channels).
   void block(const DBlock& b, const __half* x, long long x_plane, int cin, int g, __half* out, long long out_plane,
@@ -65,9 +70,15 @@ class Birefnet {
   float head_b_ = 0.0f;
   int alloc_side_ = 0;
   // working buffers
-  DeviceBuffer img_, himg_, patch_rows_, x_, tok_, qkv_, att_, ln_, hid_, mrg_;
+  DeviceBuffer img_, himg_;
+  BackboneBuffers bb_[2];  // the full-size pass, the half-size pass
   DeviceBuffer lev_[3], hf_[4], x4_, in_[4], outb_[3], out1_, t_, t2_, offs_, samp_, cat_, g16_, sums_, low_, stack_,
       pmid_;
+  DeviceBuffer offs_b_[3], samp_b_[3];  // ASPP branches 0-2, beside branch 3
+  // Side streams: the half-size backbone pass, the image-patch branches of
+  // the four levels, and the ASPP's small branches.
+  cudaStream_t s_half_ = nullptr, s_patch_ = nullptr, s_aspp_ = nullptr;
+  cudaEvent_t ev_prep_ = nullptr, ev_half_ = nullptr, ev_t_ = nullptr, ev_aspp_ = nullptr, ev_patch_[4] = {};
 };
 
 }  // namespace iec

@@ -217,6 +217,9 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
   f.finish();
   step_events_.resize(STEPS);
   for (auto& e : step_events_) IEC_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  IEC_CUDA(cudaStreamCreateWithFlags(&s_conv_, cudaStreamNonBlocking));
+  IEC_CUDA(cudaEventCreateWithFlags(&ev_in_, cudaEventDisableTiming));
+  IEC_CUDA(cudaEventCreateWithFlags(&ev_conv_, cudaEventDisableTiming));
   IEC_CUDA(cudaDeviceSynchronize());
 }
 
@@ -231,6 +234,9 @@ Scunet::~Scunet() {
   cudaGetDevice(&prev);
   cudaSetDevice(dev_.ordinal());
   for (auto& e : step_events_) cudaEventDestroy(e);
+  for (cudaEvent_t e : {ev_in_, ev_conv_})
+    if (e) cudaEventDestroy(e);
+  if (s_conv_) cudaStreamDestroy(s_conv_);
   if (prev >= 0) cudaSetDevice(prev);
 }
 
@@ -321,15 +327,22 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
     for (int b = 0; b < BLOCKS && !cancelled; b++) {
       Block& B = L.blocks[b];
       const int shift = B.shifted ? SHIFT : 0;
-      // Convolution half (network.rs:136-153): t = relu(conv(y[:h])); y[:h] += conv(t).
-      o.mode = OUT_STORE;
-      o.out = t;
-      o.plane0 = 0;
-      gemm_conv3(dev_, B.conv1, y, pl, H, W, ACT_RELU, o, s);
-      o.mode = OUT_ACCUM;
-      o.out = y;
-      o.plane0 = 0;
-      gemm_conv3(dev_, B.conv2, t, pl, H, W, ACT_NONE, o, s);
+      // Convolution half (network.rs:136-153): t = relu(conv(y[:h])); y[:h] += conv(t),
+      // on the side stream: it touches only y's first h channels and t, the
+      // attention half below only y's last h channels and its own buffers.
+      IEC_CUDA(cudaEventRecord(ev_in_, s));
+      IEC_CUDA(cudaStreamWaitEvent(s_conv_, ev_in_, 0));
+      {
+        GemmOutSpec c;
+        c.plane_elems = pl;
+        c.mode = OUT_STORE;
+        c.out = t;
+        gemm_conv3(dev_, B.conv1, y, pl, H, W, ACT_RELU, c, s_conv_);
+        c.mode = OUT_ACCUM;
+        c.out = y;
+        gemm_conv3(dev_, B.conv2, t, pl, H, W, ACT_NONE, c, s_conv_);
+      }
+      IEC_CUDA(cudaEventRecord(ev_conv_, s_conv_));
       // Attention (swin.rs:124-220) on y[h:]: LN1 + window partition, qkv,
       // attention, projection added back at the tokens' pixels.
       const WindowMap wm{8, H, W, H, W, shift};
@@ -357,6 +370,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       o.plane0 = h / 8;
       gemm_rows(dev_, B.fc2, hid, pl, Pl, ACT_NONE, o, s);
       // x += join(y); y = next split(x) (network.rs:190-212).
+      IEC_CUDA(cudaStreamWaitEvent(s, ev_conv_, 0));
       o.mode = OUT_ACCUM;
       o.out = x;
       o.plane0 = 0;

@@ -56,6 +56,10 @@ class Scunet {
   // device working buffers (planar f16)
   DeviceBuffer img_, x_, y_, t_, tok_, qkv_, att_, ln2_, hid_, gat_, skip_[3], out_;
   std::vector<cudaEvent_t> step_events_;
+  // Side stream of a block's convolution half, which runs beside its
+  // attention half.
+  cudaStream_t s_conv_ = nullptr;
+  cudaEvent_t ev_in_ = nullptr, ev_conv_ = nullptr;
 };
 
 }  // namespace iec
