@@ -55,10 +55,11 @@ def peaks():
         return FALLBACK_PEAKS, "fallback"
 
 
-def traffic_per_px():
-    """DRAM bytes per output pixel of the 64->64 conv from the committed ncu
-    summary (profiles/conv3x3_64x64_realesrgan.txt), or None."""
-    path = os.path.join(ROOT, "profiles", "conv3x3_64x64_realesrgan.txt")
+def traffic_per_px(name="conv3x3_64x64_realesrgan.txt"):
+    """DRAM bytes per output pixel of one 64->64 layer from a committed ncu
+    summary under profiles/ (the per-layer kernel's, or the fused body's), or
+    None."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         with open(path) as f:
             for line in f:
@@ -423,7 +424,16 @@ def main():
     elapsed = max_over_ranks(start.elapsed_time(end) / 1e3)
     kinds, ms = model.timing(args.steps * launches_per_step * 2 + 64)
     model.set_timing(0)
-    conv_ms = float(ms[kinds == 2].mean()) if (kinds == 2).any() else None
+    # The dominant kernel: the fused 32-layer body launch (kind 4) where the
+    # passes take it, else the per-layer 64->64 convolution (kind 2).
+    if (kinds == 4).any():
+        conv_ms, conv_layers = float(ms[kinds == 4].mean()), 32
+        conv_kernel = "conv3x3_body_sm100 (the 32 64->64 PReLU layers, one persistent launch)"
+        conv_profile = "conv3x3_body_realesrgan.txt"
+    else:
+        conv_ms, conv_layers = (float(ms[kinds == 2].mean()) if (kinds == 2).any() else None), 1
+        conv_kernel = "conv3x3_sm100<64,64,PRELU>"
+        conv_profile = "conv3x3_64x64_realesrgan.txt"
     step_s = elapsed / args.steps
     value = batch * OUT_MP / step_s
 
@@ -519,8 +529,9 @@ def main():
         pk, src = peaks()
         peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
         px_per_launch = args.chunk * WIDTH * HEIGHT
-        achieved = CONV64_FLOP_PER_PX * px_per_launch / (conv_ms / 1e3) / 1e12 if conv_ms else None
-        tpp = traffic_per_px()
+        flop_per_launch = CONV64_FLOP_PER_PX * px_per_launch * conv_layers
+        achieved = flop_per_launch / (conv_ms / 1e3) / 1e12 if conv_ms else None
+        tpp = traffic_per_px(conv_profile)
         clocks = clk.summary()
         line = {
             "metric": "output megapixels/s", "value": value, "unit": "MP/s", "n_gpus": world,
@@ -529,12 +540,13 @@ def main():
             "data": "synthetic (seeded uniform images, seeded He-normal weights)",
             "config": config(args, args.chunk),
             "e2e": e2e,
-            "roofline": {"kernel": "conv3x3_sm100<64,64,PRELU>", "bound": "tensor", "achieved": achieved,
+            "roofline": {"kernel": conv_kernel, "bound": "tensor", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if achieved else None,
                          "peak_source": f"{src} bf16 dense (sustained; f16 rate is the same)",
-                         "mean_launch_ms": conv_ms, "flop_per_launch": CONV64_FLOP_PER_PX * px_per_launch,
-                         "traffic": tpp * px_per_launch if tpp else None,
-                         "algorithmic_bytes_per_launch": px_per_launch * 64 * 2 * 2},
+                         "mean_launch_ms": conv_ms, "layers_per_launch": conv_layers,
+                         "flop_per_launch": flop_per_launch,
+                         "traffic": tpp * px_per_launch * conv_layers if tpp else None,
+                         "algorithmic_bytes_per_launch": px_per_launch * 64 * 2 * 2 * conv_layers},
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps * world,
             "clocks": clocks,

@@ -518,6 +518,13 @@ iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity) {
   });
 }
 
+iec_status iec_realesrgan_set_fused(iec_realesrgan* model, int on) {
+  return guard([&] {
+    need_model(model);
+    model->model->set_fused(on != 0);
+  });
+}
+
 size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n) {
   size_t written = 0;
   iec_status st = guard([&] {

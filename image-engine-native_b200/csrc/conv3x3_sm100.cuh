@@ -127,6 +127,11 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   float* s_slope = s_bias + COUT;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Programmatic dependent launch: the next layer's CTAs may take each SM as
+  // this grid's CTA there exits, and run their prologue (barriers, TMEM,
+  // weights) while the other SMs finish. One CTA fills an SM's shared memory,
+  // so they never share one.
+  griddep_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < CONV_NSTAGE; s++) {
@@ -163,6 +168,10 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         int bytes = L::W_BYTES - off < 32768 ? L::W_BYTES - off : 32768;
         bulk_load(w_smem + off, reinterpret_cast<const uint8_t*>(p.weights) + off, bytes, wbar);
       }
+      // The previous layer wrote this layer's input and reads its output
+      // buffer: nothing of either is touched before it has completed (the
+      // epilogue's stores follow these loads).
+      griddep_wait();
       int s = 0;
       uint32_t phase = 0;
       int issued[CONV_NSTAGE];  // parity of the last load into each stage, -1 none

@@ -10,6 +10,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "conv3x3_body_sm100.cuh"
 #include "conv3x3_sm100.cuh"
 
 namespace iec {
@@ -19,7 +20,12 @@ namespace iec {
 // f16 channel-group planes: group 0 holds R, G, B and five zeros, group 1
 // zeros (the first convolution runs with 16 input channels).
 __global__ void realesrgan_prep(const void* __restrict__ src, int src_u8, int src_w, int src_h, int rx0, int ry0,
-                                int rw, int rh, int mw, int mh, int count, __half* __restrict__ dst) {
+                                int rw, int rh, int mw, int mh, int count, __half* __restrict__ dst,
+                                int* __restrict__ rows, int nrows) {
+  griddep_wait();
+  griddep_launch_dependents();
+  // The fused body's row counters start at zero (it runs two launches on).
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nrows; i += gridDim.x * blockDim.x) rows[i] = 0;
   const size_t total = (size_t)count * rw * rh;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t per = (size_t)rw * rh;
@@ -72,8 +78,7 @@ void launch_conv(Device& dev, const void* in_maps, int count, int mw, int mh, Co
     bytes = optin;
   }
   const int grid = std::min(p.tiles, dev.sms());
-  kernel<<<grid, CONV_THREADS, bytes, s>>>(map, p);
-  IEC_CUDA(cudaGetLastError());
+  launch_pdl(kernel, grid, CONV_THREADS, (size_t)bytes, s, map, p);
 }
 
 }  // namespace
@@ -142,7 +147,7 @@ RealEsrgan::~RealEsrgan() {
       L.b.leak();
       L.s.leak();
     }
-    for (DeviceBuffer* b : {&prep_, &map_a_, &map_b_, &host_in, &host_out, &batch_in_[0], &batch_in_[1],
+    for (DeviceBuffer* b : {&prep_, &map_a_, &map_b_, &rows_, &items_, &host_in, &host_out, &batch_in_[0], &batch_in_[1],
                             &batch_out_[0], &batch_out_[1]})
       b->leak();
     return;
@@ -212,16 +217,133 @@ size_t RealEsrgan::timing(int* kinds, float* ms, size_t n) {
   return w;
 }
 
+bool RealEsrgan::body_fits(int count, int w, int h) const {
+  const long long tiles_img = (long long)((w + CONV_TILE_W - 1) / CONV_TILE_W) * ((h + CONV_TILE_H - 1) / CONV_TILE_H);
+  const long long group = std::min(count, BODY_GROUP);
+  const long long layers = STEPS - 2;
+  const long long items = layers * count * tiles_img, group_items = layers * group * tiles_img;
+  const long long group_tiles = group * tiles_img, tiles_x = (w + CONV_TILE_W - 1) / CONV_TILE_W;
+  // FastDiv's exactness (numerator x divisor < 2^40) for every division of
+  // an item index (body_item), and a fused launch that never runs short of
+  // work.
+  const long long lim = 1LL << 40;
+  const long long tiles_y = (h + CONV_TILE_H - 1) / CONV_TILE_H;
+  return !no_fuse_ && items < (1LL << 24) && items * group_items < lim && group_items * group_tiles < lim &&
+         group_tiles * tiles_img < lim && tiles_img * tiles_x < lim && items >= 4LL * dev_.sms() &&
+         count <= 256 && tiles_y <= 1024 && tiles_x <= 512;  // body_pack's fields
+}
+
+void RealEsrgan::launch_body(int count, int mw, int mh, const Region& r, cudaStream_t s) {
+  BodyParams bp{};
+  bp.H = r.rh;
+  bp.W = r.rw;
+  bp.MH = mh;
+  bp.MW = mw;
+  bp.tiles_x = (r.rw + CONV_TILE_W - 1) / CONV_TILE_W;
+  bp.tiles_y = (r.rh + CONV_TILE_H - 1) / CONV_TILE_H;
+  bp.tiles_img = bp.tiles_x * bp.tiles_y;
+  bp.count = count;
+  bp.layers = STEPS - 2;
+  bp.group = std::min(count, BODY_GROUP);
+  const int groups = (count + bp.group - 1) / bp.group;
+  const int last_images = count - (groups - 1) * bp.group;
+  bp.items = bp.layers * count * bp.tiles_img;
+  bp.group_items = bp.layers * bp.group * bp.tiles_img;
+  bp.last_group = groups - 1;
+  bp.div_tiles_x = FastDiv((uint32_t)bp.tiles_x);
+  bp.div_tiles_img = FastDiv((uint32_t)bp.tiles_img);
+  bp.div_group_items = FastDiv((uint32_t)bp.group_items);
+  bp.div_group_tiles = FastDiv((uint32_t)(bp.group * bp.tiles_img));
+  bp.div_last_tiles = FastDiv((uint32_t)(last_images * bp.tiles_img));
+  static_assert(STEPS - 2 <= BODY_MAX_LAYERS, "body layers");
+  for (int l = 0; l < bp.layers; l++) {
+    const Layer& L = layers_[l + 1];
+    bp.weights[l] = L.w.as<uint16_t>();
+    bp.bias[l] = L.b.as<float>();
+    bp.slope[l] = L.s.as<float>();
+    if (L.slope_unit) bp.slope_unit |= 1u << l;
+  }
+  bp.maps[0] = map_a_.as<__half>();
+  bp.maps[1] = map_b_.as<__half>();
+  bp.rows = rows_.as<int>();
+  // The item table (body_item of every index, packed), built once per shape.
+  const std::array<int, 3> key = {count, r.rw, r.rh};
+  if (key != items_key_) {
+    std::vector<uint32_t> words((size_t)bp.items);
+    for (int k = 0; k < bp.items; k++) {
+      const int grp = std::min(k / bp.group_items, bp.last_group);
+      const int rem = k - grp * bp.group_items;
+      const int per_layer = (grp == bp.last_group ? last_images : bp.group) * bp.tiles_img;
+      const int l = rem / per_layer, t = rem - l * per_layer;
+      const int gi = t / bp.tiles_img, tt = t - gi * bp.tiles_img;
+      words[(size_t)k] = body_pack(l, grp * bp.group + gi, tt / bp.tiles_x, tt % bp.tiles_x);
+    }
+    items_.reserve(words.size() * 4);
+    IEC_CUDA(cudaMemcpyAsync(items_.get(), words.data(), words.size() * 4, cudaMemcpyHostToDevice, s));
+    IEC_CUDA(cudaStreamSynchronize(s));
+    items_key_ = key;
+  }
+  bp.item_words = items_.as<uint32_t>();
+  bp.dev_err = dev_.dev_err();
+  CUtensorMap maps[2];
+  for (int m = 0; m < 2; m++) {
+    const uint64_t dims[4] = {(uint64_t)mw * 8, (uint64_t)mh, 8, (uint64_t)count};
+    const uint64_t plane = (uint64_t)mw * mh * 16;
+    const uint64_t strides[3] = {(uint64_t)mw * 16, plane, plane * 8};
+    const uint32_t box[4] = {CONV_HALO_W * 8, CONV_HALO_H, 8, 1};
+    encode_tensor_map(&maps[m], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, bp.maps[m], dims, strides, box);
+  }
+  auto kernel = conv3x3_body_sm100;
+  static int smem_bytes[64] = {};
+  int& bytes = smem_bytes[dev_.ordinal() & 63];
+  if (bytes == 0) {
+    int optin = 0;
+    IEC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev_.ordinal()));
+    if (optin < BodySmem::DYN_BYTES) throw Error(ERR_GPU, "not enough shared memory per block");
+    IEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+    bytes = optin;
+  }
+  // Every CTA resident at once (the dataflow waits need it): a cooperative
+  // launch, one CTA per SM.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min(bp.items, dev_.sms()));
+  cfg.blockDim = dim3(BODY_THREADS);
+  cfg.dynamicSmemBytes = (size_t)bytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = body_pdl_ ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], bp);
+  if (e != cudaSuccess && body_pdl_) {
+    // A driver that refuses the two attributes together gets the
+    // cooperative launch alone.
+    (void)cudaGetLastError();
+    body_pdl_ = false;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], bp);
+  }
+  IEC_CUDA(e);
+}
+
 bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u8, int count, int src_w, int src_h,
                              const Region& r, const std::function<bool()>& step, cudaStream_t s) {
   ensure_maps(count, r.rw, r.rh, s);
   const int mw = std::max(r.rw, CONV_HALO_W), mh = std::max(r.rh, CONV_HALO_H);
+  // Without per-layer progress reports the 32 body layers run as one fused
+  // launch.
+  const bool fused = !step && body_fits(count, r.rw, r.rh);
+  const int body_rows = (STEPS - 2) * count * ((r.rh + CONV_TILE_H - 1) / CONV_TILE_H);
+  if (fused) rows_.reserve((size_t)body_rows * sizeof(int));
   mark(0, s);
   {
     const size_t total = (size_t)count * r.rw * r.rh;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)dev_.sms() * 16);
-    realesrgan_prep<<<blocks, 256, 0, s>>>(src, src_u8, src_w, src_h, r.rx0, r.ry0, r.rw, r.rh, mw, mh, count,
-                                           prep_.as<__half>());
+    launch_pdl(realesrgan_prep, blocks, 256, 0, s, src, (int)src_u8, src_w, src_h, r.rx0, r.ry0, r.rw, r.rh, mw, mh,
+               count, prep_.as<__half>(), fused ? rows_.as<int>() : (int*)nullptr, fused ? body_rows : 0);
     IEC_CUDA(cudaGetLastError());
   }
   ConvParams p{};
@@ -240,6 +362,14 @@ bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u
   const void* in = prep_.get();
   bool cancelled = false;
   for (int i = 0; i < STEPS; i++) {
+    if (fused && i >= 1 && i < STEPS - 1) {
+      if (i == 1) {
+        mark(4, s);
+        launch_body(count, mw, mh, r, s);
+      }
+      in = (i % 2 == 0 ? map_a_ : map_b_).get();
+      continue;
+    }
     const Layer& L = layers_[i];
     p.weights = L.w.as<uint16_t>();
     p.bias = L.b.as<float>();
@@ -342,7 +472,12 @@ size_t RealEsrgan::chunk_for(size_t width, size_t height) const {
 
 size_t RealEsrgan::launches(size_t count, size_t width, size_t height) const {
   const size_t chunk = chunk_for(width, height);
-  return (count + chunk - 1) / chunk * (STEPS + 1);
+  size_t n = 0;
+  for (size_t c0 = 0; c0 < count; c0 += chunk) {
+    const int m = (int)std::min(chunk, count - c0);
+    n += body_fits(m, (int)width, (int)height) ? 4 : STEPS + 1;
+  }
+  return n;
 }
 
 void RealEsrgan::run_device(const float* src, float* dst, size_t count, size_t width, size_t height,
@@ -455,7 +590,7 @@ void RealEsrgan::run_device_noalloc(const float* src, float* dst, size_t count, 
   {
     const size_t total = count * (size_t)w * h;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)dev_.sms() * 16);
-    realesrgan_prep<<<blocks, 256, 0, s>>>(src, 0, w, h, 0, 0, w, h, mw, mh, (int)count, prep);
+    launch_pdl(realesrgan_prep, blocks, 256, 0, s, src, 0, w, h, 0, 0, w, h, mw, mh, (int)count, prep, (int*)nullptr, 0);
     IEC_CUDA(cudaGetLastError());
   }
   ConvParams p{};

@@ -59,6 +59,8 @@ class RealEsrgan {
                           cudaStream_t stream);
 
   size_t launches(size_t count, size_t width, size_t height) const;
+  // Fused body on (default) or per-layer launches everywhere.
+  void set_fused(bool on) { no_fuse_ = !on; }
   size_t chunk_for(size_t width, size_t height) const;
 
   // Measurement hooks: events around every launch (see iec_cuda.h).
@@ -83,12 +85,21 @@ class RealEsrgan {
   bool run_network(const void* src, bool src_u8, void* dst, bool dst_u8, int count, int src_w, int src_h,
                    const Region& r, const std::function<bool()>& step, cudaStream_t stream);
   void ensure_maps(size_t count, int w, int h, cudaStream_t stream);
+  // The 32 body layers as one persistent launch (conv3x3_body_sm100.cuh):
+  // whether a pass of this size takes it, and the launch.
+  bool body_fits(int count, int w, int h) const;
+  void launch_body(int count, int mw, int mh, const Region& r, cudaStream_t stream);
   // Record a timing event before a launch of `kind` (-1: after the last).
   void mark(int kind, cudaStream_t stream);
 
   Device dev_;
   std::vector<Layer> layers_;
-  DeviceBuffer prep_, map_a_, map_b_;
+  DeviceBuffer prep_, map_a_, map_b_, rows_, items_;
+  std::array<int, 3> items_key_ = {0, 0, 0};  // pass shape the item table in items_ was built for
+  // Images per layer sweep of the fused body: their two maps stay in L2.
+  static constexpr int BODY_GROUP = 2;
+  bool body_pdl_ = true;   // the fused launch also takes programmatic dependent launch
+  bool no_fuse_ = false;   // per-layer launches only (set_fused)
   size_t map_pixels_ = 0;
   int padded_ = 0;  // maps were zeroed for a region smaller than a TMA box
   std::vector<cudaEvent_t> layer_events_;

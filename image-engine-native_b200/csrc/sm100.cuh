@@ -24,10 +24,26 @@ enum : int {
   DEV_ERR_WAIT_ACC_FULL = 4,
   DEV_ERR_WAIT_ACC_EMPTY = 8,
   DEV_ERR_WAIT_WEIGHTS = 16,
+  DEV_ERR_WAIT_ROWS = 32,  // a fused network's wait for the previous layer's rows
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Global-memory flags between CTAs of one grid: relaxed polling loads, an
+// acquire fence once the flags are seen, and the fence that orders those
+// generic-proxy observations before the async proxy's (TMA) reads.
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t global_ns() {

@@ -67,6 +67,8 @@ def lib():
         L.iec_realesrgan_run_tiles_device.argtypes = [vp, vp, sz, sz, sz, sz, sz, sz, vp, vp]
         L.iec_realesrgan_run_batch.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
+        L.iec_realesrgan_set_fused.argtypes = [vp, ctypes.c_int]
+        L.iec_realesrgan_set_fused.restype = ctypes.c_int
         L.iec_realesrgan_launches.argtypes = [vp, sz, sz, sz]
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
@@ -217,8 +219,12 @@ class RealEsrgan:
     def launches(self, count: int, width: int, height: int) -> int:
         return lib().iec_realesrgan_launches(self._h, count, width, height)
 
+    def set_fused(self, on: bool):
+        """Fused 32-layer body launch (default) or one launch per layer."""
+        _check(lib().iec_realesrgan_set_fused(self._h, 1 if on else 0))
+
     # Measurement hooks (see iec_cuda.h): kinds 0 prep, 1 conv 16->64,
-    # 2 conv 64->64, 3 conv 64->48 + pixel shuffle.
+    # 2 conv 64->64, 3 conv 64->48 + pixel shuffle, 4 the fused 32 layers.
     def set_timing(self, capacity: int):
         _check(lib().iec_realesrgan_set_timing(self._h, capacity))
 

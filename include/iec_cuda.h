@@ -156,10 +156,16 @@ size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t
  * on the stream the kernel runs on, for up to `capacity` launches (0 turns
  * it off). iec_realesrgan_timing then waits for those events, writes each
  * launch's kind (0 input prep, 1 conv 16->64, 2 conv 64->64, 3 conv 64->48
- * with the pixel-shuffle store) and duration in ms, returns how many it
- * wrote (at most `n`) and starts a new record. */
+ * with the pixel-shuffle store, 4 the 32 fused 64->64 layers) and duration in
+ * ms, returns how many it wrote (at most `n`) and starts a new record. */
 iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity);
 size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n);
+
+/* Passes without per-layer progress reports run the 32 64->64 layers as one
+ * persistent launch (the default, `on` = 1) or, with `on` = 0, as 32
+ * launches like passes with progress reports do. The outputs are identical;
+ * this switch exists to compare the two. */
+iec_status iec_realesrgan_set_fused(iec_realesrgan* model, int on);
 
 /* ------------------------------------------------------------------ SCUNet
  * crates/scunet-native/src/lib.rs: SCUNet denoising, output the size of the

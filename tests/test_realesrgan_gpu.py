@@ -194,3 +194,34 @@ def test_tile_ranges_stitch_to_the_tiled_run(gpu_model):
     for first, last in shard.split_ranges([t.cost for t in tiles], 3):
         gpu_model.run_float_tiles(image, 64, 34, first, last, out)
     assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("w,h,count", [(384, 256, 1), (40, 24, 5), (131, 67, 3), (16, 10, 40)])
+def test_fused_body_matches_per_layer_launches(gpu_model, w, h, count):
+    # The persistent 32-layer body launch computes every tile as the
+    # per-layer kernel does: outputs bit for bit, including partial image
+    # groups (3 images = groups of 2 + 1) and tiny maps.
+    images = np.stack([W.realesrgan_input(w, h, 20 + s) for s in range(count)])
+    fused = gpu_model.run_batch(images)
+    gpu_model.set_fused(False)
+    try:
+        layered = gpu_model.run_batch(images)
+    finally:
+        gpu_model.set_fused(True)
+    assert np.array_equal(fused.view(np.uint32), layered.view(np.uint32))
+
+
+def test_fused_body_is_the_path_taken(gpu_model):
+    # One 384 x 256 image: prep, the first layer, the fused body, the last
+    # layer; the timing record shows the fused launch (kind 4) and no
+    # per-layer 64 -> 64 launch.
+    assert gpu_model.launches(1, 384, 256) == 4
+    image = W.realesrgan_input(384, 256, 1)
+    gpu_model.set_timing(16)
+    try:
+        gpu_model.run_batch(image[None])
+        kinds, ms = gpu_model.timing(16)
+    finally:
+        gpu_model.set_timing(0)
+    assert list(kinds) == [0, 1, 4, 3]
+    assert (ms > 0).all()
