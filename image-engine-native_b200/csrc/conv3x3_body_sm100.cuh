@@ -123,13 +123,15 @@ __device__ __forceinline__ void red_add_gpu(int* p, int v) {
 }
 
 // Bounded wait until the shared word `w` exceeds `i` (a counter another warp
-// of the CTA publishes with release).
+// of the CTA publishes with release); short sleeps between polls leave the
+// issue slots to the epilogue warps.
 __device__ __forceinline__ bool wait_word(const uint32_t* w, uint32_t i, volatile int* abort_flag, int* dev_err,
                                           int code) {
   if (ld_acquire_cta(w) > i) return true;
   const uint64_t start = global_ns();
   for (uint32_t n = 1;; n++) {
     if (ld_acquire_cta(w) > i) return true;
+    __nanosleep(32);
     if ((n & 63) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - start > IEC_WAIT_NS) {

@@ -88,17 +88,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes or `ns` pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase of `bar` with `parity` to complete, at most IEC_WAIT_NS.
-// Gives up early when another role of the CTA has aborted. try_wait itself
-// blocks for a while before it fails; the clock and the abort flag are only
-// looked at every 64 failed tries, so waiting warps take few issue slots
-// from the ones doing work.
+// Gives up early when another role of the CTA has aborted. After the first
+// try, each try sleeps up to 20 us unless the phase completes (the clock and
+// the abort flag are looked at every 64 tries), so waiting warps take almost
+// no issue slots from the ones doing work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* dev_err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   for (uint32_t n = 1;; n++) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_for(bar, parity, 20000u)) return true;
     if ((n & 63) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - start > IEC_WAIT_NS) {
