@@ -224,25 +224,30 @@ __global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, co
 // tap k of a size x size kernel, the 64 channels of `t` sampled bilinearly
 // at the tap moved by its offset, times 2 sigmoid(modulator). `offs` holds
 // the offset convolution's 3 taps channels (y, x per tap, then the logits).
-// One thread per (pixel, tap, channel group).
+// blockIdx.y is (tap, channel group); the threads of a block take
+// consecutive pixels, so a warp's 16-byte stores fill 512 contiguous bytes of
+// one output plane and its neighbour loads stay within a few rows.
 __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plane, int height, int width, int size,
                                   const __half* __restrict__ offs, long long offs_plane, __half* __restrict__ out,
                                   long long out_plane) {
   griddep_wait();
   griddep_launch_dependents();
   const int taps = size * size;
-  const long long n = (long long)height * width * taps * 8;
+  const int tap = (int)(blockIdx.y >> 3), g = (int)(blockIdx.y & 7);
+  const long long n = (long long)height * width;
   const float hs = (float)(size / 2), hf = (float)height, wf = (float)width;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int g = (int)(i & 7);
-    const long long pt = i >> 3;
-    const int tap = (int)(pt % taps);
-    const long long p = pt / taps;
+  const float ky = (float)(tap / size), kx = (float)(tap % size);
+  auto chan = [&](int c) { return offs + (long long)(c / 8) * offs_plane + (c % 8); };
+  const __half* off_y = chan(2 * tap);
+  const __half* off_x = chan(2 * tap + 1);
+  const __half* off_m = chan(2 * taps + tap);
+  const __half* src = t + g * t_plane;
+  __half* dst = out + (long long)(tap * 8 + g) * out_plane;
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < n; p += (long long)gridDim.x * blockDim.x) {
     const int y = (int)(p / width), x = (int)(p % width);
-    auto ch = [&](int c) { return __half2float(offs[(long long)(c / 8) * offs_plane + p * 8 + (c % 8)]); };
-    const float py = ((float)y - hs + (float)(tap / size)) + ch(2 * tap);
-    const float px = ((float)x - hs + (float)(tap % size)) + ch(2 * tap + 1);
-    const float m = 2.0f * sigmoid_f(ch(2 * taps + tap));
+    const float py = ((float)y - hs + ky) + __half2float(off_y[p * 8]);
+    const float px = ((float)x - hs + kx) + __half2float(off_x[p * 8]);
+    const float m = 2.0f * sigmoid_f(__half2float(off_m[p * 8]));
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (!(py <= -1.0f || py >= hf || px <= -1.0f || px >= wf)) {
       const float y0f = floorf(py), x0f = floorf(px);
@@ -250,7 +255,6 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
       const int y0 = (int)y0f, x0 = (int)x0f;
       const int cy[4] = {y0, y0, y0 + 1, y0 + 1}, cx[4] = {x0, x0 + 1, x0, x0 + 1};
       const float cw[4] = {hy * hx, hy * lx, ly * hx, ly * lx};
-      const __half* src = t + g * t_plane;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         if (cy[k] < 0 || cx[k] < 0 || cy[k] >= height || cx[k] >= width) continue;
@@ -262,7 +266,7 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
     }
 #pragma unroll
     for (int e = 0; e < 8; e++) acc[e] *= m;
-    store8(out + (long long)(tap * 8 + g) * out_plane + p * 8, acc);
+    store8(dst + p * 8, acc);
   }
 }
 
@@ -822,7 +826,8 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     o.out = offs;
     o.plane_elems = pp;
     gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, bs);
-    launch_pdl(bir_deform_sample, blocks_for(P * taps * 8, sms), 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+    launch_pdl(bir_deform_sample, dim3((unsigned)std::min<long long>((P + 255) / 256, 4LL * sms), (unsigned)(taps * 8)),
+               256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
     IEC_CUDA(cudaGetLastError());
     GemmOutSpec c;
     c.mode = OUT_STORE;
