@@ -14,6 +14,7 @@ struct FourierPlan {
   int h = 0, w = 0, half = 0, channels = 0;
   DeviceBuffer twiddles;  // cos / sin of 2 pi j / w, then of 2 pi j / h (f32, from double)
   DeviceBuffer scratch;   // row spectra [channels / 8][h][half][8] complex f32
+  bool two_pass = false;  // always the two-launch transforms (for comparisons)
 };
 
 void fourier_plan(FourierPlan& plan, int h, int w, int channels);

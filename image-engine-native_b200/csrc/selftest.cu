@@ -92,7 +92,8 @@ extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int w
   }
 }
 
-extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, float* spec, float* back) {
+extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, int two_pass, float* spec,
+                                         float* back) {
   try {
     if (c % 8 != 0 || h < 1 || w < 1) throw Error(ERR_INPUT, "rfft2 self-test: c a multiple of 8");
     Options opt;
@@ -101,6 +102,7 @@ extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int 
     DeviceScope scope(dev);
     FourierPlan plan;
     fourier_plan(plan, h, w, c);
+    plan.two_pass = two_pass != 0;
     const int half = w / 2 + 1, rows = h * w, frows = h * half;
     const long long xp = (long long)rows * 8, fp = (long long)frows * 8;
     DeviceBuffer d32, dx, dspec, dout;

@@ -73,7 +73,8 @@ def lib():
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
-        L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, f32p, f32p]
+        L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         f32p, f32p]
         L.iec_selftest_gemm_time.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)]
         L.iec_selftest_attention.argtypes = [i32, f32p, i32, i32, f32p, i32, i32, i32, f32p]
         L.iec_scunet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
@@ -423,14 +424,15 @@ class Birefnet:
         _check(lib().iec_birefnet_run_device(self._h, image_ptr, int(image_u8), side, logits_ptr, stream or None))
 
 
-def selftest_rfft2(x: np.ndarray, device: int = -1):
+def selftest_rfft2(x: np.ndarray, device: int = -1, two_pass: bool = False):
     """LaMa's planar rfft2 / irfft2 on an h x w x c array (c % 8 == 0):
-    returns (spectrum h x (w/2+1) x 2c, irfft2 of it h x w x c)."""
+    returns (spectrum h x (w/2+1) x 2c, irfft2 of it h x w x c); `two_pass`
+    forces the two-launch transforms."""
     x = np.ascontiguousarray(x, np.float32)
     h, w, c = x.shape
     spec = np.empty((h, w // 2 + 1, 2 * c), np.float32)
     back = np.empty_like(x)
-    _check(lib().iec_selftest_rfft2(device, _f32(x), h, w, c, _f32(spec), _f32(back)))
+    _check(lib().iec_selftest_rfft2(device, _f32(x), h, w, c, 1 if two_pass else 0, _f32(spec), _f32(back)))
     return spec, back
 
 

@@ -265,8 +265,11 @@ iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int w, int k, 
 /* Diagnostics: LaMa's planar Fourier transforms on host arrays: `x` h x w x c
  * floats (c a multiple of 8, rounded to f16 on the way in); `spec` gets
  * rfft2(x) as h x (w / 2 + 1) x 2c floats (real parts of the c channels, then
- * imaginary), `back` gets irfft2 of that spectrum (h x w x c). */
-iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, float* spec, float* back);
+ * imaginary), `back` gets irfft2 of that spectrum (h x w x c). `two_pass`
+ * non-zero takes the two-launch transforms even where the one-launch ones
+ * for small maps apply (the results are the same). */
+iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, int two_pass, float* spec,
+                              float* back);
 
 /* Diagnostics: per launch of the general GEMM on zero-filled buffers (mode
  * 0: m x k rows; 1: 3x3 taps over an h x w map; 2: one tap over an h x w

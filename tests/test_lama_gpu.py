@@ -138,16 +138,19 @@ def test_run_device(gpu_model, cpu_model):
     within(out.cpu().numpy(), cpu_model.run_float(image, mask))
 
 
+@pytest.mark.parametrize("two_pass", [False, True])
 @pytest.mark.parametrize("h,w,c", [(64, 64, 16), (5, 7, 8), (16, 12, 8), (9, 10, 8), (1, 8, 8), (2, 2, 8),
-                                   (32, 128, 8)])
-def test_planar_rfft2_matches_numpy(h, w, c):
+                                   (32, 128, 8), (128, 96, 8)])
+def test_planar_rfft2_matches_numpy(h, w, c, two_pass):
     """fft.cu against numpy's ortho rfft2 / irfft2 of the same f16-rounded
-    input; the spectrum is stored in f16, hence the relative bound."""
+    input; the spectrum is stored in f16, hence the relative bound. Both the
+    one-launch transforms of small maps and the two-launch ones (128 x 96
+    takes the two-launch path either way)."""
     import iec
 
     rng = np.random.default_rng(h * 1000 + w)
     x = rng.random((h, w, c), dtype=np.float32).astype(np.float16).astype(np.float32)
-    spec, back = iec.selftest_rfft2(x)
+    spec, back = iec.selftest_rfft2(x, two_pass=two_pass)
     want = np.fft.rfft2(x.astype(np.float64), axes=(0, 1), norm="ortho")
     scale = 1.0 + np.abs(want).max()
     assert np.abs(spec[:, :, :c] - want.real).max() <= 2e-3 * scale
@@ -170,3 +173,17 @@ def test_handle_of_another_model_is_refused(gpu_model):
     st = iec.lib().iec_scunet_run_float(gpu_model._h, image.ctypes.data_as(f32p), 16, 16, out.ctypes.data_as(f32p))
     assert st == 3  # IEC_ERR_INPUT
     assert gpu_model.run_float(*W.lama_input(16, 16, 0)).shape == (16, 16, 3)
+
+
+@pytest.mark.parametrize("h,w,c", [(64, 64, 192), (32, 32, 16), (24, 40, 8), (9, 10, 8)])
+def test_one_launch_rfft2_equals_two_launch(h, w, c):
+    """The one-launch transforms of small maps run the same butterflies in
+    the same order as the two-launch ones: spectra and inverses bit for bit."""
+    import iec
+
+    rng = np.random.default_rng(h * 7 + w)
+    x = rng.standard_normal((h, w, c), dtype=np.float32).astype(np.float16).astype(np.float32)
+    s1, b1 = iec.selftest_rfft2(x)
+    s2, b2 = iec.selftest_rfft2(x, two_pass=True)
+    assert np.array_equal(s1.view(np.uint32), s2.view(np.uint32))
+    assert np.array_equal(b1.view(np.uint32), b2.view(np.uint32))
