@@ -169,10 +169,12 @@ __device__ __forceinline__ uint4 pack_half8(const float* w) {
 // Sigmoid stays out of line (and GELU compact): inlined into every element of
 // the unrolled epilogue they made its loop body too large for the
 // instruction cache, and the common ReLU / identity path would pay for them.
-// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7; __expf adds about
-// 1e-7 relative): compact enough to stay inline in the epilogue.
+// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7; __expf and the
+// approximate reciprocal, both a few ulp, add about 2e-7 relative): compact
+// enough to stay inline in the epilogue (an IEEE division here cost more
+// than the rest of the activation).
 __device__ __forceinline__ float gemm_erf(float x) {
-  const float a = fabsf(x), t = 1.0f / fmaf(0.3275911f, a, 1.0f);
+  const float a = fabsf(x), t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
   const float poly =
       t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
   return copysignf(1.0f - poly * __expf(-a * a), x);
@@ -181,7 +183,7 @@ __device__ __forceinline__ float gemm_gelu(float v) { return 0.5f * v * (1.0f + 
 
 static __device__ __noinline__ float gemm_sigmoid(float v) {
   // math.rs:33-39: from exp(-|x|), so that neither tail cancels.
-  const float e = expf(-fabsf(v)), s = e / (e + 1.0f);
+  const float e = expf(-fabsf(v)), s = __fdividef(e, e + 1.0f);
   return v > 0.0f ? 1.0f - s : s;
 }
 
