@@ -7,7 +7,7 @@
 // halo loads, the weights, the last tile's epilogue) of several
 // microseconds, and each layer's 100+ MB of maps round-trips through HBM,
 // whose power pulls the SM clock down. Here the work items are (layer,
-// image, tile), ordered group by group of `group` images, layer by layer
+// image, 4 x 30 tile), ordered group by group of `group` images, layer by layer
 // within a group, tiles in row order; CTA c takes items c, c + grid, ...
 // A group's two maps (group x 2 x 12.6 MB for 256 x 384 images) stay in L2
 // while its layers run, and no CTA ever waits for a whole layer: before
@@ -38,14 +38,14 @@
 // buffer (n & 1) for this CTA's n-th layer change once the MMA issuer has
 // released that buffer (a tcgen05.commit when it moved past the layer that
 // used it before), so the next layer's weights arrive while the current
-// one runs. Four halo stages fit beside them.
+// one runs. Three 24 KB halo stages fit beside them.
 #pragma once
 
 #include "conv3x3_sm100.cuh"
 
 namespace iec {
 
-constexpr int BODY_NSTAGE = 4;
+constexpr int BODY_NSTAGE = 3;
 constexpr int BODY_MAX_LAYERS = 32;
 constexpr int BODY_LOOKAHEAD = 8;                          // items the tracker checks per poll
 constexpr int BODY_SIGNAL_WARP = 2 + CONV_EPI_WARPS;       // 18
@@ -146,7 +146,8 @@ __device__ __forceinline__ bool wait_word(const uint32_t* w, uint32_t i, volatil
 struct BodySmem {
   static constexpr int KCH = 8;
   static constexpr int W_BYTES = 9 * KCH * 64 * 16;             // 73,728
-  static constexpr int STAGE_BYTES = KCH * CONV_CHUNK_BYTES;    // 20,480 (a multiple of 1024)
+  static constexpr int STAGE_BYTES = KCH * CONV_CHUNK_BYTES;    // 24,576 (a multiple of 1024)
+  static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1024-byte aligned");
   static constexpr int A_OFF = 2 * W_BYTES;
   static constexpr int BAR_OFF = A_OFF + BODY_NSTAGE * STAGE_BYTES;
   // full[NSTAGE], empty[NSTAGE], acc_full[2], acc_empty[2], wfull[2], wempty[2]
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
     const int quarter = warp & 3;            // TMEM lanes 32 q .. 32 q + 31
     const int part = (warp - 2) >> 2;        // channels 16 part .. 16 part + 15
     const int row = quarter * 32 + lane;     // M row = partial-sum position (r, c) of the tile
-    const int pr = row >> 4, pc = row & 15;
+    const int pr = row / CONV_HALO_W, pc = row % CONV_HALO_W;
     const size_t plane = (size_t)p.MH * p.MW;
     float r_bias[16], r_slope[16];
     bool unit = false;

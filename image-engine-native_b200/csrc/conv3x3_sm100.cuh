@@ -7,24 +7,27 @@
 // network.rs:118-140 (pixel shuffle x4 plus the input repeated).
 //
 // Layout. Feature maps are f16 and "channel-group planar": [image][cin / 8]
-// [height][width][8], so a row of one plane is contiguous. One tile is 8 rows
-// x 14 columns of output pixels. Its MMA rows (M = 128) are the 8 x 16
-// positions x0 - 1 .. x0 + 14 of those rows, and its MMA columns are the
-// three horizontal taps side by side (N = 3 * cout): row (r, c), column
-// kx * cout + o accumulates Q_kx(r, c)[o] = sum over ky and channels of
-// in(r + ky - 1, c - 1) * w[ky][kx][.][o]. Output pixel (r, c) (c = 1..14)
-// is then Q_0(r, c - 1) + Q_1(r, c) + Q_2(r, c + 1): its neighbours' partial
-// sums sit in the adjacent TMEM lanes, one warp shuffle away. Three MMAs of
-// N = 192 fetch as many shared-memory operand bytes as three of N = 64 but
-// do three times the math, which is what bounds this convolution (its
-// narrow N otherwise leaves the tensor core waiting on operand fetches).
+// [height][width][8], so a row of one plane is contiguous. One tile is 4 rows
+// x 30 columns of output pixels. Its MMA rows (M = 128) are the 4 x 32
+// positions x0 - 1 .. x0 + 30 of those rows (one row per TMEM lane quarter,
+// so per epilogue warp), and its MMA columns are the three horizontal taps
+// side by side (N = 3 * cout): row (r, c), column kx * cout + o accumulates
+// Q_kx(r, c)[o] = sum over ky and channels of in(r + ky - 1, c - 1) *
+// w[ky][kx][.][o]. Output pixel (r, c) (c = 1..30) is then Q_0(r, c - 1) +
+// Q_1(r, c) + Q_2(r, c + 1): its neighbours' partial sums sit in the
+// adjacent TMEM lanes, one warp shuffle away. Three MMAs of N = 192 fetch as
+// many shared-memory operand bytes as three of N = 64 but do three times the
+// math, which is what bounds this convolution (its narrow N otherwise leaves
+// the tensor core waiting on operand fetches). 30 of every 32 positions are
+// outputs (an 8 x 16 block of positions kept 14 of 16: the MMAs and the
+// epilogue did 7 % more work per output pixel).
 //
-// A single 4-D TMA box (inner row 16 pixels x 8 channels = 256 bytes) brings
-// the tile's 10 x 16 pixel halo of every channel group into shared memory as
-// [group][10][16][8]: the no-swizzle K-major core-matrix layout tcgen05
+// A single 4-D TMA box (inner row 32 pixels x 8 channels = 512 bytes) brings
+// the tile's 6 x 32 pixel halo of every channel group into shared memory as
+// [group][6][32][8]: the no-swizzle K-major core-matrix layout tcgen05
 // reads, 8 consecutive positions of a row per core matrix (SBO 128 bytes),
-// the next channel group 2560 bytes on (LBO). Tap row ky is a start offset
-// of ky * 256 bytes into the same halo; out-of-image pixels are TMA's zero
+// the next channel group 3072 bytes on (LBO). Tap row ky is a start offset
+// of ky * 512 bytes into the same halo; out-of-image pixels are TMA's zero
 // fill.
 //
 // The weights of the layer, pre-arranged on the host as [ky][cin / 8]
@@ -50,11 +53,11 @@
 
 namespace iec {
 
-constexpr int CONV_TILE_H = 8;                    // output rows of a tile
-constexpr int CONV_TILE_W = 14;                   // output columns of a tile
-constexpr int CONV_HALO_H = CONV_TILE_H + 2;      // 10
-constexpr int CONV_HALO_W = CONV_TILE_W + 2;      // 16: also the partial-sum positions of a row
-constexpr int CONV_CHUNK_BYTES = CONV_HALO_H * CONV_HALO_W * 16;  // 2560: one channel group
+constexpr int CONV_TILE_H = 4;                    // output rows of a tile
+constexpr int CONV_TILE_W = 30;                   // output columns of a tile
+constexpr int CONV_HALO_H = CONV_TILE_H + 2;      // 6
+constexpr int CONV_HALO_W = CONV_TILE_W + 2;      // 32: also the partial-sum positions of a row (one warp)
+constexpr int CONV_CHUNK_BYTES = CONV_HALO_H * CONV_HALO_W * 16;  // 3072: one channel group
 constexpr int CONV_NSTAGE = 6;
 constexpr int CONV_EPI_WARPS = 16;                // four per TMEM lane quarter
 constexpr int CONV_THREADS = 64 + 32 * CONV_EPI_WARPS;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     const int quarter = warp & 3;            // TMEM lanes 32 q .. 32 q + 31
     const int part = (warp - 2) >> 2;        // which quarter of the channels (0..3)
     const int row = quarter * 32 + lane;     // M row = partial-sum position (r, c) of the tile
-    const int pr = row >> 4, pc = row & 15;
+    const int pr = row / CONV_HALO_W, pc = row % CONV_HALO_W;
     // This warp's channels' bias and PReLU slope, kept in registers.
     constexpr int NB = MODE == CONV_PRELU ? COUT / 4 : 12;
     float r_bias[NB], r_slope[NB];
@@ -264,8 +267,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * CONV_ACC_COLS);
       // out(r, c) = Q_0(r, c - 1) + Q_1(r, c) + Q_2(r, c + 1): the left and
-      // right partial sums come from the neighbouring lanes (same tile row:
-      // a row is 16 lanes, a warp holds two whole rows).
+      // right partial sums come from the neighbouring lanes (a warp holds
+      // one whole row of 32 positions).
       constexpr int NV = MODE == CONV_PRELU ? COUT / 4 : 12;
       float v[NV];
       if constexpr (MODE == CONV_PRELU) {
