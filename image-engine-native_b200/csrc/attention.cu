@@ -13,11 +13,16 @@
 // projection GEMM's A operand. Four warps each own 16 query rows: Q K^T and
 // P V run on mma.sync m16n8k16 (f16 in, f32 accumulate), the scores stay in
 // registers between the two (the accumulator fragment of S is the A fragment
-// of P), and the softmax uses quad shuffles for the row max and sum.
+// of P), and the softmax uses quad shuffles for the row max and sum. The bias
+// tables are stored in the order of those fragments (attention_bias_layout):
+// a thread's 32 bias values are 8 float4 loads, each warp's load 512
+// contiguous bytes (read element by element they kept L1 83 % busy).
 #include <cuda_fp16.h>
 
 #include "gemm.h"
 #include "sm100.cuh"
+
+#include <vector>
 
 namespace iec {
 
@@ -75,7 +80,8 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
   // The bias table of this window's class (swin.rs:154-159).
   int cls = 0;
   if (shifted) cls = (win % cols_w == cols_w - 1 ? 1 : 0) + 2 * (win / cols_w == rows_w - 1 ? 1 : 0);
-  const float* tb = bias + ((long long)cls * heads + head) * TOK * TOK;
+  const float4* tb = reinterpret_cast<const float4*>(bias + ((long long)cls * heads + head) * TOK * TOK) +
+                     (threadIdx.x >> 5) * 8 * 32 + (threadIdx.x & 31);
 
   const int g = lane >> 2, t = lane & 3;
   const int q0 = warp * 16;
@@ -103,13 +109,15 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
   const float scale = 0.17677669529663688f;  // 1 / sqrt(32)
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-  for (int j = 0; j < 8; j++)
+  for (int j = 0; j < 8; j++) {
+    const float4 b4 = __ldg(tb + j * 32);
+    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
     for (int e = 0; e < 4; e++) {
-      const int r = q0 + g + (e >> 1) * 8, col = 8 * j + 2 * t + (e & 1);
-      s[j][e] = s[j][e] * scale + tb[r * TOK + col];
+      s[j][e] = s[j][e] * scale + bv[e];
       mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
     }
+  }
 #pragma unroll
   for (int h = 0; h < 2; h++) {
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
@@ -162,6 +170,25 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
 }
 
 }  // namespace
+
+std::vector<float> attention_bias_layout(const std::vector<float>& tables) {
+  if (tables.size() % (TOK * TOK) != 0) throw Error(ERR_INPUT, "bias tables are 64 x 64 each");
+  std::vector<float> out(tables.size());
+  for (size_t n = 0; n < tables.size() / (TOK * TOK); n++) {
+    const float* src = tables.data() + n * TOK * TOK;
+    float* dst = out.data() + n * TOK * TOK;
+    // thread (warp w, lane l = 4 g + t), value (j, e): row 16 w + g + 8 (e / 2),
+    // column 8 j + 2 t + e % 2 of the table, at [w][j][l][e]
+    for (int w = 0; w < 4; w++)
+      for (int j = 0; j < 8; j++)
+        for (int l = 0; l < 32; l++)
+          for (int e = 0; e < 4; e++) {
+            const int r = 16 * w + (l >> 2) + 8 * (e >> 1), col = 8 * j + 2 * (l & 3) + (e & 1);
+            dst[((w * 8 + j) * 32 + l) * 4 + e] = src[r * TOK + col];
+          }
+  }
+  return out;
+}
 
 void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int windows, const float* bias,
                       bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems,

@@ -514,7 +514,8 @@ Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
       upload(blk.n1g, f.take(p + ".norm1.weight", {(size_t)c}));
       upload(blk.n1b, f.take(p + ".norm1.bias", {(size_t)c}));
       pack(f, blk.qkv, p + ".qkv", 1, c, 3 * c, true);
-      upload(blk.bias, slot_tables(f.take(p + ".position_bias", {(size_t)heads, NTOK, NTOK}), heads, blk.shifted));
+      upload(blk.bias, attention_bias_layout(
+                           slot_tables(f.take(p + ".position_bias", {(size_t)heads, NTOK, NTOK}), heads, blk.shifted)));
       pack(f, blk.proj, p + ".proj", 1, c, c, true);
       upload(blk.n2g, f.take(p + ".norm2.weight", {(size_t)c}));
       upload(blk.n2b, f.take(p + ".norm2.bias", {(size_t)c}));

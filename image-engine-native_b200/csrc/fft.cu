@@ -31,6 +31,7 @@ namespace iec {
 namespace {
 
 constexpr int FFT_THREADS = 256;
+constexpr int FFT_SMALL_THREADS = 1024;  // the one-launch transforms: a stage's butterflies at once
 constexpr int FFT_POINTS = 512;   // points per CTA when lines are short
 constexpr int FFT_MAX_N = 1536;   // longest line (shared memory: 2 x 64 n bytes)
 
@@ -351,7 +352,7 @@ __device__ __forceinline__ void store_halves(__half* dst, const float* v) {
 // 8 / C + slice): rows of the real map, the first w/2 + 1 columns kept in
 // shared memory column by column, columns, the scaled f16 spectrum.
 template <int C>
-__global__ void __launch_bounds__(FFT_THREADS) fft2_fwd_small(const __half* __restrict__ x, long long x_plane,
+__global__ void __launch_bounds__(FFT_SMALL_THREADS) fft2_fwd_small(const __half* __restrict__ x, long long x_plane,
                                                              __half* __restrict__ spec, long long spec_plane, Dims d,
                                                              Line fr, Line fc) {
   griddep_wait();
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(FFT_THREADS) fft2_fwd_small(const __half* __re
 // spectrum, the Hermitian rows built in shared memory, rows, the scaled real
 // part added on x.
 template <int C>
-__global__ void __launch_bounds__(FFT_THREADS) fft2_inv_small(const __half* __restrict__ spec, long long spec_plane,
+__global__ void __launch_bounds__(FFT_SMALL_THREADS) fft2_inv_small(const __half* __restrict__ spec, long long spec_plane,
                                                              __half* __restrict__ x, long long x_plane, Dims d,
                                                              Line fr, Line fc) {
   griddep_wait();
@@ -539,7 +540,7 @@ void launch_fwd_small(const FourierPlan& plan, const Dims& d, const __half* x, l
                       long long spec_plane, cudaStream_t s) {
   const size_t bytes = small_smem(plan, C);
   prepare(fft2_fwd_small<C>, bytes);
-  launch_pdl(fft2_fwd_small<C>, dim3(d.groups * (8 / C)), FFT_THREADS, bytes, s, x, x_plane, spec, spec_plane, d,
+  launch_pdl(fft2_fwd_small<C>, dim3(d.groups * (8 / C)), FFT_SMALL_THREADS, bytes, s, x, x_plane, spec, spec_plane, d,
              line_of(plan, true), line_of(plan, false));
   IEC_CUDA(cudaGetLastError());
 }
@@ -549,7 +550,7 @@ void launch_inv_small(const FourierPlan& plan, const Dims& d, const __half* spec
                       long long x_plane, cudaStream_t s) {
   const size_t bytes = small_smem(plan, C);
   prepare(fft2_inv_small<C>, bytes);
-  launch_pdl(fft2_inv_small<C>, dim3(d.groups * (8 / C)), FFT_THREADS, bytes, s, spec, spec_plane, x, x_plane, d,
+  launch_pdl(fft2_inv_small<C>, dim3(d.groups * (8 / C)), FFT_SMALL_THREADS, bytes, s, spec, spec_plane, x, x_plane, d,
              line_of(plan, true), line_of(plan, false));
   IEC_CUDA(cudaGetLastError());
 }

@@ -122,6 +122,10 @@ void merge_layer_norm_planar(const __half* src, long long src_plane_elems, int g
 // Fused attention over 8 x 8 windows (attention.cu): `qkv` planar [3c / 8]
 // [windows * 64][8], `bias` [classes][c / 32][64][64] f32 (classes 4 when
 // `shifted`, else 1), output planar [c / 8][windows * 64][8].
+// The bias tables ([n][64][64] f32: position bias plus shift mask per class
+// and head) in the order window_attention reads them.
+std::vector<float> attention_bias_layout(const std::vector<float>& tables);
+
 void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int windows, const float* bias,
                       bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems, cudaStream_t s);
 

@@ -178,7 +178,7 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
     upload(b.ln1g, f.take(t + ".ln1.weight", {(size_t)h}));
     upload(b.ln1b, f.take(t + ".ln1.bias", {(size_t)h}));
     linear(f, b.qkv, t + ".msa.embedding_layer", h, 3 * h, true);
-    upload(b.bias, bias_tables(f.take(t + ".msa.position_bias", {(size_t)(h / 32), 64, 64}), shifted));
+    upload(b.bias, attention_bias_layout(bias_tables(f.take(t + ".msa.position_bias", {(size_t)(h / 32), 64, 64}), shifted)));
     linear(f, b.proj, t + ".msa.linear", h, h, true);
     upload(b.ln2g, f.take(t + ".ln2.weight", {(size_t)h}));
     upload(b.ln2b, f.take(t + ".ln2.bias", {(size_t)h}));

@@ -79,7 +79,10 @@ extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int w
     do32.reserve((size_t)rows * c * 4);
     cudaStream_t s = dev.stream();
     IEC_CUDA(cudaMemcpyAsync(d32.get(), qkv, (size_t)rows * 3 * c * 4, cudaMemcpyHostToDevice, s));
-    IEC_CUDA(cudaMemcpyAsync(db.get(), bias, (size_t)classes * (c / 32) * 64 * 64 * 4, cudaMemcpyHostToDevice, s));
+    const std::vector<float> tables =
+        attention_bias_layout(std::vector<float>(bias, bias + (size_t)classes * (c / 32) * 64 * 64));
+    IEC_CUDA(cudaMemcpyAsync(db.get(), tables.data(), tables.size() * 4, cudaMemcpyHostToDevice, s));
+    dev.sync(s);  // the host vector goes out of scope
     rows_to_planar(d32.as<float>(), rows, 3 * c, dq.as<__half>(), plane, s);
     window_attention(dq.as<__half>(), plane, c, windows, db.as<float>(), shifted != 0, rows_w, cols_w,
                      dout.as<__half>(), plane, s);
