@@ -217,10 +217,10 @@ size_t RealEsrgan::timing(int* kinds, float* ms, size_t n) {
   return w;
 }
 
-bool RealEsrgan::body_fits(int count, int w, int h) const {
+bool RealEsrgan::body_fits(int count, int w, int h, int layers_per_launch) const {
   const long long tiles_img = (long long)((w + CONV_TILE_W - 1) / CONV_TILE_W) * ((h + CONV_TILE_H - 1) / CONV_TILE_H);
   const long long group = std::min(count, BODY_GROUP);
-  const long long layers = STEPS - 2;
+  const long long layers = layers_per_launch;
   const long long items = layers * count * tiles_img, group_items = layers * group * tiles_img;
   const long long group_tiles = group * tiles_img, tiles_x = (w + CONV_TILE_W - 1) / CONV_TILE_W;
   // FastDiv's exactness (numerator x divisor < 2^40) for every division of
@@ -233,7 +233,7 @@ bool RealEsrgan::body_fits(int count, int w, int h) const {
          count <= 256 && tiles_y <= 1024 && tiles_x <= 512;  // body_pack's fields
 }
 
-void RealEsrgan::launch_body(int count, int mw, int mh, const Region& r, cudaStream_t s) {
+void RealEsrgan::launch_body(int count, int mw, int mh, const Region& r, int first, int layers, cudaStream_t s) {
   BodyParams bp{};
   bp.H = r.rh;
   bp.W = r.rw;
@@ -243,7 +243,7 @@ void RealEsrgan::launch_body(int count, int mw, int mh, const Region& r, cudaStr
   bp.tiles_y = (r.rh + CONV_TILE_H - 1) / CONV_TILE_H;
   bp.tiles_img = bp.tiles_x * bp.tiles_y;
   bp.count = count;
-  bp.layers = STEPS - 2;
+  bp.layers = layers;
   bp.group = std::min(count, BODY_GROUP);
   const int groups = (count + bp.group - 1) / bp.group;
   const int last_images = count - (groups - 1) * bp.group;
@@ -256,18 +256,20 @@ void RealEsrgan::launch_body(int count, int mw, int mh, const Region& r, cudaStr
   bp.div_group_tiles = FastDiv((uint32_t)(bp.group * bp.tiles_img));
   bp.div_last_tiles = FastDiv((uint32_t)(last_images * bp.tiles_img));
   static_assert(STEPS - 2 <= BODY_MAX_LAYERS, "body layers");
+  if (first < 0 || layers < 1 || first + layers > STEPS - 2) throw Error(ERR_INPUT, "body layer range");
   for (int l = 0; l < bp.layers; l++) {
-    const Layer& L = layers_[l + 1];
+    const Layer& L = layers_[first + l + 1];
     bp.weights[l] = L.w.as<uint16_t>();
     bp.bias[l] = L.b.as<float>();
     bp.slope[l] = L.s.as<float>();
     if (L.slope_unit) bp.slope_unit |= 1u << l;
   }
-  bp.maps[0] = map_a_.as<__half>();
-  bp.maps[1] = map_b_.as<__half>();
-  bp.rows = rows_.as<int>();
+  // Body layer f reads map A when f is even (the first layer wrote A).
+  bp.maps[0] = (first % 2 == 0 ? map_a_ : map_b_).as<__half>();
+  bp.maps[1] = (first % 2 == 0 ? map_b_ : map_a_).as<__half>();
+  bp.rows = rows_.as<int>() + (size_t)first * count * bp.tiles_y;
   // The item table (body_item of every index, packed), built once per shape.
-  const std::array<int, 3> key = {count, r.rw, r.rh};
+  const std::array<int, 4> key = {count, r.rw, r.rh, layers};
   if (key != items_key_) {
     std::vector<uint32_t> words((size_t)bp.items);
     for (int k = 0; k < bp.items; k++) {
@@ -333,9 +335,10 @@ bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u
                              const Region& r, const std::function<bool()>& step, cudaStream_t s) {
   ensure_maps(count, r.rw, r.rh, s);
   const int mw = std::max(r.rw, CONV_HALO_W), mh = std::max(r.rh, CONV_HALO_H);
-  // Without per-layer progress reports the 32 body layers run as one fused
-  // launch.
-  const bool fused = !step && body_fits(count, r.rw, r.rh);
+  // The 32 body layers run as one fused launch, or with progress reports as
+  // fused launches of BODY_STAGE layers (their reports follow each launch).
+  const int stage = step ? BODY_STAGE : STEPS - 2;
+  const bool fused = body_fits(count, r.rw, r.rh, stage);
   const int body_rows = (STEPS - 2) * count * ((r.rh + CONV_TILE_H - 1) / CONV_TILE_H);
   if (fused) rows_.reserve((size_t)body_rows * sizeof(int));
   mark(0, s);
@@ -360,62 +363,65 @@ bool RealEsrgan::run_network(const void* src, bool src_u8, void* dst, bool dst_u
   p.div_tiles_y = FastDiv((uint32_t)p.tiles_y);
   p.dev_err = dev_.dev_err();
   const void* in = prep_.get();
+  // Launch units (first layer, layer count): the first layer, the body (fused
+  // launches, or one launch per layer), the last layer.
+  std::vector<std::array<int, 2>> units;
+  units.push_back({0, 1});
+  for (int f = 1; f < STEPS - 1; f += fused ? stage : 1) units.push_back({f, fused ? std::min(stage, STEPS - 1 - f) : 1});
+  units.push_back({STEPS - 1, 1});
   bool cancelled = false;
-  for (int i = 0; i < STEPS; i++) {
+  for (size_t u = 0; u < units.size(); u++) {
+    const int i = units[u][0], n = units[u][1];
+    // the unit's output map: the one its last layer writes
+    __half* out = ((i + n - 1) % 2 == 0 ? map_a_ : map_b_).as<__half>();
     if (fused && i >= 1 && i < STEPS - 1) {
-      if (i == 1) {
-        mark(4, s);
-        launch_body(count, mw, mh, r, s);
-      }
-      in = (i % 2 == 0 ? map_a_ : map_b_).get();
-      continue;
-    }
-    const Layer& L = layers_[i];
-    p.weights = L.w.as<uint16_t>();
-    p.bias = L.b.as<float>();
-    p.slope = L.s.get() ? L.s.as<float>() : nullptr;
-    p.slope_unit = L.slope_unit;
-    __half* out = (i % 2 == 0 ? map_a_ : map_b_).as<__half>();
-    p.out = out;
-    mark(i == 0 ? 1 : i < STEPS - 1 ? 2 : 3, s);
-    if (i == 0) {
-      launch_conv<16, 64, CONV_PRELU>(dev_, in, count, mw, mh, p, s);
-    } else if (i < STEPS - 1) {
-      launch_conv<64, 64, CONV_PRELU>(dev_, in, count, mw, mh, p, s);
+      mark(4, s);
+      launch_body(count, mw, mh, r, i - 1, n, s);
     } else {
-      ShuffleOut& so = p.shuffle;
-      so.src = src;
-      so.dst = dst;
-      so.src_w = src_w;
-      so.src_h = src_h;
-      so.rx0 = r.rx0;
-      so.ry0 = r.ry0;
-      so.kx0 = r.kx0;
-      so.ky0 = r.ky0;
-      so.kx1 = r.kx1;
-      so.ky1 = r.ky1;
-      so.src_u8 = src_u8;
-      so.dst_u8 = dst_u8;
-      launch_conv<64, 48, CONV_SHUFFLE>(dev_, in, count, mw, mh, p, s);
-      mark(-1, s);
+      const Layer& L = layers_[i];
+      p.weights = L.w.as<uint16_t>();
+      p.bias = L.b.as<float>();
+      p.slope = L.s.get() ? L.s.as<float>() : nullptr;
+      p.slope_unit = L.slope_unit;
+      p.out = out;
+      mark(i == 0 ? 1 : i < STEPS - 1 ? 2 : 3, s);
+      if (i == 0) {
+        launch_conv<16, 64, CONV_PRELU>(dev_, in, count, mw, mh, p, s);
+      } else if (i < STEPS - 1) {
+        launch_conv<64, 64, CONV_PRELU>(dev_, in, count, mw, mh, p, s);
+      } else {
+        ShuffleOut& so = p.shuffle;
+        so.src = src;
+        so.dst = dst;
+        so.src_w = src_w;
+        so.src_h = src_h;
+        so.rx0 = r.rx0;
+        so.ry0 = r.ry0;
+        so.kx0 = r.kx0;
+        so.ky0 = r.ky0;
+        so.kx1 = r.kx1;
+        so.ky1 = r.ky1;
+        so.src_u8 = src_u8;
+        so.dst_u8 = dst_u8;
+        launch_conv<64, 48, CONV_SHUFFLE>(dev_, in, count, mw, mh, p, s);
+        mark(-1, s);
+      }
     }
     in = out;
     if (step) {
       // Two slots, as the reference's Steps (native-vulkan lib.rs:521-572):
-      // layer i is queued before layer i - 1 is waited for and reported, so
-      // the progress reports cost the GPU no idle time.
-      IEC_CUDA(cudaEventRecord(layer_events_[i], s));
-      if (i >= 1) {
-        dev_.wait_event(layer_events_[i - 1]);
-        if (!step()) {
-          cancelled = true;
-          break;
-        }
+      // unit u is queued before unit u - 1 is waited for and its layers
+      // reported, so the progress reports cost the GPU no idle time.
+      IEC_CUDA(cudaEventRecord(layer_events_[u], s));
+      if (u >= 1) {
+        dev_.wait_event(layer_events_[u - 1]);
+        for (int k = 0; k < units[u - 1][1] && !cancelled; k++) cancelled = !step();
+        if (cancelled) break;
       }
     }
   }
   if (step && !cancelled) {
-    dev_.wait_event(layer_events_[STEPS - 1]);
+    dev_.wait_event(layer_events_[units.size() - 1]);
     if (!step()) cancelled = true;
   }
   if (cancelled) dev_.sync(s);  // nothing may still use the buffers
@@ -475,7 +481,7 @@ size_t RealEsrgan::launches(size_t count, size_t width, size_t height) const {
   size_t n = 0;
   for (size_t c0 = 0; c0 < count; c0 += chunk) {
     const int m = (int)std::min(chunk, count - c0);
-    n += body_fits(m, (int)width, (int)height) ? 4 : STEPS + 1;
+    n += body_fits(m, (int)width, (int)height, STEPS - 2) ? 4 : STEPS + 1;
   }
   return n;
 }

@@ -87,17 +87,20 @@ class RealEsrgan {
   void ensure_maps(size_t count, int w, int h, cudaStream_t stream);
   // The 32 body layers as one persistent launch (conv3x3_body_sm100.cuh):
   // whether a pass of this size takes it, and the launch.
-  bool body_fits(int count, int w, int h) const;
-  void launch_body(int count, int mw, int mh, const Region& r, cudaStream_t stream);
+  bool body_fits(int count, int w, int h, int layers_per_launch) const;
+  // Body layers first .. first + layers - 1 (0-based within the body).
+  void launch_body(int count, int mw, int mh, const Region& r, int first, int layers, cudaStream_t stream);
   // Record a timing event before a launch of `kind` (-1: after the last).
   void mark(int kind, cudaStream_t stream);
 
   Device dev_;
   std::vector<Layer> layers_;
   DeviceBuffer prep_, map_a_, map_b_, rows_, items_;
-  std::array<int, 3> items_key_ = {0, 0, 0};  // pass shape the item table in items_ was built for
+  std::array<int, 4> items_key_ = {0, 0, 0, 0};  // pass shape (count, w, h, layers) of items_'s table
   // Images per layer sweep of the fused body: their two maps stay in L2.
   static constexpr int BODY_GROUP = 2;
+  // Body layers per fused launch in passes with progress reports.
+  static constexpr int BODY_STAGE = 8;
   bool body_pdl_ = true;   // the fused launch also takes programmatic dependent launch
   bool no_fuse_ = false;   // per-layer launches only (set_fused)
   size_t map_pixels_ = 0;

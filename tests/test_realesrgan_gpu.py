@@ -225,3 +225,21 @@ def test_fused_body_is_the_path_taken(gpu_model):
         gpu_model.set_timing(0)
     assert list(kinds) == [0, 1, 4, 3]
     assert (ms > 0).all()
+
+
+def test_progress_runs_use_fused_stages_with_the_same_output(gpu_model):
+    # With a progress callback the body runs as fused launches of 8 layers,
+    # the 8 reports following each launch: still one report per layer, in
+    # order, and the per-layer launches' output bit for bit.
+    image = W.realesrgan_input(200, 120, 31)
+    seen = []
+    staged = gpu_model.run_float_tiled(image, 256, 34, lambda f: seen.append(f) or False)
+    assert len(seen) == 34 and seen[-1] == 1.0
+    assert all(a < b for a, b in zip(seen, seen[1:]))
+    gpu_model.set_fused(False)
+    try:
+        layered = gpu_model.run_float_tiled(image, 256, 34, lambda f: False)
+    finally:
+        gpu_model.set_fused(True)
+    assert np.array_equal(staged.view(np.uint32), layered.view(np.uint32))
+    assert np.array_equal(staged.view(np.uint32), gpu_model.run_float(image).view(np.uint32))
