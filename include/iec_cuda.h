@@ -161,10 +161,11 @@ size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t
 iec_status iec_realesrgan_set_timing(iec_realesrgan* model, size_t capacity);
 size_t iec_realesrgan_timing(iec_realesrgan* model, int* kinds, float* ms, size_t n);
 
-/* Passes without per-layer progress reports run the 32 64->64 layers as one
- * persistent launch (the default, `on` = 1) or, with `on` = 0, as 32
- * launches like passes with progress reports do. The outputs are identical;
- * this switch exists to compare the two. */
+/* The 32 64->64 layers run as fused persistent launches (the default, `on` =
+ * 1: one per pass, or four of 8 layers in passes with progress reports, each
+ * launch's layers reported when it completes) or, with `on` = 0, as 32
+ * launches. The outputs are identical; this switch exists to compare the
+ * two. */
 iec_status iec_realesrgan_set_fused(iec_realesrgan* model, int on);
 
 /* ------------------------------------------------------------------ SCUNet
