@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * CONV_ACC_COLS);
       // out(r, c) = Q_0(r, c - 1) + Q_1(r, c) + Q_2(r, c + 1) (neighbouring lanes)
-      float v[16];
+      float2 v[8];  // channel pairs
       {
         uint32_t q0[16], q1[16], q2[16];
         const uint32_t col = (uint32_t)(part * 16);
@@ -346,10 +346,12 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
         tmem_ld16(taddr + 128u + col, q2);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-          const float left = __shfl_up_sync(0xffffffffu, __uint_as_float(q0[e]), 1);
-          const float right = __shfl_down_sync(0xffffffffu, __uint_as_float(q2[e]), 1);
-          v[e] = (left + __uint_as_float(q1[e])) + right;
+        for (int e = 0; e < 8; e++) {
+          const float2 left = make_float2(__shfl_up_sync(0xffffffffu, __uint_as_float(q0[2 * e]), 1),
+                                          __shfl_up_sync(0xffffffffu, __uint_as_float(q0[2 * e + 1]), 1));
+          const float2 right = make_float2(__shfl_down_sync(0xffffffffu, __uint_as_float(q2[2 * e]), 1),
+                                           __shfl_down_sync(0xffffffffu, __uint_as_float(q2[2 * e + 1]), 1));
+          v[e] = fadd2(fadd2(left, make_float2(__uint_as_float(q1[2 * e]), __uint_as_float(q1[2 * e + 1]))), right);
         }
       }
       tc_fence_before();
@@ -365,14 +367,15 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 4; e++) {
             const int q = g * 8 + 2 * e;
-            float v0 = v[q] + r_bias[q];
-            float v1 = v[q + 1] + r_bias[q + 1];
+            const float2 w = fadd2(v[q / 2], make_float2(r_bias[q], r_bias[q + 1]));
+            float v0, v1;
             if (unit) {
-              v0 = fmaxf(v0, v0 * r_slope[q]);
-              v1 = fmaxf(v1, v1 * r_slope[q + 1]);
+              const float2 sw = fmul2(w, make_float2(r_slope[q], r_slope[q + 1]));
+              v0 = fmaxf(w.x, sw.x);
+              v1 = fmaxf(w.y, sw.y);
             } else {
-              v0 = v0 < 0.0f ? v0 * r_slope[q] : v0;
-              v1 = v1 < 0.0f ? v1 * r_slope[q + 1] : v1;
+              v0 = w.x < 0.0f ? w.x * r_slope[q] : w.x;
+              v1 = w.y < 0.0f ? w.y * r_slope[q + 1] : w.y;
             }
             __half2 h = __floats2half2_rn(v0, v1);
             packed[e] = *reinterpret_cast<uint32_t*>(&h);

@@ -281,10 +281,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         tmem_ld16(taddr + (uint32_t)(2 * COUT) + col, q2);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-          const float left = __shfl_up_sync(0xffffffffu, __uint_as_float(q0[e]), 1);
-          const float right = __shfl_down_sync(0xffffffffu, __uint_as_float(q2[e]), 1);
-          v[e] = (left + __uint_as_float(q1[e])) + right;
+        for (int e = 0; e < 16; e += 2) {
+          const float2 left = make_float2(__shfl_up_sync(0xffffffffu, __uint_as_float(q0[e]), 1),
+                                          __shfl_up_sync(0xffffffffu, __uint_as_float(q0[e + 1]), 1));
+          const float2 right = make_float2(__shfl_down_sync(0xffffffffu, __uint_as_float(q2[e]), 1),
+                                           __shfl_down_sync(0xffffffffu, __uint_as_float(q2[e + 1]), 1));
+          const float2 sum =
+              fadd2(fadd2(left, make_float2(__uint_as_float(q1[e]), __uint_as_float(q1[e + 1]))), right);
+          v[e] = sum.x;
+          v[e + 1] = sum.y;
         }
       } else {
         // output row i = part of the pixel shuffle needs channels
@@ -326,14 +331,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 4; e++) {
             const int k = g * 8 + 2 * e;
-            float v0 = v[k] + r_bias[k];
-            float v1 = v[k + 1] + r_bias[k + 1];
+            const float2 w = fadd2(make_float2(v[k], v[k + 1]), make_float2(r_bias[k], r_bias[k + 1]));
+            float v0, v1;
             if (slope_unit) {
-              v0 = fmaxf(v0, v0 * r_slope[k]);
-              v1 = fmaxf(v1, v1 * r_slope[k + 1]);
+              const float2 sw = fmul2(w, make_float2(r_slope[k], r_slope[k + 1]));
+              v0 = fmaxf(w.x, sw.x);
+              v1 = fmaxf(w.y, sw.y);
             } else {
-              v0 = v0 < 0.0f ? v0 * r_slope[k] : v0;
-              v1 = v1 < 0.0f ? v1 * r_slope[k + 1] : v1;
+              v0 = w.x < 0.0f ? w.x * r_slope[k] : w.x;
+              v1 = w.y < 0.0f ? w.y * r_slope[k + 1] : w.y;
             }
             __half2 h = __floats2half2_rn(v0, v1);
             packed[e] = *reinterpret_cast<uint32_t*>(&h);
