@@ -312,7 +312,9 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
     const int part = (warp - 2) >> 2;        // channels 16 part .. 16 part + 15
     const int row = quarter * 32 + lane;     // M row = partial-sum position (r, c) of the tile
     const int pr = row / CONV_HALO_W, pc = row % CONV_HALO_W;
-    const size_t plane = (size_t)p.MH * p.MW;
+    const size_t plane8 = (size_t)p.MH * p.MW * 8;         // halves per channel-group plane
+    const size_t img_stride = 8 * plane8;                    // halves per image (8 groups)
+    const size_t group_off = (size_t)(part * 2) * plane8;    // this warp's first group
     float r_bias[16], r_slope[16];
     bool unit = false;
     int cur = -1, i = 0;
@@ -360,7 +362,10 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
 
       const int y = it.ty * CONV_TILE_H + pr, x = it.tx * CONV_TILE_W + pc - 1;
       if (pc >= 1 && pc <= CONV_TILE_W && y < p.H && x < p.W) {
-        __half* base = p.maps[(cur + 1) & 1] + ((size_t)it.img * 8 * plane + (size_t)y * p.MW + x) * 8;
+        // this thread's two channel groups of pixel (y, x): plane offsets
+        // hoisted out of the item loop, the pixel offset in 32 bits
+        __half* base = p.maps[(cur + 1) & 1] + (size_t)it.img * img_stride + group_off +
+                       (size_t)(((uint32_t)y * (uint32_t)p.MW + (uint32_t)x) * 8u);
 #pragma unroll
         for (int g = 0; g < 2; g++) {
           uint32_t packed[4];
@@ -380,8 +385,7 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
             __half2 h = __floats2half2_rn(v0, v1);
             packed[e] = *reinterpret_cast<uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(base + (size_t)(part * 2 + g) * plane * 8) =
-              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint4*>(base + (g ? plane8 : 0)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
       }
       // This warp's share of the tile is stored: publish it to the signaller.
