@@ -95,6 +95,51 @@ extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int w
   }
 }
 
+namespace {
+
+// A wait that nothing ends: an mbarrier no thread arrives on (which 0), or a
+// shared word no warp publishes (which 1, the fused body's wait for ready
+// items). The bounded wait gives up after IEC_WAIT_NS, sets the error word
+// and returns; the kernel then exits normally.
+__global__ void selftest_wait_kernel(int which, int* dev_err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  __shared__ uint32_t word;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    word = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    volatile int* flag = &abort_flag;
+    if (which == 0)
+      mbar_wait(&bar, 0, flag, dev_err, DEV_ERR_WAIT_FULL);
+    else
+      wait_word(&word, 0, flag, dev_err, DEV_ERR_WAIT_ROWS);
+  }
+}
+
+}  // namespace
+
+extern "C" iec_status iec_selftest_wait_timeout(int device, int which) {
+  try {
+    if (which != 0 && which != 1) throw Error(ERR_INPUT, "wait self-test: which is 0 or 1");
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    cudaStream_t s = dev.stream();
+    selftest_wait_kernel<<<1, 32, 0, s>>>(which, dev.dev_err());
+    IEC_CUDA(cudaGetLastError());
+    dev.sync(s);  // reads the error word back: IEC_ERR_TIMEOUT
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
 extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, int two_pass, float* spec,
                                          float* back) {
   try {

@@ -124,6 +124,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Shared words published between warps of one CTA (release / acquire at
+// CTA scope), and a bounded wait on one.
+__device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_cta(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_add_gpu(int* p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until the shared word `w` exceeds `i` (a counter another warp
+// of the CTA publishes with release); short sleeps between polls leave the
+// issue slots to the epilogue warps.
+__device__ __forceinline__ bool wait_word(const uint32_t* w, uint32_t i, volatile int* abort_flag, int* dev_err,
+                                          int code) {
+  if (ld_acquire_cta(w) > i) return true;
+  const uint64_t start = global_ns();
+  for (uint32_t n = 1;; n++) {
+    if (ld_acquire_cta(w) > i) return true;
+    __nanosleep(32);
+    if ((n & 63) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - start > IEC_WAIT_NS) {
+        *abort_flag = 1;
+        atomicOr(dev_err, code);
+        return false;
+      }
+    }
+  }
+}
+
 // n / d for n < 2^24 and 0 < d < 2^16 by one 64-bit multiply: m = ceil(2^40
 // / d) makes n * m / 2^40 exceed n / d by less than 2^-16 < 1 / d.
 struct FastDiv {

@@ -75,6 +75,8 @@ def lib():
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
         L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          f32p, f32p]
+        L.iec_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.iec_selftest_wait_timeout.restype = ctypes.c_int
         L.iec_selftest_gemm_time.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)]
         L.iec_selftest_attention.argtypes = [i32, f32p, i32, i32, f32p, i32, i32, i32, f32p]
         L.iec_scunet_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(Options), ctypes.POINTER(vp)]
@@ -434,6 +436,12 @@ def selftest_rfft2(x: np.ndarray, device: int = -1, two_pass: bool = False):
     back = np.empty_like(x)
     _check(lib().iec_selftest_rfft2(device, _f32(x), h, w, c, 1 if two_pass else 0, _f32(spec), _f32(back)))
     return spec, back
+
+
+def selftest_wait_timeout(which: int, device: int = -1) -> int:
+    """Status of a kernel whose bounded wait nothing ends (0: an mbarrier,
+    1: a shared word); IEC_ERR_TIMEOUT when the bound works."""
+    return lib().iec_selftest_wait_timeout(device, which)
 
 
 def selftest_gemm_time(mode: int, m_or_h: int, w: int, k: int, n: int, out_map: bool = False, sources: int = 0,

@@ -288,6 +288,14 @@ iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, int w, int k
 iec_status iec_selftest_attention(int device, const float* qkv, int windows, int c, const float* bias,
                                   int shifted, int rows_w, int cols_w, float* out);
 
+/* Diagnostics: failure detection without a fault. One kernel waits on
+ * something nothing provides (`which` 0: an mbarrier no thread arrives on;
+ * 1: a shared word no warp publishes, as the fused Real-ESRGAN body's
+ * producer waits for ready items); its bounded wait gives up after about 2 s,
+ * sets the device error word and returns, and the call returns
+ * IEC_ERR_TIMEOUT. The CUDA context stays usable. */
+iec_status iec_selftest_wait_timeout(int device, int which);
+
 #ifdef __cplusplus
 }
 #endif
