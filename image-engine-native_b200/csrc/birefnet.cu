@@ -624,6 +624,7 @@ Birefnet::~Birefnet() {
     if (prev >= 0) cudaSetDevice(prev);
   }
   if (dev_.poisoned()) {
+    graph_.leak();
     for (BackboneBuffers& bb : bb_)
       for (DeviceBuffer* b : {&bb.patch_rows, &bb.x, &bb.tok, &bb.qkv, &bb.att, &bb.ln, &bb.hid, &bb.mrg}) b->leak();
     for (int i = 0; i < 3; i++) {
@@ -640,6 +641,7 @@ Birefnet::~Birefnet() {
 
 void Birefnet::ensure(int side) {
   if (side == alloc_side_) return;
+  alloc_gen_++;  // buffers may move: captured passes must not replay
   const long long g0 = side / 4, P0 = g0 * g0;
   auto bytes = [](long long planes, long long elems) { return (size_t)(planes * elems * 2); };
   img_.reserve((size_t)side * side * 3 * 4);
@@ -868,6 +870,14 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
 }
 
 void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStream_t s) {
+  // Replayed as a graph while the same buffers and size repeat (PassGraph).
+  graph_.run({(long long)(uintptr_t)image, u8, side, (long long)(uintptr_t)logits, (long long)alloc_gen_,
+              (long long)dev_.scratch_generation()},
+             s,
+             [&](cudaStream_t st) { run_pass(image, u8, side, logits, st); });
+}
+
+void Birefnet::run_pass(const void* image, bool u8, int side, float* logits, cudaStream_t s) {
   if (side <= 0 || side % 64 != 0)
     throw Error(ERR_INPUT, "side " + std::to_string(side) + " is not a positive multiple of 64");
   ensure(side);

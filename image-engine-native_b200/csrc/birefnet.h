@@ -43,6 +43,7 @@ class Birefnet {
 
  private:
   void ensure(int side);
+  void run_pass(const void* image, bool u8, int side, float* logits, cudaStream_t s);
   // The backbone's working buffers (one set per concurrent pass).
   struct BackboneBuffers {
     DeviceBuffer patch_rows, x, tok, qkv, att, ln, hid, mrg;
@@ -79,6 +80,8 @@ class Birefnet {
   // the four levels, and the ASPP's small branches.
   cudaStream_t s_half_ = nullptr, s_patch_ = nullptr, s_aspp_ = nullptr;
   cudaEvent_t ev_prep_ = nullptr, ev_half_ = nullptr, ev_t_ = nullptr, ev_aspp_ = nullptr, ev_patch_[4] = {};
+  PassGraph graph_;
+  uint64_t alloc_gen_ = 0;  // counts ensure()'s reallocations
 };
 
 }  // namespace iec

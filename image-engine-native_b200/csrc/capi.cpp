@@ -346,8 +346,7 @@ iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t w
     Scunet& m = *model->model;
     DeviceScope scope(m.device());
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
-    m.run_region(image, false, out, false, (int)width, (int)height, 0, 0, (int)width, (int)height, 0, 0, (int)width,
-                 (int)height, nullptr, s);
+    m.run_whole_device(image, out, (int)width, (int)height, s);
   });
 }
 

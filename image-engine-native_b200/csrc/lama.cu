@@ -212,6 +212,7 @@ Lama::Lama(const std::string& path, const Options& opt) : dev_(opt) {
 
 Lama::~Lama() {
   if (dev_.poisoned()) {
+    graph_.leak();
     for (DeviceBuffer* b : {&in0_, &d0_, &d1_, &d2_, &x_, &mid_, &tmp_, &spectral_, &spectrum_, &filtered_, &u0_,
                             &u1_, &u2_, &out_, &host_in, &host_mask, &host_out, &plan_.twiddles, &plan_.scratch})
       b->leak();
@@ -230,6 +231,7 @@ Lama::~Lama() {
 
 void Lama::ensure(int hp, int wp) {
   if (hp == alloc_h_ && wp == alloc_w_) return;
+  alloc_gen_++;  // buffers may move: captured passes must not replay
   const int h8 = hp / 8, w8 = wp / 8, half = w8 / 2 + 1;
   auto bytes = [](long long planes, long long elems) { return (size_t)(planes * elems * 2); };
   in0_.reserve(bytes(4, (long long)(hp + 6) * wp * 8));
@@ -304,6 +306,17 @@ void Lama::ffc(const Ffc& F, const __half* in, __half* out, __half* tmp, bool re
 }
 
 bool Lama::run(const void* image, bool image_u8, const void* mask, bool mask_u8, void* dst, bool dst_u8, int width,
+               int height, const std::function<bool()>& step, cudaStream_t s) {
+  // Progress reports wait on the GPU between steps: those passes run as plain
+  // launches; the others replay as a graph (PassGraph).
+  if (step) return run_pass(image, image_u8, mask, mask_u8, dst, dst_u8, width, height, step, s);
+  graph_.run({(long long)(uintptr_t)image, image_u8, (long long)(uintptr_t)mask, mask_u8, (long long)(uintptr_t)dst,
+              dst_u8, width, height, (long long)alloc_gen_, (long long)dev_.scratch_generation()},
+             s, [&](cudaStream_t st) { run_pass(image, image_u8, mask, mask_u8, dst, dst_u8, width, height, {}, st); });
+  return true;
+}
+
+bool Lama::run_pass(const void* image, bool image_u8, const void* mask, bool mask_u8, void* dst, bool dst_u8, int width,
                int height, const std::function<bool()>& step, cudaStream_t s) {
   if (width < MIN_SIDE || height < MIN_SIDE)
     throw Error(ERR_INPUT, std::to_string(width) + " x " + std::to_string(height) + " image: sides of at least " +

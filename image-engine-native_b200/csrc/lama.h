@@ -49,6 +49,8 @@ class Lama {
 
  private:
   void ensure(int hp, int wp);
+  bool run_pass(const void* image, bool image_u8, const void* mask, bool mask_u8, void* dst, bool dst_u8, int width,
+                int height, const std::function<bool()>& step, cudaStream_t s);
   void ffc(const Ffc& f, const __half* in, __half* out, __half* tmp, bool residual, cudaStream_t s);
 
   Device dev_;
@@ -63,6 +65,8 @@ class Lama {
   // beside the cross convolution (each alone fills a fraction of the GPU).
   cudaStream_t s_local_ = nullptr, s_spec_ = nullptr;
   cudaEvent_t ev_in_ = nullptr, ev_local_ = nullptr, ev_spec_ = nullptr;
+  PassGraph graph_;
+  uint64_t alloc_gen_ = 0;  // counts ensure()'s reallocations  // passes without progress reports
 };
 
 }  // namespace iec

@@ -315,6 +315,64 @@ void Device::check_device_errors() {
   }
 }
 
+// --------------------------------------------------------------- graphs
+PassGraph::~PassGraph() { reset(); }
+
+void PassGraph::reset() {
+  for (auto& e : entries_)
+    if (e.exec) cudaGraphExecDestroy(e.exec);
+  entries_.clear();
+}
+
+void PassGraph::run(const std::vector<long long>& key, cudaStream_t s,
+                    const std::function<void(cudaStream_t)>& body) {
+  if (!enabled) return body(s);
+  Entry* hit = nullptr;
+  for (auto& e : entries_)
+    if (e.key == key) hit = &e;
+  if (!hit) {
+    if (entries_.size() == MAX_ENTRIES) {
+      auto lru = entries_.begin();
+      for (auto it = entries_.begin(); it != entries_.end(); ++it)
+        if (it->used < lru->used) lru = it;
+      if (lru->exec) cudaGraphExecDestroy(lru->exec);
+      entries_.erase(lru);
+    }
+    entries_.push_back(Entry{key, 0, nullptr, 0});
+    hit = &entries_.back();
+  }
+  hit->used = ++clock_;
+  if (hit->exec) {
+    IEC_CUDA(cudaGraphLaunch(hit->exec, s));
+    return;
+  }
+  if (hit->seen++ == 0) return body(s);  // the warm run: allocations, attributes
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  IEC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+  try {
+    body(s);
+  } catch (...) {
+    cudaStreamEndCapture(s, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    (void)cudaGetLastError();
+    enabled = false;
+    throw;
+  }
+  cudaError_t e = cudaStreamEndCapture(s, &graph);
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    // Not capturable here: run it the plain way from now on (the captured
+    // launches did not execute).
+    (void)cudaGetLastError();
+    enabled = false;
+    return body(s);
+  }
+  hit->exec = exec;
+  IEC_CUDA(cudaGraphLaunch(exec, s));
+}
+
 // ------------------------------------------------------------ tensor maps
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,

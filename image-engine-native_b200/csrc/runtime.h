@@ -15,6 +15,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <map>
 #include <stdexcept>
 #include <string>
@@ -161,13 +162,20 @@ class Device {
   void* scratch(size_t bytes, cudaStream_t stream) {
     for (auto& e : scratch_)
       if (e.first == stream) {
-        if (e.second.size() < bytes) e.second.reserve(bytes);
+        if (e.second.size() < bytes) {
+          e.second.reserve(bytes);
+          scratch_gen_++;
+        }
         return e.second.get();
       }
     scratch_.emplace_back(stream, DeviceBuffer());
     scratch_.back().second.reserve(bytes);
+    scratch_gen_++;
     return scratch_.back().second.get();
   }
+  // Counts the scratch buffers' (re)allocations (a captured pass that used
+  // an older one must not replay).
+  uint64_t scratch_generation() const { return scratch_gen_; }
 
  private:
   int ordinal_ = 0;
@@ -179,11 +187,41 @@ class Device {
   cudaStream_t copy_stream_ = nullptr;
   DeviceBuffer dev_err_;
   std::vector<std::pair<cudaStream_t, DeviceBuffer>> scratch_;
+  uint64_t scratch_gen_ = 0;
   PinnedBuffer host_err_;
   std::string poisoned_;
 };
 
 // RAII: make the device current for a call and restore the caller's.
+// Model passes kept as CUDA graphs: hundreds of small launches replay with
+// less per-launch cost. A pass runs eagerly the first time its key is seen
+// (that run makes every allocation), is captured the second time and
+// replayed after that. The key holds the shapes, the caller's buffers and
+// the generations of the model's and the device's allocations, so a graph
+// never replays over buffers that have moved; the four most recent keys
+// keep their graphs. A pass that cannot be captured turns the graphs off
+// for the model.
+class PassGraph {
+ public:
+  ~PassGraph();
+  void run(const std::vector<long long>& key, cudaStream_t s, const std::function<void(cudaStream_t)>& body);
+  void reset();
+  // a poisoned device: nothing is freed under possibly running work
+  void leak() { entries_.clear(); }
+  bool enabled = true;
+
+ private:
+  struct Entry {
+    std::vector<long long> key;
+    int seen = 0;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t used = 0;
+  };
+  static constexpr size_t MAX_ENTRIES = 4;
+  std::vector<Entry> entries_;
+  uint64_t clock_ = 0;
+};
+
 class DeviceScope {
  public:
   explicit DeviceScope(Device& d);

@@ -225,6 +225,7 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
 
 Scunet::~Scunet() {
   if (dev_.poisoned()) {
+    graph_.leak();
     for (DeviceBuffer* b : {&img_, &x_, &y_, &t_, &tok_, &qkv_, &att_, &ln2_, &hid_, &gat_, &skip_[0], &skip_[1],
                             &skip_[2], &out_, &host_in, &host_out})
       b->leak();
@@ -243,6 +244,7 @@ Scunet::~Scunet() {
 void Scunet::ensure(int ph, int pw) {
   const long long P = (long long)ph * pw;
   if (P <= alloc_pixels_) return;
+  alloc_gen_++;  // buffers may move: captured passes must not replay
   // Per level (c channels, Pl pixels): the largest need of each buffer, in
   // planes x max(rows, 128) x 8 halves.
   auto bytes = [](long long planes, long long rows) { return (size_t)(planes * rows_alloc(rows) * 8 * 2); };
@@ -450,6 +452,15 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
   return true;
 }
 
+void Scunet::run_whole_device(const float* src, float* dst, int width, int height, cudaStream_t s) {
+  graph_.run({(long long)(uintptr_t)src, (long long)(uintptr_t)dst, width, height, -1, (long long)alloc_gen_,
+              (long long)dev_.scratch_generation()},
+             s, [&](cudaStream_t st) {
+               run_region(src, false, dst, false, width, height, 0, 0, width, height, 0, 0, width, height, nullptr,
+                          st);
+             });
+}
+
 void Scunet::run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_u8, size_t width, size_t height,
                               size_t tile, size_t margin, const std::function<bool(float)>& progress,
                               cudaStream_t s) {
@@ -459,18 +470,28 @@ void Scunet::run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_
   size_t done = 0;
   std::function<bool()> step;
   if (progress) step = [&] { return progress((float)(++done) / steps); };
-  for (size_t j = 0; j < rows; j++) {
-    const size_t y0 = j * height / rows, y1 = (j + 1) * height / rows;
-    for (size_t i = 0; i < cols; i++) {
-      const size_t x0 = i * width / cols, x1 = (i + 1) * width / cols;
-      const size_t rx0 = x0 > margin ? x0 - margin : 0, ry0 = y0 > margin ? y0 - margin : 0;
-      const size_t rx1 = margin > width - x1 ? width : x1 + margin;
-      const size_t ry1 = margin > height - y1 ? height : y1 + margin;
-      if (!run_region(src, src_u8, dst, dst_u8, (int)width, (int)height, (int)rx0, (int)ry0, (int)(rx1 - rx0),
-                      (int)(ry1 - ry0), (int)(x0 - rx0), (int)(y0 - ry0), (int)(x1 - rx0), (int)(y1 - ry0), step, s))
-        throw Error(CANCELLED, "cancelled");
+  auto pass = [&](cudaStream_t st) {
+    for (size_t j = 0; j < rows; j++) {
+      const size_t y0 = j * height / rows, y1 = (j + 1) * height / rows;
+      for (size_t i = 0; i < cols; i++) {
+        const size_t x0 = i * width / cols, x1 = (i + 1) * width / cols;
+        const size_t rx0 = x0 > margin ? x0 - margin : 0, ry0 = y0 > margin ? y0 - margin : 0;
+        const size_t rx1 = margin > width - x1 ? width : x1 + margin;
+        const size_t ry1 = margin > height - y1 ? height : y1 + margin;
+        if (!run_region(src, src_u8, dst, dst_u8, (int)width, (int)height, (int)rx0, (int)ry0, (int)(rx1 - rx0),
+                        (int)(ry1 - ry0), (int)(x0 - rx0), (int)(y0 - ry0), (int)(x1 - rx0), (int)(y1 - ry0), step,
+                        st))
+          throw Error(CANCELLED, "cancelled");
+      }
     }
-  }
+  };
+  // Progress reports wait on the GPU between blocks: those passes run as
+  // plain launches; the others replay as a graph (PassGraph).
+  if (progress) return pass(s);
+  graph_.run({(long long)(uintptr_t)src, src_u8, (long long)(uintptr_t)dst, dst_u8, (long long)width,
+              (long long)height, (long long)tile, (long long)margin, (long long)alloc_gen_,
+              (long long)dev_.scratch_generation()},
+             s, pass);
 }
 
 }  // namespace iec

@@ -37,6 +37,9 @@ class Scunet {
   bool run_region(const void* src, bool src_u8, void* dst, bool dst_u8, int src_w, int src_h, int rx0, int ry0,
                   int rw, int rh, int kx0, int ky0, int kx1, int ky1, const std::function<bool()>& step,
                   cudaStream_t s);
+  // run_region over a whole f32 image on device buffers, replayed as a graph
+  // while the buffers and size repeat (PassGraph).
+  void run_whole_device(const float* src, float* dst, int width, int height, cudaStream_t s);
   // lib.rs:160-247: tiles of `tile` with `margin` context.
   void run_tiled_device(const void* src, bool src_u8, void* dst, bool dst_u8, size_t width, size_t height, size_t tile,
                         size_t margin, const std::function<bool(float)>& progress, cudaStream_t s);
@@ -60,6 +63,8 @@ class Scunet {
   // attention half.
   cudaStream_t s_conv_ = nullptr;
   cudaEvent_t ev_in_ = nullptr, ev_conv_ = nullptr;
+  PassGraph graph_;
+  uint64_t alloc_gen_ = 0;  // counts ensure()'s reallocations  // passes without progress reports
 };
 
 }  // namespace iec
