@@ -117,7 +117,7 @@ struct BodySmem {
   static constexpr int BAR_OFF = A_OFF + BODY_NSTAGE * STAGE_BYTES;
   // full[NSTAGE], empty[NSTAGE], acc_full[2], acc_empty[2], wfull[2], wempty[2]
   static constexpr int NBARS = 2 * BODY_NSTAGE + 8;
-  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;          // tmem slot, abort flag, ready
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;          // tmem slot, abort flag, ready, want
   static constexpr int PROGRESS_OFF = MISC_OFF + 16;              // [16] items stored per epilogue warp
   static constexpr int TOTAL = PROGRESS_OFF + 4 * CONV_EPI_WARPS;
   static constexpr int DYN_BYTES = TOTAL + 1024;                // room to align the base
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
       int s = 0, cur = -1, nw = 0, i = 0;
       uint32_t phase = 0;
       int issued[BODY_NSTAGE], wissued[2] = {-1, -1};
-      for (int i = 0; i < BODY_NSTAGE; i++) issued[i] = -1;
+      for (int j = 0; j < BODY_NSTAGE; j++) issued[j] = -1;
       for (int k = blockIdx.x; k < p.items; k += gridDim.x, i++) {
         const BodyItem it = body_item(p, k);
         *want = (uint32_t)i;
@@ -218,8 +218,8 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
         }
       }
       // No copy may still be writing shared memory when the CTA exits.
-      for (int i = 0; i < BODY_NSTAGE; i++)
-        if (issued[i] >= 0) mbar_wait(&full[i], (uint32_t)issued[i], abort_flag, p.dev_err, 0);
+      for (int j = 0; j < BODY_NSTAGE; j++)
+        if (issued[j] >= 0) mbar_wait(&full[j], (uint32_t)issued[j], abort_flag, p.dev_err, 0);
       for (int b = 0; b < 2; b++)
         if (wissued[b] >= 0) mbar_wait(&wfull[b], (uint32_t)wissued[b], abort_flag, p.dev_err, 0);
     }
