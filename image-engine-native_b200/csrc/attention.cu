@@ -28,7 +28,7 @@ namespace iec {
 
 namespace {
 
-constexpr int TOK = 64, HD = 32, PITCH = HD + 8;  // smem row pitch in halves (80 bytes)
+constexpr int TOK = 64, HD = 32;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -59,23 +59,36 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __restrict__ qkv, long long qkv_plane,
                                                                int c, const float* __restrict__ bias, int shifted,
                                                                int rows_w, int cols_w, __half* __restrict__ out,
-                                                               long long out_plane) {
-  griddep_wait();
-  griddep_launch_dependents();
-  __shared__ __align__(16) __half sq[TOK * PITCH], sk[TOK * PITCH], sv[TOK * PITCH];
+                                                               long long out_plane, int* dev_err) {
+  // Q, K, V of this head as 12 planes of [64 tokens][8]: plane 4 w + g is
+  // channel group g of q (w 0), k (1) or v (2). Each is a contiguous 1 KB
+  // run of the planar qkv map, brought by one bulk copy (the 8 x 8 blocks
+  // ldmatrix reads are then 128 contiguous bytes: no bank conflicts).
+  __shared__ __align__(128) __half sm[12 * TOK * 8];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
   const int win = blockIdx.x, head = blockIdx.y, heads = gridDim.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row0 = (long long)win * TOK;
-  // Q, K, V of this head: 64 tokens x 4 channel groups each.
-  for (int i = threadIdx.x; i < 3 * TOK * 4; i += 128) {
-    const int which = i / (TOK * 4), r = i % (TOK * 4);
-    const int t = r >> 2, g = r & 3;
-    const int plane = which * (c / 8) + head * 4 + g;
-    const uint4 v = *reinterpret_cast<const uint4*>(qkv + plane * qkv_plane + (row0 + t) * 8);
-    __half* dst = (which == 0 ? sq : which == 1 ? sk : sv) + t * PITCH + g * 8;
-    *reinterpret_cast<uint4*>(dst) = v;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, 12 * TOK * 16);
+    for (int j = 0; j < 12; j++) {
+      const long long plane = (j >> 2) * (c / 8) + head * 4 + (j & 3);
+      bulk_load(sm + j * TOK * 8, qkv + plane * qkv_plane + row0 * 8, TOK * 16, &bar);
+    }
+  }
+  if (!mbar_wait(&bar, 0, &abort_flag, dev_err, DEV_ERR_WAIT_FULL)) return;
+  const __half* sq = sm;
+  const __half* sk = sm + 4 * TOK * 8;
+  const __half* sv = sm + 8 * TOK * 8;
 
   // The bias table of this window's class (swin.rs:154-159).
   int cls = 0;
@@ -92,15 +105,15 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
 #pragma unroll
   for (int kk = 0; kk < 2; kk++) {
     uint32_t a0, a1, a2, a3;
-    ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + (q0 + (lane & 15)) * PITCH + kk * 16 + (lane >> 4) * 8), a0, a1,
-            a2, a3);
+    ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8), a0,
+            a1, a2, a3);
 #pragma unroll
     for (int j = 0; j < 8; j += 2) {
       // keys 8j .. 8j + 15, dims 16 kk .. 16 kk + 15: two B fragments
       uint32_t b0, b1, b2, b3;
       const int key = 8 * j + (lane & 7) + ((lane >> 4) << 3);
-      const int dim = kk * 16 + ((lane >> 3) & 1) * 8;
-      ldsm_x4((uint32_t)__cvta_generic_to_shared(sk + key * PITCH + dim), b0, b1, b2, b3);
+      const int grp = kk * 2 + ((lane >> 3) & 1);  // dims 8 grp .. 8 grp + 7
+      ldsm_x4((uint32_t)__cvta_generic_to_shared(sk + grp * TOK * 8 + key * 8), b0, b1, b2, b3);
       mma16816(s[j], a0, a1, a2, a3, b0, b1);
       mma16816(s[j + 1], a0, a1, a2, a3, b2, b3);
     }
@@ -151,8 +164,8 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
       // tokens 16 kk .. 16 kk + 15, dims 8 j .. 8 j + 15, transposed
       uint32_t b0, b1, b2, b3;
       const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int dim = 8 * j + (lane >> 4) * 8;
-      ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv + tok * PITCH + dim), b0, b1, b2, b3);
+      const int grp = j + (lane >> 4);  // dims 8 grp .. 8 grp + 7
+      ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv + grp * TOK * 8 + tok * 8), b0, b1, b2, b3);
       mma16816(o[j], a0, a1, a2, a3, b0, b1);
       mma16816(o[j + 1], a0, a1, a2, a3, b2, b3);
     }
@@ -191,12 +204,13 @@ std::vector<float> attention_bias_layout(const std::vector<float>& tables) {
 }
 
 void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int windows, const float* bias,
-                      bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems,
+                      bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems, int* dev_err,
                       cudaStream_t s) {
   if (c % 32 != 0) throw Error(ERR_INPUT, "attention channels must be a multiple of 32");
   dim3 grid(windows, c / 32);
+  if ((qkv_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "attention planes must be 16-byte multiples");
   launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w, out,
-                                               out_plane_elems);
+             out_plane_elems, dev_err);
   IEC_CUDA(cudaGetLastError());
 }
 

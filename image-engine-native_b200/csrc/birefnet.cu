@@ -747,7 +747,7 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
       o.plane_elems = sp;
       gemm_rows(dev_, B.qkv, bb.tok.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
       window_attention(bb.qkv.as<__half>(), sp, c, (int)(slots / 64), B.bias.as<float>(), B.shifted, wins, wins,
-                       bb.att.as<__half>(), sp, s);
+                       bb.att.as<__half>(), sp, dev_.dev_err(), s);
       o.mode = OUT_WINDOW_ACCUM;
       o.out = x;
       o.plane_elems = xp;

@@ -127,6 +127,7 @@ void merge_layer_norm_planar(const __half* src, long long src_plane_elems, int g
 std::vector<float> attention_bias_layout(const std::vector<float>& tables);
 
 void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int windows, const float* bias,
-                      bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems, cudaStream_t s);
+                      bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems, int* dev_err,
+                      cudaStream_t s);
 
 }  // namespace iec

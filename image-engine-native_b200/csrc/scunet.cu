@@ -353,7 +353,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       o.out = qkv;
       o.plane0 = 0;
       gemm_rows(dev_, B.qkv, tok, pl, Pl, ACT_NONE, o, s);
-      window_attention(qkv, pl, h, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, att, pl, s);
+      window_attention(qkv, pl, h, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, att, pl, dev_.dev_err(), s);
       o.mode = OUT_WINDOW_ACCUM;
       o.out = y;
       o.plane0 = h / 8;

@@ -85,7 +85,7 @@ extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int w
     dev.sync(s);  // the host vector goes out of scope
     rows_to_planar(d32.as<float>(), rows, 3 * c, dq.as<__half>(), plane, s);
     window_attention(dq.as<__half>(), plane, c, windows, db.as<float>(), shifted != 0, rows_w, cols_w,
-                     dout.as<__half>(), plane, s);
+                     dout.as<__half>(), plane, dev.dev_err(), s);
     planar_to_rows(dout.as<__half>(), plane, rows, c, do32.as<float>(), s);
     IEC_CUDA(cudaMemcpyAsync(out, do32.get(), (size_t)rows * c * 4, cudaMemcpyDeviceToHost, s));
     dev.sync(s);
