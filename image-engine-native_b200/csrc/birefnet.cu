@@ -238,15 +238,17 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
   const float hs = (float)(size / 2), hf = (float)height, wf = (float)width;
   const float ky = (float)(tap / size), kx = (float)(tap % size);
   auto chan = [&](int c) { return offs + (long long)(c / 8) * offs_plane + (c % 8); };
-  const __half* off_y = chan(2 * tap);
-  const __half* off_x = chan(2 * tap + 1);
+  // (y, x) of a tap are channels 2 tap and 2 tap + 1: one pixel group, one
+  // 4-byte load
+  const __half* off_yx = chan(2 * tap);
   const __half* off_m = chan(2 * taps + tap);
   const __half* src = t + g * t_plane;
   __half* dst = out + (long long)(tap * 8 + g) * out_plane;
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < n; p += (long long)gridDim.x * blockDim.x) {
     const int y = (int)(p / width), x = (int)(p % width);
-    const float py = ((float)y - hs + ky) + __half2float(off_y[p * 8]);
-    const float px = ((float)x - hs + kx) + __half2float(off_x[p * 8]);
+    const float2 oyx = __half22float2(*reinterpret_cast<const __half2*>(off_yx + p * 8));
+    const float py = ((float)y - hs + ky) + oyx.x;
+    const float px = ((float)x - hs + kx) + oyx.y;
     const float m = 2.0f * sigmoid_f(__half2float(off_m[p * 8]));
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (!(py <= -1.0f || py >= hf || px <= -1.0f || px >= wf)) {
