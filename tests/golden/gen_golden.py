@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container that has the reference checkout (read-only) at REFERENCE
-(default /root/reference):
+Run in a container that has the reference checkout (read-only), giving its
+path as the argument or in IEC_REFERENCE:
 
-    python tests/golden/gen_golden.py [REFERENCE]
+    python tests/golden/gen_golden.py REFERENCE
 
 Real-ESRGAN: the reference's own PyTorch definition of SRVGGNetCompact
 (tools/realesrgan/torch_reference.py:25-43, the network its CPU path is
@@ -74,7 +74,9 @@ def realesrgan(reference: str):
 
 
 def main():
-    reference = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("IEC_REFERENCE")
+    if not reference:
+        sys.exit("usage: gen_golden.py REFERENCE (the reference checkout; or set IEC_REFERENCE)")
     realesrgan(reference)
 
 
