@@ -224,16 +224,20 @@ __global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, co
 // tap k of a size x size kernel, the 64 channels of `t` sampled bilinearly
 // at the tap moved by its offset, times 2 sigmoid(modulator). `offs` holds
 // the offset convolution's 3 taps channels (y, x per tap, then the logits).
-// blockIdx.y is (tap, channel group); the threads of a block take
+// blockIdx.y is (tap, quarter of GPT channel groups): a thread computes the
+// sample point, corner weights and modulator of its (pixel, tap) once and
+// gathers GPT channel groups with them. The threads of a block take
 // consecutive pixels, so a warp's 16-byte stores fill 512 contiguous bytes of
-// one output plane and its neighbour loads stay within a few rows.
+// each output plane and its neighbour loads stay within a few rows.
+template <int GPT>
 __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plane, int height, int width, int size,
                                   const __half* __restrict__ offs, long long offs_plane, __half* __restrict__ out,
                                   long long out_plane) {
   griddep_wait();
   griddep_launch_dependents();
+  constexpr int PARTS = 8 / GPT;
   const int taps = size * size;
-  const int tap = (int)(blockIdx.y >> 3), g = (int)(blockIdx.y & 7);
+  const int tap = (int)blockIdx.y / PARTS, g0 = ((int)blockIdx.y % PARTS) * GPT;
   const long long n = (long long)height * width;
   const float hs = (float)(size / 2), hf = (float)height, wf = (float)width;
   const float ky = (float)(tap / size), kx = (float)(tap % size);
@@ -242,15 +246,19 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
   // 4-byte load
   const __half* off_yx = chan(2 * tap);
   const __half* off_m = chan(2 * taps + tap);
-  const __half* src = t + g * t_plane;
-  __half* dst = out + (long long)(tap * 8 + g) * out_plane;
+  const __half* src = t + g0 * t_plane;
+  __half* dst = out + (long long)(tap * 8 + g0) * out_plane;
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < n; p += (long long)gridDim.x * blockDim.x) {
     const int y = (int)(p / width), x = (int)(p % width);
     const float2 oyx = __half22float2(*reinterpret_cast<const __half2*>(off_yx + p * 8));
     const float py = ((float)y - hs + ky) + oyx.x;
     const float px = ((float)x - hs + kx) + oyx.y;
     const float m = 2.0f * sigmoid_f(__half2float(off_m[p * 8]));
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float acc[GPT][8];
+#pragma unroll
+    for (int q = 0; q < GPT; q++)
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[q][e] = 0.0f;
     if (!(py <= -1.0f || py >= hf || px <= -1.0f || px >= wf)) {
       const float y0f = floorf(py), x0f = floorf(px);
       const float ly = py - y0f, lx = px - x0f, hy = 1.0f - ly, hx = 1.0f - lx;
@@ -260,15 +268,22 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         if (cy[k] < 0 || cx[k] < 0 || cy[k] >= height || cx[k] >= width) continue;
-        float v[8];
-        load8(src + ((long long)cy[k] * width + cx[k]) * 8, v);
+        const __half* at = src + ((long long)cy[k] * width + cx[k]) * 8;
 #pragma unroll
-        for (int e = 0; e < 8; e++) acc[e] += cw[k] * v[e];
+        for (int q = 0; q < GPT; q++) {
+          float v[8];
+          load8(at + q * t_plane, v);
+#pragma unroll
+          for (int e = 0; e < 8; e++) acc[q][e] += cw[k] * v[e];
+        }
       }
     }
 #pragma unroll
-    for (int e = 0; e < 8; e++) acc[e] *= m;
-    store8(dst + p * 8, acc);
+    for (int q = 0; q < GPT; q++) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[q][e] *= m;
+      store8(dst + q * out_plane + p * 8, acc[q]);
+    }
   }
 }
 
@@ -831,8 +846,18 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     o.out = offs;
     o.plane_elems = pp;
     gemm_taps(dev_, b.offsets[i], TapSource{t, pp, g, g, 1}, tl, g, g, ACT_NONE, o, bs);
-    launch_pdl(bir_deform_sample, dim3((unsigned)std::min<long long>((P + 255) / 256, 4LL * sms), (unsigned)(taps * 8)),
-               256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+    // Channel groups per thread: 4 where the (pixel, tap) pairs alone fill
+    // the GPU about once over, fewer on the small maps (all 8 in a thread
+    // took 127 registers and ran 0.4 % slower on the whole network).
+    const long long pairs = P * taps;
+    const int gpt = pairs >= 1024LL * sms ? 4 : pairs >= 512LL * sms ? 2 : 1;
+    const dim3 grid((unsigned)std::min<long long>((P + 255) / 256, 4LL * sms), (unsigned)(taps * (8 / gpt)));
+    if (gpt == 4)
+      launch_pdl(bir_deform_sample<4>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+    else if (gpt == 2)
+      launch_pdl(bir_deform_sample<2>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+    else
+      launch_pdl(bir_deform_sample<1>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
     IEC_CUDA(cudaGetLastError());
     GemmOutSpec c;
     c.mode = OUT_STORE;
