@@ -288,26 +288,35 @@ __global__ void bir_deform_sample(const __half* __restrict__ t, long long t_plan
 }
 
 // decoder.rs:382-404: the gate sigmoid(b + w . g16) multiplied onto the
-// block's output (`planes` channel groups).
+// block's output (`planes` channel groups). Items are (pixel, run of up to 4
+// planes), consecutive threads on consecutive pixels; each item recomputes
+// its pixel's gate (two 16-byte loads, cache hits) so that its four plane
+// loads are in flight together.
 __global__ void bir_gate(const __half* __restrict__ g16, long long g_plane, const float* __restrict__ w, float b,
                          __half* __restrict__ out, long long out_plane, int planes, long long pixels) {
   griddep_wait();
   griddep_launch_dependents();
-  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < pixels;
-       p += (long long)gridDim.x * blockDim.x) {
+  const int runs = (planes + 3) / 4;
+  const long long n = pixels * runs;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int q0 = (int)(i / pixels) * 4;
+    const long long p = i % pixels;
     float v[16];
     load8(g16 + p * 8, v);
     load8(g16 + g_plane + p * 8, v + 8);
     float s = b;
     for (int k = 0; k < 16; k++) s = s + v[k] * w[k];
     const float gate = sigmoid_f(s);
-    for (int q = 0; q < planes; q++) {
-      float o[8];
-      __half* d = out + q * out_plane + p * 8;
-      load8(d, o);
+    float o[4][8];
 #pragma unroll
-      for (int e = 0; e < 8; e++) o[e] *= gate;
-      store8(d, o);
+    for (int j = 0; j < 4; j++)
+      if (q0 + j < planes) load8(out + (q0 + j) * out_plane + p * 8, o[j]);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (q0 + j >= planes) continue;
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[j][e] *= gate;
+      store8(out + (q0 + j) * out_plane + p * 8, o[j]);
     }
   }
 }
@@ -355,33 +364,60 @@ __global__ void bir_head(const __half* __restrict__ x, long long plane, const fl
 // decoder.rs:899-925 and 637-752: logits = head bias + the low-resolution
 // logits resized to the image + the full-resolution branch, here as the
 // composed 5x5 convolution; border pixels get the branch from bir_edges.
-__global__ void bir_logits(const float* __restrict__ low, int lg, const float* __restrict__ img, int side,
-                           const float* __restrict__ fr, float head_b, float* __restrict__ logits) {
+// A thread takes 4 horizontally adjacent pixels: each row of their 5 x 8
+// input window is loaded once and serves all four (the per-pixel sums run
+// in the same order as one pixel at a time), the 75 weights sit in shared
+// memory.
+__global__ void __launch_bounds__(256) bir_logits(const float* __restrict__ low, int lg, const float* __restrict__ img,
+                                                  int side, const float* __restrict__ fr, float head_b,
+                                                  float* __restrict__ logits) {
   griddep_wait();
   griddep_launch_dependents();
-  const long long n = (long long)side * side;
+  __shared__ float wk[76];
+  if (threadIdx.x < 76) wk[threadIdx.x] = fr[threadIdx.x < 75 ? FR_COMPOSED + threadIdx.x : FR_SCALARS + 1];
+  __syncthreads();
+  const int quads = (side + 3) / 4;
+  const long long n = (long long)side * quads;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int y = (int)(i / side), x = (int)(i % side);
-    int y1, y2, x1, x2;
-    float dy1, dy2, dx1, dx2;
+    const int y = (int)(i / quads), x0 = (int)(i % quads) * 4;
+    float acc[4] = {wk[75], wk[75], wk[75], wk[75]};
+#pragma unroll
+    for (int dy = 0; dy < 5; dy++) {
+      const int py = y + dy - 2;
+      float r[8][3];
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int px = x0 + k - 2;
+        const bool in = py >= 0 && px >= 0 && py < side && px < side;
+        const float* q = img + ((long long)py * side + px) * 3;
+        r[k][0] = in ? q[0] : 0.0f;
+        r[k][1] = in ? q[1] : 0.0f;
+        r[k][2] = in ? q[2] : 0.0f;
+      }
+#pragma unroll
+      for (int dx = 0; dx < 5; dx++) {
+        const int e = dy * 5 + dx;
+        const float w0 = wk[e * 3], w1 = wk[e * 3 + 1], w2 = wk[e * 3 + 2];
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[j] += w0 * r[j + dx][0] + w1 * r[j + dx][1] + w2 * r[j + dx][2];
+      }
+    }
+    int y1, y2;
+    float dy1, dy2;
     axis(y, lg, side, y1, y2, dy1, dy2);
-    axis(x, lg, side, x1, x2, dx1, dx2);
-    const float v = dx2 * dy2 * low[y1 * lg + x1] + dx1 * dy2 * low[y1 * lg + x2] + dx2 * dy1 * low[y2 * lg + x1] +
-                    dx1 * dy1 * low[y2 * lg + x2];
-    const float d = head_b + v;
-    if (y == 0 || x == 0 || y == side - 1 || x == side - 1) {
-      logits[i] = d;
-      continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int x = x0 + j;
+      if (x >= side) break;
+      int x1, x2;
+      float dx1, dx2;
+      axis(x, lg, side, x1, x2, dx1, dx2);
+      const float v = dx2 * dy2 * low[y1 * lg + x1] + dx1 * dy2 * low[y1 * lg + x2] + dx2 * dy1 * low[y2 * lg + x1] +
+                      dx1 * dy1 * low[y2 * lg + x2];
+      const float d = head_b + v;
+      const bool border = y == 0 || x == 0 || y == side - 1 || x == side - 1;
+      logits[(long long)y * side + x] = border ? d : d + acc[j];
     }
-    float s = fr[FR_SCALARS + 1];
-    for (int e = 0; e < 25; e++) {
-      const int py = y + e / 5 - 2, px = x + e % 5 - 2;
-      const bool in = py >= 0 && px >= 0 && py < side && px < side;
-      const float* q = img + ((long long)py * side + px) * 3;
-      const float p0 = in ? q[0] : 0.0f, p1 = in ? q[1] : 0.0f, p2 = in ? q[2] : 0.0f;
-      s += fr[FR_COMPOSED + e * 3] * p0 + fr[FR_COMPOSED + e * 3 + 1] * p1 + fr[FR_COMPOSED + e * 3 + 2] * p2;
-    }
-    logits[i] = d + s;
   }
 }
 
@@ -890,8 +926,9 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     go.out = g16_.as<__half>();
     go.plane_elems = pp;
     gemm_conv3(dev_, b.gdt, base, out_plane, g, g, ACT_RELU, go, s);
-    launch_pdl(bir_gate, blocks_for(P, sms), 256, 0, s, g16_.as<__half>(), pp, b.gw.as<float>(), b.gb, base, out_plane,
-                                                 b.cout / 8, P);
+    const int planes = b.cout / 8;
+    launch_pdl(bir_gate, blocks_for(P * ((planes + 3) / 4), sms), 256, 0, s, g16_.as<__half>(), pp,
+               b.gw.as<float>(), b.gb, base, out_plane, planes, P);
     IEC_CUDA(cudaGetLastError());
   }
 }
@@ -1017,7 +1054,7 @@ void Birefnet::run_pass(const void* image, bool u8, int side, float* logits, cud
     launch_pdl(bir_head, blocks_for(P0, sms), 256, 0, s, out1_.as<__half>(), pe(P0), head_w_.as<float>(), P0,
                                                   low_.as<float>());
     IEC_CUDA(cudaGetLastError());
-    launch_pdl(bir_logits, blocks_for((long long)side * side, sms), 256, 0, s, low_.as<float>(), g0, img, side,
+    launch_pdl(bir_logits, blocks_for((long long)side * ((side + 3) / 4), sms), 256, 0, s, low_.as<float>(), g0, img, side,
                                                                         full_.as<float>(), head_b_, logits);
     IEC_CUDA(cudaGetLastError());
     launch_pdl(bir_edges, blocks_for((long long)(4 * side - 4) * 32, sms), 256, 0, s, img, side, full_.as<float>(), logits);

@@ -423,14 +423,22 @@ __global__ void __launch_bounds__(256) layer_norm_rows(const __half* __restrict_
   for (int k = 0; k < G; k++) {
     const int g = lane + k * S;
     if (g >= groups) continue;
+    // the group's 8 scales and 8 shifts in four 16-byte loads
+    float gm[8], bt[8];
+    if (!zero) {
+      const float4* g4 = reinterpret_cast<const float4*>(gamma + g * 8);
+      const float4* b4 = reinterpret_cast<const float4*>(beta + g * 8);
+      const float4 ga = __ldg(g4), gb = __ldg(g4 + 1), ba = __ldg(b4), bb = __ldg(b4 + 1);
+      gm[0] = ga.x, gm[1] = ga.y, gm[2] = ga.z, gm[3] = ga.w, gm[4] = gb.x, gm[5] = gb.y, gm[6] = gb.z, gm[7] = gb.w;
+      bt[0] = ba.x, bt[1] = ba.y, bt[2] = ba.z, bt[3] = ba.w, bt[4] = bb.x, bt[5] = bb.y, bt[6] = bb.z, bt[7] = bb.w;
+    }
     uint32_t packed[4];
 #pragma unroll
     for (int e = 0; e < 4; e++) {
       float a = 0.0f, b = 0.0f;
       if (!zero) {
-        const int ch = g * 8 + 2 * e;
-        a = (v[k][2 * e] - mean) * inv * gamma[ch] + beta[ch];
-        b = (v[k][2 * e + 1] - mean) * inv * gamma[ch + 1] + beta[ch + 1];
+        a = (v[k][2 * e] - mean) * inv * gm[2 * e] + bt[2 * e];
+        b = (v[k][2 * e + 1] - mean) * inv * gm[2 * e + 1] + bt[2 * e + 1];
       }
       __half2 o = __floats2half2_rn(a, b);
       packed[e] = *reinterpret_cast<uint32_t*>(&o);
@@ -445,6 +453,7 @@ static void launch_ln(const __half* src, long long src_plane, int plane0, int ro
                       cudaStream_t s) {
   const int groups = c / 8;
   if (c % 8 != 0 || groups < 1) throw Error(ERR_INPUT, "layer norm over a channel count not a multiple of 8");
+  if (((uintptr_t)gamma | (uintptr_t)beta) % 16 != 0) throw Error(ERR_INPUT, "layer norm parameters not 16-byte aligned");
   if (groups <= 8) {
     launch_pdl(layer_norm_rows<2, 4>, (rows + 127) / 128, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                              dst_plane, mode, wm, grid);
