@@ -197,27 +197,36 @@ __global__ void bir_channel_sums(const __half* __restrict__ t, long long plane, 
 }
 
 // decoder.rs:141-165: the pooling branch (mean, 1x1 to 256, ReLU) and its
-// share of conv1, as the bias of conv1 for this map.
-__global__ void bir_aspp_bias(const double* __restrict__ sums, double pixels, const float* __restrict__ pool_w,
-                              const float* __restrict__ pool_b, const float* __restrict__ conv1_pool,
-                              const float* __restrict__ conv1_bias, float* __restrict__ bias) {
+// share of conv1, as the bias of conv1 for this map. One block of 256
+// threads; the 256-term products of the second step are split in four
+// quarters of 64 terms (one per 64 threads), added in quarter order.
+__global__ void __launch_bounds__(256) bir_aspp_bias(const double* __restrict__ sums, double pixels,
+                                                     const float* __restrict__ pool_w, const float* __restrict__ pool_b,
+                                                     const float* __restrict__ conv1_pool,
+                                                     const float* __restrict__ conv1_bias, float* __restrict__ bias) {
+  static_assert(BRANCH == 256 && BRANCH == 4 * INTER, "one thread per pooled channel, four quarters of conv1's");
   griddep_wait();
   griddep_launch_dependents();
-  __shared__ float mean[INTER], pooled[BRANCH];
+  __shared__ float mean[INTER], pooled[BRANCH], part[4][INTER];
   const int t = threadIdx.x;
   if (t < INTER) mean[t] = (float)(sums[t] / pixels);
   __syncthreads();
-  if (t < BRANCH) {
+  {
     float p = pool_b[t];
+#pragma unroll 16
     for (int c = 0; c < INTER; c++) p += mean[c] * pool_w[c * BRANCH + t];
     pooled[t] = p > 0.0f ? p : 0.0f;
   }
   __syncthreads();
-  if (t < INTER) {
-    float b = conv1_bias[t];
-    for (int j = 0; j < BRANCH; j++) b += pooled[j] * conv1_pool[j * INTER + t];
-    bias[t] = b;
+  {
+    const int q = t / INTER, o = t % INTER;
+    float b = 0.0f;
+#pragma unroll 16
+    for (int j = q * INTER; j < (q + 1) * INTER; j++) b += pooled[j] * conv1_pool[j * INTER + o];
+    part[q][o] = b;
   }
+  __syncthreads();
+  if (t < INTER) bias[t] = conv1_bias[t] + part[0][t] + part[1][t] + part[2][t] + part[3][t];
 }
 
 // decoder.rs:243-313: the deformable convolution's input: for pixel p and
