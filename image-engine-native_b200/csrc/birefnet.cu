@@ -233,9 +233,9 @@ __global__ void __launch_bounds__(256) bir_aspp_bias(const double* __restrict__ 
 // tap k of a size x size kernel, the 64 channels of `t` sampled bilinearly
 // at the tap moved by its offset, times 2 sigmoid(modulator). `offs` holds
 // the offset convolution's 3 taps channels (y, x per tap, then the logits).
-// blockIdx.y is (tap, quarter of GPT channel groups): a thread computes the
-// sample point, corner weights and modulator of its (pixel, tap) once and
-// gathers GPT channel groups with them. The threads of a block take
+// blockIdx.y is (tap, run of GPT of the 8 channel groups): a thread computes
+// the sample point, corner weights and modulator of its (pixel, tap) once
+// and gathers its run's GPT channel groups with them. The threads of a block take
 // consecutive pixels, so a warp's 16-byte stores fill 512 contiguous bytes of
 // each output plane and its neighbour loads stay within a few rows.
 template <int GPT>
