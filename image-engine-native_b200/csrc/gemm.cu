@@ -354,12 +354,21 @@ void planar_to_rows(const __half* src, long long src_plane_elems, int rows, int 
 // computes them), then the normalised groups. mode 0: row r is pixel r;
 // mode 1: window order (zero rows where WindowMap says so); mode 2: patch
 // merge, row r of the (grid / 2)^2 map gathering its 2 x 2 pixels in the
-// order (0,0), (1,0), (0,1), (1,1) (birefnet swin.rs:366-404).
+// order (0,0), (1,0), (0,1), (1,1) (birefnet swin.rs:366-404). The scales
+// and shifts (weights, which no kernel writes) are staged in shared memory
+// before the wait for the previous kernel, so their fetch overlaps its tail
+// instead of following the two reductions.
 template <int S, int G>
 __global__ void __launch_bounds__(256) layer_norm_rows(const __half* __restrict__ src, long long src_plane, int plane0,
                                                        int rows, int c, const float* __restrict__ gamma,
                                                        const float* __restrict__ beta, __half* __restrict__ dst,
                                                        long long dst_plane, int mode, WindowMap wm, int grid) {
+  extern __shared__ float4 ln_params[];  // [c / 4] scales, then [c / 4] shifts
+  for (int i = threadIdx.x; i < c / 4; i += blockDim.x) {
+    ln_params[i] = __ldg(reinterpret_cast<const float4*>(gamma) + i);
+    ln_params[c / 4 + i] = __ldg(reinterpret_cast<const float4*>(beta) + i);
+  }
+  __syncthreads();
   griddep_wait();
   griddep_launch_dependents();
   const int lane = threadIdx.x % S, sub = threadIdx.x / S;
@@ -423,14 +432,21 @@ __global__ void __launch_bounds__(256) layer_norm_rows(const __half* __restrict_
   for (int k = 0; k < G; k++) {
     const int g = lane + k * S;
     if (g >= groups) continue;
-    // the group's 8 scales and 8 shifts in four 16-byte loads
+    // the group's 8 scales and 8 shifts: four 16-byte shared-memory loads
     float gm[8], bt[8];
     if (!zero) {
-      const float4* g4 = reinterpret_cast<const float4*>(gamma + g * 8);
-      const float4* b4 = reinterpret_cast<const float4*>(beta + g * 8);
-      const float4 ga = __ldg(g4), gb = __ldg(g4 + 1), ba = __ldg(b4), bb = __ldg(b4 + 1);
-      gm[0] = ga.x, gm[1] = ga.y, gm[2] = ga.z, gm[3] = ga.w, gm[4] = gb.x, gm[5] = gb.y, gm[6] = gb.z, gm[7] = gb.w;
-      bt[0] = ba.x, bt[1] = ba.y, bt[2] = ba.z, bt[3] = ba.w, bt[4] = bb.x, bt[5] = bb.y, bt[6] = bb.z, bt[7] = bb.w;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const float4 gq = ln_params[g * 2 + h], bq = ln_params[c / 4 + g * 2 + h];
+        gm[4 * h] = gq.x;
+        gm[4 * h + 1] = gq.y;
+        gm[4 * h + 2] = gq.z;
+        gm[4 * h + 3] = gq.w;
+        bt[4 * h] = bq.x;
+        bt[4 * h + 1] = bq.y;
+        bt[4 * h + 2] = bq.z;
+        bt[4 * h + 3] = bq.w;
+      }
     }
     uint32_t packed[4];
 #pragma unroll
@@ -454,17 +470,18 @@ static void launch_ln(const __half* src, long long src_plane, int plane0, int ro
   const int groups = c / 8;
   if (c % 8 != 0 || groups < 1) throw Error(ERR_INPUT, "layer norm over a channel count not a multiple of 8");
   if (((uintptr_t)gamma | (uintptr_t)beta) % 16 != 0) throw Error(ERR_INPUT, "layer norm parameters not 16-byte aligned");
+  const size_t smem = (size_t)2 * c * sizeof(float);  // at most 24 KB (3072 channels)
   if (groups <= 8) {
-    launch_pdl(layer_norm_rows<2, 4>, (rows + 127) / 128, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<2, 4>, (rows + 127) / 128, 256, smem, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                              dst_plane, mode, wm, grid);
   } else if (groups <= 16) {
-    launch_pdl(layer_norm_rows<4, 4>, (rows + 63) / 64, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<4, 4>, (rows + 63) / 64, 256, smem, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                            dst_plane, mode, wm, grid);
   } else if (groups <= 48) {
-    launch_pdl(layer_norm_rows<8, 6>, (rows + 31) / 32, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<8, 6>, (rows + 31) / 32, 256, smem, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                            dst_plane, mode, wm, grid);
   } else if (groups <= 384) {
-    launch_pdl(layer_norm_rows<32, 12>, (rows + 7) / 8, 256, 0, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
+    launch_pdl(layer_norm_rows<32, 12>, (rows + 7) / 8, 256, smem, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                            dst_plane, mode, wm, grid);
   } else {
     throw Error(ERR_INPUT, "layer norm over more than 3072 channels");
