@@ -1,6 +1,7 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) features the kernels
-// use: mbarriers, TMA (cp.async.bulk / cp.async.bulk.tensor, never with
-// cluster multicast), tcgen05 tensor-core MMAs with TMEM accumulators.
+// use: mbarriers, TMA (cp.async.bulk / cp.async.bulk.tensor, each copy into
+// the issuing CTA's own shared memory only), tcgen05 tensor-core MMAs with
+// TMEM accumulators.
 //
 // Every wait is bounded: past IEC_WAIT_NS of global time it sets the CTA's
 // abort flag and the kernel's device error word, and returns false, so a
@@ -182,7 +183,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-// Tiled 5-D tensor load (no multicast). The innermost coordinate c0 is
+// Tiled 5-D tensor load into this CTA's shared memory. The innermost coordinate c0 is
 // always 0 here (a 16-byte channel group), so it meets TMA's 16-byte rule;
 // the others may be negative or past the end, where the box reads zeros.
 __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
@@ -194,7 +195,7 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Tiled 3-D tensor load (no multicast); c0 * element size a multiple of 16.
+// Tiled 3-D tensor load into this CTA's shared memory; c0 * element size a multiple of 16.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
   asm volatile(
@@ -204,7 +205,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Tiled 4-D tensor load (no multicast). The caller keeps c0 * element size a
+// Tiled 4-D tensor load into this CTA's shared memory. The caller keeps c0 * element size a
 // multiple of 16 bytes; negative or past-the-end coordinates read zeros.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3) {
