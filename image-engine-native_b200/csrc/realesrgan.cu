@@ -497,36 +497,40 @@ void RealEsrgan::run_device(const float* src, float* dst, size_t count, size_t w
   }
 }
 
-void RealEsrgan::run_batch_host(const float* src, float* dst, size_t count, size_t width, size_t height,
-                                cudaStream_t s) {
+void RealEsrgan::run_batch_host(const void* src, bool src_u8, void* dst, bool dst_u8, size_t count, size_t width,
+                                size_t height, cudaStream_t s) {
   // Three streams: H2D of chunk c + 1 and D2H of chunk c - 1 run while chunk
-  // c computes; two device buffers of each kind alternate.
+  // c computes; two device buffers of each kind alternate. 8-bit images move
+  // a quarter of the bytes of f32 ones over the host link.
   const size_t chunk = chunk_for(width, height);
-  const size_t in_bytes = chunk * width * height * 3 * 4, out_bytes = in_bytes * SCALE * SCALE;
+  const size_t in_elem = src_u8 ? 1 : 4, out_elem = dst_u8 ? 1 : 4;
+  const size_t img_vals = width * height * 3, out_vals = img_vals * SCALE * SCALE;
   for (int b = 0; b < 2; b++) {
-    batch_in_[b].reserve(in_bytes);
-    batch_out_[b].reserve(out_bytes);
+    batch_in_[b].reserve(chunk * img_vals * in_elem);
+    batch_out_[b].reserve(chunk * out_vals * out_elem);
   }
   Region r{0, 0, (int)width, (int)height, 0, 0, (int)width, (int)height};
   IEC_CUDA(cudaEventRecord(ev_start_, s));
   IEC_CUDA(cudaStreamWaitEvent(h2d_, ev_start_, 0));
   IEC_CUDA(cudaStreamWaitEvent(d2h_, ev_start_, 0));
+  const uint8_t* in_bytes = static_cast<const uint8_t*>(src);
+  uint8_t* out_bytes = static_cast<uint8_t*>(dst);
   size_t k = 0;
   for (size_t c0 = 0; c0 < count; c0 += chunk, k++) {
     const int b = (int)(k & 1);
     const size_t n = std::min(chunk, count - c0);
-    const size_t ib = n * width * height * 3 * 4, ob = ib * SCALE * SCALE;
+    const size_t ib = n * img_vals * in_elem, ob = n * out_vals * out_elem;
     if (k >= 2) IEC_CUDA(cudaStreamWaitEvent(h2d_, ev_done_[b], 0));  // chunk k - 2 has read batch_in_[b]
-    IEC_CUDA(cudaMemcpyAsync(batch_in_[b].get(), src + c0 * width * height * 3, ib, cudaMemcpyHostToDevice, h2d_));
+    IEC_CUDA(cudaMemcpyAsync(batch_in_[b].get(), in_bytes + c0 * img_vals * in_elem, ib, cudaMemcpyHostToDevice, h2d_));
     IEC_CUDA(cudaEventRecord(ev_h2d_[b], h2d_));
     IEC_CUDA(cudaStreamWaitEvent(s, ev_h2d_[b], 0));
     if (k >= 2) IEC_CUDA(cudaStreamWaitEvent(s, ev_d2h_[b], 0));  // chunk k - 2's output is copied out
-    run_network(batch_in_[b].get(), false, batch_out_[b].get(), false, (int)n, (int)width, (int)height, r, nullptr,
+    run_network(batch_in_[b].get(), src_u8, batch_out_[b].get(), dst_u8, (int)n, (int)width, (int)height, r, nullptr,
                 s);
     IEC_CUDA(cudaEventRecord(ev_done_[b], s));
     IEC_CUDA(cudaStreamWaitEvent(d2h_, ev_done_[b], 0));
-    IEC_CUDA(cudaMemcpyAsync(dst + c0 * width * height * 3 * SCALE * SCALE, batch_out_[b].get(), ob,
-                             cudaMemcpyDeviceToHost, d2h_));
+    IEC_CUDA(cudaMemcpyAsync(out_bytes + c0 * out_vals * out_elem, batch_out_[b].get(), ob, cudaMemcpyDeviceToHost,
+                             d2h_));
     IEC_CUDA(cudaEventRecord(ev_d2h_[b], d2h_));
   }
   // The caller's stream completes only once every output is in host memory.
@@ -575,13 +579,27 @@ void RealEsrgan::run_device_noalloc(const float* src, float* dst, size_t count, 
                                     cudaStream_t s) {
   const int w = (int)width, h = (int)height;
   const int mw = std::max(w, CONV_HALO_W), mh = std::max(h, CONV_HALO_H);
-  // (count is bounded first so that the product cannot wrap around)
-  const size_t pixels = count > NOALLOC_MAX_PIXELS ? NOALLOC_MAX_PIXELS + 1 : count * (size_t)mw * mh;
-  if (pixels > NOALLOC_MAX_PIXELS)
+  // Every input check comes before any work is queued. The scratch holds
+  // count x mw x mh pixels; each factor is compared against the limit
+  // divided by the others, so no product can wrap around.
+  const size_t per_image = (size_t)mw * (size_t)mh;
+  const bool fits = count >= 1 && per_image <= NOALLOC_MAX_PIXELS && count <= NOALLOC_MAX_PIXELS / per_image;
+  if (!fits)
     throw Error(ERR_INPUT, std::to_string(count) + " images of " + std::to_string(width) + " x " +
-                               std::to_string(height) + " need " + std::to_string(pixels) +
-                               " pixels of scratch; the allocation-free entry point holds " +
+                               std::to_string(height) + " need " + std::to_string(count) + " x " +
+                               std::to_string(per_image) + " pixels of scratch; the allocation-free entry point holds " +
                                std::to_string(NOALLOC_MAX_PIXELS));
+  const size_t pixels = count * per_image;
+  ConvParams p{};
+  p.H = h;
+  p.W = w;
+  p.MW = mw;
+  p.MH = mh;
+  p.tiles_x = (w + CONV_TILE_W - 1) / CONV_TILE_W;
+  p.tiles_y = (h + CONV_TILE_H - 1) / CONV_TILE_H;
+  if ((size_t)p.tiles_x * p.tiles_y * count >= (1u << 24) || p.tiles_x >= (1 << 16) || p.tiles_y >= (1 << 16))
+    throw Error(ERR_INPUT, "too many tiles for one pass");
+  p.tiles = p.tiles_x * p.tiles_y * (int)count;
   uint8_t* base = noalloc_scratch(dev_.ordinal());
   __half* prep = reinterpret_cast<__half*>(base);
   __half* maps[2] = {reinterpret_cast<__half*>(base + NOALLOC_PREP_BYTES),
@@ -599,16 +617,6 @@ void RealEsrgan::run_device_noalloc(const float* src, float* dst, size_t count, 
     launch_pdl(realesrgan_prep, blocks, 256, 0, s, src, 0, w, h, 0, 0, w, h, mw, mh, (int)count, prep, (int*)nullptr, 0);
     IEC_CUDA(cudaGetLastError());
   }
-  ConvParams p{};
-  p.H = h;
-  p.W = w;
-  p.MW = mw;
-  p.MH = mh;
-  p.tiles_x = (w + CONV_TILE_W - 1) / CONV_TILE_W;
-  p.tiles_y = (h + CONV_TILE_H - 1) / CONV_TILE_H;
-  p.tiles = p.tiles_x * p.tiles_y * (int)count;
-  if ((size_t)p.tiles_x * p.tiles_y * count >= (1u << 24) || p.tiles_x >= (1 << 16) || p.tiles_y >= (1 << 16))
-    throw Error(ERR_INPUT, "too many tiles for one pass");
   p.div_tiles_x = FastDiv((uint32_t)p.tiles_x);
   p.div_tiles_y = FastDiv((uint32_t)p.tiles_y);
   p.dev_err = dev_.dev_err();

@@ -100,6 +100,15 @@ iec_status iec_realesrgan_run(iec_realesrgan* model, const uint8_t* rgb, size_t 
 iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, size_t count,
                                     size_t width, size_t height, float* out, void* stream);
 
+/* Batched Model::run (lib.rs:161-191) over `count` images of one size:
+ * 8-bit RGB in (v / 255) and out (clamp(0, 1) * 255 rounded), HOST buffers,
+ * each image run whole, which gives the tiled run's pixels bit for bit. The
+ * host link carries a quarter of iec_realesrgan_run_batch's bytes. Queued on
+ * `stream` (NULL: the model's stream); returns when the outputs are in
+ * `out`. */
+iec_status iec_realesrgan_run_batch_u8(iec_realesrgan* model, const uint8_t* images, size_t count,
+                                       size_t width, size_t height, uint8_t* out, void* stream);
+
 /* Part of Model::run_float_tiled for sharding one large image over GPUs: of
  * the grid of tiles run_float_tiled would cut (row-major order), only tiles
  * first .. last - 1 run, and only their own output windows of `out` (the
@@ -132,8 +141,10 @@ iec_status iec_realesrgan_run_device(iec_realesrgan* model, const float* images,
  * their feature maps with cudaMalloc on demand; this one keeps them in a
  * fixed scratch array built into the library, 31.5 MiB that every GPU which
  * loads the library holds until the process exits.
- *  - Limit: count x max(width, 16) x max(height, 10) <= 114688 pixels (for
- *    example one 384 x 256 image); a larger call returns IEC_ERR_INPUT.
+ *  - Limit: count x max(width, 32) x max(height, 6) <= 114688 pixels (for
+ *    example one 384 x 256 image; 32 x 6 is the input box one tile of the
+ *    convolution reads, so narrower or shorter images are counted at that
+ *    size); a larger call returns IEC_ERR_INPUT before any work is queued.
  *  - The model itself is loaded beforehand with iec_realesrgan_load, which
  *    does allocate; the call only uses `images`, `out` and the scratch.
  *  - The first call on a device looks up the scratch array's device address
