@@ -13,8 +13,11 @@ value = 256 x 1.5729 output MP / step time (device time, max over ranks).
 Printed as one JSON line by rank 0:
   value      inputs resident in HBM (302 MB in, 4.8 GB out: larger than L2),
              CUDA events on the stream the kernels run on;
-  e2e        the same through the C ABI's host-buffer entry point from
-             page-locked memory, the H2D and D2H copies inside the timed region;
+  e2e        the same through the C ABI's host-buffer entry points from
+             page-locked memory, the H2D and D2H copies inside the timed
+             region: 8-bit images (iec_realesrgan_run_batch_u8, Model::run's
+             semantics) as the value, f32 ones (iec_realesrgan_run_batch) in
+             e2e.f32;
   roofline   the dominant kernel (conv3x3 64->64, 32 of 34 layers): its
              algorithmic FLOPs per launch over its mean launch time, both
              measured by events around each launch during the timed steps;
@@ -134,24 +137,51 @@ class Clocks:
                 "samples": len(rows), "power_w_max": max(power)}
 
 
-def cpu_sample(weights_path, seconds=12.0, cap=30.0):
-    """The CPU oracle on whole 3x256x384 images until `seconds` have passed."""
+def host_threads():
+    """Threads the CPU path may use: every core of this process's affinity
+    mask, whatever OMP_NUM_THREADS a launcher such as torchrun has set."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def oracle_threads(n):
+    from oracle import refcpu
+
+    refcpu.set_threads(n)
+    return refcpu.threads()
+
+
+def cpu_sample(weights_path, seconds=12.0, cap=30.0, six_seconds=8.0):
+    """The CPU oracle on whole 3x256x384 images until `seconds` have passed,
+    on every core of the affinity mask; then the same with 6 threads (the
+    reference's published protocol times 6 threads, README.md:26-27)."""
     from iec import weights as W
     from oracle import refcpu
 
     model = refcpu.RealEsrgan(weights_path)
     image = W.realesrgan_input(WIDTH, HEIGHT, 0)
-    model.run_float(image[:32, :32])  # warm-up of the threads
-    n, t0 = 0, time.perf_counter()
-    while True:
-        model.run_float(image)
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or el + el / n > cap:
-            break
-    cores = refcpu.threads()
-    return {"value": n * OUT_MP / el, "unit": "MP/s", "cores": cores, "kind": "port",
-            "sample": f"{n} whole 3x256x384 images of the batch, {el:.1f} s, oracle/refcpu (restated reference CPU f32 path: Winograd F(4x4) + FMA products), {cores} threads"}
+
+    def timed(threads, secs):
+        cores = oracle_threads(threads)
+        model.run_float(image[:32, :32])  # warm-up of the threads
+        n, t0 = 0, time.perf_counter()
+        while True:
+            model.run_float(image)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= secs or el + el / n > cap:
+                return n, el, cores
+
+    n, el, cores = timed(host_threads(), seconds)
+    out = {"value": n * OUT_MP / el, "unit": "MP/s", "cores": cores, "kind": "port",
+           "sample": f"{n} whole 3x256x384 images of the batch, {el:.1f} s, oracle/refcpu (restated reference CPU f32 path: Winograd F(4x4) + FMA products), {cores} threads (the affinity mask)"}
+    n6, el6, c6 = timed(min(6, host_threads()), six_seconds)
+    out["six_threads"] = {"value": n6 * OUT_MP / el6, "unit": "MP/s", "cores": c6,
+                          "sample": f"{n6} whole images, {el6:.1f} s"}
+    oracle_threads(host_threads())
+    return out
 
 
 def reference_arm(args, weights_path):
@@ -161,6 +191,7 @@ def reference_arm(args, weights_path):
     from iec import weights as W
     from oracle import refcpu
 
+    oracle_threads(host_threads())
     model = refcpu.RealEsrgan(weights_path)
     image = W.realesrgan_input(WIDTH, HEIGHT, 0)
     for _ in range(args.warmup):
@@ -175,7 +206,7 @@ def reference_arm(args, weights_path):
         "impl": "reference", "metric": "output megapixels/s", "value": value, "unit": "MP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config(args, 0),
+        "config": config(args, args.chunk),
         "cpu_baseline": {"value": value, "unit": "MP/s", "cores": cores, "kind": "port",
                          "sample": f"one 3x256x384 image of the batch per step, oracle/refcpu (the reference CPU f32 path restated; the Rust reference cannot be built here), {cores} threads"},
         "e2e": {"value": value, "unit": "MP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -220,6 +251,7 @@ def cpu_once(fn, mp):
     small warm-up of its threads): the per-model CPU baseline."""
     from oracle import refcpu
 
+    oracle_threads(host_threads())
     t0 = time.perf_counter()
     fn()
     el = time.perf_counter() - t0
@@ -240,15 +272,22 @@ def scunet_leg(wdir, stream, sptr, cpu):
     img = torch.from_numpy(W.scunet_input(768, 512, 0)).cuda()
     res = torch.empty_like(img)
     t = time_device(lambda: m.run_device(img.data_ptr(), 768, 512, res.data_ptr(), sptr), stream)
+    image = W.scunet_input(768, 512, 0)
+    for _ in range(3):  # warm-up: buffers, then the pass's graph (captured on the second call)
+        m.run_float(image)
+    t0 = time.perf_counter()
+    for _ in range(5):
+        m.run_float(image)
+    te = (time.perf_counter() - t0) / 5
     out["scunet_768x512"] = {"workload": "SCUNet 3x512x768 (single-image configuration)", "value": 768 * 512 / 1e6 / t,
                              "unit": "MP/s", "ms": t * 1e3, "gflop": 899.58,
-                             "tflops_achieved": 899.58e9 / t / 1e12}
+                             "tflops_achieved": 899.58e9 / t / 1e12, "e2e_ms": te * 1e3,
+                             "e2e_value": 768 * 512 / 1e6 / te}
     m.close()
     if cpu:
         from oracle import refcpu
 
         ref = refcpu.Scunet(path)
-        image = W.scunet_input(768, 512, 0)
         ref.run_float(image[:64, :64])
         out["scunet_768x512"]["cpu_baseline"] = cpu_once(lambda: ref.run_float(image), 768 * 512 / 1e6)
     return out
@@ -347,6 +386,8 @@ def main():
     ap.add_argument("--profile-models", action="store_true",
                     help="run only the other models' single-image legs (for profiler launch lists)")
     ap.add_argument("--models", default="scunet,lama,birefnet", help="which single-image legs run (comma list)")
+    ap.add_argument("--warm-seconds", type=float, default=3.0,
+                    help="minimum seconds of warm-up work before the timed steps (power-capped steady state)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="images per step (a smaller batch only for profiling captures)")
     args = ap.parse_args()
@@ -408,8 +449,15 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
+    # Warm-up: at least W steps and at least --warm-seconds of work, so every
+    # GPU is at its power-capped steady state (clock and power) when the
+    # timed region starts, whatever N makes one step's length.
+    warm_steps, w0 = 0, time.perf_counter()
+    while warm_steps < args.warmup or time.perf_counter() - w0 < args.warm_seconds:
         step()
+        warm_steps += 1
+        if warm_steps >= args.warmup:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
     launches_per_step = model.launches(count, WIDTH, HEIGHT)
     model.set_timing(args.steps * launches_per_step * 2 + 64)
@@ -441,28 +489,45 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        # End to end through the host-buffer entry point, page-locked buffers.
+        # End to end through the host-buffer entry points, page-locked
+        # buffers, every step's H2D copy of its inputs and D2H copy of its
+        # outputs inside the timed region: 8-bit images (Model::run, the
+        # reference's public byte API) and f32 ones (Model::run_float).
+        e2e_steps = max(2, args.steps // 2)
+
+        def host_leg(run, h_in, h_out):
+            run(h_in, h_out, sptr)
+            barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(e2e_steps):
+                run(h_in, h_out, sptr)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            sec = max_over_ranks(e0.elapsed_time(e1) / 1e3) / e2e_steps
+            bi = batch * WIDTH * HEIGHT * 3 * h_in.element_size()
+            bo = batch * WIDTH * HEIGHT * 3 * 16 * h_out.element_size()
+            return {"value": batch * OUT_MP / sec, "unit": "MP/s", "h2d_bytes_per_step": bi,
+                    "d2h_bytes_per_step": bo, "ms_per_step": sec * 1e3,
+                    "d2h_gbs_aggregate": bo / sec / 1e9}
+
         h_in = torch.empty((count, HEIGHT, WIDTH, 3), dtype=torch.float32, pin_memory=True)
         h_in.copy_(d_in)
         h_out = torch.empty((count, HEIGHT * 4, WIDTH * 4, 3), dtype=torch.float32, pin_memory=True)
-        e2e_steps = max(2, args.steps // 2)
-        model.run_batch(h_in, h_out, sptr)
-        barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            model.run_batch(h_in, h_out, sptr)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3) / e2e_steps
+        f32 = host_leg(model.run_batch, h_in, h_out)
         # The host path gives the device path's numbers bit for bit.
-        same = bool(torch.equal(h_out[:2].cuda(), d_out[:2]))
-        e2e = {"value": batch * OUT_MP / e2e_s, "unit": "MP/s",
-               "h2d_bytes_per_step": batch * WIDTH * HEIGHT * 3 * 4,
-               "d2h_bytes_per_step": batch * WIDTH * HEIGHT * 3 * 4 * 16,
-               "api": "iec_realesrgan_run_batch (host buffers, page-locked)", "matches_device_path": same}
+        f32["matches_device_path"] = bool(torch.equal(h_out[:2].cuda(), d_out[:2]))
+        f32["api"] = "iec_realesrgan_run_batch (f32 host buffers, page-locked)"
+        del h_out
+        b_in = torch.empty((count, HEIGHT, WIDTH, 3), dtype=torch.uint8, pin_memory=True)
+        b_in.copy_((d_in * 255).round().to(torch.uint8))
+        b_out = torch.empty((count, HEIGHT * 4, WIDTH * 4, 3), dtype=torch.uint8, pin_memory=True)
+        e2e = host_leg(model.run_batch_u8, b_in, b_out)
+        e2e["api"] = "iec_realesrgan_run_batch_u8 (8-bit host buffers, page-locked: Model::run semantics)"
+        e2e["f32"] = f32
+        del b_in, b_out, h_in
 
     # The other sharded workload: one 3x4096x4096 image cut into 512 x 512
     # tiles with a 34-pixel margin; each rank runs its cost-balanced range of
@@ -537,7 +602,8 @@ def main():
         clocks = clk.summary()
         line = {
             "metric": "output megapixels/s", "value": value, "unit": "MP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "steps": args.steps, "warmup": warm_steps, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "warmup_floor_s": args.warm_seconds,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
             "data": "synthetic (seeded uniform images, seeded He-normal weights)",
             "config": config(args, args.chunk),

@@ -232,7 +232,22 @@ iec_status iec_realesrgan_run_batch(iec_realesrgan* model, const float* images, 
     RealEsrgan& m = *model->model;
     DeviceScope scope(m.device());
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
-    m.run_batch_host(images, out, count, width, height, s);
+    m.run_batch_host(images, false, out, false, count, width, height, s);
+  });
+}
+
+iec_status iec_realesrgan_run_batch_u8(iec_realesrgan* model, const uint8_t* images, size_t count, size_t width,
+                                       size_t height, uint8_t* out, void* stream) {
+  return guard([&] {
+    need_model(model);
+    need(images, "images");
+    need(out, "out");
+    if (count == 0) return;
+    check_realesrgan_size(width, height);
+    RealEsrgan& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    m.run_batch_host(images, true, out, true, count, width, height, s);
   });
 }
 

@@ -47,9 +47,10 @@ class RealEsrgan {
   // Whole images (one region each), `count` at a time in chunks; no waits.
   void run_device(const float* src, float* dst, size_t count, size_t width, size_t height, cudaStream_t stream);
 
-  // Host buffers, copies overlapped with the kernels; returns when done.
-  void run_batch_host(const float* src, float* dst, size_t count, size_t width, size_t height,
-                      cudaStream_t stream);
+  // Host buffers (f32 or 8-bit images in and out), copies overlapped with
+  // the kernels; returns when done.
+  void run_batch_host(const void* src, bool src_u8, void* dst, bool dst_u8, size_t count, size_t width,
+                      size_t height, cudaStream_t stream);
 
   // As run_device, but the feature maps live in a fixed scratch array that
   // the library holds on every device (no allocation at all); see

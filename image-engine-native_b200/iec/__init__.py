@@ -66,6 +66,7 @@ def lib():
         L.iec_realesrgan_run_float_tiles.argtypes = [vp, f32p, sz, sz, sz, sz, sz, sz, f32p]
         L.iec_realesrgan_run_tiles_device.argtypes = [vp, vp, sz, sz, sz, sz, sz, sz, vp, vp]
         L.iec_realesrgan_run_batch.argtypes = [vp, vp, sz, sz, sz, vp, vp]
+        L.iec_realesrgan_run_batch_u8.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_set_fused.argtypes = [vp, ctypes.c_int]
         L.iec_realesrgan_set_fused.restype = ctypes.c_int
@@ -213,6 +214,15 @@ class RealEsrgan:
         if out is None:
             out = np.empty((n, 4 * h, 4 * w, 3), np.float32)
         _check(lib().iec_realesrgan_run_batch(self._h, _addr(images), n, w, h, _addr(out), stream or None))
+        return out
+
+    def run_batch_u8(self, images, out=None, stream: int = 0):
+        """Batched run (8-bit RGB in and out) on host arrays (N x H x W x 3);
+        page-locked torch tensors or numpy arrays."""
+        n, h, w, _ = images.shape
+        if out is None:
+            out = np.empty((n, 4 * h, 4 * w, 3), np.uint8)
+        _check(lib().iec_realesrgan_run_batch_u8(self._h, _addr(images), n, w, h, _addr(out), stream or None))
         return out
 
     def run_device(self, images_ptr: int, count: int, width: int, height: int, out_ptr: int, stream: int = 0):

@@ -143,6 +143,17 @@ def test_batch_and_device_paths_match_single_runs(gpu_model):
     assert np.array_equal(d_out.cpu().numpy().view(np.uint32), singles.view(np.uint32))
 
 
+def test_8bit_batch_matches_8bit_single_runs(gpu_model):
+    # iec_realesrgan_run_batch_u8: Model::run's byte semantics over a batch
+    # of whole images, equal to the tiled single-image run byte for byte.
+    rng = np.random.default_rng(17)
+    images = rng.integers(0, 256, (9, 20, 36, 3), dtype=np.uint8)
+    singles = np.stack([gpu_model.run(im) for im in images])
+    batch = gpu_model.run_batch_u8(images)
+    assert batch.dtype == np.uint8 and batch.shape == (9, 80, 144, 3)
+    assert np.array_equal(batch, singles)
+
+
 def test_runs_are_deterministic(gpu_model):
     image = W.realesrgan_input(100, 60, 12)
     a = gpu_model.run_float(image)
