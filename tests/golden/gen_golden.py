@@ -10,11 +10,12 @@ Real-ESRGAN: the reference's own PyTorch definition of SRVGGNetCompact
 (tools/realesrgan/torch_reference.py:25-43, the network its CPU path is
 tested against in crates/realesrgan-native/tests/reference.rs:61-80) is
 imported from the reference checkout, loaded with the seeded random-init
-weights of iec.weights.realesrgan_tensors (converted back from the engine's
-[(ky, kx, cin), cout] matrices to PyTorch's [cout, cin, ky, kx], the inverse
-of tools/realesrgan/export_weights.py:48-55) and run on seeded inputs. The
-outputs, with the inputs and the SHA-256 of the weights file, are written as
-realesrgan_torch.npz. The reference itself is never needed at test time.
+checkpoint iec.weights.realesrgan_checkpoint (PyTorch's [cout, cin, ky, kx]
+layout; the weights file the oracle and the backend read is what the
+reference's tools/realesrgan/export_weights.py writes from it, byte for
+byte) and run on seeded inputs. The outputs, with the inputs and the SHA-256
+of the weights file, are written as realesrgan_torch.npz. The reference
+itself is never needed at test time.
 """
 
 from __future__ import annotations
@@ -48,16 +49,11 @@ def realesrgan(reference: str):
 
     torch.set_num_threads(4)
     mod = load_reference_module(reference)
-    tensors = W.realesrgan_tensors(0)
-    data = W.encode(W.MAGIC["realesrgan"], tensors)
+    data = W.encode(W.MAGIC["realesrgan"], W.realesrgan_tensors(0))
     sha = hashlib.sha256(data).hexdigest()
-    state = {}
-    for name, array, _half in tensors:
-        if name.endswith(".weight") and array.ndim == 2:
-            k, cout = array.shape
-            cin = k // 9
-            array = array.reshape(3, 3, cin, cout).transpose(3, 2, 0, 1)
-        state[name] = torch.from_numpy(np.ascontiguousarray(array))
+    # The seeded checkpoint in the upstream layout; the weights file is what
+    # the reference's exporter writes from it (tests/test_export_pinning.py).
+    state = {name: torch.from_numpy(a) for name, a in W.realesrgan_checkpoint(0).items()}
     model = mod.SRVGGNetCompact()
     model.load_state_dict(state, strict=True)
     model.eval()

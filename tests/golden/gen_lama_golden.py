@@ -6,24 +6,20 @@
 The reference checks its LaMa against LaMa's own PyTorch generator
 (tools/lama/torch_reference.py), which imports the third-party LaMa sources;
 those are not in this container. So this script restates the generator's
-published forward pass (FFCResNetGenerator with every batch norm folded, as
-tools/lama/export_weights.py:86-164 folds them) in float64 PyTorch of its own,
-built from the same seeded weights file the oracle reads, converted back
-through the inverse of the exporter's mapping:
-
-- matrices [(ky, kx, cin), cout] -> conv weights [cout, cin, ky, kx]
-  (export_weights.py:80-83);
-- the Fourier unit's matrix from the planar order [re(c) | im(c)] back to
-  the interleaved channels 2c + j that torch.stack(real, imag) makes
-  (export_weights.py:104,130-131);
-- the four phase matrices of each transposed convolution back to one
-  ConvTranspose2d weight [cin, cout, 3, 3] (export_weights.py:146-152).
-
-It then runs torch's own reflect padding, strided and transposed
-convolutions and rfftn / irfftn with norm="ortho". This pins the oracle's
-restatement of the things the weights file alone does not say: the phase
+published forward pass in float64 PyTorch of its own, run directly on the
+seeded upstream checkpoint (iec.weights.lama_checkpoint: the tensors the
+reference's tools/lama/export_weights.py reads, under its names): batch norms
+in evaluation mode, the fast Fourier convolutions' four convolutions, the
+Fourier unit's 1x1 convolution over channels that alternate real and
+imaginary parts (torch.stack(real, imag) order), and ConvTranspose2d for the
+upsamplings. The oracle reads the weights file that the reference's exporter
+writes from that checkpoint (byte for byte: tests/test_export_pinning.py), so
+this fixture pins the oracle's reading of the exported layout (folded batch
+norms, the planar real|imaginary reorder, the phase split of the transposed
+convolutions) together with what the file alone does not say: the phase
 taps, the FFT conventions (which parts the inverse reads), the channel order
-of the spectrum and the padding modes.
+of the spectrum and the padding modes. It uses torch's own reflect padding,
+strided and transposed convolutions and rfftn / irfftn with norm="ortho".
 """
 
 from __future__ import annotations
@@ -44,32 +40,14 @@ from iec import weights as W  # noqa: E402
 CASES = [(40, 24, 1), (9, 9, 2), (27, 35, 3)]
 
 
-def torch_state(tensors):
+BN_EPS = 1e-5
+
+
+def torch_state(state):
     import torch
 
-    return {name: torch.from_numpy(np.asarray(a, np.float64)) for name, a, _ in tensors}
-
-
-def conv_weight(m, size):
-    """[(ky, kx, cin), cout] -> [cout, cin, ky, kx]."""
-    k, cout = m.shape
-    cin = k // (size * size)
-    return m.reshape(size, size, cin, cout).permute(3, 2, 0, 1).contiguous()
-
-
-def transposed_weight(phases, cin, cout):
-    """The inverse of weights.lama_phase_matrices."""
-    import torch
-
-    w = torch.zeros(cin, cout, 3, 3, dtype=torch.float64)
-    for p, m in enumerate(phases):
-        ys, xs = W.LAMA_PHASE_TAPS[p // 2], W.LAMA_PHASE_TAPS[p % 2]
-        t = 0
-        for _, ky in ys:
-            for _, kx in xs:
-                w[:, :, ky, kx] = m[t * cin:(t + 1) * cin]
-                t += 1
-    return w
+    return {name: torch.from_numpy(np.asarray(a, np.float64)) for name, a in state.items()
+            if not name.endswith("num_batches_tracked")}
 
 
 def forward(state, image, mask):
@@ -89,47 +67,48 @@ def forward(state, image, mask):
     xs = np.pad(xs, ((0, 0), (0, h - height), (0, w - width)), mode="symmetric")
     x = torch.from_numpy(xs)[None]
 
-    def conv(x, name, size, stride=1, bias=True, reflect=True):
-        pad = size // 2
-        if reflect and pad:
+    def bn(x, name):
+        return F.batch_norm(x, s[f"{name}.running_mean"], s[f"{name}.running_var"], s[f"{name}.weight"],
+                            s[f"{name}.bias"], training=False, eps=BN_EPS)
+
+    def conv(x, weight, stride=1, bias=None):
+        pad = weight.shape[-1] // 2
+        if pad:
             x = F.pad(x, (pad, pad, pad, pad), mode="reflect")
-        b = s[f"{name}.bias"] if bias else None
-        return F.conv2d(x, conv_weight(s[f"{name}.weight"], size), b, stride=stride)
+        return F.conv2d(x, s[weight] if isinstance(weight, str) else weight, bias, stride=stride)
 
-    x = F.relu(conv(x, "first", 7))
-    for i in range(3):
-        x = F.relu(conv(x, f"down{i}", 3, stride=2))
+    x = F.relu(bn(F.conv2d(F.pad(x, (3, 3, 3, 3), mode="reflect"), s["1.ffc.convl2l.weight"]), "1.bn_l"))
+    for layer in (2, 3):
+        x = F.relu(bn(conv(x, s[f"{layer}.ffc.convl2l.weight"], 2), f"{layer}.bn_l"))
+    xl = F.relu(bn(conv(x, s["4.ffc.convl2l.weight"], 2), "4.bn_l"))
+    xg = F.relu(bn(conv(x, s["4.ffc.convl2g.weight"], 2), "4.bn_g"))
 
-    def spectral(xg, name):
-        y = F.relu(conv(xg, f"{name}.spectral_in", 1))
+    def spectral(xg, g):
+        y = F.relu(bn(F.conv2d(xg, s[f"{g}.conv1.0.weight"]), f"{g}.conv1.1"))
         c = y.shape[1]
         hh, ww = y.shape[-2:]
         f = torch.fft.rfftn(y, dim=(-2, -1), norm="ortho")
         f = torch.stack((f.real, f.imag), dim=2).reshape(1, 2 * c, hh, ww // 2 + 1)
-        planar = np.array([2 * ch + j for j in range(2) for ch in range(c)])
-        wf = torch.zeros_like(s[f"{name}.fourier.weight"])
-        bf = torch.zeros_like(s[f"{name}.fourier.bias"])
-        wf[np.ix_(planar, planar)] = s[f"{name}.fourier.weight"]
-        bf[planar] = s[f"{name}.fourier.bias"]
-        f = F.relu(F.conv2d(f, wf.t().reshape(2 * c, 2 * c, 1, 1), bf))
+        f = F.relu(bn(F.conv2d(f, s[f"{g}.fu.conv_layer.weight"]), f"{g}.fu.bn"))
         f = f.reshape(1, c, 2, hh, ww // 2 + 1)
         f = torch.complex(f[:, :, 0], f[:, :, 1])
         back = torch.fft.irfftn(f, s=(hh, ww), dim=(-2, -1), norm="ortho")
-        return F.conv2d(y + back, conv_weight(s[f"{name}.spectral_out.weight"], 1))
+        return F.conv2d(y + back, s[f"{g}.conv2.weight"])
 
-    def ffc(x, name):
-        xl = x[:, :128]
-        local = F.relu(conv(x, f"{name}.local", 3))
-        glob = F.relu(conv(xl, f"{name}.cross", 3) + spectral(x[:, 128:], name))
-        return torch.cat([local, glob], dim=1)
+    def ffc(xl, xg, p):
+        local = conv(xl, s[f"{p}.ffc.convl2l.weight"]) + conv(xg, s[f"{p}.ffc.convg2l.weight"])
+        glob = conv(xl, s[f"{p}.ffc.convl2g.weight"]) + spectral(xg, f"{p}.ffc.convg2g")
+        return F.relu(bn(local, f"{p}.bn_l")), F.relu(bn(glob, f"{p}.bn_g"))
 
     for b in range(18):
-        x = x + ffc(ffc(x, f"block{b}.ffc0"), f"block{b}.ffc1")
-    for i, (cin, cout) in enumerate([(512, 256), (256, 128), (128, 64)]):
-        phases = [s[f"up{i}.phase{p}.weight"] for p in range(4)]
-        wt = transposed_weight(phases, cin, cout)
-        x = F.relu(F.conv_transpose2d(x, wt, s[f"up{i}.phase0.bias"], stride=2, padding=1, output_padding=1))
-    x = torch.sigmoid(conv(x, "last", 7))
+        yl, yg = ffc(xl, xg, f"{5 + b}.conv1")
+        yl, yg = ffc(yl, yg, f"{5 + b}.conv2")
+        xl, xg = xl + yl, xg + yg
+    x = torch.cat([xl, xg], dim=1)
+    for layer in (24, 27, 30):
+        x = F.conv_transpose2d(x, s[f"{layer}.weight"], s[f"{layer}.bias"], stride=2, padding=1, output_padding=1)
+        x = F.relu(bn(x, str(layer + 1)))
+    x = torch.sigmoid(conv(x, s["34.weight"], bias=s["34.bias"]))
     return x[0, :, :height, :width].permute(1, 2, 0).numpy()
 
 
@@ -137,9 +116,8 @@ def main():
     import torch
 
     torch.set_num_threads(8)
-    tensors = W.lama_tensors(0)
-    sha = hashlib.sha256(W.encode(W.MAGIC["lama"], tensors)).hexdigest()
-    state = torch_state(tensors)
+    sha = hashlib.sha256(W.encode(W.MAGIC["lama"], W.lama_tensors(0))).hexdigest()
+    state = torch_state(W.lama_checkpoint(0))
     out = {"weights_sha256": np.array(sha)}
     for i, (width, height, seed) in enumerate(CASES):
         image, mask = W.lama_input(width, height, seed)

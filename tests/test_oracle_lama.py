@@ -1,7 +1,8 @@
 """The CPU oracle's LaMa restatement: its Fourier transforms against the
 reference's own test (crates/lama-native/src/fourier.rs:448-484: the sizes,
 the input sequence and the 1e-5 bound, restated), the network against the
-float64 PyTorch formulation of tests/golden/gen_lama_golden.py, and the
+float64 PyTorch formulation of tests/golden/gen_lama_golden.py run on the
+upstream checkpoint whose exported file the oracle reads, and the
 public API's checks, progress and compositing (lib.rs:118-194)."""
 
 import os
@@ -59,7 +60,8 @@ def test_golden_matches_float64_torch(lama):
         out = model.run_float(g[f"case{i}_image"], g[f"case{i}_mask"])
         ref = g[f"case{i}_out"]
         assert out.shape == ref.shape
-        assert np.abs(out - ref).max() < 1e-3
+        # f32 weights file: the oracle's f32 arithmetic is the only difference
+        assert np.abs(out - ref).max() < 5e-5
 
 
 def test_check_size(lama):

@@ -47,21 +47,30 @@ def test_no_alloc_entry_point_matches_run_device(realesrgan_weights):
             model.run_device(d_in.data_ptr(), count, width, height, want.data_ptr(), stream)
             got = torch.empty_like(want)
             cases.append((count, width, height, d_in, want, got))
-        # One warm call per shape: the first call on a device looks up the
-        # scratch array's address and loads the kernels' code.
+        # One warm call per shape, with every torch operation this test
+        # uses around it: the first call on a device looks up the scratch
+        # array's address, and the first use of a kernel loads its code.
         for count, width, height, d_in, _, got in cases:
-            assert fn(model._h, d_in.data_ptr(), count, width, height, got.data_ptr(), stream) == iec.OK
-        torch.cuda.synchronize()
-        free_before = torch.cuda.mem_get_info()[0]
-        for count, width, height, d_in, want, got in cases:
             got.fill_(float("nan"))
+            assert fn(model._h, d_in.data_ptr(), count, width, height, got.data_ptr(), stream) == iec.OK
+            torch.cuda.synchronize()
+            got.cpu()
+        for case in cases:
+            case[5].fill_(float("nan"))
+        torch.cuda.synchronize()
+        # The two calls in a row, and nothing else, between the two readings
+        # of the device's free memory.
+        free_before = torch.cuda.mem_get_info()[0]
+        for count, width, height, d_in, _, got in cases:
             status = fn(model._h, d_in.data_ptr(), count, width, height, got.data_ptr(), stream)
             assert status == iec.OK, L.iec_last_error()
-            torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        free_after = torch.cuda.mem_get_info()[0]
+        for count, width, height, d_in, want, got in cases:
             g, w = got.cpu().numpy(), want.cpu().numpy()
             assert np.isfinite(g).all()
             assert np.array_equal(g, w), float(np.abs(g - w).max())
-        assert torch.cuda.mem_get_info()[0] == free_before
+        assert free_after == free_before, (free_before - free_after, "bytes of device memory taken")
         # Beyond the fixed scratch: a clear input error, and nothing runs.
         d_in, got = cases[0][3], cases[0][5]
         status = fn(model._h, d_in.data_ptr(), 2, 384, 256, got.data_ptr(), stream)
