@@ -451,6 +451,13 @@ iec_status iec_lama_run_device(iec_lama* model, const float* image, const float*
   });
 }
 
+iec_status iec_lama_set_fused(iec_lama* model, int on) {
+  return guard([&] {
+    need_model(model);
+    model->model->set_fused(on != 0);
+  });
+}
+
 // -------------------------------------------------------------------- BiRefNet
 iec_status iec_birefnet_load(const char* weights_path, const iec_options* options, iec_birefnet** out) {
   return guard([&] {

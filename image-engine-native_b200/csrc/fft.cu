@@ -62,7 +62,7 @@ __device__ __forceinline__ float4 mul_si(float4 v, float s) { return make_float4
 template <int C>
 __device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, const float* ct, const float* st,
                              float sign) {
-  static_assert(C == 2 || C == 4 || C == 8, "channel pairs per point");
+  static_assert(C % 2 == 0 && C >= 2 && C <= 24, "channel pairs per point");
   constexpr int P = C / 2;  // float4 (channel pairs) per point
   const int n = f.n;
   if (f.log2n >= 0) {
@@ -463,6 +463,258 @@ __global__ void __launch_bounds__(FFT_SMALL_THREADS) fft2_inv_small(const __half
   }
 }
 
+// ---------------------------------------------------------------- Fourier unit
+// The spectral 1x1 convolution fused between the column transforms
+// (fft.h, fourier_unit_planar). A cluster of FU_Q CTAs owns the spectrum
+// columns 2 p and 2 p + 1 (MMA rows l * 64 + ky, l the column of the pair);
+// CTA q of the cluster transforms the columns of complex channels
+// 48 q .. 48 q + 47 and puts their f16 spectrum (real parts at K = channel,
+// imaginary parts at K = 192 + channel) into its own A operand; after a
+// cluster barrier each CTA copies the other three quarters of K from its
+// peers' shared memory, issues the 24 K16 MMAs of its output quarter
+// (N = 96: the real and imaginary parts of channels 48 q .. 48 q + 47) and
+// runs bias, ReLU, the f16 rounding and the inverse column transforms of
+// those channels into the row-spectrum scratch.
+constexpr int FU_CH = FOURIER_UNIT_CHANNELS;  // complex channels
+constexpr int FU_K = 2 * FU_CH;               // MMA K: real parts, then imaginary parts
+constexpr int FU_Q = 4;                       // CTAs per cluster: output quarters
+constexpr int FU_QCH = FU_CH / FU_Q;          // 48 complex channels per CTA
+constexpr int FU_N = 2 * FU_QCH;              // 96 MMA columns per CTA
+constexpr int FU_CC = 24;                     // channels per transform chunk
+constexpr int FU_CHUNKS = FU_QCH / FU_CC;     // 2
+constexpr int FU_THREADS = 384;
+constexpr int FU_MAXH = 64;                   // spectrum rows per column (MMA rows per column)
+constexpr int FU_A_BYTES = (FU_K / 8) * 128 * 16;             // 98304
+constexpr int FU_B_BYTES = (FU_K / 8) * FU_N * 16;            // 73728
+constexpr int FU_F_BYTES = 2 * FU_MAXH * FU_CC * 8;           // 24576 per buffer
+constexpr int FU_B_OFF = FU_A_BYTES;
+constexpr int FU_F_OFF = FU_B_OFF + FU_B_BYTES;
+constexpr int FU_TW_OFF = FU_F_OFF + 2 * FU_F_BYTES;
+constexpr int FU_BIAS_OFF = FU_TW_OFF + 2 * FU_MAXH * 4;
+constexpr int FU_BAR_OFF = FU_BIAS_OFF + FU_N * 4;
+constexpr int FU_SMEM = FU_BAR_OFF + 64;
+constexpr uint32_t FU_TMEM_COLS = 128;
+static_assert(FU_SMEM <= 227 * 1024, "Fourier unit shared memory");
+static_assert(FU_CH % (8 * FU_Q) == 0 && FU_QCH % FU_CC == 0 && FU_CC % 8 == 0, "channel split");
+
+struct FuParams {
+  float2* T;             // row spectra [c / 8][h][half][8] complex: read, then overwritten
+  const uint16_t* b;     // [FU_Q][FU_K / 8][FU_N][8] f16
+  const float* bias;     // [FU_Q][FU_N]
+  Dims d;
+  Line f;                // the column transform (n = h)
+  int* dev_err;
+};
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// 16 bytes of CTA `rank`'s shared memory at the offset of `local` in ours.
+__device__ __forceinline__ uint4 ld_peer16(const void* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(remote));
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(FU_THREADS, 1) fourier_unit_cols(const FuParams p) {
+  extern __shared__ __align__(128) uint8_t fu_smem[];
+  uint8_t* A = fu_smem;
+  uint8_t* B = fu_smem + FU_B_OFF;
+  float2* fa = reinterpret_cast<float2*>(fu_smem + FU_F_OFF);
+  float2* fb = reinterpret_cast<float2*>(fu_smem + FU_F_OFF + FU_F_BYTES);
+  float* ct = reinterpret_cast<float*>(fu_smem + FU_TW_OFF);
+  float* st = ct + FU_MAXH;
+  float* sbias = reinterpret_cast<float*>(fu_smem + FU_BIAS_OFF);
+  uint64_t* bbar = reinterpret_cast<uint64_t*>(fu_smem + FU_BAR_OFF);
+  uint64_t* mbar = bbar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fu_smem + FU_BAR_OFF + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(fu_smem + FU_BAR_OFF + 20);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t q = cluster_rank();
+  const int pair = blockIdx.x / FU_Q;
+  const int h = p.d.h, half = p.d.half;
+  const int k0 = 2 * pair;  // first spectrum column of the pair
+  const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)q * FU_B_BYTES;
+
+  if (tid == 0) {
+    mbar_init(bbar, 1);
+    mbar_init(mbar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, FU_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // The weights and bias do not depend on the previous kernel: fetch them
+  // while it drains.
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bbar, (uint32_t)FU_B_BYTES);
+    bulk_load(B, bsrc, (uint32_t)FU_B_BYTES, bbar);
+  }
+  if (tid < FU_N) sbias[tid] = p.bias[q * FU_N + tid];
+  griddep_launch_dependents();
+  griddep_wait();
+  load_twiddles(p.f, ct, st);
+
+  // ---- forward column transforms of this CTA's 48 channels, in chunks.
+  // Every thread's row-spectrum points of both chunks are loaded at once
+  // (one latency), then each chunk is transformed in shared memory.
+  const float scale = p.d.scale;
+  constexpr int TASKS = 2 * FU_MAXH * (FU_CC / 8);  // points of a chunk (lines x rows x groups)
+  constexpr int PER = (TASKS + FU_THREADS - 1) / FU_THREADS;
+  float4 pts[FU_CHUNKS][PER][4];
+#pragma unroll
+  for (int c = 0; c < FU_CHUNKS; c++) {
+    const int g0 = (int)q * (FU_QCH / 8) + c * (FU_CC / 8);
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int t = tid + i * FU_THREADS;
+      const int l = t / (h * (FU_CC / 8)), r = t - l * (h * (FU_CC / 8));
+      const int y = r / (FU_CC / 8), j = r - y * (FU_CC / 8);
+      const bool live = t < 2 * h * (FU_CC / 8) && k0 + l < half;
+      const float4* src = reinterpret_cast<const float4*>(p.T + (((size_t)(g0 + j) * h + y) * half + k0 + l) * 8);
+#pragma unroll
+      for (int e = 0; e < 4; e++) pts[c][i][e] = live ? src[e] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < FU_CHUNKS; c++) {
+    const int g0 = (int)q * (FU_QCH / 8) + c * (FU_CC / 8);
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int t = tid + i * FU_THREADS;
+      if (t < 2 * h * (FU_CC / 8)) {
+        const int l = t / (h * (FU_CC / 8)), r = t - l * (h * (FU_CC / 8));
+        const int y = r / (FU_CC / 8), j = r - y * (FU_CC / 8);
+        float4* dst = reinterpret_cast<float4*>(fa + ((size_t)l * h + y) * FU_CC + 8 * j);
+#pragma unroll
+        for (int e = 0; e < 4; e++) dst[e] = pts[c][i][e];
+      }
+    }
+    __syncthreads();
+    const float2* r = fft_lines<FU_CC>(fa, fb, 2, p.f, ct, st, -1.0f);
+    for (int t = tid; t < 2 * h * (FU_CC / 8); t += FU_THREADS) {
+      const int l = t / (h * (FU_CC / 8)), rr = t - l * (h * (FU_CC / 8));
+      const int ky = rr / (FU_CC / 8), j = rr - ky * (FU_CC / 8);
+      const float2* v = r + ((size_t)l * h + ky) * FU_CC + 8 * j;
+      float vr[8], vi[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        vr[e] = v[e].x * scale;
+        vi[e] = v[e].y * scale;
+      }
+      const int row = l * FU_MAXH + ky, kg = g0 + j;
+      store_half8(reinterpret_cast<__half*>(A + ((size_t)kg * 128 + row) * 16), vr);
+      store_half8(reinterpret_cast<__half*>(A + ((size_t)(FU_CH / 8 + kg) * 128 + row) * 16), vi);
+    }
+    __syncthreads();
+  }
+
+  // ---- the other quarters of K from the cluster's peers: every load of a
+  // thread issued before its stores
+  cluster_sync_all();
+  {
+    constexpr int COPIES = (FU_Q - 1) * 2 * (FU_QCH / 8) * 128;
+    constexpr int CPER = (COPIES + FU_THREADS - 1) / FU_THREADS;
+    uint4 v[CPER];
+    uint8_t* at[CPER];
+#pragma unroll
+    for (int i = 0; i < CPER; i++) {
+      const int t = tid + i * FU_THREADS;
+      const int tt = t < COPIES ? t : 0;
+      const int peer_i = tt / (2 * (FU_QCH / 8) * 128), rest = tt - peer_i * (2 * (FU_QCH / 8) * 128);
+      const uint32_t peer = ((uint32_t)peer_i + q + 1) % FU_Q;
+      const int which = rest / ((FU_QCH / 8) * 128), rr = rest - which * ((FU_QCH / 8) * 128);
+      const int kg = which * (FU_CH / 8) + (int)peer * (FU_QCH / 8) + rr / 128, row = rr % 128;
+      at[i] = t < COPIES ? A + ((size_t)kg * 128 + row) * 16 : nullptr;
+      if (at[i]) v[i] = ld_peer16(at[i], peer);
+    }
+#pragma unroll
+    for (int i = 0; i < CPER; i++)
+      if (at[i]) *reinterpret_cast<uint4*>(at[i]) = v[i];
+  }
+  fence_proxy_async_smem();
+  cluster_sync_all();  // every peer has read our quarter: we may leave at any time from here
+
+  // ---- the 1x1 product: D[128 rows][96] = A[128][384] x B[384][96]
+  if (tid == 0) {
+    if (mbar_wait(bbar, 0, abort_flag, p.dev_err, DEV_ERR_WAIT_WEIGHTS)) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_f16_f32(128, FU_N);
+      const uint32_t abase = smem_u32(A), bbase = smem_u32(B);
+#pragma unroll 4
+      for (int j = 0; j < FU_K / 16; j++) {
+        const uint64_t adesc = smem_desc(abase + (uint32_t)(2 * j * 128 * 16), 128 * 16, 128);
+        const uint64_t bdesc = smem_desc(bbase + (uint32_t)(2 * j * FU_N * 16), FU_N * 16, 128);
+        umma_f16(tmem, adesc, bdesc, idesc, j > 0 ? 1u : 0u);
+      }
+      umma_commit(mbar);
+    }
+  }
+  const bool have = mbar_wait(mbar, 0, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL);
+  tc_fence_after();
+
+  // ---- bias, ReLU, f16, inverse column transforms, chunk by chunk
+  const int quarter = warp & 3, part = warp >> 2;  // TMEM lanes 32 quarter.., 8 channels each
+  const int row = quarter * 32 + lane, l = row / FU_MAXH, ky = row % FU_MAXH;
+  for (int c = 0; c < FU_CHUNKS; c++) {
+    const int cl = c * FU_CC + part * 8;  // this warp's first channel (of the CTA's 48)
+    uint32_t re[8], im[8];
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    tmem_ld8(tmem + lanes + (uint32_t)cl, re);
+    tmem_ld8(tmem + lanes + (uint32_t)(FU_QCH + cl), im);
+    tmem_wait_ld();
+    if (ky < h) {
+      float2 val[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        float vr = __uint_as_float(re[e]) + sbias[cl + e], vi = __uint_as_float(im[e]) + sbias[FU_QCH + cl + e];
+        vr = vr > 0.0f ? vr : 0.0f;
+        vi = vi > 0.0f ? vi : 0.0f;
+        const float2 rounded = __half22float2(__floats2half2_rn(vr, vi));
+        val[e] = have ? rounded : make_float2(0.0f, 0.0f);
+      }
+      float2* dst = fa + ((size_t)l * h + ky) * FU_CC + part * 8;
+#pragma unroll
+      for (int e = 0; e < 8; e++) dst[e] = val[e];
+    }
+    __syncthreads();
+    const float2* r = fft_lines<FU_CC>(fa, fb, 2, p.f, ct, st, 1.0f);
+    const int g0 = (int)q * (FU_QCH / 8) + c * (FU_CC / 8);
+    for (int t = tid; t < 2 * h * (FU_CC / 8); t += FU_THREADS) {
+      const int ll = t / (h * (FU_CC / 8)), rr = t - ll * (h * (FU_CC / 8));
+      const int y = rr / (FU_CC / 8), j = rr - y * (FU_CC / 8);
+      if (k0 + ll < half)
+        copy_point(p.T + (((size_t)(g0 + j) * h + y) * half + k0 + ll) * 8, r + ((size_t)ll * h + y) * FU_CC + 8 * j);
+    }
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, FU_TMEM_COLS);
+}
+
 // Shared memory of the one-launch transforms for C channels per CTA.
 size_t small_smem(const FourierPlan& p, int c) {
   const size_t pts = std::max((size_t)p.h * p.w, (size_t)p.half * p.h);
@@ -507,6 +759,24 @@ size_t smem_for(int lines, int n) { return (size_t)2 * lines * n * 8 * sizeof(fl
 template <class K>
 void prepare(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) IEC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
+// The row passes of the two-launch transforms: x -> row spectra, and row
+// spectra -> added on x.
+void launch_rows_fwd(const FourierPlan& plan, const Dims& d, const __half* x, long long x_plane_elems, cudaStream_t s) {
+  const size_t sr = smem_for(d.lines_rows, d.w);
+  prepare(fft_rows_fwd, sr);
+  launch_pdl(fft_rows_fwd, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, x,
+             x_plane_elems, plan.scratch.as<float2>(), d, line_of(plan, true));
+  IEC_CUDA(cudaGetLastError());
+}
+
+void launch_rows_inv(const FourierPlan& plan, const Dims& d, __half* x, long long x_plane_elems, cudaStream_t s) {
+  const size_t sr = smem_for(d.lines_rows, d.w);
+  prepare(fft_rows_inv, sr);
+  launch_pdl(fft_rows_inv, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s,
+             (const float2*)plan.scratch.as<float2>(), x, x_plane_elems, d, line_of(plan, true));
+  IEC_CUDA(cudaGetLastError());
 }
 
 }  // namespace
@@ -565,12 +835,9 @@ void rfft2_planar(const FourierPlan& plan, const __half* x, long long x_plane_el
     default: break;
   }
   float2* T = plan.scratch.as<float2>();
-  const size_t sr = smem_for(d.lines_rows, d.w), sc = smem_for(d.lines_cols, d.h);
-  prepare(fft_rows_fwd, sr);
+  const size_t sc = smem_for(d.lines_cols, d.h);
+  launch_rows_fwd(plan, d, x, x_plane_elems, s);
   prepare(fft_cols_fwd, sc);
-  launch_pdl(fft_rows_fwd, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, 
-      x, x_plane_elems, T, d, line_of(plan, true));
-  IEC_CUDA(cudaGetLastError());
   launch_pdl(fft_cols_fwd, dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s, 
       T, spec, spec_plane_elems, d, line_of(plan, false));
   IEC_CUDA(cudaGetLastError());
@@ -586,15 +853,79 @@ void irfft2_add_planar(const FourierPlan& plan, const __half* spec, long long sp
     default: break;
   }
   float2* T = plan.scratch.as<float2>();
-  const size_t sr = smem_for(d.lines_rows, d.w), sc = smem_for(d.lines_cols, d.h);
+  const size_t sc = smem_for(d.lines_cols, d.h);
   prepare(fft_cols_inv, sc);
-  prepare(fft_rows_inv, sr);
   launch_pdl(fft_cols_inv, dim3((d.half + d.lines_cols - 1) / d.lines_cols, d.groups), FFT_THREADS, sc, s, 
       spec, spec_plane_elems, T, d, line_of(plan, false));
   IEC_CUDA(cudaGetLastError());
-  launch_pdl(fft_rows_inv, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, 
-      T, x, x_plane_elems, d, line_of(plan, true));
-  IEC_CUDA(cudaGetLastError());
+  launch_rows_inv(plan, d, x, x_plane_elems, s);
+}
+
+void pack_fourier_weights(FourierWeights& fw, const std::vector<float>& w, const std::vector<float>& bias) {
+  if (w.size() != (size_t)FU_K * FU_K || bias.size() != (size_t)FU_K)
+    throw Error(ERR_WEIGHTS, "Fourier unit weights of the wrong size");
+  // CTA q's MMA column n: the real part (n < 48) or the imaginary part of
+  // complex channel 48 q + n % 48, whose planar column is that channel or
+  // 192 + that channel.
+  auto column = [](int quarter, int n) { return (n < FU_QCH ? 0 : FU_CH) + quarter * FU_QCH + n % FU_QCH; };
+  std::vector<uint16_t> b((size_t)FU_Q * FU_K * FU_N);
+  std::vector<float> bb((size_t)FU_Q * FU_N);
+  for (int q = 0; q < FU_Q; q++)
+    for (int n = 0; n < FU_N; n++) {
+      const int col = column(q, n);
+      bb[(size_t)q * FU_N + n] = bias[col];
+      for (int k = 0; k < FU_K; k++)
+        b[(((size_t)q * (FU_K / 8) + k / 8) * FU_N + n) * 8 + k % 8] = f32_to_half(w[(size_t)k * FU_K + col]);
+    }
+  fw.b.reserve(b.size() * 2);
+  fw.bias.reserve(bb.size() * 4);
+  IEC_CUDA(cudaMemcpy(fw.b.get(), b.data(), b.size() * 2, cudaMemcpyHostToDevice));
+  IEC_CUDA(cudaMemcpy(fw.bias.get(), bb.data(), bb.size() * 4, cudaMemcpyHostToDevice));
+}
+
+bool fourier_unit_fits(const FourierPlan& plan) {
+  return plan.channels == FU_CH && plan.h <= FU_MAXH && plan.w >= 1 && !plan.two_pass;
+}
+
+void fourier_unit_planar(const FourierPlan& plan, const FourierWeights& fw, __half* x, long long x_plane_elems,
+                         int* dev_err, cudaStream_t s, int only) {
+  if (!fourier_unit_fits(plan)) throw Error(ERR_INPUT, "the fused Fourier unit takes 192 channels and up to 64 rows");
+  const Dims d = dims_of(plan);
+  if (only == 0 || only == 1) launch_rows_fwd(plan, d, x, x_plane_elems, s);
+  if (only == 1 || only == 3) {
+    if (only == 3) launch_rows_inv(plan, d, x, x_plane_elems, s);
+    return;
+  }
+  static bool prepared[64] = {};
+  int dev = 0;
+  IEC_CUDA(cudaGetDevice(&dev));
+  if (!prepared[dev & 63]) {
+    IEC_CUDA(cudaFuncSetAttribute(fourier_unit_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, FU_SMEM));
+    prepared[dev & 63] = true;
+  }
+  FuParams fp;
+  fp.T = plan.scratch.as<float2>();
+  fp.b = fw.b.as<uint16_t>();
+  fp.bias = fw.bias.as<float>();
+  fp.d = d;
+  fp.f = line_of(plan, false);
+  fp.dev_err = dev_err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(FU_Q * ((d.half + 1) / 2));
+  cfg.blockDim = dim3(FU_THREADS);
+  cfg.dynamicSmemBytes = FU_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = FU_Q;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  IEC_CUDA(cudaLaunchKernelEx(&cfg, fourier_unit_cols, fp));
+  if (only == 0) launch_rows_inv(plan, d, x, x_plane_elems, s);
 }
 
 }  // namespace iec

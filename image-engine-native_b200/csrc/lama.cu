@@ -33,6 +33,7 @@ namespace iec {
 
 struct Lama::Ffc {
   PackedWeights local, cross, spectral_in, fourier, spectral_out;
+  FourierWeights fourier_unit;  // the same Fourier matrix for the fused unit
 };
 
 namespace {
@@ -189,7 +190,12 @@ Lama::Lama(const std::string& path, const Options& opt) : dev_(opt) {
       matrix(f, F->local, name + ".local", 9, CHANNELS, LOCAL, true);
       matrix(f, F->cross, name + ".cross", 9, LOCAL, GLOBAL, true);
       matrix(f, F->spectral_in, name + ".spectral_in", 1, GLOBAL, SPECTRAL, true);
-      matrix(f, F->fourier, name + ".fourier", 1, 2 * SPECTRAL, 2 * SPECTRAL, true);
+      {
+        HostTensor w = f.take_tensor(name + ".fourier.weight", {2 * SPECTRAL, 2 * SPECTRAL});
+        std::vector<float> b = f.take(name + ".fourier.bias", {2 * SPECTRAL});
+        pack_weights(F->fourier, w.values, 1, 2 * SPECTRAL, 2 * SPECTRAL, b.data());
+        pack_fourier_weights(F->fourier_unit, w.values, b);
+      }
       matrix(f, F->spectral_out, name + ".spectral_out", 1, SPECTRAL, GLOBAL, false);
       ffc_.push_back(std::move(F));
     }
@@ -284,15 +290,19 @@ void Lama::ffc(const Ffc& F, const __half* in, __half* out, __half* tmp, bool re
     so.plane_elems = spec_plane;
     gemm_taps(dev_, F.spectral_in, g.source(in, LOCAL / 8), {{1, 1, 0}}, h8, w8, ACT_RELU, so, s_spec_);
   }
-  rfft2_planar(plan_, spectral, spec_plane, spectrum_.as<__half>(), freq_plane, s_spec_);
-  {
+  if (fused_unit_ && fourier_unit_fits(plan_)) {
+    // rfft2, the Fourier 1x1 (ReLU) and irfft2 added on the spectral map,
+    // the spectrum kept on chip (fft.h)
+    fourier_unit_planar(plan_, F.fourier_unit, spectral, spec_plane, dev_.dev_err(), s_spec_);
+  } else {
+    rfft2_planar(plan_, spectral, spec_plane, spectrum_.as<__half>(), freq_plane, s_spec_);
     GemmOutSpec fo;
     fo.mode = OUT_STORE;
     fo.out = filtered_.as<__half>();
     fo.plane_elems = freq_plane;
     gemm_rows(dev_, F.fourier, spectrum_.as<__half>(), freq_plane, h8 * half, ACT_RELU, fo, s_spec_);
+    irfft2_add_planar(plan_, filtered_.as<__half>(), freq_plane, spectral, spec_plane, s_spec_);
   }
-  irfft2_add_planar(plan_, filtered_.as<__half>(), freq_plane, spectral, spec_plane, s_spec_);
   IEC_CUDA(cudaEventRecord(ev_spec_, s_spec_));
   // global = cross(local part) + spectral_out(spectral + irfft2(...)), then ReLU
   __half* global = residual ? tmp : out;

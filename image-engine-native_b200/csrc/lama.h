@@ -45,6 +45,13 @@ class Lama {
 
   DeviceBuffer host_in, host_mask, host_out;  // staging of the host entry points
 
+  // The fused Fourier unit (default) or rfft2, GEMM and irfft2 as separate
+  // launches (for comparisons); the two give the same values.
+  void set_fused(bool on) {
+    fused_unit_ = on;
+    alloc_gen_++;  // no captured pass of the other path replays
+  }
+
   struct Ffc;
 
  private:
@@ -66,6 +73,7 @@ class Lama {
   cudaStream_t s_local_ = nullptr, s_spec_ = nullptr;
   cudaEvent_t ev_in_ = nullptr, ev_local_ = nullptr, ev_spec_ = nullptr;
   PassGraph graph_;
+  bool fused_unit_ = true;
   uint64_t alloc_gen_ = 0;  // counts ensure()'s reallocations  // passes without progress reports
 };
 

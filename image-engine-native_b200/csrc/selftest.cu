@@ -5,6 +5,8 @@
 
 #include <algorithm>
 #include <chrono>
+#include <functional>
+#include <vector>
 #include <memory>
 #include <string>
 
@@ -167,6 +169,68 @@ extern "C" iec_status iec_selftest_rfft2(int device, const float* x, int h, int 
     irfft2_add_planar(plan, dspec.as<__half>(), fp, dx.as<__half>(), xp, s);
     planar_to_rows(dx.as<__half>(), xp, rows, c, d32.as<float>(), s);
     IEC_CUDA(cudaMemcpyAsync(back, d32.get(), (size_t)rows * c * 4, cudaMemcpyDeviceToHost, s));
+    dev.sync(s);
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
+// Diagnostics: LaMa's Fourier unit (x += irfft2(relu(rfft2(x) W + b))) on an
+// h x w map of 192 channels, zero weights and a seeded map, `iters` times
+// back to back after 3 warm-up runs: us[0] the fused unit, us[1] its row
+// transforms alone, us[2] its column kernel alone, us[3] its inverse row
+// transforms alone, us[4] rfft2, the GEMM and irfft2 as separate launches;
+// device microseconds per run (CUDA events on the launch stream).
+extern "C" iec_status iec_selftest_fourier_unit_time(int device, int h, int w, int iters, float* us) {
+  try {
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    const int c = FOURIER_UNIT_CHANNELS, half = w / 2 + 1;
+    FourierPlan plan;
+    fourier_plan(plan, h, w, c);
+    if (!fourier_unit_fits(plan)) throw Error(ERR_INPUT, "Fourier unit timing: up to 64 rows");
+    std::vector<float> wm((size_t)2 * c * 2 * c, 0.0f), bias((size_t)2 * c, 0.0f);
+    FourierWeights fw;
+    pack_fourier_weights(fw, wm, bias);
+    PackedWeights pw;
+    pack_weights(pw, wm, 1, 2 * c, 2 * c, bias.data());
+    const long long xp = (long long)gemm_rows_alloc(h * w) * 8, fp = (long long)gemm_rows_alloc(h * half) * 8;
+    DeviceBuffer x, spec, filt;
+    x.reserve((size_t)xp * (c / 8) * 2);
+    spec.reserve((size_t)fp * (2 * c / 8) * 2);
+    filt.reserve((size_t)fp * (2 * c / 8) * 2);
+    cudaStream_t s = dev.stream();
+    IEC_CUDA(cudaMemsetAsync(x.get(), 0, (size_t)xp * (c / 8) * 2, s));
+    IEC_CUDA(cudaMemsetAsync(spec.get(), 0, (size_t)fp * (2 * c / 8) * 2, s));
+    cudaEvent_t e0, e1;
+    IEC_CUDA(cudaEventCreate(&e0));
+    IEC_CUDA(cudaEventCreate(&e1));
+    auto timed = [&](const std::function<void()>& run) {
+      for (int i = 0; i < 3; i++) run();
+      IEC_CUDA(cudaEventRecord(e0, s));
+      for (int i = 0; i < iters; i++) run();
+      IEC_CUDA(cudaEventRecord(e1, s));
+      dev.sync(s);
+      float ms = 0;
+      IEC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+      return ms * 1000.0f / (float)iters;
+    };
+    for (int only = 0; only < 4; only++)
+      us[only] = timed([&] { fourier_unit_planar(plan, fw, x.as<__half>(), xp, dev.dev_err(), s, only); });
+    us[4] = timed([&] {
+      rfft2_planar(plan, x.as<__half>(), xp, spec.as<__half>(), fp, s);
+      GemmOutSpec fo;
+      fo.mode = OUT_STORE;
+      fo.out = filt.as<__half>();
+      fo.plane_elems = fp;
+      gemm_rows(dev, pw, spec.as<__half>(), fp, h * half, ACT_RELU, fo, s);
+      irfft2_add_planar(plan, filt.as<__half>(), fp, x.as<__half>(), xp, s);
+    });
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
     dev.sync(s);
     return IEC_OK;
   } catch (const Error& e) {

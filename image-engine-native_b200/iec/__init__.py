@@ -70,6 +70,10 @@ def lib():
         L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_set_fused.argtypes = [vp, ctypes.c_int]
         L.iec_realesrgan_set_fused.restype = ctypes.c_int
+        L.iec_lama_set_fused.argtypes = [vp, ctypes.c_int]
+        L.iec_selftest_fourier_unit_time.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.POINTER(ctypes.c_float)]
+        L.iec_lama_set_fused.restype = ctypes.c_int
         L.iec_realesrgan_launches.argtypes = [vp, sz, sz, sz]
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
@@ -363,6 +367,10 @@ class Lama:
     def gpu(self) -> str:
         return lib().iec_lama_device_name(self._h).decode()
 
+    def set_fused(self, on: bool):
+        """Fused Fourier units (default) or rfft2, GEMM and irfft2 apart."""
+        _check(lib().iec_lama_set_fused(self._h, 1 if on else 0))
+
     def run_float(self, image: np.ndarray, mask: np.ndarray) -> np.ndarray:
         """Model::run_float: the prediction (HxWx3) for an HxWx3 image in
         0..=1 and an HxW mask (1 fills)."""
@@ -446,6 +454,15 @@ def selftest_rfft2(x: np.ndarray, device: int = -1, two_pass: bool = False):
     back = np.empty_like(x)
     _check(lib().iec_selftest_rfft2(device, _f32(x), h, w, c, 1 if two_pass else 0, _f32(spec), _f32(back)))
     return spec, back
+
+
+def selftest_fourier_unit_time(h: int = 64, w: int = 64, iters: int = 50, device: int = -1):
+    """Device microseconds per run of LaMa's Fourier unit on an h x w map of
+    192 channels: (fused unit, its row transforms, its column kernel, its
+    inverse row transforms, rfft2 + GEMM + irfft2 as separate launches)."""
+    us = (ctypes.c_float * 5)()
+    _check(lib().iec_selftest_fourier_unit_time(device, h, w, iters, us))
+    return tuple(us)
 
 
 def selftest_wait_timeout(which: int, device: int = -1) -> int:

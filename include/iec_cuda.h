@@ -240,6 +240,13 @@ iec_status iec_lama_run(iec_lama* model, const uint8_t* rgb, const uint8_t* mask
 iec_status iec_lama_run_device(iec_lama* model, const float* image, const float* mask, size_t width,
                                size_t height, float* out, void* stream);
 
+/* Each Fourier unit runs fused (the default, `on` = 1: rfft2, the spectral
+ * 1x1 convolution and irfft2 in three launches, the spectrum kept in shared
+ * memory and TMEM) or, with `on` = 0, as a forward transform, a GEMM and an
+ * inverse transform through device buffers. The outputs are identical; this
+ * switch exists to compare the two (no counterpart in the reference). */
+iec_status iec_lama_set_fused(iec_lama* model, int on);
+
 /* ---------------------------------------------------------------- BiRefNet
  * crates/birefnet-native/src/lib.rs: BiRefNet-lite background removal. The
  * side must be a positive multiple of 64 (lib.rs:175-187); at most 8192 here. */
@@ -292,6 +299,13 @@ iec_status iec_selftest_rfft2(int device, const float* x, int h, int w, int c, i
  * microseconds replayed from a CUDA graph. */
 iec_status iec_selftest_gemm_time(int device, int mode, int m_or_h, int w, int k, int n, int out_map,
                                   int sources, int act, int iters, float* us);
+
+/* Diagnostics: LaMa's Fourier unit (x += irfft2(relu(rfft2(x) W + b)), 192
+ * channels, h <= 64) on device buffers, `iters` runs back to back: us[0] the
+ * fused unit, us[1] its row transforms alone, us[2] its column kernel alone,
+ * us[3] its inverse row transforms alone, us[4] rfft2, the GEMM and irfft2
+ * as separate launches; device microseconds per run. */
+iec_status iec_selftest_fourier_unit_time(int device, int h, int w, int iters, float* us);
 
 /* Diagnostics: the fused window attention on host arrays: `qkv` windows * 64
  * rows of 3c (q | k | v), `bias` classes x (c / 32) x 64 x 64, `out` windows *

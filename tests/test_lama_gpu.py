@@ -187,3 +187,23 @@ def test_one_launch_rfft2_equals_two_launch(h, w, c):
     s2, b2 = iec.selftest_rfft2(x, two_pass=True)
     assert np.array_equal(s1.view(np.uint32), s2.view(np.uint32))
     assert np.array_equal(b1.view(np.uint32), b2.view(np.uint32))
+
+
+@pytest.mark.parametrize("width,height,seed", [(512, 512, 0), (392, 512, 1), (27, 35, 3), (9, 9, 5), (40, 600, 6)])
+def test_fused_fourier_unit_equals_separate_launches(gpu_model, width, height, seed):
+    """The fused Fourier unit (column transforms, the spectral 1x1 on tcgen05
+    and the inverse column transforms in one kernel, the spectrum in shared
+    memory and TMEM) rounds exactly where rfft2, the GEMM and irfft2 round
+    through device buffers: the network's output is the same bit for bit.
+    392 wide: 25 spectrum columns (an odd count, a column pair half empty)
+    and a 49-point row transform; 600 high: a 75-row map, which takes the
+    separate launches either way."""
+    image, mask = W.lama_input(width, height, seed)
+    try:
+        fused = gpu_model.run_float(image, mask)
+        gpu_model.set_fused(False)
+        apart = gpu_model.run_float(image, mask)
+    finally:
+        gpu_model.set_fused(True)
+    assert np.isfinite(fused).all()
+    assert np.array_equal(fused.view(np.uint32), apart.view(np.uint32)), float(np.abs(fused - apart).max())
