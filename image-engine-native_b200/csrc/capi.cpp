@@ -5,6 +5,7 @@
 
 #include <cstring>
 #include <limits>
+#include <functional>
 #include <memory>
 #include <string>
 
@@ -74,10 +75,96 @@ struct iec_realesrgan {
   ~iec_realesrgan() { tag = 0; }
 };
 
+namespace iec {
+
+// The copies and kernels of a batched host entry point overlapped on three
+// streams: the H2D copy of image i + 1 and the D2H copy of image i - 1 run
+// while image i computes on the caller's stream; two device buffers of each
+// kind alternate, so every image runs on one of two fixed buffer pairs.
+struct BatchPipe {
+  int device = -1;
+  DeviceBuffer in[2], out[2];
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_h2d[2] = {}, ev_done[2] = {}, ev_d2h[2] = {};
+
+  struct Source {
+    const void* ptr;
+    size_t bytes;  // per image
+  };
+  using Compute = std::function<void(size_t, const uint8_t*, uint8_t*, cudaStream_t)>;
+
+  ~BatchPipe() {
+    if (device < 0) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    for (cudaEvent_t e : {ev_start, ev_h2d[0], ev_h2d[1], ev_done[0], ev_done[1], ev_d2h[0], ev_d2h[1]})
+      if (e) cudaEventDestroy(e);
+    for (cudaStream_t st : {h2d, d2h})
+      if (st) cudaStreamDestroy(st);
+    for (int b = 0; b < 2; b++) {
+      in[b].release();
+      out[b].release();
+    }
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+
+  // `compute(i, d_in, d_out, s)` runs image i from d_in (the sources' bytes
+  // one after another) into d_out (out_bytes) on s. Returns when every
+  // output is in `dst` (image i at dst + i out_bytes).
+  void run(Device& dev, size_t count, const std::vector<Source>& srcs, void* dst, size_t out_bytes, cudaStream_t s,
+           const Compute& compute) {
+    if (device < 0) {
+      device = dev.ordinal();
+      IEC_CUDA(cudaStreamCreateWithFlags(&h2d, cudaStreamNonBlocking));
+      IEC_CUDA(cudaStreamCreateWithFlags(&d2h, cudaStreamNonBlocking));
+      IEC_CUDA(cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming));
+      for (int b = 0; b < 2; b++) {
+        IEC_CUDA(cudaEventCreateWithFlags(&ev_h2d[b], cudaEventDisableTiming));
+        IEC_CUDA(cudaEventCreateWithFlags(&ev_done[b], cudaEventDisableTiming));
+        IEC_CUDA(cudaEventCreateWithFlags(&ev_d2h[b], cudaEventDisableTiming));
+      }
+    }
+    size_t in_bytes = 0;
+    for (const Source& src : srcs) in_bytes += src.bytes;
+    for (int b = 0; b < 2; b++) {
+      in[b].reserve(in_bytes);
+      out[b].reserve(out_bytes);
+    }
+    IEC_CUDA(cudaEventRecord(ev_start, s));
+    IEC_CUDA(cudaStreamWaitEvent(h2d, ev_start, 0));
+    IEC_CUDA(cudaStreamWaitEvent(d2h, ev_start, 0));
+    for (size_t i = 0; i < count; i++) {
+      const int b = (int)(i & 1);
+      if (i >= 2) IEC_CUDA(cudaStreamWaitEvent(h2d, ev_done[b], 0));  // image i - 2 has read in[b]
+      size_t at = 0;
+      for (const Source& src : srcs) {
+        IEC_CUDA(cudaMemcpyAsync(in[b].as<uint8_t>() + at, static_cast<const uint8_t*>(src.ptr) + i * src.bytes,
+                                 src.bytes, cudaMemcpyHostToDevice, h2d));
+        at += src.bytes;
+      }
+      IEC_CUDA(cudaEventRecord(ev_h2d[b], h2d));
+      IEC_CUDA(cudaStreamWaitEvent(s, ev_h2d[b], 0));
+      if (i >= 2) IEC_CUDA(cudaStreamWaitEvent(s, ev_d2h[b], 0));  // image i - 2's output is copied out
+      compute(i, in[b].as<uint8_t>(), out[b].as<uint8_t>(), s);
+      IEC_CUDA(cudaEventRecord(ev_done[b], s));
+      IEC_CUDA(cudaStreamWaitEvent(d2h, ev_done[b], 0));
+      IEC_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(dst) + i * out_bytes, out[b].get(), out_bytes,
+                               cudaMemcpyDeviceToHost, d2h));
+      IEC_CUDA(cudaEventRecord(ev_d2h[b], d2h));
+    }
+    for (int b = 0; b < 2 && (size_t)b < count; b++) IEC_CUDA(cudaStreamWaitEvent(s, ev_d2h[b], 0));
+    dev.sync(s);
+  }
+};
+
+}  // namespace iec
+
 struct iec_scunet {
   static constexpr uint32_t TAG = 0x53434e54;  // "SCNT"
   uint32_t tag = TAG;
   std::unique_ptr<Scunet> model;
+  BatchPipe batch;
   ~iec_scunet() { tag = 0; }
 };
 
@@ -85,6 +172,7 @@ struct iec_lama {
   static constexpr uint32_t TAG = 0x4c414d41;  // "LAMA"
   uint32_t tag = TAG;
   std::unique_ptr<Lama> model;
+  BatchPipe batch;
   ~iec_lama() { tag = 0; }
 };
 
@@ -92,6 +180,7 @@ struct iec_birefnet {
   static constexpr uint32_t TAG = 0x42524e54;  // "BRNT"
   uint32_t tag = TAG;
   std::unique_ptr<Birefnet> model;
+  BatchPipe batch;
   ~iec_birefnet() { tag = 0; }
 };
 
@@ -365,6 +454,26 @@ iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t w
   });
 }
 
+iec_status iec_scunet_run_batch(iec_scunet* model, const float* images, size_t count, size_t width, size_t height,
+                                float* out, void* stream) {
+  return guard([&] {
+    need_model(model);
+    need(images, "images");
+    need(out, "out");
+    if (count == 0) return;
+    check_scunet_size(width, height);
+    Scunet& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    const size_t bytes = width * height * 3 * 4;
+    model->batch.run(m.device(), count, {{images, bytes}}, out, bytes, s,
+                     [&](size_t, const uint8_t* in, uint8_t* o, cudaStream_t st) {
+                       m.run_whole_device(reinterpret_cast<const float*>(in), reinterpret_cast<float*>(o),
+                                          (int)width, (int)height, st);
+                     });
+  });
+}
+
 iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, size_t height, uint8_t* out,
                           iec_progress_fn progress, void* user) {
   return scunet_host(model, rgb, true, width, height, false, Scunet::TILE, Scunet::MARGIN, out, progress, user);
@@ -458,6 +567,26 @@ iec_status iec_lama_set_fused(iec_lama* model, int on) {
   });
 }
 
+iec_status iec_lama_run_batch(iec_lama* model, const float* images, const float* masks, size_t count, size_t width,
+                              size_t height, float* out, void* stream) {
+  return guard([&] {
+    need_model(model);
+    need(images, "images");
+    need(masks, "masks");
+    need(out, "out");
+    if (count == 0) return;
+    check_lama_size(width, height);
+    Lama& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    const size_t ib = width * height * 3 * 4, mb = width * height * 4;
+    model->batch.run(m.device(), count, {{images, ib}, {masks, mb}}, out, ib, s,
+                     [&](size_t, const uint8_t* in, uint8_t* o, cudaStream_t st) {
+                       m.run(in, false, in + ib, false, o, false, (int)width, (int)height, nullptr, st);
+                     });
+  });
+}
+
 // -------------------------------------------------------------------- BiRefNet
 iec_status iec_birefnet_load(const char* weights_path, const iec_options* options, iec_birefnet** out) {
   return guard([&] {
@@ -524,6 +653,24 @@ iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int i
     DeviceScope scope(m.device());
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
     m.run(image, image_u8 != 0, (int)side, logits, s);
+  });
+}
+
+iec_status iec_birefnet_run_batch(iec_birefnet* model, const uint8_t* images, size_t count, size_t side,
+                                  float* logits, void* stream) {
+  return guard([&] {
+    need_model(model);
+    need(images, "images");
+    need(logits, "logits");
+    if (count == 0) return;
+    check_birefnet_size(side);
+    Birefnet& m = *model->model;
+    DeviceScope scope(m.device());
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.device().stream();
+    model->batch.run(m.device(), count, {{images, side * side * 3}}, logits, side * side * 4, s,
+                     [&](size_t, const uint8_t* in, uint8_t* o, cudaStream_t st) {
+                       m.run(in, true, (int)side, reinterpret_cast<float*>(o), st);
+                     });
   });
 }
 

@@ -6,9 +6,12 @@
 // store moves whole 16-byte pixel groups. A CTA holds up to 512 points
 // (several short lines, or one long one) in shared memory and transforms them
 // in place of fourier.rs's recursive mixed-radix FFT (fourier.rs:16-139):
-// radix-2 Stockham passes when n is a power of two, else the direct sum of
-// the transform's definition. Twiddles are cos / sin of 2 pi j / n computed
-// in double and rounded to f32, as fourier.rs:45-52 makes them.
+// radix-4 (and one radix-2) Stockham passes when n is a power of two, else
+// mixed-radix Stockham passes over n's factors in fourier.rs's order (4 while
+// it divides n, then 2, then the odd primes ascending; radices 3, 5 and 7
+// unrolled, any other prime as its own r-point sum). Twiddles are cos / sin
+// of 2 pi j / n computed in double and rounded to f32, as fourier.rs:45-52
+// makes them.
 //   forward: rows  real -> complex (all n outputs, the first w/2 + 1 kept)
 //            cols  complex, times 1 / sqrt(h w), to the f16 spectrum
 //   inverse: cols  complex from the f16 spectrum
@@ -35,13 +38,6 @@ constexpr int FFT_SMALL_THREADS = 1024;  // the one-launch transforms: a stage's
 constexpr int FFT_POINTS = 512;   // points per CTA when lines are short
 constexpr int FFT_MAX_N = 1536;   // longest line (shared memory: 2 x 64 n bytes)
 
-struct Line {
-  int n, log2n;  // log2n < 0: not a power of two
-  const float* cos_t;
-  const float* sin_t;
-};
-
-
 __device__ __forceinline__ float4 cmul2(float4 v, float wr, float wi) {
   return make_float4(v.x * wr - v.y * wi, v.x * wi + v.y * wr, v.z * wr - v.w * wi, v.z * wi + v.w * wr);
 }
@@ -49,6 +45,60 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) { return make_float4(
 __device__ __forceinline__ float4 sub4(float4 a, float4 b) { return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w); }
 // v times (s i): (x + i y)(s i) = -s y + i s x, for both complex values of v.
 __device__ __forceinline__ float4 mul_si(float4 v, float s) { return make_float4(-s * v.y, s * v.x, -s * v.w, s * v.z); }
+
+struct Line {
+  int n, log2n;  // log2n < 0: not a power of two
+  const float* cos_t;
+  const float* sin_t;
+  int nf;        // other lengths: the radices of the stages, in order
+  int fac[12];
+};
+
+// One Stockham stage of radix r for lines of n points x C channels:
+// for span m (the product of the earlier radices) the r points
+// k + j m + q n / r (q < r) of sub-transform (j, k) go through an r-point
+// DFT (its roots of unity w^(n / r (p q mod r)) from the n-point table) and
+// out to k + (r j + p) m turned by w^(p j m), w = exp(sign 2 pi i / n): the
+// radix-2 and radix-4 stages of the power-of-two path, for any radix.
+template <int C, int R>
+__device__ __forceinline__ void radix_stage(const float4* __restrict__ src4, float4* __restrict__ dst4, int lines,
+                                            int n, int r, int m, const float* ct, const float* st, float sign) {
+  constexpr int P = C / 2;
+  const int rr = R > 0 ? R : r, stride = n / rr, total = lines * stride * P;
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int cc = t % P, rest = t / P, line = rest / stride, i = rest - line * stride;
+    const int j = i / m, k = i - j * m;
+    const int base = line * n * P + cc;
+    if constexpr (R > 0) {
+      float4 x[R];
+#pragma unroll
+      for (int q = 0; q < R; q++) x[q] = src4[base + (k + j * m + q * stride) * P];
+#pragma unroll
+      for (int p = 0; p < R; p++) {
+        float4 acc = x[0];
+#pragma unroll
+        for (int q = 1; q < R; q++) {
+          const int idx = stride * ((p * q) % R);
+          acc = add4(acc, cmul2(x[q], ct[idx], sign * st[idx]));
+        }
+        const int tw = p * j * m;
+        dst4[base + (k + (R * j + p) * m) * P] = p == 0 ? acc : cmul2(acc, ct[tw], sign * st[tw]);
+      }
+    } else {
+      for (int p = 0; p < rr; p++) {
+        float4 acc = src4[base + (k + j * m) * P];
+        for (int q = 1; q < rr; q++) {
+          const int idx = stride * ((p * q) % rr);
+          acc = add4(acc, cmul2(src4[base + (k + j * m + q * stride) * P], ct[idx], sign * st[idx]));
+        }
+        const int tw = p * j * m;
+        dst4[base + (k + (rr * j + p) * m) * P] = p == 0 ? acc : cmul2(acc, ct[tw], sign * st[tw]);
+      }
+    }
+  }
+}
+
+
 
 // Transforms `lines` lines of f.n points x C channels held in `a`
 // ([line][n][C] complex) with `b` as the other buffer, sign -1 forward or +1
@@ -111,25 +161,28 @@ __device__ float2* fft_lines(float2* a, float2* b, int lines, const Line f, cons
     }
     return a;
   }
-  const int total = lines * n * C;
-  for (int t = threadIdx.x; t < total; t += blockDim.x) {
-    const int c = t % C, r = t / C;
-    const int line = r / n, k = r - line * n;
-    const float2* src = a + (size_t)line * n * C;
-    float re = 0.0f, im = 0.0f;
-    int idx = 0;
-    for (int j = 0; j < n; j++) {
-      const float2 x = src[j * C + c];
-      const float wr = ct[idx], wi = sign * st[idx];
-      re += x.x * wr - x.y * wi;
-      im += x.x * wi + x.y * wr;
-      idx += k;
-      if (idx >= n) idx -= n;
+  // Other lengths: mixed-radix stages (radix 4 while it divides n, then 2,
+  // then the odd primes ascending, as fourier.rs:34-50 factors n).
+  int m = 1;
+  for (int s = 0; s < f.nf; s++) {
+    const int r = f.fac[s];
+    const float4* src4 = reinterpret_cast<const float4*>(a);
+    float4* dst4 = reinterpret_cast<float4*>(b);
+    switch (r) {
+      case 2: radix_stage<C, 2>(src4, dst4, lines, n, r, m, ct, st, sign); break;
+      case 3: radix_stage<C, 3>(src4, dst4, lines, n, r, m, ct, st, sign); break;
+      case 4: radix_stage<C, 4>(src4, dst4, lines, n, r, m, ct, st, sign); break;
+      case 5: radix_stage<C, 5>(src4, dst4, lines, n, r, m, ct, st, sign); break;
+      case 7: radix_stage<C, 7>(src4, dst4, lines, n, r, m, ct, st, sign); break;
+      default: radix_stage<C, 0>(src4, dst4, lines, n, r, m, ct, st, sign); break;
     }
-    b[((size_t)line * n + k) * C + c] = make_float2(re, im);
+    m *= r;
+    __syncthreads();
+    float2* tmp = a;
+    a = b;
+    b = tmp;
   }
-  __syncthreads();
-  return b;
+  return a;
 }
 
 // The twiddle table of `f` copied into shared memory after the two buffers.
@@ -750,8 +803,25 @@ Dims dims_of(const FourierPlan& p) {
 
 Line line_of(const FourierPlan& p, bool rows) {
   const float* t = p.twiddles.as<float>();
-  if (rows) return Line{p.w, log2_exact(p.w), t, t + p.w};
-  return Line{p.h, log2_exact(p.h), t + 2 * p.w, t + 2 * p.w + p.h};
+  Line f{};
+  f.n = rows ? p.w : p.h;
+  f.log2n = log2_exact(f.n);
+  f.cos_t = rows ? t : t + 2 * p.w;
+  f.sin_t = rows ? t + p.w : t + 2 * p.w + p.h;
+  if (f.log2n < 0) {
+    int left = f.n;
+    for (int r : {4, 2})
+      while (left % r == 0) {
+        f.fac[f.nf++] = r;
+        left /= r;
+      }
+    for (int r = 3; left > 1; r += 2)
+      while (left % r == 0) {
+        f.fac[f.nf++] = r;
+        left /= r;
+      }
+  }
+  return f;
 }
 
 size_t smem_for(int lines, int n) { return (size_t)2 * lines * n * 8 * sizeof(float2) + (size_t)2 * n * sizeof(float); }

@@ -70,6 +70,9 @@ def lib():
         L.iec_realesrgan_run_device.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_realesrgan_set_fused.argtypes = [vp, ctypes.c_int]
         L.iec_realesrgan_set_fused.restype = ctypes.c_int
+        L.iec_scunet_run_batch.argtypes = [vp, vp, sz, sz, sz, vp, vp]
+        L.iec_lama_run_batch.argtypes = [vp, vp, vp, sz, sz, sz, vp, vp]
+        L.iec_birefnet_run_batch.argtypes = [vp, vp, sz, sz, vp, vp]
         L.iec_lama_set_fused.argtypes = [vp, ctypes.c_int]
         L.iec_selftest_fourier_unit_time.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_float)]
@@ -334,6 +337,15 @@ class Scunet:
         """run_float on device pointers, queued on `stream`."""
         _check(lib().iec_scunet_run_device(self._h, image_ptr, width, height, out_ptr, stream or None))
 
+    def run_batch(self, images, out=None, stream: int = 0):
+        """Batched run_float on host arrays (N x H x W x 3 float32; numpy or
+        page-locked torch tensors), copies overlapped with the kernels."""
+        n, h, w, _ = images.shape
+        if out is None:
+            out = np.empty((n, h, w, 3), np.float32)
+        _check(lib().iec_scunet_run_batch(self._h, _addr(images), n, w, h, _addr(out), stream or None))
+        return out
+
     def run(self, rgb: np.ndarray, progress=None) -> np.ndarray:
         rgb = np.ascontiguousarray(rgb, np.uint8)
         h, w, _ = rgb.shape
@@ -366,6 +378,15 @@ class Lama:
 
     def gpu(self) -> str:
         return lib().iec_lama_device_name(self._h).decode()
+
+    def run_batch(self, images, masks, out=None, stream: int = 0):
+        """Batched run_float on host arrays: images N x H x W x 3, masks
+        N x H x W (float32; numpy or page-locked torch tensors)."""
+        n, h, w, _ = images.shape
+        if out is None:
+            out = np.empty((n, h, w, 3), np.float32)
+        _check(lib().iec_lama_run_batch(self._h, _addr(images), _addr(masks), n, w, h, _addr(out), stream or None))
+        return out
 
     def set_fused(self, on: bool):
         """Fused Fourier units (default) or rfft2, GEMM and irfft2 apart."""
@@ -437,6 +458,15 @@ class Birefnet:
         side = image.shape[0]
         out = np.empty((side, side), np.float32)
         _check(lib().iec_birefnet_run_normalized(self._h, _f32(image), side, _f32(out)))
+        return out
+
+    def run_batch(self, images, out=None, stream: int = 0):
+        """Batched run on host arrays: N x side x side x 3 uint8 images to
+        N x side x side float32 logits."""
+        n, side, _, _ = images.shape
+        if out is None:
+            out = np.empty((n, side, side), np.float32)
+        _check(lib().iec_birefnet_run_batch(self._h, _addr(images), n, side, _addr(out), stream or None))
         return out
 
     def run_device(self, image_ptr: int, image_u8: bool, side: int, logits_ptr: int, stream: int = 0):

@@ -212,6 +212,15 @@ iec_status iec_scunet_run(iec_scunet* model, const uint8_t* rgb, size_t width, s
 iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t width, size_t height,
                                  float* out, void* stream);
 
+/* Batched Model::run_float over `count` images of one size (each run whole,
+ * as run_device runs it), HOST buffers: count x height x width x 3 in and
+ * out. The H2D copy of the next image and the D2H copy of the previous one
+ * overlap each image's kernels (page-locked buffers let them); queued on
+ * `stream` (NULL: the model's stream), returns when the outputs are in
+ * `out`. For sharding a batch of images over GPUs, one handle per GPU. */
+iec_status iec_scunet_run_batch(iec_scunet* model, const float* images, size_t count, size_t width,
+                                size_t height, float* out, void* stream);
+
 /* -------------------------------------------------------------------- LaMa
  * crates/lama-native/src/lib.rs: Big LaMa inpainting, output the size of the
  * input. Sides of at least 9 pixels (lib.rs:180-194); at most 12288 here. */
@@ -239,6 +248,13 @@ iec_status iec_lama_run(iec_lama* model, const uint8_t* rgb, const uint8_t* mask
  * `stream` (NULL: the model's stream), no wait. */
 iec_status iec_lama_run_device(iec_lama* model, const float* image, const float* mask, size_t width,
                                size_t height, float* out, void* stream);
+
+/* Batched Model::run_float over `count` images of one size: images count x
+ * height x width x 3 and masks count x height x width (1 fills) in, count x
+ * height x width x 3 predictions out, HOST buffers, copies overlapped with
+ * the kernels as in iec_scunet_run_batch. */
+iec_status iec_lama_run_batch(iec_lama* model, const float* images, const float* masks, size_t count,
+                              size_t width, size_t height, float* out, void* stream);
 
 /* Each Fourier unit runs fused (the default, `on` = 1: rfft2, the spectral
  * 1x1 convolution and irfft2 in three launches, the spectrum kept in shared
@@ -272,6 +288,12 @@ iec_status iec_birefnet_run_normalized(iec_birefnet* model, const float* image, 
  * model's stream), no wait. */
 iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int image_u8, size_t side,
                                    float* logits, void* stream);
+
+/* Batched Model::run over `count` 8-bit RGB images of side x side (HOST
+ * buffers, count x side x side x 3 in), count x side x side logits out,
+ * copies overlapped with the kernels as in iec_scunet_run_batch. */
+iec_status iec_birefnet_run_batch(iec_birefnet* model, const uint8_t* images, size_t count, size_t side,
+                                  float* logits, void* stream);
 
 /* Diagnostics (no counterpart in the reference): one launch of the general
  * GEMM on host arrays. conv = 0: `a` rows_or_h x k, `weights` k x n; conv = 1:

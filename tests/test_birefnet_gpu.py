@@ -103,3 +103,12 @@ def test_run_device(gpu_model, cpu_model):
     gpu_model.run_device(t.data_ptr(), True, 128, out.data_ptr(), s.cuda_stream)
     s.synchronize()
     within(out.cpu().numpy(), cpu_model.run(rgb))
+
+
+def test_batch_matches_single_runs(gpu_model):
+    """iec_birefnet_run_batch: 8-bit images in host buffers, each image's
+    logits as run gives them, bit for bit."""
+    images = np.stack([W.birefnet_input(128, s) for s in range(3)])
+    singles = np.stack([gpu_model.run(im) for im in images])
+    batch = gpu_model.run_batch(images)
+    assert np.array_equal(batch.view(np.uint32), singles.view(np.uint32))

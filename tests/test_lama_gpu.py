@@ -140,12 +140,15 @@ def test_run_device(gpu_model, cpu_model):
 
 @pytest.mark.parametrize("two_pass", [False, True])
 @pytest.mark.parametrize("h,w,c", [(64, 64, 16), (5, 7, 8), (16, 12, 8), (9, 10, 8), (1, 8, 8), (2, 2, 8),
-                                   (32, 128, 8), (128, 96, 8)])
+                                   (32, 128, 8), (128, 96, 8), (45, 60, 8), (49, 22, 8), (135, 240, 8),
+                                   (97, 14, 8)])
 def test_planar_rfft2_matches_numpy(h, w, c, two_pass):
     """fft.cu against numpy's ortho rfft2 / irfft2 of the same f16-rounded
     input; the spectrum is stored in f16, hence the relative bound. Both the
     one-launch transforms of small maps and the two-launch ones (128 x 96
-    takes the two-launch path either way)."""
+    takes the two-launch path either way). Lengths with radices 3, 5 and 7
+    (45, 60, 49, 135, 240, 14), a generic prime radix (22 = 2 x 11) and a
+    prime length (97) take the mixed-radix stages."""
     import iec
 
     rng = np.random.default_rng(h * 1000 + w)
@@ -207,3 +210,14 @@ def test_fused_fourier_unit_equals_separate_launches(gpu_model, width, height, s
         gpu_model.set_fused(True)
     assert np.isfinite(fused).all()
     assert np.array_equal(fused.view(np.uint32), apart.view(np.uint32)), float(np.abs(fused - apart).max())
+
+
+def test_batch_matches_single_runs(gpu_model):
+    """iec_lama_run_batch: images and masks in host buffers, each image as
+    run_float gives it, bit for bit."""
+    pairs = [W.lama_input(48, 40, s) for s in range(4)]
+    images = np.stack([p[0] for p in pairs])
+    masks = np.stack([p[1] for p in pairs])
+    singles = np.stack([gpu_model.run_float(i, m) for i, m in pairs])
+    batch = gpu_model.run_batch(images, masks)
+    assert np.array_equal(batch.view(np.uint32), singles.view(np.uint32))

@@ -141,3 +141,13 @@ def test_8bit_run(gpu_model, cpu_model):
     want8 = np.round(np.clip(want, 0, 1) * 255).astype(np.int32)
     assert np.abs(got.astype(np.int32) - want8).max() <= 6
     assert psnr(got / 255.0, want8 / 255.0) > 45.0
+
+
+def test_batch_matches_single_runs(gpu_model):
+    """iec_scunet_run_batch: host buffers, copies overlapped with the
+    kernels, two alternating device buffer pairs; each image as run_float
+    gives it, bit for bit."""
+    images = np.stack([W.scunet_input(40, 24, s) for s in range(5)])
+    singles = np.stack([gpu_model.run_float(im) for im in images])
+    batch = gpu_model.run_batch(images)
+    assert np.array_equal(batch.view(np.uint32), singles.view(np.uint32))
