@@ -259,6 +259,58 @@ def cpu_once(fn, mp):
     return {"value": mp / el, "unit": "MP/s", "seconds": el, "cores": cores, "kind": "port"}
 
 
+def launch_table(model, run, pk):
+    """One eager pass of `run` with launch timing on (iec_set_launch_timing:
+    CUDA events around each instrumented launch, the pass's side-stream work
+    serialised onto its stream so each pair times one kernel alone), summarised:
+    the dominant GEMM shape by total time (its algorithmic FLOPs per launch
+    over its mean event time, against the sustained dense peak), all GEMM
+    launches together, and achieved GB/s of the bandwidth-bound kernels
+    (algorithmic bytes over event time, against the measured copy rate)."""
+    import torch
+
+    import iec
+
+    iec.set_launch_timing(model, True)
+    run()
+    torch.cuda.synchronize()
+    recs = iec.launch_timing(model)
+    iec.set_launch_timing(model, False)
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    groups = {}
+    for r in recs:
+        g = groups.setdefault(r["name"], {"launches": 0, "ms": 0.0, "flop": 0.0, "bytes": 0.0})
+        g["launches"] += 1
+        g["ms"] += r["ms"]
+        g["flop"] += r["flop"]
+        g["bytes"] += r["bytes"]
+    gemms = {k: v for k, v in groups.items() if k.startswith("igemm_sm100")}
+    out = {"launches_timed": len(recs), "ms_sum": sum(r["ms"] for r in recs)}
+    if gemms:
+        name, g = max(gemms.items(), key=lambda kv: kv[1]["ms"])
+        tf = g["flop"] / (g["ms"] / 1e3) / 1e12
+        out["roofline"] = {"kernel": name + " (A x W: M x N x K)", "bound": "tensor", "launches": g["launches"],
+                           "mean_launch_ms": g["ms"] / g["launches"], "flop_per_launch": g["flop"] / g["launches"],
+                           "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                           "share_of_timed": g["ms"] / out["ms_sum"]}
+        fl = sum(v["flop"] for v in gemms.values())
+        ms = sum(v["ms"] for v in gemms.values())
+        out["all_gemms"] = {"launches": sum(v["launches"] for v in gemms.values()), "ms": ms,
+                            "achieved_tflops": fl / (ms / 1e3) / 1e12, "frac": fl / (ms / 1e3) / 1e12 / peak}
+        top = sorted(gemms.items(), key=lambda kv: -kv[1]["ms"])[:6]
+        out["top_gemms"] = [{"kernel": k, "launches": v["launches"], "mean_ms": v["ms"] / v["launches"],
+                             "tflops": v["flop"] / (v["ms"] / 1e3) / 1e12} for k, v in top]
+    bw = {}
+    for k, v in groups.items():
+        if k.startswith("igemm_sm100") or v["bytes"] <= 0:
+            continue
+        gbs = v["bytes"] / (v["ms"] / 1e3) / 1e9
+        bw[k] = {"launches": v["launches"], "mean_ms": v["ms"] / v["launches"], "gbs": gbs,
+                 "frac_hbm": gbs / pk["hbm_gbs"], "share_of_timed": v["ms"] / out["ms_sum"]}
+    out["bandwidth_kernels"] = bw
+    return out
+
+
 def scunet_leg(wdir, stream, sptr, cpu):
     import torch
 
@@ -272,6 +324,7 @@ def scunet_leg(wdir, stream, sptr, cpu):
     img = torch.from_numpy(W.scunet_input(768, 512, 0)).cuda()
     res = torch.empty_like(img)
     t = time_device(lambda: m.run_device(img.data_ptr(), 768, 512, res.data_ptr(), sptr), stream)
+    table = launch_table(m, lambda: m.run_device(img.data_ptr(), 768, 512, res.data_ptr(), sptr), peaks()[0])
     image = W.scunet_input(768, 512, 0)
     for _ in range(3):  # warm-up: buffers, then the pass's graph (captured on the second call)
         m.run_float(image)
@@ -282,7 +335,7 @@ def scunet_leg(wdir, stream, sptr, cpu):
     out["scunet_768x512"] = {"workload": "SCUNet 3x512x768 (single-image configuration)", "value": 768 * 512 / 1e6 / t,
                              "unit": "MP/s", "ms": t * 1e3, "gflop": 899.58,
                              "tflops_achieved": 899.58e9 / t / 1e12, "e2e_ms": te * 1e3,
-                             "e2e_value": 768 * 512 / 1e6 / te}
+                             "e2e_value": 768 * 512 / 1e6 / te, **table}
     m.close()
     if cpu:
         from oracle import refcpu
@@ -309,6 +362,8 @@ def lama_leg(wdir, stream, sptr, cpu):
     msk = torch.from_numpy(mask).cuda()
     res = torch.empty_like(img)
     t = time_device(lambda: m.run_device(img.data_ptr(), msk.data_ptr(), 512, 512, res.data_ptr(), sptr), stream)
+    table = launch_table(m, lambda: m.run_device(img.data_ptr(), msk.data_ptr(), 512, 512, res.data_ptr(), sptr),
+                         peaks()[0])
     for _ in range(3):  # warm-up: buffers, then the pass's graph (captured on the second call)
         m.run_float(image, mask)
     t0 = time.perf_counter()
@@ -317,7 +372,7 @@ def lama_leg(wdir, stream, sptr, cpu):
     te = (time.perf_counter() - t0) / 5
     out["lama_512x512"] = {"workload": "Big LaMa 4x512x512 (single-image configuration)", "value": 512 * 512 / 1e6 / t,
                            "unit": "MP/s", "ms": t * 1e3, "gflop": 439.8, "tflops_achieved": 439.8e9 / t / 1e12,
-                           "e2e_ms": te * 1e3, "e2e_value": 512 * 512 / 1e6 / te}
+                           "e2e_ms": te * 1e3, "e2e_value": 512 * 512 / 1e6 / te, **table}
     m.close()
     if cpu:
         from oracle import refcpu
@@ -344,6 +399,7 @@ def birefnet_leg(wdir, stream, sptr, cpu):
     img = torch.from_numpy(rgb).cuda()
     res = torch.empty((1024, 1024), dtype=torch.float32, device="cuda")
     t = time_device(lambda: m.run_device(img.data_ptr(), True, 1024, res.data_ptr(), sptr), stream)
+    table = launch_table(m, lambda: m.run_device(img.data_ptr(), True, 1024, res.data_ptr(), sptr), peaks()[0])
     for _ in range(3):  # warm-up: buffers, then the pass's graph (captured on the second call)
         m.run(rgb)
     t0 = time.perf_counter()
@@ -353,7 +409,7 @@ def birefnet_leg(wdir, stream, sptr, cpu):
     out["birefnet_1024"] = {"workload": "BiRefNet-lite 3x1024x1024 (single-image configuration)",
                             "value": 1024 * 1024 / 1e6 / t, "unit": "MP/s", "ms": t * 1e3, "gflop": 606.36,
                             "tflops_achieved": 606.36e9 / t / 1e12, "e2e_ms": te * 1e3,
-                            "e2e_value": 1024 * 1024 / 1e6 / te}
+                            "e2e_value": 1024 * 1024 / 1e6 / te, **table}
     m.close()
     if cpu:
         from oracle import refcpu

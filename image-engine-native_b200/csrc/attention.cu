@@ -209,9 +209,14 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
   if (c % 32 != 0) throw Error(ERR_INPUT, "attention channels must be a multiple of 32");
   dim3 grid(windows, c / 32);
   if ((qkv_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "attention planes must be 16-byte multiples");
-  launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w, out,
-             out_plane_elems, dev_err);
-  IEC_CUDA(cudaGetLastError());
+  // per window and head: S = Q K^T and O = P V, 2 x 64 x 64 x 32 MACs;
+  // bytes: q, k, v read and the output written once (f16)
+  const double heads = (double)windows * (c / 32);
+  timed_launch("window_attention_kernel", heads * 4.0 * 64 * 64 * 32, (double)windows * 64 * 4 * c * 2, s, [&] {
+    launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w,
+               out, out_plane_elems, dev_err);
+    IEC_CUDA(cudaGetLastError());
+  });
 }
 
 }  // namespace iec

@@ -153,6 +153,17 @@ __global__ void bir_resize_planar(const __half* __restrict__ src, long long src_
   }
 }
 
+// One bir_resize_planar launch, recorded for launch timing with its bytes:
+// the source read once, the destination written (and read when adding).
+void launch_resize(const __half* src, long long src_plane, int sh, int sw, __half* dst, long long dst_plane, int dh,
+                   int dw, int c8, int add, int sms, cudaStream_t s) {
+  const double bytes = ((double)sh * sw + (double)dh * dw * (1 + add)) * c8 * 16;
+  timed_launch("bir_resize_planar", 0.0, bytes, s, [&] {
+    launch_pdl(bir_resize_planar, blocks_for((long long)dh * dw * c8, sms), 256, 0, s, src, src_plane, sh, sw, dst,
+               dst_plane, dh, dw, c8, add);
+  });
+}
+
 // swin.rs:188-204: each 4 x 4 patch's 48 values, (ky, kx, c) order.
 __global__ void bir_embed_gather(const float* __restrict__ img, int side, __half* __restrict__ dst, long long plane) {
   griddep_wait();
@@ -897,13 +908,17 @@ void Birefnet::block(const DBlock& b, const __half* x, long long x_plane, int ci
     const long long pairs = P * taps;
     const int gpt = pairs >= 1024LL * sms ? 4 : pairs >= 512LL * sms ? 2 : 1;
     const dim3 grid((unsigned)std::min<long long>((P + 255) / 256, 4LL * sms), (unsigned)(taps * (8 / gpt)));
-    if (gpt == 4)
-      launch_pdl(bir_deform_sample<4>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
-    else if (gpt == 2)
-      launch_pdl(bir_deform_sample<2>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
-    else
-      launch_pdl(bir_deform_sample<1>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
-    IEC_CUDA(cudaGetLastError());
+    // bytes: the offsets and modulators (3 per tap), the 64-channel map read
+    // once and the sampled operand (64 channels per tap) written, f16
+    timed_launch("bir_deform_sample", 0.0, (double)P * (3 * taps + 64 + 64 * taps) * 2, bs, [&] {
+      if (gpt == 4)
+        launch_pdl(bir_deform_sample<4>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+      else if (gpt == 2)
+        launch_pdl(bir_deform_sample<2>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+      else
+        launch_pdl(bir_deform_sample<1>, grid, 256, 0, bs, t, pp, g, g, k, offs, pp, samp, pp);
+      IEC_CUDA(cudaGetLastError());
+    });
     GemmOutSpec c;
     c.mode = OUT_STORE;
     c.out = cat_.as<__half>();
@@ -951,6 +966,7 @@ void Birefnet::run(const void* image, bool u8, int side, float* logits, cudaStre
 }
 
 void Birefnet::run_pass(const void* image, bool u8, int side, float* logits, cudaStream_t s) {
+  SerialStreams serial(dev_.timing(), {&s_half_, &s_patch_, &s_aspp_}, s);
   if (side <= 0 || side % 64 != 0)
     throw Error(ERR_INPUT, "side " + std::to_string(side) + " is not a positive multiple of 64");
   ensure(side);
@@ -1015,8 +1031,7 @@ void Birefnet::run_pass(const void* image, bool u8, int side, float* logits, cud
     __half* dst = i < 3 ? lev_[i].as<__half>() : x4_.as<__half>();
     const int plane = i < 3 ? c8 : 168 + c8;
     const long long dp = pe((long long)g[i] * g[i]);
-    launch_pdl(bir_resize_planar, blocks_for((long long)g[i] * g[i] * c8, sms), 256, 0, s, 
-        hf_[i].as<__half>(), pe((long long)hg * hg), hg, hg, dst + plane * dp, dp, g[i], g[i], c8, 0);
+    launch_resize(hf_[i].as<__half>(), pe((long long)hg * hg), hg, hg, dst + plane * dp, dp, g[i], g[i], c8, 0, sms, s);
     IEC_CUDA(cudaGetLastError());
   }
   // x4: levels 1-3 resized to 1/32 (planes 0..167), level 4 after them.
@@ -1025,9 +1040,8 @@ void Birefnet::run_pass(const void* image, bool u8, int side, float* logits, cud
     int plane = 0;
     for (int i = 0; i < 3; i++) {
       const int c8 = 2 * STAGE_C[i] / 8;
-      launch_pdl(bir_resize_planar, blocks_for((long long)g[3] * g[3] * c8, sms), 256, 0, s, 
-          lev_[i].as<__half>(), pe((long long)g[i] * g[i]), g[i], g[i], x4_.as<__half>() + plane * p3, p3, g[3], g[3],
-          c8, 0);
+      launch_resize(lev_[i].as<__half>(), pe((long long)g[i] * g[i]), g[i], g[i], x4_.as<__half>() + plane * p3, p3,
+                    g[3], g[3], c8, 0, sms, s);
       IEC_CUDA(cudaGetLastError());
       plane += c8;
     }
@@ -1048,8 +1062,7 @@ void Birefnet::run_pass(const void* image, bool u8, int side, float* logits, cud
       gemm_rows(dev_, laterals_[i - 1], lev_[level].as<__half>(), ip, gi * gi, ACT_NONE, o, s);
       const int pg = g[level + 1];
       const __half* prev = outb_[i - 1].as<__half>();
-      launch_pdl(bir_resize_planar, blocks_for((long long)gi * gi * (main_c[i] / 8), sms), 256, 0, s, 
-          prev, pe((long long)pg * pg), pg, pg, in, ip, gi, gi, main_c[i] / 8, 1);
+      launch_resize(prev, pe((long long)pg * pg), pg, pg, in, ip, gi, gi, main_c[i] / 8, 1, sms, s);
       IEC_CUDA(cudaGetLastError());
     }
     // the level's image patches, through two convolutions (side stream)

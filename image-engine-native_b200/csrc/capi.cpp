@@ -674,6 +674,47 @@ iec_status iec_birefnet_run_batch(iec_birefnet* model, const uint8_t* images, si
   });
 }
 
+namespace {
+// The device of a model handle of any kind (by its type tag), or null.
+Device* handle_device(void* handle) {
+  if (!handle) return nullptr;
+  const uint32_t tag = *static_cast<const uint32_t*>(handle);
+  if (tag == iec_scunet::TAG) return &static_cast<iec_scunet*>(handle)->model->device();
+  if (tag == iec_lama::TAG) return &static_cast<iec_lama*>(handle)->model->device();
+  if (tag == iec_birefnet::TAG) return &static_cast<iec_birefnet*>(handle)->model->device();
+  if (tag == iec_realesrgan::TAG) return &static_cast<iec_realesrgan*>(handle)->model->device();
+  return nullptr;
+}
+}  // namespace
+
+iec_status iec_set_launch_timing(void* model, int on) {
+  return guard([&] {
+    Device* d = handle_device(model);
+    if (!d) throw Error(ERR_INPUT, "not a model handle");
+    d->set_timing(on != 0);
+  });
+}
+
+size_t iec_launch_timing(void* model, iec_launch_record* records, size_t n) {
+  size_t written = 0;
+  iec_status st = guard([&] {
+    Device* d = handle_device(model);
+    if (!d) throw Error(ERR_INPUT, "not a model handle");
+    need(records, "records");
+    DeviceScope scope(*d);
+    const auto& t = d->timed();
+    for (size_t i = 0; i < t.size() && written < n; i++, written++) {
+      iec_launch_record& r = records[written];
+      std::memset(r.name, 0, sizeof r.name);
+      std::strncpy(r.name, t[i].name.c_str(), sizeof r.name - 1);
+      r.flop = t[i].flop;
+      r.bytes = t[i].bytes;
+      r.ms = d->timed_ms(i);
+    }
+  });
+  return st == IEC_OK ? written : 0;
+}
+
 size_t iec_realesrgan_launches(const iec_realesrgan* model, size_t count, size_t width, size_t height) {
   return valid(model) ? model->model->launches(count, width, height) : 0;
 }

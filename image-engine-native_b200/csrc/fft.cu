@@ -836,17 +836,25 @@ void prepare(K kernel, size_t bytes) {
 void launch_rows_fwd(const FourierPlan& plan, const Dims& d, const __half* x, long long x_plane_elems, cudaStream_t s) {
   const size_t sr = smem_for(d.lines_rows, d.w);
   prepare(fft_rows_fwd, sr);
-  launch_pdl(fft_rows_fwd, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, x,
-             x_plane_elems, plan.scratch.as<float2>(), d, line_of(plan, true));
-  IEC_CUDA(cudaGetLastError());
+  // bytes: the map read (f16), the row spectra written (complex f32)
+  const double io = (double)plan.h * plan.w * plan.channels * 2 + (double)plan.h * plan.half * plan.channels * 8;
+  timed_launch("fft_rows_fwd", 0.0, io, s, [&] {
+    launch_pdl(fft_rows_fwd, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s, x,
+               x_plane_elems, plan.scratch.as<float2>(), d, line_of(plan, true));
+    IEC_CUDA(cudaGetLastError());
+  });
 }
 
 void launch_rows_inv(const FourierPlan& plan, const Dims& d, __half* x, long long x_plane_elems, cudaStream_t s) {
   const size_t sr = smem_for(d.lines_rows, d.w);
   prepare(fft_rows_inv, sr);
-  launch_pdl(fft_rows_inv, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s,
-             (const float2*)plan.scratch.as<float2>(), x, x_plane_elems, d, line_of(plan, true));
-  IEC_CUDA(cudaGetLastError());
+  // bytes: the row spectra read, the map read and written
+  const double io = (double)plan.h * plan.half * plan.channels * 8 + (double)plan.h * plan.w * plan.channels * 4;
+  timed_launch("fft_rows_inv", 0.0, io, s, [&] {
+    launch_pdl(fft_rows_inv, dim3((d.h + d.lines_rows - 1) / d.lines_rows, d.groups), FFT_THREADS, sr, s,
+               (const float2*)plan.scratch.as<float2>(), x, x_plane_elems, d, line_of(plan, true));
+    IEC_CUDA(cudaGetLastError());
+  });
 }
 
 }  // namespace
@@ -880,9 +888,13 @@ void launch_fwd_small(const FourierPlan& plan, const Dims& d, const __half* x, l
                       long long spec_plane, cudaStream_t s) {
   const size_t bytes = small_smem(plan, C);
   prepare(fft2_fwd_small<C>, bytes);
-  launch_pdl(fft2_fwd_small<C>, dim3(d.groups * (8 / C)), FFT_SMALL_THREADS, bytes, s, x, x_plane, spec, spec_plane, d,
-             line_of(plan, true), line_of(plan, false));
-  IEC_CUDA(cudaGetLastError());
+  // bytes: the map read (f16) and the spectrum written (f16, real and imaginary)
+  const double io = (double)plan.h * plan.w * plan.channels * 2 + (double)plan.h * plan.half * plan.channels * 4;
+  timed_launch("fft2_fwd_small", 0.0, io, s, [&] {
+    launch_pdl(fft2_fwd_small<C>, dim3(d.groups * (8 / C)), FFT_SMALL_THREADS, bytes, s, x, x_plane, spec, spec_plane,
+               d, line_of(plan, true), line_of(plan, false));
+    IEC_CUDA(cudaGetLastError());
+  });
 }
 
 template <int C>
@@ -890,9 +902,13 @@ void launch_inv_small(const FourierPlan& plan, const Dims& d, const __half* spec
                       long long x_plane, cudaStream_t s) {
   const size_t bytes = small_smem(plan, C);
   prepare(fft2_inv_small<C>, bytes);
-  launch_pdl(fft2_inv_small<C>, dim3(d.groups * (8 / C)), FFT_SMALL_THREADS, bytes, s, spec, spec_plane, x, x_plane, d,
-             line_of(plan, true), line_of(plan, false));
-  IEC_CUDA(cudaGetLastError());
+  // bytes: the spectrum read, the map read and written
+  const double io = (double)plan.h * plan.half * plan.channels * 4 + (double)plan.h * plan.w * plan.channels * 4;
+  timed_launch("fft2_inv_small", 0.0, io, s, [&] {
+    launch_pdl(fft2_inv_small<C>, dim3(d.groups * (8 / C)), FFT_SMALL_THREADS, bytes, s, spec, spec_plane, x, x_plane,
+               d, line_of(plan, true), line_of(plan, false));
+    IEC_CUDA(cudaGetLastError());
+  });
 }
 
 void rfft2_planar(const FourierPlan& plan, const __half* x, long long x_plane_elems, __half* spec,
@@ -994,7 +1010,11 @@ void fourier_unit_planar(const FourierPlan& plan, const FourierWeights& fw, __ha
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  IEC_CUDA(cudaLaunchKernelEx(&cfg, fourier_unit_cols, fp));
+  // FLOPs: the 1x1 product over the spectrum (h half rows, K = N = 2c);
+  // bytes: the row spectra read and written (complex f32) and the weights
+  const double rows = (double)plan.h * plan.half;
+  timed_launch("fourier_unit_cols", 2.0 * rows * FU_K * FU_K, rows * plan.channels * 16 + (double)FU_K * FU_K * 2, s,
+               [&] { IEC_CUDA(cudaLaunchKernelEx(&cfg, fourier_unit_cols, fp)); });
   if (only == 0) launch_rows_inv(plan, d, x, x_plane_elems, s);
 }
 

@@ -101,7 +101,16 @@ void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, Gemm
     p.ws = static_cast<float*>(dev.scratch((size_t)p.ksplit * p.M * p.ws_n * sizeof(float), s));
     p.tiles = p.tiles_mn * p.ksplit;
   }
-  dispatch<AMODE>(dev, pw.bn, pw.kb, map, p, s);
+  // Algorithmic work of the product: 2 M N K FLOPs (K over all taps); bytes:
+  // the input read once (M x K), the weights, the output and the old values
+  // the epilogue reads (accumulate, acc_src, resid).
+  const double M = p.M, N = p.N, K1 = p.K, KT = pw.ktot;
+  const int sources = (p.out_mode == OUT_ACCUM || p.out_mode == OUT_WINDOW_ACCUM ? 1 : 0) +
+                      (p.acc_src ? 1 : 0) + (p.resid ? 1 : 0);
+  const double gbytes = M * K1 * 2 + KT * N * 2 + M * N * 2 * (1 + sources);
+  char name[96];
+  snprintf(name, sizeof name, "igemm_sm100<%d,%d,%d> %dx%dx%d", pw.bn, pw.kb, AMODE, p.M, p.N, pw.ktot);
+  timed_launch(name, 2.0 * M * N * KT, gbytes, s, [&] { dispatch<AMODE>(dev, pw.bn, pw.kb, map, p, s); });
   if (p.ksplit > 1) {
     const long long total = (long long)p.M * ((p.N + 7) / 8);
     const int grid = (int)std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)dev.sms() * 16));
@@ -115,8 +124,11 @@ void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, Gemm
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    IEC_CUDA(cudaLaunchKernelEx(&cfg, gemm_splitk_reduce, p));
-    IEC_CUDA(cudaGetLastError());
+    const double rbytes = (double)p.ksplit * p.M * p.ws_n * 4 + M * N * 2 * (1 + sources);
+    timed_launch("gemm_splitk_reduce", 0.0, rbytes, s, [&] {
+      IEC_CUDA(cudaLaunchKernelEx(&cfg, gemm_splitk_reduce, p));
+      IEC_CUDA(cudaGetLastError());
+    });
   }
 }
 
@@ -471,6 +483,8 @@ static void launch_ln(const __half* src, long long src_plane, int plane0, int ro
   if (c % 8 != 0 || groups < 1) throw Error(ERR_INPUT, "layer norm over a channel count not a multiple of 8");
   if (((uintptr_t)gamma | (uintptr_t)beta) % 16 != 0) throw Error(ERR_INPUT, "layer norm parameters not 16-byte aligned");
   const size_t smem = (size_t)2 * c * sizeof(float);  // at most 24 KB (3072 channels)
+  // bytes: every output row's c values read and written once (f16)
+  timed_launch("layer_norm_rows", 0.0, (double)rows * c * 4, s, [&] {
   if (groups <= 8) {
     launch_pdl(layer_norm_rows<2, 4>, (rows + 127) / 128, 256, smem, s, src, src_plane, plane0, rows, c, gamma, beta, dst,
                                                              dst_plane, mode, wm, grid);
@@ -487,6 +501,7 @@ static void launch_ln(const __half* src, long long src_plane, int plane0, int ro
     throw Error(ERR_INPUT, "layer norm over more than 3072 channels");
   }
   IEC_CUDA(cudaGetLastError());
+  });
 }
 
 void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0, int rows, int c, const float* gamma,

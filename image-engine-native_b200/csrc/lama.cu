@@ -328,6 +328,7 @@ bool Lama::run(const void* image, bool image_u8, const void* mask, bool mask_u8,
 
 bool Lama::run_pass(const void* image, bool image_u8, const void* mask, bool mask_u8, void* dst, bool dst_u8, int width,
                int height, const std::function<bool()>& step, cudaStream_t s) {
+  SerialStreams serial(dev_.timing(), {&s_local_, &s_spec_}, s);
   if (width < MIN_SIDE || height < MIN_SIDE)
     throw Error(ERR_INPUT, std::to_string(width) + " x " + std::to_string(height) + " image: sides of at least " +
                                std::to_string(MIN_SIDE) + " pixels");

@@ -197,15 +197,24 @@ int device_count() {
   return n;
 }
 
+namespace {
+thread_local Device* g_scope_device = nullptr;
+}
+
+Device* scoped_device() { return g_scope_device; }
+
 DeviceScope::DeviceScope(Device& d) {
   if (cudaGetDevice(&prev_) != cudaSuccess) {
     cudaGetLastError();
     prev_ = -1;
   }
   d.enter();
+  prev_device_ = g_scope_device;
+  g_scope_device = &d;
 }
 
 DeviceScope::~DeviceScope() {
+  g_scope_device = prev_device_;
   if (prev_ >= 0) cudaSetDevice(prev_);
 }
 
@@ -243,6 +252,7 @@ Device::~Device() {
   if (!poisoned()) {
     if (stream_) cudaStreamDestroy(stream_);
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
+    for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
   }
   // A poisoned device may still run work; its buffers and streams are leaked
   // rather than freed under it (as the reference's busy flag does).
@@ -251,6 +261,42 @@ Device::~Device() {
     for (auto& e : scratch_) e.second.leak();
   }
   if (prev >= 0) cudaSetDevice(prev);
+}
+
+void Device::set_timing(bool on) {
+  timing_ = on;
+  timed_.clear();
+  events_used_ = 0;
+}
+
+int Device::time_begin(const std::string& name, double flop, double bytes, cudaStream_t s) {
+  if (!timing_) return -1;
+  while (event_pool_.size() < events_used_ + 2) {
+    cudaEvent_t e;
+    IEC_CUDA(cudaEventCreate(&e));
+    event_pool_.push_back(e);
+  }
+  TimedLaunch t;
+  t.name = name;
+  t.flop = flop;
+  t.bytes = bytes;
+  t.a = event_pool_[events_used_++];
+  t.b = event_pool_[events_used_++];
+  IEC_CUDA(cudaEventRecord(t.a, s));
+  timed_.push_back(t);
+  return (int)timed_.size() - 1;
+}
+
+void Device::time_end(int index, cudaStream_t s) {
+  if (index >= 0 && (size_t)index < timed_.size()) IEC_CUDA(cudaEventRecord(timed_[index].b, s));
+}
+
+float Device::timed_ms(size_t i) {
+  if (i >= timed_.size()) return 0.0f;
+  wait_event(timed_[i].b);
+  float ms = 0.0f;
+  IEC_CUDA(cudaEventElapsedTime(&ms, timed_[i].a, timed_[i].b));
+  return ms;
 }
 
 void Device::enter() {
@@ -326,7 +372,9 @@ void PassGraph::reset() {
 
 void PassGraph::run(const std::vector<long long>& key, cudaStream_t s,
                     const std::function<void(cudaStream_t)>& body) {
-  if (!enabled) return body(s);
+  // Launch timing records events around each launch: such passes run eagerly.
+  const Device* d = scoped_device();
+  if (!enabled || (d && d->timing())) return body(s);
   Entry* hit = nullptr;
   for (auto& e : entries_)
     if (e.key == key) hit = &e;

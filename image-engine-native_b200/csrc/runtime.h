@@ -16,6 +16,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <functional>
+#include <initializer_list>
 #include <map>
 #include <stdexcept>
 #include <string>
@@ -177,6 +178,25 @@ class Device {
   // an older one must not replay).
   uint64_t scratch_generation() const { return scratch_gen_; }
 
+  // Launch timing (diagnostics, no counterpart in the reference): while it is
+  // on, the kernels that report themselves record a CUDA event before and
+  // after their launch on the stream they run on, with their name and
+  // algorithmic FLOPs and bytes; models run their passes eagerly meanwhile.
+  // Turning it on starts a new record.
+  struct TimedLaunch {
+    std::string name;
+    double flop = 0, bytes = 0;
+    cudaEvent_t a = nullptr, b = nullptr;
+  };
+  void set_timing(bool on);
+  bool timing() const { return timing_; }
+  // Record the start of a launch; returns its index, or -1 when off.
+  int time_begin(const std::string& name, double flop, double bytes, cudaStream_t s);
+  void time_end(int index, cudaStream_t s);
+  const std::vector<TimedLaunch>& timed() const { return timed_; }
+  // Waits for the recorded events; the duration of launch i in ms.
+  float timed_ms(size_t i);
+
  private:
   int ordinal_ = 0;
   std::string name_;
@@ -190,7 +210,12 @@ class Device {
   uint64_t scratch_gen_ = 0;
   PinnedBuffer host_err_;
   std::string poisoned_;
+  bool timing_ = false;
+  std::vector<TimedLaunch> timed_;
+  std::vector<cudaEvent_t> event_pool_;
+  size_t events_used_ = 0;
 };
+
 
 // RAII: make the device current for a call and restore the caller's.
 // Model passes kept as CUDA graphs: hundreds of small launches replay with
@@ -229,7 +254,43 @@ class DeviceScope {
 
  private:
   int prev_ = -1;
+  Device* prev_device_ = nullptr;
 };
+
+// While `on`, the side streams listed are the pass's own stream `main`
+// (restored on scope exit): a pass whose launches are being timed runs them
+// one after another, so each event pair measures one kernel alone.
+class SerialStreams {
+ public:
+  SerialStreams(bool on, std::initializer_list<cudaStream_t*> side, cudaStream_t main) {
+    if (!on) return;
+    for (cudaStream_t* st : side) {
+      saved_.emplace_back(st, *st);
+      *st = main;
+    }
+  }
+  ~SerialStreams() {
+    for (auto& e : saved_) *e.first = e.second;
+  }
+  SerialStreams(const SerialStreams&) = delete;
+  SerialStreams& operator=(const SerialStreams&) = delete;
+
+ private:
+  std::vector<std::pair<cudaStream_t*, cudaStream_t>> saved_;
+};
+
+// The device of the innermost DeviceScope on this thread (null outside one).
+Device* scoped_device();
+
+// Run `launch` (one kernel launch on `s`), recorded as `name` with its
+// algorithmic FLOPs and bytes when the scoped device's launch timing is on.
+template <class F>
+void timed_launch(const char* name, double flop, double bytes, cudaStream_t s, F&& launch) {
+  Device* d = scoped_device();
+  const int t = d && d->timing() ? d->time_begin(name, flop, bytes, s) : -1;
+  launch();
+  if (t >= 0) d->time_end(t, s);
+}
 
 // Launch `kernel` as a programmatic dependent of the work before it on `s`:
 // it may start while its predecessor drains, so it must execute

@@ -280,6 +280,7 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
                         int ry0, int rw, int rh, int kx0, int ky0, int kx1, int ky1,
                         const std::function<bool()>& step, cudaStream_t s) {
   (void)src_h;
+  SerialStreams serial(dev_.timing(), {&s_conv_}, s);
   const int ph = (rh + MULTIPLE - 1) / MULTIPLE * MULTIPLE, pw = (rw + MULTIPLE - 1) / MULTIPLE * MULTIPLE;
   ensure(ph, pw);
   const int sms = dev_.sms();

@@ -42,6 +42,11 @@ class Options(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("timeout_ms", ctypes.c_int), ("batch_chunk", ctypes.c_int)]
 
 
+class LaunchRecord(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 64), ("flop", ctypes.c_double), ("bytes", ctypes.c_double),
+                ("ms", ctypes.c_float)]
+
+
 _lib = None
 
 
@@ -73,6 +78,9 @@ def lib():
         L.iec_scunet_run_batch.argtypes = [vp, vp, sz, sz, sz, vp, vp]
         L.iec_lama_run_batch.argtypes = [vp, vp, vp, sz, sz, sz, vp, vp]
         L.iec_birefnet_run_batch.argtypes = [vp, vp, sz, sz, vp, vp]
+        L.iec_set_launch_timing.argtypes = [vp, ctypes.c_int]
+        L.iec_launch_timing.argtypes = [vp, ctypes.POINTER(LaunchRecord), sz]
+        L.iec_launch_timing.restype = sz
         L.iec_lama_set_fused.argtypes = [vp, ctypes.c_int]
         L.iec_selftest_fourier_unit_time.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_float)]
@@ -493,6 +501,20 @@ def selftest_fourier_unit_time(h: int = 64, w: int = 64, iters: int = 50, device
     us = (ctypes.c_float * 5)()
     _check(lib().iec_selftest_fourier_unit_time(device, h, w, iters, us))
     return tuple(us)
+
+
+def set_launch_timing(model, on: bool):
+    """Record CUDA events around every instrumented launch of `model` (a
+    Scunet, Lama or Birefnet), passes eager meanwhile (iec_set_launch_timing)."""
+    _check(lib().iec_set_launch_timing(model._h, 1 if on else 0))
+
+
+def launch_timing(model, n: int = 100000):
+    """The launches recorded since set_launch_timing(model, True), in order:
+    dicts of name, flop, bytes (algorithmic) and ms (CUDA events)."""
+    recs = (LaunchRecord * n)()
+    k = lib().iec_launch_timing(model._h, recs, n)
+    return [{"name": r.name.decode(), "flop": r.flop, "bytes": r.bytes, "ms": r.ms} for r in recs[:k]]
 
 
 def selftest_wait_timeout(which: int, device: int = -1) -> int:

@@ -295,6 +295,27 @@ iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int i
 iec_status iec_birefnet_run_batch(iec_birefnet* model, const uint8_t* images, size_t count, size_t side,
                                   float* logits, void* stream);
 
+/* Launch timing (measurement hooks, no counterpart in the reference).
+ * iec_set_launch_timing(model, 1) on any model handle (SCUNet, LaMa,
+ * BiRefNet; Real-ESRGAN has its own hooks above) starts a new record: every
+ * later launch of the general GEMM, its split-K reduce, the layer norms,
+ * the window attention, the Fourier transforms and BiRefNet's deformable
+ * sampling and resizes records a CUDA event before and after itself on the
+ * stream it runs on, with its algorithmic FLOPs and bytes (the inputs read
+ * once, the outputs written once); meanwhile passes run eagerly instead of
+ * as CUDA graphs, with the work of their side streams on the pass's own
+ * stream, so that each event pair times one kernel alone. iec_launch_timing waits for the events and writes up to
+ * `n` records in launch order, returning how many; 0 turns recording off. */
+typedef struct iec_launch_record {
+  char name[64];  /* kernel, with the product's M x N x K for the GEMM */
+  double flop;    /* algorithmic FLOPs of the launch (0 for data movement) */
+  double bytes;   /* algorithmic bytes */
+  float ms;       /* CUDA-event duration */
+} iec_launch_record;
+
+iec_status iec_set_launch_timing(void* model, int on);
+size_t iec_launch_timing(void* model, iec_launch_record* records, size_t n);
+
 /* Diagnostics (no counterpart in the reference): one launch of the general
  * GEMM on host arrays. conv = 0: `a` rows_or_h x k, `weights` k x n; conv = 1:
  * `a` rows_or_h x w x k, `weights` 9k x n (3x3, zero padding). act 0 none,

@@ -87,3 +87,37 @@ def test_birefnet_replays_match_the_eager_run(workdir):
     m.close()
     assert all(_same(o, outs[0]) for o in outs[1:])
     assert all(_same(h, outs[0]) for h in host)
+
+
+def test_launch_timing_records_an_eager_pass_with_the_same_output(workdir):
+    """iec_set_launch_timing: the pass runs eagerly with events around every
+    instrumented launch; its output equals the graph replay's bit for bit and
+    every record has a duration and algorithmic work."""
+    import torch
+
+    import iec
+
+    path = str(workdir / "scunet_timing.weights")
+    W.write_scunet(path, 0)
+    m = iec.Scunet(path)
+    s = torch.cuda.Stream()
+    img = torch.from_numpy(W.scunet_input(96, 64, 5)).cuda()
+    try:
+        want = None
+        for _ in range(3):  # eager, captured, replayed
+            want = torch.empty_like(img)
+            m.run_device(img.data_ptr(), 96, 64, want.data_ptr(), s.cuda_stream)
+        iec.set_launch_timing(m, True)
+        got = torch.empty_like(img)
+        m.run_device(img.data_ptr(), 96, 64, got.data_ptr(), s.cuda_stream)
+        s.synchronize()
+        recs = iec.launch_timing(m)
+        iec.set_launch_timing(m, False)
+        assert _same(got.cpu().numpy(), want.cpu().numpy())
+        names = {r["name"].split(" ")[0] for r in recs}
+        assert any(n.startswith("igemm_sm100") for n in names)
+        assert {"layer_norm_rows", "window_attention_kernel"} <= names
+        assert all(r["ms"] > 0 and (r["flop"] > 0 or r["bytes"] > 0) for r in recs)
+        assert iec.launch_timing(m) == []  # off: a new, empty record
+    finally:
+        m.close()
