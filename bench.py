@@ -619,6 +619,29 @@ def main():
                      "value": TW * TW * 16 / 1e6 / t_s, "unit": "MP/s", "ms_per_step": t_s * 1e3,
                      "steps": tiles_steps, "tiles_rank0": [first, last],
                      "computed_over_algorithmic_px": sum(t.cost for t in grid) / (TW * TW)}
+        if world > 1:
+            # Reassembly on rank 0 over NCCL (each rank's band of output rows,
+            # point to point, device to device), timed as the max over ranks,
+            # then checked bit for bit against rank 0's own run of all 64 tiles.
+            ranges = shard.split_ranges([t.cost for t in grid], world)
+            shard.gather_bands(big_out, grid, ranges, rank, world, dist)  # warm: NCCL sets up its P2P links
+            barrier()
+            torch.cuda.synchronize()
+            g0 = time.perf_counter()
+            shard.gather_bands(big_out, grid, ranges, rank, world, dist)
+            torch.cuda.synchronize()
+            g_s = max_over_ranks(time.perf_counter() - g0)
+            barrier()
+            equal = None
+            if rank == 0:
+                ref = torch.empty_like(big_out)
+                model.run_tiles_device(big_in.data_ptr(), TW, TW, TILE, MARGIN, 0, len(grid), ref.data_ptr(), sptr)
+                torch.cuda.synchronize()
+                equal = bool(torch.equal(big_out.view(torch.int32), ref.view(torch.int32)))
+                del ref
+            barrier()
+            tiles_leg.update({"gather_ms": g_s * 1e3, "gather": "NCCL point-to-point bands of output rows to rank 0 (second gather; the first sets up the links)",
+                              "reassembled_bit_equal": equal})
         del big_in, big_out
 
     # One image (the single-image configuration) on one GPU, device-resident.

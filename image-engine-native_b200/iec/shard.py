@@ -104,3 +104,39 @@ def gather_windows(local, rank: int, world: int, dist=None):
     if rank != 0:
         return None
     return [w for part in parts for w in part]
+
+
+def band_of(tiles: list[Tile], first: int, last: int, scale: int = 4) -> tuple[int, int]:
+    """Output rows [y0, y1) that hold the windows of tiles first .. last - 1
+    (a contiguous row-major range, so one band of whole output rows)."""
+    if first >= last:
+        return 0, 0
+    return scale * min(t.y0 for t in tiles[first:last]), scale * max(t.y1 for t in tiles[first:last])
+
+
+def gather_bands(out, tiles: list[Tile], ranges: list[tuple[int, int]], rank: int, world: int, dist, scale: int = 4):
+    """Reassemble a tiled output on rank 0 without leaving the devices: rank
+    r > 0 sends the band of output rows its tiles' windows lie in (a
+    contiguous slice of `out`, a (scale H) x (scale W) x 3 tensor) with
+    torch.distributed point-to-point sends (NCCL over NVLink for CUDA
+    tensors, gloo for CPU ones); rank 0 receives the bands in rank order and
+    copies only that rank's windows into its own `out`. Every rank takes the
+    same steps; returns `out` (complete on rank 0)."""
+    if world == 1:
+        return out
+    if rank != 0:
+        y0, y1 = band_of(tiles, *ranges[rank], scale)
+        if y1 > y0:
+            dist.send(out[y0:y1].contiguous(), dst=0)
+        return out
+    for r in range(1, world):
+        first, last = ranges[r]
+        y0, y1 = band_of(tiles, first, last, scale)
+        if y1 <= y0:
+            continue
+        band = out.new_empty((y1 - y0,) + tuple(out.shape[1:]))
+        dist.recv(band, src=r)
+        for t in tiles[first:last]:
+            out[scale * t.y0:scale * t.y1, scale * t.x0:scale * t.x1] = \
+                band[scale * t.y0 - y0:scale * t.y1 - y0, scale * t.x0:scale * t.x1]
+    return out

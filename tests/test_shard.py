@@ -91,3 +91,41 @@ def test_two_ranks_over_gloo_reassemble_the_tiled_run(realesrgan_weights, tmp_pa
     assert np.array_equal(stitched.view(np.uint32), tiled.view(np.uint32))
     whole = model.run_float(image)
     assert np.abs(stitched - whole).max() < 1e-4
+
+
+def _band_rank(rank, world, port, result_path):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tiles = shard.tile_grid(70, 45, 24, 34)
+        ranges = shard.split_ranges([t.cost for t in tiles], world)
+        first, last = ranges[rank]
+        out = torch.full((180, 280, 3), -1.0)
+        for t in tiles[first:last]:  # this rank's windows: the tile's index as the value
+            out[4 * t.y0:4 * t.y1, 4 * t.x0:4 * t.x1] = float(t.index)
+        shard.gather_bands(out, tiles, ranges, rank, world, dist)
+        if rank == 0:
+            np.save(result_path, out.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bands_gathered_point_to_point_reassemble_every_window(tmp_path):
+    """shard.gather_bands (device tensors on GPUs, here CPU tensors over
+    gloo): three ranks whose tile ranges split a row of tiles; rank 0 ends
+    with every tile's window and nothing else overwritten."""
+    import torch.multiprocessing as mp
+
+    result = str(tmp_path / "bands.npy")
+    mp.start_processes(_band_rank, args=(3, _free_port(), result), nprocs=3, join=True, start_method="spawn")
+    out = np.load(result)
+    tiles = shard.tile_grid(70, 45, 24, 34)
+    want = np.full((180, 280, 3), -1.0, np.float32)
+    for t in tiles:
+        want[4 * t.y0:4 * t.y1, 4 * t.x0:4 * t.x1] = t.index
+    assert np.array_equal(out, want)
+    ranges = shard.split_ranges([t.cost for t in tiles], 3)
+    assert any(ranges[r][0] % 3 for r in range(1, 3))  # a range starts inside a tile row
