@@ -546,6 +546,7 @@ struct Birefnet::SwinBlock {
   bool shifted = false;
   DeviceBuffer n1g, n1b, n2g, n2b, bias;
   PackedWeights qkv, proj, fc1, fc2;
+  MlpWeights mlp;  // norm2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
 };
 
 struct Birefnet::Stage {
@@ -590,10 +591,21 @@ Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
       upload(blk.bias, attention_bias_layout(
                            slot_tables(f.take(p + ".position_bias", {(size_t)heads, NTOK, NTOK}), heads, blk.shifted)));
       pack(f, blk.proj, p + ".proj", 1, c, c, true);
-      upload(blk.n2g, f.take(p + ".norm2.weight", {(size_t)c}));
-      upload(blk.n2b, f.take(p + ".norm2.bias", {(size_t)c}));
-      pack(f, blk.fc1, p + ".fc1", 1, c, 4 * c, true);
-      pack(f, blk.fc2, p + ".fc2", 1, 4 * c, c, true);
+      {
+        // norm2 and the MLP: the separate launches' weights, and the same
+        // values packed for the fused MLP kernel
+        const std::vector<float> g2 = f.take(p + ".norm2.weight", {(size_t)c});
+        const std::vector<float> be2 = f.take(p + ".norm2.bias", {(size_t)c});
+        HostTensor w1 = f.take_tensor(p + ".fc1.weight", {(size_t)c, (size_t)(4 * c)});
+        const std::vector<float> bb1 = f.take(p + ".fc1.bias", {(size_t)(4 * c)});
+        HostTensor w2 = f.take_tensor(p + ".fc2.weight", {(size_t)(4 * c), (size_t)c});
+        const std::vector<float> bb2 = f.take(p + ".fc2.bias", {(size_t)c});
+        upload(blk.n2g, g2);
+        upload(blk.n2b, be2);
+        pack_weights(blk.fc1, w1.values, 1, c, 4 * c, bb1.data());
+        pack_weights(blk.fc2, w2.values, 1, 4 * c, c, bb2.data());
+        if (mlp_preferred(c)) pack_mlp(blk.mlp, c, w1.values, bb1, w2.values, bb2, g2, be2);
+      }
       st->blocks.push_back(std::move(blk));
     }
     const std::string sn = "stage" + std::to_string(s);
@@ -832,18 +844,22 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
       o.pad_w = pad;
       gemm_rows(dev_, B.proj, bb.att.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
       // MLP: x += fc2(GELU(fc1(LN2(x))))
-      layer_norm_planar(x, xp, 0, (int)tokens, c, B.n2g.as<float>(), B.n2b.as<float>(), bb.ln.as<__half>(), xp, nullptr,
-                        s);
-      GemmOutSpec h;
-      h.mode = OUT_STORE;
-      h.out = bb.hid.as<__half>();
-      h.plane_elems = xp;
-      gemm_rows(dev_, B.fc1, bb.ln.as<__half>(), xp, (int)tokens, ACT_GELU, h, s);
-      GemmOutSpec a;
-      a.mode = OUT_ACCUM;
-      a.out = x;
-      a.plane_elems = xp;
-      gemm_rows(dev_, B.fc2, bb.hid.as<__half>(), xp, (int)tokens, ACT_NONE, a, s);
+      if (fused_mlp_ && B.mlp.c == c) {
+        mlp_planar(dev_, B.mlp, x, xp, (int)tokens, s);
+      } else {
+        layer_norm_planar(x, xp, 0, (int)tokens, c, B.n2g.as<float>(), B.n2b.as<float>(), bb.ln.as<__half>(), xp,
+                          nullptr, s);
+        GemmOutSpec h;
+        h.mode = OUT_STORE;
+        h.out = bb.hid.as<__half>();
+        h.plane_elems = xp;
+        gemm_rows(dev_, B.fc1, bb.ln.as<__half>(), xp, (int)tokens, ACT_GELU, h, s);
+        GemmOutSpec a;
+        a.mode = OUT_ACCUM;
+        a.out = x;
+        a.plane_elems = xp;
+        gemm_rows(dev_, B.fc2, bb.hid.as<__half>(), xp, (int)tokens, ACT_NONE, a, s);
+      }
     }
     // the stage's normalised output
     layer_norm_planar(x, xp, 0, (int)tokens, c, st.ng.as<float>(), st.nb.as<float>(),

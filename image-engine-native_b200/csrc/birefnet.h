@@ -36,6 +36,14 @@ class Birefnet {
 
   DeviceBuffer host_in, host_out;  // staging of the host entry points
 
+  // Each backbone block's MLP runs fused where its width allows (the
+  // default: norm2, fc1, GELU and fc2 in one kernel, mlp_sm100.cuh) or as a
+  // LayerNorm launch and two GEMMs (for comparisons).
+  void set_fused(bool on) {
+    fused_mlp_ = on;
+    alloc_gen_++;  // no captured pass of the other path replays
+  }
+
   struct SwinBlock;
   struct Stage;
   struct DBlock;
@@ -81,6 +89,7 @@ class Birefnet {
   cudaStream_t s_half_ = nullptr, s_patch_ = nullptr, s_aspp_ = nullptr;
   cudaEvent_t ev_prep_ = nullptr, ev_half_ = nullptr, ev_t_ = nullptr, ev_aspp_ = nullptr, ev_patch_[4] = {};
   PassGraph graph_;
+  bool fused_mlp_ = true;
   uint64_t alloc_gen_ = 0;  // counts ensure()'s reallocations
 };
 

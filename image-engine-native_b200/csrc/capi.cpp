@@ -560,6 +560,20 @@ iec_status iec_lama_run_device(iec_lama* model, const float* image, const float*
   });
 }
 
+iec_status iec_scunet_set_fused(iec_scunet* model, int on) {
+  return guard([&] {
+    need_model(model);
+    model->model->set_fused(on != 0);
+  });
+}
+
+iec_status iec_birefnet_set_fused(iec_birefnet* model, int on) {
+  return guard([&] {
+    need_model(model);
+    model->model->set_fused(on != 0);
+  });
+}
+
 iec_status iec_lama_set_fused(iec_lama* model, int on) {
   return guard([&] {
     need_model(model);

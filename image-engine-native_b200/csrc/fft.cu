@@ -580,9 +580,6 @@ __device__ __forceinline__ uint4 ld_peer16(const void* local, uint32_t rank) {
   return v;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __global__ void __launch_bounds__(FU_THREADS, 1) fourier_unit_cols(const FuParams p) {
   extern __shared__ __align__(128) uint8_t fu_smem[];
@@ -707,7 +704,7 @@ __global__ void __launch_bounds__(FU_THREADS, 1) fourier_unit_cols(const FuParam
     for (int i = 0; i < CPER; i++)
       if (at[i]) *reinterpret_cast<uint4*>(at[i]) = v[i];
   }
-  fence_proxy_async_smem();
+  fence_proxy_async_shared();
   cluster_sync_all();  // every peer has read our quarter: we may leave at any time from here
 
   // ---- the 1x1 product: D[128 rows][96] = A[128][384] x B[384][96]

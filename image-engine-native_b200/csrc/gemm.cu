@@ -5,6 +5,7 @@
 #include <algorithm>
 
 #include "igemm_sm100.cuh"
+#include "mlp_sm100.cuh"
 
 namespace iec {
 
@@ -253,6 +254,101 @@ void gemm_rows(Device& dev, const PackedWeights& pw, const __half* a, long long 
   p.dev_err = dev.dev_err();
   if (p.tiles >= (1 << 24)) throw Error(ERR_INPUT, "GEMM too large for one launch");
   run_gemm<A_ROWS>(dev, pw, map, p, s);
+}
+
+bool mlp_fits(int c) {
+  return c == 32 || c == 64 || c == 96 || c == 128 || c == 192 || c == 256 || c == 384;
+}
+
+// Wider MLPs run as LayerNorm and two GEMM launches: with their few row
+// tiles and many hidden chunks the fused kernel's per-chunk hand-offs cost
+// more than the launches it saves (measured: 256 channels over 6144 rows
+// took 74 us fused against about 42 as three launches).
+bool mlp_preferred(int c) { return mlp_fits(c) && c <= 192; }
+
+void pack_mlp(MlpWeights& mw, int c, const std::vector<float>& w1, const std::vector<float>& b1,
+              const std::vector<float>& w2, const std::vector<float>& b2, const std::vector<float>& gamma,
+              const std::vector<float>& beta) {
+  if (!mlp_fits(c)) throw Error(ERR_INPUT, "fused MLP of " + std::to_string(c) + " channels");
+  const size_t hid = (size_t)4 * c;
+  if (w1.size() != c * hid || w2.size() != c * hid || b1.size() != hid || b2.size() != (size_t)c ||
+      gamma.size() != (size_t)c || beta.size() != (size_t)c)
+    throw Error(ERR_WEIGHTS, "MLP weights of the wrong size");
+  const int nh = mlp_nh(c), chunks = (int)hid / nh;
+  // per chunk j: W1 columns j nh .. as [c / 8][nh][8], then W2 rows j nh ..
+  // as [nh / 8][c][8] (the core-matrix images of fc1's and fc2's B operands)
+  std::vector<uint16_t> w((size_t)chunks * 2 * c * nh);
+  size_t at = 0;
+  for (int j = 0; j < chunks; j++) {
+    for (int g = 0; g < c / 8; g++)
+      for (int n = 0; n < nh; n++)
+        for (int e = 0; e < 8; e++) w[at++] = f32_to_half(w1[(size_t)(8 * g + e) * hid + (size_t)j * nh + n]);
+    for (int g = 0; g < nh / 8; g++)
+      for (int n = 0; n < c; n++)
+        for (int e = 0; e < 8; e++) w[at++] = f32_to_half(w2[((size_t)j * nh + 8 * g + e) * c + n]);
+  }
+  std::vector<float> par;
+  par.insert(par.end(), gamma.begin(), gamma.end());
+  par.insert(par.end(), beta.begin(), beta.end());
+  par.insert(par.end(), b1.begin(), b1.end());
+  par.insert(par.end(), b2.begin(), b2.end());
+  mw.c = c;
+  mw.w.reserve(w.size() * 2);
+  mw.params.reserve(par.size() * 4);
+  IEC_CUDA(cudaMemcpy(mw.w.get(), w.data(), w.size() * 2, cudaMemcpyHostToDevice));
+  IEC_CUDA(cudaMemcpy(mw.params.get(), par.data(), par.size() * 4, cudaMemcpyHostToDevice));
+}
+
+namespace {
+
+template <int C>
+void launch_mlp(Device& dev, const CUtensorMap& map, const MlpParams& p, cudaStream_t s) {
+  using L = MlpSmem<C>;
+  static bool prepared[64] = {};
+  if (!prepared[dev.ordinal() & 63]) {
+    IEC_CUDA(cudaFuncSetAttribute(mlp_sm100<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    prepared[dev.ordinal() & 63] = true;
+  }
+  launch_pdl(mlp_sm100<C>, std::min(p.tiles, dev.sms() * L::CTAS), L::THREADS, (size_t)L::TOTAL, s, map, p);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_elems, int rows, cudaStream_t s) {
+  const int c = mw.c;
+  if (!mlp_fits(c) || rows <= 0) throw Error(ERR_INPUT, "fused MLP shape");
+  const int alloc = gemm_rows_alloc(rows);
+  if (plane_elems < (long long)alloc * 8) throw Error(ERR_INPUT, "MLP planes too short");
+  // the A_ROWS box of gemm_rows with every channel group in one box
+  CUtensorMap map;
+  const uint64_t dims[3] = {128, (uint64_t)alloc / 16, (uint64_t)c / 8};
+  const uint64_t strides[2] = {256, (uint64_t)plane_elems * 2};
+  const uint32_t box[3] = {128, 8, (uint32_t)c / 8};
+  encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, strides, box);
+  MlpParams p{};
+  p.M = rows;
+  p.tiles = (rows + 127) / 128;
+  p.x = x;
+  p.plane_elems = plane_elems;
+  p.w = mw.w.as<uint8_t>();
+  p.params = mw.params.as<float>();
+  p.dev_err = dev.dev_err();
+  const double hid = 4.0 * c;
+  char name[64];
+  snprintf(name, sizeof name, "mlp_sm100<%d> %dx%d", c, rows, c);
+  // FLOPs of fc1 and fc2; bytes: the rows read and written, the weights
+  timed_launch(name, 4.0 * rows * c * hid, (double)rows * c * 4 + 4.0 * c * hid, s, [&] {
+    switch (c) {
+      case 32: return launch_mlp<32>(dev, map, p, s);
+      case 64: return launch_mlp<64>(dev, map, p, s);
+      case 96: return launch_mlp<96>(dev, map, p, s);
+      case 128: return launch_mlp<128>(dev, map, p, s);
+      case 192: return launch_mlp<192>(dev, map, p, s);
+      case 256: return launch_mlp<256>(dev, map, p, s);
+      default: return launch_mlp<384>(dev, map, p, s);
+    }
+  });
 }
 
 void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map_ptr, long long map_plane_elems, int h, int w,

@@ -119,6 +119,22 @@ void layer_norm_planar(const __half* src, long long src_plane_elems, int plane0,
 void merge_layer_norm_planar(const __half* src, long long src_plane_elems, int grid, int c, const float* gamma,
                              const float* beta, __half* dst, long long dst_plane_elems, cudaStream_t s);
 
+// The fused transformer MLP (mlp_sm100.cuh): x += fc2(GELU(fc1(LN(x)))) over
+// `rows` rows of the C channels at `x` (planar, plane stride plane_elems,
+// planes of at least gemm_rows_alloc(rows) rows), C in {32, 64, 96, 128, 192,
+// 256, 384}; LN eps 1e-5.
+struct MlpWeights {
+  int c = 0;
+  DeviceBuffer w, params;
+};
+bool mlp_fits(int c);
+bool mlp_preferred(int c);  // fused where it is the faster form
+// w1: c x 4c (row k, column n), w2: 4c x c; biases and LayerNorm weights f32.
+void pack_mlp(MlpWeights& mw, int c, const std::vector<float>& w1, const std::vector<float>& b1,
+              const std::vector<float>& w2, const std::vector<float>& b2, const std::vector<float>& gamma,
+              const std::vector<float>& beta);
+void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_elems, int rows, cudaStream_t s);
+
 // Fused attention over 8 x 8 windows (attention.cu): `qkv` planar [3c / 8]
 // [windows * 64][8], `bias` [classes][c / 32][64][64] f32 (classes 4 when
 // `shifted`, else 1), output planar [c / 8][windows * 64][8].

@@ -19,6 +19,7 @@ struct Scunet::Block {
   int c = 0, h = 0;
   bool shifted = false;
   PackedWeights split, conv1, conv2, join, qkv, proj, fc1, fc2;
+  MlpWeights mlp;  // LN2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
   DeviceBuffer ln1g, ln1b, ln2g, ln2b, bias;  // LN params f32; attention bias tables f32
 };
 
@@ -180,10 +181,20 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
     linear(f, b.qkv, t + ".msa.embedding_layer", h, 3 * h, true);
     upload(b.bias, attention_bias_layout(bias_tables(f.take(t + ".msa.position_bias", {(size_t)(h / 32), 64, 64}), shifted)));
     linear(f, b.proj, t + ".msa.linear", h, h, true);
-    upload(b.ln2g, f.take(t + ".ln2.weight", {(size_t)h}));
-    upload(b.ln2b, f.take(t + ".ln2.bias", {(size_t)h}));
-    linear(f, b.fc1, t + ".mlp.0", h, 4 * h, true);
-    linear(f, b.fc2, t + ".mlp.2", 4 * h, h, true);
+    {
+      // LN2 and the MLP: the separate launches' weights, and the same values
+      // packed for the fused MLP kernel.
+      const std::vector<float> g2 = f.take(t + ".ln2.weight", {(size_t)h}), be2 = f.take(t + ".ln2.bias", {(size_t)h});
+      HostTensor w1 = f.take_tensor(t + ".mlp.0.weight", {(size_t)h, (size_t)(4 * h)});
+      const std::vector<float> bb1 = f.take(t + ".mlp.0.bias", {(size_t)(4 * h)});
+      HostTensor w2 = f.take_tensor(t + ".mlp.2.weight", {(size_t)(4 * h), (size_t)h});
+      const std::vector<float> bb2 = f.take(t + ".mlp.2.bias", {(size_t)h});
+      upload(b.ln2g, g2);
+      upload(b.ln2b, be2);
+      pack_weights(b.fc1, w1.values, 1, h, 4 * h, bb1.data());
+      pack_weights(b.fc2, w2.values, 1, 4 * h, h, bb2.data());
+      if (mlp_fits(h)) pack_mlp(b.mlp, h, w1.values, bb1, w2.values, bb2, g2, be2);
+    }
     linear(f, b.join, name + ".conv1_2", c, c, true);
   };
   auto load_level = [&](Level& L, const std::string& name, int first, int c) {
@@ -363,15 +374,19 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       o.shift = shift;
       gemm_rows(dev_, B.proj, att, pl, Pl, ACT_NONE, o, s);
       // MLP (swin.rs:222-254): y[h:] += fc2(gelu(fc1(LN2(y[h:])))).
-      layer_norm_planar(y, pl, h / 8, Pl, h, B.ln2g.as<float>(), B.ln2b.as<float>(), ln2, pl, nullptr, s);
-      o.mode = OUT_STORE;
-      o.out = hid;
-      o.plane0 = 0;
-      gemm_rows(dev_, B.fc1, ln2, pl, Pl, ACT_GELU, o, s);
-      o.mode = OUT_ACCUM;
-      o.out = y;
-      o.plane0 = h / 8;
-      gemm_rows(dev_, B.fc2, hid, pl, Pl, ACT_NONE, o, s);
+      if (fused_mlp_ && B.mlp.c == h && mlp_preferred(h)) {
+        mlp_planar(dev_, B.mlp, y + (long long)(h / 8) * pl, pl, Pl, s);
+      } else {
+        layer_norm_planar(y, pl, h / 8, Pl, h, B.ln2g.as<float>(), B.ln2b.as<float>(), ln2, pl, nullptr, s);
+        o.mode = OUT_STORE;
+        o.out = hid;
+        o.plane0 = 0;
+        gemm_rows(dev_, B.fc1, ln2, pl, Pl, ACT_GELU, o, s);
+        o.mode = OUT_ACCUM;
+        o.out = y;
+        o.plane0 = h / 8;
+        gemm_rows(dev_, B.fc2, hid, pl, Pl, ACT_NONE, o, s);
+      }
       // x += join(y); y = next split(x) (network.rs:190-212).
       IEC_CUDA(cudaStreamWaitEvent(s, ev_conv_, 0));
       o.mode = OUT_ACCUM;

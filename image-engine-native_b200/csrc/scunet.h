@@ -46,6 +46,14 @@ class Scunet {
 
   DeviceBuffer host_in, host_out;
 
+  // Each transformer MLP runs fused (the default: LayerNorm, fc1, GELU and
+  // fc2 in one kernel, mlp_sm100.cuh) or as a LayerNorm launch and two GEMMs
+  // (for comparisons).
+  void set_fused(bool on) {
+    fused_mlp_ = on;
+    alloc_gen_++;  // no captured pass of the other path replays
+  }
+
   struct Block;
   struct Level;
 
@@ -64,6 +72,7 @@ class Scunet {
   cudaStream_t s_conv_ = nullptr;
   cudaEvent_t ev_in_ = nullptr, ev_conv_ = nullptr;
   PassGraph graph_;
+  bool fused_mlp_ = true;
   uint64_t alloc_gen_ = 0;  // counts ensure()'s reallocations  // passes without progress reports
 };
 

@@ -81,6 +81,10 @@ def lib():
         L.iec_set_launch_timing.argtypes = [vp, ctypes.c_int]
         L.iec_launch_timing.argtypes = [vp, ctypes.POINTER(LaunchRecord), sz]
         L.iec_launch_timing.restype = sz
+        L.iec_scunet_set_fused.argtypes = [vp, ctypes.c_int]
+        L.iec_scunet_set_fused.restype = ctypes.c_int
+        L.iec_birefnet_set_fused.argtypes = [vp, ctypes.c_int]
+        L.iec_birefnet_set_fused.restype = ctypes.c_int
         L.iec_lama_set_fused.argtypes = [vp, ctypes.c_int]
         L.iec_selftest_fourier_unit_time.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_float)]
@@ -345,6 +349,10 @@ class Scunet:
         """run_float on device pointers, queued on `stream`."""
         _check(lib().iec_scunet_run_device(self._h, image_ptr, width, height, out_ptr, stream or None))
 
+    def set_fused(self, on: bool):
+        """Fused transformer MLPs (default) or LayerNorm + two GEMMs apart."""
+        _check(lib().iec_scunet_set_fused(self._h, 1 if on else 0))
+
     def run_batch(self, images, out=None, stream: int = 0):
         """Batched run_float on host arrays (N x H x W x 3 float32; numpy or
         page-locked torch tensors), copies overlapped with the kernels."""
@@ -467,6 +475,10 @@ class Birefnet:
         out = np.empty((side, side), np.float32)
         _check(lib().iec_birefnet_run_normalized(self._h, _f32(image), side, _f32(out)))
         return out
+
+    def set_fused(self, on: bool):
+        """Fused backbone MLPs (default) or LayerNorm + two GEMMs apart."""
+        _check(lib().iec_birefnet_set_fused(self._h, 1 if on else 0))
 
     def run_batch(self, images, out=None, stream: int = 0):
         """Batched run on host arrays: N x side x side x 3 uint8 images to

@@ -221,6 +221,13 @@ iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t w
 iec_status iec_scunet_run_batch(iec_scunet* model, const float* images, size_t count, size_t width,
                                 size_t height, float* out, void* stream);
 
+/* Each transformer block's MLP runs fused (the default, `on` = 1: LayerNorm,
+ * fc1, GELU and fc2 in one kernel, the hidden layer kept in shared memory)
+ * or, with `on` = 0, as a LayerNorm launch and two GEMM launches through a
+ * device buffer (for comparisons; no counterpart in the reference). The two
+ * agree to f16 rounding (the LayerNorm sums run in another order). */
+iec_status iec_scunet_set_fused(iec_scunet* model, int on);
+
 /* -------------------------------------------------------------------- LaMa
  * crates/lama-native/src/lib.rs: Big LaMa inpainting, output the size of the
  * input. Sides of at least 9 pixels (lib.rs:180-194); at most 12288 here. */
@@ -294,6 +301,12 @@ iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int i
  * copies overlapped with the kernels as in iec_scunet_run_batch. */
 iec_status iec_birefnet_run_batch(iec_birefnet* model, const uint8_t* images, size_t count, size_t side,
                                   float* logits, void* stream);
+
+/* The backbone blocks' MLPs of widths 96 and 192 run fused (the default,
+ * `on` = 1: norm2, fc1, GELU and fc2 in one kernel) or, with `on` = 0, as a
+ * LayerNorm launch and two GEMM launches (for comparisons; no counterpart in
+ * the reference). The two agree to f16 rounding. */
+iec_status iec_birefnet_set_fused(iec_birefnet* model, int on);
 
 /* Launch timing (measurement hooks, no counterpart in the reference).
  * iec_set_launch_timing(model, 1) on any model handle (SCUNet, LaMa,

@@ -112,3 +112,21 @@ def test_batch_matches_single_runs(gpu_model):
     singles = np.stack([gpu_model.run(im) for im in images])
     batch = gpu_model.run_batch(images)
     assert np.array_equal(batch.view(np.uint32), singles.view(np.uint32))
+
+
+def test_fused_mlp_matches_separate_launches(gpu_model):
+    """The fused backbone MLPs (widths 96 and 192) against LayerNorm + fc1 +
+    fc2 as separate launches: the same f16 roundings, the LayerNorm sums in
+    another order; the masks agree far inside the 1/255 bar."""
+    rgb = W.birefnet_input(256, 7)
+    try:
+        fused = gpu_model.run(rgb)
+        gpu_model.set_fused(False)
+        apart = gpu_model.run(rgb)
+    finally:
+        gpu_model.set_fused(True)
+    assert np.isfinite(fused).all()
+    sig = lambda z: 1.0 / (1.0 + np.exp(-z.astype(np.float64)))  # noqa: E731
+    err = float(np.abs(sig(fused) - sig(apart)).max())
+    print(f"fused vs separate: mask max abs {err:.3g}")
+    assert err <= 1.0 / 1020

@@ -151,3 +151,24 @@ def test_batch_matches_single_runs(gpu_model):
     singles = np.stack([gpu_model.run_float(im) for im in images])
     batch = gpu_model.run_batch(images)
     assert np.array_equal(batch.view(np.uint32), singles.view(np.uint32))
+
+
+@pytest.mark.parametrize("w,h,seed", [(768, 512, 0), (100, 70, 8)])
+def test_fused_mlp_matches_separate_launches(gpu_model, w, h, seed):
+    """The fused transformer MLP (LayerNorm in shared memory, fc1, GELU and
+    fc2 in one kernel) against LayerNorm + fc1 + fc2 as separate launches.
+    Both round the normalised rows, the hidden layer and the sums to f16 at
+    the same points; only the LayerNorm sums run in another order, which can
+    move an f16 rounding by one step."""
+    image = W.scunet_input(w, h, seed)
+    try:
+        fused = gpu_model.run_float(image)
+        gpu_model.set_fused(False)
+        apart = gpu_model.run_float(image)
+    finally:
+        gpu_model.set_fused(True)
+    assert np.isfinite(fused).all()
+    err = float(np.abs(fused - apart).max())
+    p = psnr(fused, apart)
+    print(f"{w}x{h}: fused vs separate max abs {err:.3g}, PSNR {p:.1f} dB")
+    assert err <= 1e-2 and p >= 60.0, (err, p)
