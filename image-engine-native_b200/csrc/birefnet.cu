@@ -547,6 +547,7 @@ struct Birefnet::SwinBlock {
   DeviceBuffer n1g, n1b, n2g, n2b, bias;
   PackedWeights qkv, proj, fc1, fc2;
   MlpWeights mlp;  // norm2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
+  LnRowsWeights lnqkv;  // norm1 + window partition + qkv (lnrows_sm100.cuh), where the width fits
 };
 
 struct Birefnet::Stage {
@@ -585,9 +586,19 @@ Birefnet::Birefnet(const std::string& path, const Options& opt) : dev_(opt) {
       blk.c = c;
       blk.heads = heads;
       blk.shifted = b % 2 == 1;
-      upload(blk.n1g, f.take(p + ".norm1.weight", {(size_t)c}));
-      upload(blk.n1b, f.take(p + ".norm1.bias", {(size_t)c}));
-      pack(f, blk.qkv, p + ".qkv", 1, c, 3 * c, true);
+      {
+        // norm1 and qkv: the separate launches' weights, and the same values
+        // for the kernel that folds norm1 and the window partition into the
+        // product's staged rows
+        const std::vector<float> g1 = f.take(p + ".norm1.weight", {(size_t)c});
+        const std::vector<float> be1 = f.take(p + ".norm1.bias", {(size_t)c});
+        HostTensor wq = f.take_tensor(p + ".qkv.weight", {(size_t)c, (size_t)(3 * c)});
+        const std::vector<float> bq = f.take(p + ".qkv.bias", {(size_t)(3 * c)});
+        upload(blk.n1g, g1);
+        upload(blk.n1b, be1);
+        pack_weights(blk.qkv, wq.values, 1, c, 3 * c, bq.data());
+        if (lnrows_fits(c, 3 * c)) pack_lnrows(blk.lnqkv, c, 3 * c, wq.values, bq, g1, be1);
+      }
       upload(blk.bias, attention_bias_layout(
                            slot_tables(f.take(p + ".position_bias", {(size_t)heads, NTOK, NTOK}), heads, blk.shifted)));
       pack(f, blk.proj, p + ".proj", 1, c, c, true);
@@ -825,12 +836,17 @@ void Birefnet::backbone(const float* img, int side, __half* const dst[4], const 
       const int shift = B.shifted ? SHIFT : 0;
       // attention: x += proj(attn(window(LN1(x))))
       const WindowMap wm{WS, pad, pad, grid, grid, shift};
-      layer_norm_planar(x, xp, 0, (int)slots, c, B.n1g.as<float>(), B.n1b.as<float>(), bb.tok.as<__half>(), sp, &wm, s);
       GemmOutSpec o;
-      o.mode = OUT_STORE;
-      o.out = bb.qkv.as<__half>();
-      o.plane_elems = sp;
-      gemm_rows(dev_, B.qkv, bb.tok.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
+      if (fused_mlp_ && B.lnqkv.c == c) {
+        lnrows_planar(dev_, B.lnqkv, x, xp, (int)slots, wm, bb.qkv.as<__half>(), sp, s);
+      } else {
+        layer_norm_planar(x, xp, 0, (int)slots, c, B.n1g.as<float>(), B.n1b.as<float>(), bb.tok.as<__half>(), sp, &wm,
+                          s);
+        o.mode = OUT_STORE;
+        o.out = bb.qkv.as<__half>();
+        o.plane_elems = sp;
+        gemm_rows(dev_, B.qkv, bb.tok.as<__half>(), sp, (int)slots, ACT_NONE, o, s);
+      }
       window_attention(bb.qkv.as<__half>(), sp, c, (int)(slots / 64), B.bias.as<float>(), B.shifted, wins, wins,
                        bb.att.as<__half>(), sp, dev_.dev_err(), s);
       o.mode = OUT_WINDOW_ACCUM;

@@ -6,6 +6,7 @@
 
 #include "igemm_sm100.cuh"
 #include "mlp_sm100.cuh"
+#include "lnrows_sm100.cuh"
 
 namespace iec {
 
@@ -348,6 +349,76 @@ void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_el
       case 256: return launch_mlp<256>(dev, map, p, s);
       default: return launch_mlp<384>(dev, map, p, s);
     }
+  });
+}
+
+bool lnrows_fits(int c, int n) {
+  return (c == 32 && n == 96) || (c == 64 && n == 192) || (c == 96 && n == 288) || (c == 128 && n == 384);
+}
+
+void pack_lnrows(LnRowsWeights& lw, int c, int n, const std::vector<float>& w, const std::vector<float>& bias,
+                 const std::vector<float>& gamma, const std::vector<float>& beta) {
+  if (!lnrows_fits(c, n)) throw Error(ERR_INPUT, "folded LayerNorm product of this shape");
+  if (w.size() != (size_t)c * n || bias.size() != (size_t)n || gamma.size() != (size_t)c || beta.size() != (size_t)c)
+    throw Error(ERR_WEIGHTS, "folded LayerNorm product weights of the wrong size");
+  std::vector<uint16_t> img((size_t)c * n);
+  size_t at = 0;
+  for (int g = 0; g < c / 8; g++)
+    for (int j = 0; j < n; j++)
+      for (int e = 0; e < 8; e++) img[at++] = f32_to_half(w[(size_t)(8 * g + e) * n + j]);
+  std::vector<float> par;
+  par.insert(par.end(), gamma.begin(), gamma.end());
+  par.insert(par.end(), beta.begin(), beta.end());
+  par.insert(par.end(), bias.begin(), bias.end());
+  lw.c = c;
+  lw.n = n;
+  lw.w.reserve(img.size() * 2);
+  lw.params.reserve(par.size() * 4);
+  IEC_CUDA(cudaMemcpy(lw.w.get(), img.data(), img.size() * 2, cudaMemcpyHostToDevice));
+  IEC_CUDA(cudaMemcpy(lw.params.get(), par.data(), par.size() * 4, cudaMemcpyHostToDevice));
+}
+
+namespace {
+
+template <int C, int N>
+void launch_lnrows(Device& dev, const LnRowsParams& p, cudaStream_t s) {
+  using L = LnRowsSmem<C, N>;
+  static bool prepared[64] = {};
+  if (!prepared[dev.ordinal() & 63]) {
+    IEC_CUDA(cudaFuncSetAttribute(lnrows_sm100<C, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    prepared[dev.ordinal() & 63] = true;
+  }
+  launch_pdl(lnrows_sm100<C, N>, std::min(p.tiles, dev.sms()), L::THREADS, (size_t)L::TOTAL, s, p);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+void lnrows_planar(Device& dev, const LnRowsWeights& lw, const __half* src, long long src_plane, int rows,
+                   const WindowMap& wm, __half* out, long long out_plane, cudaStream_t s) {
+  if (!lnrows_fits(lw.c, lw.n) || rows <= 0) throw Error(ERR_INPUT, "folded LayerNorm product shape");
+  if (wm.ws < 1 || wm.ws > 8 || wm.pad_h % wm.ws || wm.pad_w % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w)
+    throw Error(ERR_INPUT, "window partition geometry is inconsistent");
+  if (out_plane < (long long)rows * 8) throw Error(ERR_INPUT, "output planes too short");
+  LnRowsParams p{};
+  p.rows = rows;
+  p.tiles = (rows + 127) / 128;
+  p.src = src;
+  p.src_plane = src_plane;
+  p.wm = wm;
+  p.w = lw.w.as<uint8_t>();
+  p.params = lw.params.as<float>();
+  p.out = out;
+  p.out_plane = out_plane;
+  p.dev_err = dev.dev_err();
+  char name[64];
+  snprintf(name, sizeof name, "lnrows_sm100<%d,%d> %dx%dx%d", lw.c, lw.n, rows, lw.n, lw.c);
+  // FLOPs of the product; bytes: the rows gathered once, the output, the weights
+  timed_launch(name, 2.0 * rows * lw.n * lw.c, (double)rows * (lw.c + lw.n) * 2 + 2.0 * lw.c * lw.n, s, [&] {
+    if (lw.c == 32) return launch_lnrows<32, 96>(dev, p, s);
+    if (lw.c == 64) return launch_lnrows<64, 192>(dev, p, s);
+    if (lw.c == 96) return launch_lnrows<96, 288>(dev, p, s);
+    return launch_lnrows<128, 384>(dev, p, s);
   });
 }
 

@@ -135,6 +135,22 @@ void pack_mlp(MlpWeights& mw, int c, const std::vector<float>& w1, const std::ve
               const std::vector<float>& beta);
 void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_elems, int rows, cudaStream_t s);
 
+// LayerNorm and the window partition folded into one product
+// (lnrows_sm100.cuh): out row r (window order, as layer_norm_planar's
+// window mode writes) = LN(src[pixel(r)]) x W + b over `rows` rows, for the
+// (c, n) shapes of the window attention's qkv layer: (32, 96), (64, 192),
+// (96, 288), (128, 384).
+struct LnRowsWeights {
+  int c = 0, n = 0;
+  DeviceBuffer w, params;
+};
+bool lnrows_fits(int c, int n);
+// w: c x n (row k, column n); gamma, beta: c; bias: n.
+void pack_lnrows(LnRowsWeights& lw, int c, int n, const std::vector<float>& w, const std::vector<float>& bias,
+                 const std::vector<float>& gamma, const std::vector<float>& beta);
+void lnrows_planar(Device& dev, const LnRowsWeights& lw, const __half* src, long long src_plane, int rows,
+                   const WindowMap& wm, __half* out, long long out_plane, cudaStream_t s);
+
 // Fused attention over 8 x 8 windows (attention.cu): `qkv` planar [3c / 8]
 // [windows * 64][8], `bias` [classes][c / 32][64][64] f32 (classes 4 when
 // `shifted`, else 1), output planar [c / 8][windows * 64][8].

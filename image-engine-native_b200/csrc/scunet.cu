@@ -20,6 +20,7 @@ struct Scunet::Block {
   bool shifted = false;
   PackedWeights split, conv1, conv2, join, qkv, proj, fc1, fc2;
   MlpWeights mlp;  // LN2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
+  LnRowsWeights lnqkv;  // LN1 + window partition + qkv (lnrows_sm100.cuh), where the width fits
   DeviceBuffer ln1g, ln1b, ln2g, ln2b, bias;  // LN params f32; attention bias tables f32
 };
 
@@ -176,9 +177,18 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
     conv3(f, b.conv1, name + ".conv_block.0", h, h, h);
     conv3(f, b.conv2, name + ".conv_block.2", h, h, h);
     const std::string t = name + ".trans_block";
-    upload(b.ln1g, f.take(t + ".ln1.weight", {(size_t)h}));
-    upload(b.ln1b, f.take(t + ".ln1.bias", {(size_t)h}));
-    linear(f, b.qkv, t + ".msa.embedding_layer", h, 3 * h, true);
+    {
+      // LN1 and the qkv layer: the separate launches' weights, and the same
+      // values for the kernel that folds LN1 and the window partition into
+      // the product's staged rows
+      const std::vector<float> g1 = f.take(t + ".ln1.weight", {(size_t)h}), be1 = f.take(t + ".ln1.bias", {(size_t)h});
+      HostTensor wq = f.take_tensor(t + ".msa.embedding_layer.weight", {(size_t)h, (size_t)(3 * h)});
+      const std::vector<float> bq = f.take(t + ".msa.embedding_layer.bias", {(size_t)(3 * h)});
+      upload(b.ln1g, g1);
+      upload(b.ln1b, be1);
+      pack_weights(b.qkv, wq.values, 1, h, 3 * h, bq.data());
+      if (lnrows_fits(h, 3 * h)) pack_lnrows(b.lnqkv, h, 3 * h, wq.values, bq, g1, be1);
+    }
     upload(b.bias, attention_bias_layout(bias_tables(f.take(t + ".msa.position_bias", {(size_t)(h / 32), 64, 64}), shifted)));
     linear(f, b.proj, t + ".msa.linear", h, h, true);
     {
@@ -360,11 +370,15 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       // Attention (swin.rs:124-220) on y[h:]: LN1 + window partition, qkv,
       // attention, projection added back at the tokens' pixels.
       const WindowMap wm{8, H, W, H, W, shift};
-      layer_norm_planar(y, pl, h / 8, Pl, h, B.ln1g.as<float>(), B.ln1b.as<float>(), tok, pl, &wm, s);
-      o.mode = OUT_STORE;
-      o.out = qkv;
-      o.plane0 = 0;
-      gemm_rows(dev_, B.qkv, tok, pl, Pl, ACT_NONE, o, s);
+      if (fused_mlp_ && B.lnqkv.c == h) {
+        lnrows_planar(dev_, B.lnqkv, y + (long long)(h / 8) * pl, pl, Pl, wm, qkv, pl, s);
+      } else {
+        layer_norm_planar(y, pl, h / 8, Pl, h, B.ln1g.as<float>(), B.ln1b.as<float>(), tok, pl, &wm, s);
+        o.mode = OUT_STORE;
+        o.out = qkv;
+        o.plane0 = 0;
+        gemm_rows(dev_, B.qkv, tok, pl, Pl, ACT_NONE, o, s);
+      }
       window_attention(qkv, pl, h, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, att, pl, dev_.dev_err(), s);
       o.mode = OUT_WINDOW_ACCUM;
       o.out = y;

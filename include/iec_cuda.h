@@ -221,11 +221,13 @@ iec_status iec_scunet_run_device(iec_scunet* model, const float* image, size_t w
 iec_status iec_scunet_run_batch(iec_scunet* model, const float* images, size_t count, size_t width,
                                 size_t height, float* out, void* stream);
 
-/* Each transformer block's MLP runs fused (the default, `on` = 1: LayerNorm,
- * fc1, GELU and fc2 in one kernel, the hidden layer kept in shared memory)
- * or, with `on` = 0, as a LayerNorm launch and two GEMM launches through a
- * device buffer (for comparisons; no counterpart in the reference). The two
- * agree to f16 rounding (the LayerNorm sums run in another order). */
+/* Each transformer block runs its LayerNorms fused (the default, `on` = 1:
+ * LN1 and the window partition folded into the qkv product's staged rows;
+ * LN2, fc1, GELU and fc2 in one kernel with the hidden layer kept in shared
+ * memory, for the widths those kernels take) or, with `on` = 0, as
+ * LayerNorm launches and GEMM launches through device buffers (for
+ * comparisons; no counterpart in the reference). The two agree to f16
+ * rounding (the LayerNorm sums run in another order). */
 iec_status iec_scunet_set_fused(iec_scunet* model, int on);
 
 /* -------------------------------------------------------------------- LaMa
@@ -302,10 +304,12 @@ iec_status iec_birefnet_run_device(iec_birefnet* model, const void* image, int i
 iec_status iec_birefnet_run_batch(iec_birefnet* model, const uint8_t* images, size_t count, size_t side,
                                   float* logits, void* stream);
 
-/* The backbone blocks' MLPs of widths 96 and 192 run fused (the default,
- * `on` = 1: norm2, fc1, GELU and fc2 in one kernel) or, with `on` = 0, as a
- * LayerNorm launch and two GEMM launches (for comparisons; no counterpart in
- * the reference). The two agree to f16 rounding. */
+/* The backbone blocks run their LayerNorms fused (the default, `on` = 1:
+ * norm1 and the window partition folded into the qkv product's staged rows
+ * at width 96; norm2, fc1, GELU and fc2 in one kernel at widths 96 and 192)
+ * or, with `on` = 0, as LayerNorm launches and GEMM launches (for
+ * comparisons; no counterpart in the reference). The two agree to f16
+ * rounding. */
 iec_status iec_birefnet_set_fused(iec_birefnet* model, int on);
 
 /* Launch timing (measurement hooks, no counterpart in the reference).
