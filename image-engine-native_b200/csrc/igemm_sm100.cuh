@@ -449,8 +449,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
       const int a = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
-      if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
-      tc_fence_after();
       const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
       const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
       // This thread's output row, and for A_TAPS its pixel.
@@ -489,6 +487,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         else
           dest = (long long)py * p.map_w + px;
       }
+      // The accumulating epilogues read the old values of their rows: fetch
+      // them towards L1 before waiting for the accumulator, so that their
+      // latency overlaps the tile's MMAs instead of following each TMEM load
+      // (a hint: nothing is held in registers; the rows are this launch's own).
+      if (p.ksplit == 1 && (p.out_mode == OUT_ACCUM || p.out_mode == OUT_WINDOW_ACCUM) && m >= 0) {
+#pragma unroll 1
+        for (int c = part * HALF; c < part * HALF + HALF && c < ACC_USED; c += 8) {
+          const int n = nt * BN + (c - cb);
+          if (n >= p.N) break;
+          prefetch_l1(p.out + (long long)(p.out_plane0 + n / 8) * p.out_plane_elems + dest * 8);
+        }
+      }
+      if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
+      tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * L::ACC_COLS);
       if (p.ksplit > 1) {
         // the slice's raw partial sums, f32
