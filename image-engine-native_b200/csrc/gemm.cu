@@ -91,7 +91,8 @@ void run_gemm(Device& dev, const PackedWeights& pw, const CUtensorMap& map, Gemm
   p.kslice = p.ksteps;
   p.ws = nullptr;
   p.ws_n = p.tiles_n * pw.bn;
-  const bool splittable = p.out_mode == OUT_STORE || p.out_mode == OUT_ACCUM || p.out_mode == OUT_MAP;
+  const bool splittable =
+      AMODE != A_HALO && (p.out_mode == OUT_STORE || p.out_mode == OUT_ACCUM || p.out_mode == OUT_MAP);
   if (splittable && p.tiles_mn * 2 <= dev.sms() && p.ksteps >= 32) {
     const int want = std::min(dev.sms() / p.tiles_mn, p.ksteps / 16);  // one wave of tiles
     if (want >= 2) {
@@ -213,6 +214,29 @@ void pack_weights(PackedWeights& pw, const std::vector<float>& w, int taps, int 
           }
   pw.w.reserve(packed.size() * 2);
   IEC_CUDA(cudaMemcpy(pw.w.get(), packed.data(), packed.size() * 2, cudaMemcpyHostToDevice));
+  // The row-tap packing of an s x s grid (taps in row-major order).
+  int side = 0;
+  for (int c = 3; c <= 7; c += 2)
+    if (c * c == taps) side = c;
+  if (side && side * pw.bn <= 256 && k % pw.kb == 0) {
+    const int chunks = k / pw.kb, np = side * pw.bn;
+    std::vector<uint16_t> rt((size_t)pw.n_tiles * side * chunks * kg * np * 8, 0);
+    for (int nt = 0; nt < pw.n_tiles; nt++)
+      for (int ky = 0; ky < side; ky++)
+        for (int kb = 0; kb < chunks; kb++)
+          for (int g = 0; g < kg; g++)
+            for (int dx = 0; dx < side; dx++)
+              for (int j = 0; j < pw.bn; j++) {
+                const int nn = nt * pw.bn + j;
+                if (nn >= n) continue;
+                const size_t at = (((((size_t)nt * side + ky) * chunks + kb) * kg + g) * np + dx * pw.bn + j) * 8;
+                const size_t kk = (size_t)(ky * side + dx) * k + kb * pw.kb + g * 8;
+                for (int e = 0; e < 8; e++) rt[at + e] = f32_to_half(w[(kk + e) * n + nn]);
+              }
+    pw.rt.reserve(rt.size() * 2);
+    IEC_CUDA(cudaMemcpy(pw.rt.get(), rt.data(), rt.size() * 2, cudaMemcpyHostToDevice));
+    pw.rt_kw = side;
+  }
   pw.has_bias = bias != nullptr;
   if (bias) {
     pw.bias.reserve((size_t)n * 4);
@@ -430,13 +454,95 @@ void gemm_conv3(Device& dev, const PackedWeights& pw, const __half* map_ptr, lon
   gemm_taps(dev, pw, src, taps, h, w, act, out, s);
 }
 
+namespace {
+
+// The taps as a kh x kw grid from (dy0, dx0), row-major, over phase 0; or false.
+bool tap_grid(const std::vector<Tap>& taps, int& kh, int& kw, int& dy0, int& dx0) {
+  if (taps.empty()) return false;
+  dy0 = taps[0].dy;
+  dx0 = taps[0].dx;
+  kw = 0;
+  while (kw < (int)taps.size() && taps[kw].dy == dy0) kw++;
+  kh = (int)taps.size() / kw;
+  if (kh * kw != (int)taps.size()) return false;
+  for (int t = 0; t < (int)taps.size(); t++)
+    if (taps[t].dy != dy0 + t / kw || taps[t].dx != dx0 + t % kw || taps[t].phase != 0) return false;
+  return true;
+}
+
+}  // namespace
+
 void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const std::vector<Tap>& taps, int h, int w,
-               int act, const GemmOutSpec& out, cudaStream_t s) {
+               int act, const GemmOutSpec& out, cudaStream_t s, int halo) {
   if (pw.taps != (int)taps.size() || taps.size() > (size_t)GEMM_MAX_TAPS)
     throw Error(ERR_INPUT, "tap table does not match the weights");
   if (w < 1 || h < 1) throw Error(ERR_INPUT, "empty convolution output");
   if (out.mode == OUT_MAP && (out.dst_w != w * out.ostep || out.dst_h != h * out.ostep))
     throw Error(ERR_INPUT, "convolution output does not match the output map");
+  // Halo tiles (A_HALO): a full kh x kw grid of taps over a single-phase
+  // source at least 32 pixels wide, with the row-tap packing; tiles of
+  // 4 msub rows x (33 - kw) outputs, each channel chunk's halo box loaded
+  // once and read by one MMA of N = kw bn per kernel row. Taken when the
+  // tiles fill at least half the GPU (fewer tiles keep the tap boxes and
+  // split-K) and two halo boxes and two weight stages fit the ring; `halo`
+  // 0 never, 1 whenever it fits.
+  int kh = 0, kw = 0, dy0 = 0, dx0 = 0;
+  if (halo != 0 && pw.rt_kw > 0 && src.phases == 1 && src.w >= 32 && out.mode != OUT_WINDOW_ACCUM &&
+      tap_grid(taps, kh, kw, dy0, dx0) && kw == pw.rt_kw && kh == pw.rt_kw &&
+      ((kw == 3 && pw.bn <= 64) || ((kw == 5 || kw == 7) && pw.bn <= 32))) {
+    const int np = kw * pw.bn, msub = halo_msub(pw.bn, kw);
+    const int th = 4 * msub, tv = 33 - kw, kg = pw.kb / 8;
+    const int tiles_w = (w + tv - 1) / tv, tiles_h = (h + th - 1) / th;
+    const int halo_rows = th + kh - 1;
+    const int stride = (kg * halo_rows * 32 * 16 + 1023) / 1024 * 1024;
+    const int b_stage = kg * np * 16;
+    const int b_stages = std::min(8, (200 * 1024 - 2 * stride) / b_stage);
+    const long long tiles = (long long)tiles_w * tiles_h * pw.n_tiles;
+    if (src.h >= halo_rows && b_stages >= 2 && (halo == 1 || tiles * 2 >= dev.sms()) && tiles < (1 << 24)) {
+      CUtensorMap map;
+      const uint64_t dims[5] = {(uint64_t)src.w * 8, (uint64_t)src.h, 1, (uint64_t)pw.k / 8, 1};
+      const uint64_t strides[4] = {(uint64_t)src.w * 16, (uint64_t)src.w * src.h * 16, (uint64_t)src.plane_elems * 2,
+                                   (uint64_t)src.plane_elems * 2 * (pw.k / 8)};
+      const uint32_t box[5] = {32 * 8, (uint32_t)halo_rows, 1, (uint32_t)kg, 1};
+      encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, src.ptr, dims, strides, box);
+      GemmParams p{};
+      p.taps = (int)taps.size();
+      p.phase_y = out.phase_y;
+      p.phase_x = out.phase_x;
+      p.M = h * w;
+      p.N = pw.n;
+      p.K = pw.k;
+      p.H = h;
+      p.W = w;
+      p.TW = 32;
+      p.tiles_w = tiles_w;
+      p.tiles_m = tiles_w * tiles_h;
+      p.tiles_n = pw.n_tiles;
+      p.tiles = (int)tiles;
+      p.div_tiles_n = FastDiv((uint32_t)p.tiles_n);
+      p.div_tiles_w = FastDiv((uint32_t)p.tiles_w);
+      p.ksteps = pw.ksteps;
+      p.b = pw.rt.as<uint16_t>();
+      p.bias = pw.has_bias ? pw.bias.as<float>() : nullptr;
+      p.act = act;
+      fill_out(p, out);
+      p.dev_err = dev.dev_err();
+      p.halo_kh = kh;
+      p.halo_kw = kw;
+      p.halo_dy0 = dy0;
+      p.halo_dx0 = dx0;
+      p.halo_rows = halo_rows;
+      p.halo_tv = tv;
+      p.halo_stride = stride;
+      p.halo_msub = msub;
+      p.halo_np = np;
+      p.b_stage = b_stage;
+      p.b_off = 2 * stride;
+      p.b_stages = b_stages;
+      run_gemm<A_HALO>(dev, pw, map, p, s);
+      return;
+    }
+  }
   // Tiles of 8 rows x 16 (or, for narrow outputs, 8) columns; boxes that
   // reach past the source read TMA's zero fill.
   const int tw = w > 8 ? 16 : 8;

@@ -19,6 +19,11 @@ struct PackedWeights {
   int n = 0, k = 0, ktot = 0, taps = 1, bn = 0, kb = 0, n_tiles = 0, ksteps = 0;
   DeviceBuffer w, bias;
   bool has_bias = false;
+  // For an s x s grid of taps (s = 3, 5, 7; s bn <= 256), the same weights
+  // packed per kernel row for halo tiles: [n tile][ky][k chunk][kb / 8]
+  // [s bn][8], column dx bn + j of row ky holding tap (ky, dx)'s output j.
+  DeviceBuffer rt;
+  int rt_kw = 0;
 };
 
 // `w` is ktot x n row-major (ktot = taps * k), `bias` n floats or null.
@@ -74,8 +79,11 @@ GemmOutSpec map_out(const MapGeom& g, __half* out, int plane0 = 0);
 
 // out (h x w pixels) = act(sum over taps and channels + bias), the taps'
 // weights row-major in tap order (pw packed with taps = taps.size()).
+// `halo`: -1 chooses (halo tiles where they fit and fill the GPU), 0 never
+// takes them (one box per tap), 1 takes them wherever they fit. Halo tiles
+// need the row-tap packing (PackedWeights::rt) and a full grid of taps.
 void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const std::vector<Tap>& taps, int h, int w,
-               int act, const GemmOutSpec& out, cudaStream_t s);
+               int act, const GemmOutSpec& out, cudaStream_t s, int halo = -1);
 
 // out = act(A x W + bias) over `m` rows of the planar input `a` (k / 8
 // planes of a_plane_elems / 8 >= gemm_rows_alloc(m) rows each; the rows past

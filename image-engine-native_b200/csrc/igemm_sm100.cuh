@@ -61,7 +61,7 @@
 
 namespace iec {
 
-enum GemmA { A_ROWS = 0, A_TAPS = 1 };
+enum GemmA { A_ROWS = 0, A_TAPS = 1, A_HALO = 2 };
 enum GemmOut { OUT_STORE = 0, OUT_ACCUM = 1, OUT_WINDOW_ACCUM = 2, OUT_DOUBLE = 3, OUT_PHASE = 4, OUT_MAP = 5 };
 enum GemmAct { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU = 2, ACT_SIGMOID = 3 };
 
@@ -100,6 +100,16 @@ struct GemmParams {
   // to ws[slice][row][ws_n], summed by gemm_splitk_reduce.
   int ksplit, kslice, tiles_mn, ws_n;
   float* ws;
+  // A_HALO: a kh x kw grid of taps from (dy0, dx0); tiles of 4 halo_msub
+  // rows x halo_tv (33 - kw) outputs; each channel chunk's halo box
+  // (halo_rows x 32 pixels) in one of two buffers halo_stride bytes apart.
+  // The weights are packed per kernel row (ky) and chunk with the kw taps of
+  // the row side by side in N (halo_np = kw BN columns, b_stage bytes), in a
+  // ring of b_stages stages from byte b_off: one MMA per kernel row gives
+  // each position's products with all kw taps, and the epilogue adds the
+  // products of tap dx found dx positions to the right.
+  int halo_kh, halo_kw, halo_dy0, halo_dx0, halo_rows, halo_tv, halo_stride, b_off, b_stages;
+  int halo_msub, halo_np, b_stage;
   int* dev_err;
 };
 
@@ -132,9 +142,11 @@ struct GemmSmem {
   static constexpr int A_BYTES = MSUB * A_ONE;
   static constexpr int B_BYTES = (KB / 8) * BN * 16;
   static constexpr int STAGE = ((A_BYTES + B_BYTES) + 1023) / 1024 * 1024;
-  static constexpr int NSTAGE = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
-  static constexpr int BAR_OFF = NSTAGE * STAGE;
-  static constexpr int NBARS = 2 * NSTAGE + 4;
+  static constexpr int RING = 200 * 1024;  // the stages (or, for A_HALO, two halo boxes and a weight ring)
+  static constexpr int NSTAGE = RING / STAGE > 8 ? 8 : RING / STAGE;
+  static constexpr int NSLOT = 8;  // full / empty barrier pairs (A_HALO's weight ring may use all)
+  static constexpr int BAR_OFF = RING;
+  static constexpr int NBARS = 2 * NSLOT + 4 + 4;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   // The bias, staged once per CTA for the epilogue (when N fits).
   static constexpr int BIAS_FLOATS = 4096;
@@ -237,7 +249,33 @@ __device__ __forceinline__ float gemm_act(float v, int act) {
 // [c_begin, c_end) of its tile (output column = that - cb + the N tile's): in batches of 32 columns (two TMEM loads), the old values of the
 // batch's four 8-column groups are loaded together ahead of the
 // accumulators, so that their latencies overlap.
-template <int BN>
+// 16 accumulator columns from output column c0 (a multiple of 16) for the
+// warp's 32 rows. A_HALO: the sum over the kernel row's kw taps of the
+// products of tap dx held by the position dx to the right (lane + dx), which
+// is this row's output; lanes past the last output read their own values.
+template <int BN, int AMODE>
+__device__ __forceinline__ void acc_ld16(const GemmParams& p, uint32_t taddr, int c0, uint32_t* r) {
+  if constexpr (AMODE == A_HALO) {
+    const int sb = c0 / BN, c = c0 - sb * BN;
+    const uint32_t base = taddr + (uint32_t)(sb * p.halo_np + c);
+    tmem_ld16(base, r);
+    tmem_wait_ld();
+#pragma unroll 1
+    for (int dx = 1; dx < p.halo_kw; dx++) {
+      uint32_t t[16];
+      tmem_ld16(base + (uint32_t)(dx * BN), t);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; e++)
+        r[e] = __float_as_uint(__uint_as_float(r[e]) + __shfl_down_sync(0xffffffffu, __uint_as_float(t[e]), dx));
+    }
+  } else {
+    tmem_ld16(taddr + (uint32_t)c0, r);
+    tmem_wait_ld();
+  }
+}
+
+template <int BN, int AMODE>
 __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* bias, uint32_t taddr, int c_begin,
                                              int c_end, int cb, int nt, int m, const int* ry, const int* rx, int nry,
                                              int nrx) {
@@ -259,9 +297,13 @@ __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* b
       }
     }
     uint32_t r[32];
-    tmem_ld16(taddr + (uint32_t)c0, r);
-    if (two) tmem_ld16(taddr + (uint32_t)c0 + 16, r + 16);
-    tmem_wait_ld();
+    if constexpr (AMODE == A_HALO) {
+      acc_ld16<BN, AMODE>(p, taddr, c0, r);  // 16 columns per part: `two` is false
+    } else {
+      tmem_ld16(taddr + (uint32_t)c0, r);
+      if (two) tmem_ld16(taddr + (uint32_t)c0 + 16, r + 16);
+      tmem_wait_ld();
+    }
     if (!live) continue;
 #pragma unroll
     for (int q = 0; q < 4; q++) {
@@ -287,6 +329,76 @@ __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* b
   }
 }
 
+// M blocks per A_HALO tile for kernel width kw: as many as two accumulators
+// of kw BN columns each leave room for in 512 TMEM columns (at most MSUB).
+__host__ __device__ constexpr int halo_msub(int bn, int kw) {
+  return gemm_msub(bn) < 256 / (kw * bn) ? gemm_msub(bn) : 256 / (kw * bn);
+}
+
+// The A_HALO MMA issuer for kernels of KW x KW taps. Kernel row ky of M
+// block sb reads the halo box from row 4 sb + ky: its 128 MMA rows are the
+// 4 x 32 positions of box rows 4 sb + ky .. 4 sb + ky + 3, its N = KW BN
+// columns the row's KW taps; the accumulator of M block sb starts at column
+// sb KW BN. Every MMA of a channel chunk is unrolled, with its descriptors
+// a stage's base plus constant offsets: a loop or branch between MMAs costs
+// the single issuing thread about as much as an MMA.
+template <int BN, int KB, int KW>
+__device__ __forceinline__ void halo_mma_issuer(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                                uint64_t* acc_full, uint64_t* acc_empty, uint64_t* halo_full,
+                                                uint64_t* halo_empty, uint32_t tmem_base, volatile int* abort_flag) {
+  constexpr int NP = KW * BN, MS = halo_msub(BN, KW), ROWS = 4 * MS + KW - 1;
+  constexpr uint32_t LBO_A = ROWS * 32 * 16, LBO_B = NP * 16;
+  constexpr uint32_t IDESC = idesc_f16_f32(128, NP);
+  const int chunks = p.K / KB, stages = p.b_stages;
+  int hb = 0, s = 0, i = 0, last_acc = -1;
+  uint32_t hph = 0, phase = 0, last_parity = 0;
+  bool ok = true;
+  for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
+    const int a = i & 1;
+    const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
+    if (!mbar_wait(&acc_empty[a], acc_phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_EMPTY)) break;
+    tc_fence_after();
+    const uint32_t d = tmem_base + (uint32_t)(a * 256);
+    for (int kb = 0; kb < chunks && ok; kb++) {
+      if (!mbar_wait(&halo_full[hb], hph, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t a0 = smem_desc(smem_u32(smem + hb * p.halo_stride), LBO_A, 128);
+      const uint32_t more = kb != 0 ? 1u : 0u;
+#pragma unroll
+      for (int ky = 0; ky < KW; ky++) {
+        if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t b0 = smem_desc(smem_u32(smem + p.b_off + s * p.b_stage), LBO_B, 128);
+#pragma unroll
+        for (int j = 0; j < KB / 16; j++)
+#pragma unroll
+          for (int sb = 0; sb < MS; sb++)
+            umma_f16(d + (uint32_t)(sb * NP), a0 + (uint64_t)((2 * j * LBO_A + (4 * sb + ky) * 512) >> 4),
+                     b0 + (uint64_t)((2 * j * LBO_B) >> 4), IDESC, (ky != 0 || j != 0) ? 1u : more);
+        umma_commit(&empty[s]);
+        const bool wrap = s + 1 == stages;
+        s = wrap ? 0 : s + 1;
+        phase ^= wrap ? 1u : 0u;
+      }
+      if (!ok) break;
+      umma_commit(&halo_empty[hb]);
+      hph ^= (uint32_t)hb;
+      hb ^= 1;
+    }
+    if (!ok) break;
+    umma_commit(&acc_full[a]);
+    last_acc = a;
+    last_parity = acc_phase;
+  }
+  if (last_acc >= 0) mbar_wait(&acc_full[last_acc], last_parity, abort_flag, p.dev_err, 0);
+}
+
 template <int BN, int KB, int AMODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     igemm_sm100(const __grid_constant__ CUtensorMap a_map, const GemmParams p) {
@@ -297,31 +409,38 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* full = bars;
-  uint64_t* empty = bars + L::NSTAGE;
-  uint64_t* acc_full = bars + 2 * L::NSTAGE;
+  uint64_t* empty = bars + L::NSLOT;
+  uint64_t* acc_full = bars + 2 * L::NSLOT;
   uint64_t* acc_empty = acc_full + 2;
+  uint64_t* halo_full = acc_empty + 2;  // A_HALO: the two halo buffers
+  uint64_t* halo_empty = halo_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // A tile: rows of the box, and the A-side bytes one TMA load delivers.
   const int a_rows = AMODE == A_ROWS ? 128 : 8 * p.TW;
-  const uint32_t a_bytes = (uint32_t)(KG * a_rows * 16);
+  const uint32_t a_bytes = AMODE == A_HALO ? (uint32_t)(KG * p.halo_rows * 32 * 16) : (uint32_t)(KG * a_rows * 16);
+  // TMEM: two accumulators; A_HALO's hold up to 256 columns each.
+  constexpr int ACC = AMODE == A_HALO ? 256 : L::ACC_COLS;
+  constexpr int TMEM_COLS = AMODE == A_HALO ? 512 : L::TMEM_COLS;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < L::NSTAGE; s++) {
+    for (int s = 0; s < L::NSLOT; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], GEMM_EPI_WARPS);
+      mbar_init(&halo_full[a], 1);
+      mbar_init(&halo_empty[a], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -339,6 +458,53 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       // ------------------------------------------------------------ producer
       prefetch_tensor_map(&a_map);
+      if constexpr (AMODE == A_HALO) {
+        // per tile and channel chunk: one halo box, then the weights of each
+        // kernel row (block (nt kh + ky) chunks + chunk) through the ring
+        const int chunks = p.K / KB;
+        int hb = 0, s = 0, n_halo = 0, n_b = 0;
+        uint32_t hph = 0, phase = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+          const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
+          const int ty = (int)p.div_tiles_w.div((uint32_t)mt), tx = mt - ty * p.tiles_w;
+          const int x0 = tx * p.halo_tv, y0 = ty * 4 * p.halo_msub;
+          const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.halo_kh * chunks * p.b_stage;
+          for (int kb = 0; kb < chunks && ok; kb++) {
+            if (!mbar_wait(&halo_empty[hb], hph ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&halo_full[hb], a_bytes);
+            tma_load_5d(smem + hb * p.halo_stride, &a_map, &halo_full[hb], (x0 + p.halo_dx0) * 8, y0 + p.halo_dy0, 0,
+                        kb * KG, 0);
+            n_halo++;
+            if (++hb == 2) {
+              hb = 0;
+              hph ^= 1;
+            }
+            for (int ky = 0; ky < p.halo_kh; ky++) {
+              if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
+                ok = false;
+                break;
+              }
+              uint8_t* st = smem + p.b_off + s * p.b_stage;
+              mbar_arrive_expect_tx(&full[s], (uint32_t)p.b_stage);
+              bulk_load(st, bsrc + (size_t)(ky * chunks + kb) * p.b_stage, (uint32_t)p.b_stage, &full[s]);
+              n_b++;
+              if (++s == p.b_stages) {
+                s = 0;
+                phase ^= 1;
+              }
+            }
+          }
+        }
+        // the copies in flight land before the CTA may leave
+        for (int c = n_halo - 2; c < n_halo; c++)
+          if (c >= 0) mbar_wait(&halo_full[c & 1], (uint32_t)(c >> 1) & 1, abort_flag, p.dev_err, 0);
+        for (int c = n_b - p.b_stages; c < n_b; c++)
+          if (c >= 0) mbar_wait(&full[c % p.b_stages], (uint32_t)(c / p.b_stages) & 1, abort_flag, p.dev_err, 0);
+      } else {
       int s = 0;
       uint32_t phase = 0;
       int issued[L::NSTAGE];
@@ -380,11 +546,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       for (int i = 0; i < L::NSTAGE; i++)
         if (issued[i] >= 0) mbar_wait(&full[i], (uint32_t)issued[i], abort_flag, p.dev_err, 0);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      if constexpr (AMODE == A_HALO) {
+        // (the launch checks kw: 3 for bn <= 64, 5 and 7 for bn 32)
+        if constexpr (BN <= 64) {
+          if (p.halo_kw == 3)
+            halo_mma_issuer<BN, KB, 3>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base,
+                                       abort_flag);
+        }
+        if constexpr (BN <= 32) {
+          if (p.halo_kw == 5)
+            halo_mma_issuer<BN, KB, 5>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base,
+                                       abort_flag);
+          else if (p.halo_kw == 7)
+            halo_mma_issuer<BN, KB, 7>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base,
+                                       abort_flag);
+        }
+      } else {
       const uint32_t lbo_a = (uint32_t)(a_rows * 16);
       int s = 0, i = 0, last_acc = -1;
       uint32_t phase = 0, last_parity = 0;
@@ -424,6 +607,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         last_parity = acc_phase;
       }
       if (last_acc >= 0) mbar_wait(&acc_full[last_acc], last_parity, abort_flag, p.dev_err, 0);
+      }
     }
   } else {
     // ------------------------------------------------------------- epilogue
@@ -432,8 +616,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int row = quarter * 32 + lane;
     // columns per part (a multiple of 16); with several M blocks a part's
     // columns lie in one block's accumulator
-    constexpr int HALF = (L::MSUB * BN + 63) / 64 * 16;
-    constexpr int ACC_USED = L::MSUB * BN;
+    // (A_HALO: 16 columns per part, of halo_msub M blocks)
+    const int HALF = AMODE == A_HALO ? 16 : (L::MSUB * BN + 63) / 64 * 16;
+    const int ACC_USED = AMODE == A_HALO ? p.halo_msub * BN : L::MSUB * BN;
     const int sb = (part * HALF) / BN;  // this part's M block within the tile
     const int cb = sb * BN;             // its first accumulator column
     // Stage the bias in shared memory: the epilogue then reads it at shared
@@ -457,6 +642,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (AMODE == A_ROWS) {
         m = blk * 128 + row;
         if (m >= p.M) m = -1;
+      } else if (AMODE == A_HALO) {
+        // M block sb: tile rows 4 sb .. 4 sb + 3 (one per lane quarter),
+        // positions 0 .. 31 (one per lane), of which halo_tv are outputs
+        const int ty = (int)p.div_tiles_w.div((uint32_t)mt), tx = mt - ty * p.tiles_w;
+        oy = ty * 4 * p.halo_msub + 4 * sb + quarter;
+        ox = tx * p.halo_tv + lane;
+        if (lane < p.halo_tv && oy < p.H && ox < p.W) m = oy * p.W + ox;
       } else {
         const int ty = (int)p.div_tiles_w.div((uint32_t)blk);
         const int x0 = (blk - ty * p.tiles_w) * p.TW, y0 = ty * 8;
@@ -501,7 +693,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       if (!mbar_wait(&acc_full[a], acc_phase, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * L::ACC_COLS);
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * ACC);
       if (p.ksplit > 1) {
         // the slice's raw partial sums, f32
 #pragma unroll 1
@@ -517,13 +709,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                __uint_as_float(r[4 * q + 3]));
         }
       } else if (p.out_mode == OUT_MAP)
-        map_epilogue<BN>(p, bias, taddr, part * HALF, min(part * HALF + HALF, ACC_USED), cb, nt, m, ry, rx, nry, nrx);
+        map_epilogue<BN, AMODE>(p, bias, taddr, part * HALF, min(part * HALF + HALF, ACC_USED), cb, nt, m, ry, rx, nry, nrx);
 #pragma unroll 1
       for (int c0 = part * HALF; p.ksplit == 1 && p.out_mode != OUT_MAP && c0 < part * HALF + HALF && c0 < ACC_USED;
            c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(taddr + (uint32_t)c0, r);
-        tmem_wait_ld();
+        acc_ld16<BN, AMODE>(p, taddr, c0, r);
         const int n0 = nt * BN + (c0 - cb);
         if (m < 0 || n0 >= p.N) continue;
         float v[16];
@@ -604,7 +795,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::TMEM_COLS);
+    tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

@@ -64,6 +64,61 @@ extern "C" iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int
   }
 }
 
+extern "C" iec_status iec_selftest_conv(int device, int h, int w, int k, int n, int size, int halo, const float* a,
+                                        const float* weights, const float* bias, int act, float* out, int iters,
+                                        float* us) {
+  try {
+    if (h < 1 || w < 1 || size < 1 || size > 7 || k % 8 != 0 || n < 1) throw Error(ERR_INPUT, "bad convolution");
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    const int rows = h * w, taps = size * size;
+    std::vector<float> wv(weights, weights + (size_t)taps * k * n);
+    PackedWeights pw;
+    pack_weights(pw, wv, taps, k, n, bias);
+    std::vector<Tap> tt;
+    for (int t = 0; t < taps; t++) tt.push_back(Tap{t / size - size / 2, t % size - size / 2, 0});
+    const long long plane = (long long)gemm_rows_alloc(rows) * 8;
+    const int out_groups = (n + 7) / 8;
+    DeviceBuffer d_a32, d_a16, d_o32, d_o16;
+    d_a32.reserve((size_t)rows * k * 4);
+    d_a16.reserve((size_t)plane * (k / 8) * 2);
+    d_o32.reserve((size_t)rows * out_groups * 8 * 4);
+    d_o16.reserve((size_t)plane * out_groups * 2);
+    cudaStream_t s = dev.stream();
+    IEC_CUDA(cudaMemcpyAsync(d_a32.get(), a, (size_t)rows * k * 4, cudaMemcpyHostToDevice, s));
+    rows_to_planar(d_a32.as<float>(), rows, k, d_a16.as<__half>(), plane, s);
+    GemmOutSpec o;
+    o.mode = OUT_STORE;
+    o.out = d_o16.as<__half>();
+    o.plane_elems = plane;
+    const TapSource src{d_a16.as<__half>(), plane, w, h, 1};
+    gemm_taps(dev, pw, src, tt, h, w, act, o, s, halo);
+    planar_to_rows(d_o16.as<__half>(), plane, rows, out_groups * 8, d_o32.as<float>(), s);
+    IEC_CUDA(cudaMemcpy2DAsync(out, (size_t)n * 4, d_o32.get(), (size_t)out_groups * 8 * 4, (size_t)n * 4, rows,
+                               cudaMemcpyDeviceToHost, s));
+    if (iters > 0 && us) {
+      cudaEvent_t e0, e1;
+      IEC_CUDA(cudaEventCreate(&e0));
+      IEC_CUDA(cudaEventCreate(&e1));
+      IEC_CUDA(cudaEventRecord(e0, s));
+      for (int i = 0; i < iters; i++) gemm_taps(dev, pw, src, tt, h, w, act, o, s, halo);
+      IEC_CUDA(cudaEventRecord(e1, s));
+      dev.sync(s);
+      float ms = 0.0f;
+      IEC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+      us[0] = ms * 1000.0f / (float)iters;
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+    }
+    dev.sync(s);
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
 extern "C" iec_status iec_selftest_attention(int device, const float* qkv, int windows, int c, const float* bias,
                                              int shifted, int rows_w, int cols_w, float* out) {
   try {

@@ -93,6 +93,7 @@ def lib():
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
+        L.iec_selftest_conv.argtypes = [i32, i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, f32p, i32, f32p]
         L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          f32p, f32p]
         L.iec_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int]
@@ -294,6 +295,24 @@ def selftest_gemm(a, w, bias=None, *, conv=False, shape=None, act=0, accumulate_
                                  _f32(b) if b is not None else None, act, int(accumulate_onto is not None), _f32(out))
     _check(st)
     return out
+
+
+def selftest_conv(a, w, bias=None, *, size=3, halo=-1, act=0, iters=0, device=0):
+    """Diagnostics: a size x size convolution with zero padding through the
+    general GEMM: `a` h x w x k, `w` (size^2 k) x n tap-major. halo -1 lets
+    the GEMM choose its A operand, 0 one box per tap, 1 halo tiles wherever
+    they fit. Returns (h w x n float32, microseconds per launch or None)."""
+    a = np.ascontiguousarray(a, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    h, wd, k = a.shape
+    n = w.shape[1]
+    out = np.zeros((h * wd, n), np.float32)
+    us = np.zeros(1, np.float32)
+    b = np.ascontiguousarray(bias, np.float32) if bias is not None else None
+    _check(lib().iec_selftest_conv(device, h, wd, k, n, size, halo, _f32(a), _f32(w),
+                                   _f32(b) if b is not None else None, act, _f32(out), iters,
+                                   _f32(us) if iters > 0 else None))
+    return out, (float(us[0]) if iters > 0 else None)
 
 
 def selftest_attention(qkv, windows, c, bias, shifted, rows_w, cols_w, device=0):

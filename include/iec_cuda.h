@@ -341,6 +341,15 @@ iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int w, int k, 
                              const float* a, const float* weights, const float* bias, int act,
                              int accumulate, float* out);
 
+/* Diagnostics: a size x size convolution (zero padding size / 2) through the
+ * general GEMM on host arrays: `a` h x w x k, `weights` size^2 k x n (tap-
+ * major), out h x w x n. halo -1 lets the GEMM choose its A operand, 0 takes
+ * one box per tap, 1 the halo tiles wherever they fit. With iters > 0 and
+ * `us` non-null, us[0] gets the device microseconds per launch over `iters`
+ * launches after the checked one. */
+iec_status iec_selftest_conv(int device, int h, int w, int k, int n, int size, int halo, const float* a,
+                             const float* weights, const float* bias, int act, float* out, int iters, float* us);
+
 /* Diagnostics: LaMa's planar Fourier transforms on host arrays: `x` h x w x c
  * floats (c a multiple of 8, rounded to f16 on the way in); `spec` gets
  * rfft2(x) as h x (w / 2 + 1) x 2c floats (real parts of the c channels, then

@@ -66,3 +66,27 @@ def test_conv3_matches_oracle(h, w, k, n, act):
     want = refcpu.multiply(img.ravel(), wt, bias, kind="conv", shape=(h, w, k), size=3, act=act).reshape(h * w, n)
     got = iec.selftest_gemm(img, wt, bias, conv=True, shape=(h, w), act=act)
     close(got, want)
+
+
+@pytest.mark.parametrize("h,w,k,n,size", [
+    (24, 40, 64, 32, 3), (30, 70, 64, 64, 3), (20, 45, 32, 128, 3), (40, 64, 64, 3, 7), (24, 33, 16, 32, 5),
+    (12, 50, 128, 96, 3), (9, 61, 256, 256, 3), (23, 97, 64, 3, 7), (40, 32, 64, 32, 1), (17, 100, 32, 48, 3),
+    (64, 64, 128, 64, 3), (33, 47, 16, 32, 3), (13, 64, 256, 32, 3),
+])
+def test_conv_halo_tiles_match_oracle(h, w, k, n, size):
+    """Square convolutions through halo tiles (one box per channel chunk, one
+    MMA per kernel row with the row's taps side by side in N, the taps'
+    products added across lanes in the epilogue) and through one box per
+    tap, both against the oracle; partial tiles on both axes."""
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(h * w * size + k + n)
+    img = f16(rng.standard_normal((h, w, k)))
+    taps = size * size
+    wt = f16(rng.standard_normal((taps * k, n)) / np.sqrt(taps * k))
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    want = refcpu.multiply(img.ravel(), wt, bias, kind="conv", shape=(h, w, k), size=size, act=1).reshape(h * w, n)
+    for halo in (1, 0):
+        got, _ = iec.selftest_conv(img, wt, bias, size=size, halo=halo, act=1)
+        close(got, want)
