@@ -494,11 +494,20 @@ void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const
     const int th = 4 * msub, tv = 33 - kw, kg = pw.kb / 8;
     const int tiles_w = (w + tv - 1) / tv, tiles_h = (h + th - 1) / th;
     const int halo_rows = th + kh - 1;
+    // Shared memory (200 KB): the weights resident when one n tile's fit
+    // beside two halo buffers, else a ring of up to 2 kh weight stages; the
+    // rest a ring of up to 8 halo buffers.
+    constexpr int RING = 200 * 1024;
     const int stride = (kg * halo_rows * 32 * 16 + 1023) / 1024 * 1024;
-    const int b_stage = kg * np * 16;
-    const int b_stages = std::min(8, (200 * 1024 - 2 * stride) / b_stage);
+    const int b_stage = kg * np * 16, chunks = pw.k / pw.kb;
+    const int b_all = kh * chunks * b_stage;
+    const bool resident = pw.n_tiles == 1 && b_all + 2 * stride <= RING;
+    const int b_stages = resident ? 1 : std::min({8, 2 * kh, (RING - 2 * stride) / b_stage});
+    const int b_bytes = resident ? b_all : b_stages * b_stage;
+    const int bufs = std::min(8, (RING - b_bytes) / stride);
     const long long tiles = (long long)tiles_w * tiles_h * pw.n_tiles;
-    if (src.h >= halo_rows && b_stages >= 2 && (halo == 1 || tiles * 2 >= dev.sms()) && tiles < (1 << 24)) {
+    if (src.h >= halo_rows && (resident || b_stages >= 2) && bufs >= 2 && (halo == 1 || tiles * 2 >= dev.sms()) &&
+        tiles < (1 << 24)) {
       CUtensorMap map;
       const uint64_t dims[5] = {(uint64_t)src.w * 8, (uint64_t)src.h, 1, (uint64_t)pw.k / 8, 1};
       const uint64_t strides[4] = {(uint64_t)src.w * 16, (uint64_t)src.w * src.h * 16, (uint64_t)src.plane_elems * 2,
@@ -537,7 +546,9 @@ void gemm_taps(Device& dev, const PackedWeights& pw, const TapSource& src, const
       p.halo_msub = msub;
       p.halo_np = np;
       p.b_stage = b_stage;
-      p.b_off = 2 * stride;
+      p.halo_bufs = bufs;
+      p.b_resident = resident ? 1 : 0;
+      p.b_off = bufs * stride;
       p.b_stages = b_stages;
       run_gemm<A_HALO>(dev, pw, map, p, s);
       return;

@@ -102,14 +102,15 @@ struct GemmParams {
   float* ws;
   // A_HALO: a kh x kw grid of taps from (dy0, dx0); tiles of 4 halo_msub
   // rows x halo_tv (33 - kw) outputs; each channel chunk's halo box
-  // (halo_rows x 32 pixels) in one of two buffers halo_stride bytes apart.
-  // The weights are packed per kernel row (ky) and chunk with the kw taps of
-  // the row side by side in N (halo_np = kw BN columns, b_stage bytes), in a
-  // ring of b_stages stages from byte b_off: one MMA per kernel row gives
-  // each position's products with all kw taps, and the epilogue adds the
-  // products of tap dx found dx positions to the right.
+  // (halo_rows x 32 pixels) in a ring of halo_bufs buffers halo_stride
+  // bytes apart. The weights are packed per kernel row (ky) and chunk with
+  // the kw taps of the row side by side in N (halo_np = kw BN columns,
+  // b_stage bytes per block) from byte b_off: resident (b_resident, all
+  // blocks loaded once) or through a ring of b_stages stages. One MMA per
+  // kernel row gives each position's products with all kw taps, and the
+  // epilogue adds the products of tap dx found dx positions to the right.
   int halo_kh, halo_kw, halo_dy0, halo_dx0, halo_rows, halo_tv, halo_stride, b_off, b_stages;
-  int halo_msub, halo_np, b_stage;
+  int halo_msub, halo_np, b_stage, halo_bufs, b_resident;
   int* dev_err;
 };
 
@@ -146,7 +147,7 @@ struct GemmSmem {
   static constexpr int NSTAGE = RING / STAGE > 8 ? 8 : RING / STAGE;
   static constexpr int NSLOT = 8;  // full / empty barrier pairs (A_HALO's weight ring may use all)
   static constexpr int BAR_OFF = RING;
-  static constexpr int NBARS = 2 * NSLOT + 4 + 4;
+  static constexpr int NBARS = 2 * NSLOT + 4 + 2 * NSLOT;  // + A_HALO's halo ring
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   // The bias, staged once per CTA for the epilogue (when N fits).
   static constexpr int BIAS_FLOATS = 4096;
@@ -258,16 +259,25 @@ __device__ __forceinline__ void acc_ld16(const GemmParams& p, uint32_t taddr, in
   if constexpr (AMODE == A_HALO) {
     const int sb = c0 / BN, c = c0 - sb * BN;
     const uint32_t base = taddr + (uint32_t)(sb * p.halo_np + c);
+    // the loads of two taps in flight together, one wait per pair
+    uint32_t t1[16], t2[16];
     tmem_ld16(base, r);
+    tmem_ld16(base + (uint32_t)BN, t1);
+    tmem_ld16(base + (uint32_t)(2 * BN), t2);
     tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; e++)
+      r[e] = __float_as_uint(__uint_as_float(r[e]) + __shfl_down_sync(0xffffffffu, __uint_as_float(t1[e]), 1) +
+                             __shfl_down_sync(0xffffffffu, __uint_as_float(t2[e]), 2));
 #pragma unroll 1
-    for (int dx = 1; dx < p.halo_kw; dx++) {
-      uint32_t t[16];
-      tmem_ld16(base + (uint32_t)(dx * BN), t);
+    for (int dx = 3; dx < p.halo_kw; dx += 2) {
+      tmem_ld16(base + (uint32_t)(dx * BN), t1);
+      tmem_ld16(base + (uint32_t)((dx + 1) * BN), t2);
       tmem_wait_ld();
 #pragma unroll
       for (int e = 0; e < 16; e++)
-        r[e] = __float_as_uint(__uint_as_float(r[e]) + __shfl_down_sync(0xffffffffu, __uint_as_float(t[e]), dx));
+        r[e] = __float_as_uint(__uint_as_float(r[e]) + __shfl_down_sync(0xffffffffu, __uint_as_float(t1[e]), dx) +
+                               __shfl_down_sync(0xffffffffu, __uint_as_float(t2[e]), dx + 1));
     }
   } else {
     tmem_ld16(taddr + (uint32_t)c0, r);
@@ -341,18 +351,24 @@ __host__ __device__ constexpr int halo_msub(int bn, int kw) {
 // columns the row's KW taps; the accumulator of M block sb starts at column
 // sb KW BN. Every MMA of a channel chunk is unrolled, with its descriptors
 // a stage's base plus constant offsets: a loop or branch between MMAs costs
-// the single issuing thread about as much as an MMA.
-template <int BN, int KB, int KW>
+// the single issuing thread about as much as an MMA. RES: the weights are
+// resident (all loaded once on full[0]), else they stream through the ring.
+template <int BN, int KB, int KW, bool RES>
 __device__ __forceinline__ void halo_mma_issuer(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                                 uint64_t* acc_full, uint64_t* acc_empty, uint64_t* halo_full,
                                                 uint64_t* halo_empty, uint32_t tmem_base, volatile int* abort_flag) {
   constexpr int NP = KW * BN, MS = halo_msub(BN, KW), ROWS = 4 * MS + KW - 1;
   constexpr uint32_t LBO_A = ROWS * 32 * 16, LBO_B = NP * 16;
   constexpr uint32_t IDESC = idesc_f16_f32(128, NP);
-  const int chunks = p.K / KB, stages = p.b_stages;
+  const int chunks = p.K / KB, stages = p.b_stages, nh = p.halo_bufs;
   int hb = 0, s = 0, i = 0, last_acc = -1;
   uint32_t hph = 0, phase = 0, last_parity = 0;
   bool ok = true;
+  if (RES) {
+    ok = mbar_wait(&full[0], 0, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL);
+    tc_fence_after();
+  }
+  const uint32_t bres = smem_u32(smem + p.b_off);
   for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
     const int a = i & 1;
     const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
@@ -369,27 +385,35 @@ __device__ __forceinline__ void halo_mma_issuer(const GemmParams& p, uint8_t* sm
       const uint32_t more = kb != 0 ? 1u : 0u;
 #pragma unroll
       for (int ky = 0; ky < KW; ky++) {
-        if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
-          ok = false;
-          break;
+        uint64_t b0;
+        if (RES) {
+          b0 = smem_desc(bres + (uint32_t)((ky * chunks + kb) * p.b_stage), LBO_B, 128);
+        } else {
+          if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          b0 = smem_desc(smem_u32(smem + p.b_off + s * p.b_stage), LBO_B, 128);
         }
-        tc_fence_after();
-        const uint64_t b0 = smem_desc(smem_u32(smem + p.b_off + s * p.b_stage), LBO_B, 128);
 #pragma unroll
         for (int j = 0; j < KB / 16; j++)
 #pragma unroll
           for (int sb = 0; sb < MS; sb++)
             umma_f16(d + (uint32_t)(sb * NP), a0 + (uint64_t)((2 * j * LBO_A + (4 * sb + ky) * 512) >> 4),
                      b0 + (uint64_t)((2 * j * LBO_B) >> 4), IDESC, (ky != 0 || j != 0) ? 1u : more);
-        umma_commit(&empty[s]);
-        const bool wrap = s + 1 == stages;
-        s = wrap ? 0 : s + 1;
-        phase ^= wrap ? 1u : 0u;
+        if (!RES) {
+          umma_commit(&empty[s]);
+          const bool wrap = s + 1 == stages;
+          s = wrap ? 0 : s + 1;
+          phase ^= wrap ? 1u : 0u;
+        }
       }
       if (!ok) break;
       umma_commit(&halo_empty[hb]);
-      hph ^= (uint32_t)hb;
-      hb ^= 1;
+      const bool hwrap = hb + 1 == nh;
+      hb = hwrap ? 0 : hb + 1;
+      hph ^= hwrap ? 1u : 0u;
     }
     if (!ok) break;
     umma_commit(&acc_full[a]);
@@ -412,8 +436,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* empty = bars + L::NSLOT;
   uint64_t* acc_full = bars + 2 * L::NSLOT;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* halo_full = acc_empty + 2;  // A_HALO: the two halo buffers
-  uint64_t* halo_empty = halo_full + 2;
+  uint64_t* halo_full = acc_empty + 2;  // A_HALO: the ring of halo buffers
+  uint64_t* halo_empty = halo_full + L::NSLOT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
@@ -433,8 +457,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int a = 0; a < 2; a++) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], GEMM_EPI_WARPS);
-      mbar_init(&halo_full[a], 1);
-      mbar_init(&halo_empty[a], 1);
+    }
+    for (int h = 0; h < L::NSLOT; h++) {
+      mbar_init(&halo_full[h], 1);
+      mbar_init(&halo_empty[h], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -459,12 +485,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // ------------------------------------------------------------ producer
       prefetch_tensor_map(&a_map);
       if constexpr (AMODE == A_HALO) {
-        // per tile and channel chunk: one halo box, then the weights of each
-        // kernel row (block (nt kh + ky) chunks + chunk) through the ring
-        const int chunks = p.K / KB;
+        // Per tile and channel chunk one halo box through the ring of
+        // halo_bufs buffers. The weights of each kernel row and chunk (block
+        // (nt kh + ky) chunks + chunk) either stream through the weight ring
+        // after their chunk's box, or, with b_resident, are all loaded once
+        // up front on full[0] and stay.
+        const int chunks = p.K / KB, nh = p.halo_bufs;
         int hb = 0, s = 0, n_halo = 0, n_b = 0;
         uint32_t hph = 0, phase = 0;
         bool ok = true;
+        if (p.b_resident) {
+          const uint32_t total = (uint32_t)(p.halo_kh * chunks * p.b_stage);
+          mbar_arrive_expect_tx(&full[0], total);
+          for (int blk = 0; blk < p.halo_kh * chunks; blk++)
+            bulk_load(smem + p.b_off + blk * p.b_stage, reinterpret_cast<const uint8_t*>(p.b) + (size_t)blk * p.b_stage,
+                      (uint32_t)p.b_stage, &full[0]);
+        }
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
           const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
           const int ty = (int)p.div_tiles_w.div((uint32_t)mt), tx = mt - ty * p.tiles_w;
@@ -479,10 +515,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             tma_load_5d(smem + hb * p.halo_stride, &a_map, &halo_full[hb], (x0 + p.halo_dx0) * 8, y0 + p.halo_dy0, 0,
                         kb * KG, 0);
             n_halo++;
-            if (++hb == 2) {
+            if (++hb == nh) {
               hb = 0;
               hph ^= 1;
             }
+            if (p.b_resident) continue;
             for (int ky = 0; ky < p.halo_kh; ky++) {
               if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
                 ok = false;
@@ -500,8 +537,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
         // the copies in flight land before the CTA may leave
-        for (int c = n_halo - 2; c < n_halo; c++)
-          if (c >= 0) mbar_wait(&halo_full[c & 1], (uint32_t)(c >> 1) & 1, abort_flag, p.dev_err, 0);
+        for (int c = n_halo - nh; c < n_halo; c++)
+          if (c >= 0) mbar_wait(&halo_full[c % nh], (uint32_t)(c / nh) & 1, abort_flag, p.dev_err, 0);
+        if (p.b_resident) mbar_wait(&full[0], 0, abort_flag, p.dev_err, 0);
         for (int c = n_b - p.b_stages; c < n_b; c++)
           if (c >= 0) mbar_wait(&full[c % p.b_stages], (uint32_t)(c / p.b_stages) & 1, abort_flag, p.dev_err, 0);
       } else {
@@ -554,19 +592,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       constexpr uint32_t idesc = idesc_f16_f32(128, BN);
       if constexpr (AMODE == A_HALO) {
         // (the launch checks kw: 3 for bn <= 64, 5 and 7 for bn 32)
+#define IEC_HALO_ISSUE(KW_)                                                                                        \
+  do {                                                                                                             \
+    if (p.b_resident)                                                                                              \
+      halo_mma_issuer<BN, KB, KW_, true>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base, \
+                                         abort_flag);                                                              \
+    else                                                                                                           \
+      halo_mma_issuer<BN, KB, KW_, false>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty,          \
+                                          tmem_base, abort_flag);                                                  \
+  } while (0)
         if constexpr (BN <= 64) {
-          if (p.halo_kw == 3)
-            halo_mma_issuer<BN, KB, 3>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base,
-                                       abort_flag);
+          if (p.halo_kw == 3) IEC_HALO_ISSUE(3);
         }
         if constexpr (BN <= 32) {
-          if (p.halo_kw == 5)
-            halo_mma_issuer<BN, KB, 5>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base,
-                                       abort_flag);
-          else if (p.halo_kw == 7)
-            halo_mma_issuer<BN, KB, 7>(p, smem, full, empty, acc_full, acc_empty, halo_full, halo_empty, tmem_base,
-                                       abort_flag);
+          if (p.halo_kw == 5) IEC_HALO_ISSUE(5);
+          if (p.halo_kw == 7) IEC_HALO_ISSUE(7);
         }
+#undef IEC_HALO_ISSUE
       } else {
       const uint32_t lbo_a = (uint32_t)(a_rows * 16);
       int s = 0, i = 0, last_acc = -1;
