@@ -180,6 +180,119 @@ __global__ void selftest_wait_kernel(int which, int* dev_err) {
 
 }  // namespace
 
+namespace {
+
+// Issue rate of tcgen05.mma kind::f16 128 x N x 16 from zeroed shared
+// memory (no-swizzle K-major operands as the GEMMs lay them out), one CTA
+// per SM, `iters` x 4 MMAs into one accumulator. V 0: the four MMAs of an
+// iteration unrolled with descriptors computed before the loop; V 1: the
+// same MMAs issued through an inner loop whose trip count is only known at
+// run time (2 x 2). cycles[cta] = SM cycles from the first issue to the
+// completion of the last MMA.
+template <int N, int V>
+__global__ void __launch_bounds__(128, 1) selftest_mma_rate_kernel(int iters, int inner, unsigned long long* cycles,
+                                                                   int* dev_err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tslot;
+  __shared__ int abort_flag;
+  constexpr int A_BYTES = 128 * 64 * 2, B_BYTES = N * 64 * 2;
+  for (int i = threadIdx.x; i < (A_BYTES + B_BYTES) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  fence_proxy_async_shared();
+  if (threadIdx.x < 32) tmem_alloc(&tslot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+  if (threadIdx.x == 0) {
+    const uint32_t a = smem_u32(smem), b = a + A_BYTES;
+    constexpr uint32_t idesc = idesc_f16_f32(128, N);
+    const unsigned long long t0 = clock64();
+    if (V == 0) {
+      uint64_t ad[4], bd[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        ad[j] = smem_desc(a + (uint32_t)(2 * j * 128 * 16), 128 * 16, 128);
+        bd[j] = smem_desc(b + (uint32_t)(2 * j * N * 16), N * 16, 128);
+      }
+      for (int it = 0; it < iters; it++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) umma_f16(tmem, ad[j], bd[j], idesc, (it | j) != 0);
+      }
+    } else {
+      for (int it = 0; it < iters; it++)
+        for (int o = 0; o < 2; o++)
+          for (int j = 0; j < inner; j++) {
+            const int q = 2 * o + j;
+            umma_f16(tmem, smem_desc(a + (uint32_t)(2 * q * 128 * 16), 128 * 16, 128),
+                     smem_desc(b + (uint32_t)(2 * q * N * 16), N * 16, 128), idesc, (it | q) != 0);
+          }
+    }
+    umma_commit(&bar);
+    volatile int* flag = &abort_flag;
+    mbar_wait(&bar, 0, flag, dev_err, DEV_ERR_WAIT_FULL);
+    cycles[blockIdx.x] = clock64() - t0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(tmem, 256);
+}
+
+template <int N>
+void mma_rate_launch(Device& dev, int variant, int iters, unsigned long long* cycles, cudaStream_t s) {
+  // 120 KB of shared memory: one CTA per SM
+  const int smem = 120 * 1024;
+  auto k = variant == 0 ? selftest_mma_rate_kernel<N, 0> : selftest_mma_rate_kernel<N, 1>;
+  IEC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  k<<<dev.sms(), 128, smem, s>>>(iters, 2, cycles, dev.dev_err());
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" iec_status iec_selftest_mma_rate(int device, int n, int variant, float* cycles_per_mma) {
+  try {
+    if (variant != 0 && variant != 1) throw Error(ERR_INPUT, "mma rate: variant is 0 or 1");
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    cudaStream_t s = dev.stream();
+    const int iters = 4096, ctas = dev.sms();
+    DeviceBuffer cyc;
+    cyc.reserve((size_t)ctas * 8);
+    for (int rep = 0; rep < 2; rep++) {  // the first launch warms up
+      switch (n) {
+        case 32: mma_rate_launch<32>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        case 64: mma_rate_launch<64>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        case 96: mma_rate_launch<96>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        case 128: mma_rate_launch<128>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        case 192: mma_rate_launch<192>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        case 224: mma_rate_launch<224>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        case 256: mma_rate_launch<256>(dev, variant, iters, cyc.as<unsigned long long>(), s); break;
+        default: throw Error(ERR_INPUT, "mma rate: n is 32, 64, 96, 128, 192, 224 or 256");
+      }
+    }
+    std::vector<unsigned long long> host(ctas);
+    IEC_CUDA(cudaMemcpyAsync(host.data(), cyc.get(), (size_t)ctas * 8, cudaMemcpyDeviceToHost, s));
+    dev.sync(s);
+    double sum = 0;
+    for (unsigned long long c : host) sum += (double)c;
+    *cycles_per_mma = (float)(sum / ctas / (iters * 4.0));
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
 extern "C" iec_status iec_selftest_wait_timeout(int device, int which) {
   try {
     if (which != 0 && which != 1) throw Error(ERR_INPUT, "wait self-test: which is 0 or 1");

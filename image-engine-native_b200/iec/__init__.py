@@ -93,6 +93,7 @@ def lib():
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
+        L.iec_selftest_mma_rate.argtypes = [i32, i32, i32, f32p]
         L.iec_selftest_conv.argtypes = [i32, i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, f32p, i32, f32p]
         L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          f32p, f32p]
@@ -313,6 +314,14 @@ def selftest_conv(a, w, bias=None, *, size=3, halo=-1, act=0, iters=0, device=0)
                                    _f32(b) if b is not None else None, act, _f32(out), iters,
                                    _f32(us) if iters > 0 else None))
     return out, (float(us[0]) if iters > 0 else None)
+
+
+def selftest_mma_rate(n: int, variant: int = 0, device: int = 0) -> float:
+    """Diagnostics: SM cycles per tcgen05.mma kind::f16 128 x n x 16 (see
+    iec_selftest_mma_rate); variant 0 unrolled, 1 through a run-time loop."""
+    out = np.zeros(1, np.float32)
+    _check(lib().iec_selftest_mma_rate(device, n, variant, _f32(out)))
+    return float(out[0])
 
 
 def selftest_attention(qkv, windows, c, bias, shifted, rows_w, cols_w, device=0):

@@ -350,6 +350,13 @@ iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int w, int k, 
 iec_status iec_selftest_conv(int device, int h, int w, int k, int n, int size, int halo, const float* a,
                              const float* weights, const float* bias, int act, float* out, int iters, float* us);
 
+/* Diagnostics: the issue rate of tcgen05.mma kind::f16 128 x n x 16 (n 32,
+ * 64, 96, 128, 192, 224 or 256) on zeroed no-swizzle operands, one CTA per
+ * SM: *cycles_per_mma = SM cycles per MMA. variant 0 issues unrolled MMAs
+ * with precomputed descriptors; 1 issues the same MMAs through an inner
+ * loop whose trip count is known only at run time. */
+iec_status iec_selftest_mma_rate(int device, int n, int variant, float* cycles_per_mma);
+
 /* Diagnostics: LaMa's planar Fourier transforms on host arrays: `x` h x w x c
  * floats (c a multiple of 8, rounded to f16 on the way in); `spec` gets
  * rfft2(x) as h x (w / 2 + 1) x 2c floats (real parts of the c channels, then

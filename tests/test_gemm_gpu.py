@@ -90,3 +90,14 @@ def test_conv_halo_tiles_match_oracle(h, w, k, n, size):
     for halo in (1, 0):
         got, _ = iec.selftest_conv(img, wt, bias, size=size, halo=halo, act=1)
         close(got, want)
+
+
+def test_mma_rate_diagnostic_runs():
+    """The issue-rate diagnostic runs for every MMA width and both issue
+    forms and returns a finite positive cycle count (no rate is asserted)."""
+    import iec
+
+    for n in (32, 96, 256):
+        for variant in (0, 1):
+            c = iec.selftest_mma_rate(n, variant)
+            assert np.isfinite(c) and c > 0
