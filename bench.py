@@ -263,9 +263,11 @@ def launch_table(model, run, pk):
     """One eager pass of `run` with launch timing on (iec_set_launch_timing:
     CUDA events around each instrumented launch, the pass's side-stream work
     serialised onto its stream so each pair times one kernel alone), summarised:
-    the dominant GEMM shape by total time (its algorithmic FLOPs per launch
-    over its mean event time, against the sustained dense peak), all GEMM
-    launches together, and achieved GB/s of the bandwidth-bound kernels
+    the dominant GEMM shape by total time against its own roofline (tensor
+    when its algorithmic FLOPs per algorithmic byte reach the ridge point of
+    the sustained dense peak over the measured copy rate, else HBM), all GEMM
+    launches together (the time they would take at their rooflines over the
+    time they took), and achieved GB/s of the bandwidth-bound kernels
     (algorithmic bytes over event time, against the measured copy rate)."""
     import torch
 
@@ -277,6 +279,18 @@ def launch_table(model, run, pk):
     recs = iec.launch_timing(model)
     iec.set_launch_timing(model, False)
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    hbm = pk["hbm_gbs"]
+    ridge = peak * 1e12 / (hbm * 1e9)  # FLOP per byte
+
+    def bound(g):
+        """(bound, achieved, unit, frac, frac_tensor, frac_hbm) of one GEMM group."""
+        sec = g["ms"] / 1e3
+        tf = g["flop"] / sec / 1e12
+        gbs = g["bytes"] / sec / 1e9
+        if g["bytes"] > 0 and g["flop"] / g["bytes"] < ridge:
+            return "hbm", gbs, "GB/s", gbs / hbm, tf / peak, gbs / hbm
+        return "tensor", tf, "TFLOP/s", tf / peak, tf / peak, gbs / hbm
+
     groups = {}
     for r in recs:
         g = groups.setdefault(r["name"], {"launches": 0, "ms": 0.0, "flop": 0.0, "bytes": 0.0})
@@ -288,18 +302,26 @@ def launch_table(model, run, pk):
     out = {"launches_timed": len(recs), "ms_sum": sum(r["ms"] for r in recs)}
     if gemms:
         name, g = max(gemms.items(), key=lambda kv: kv[1]["ms"])
-        tf = g["flop"] / (g["ms"] / 1e3) / 1e12
-        out["roofline"] = {"kernel": name + " (A x W: M x N x K)", "bound": "tensor", "launches": g["launches"],
+        b, ach, unit, frac, ft, fh = bound(g)
+        out["roofline"] = {"kernel": name + " (A x W: M x N x K)", "bound": b, "launches": g["launches"],
                            "mean_launch_ms": g["ms"] / g["launches"], "flop_per_launch": g["flop"] / g["launches"],
-                           "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
-                           "share_of_timed": g["ms"] / out["ms_sum"]}
+                           "bytes_per_launch": g["bytes"] / g["launches"],
+                           "flop_per_byte": g["flop"] / g["bytes"] if g["bytes"] else None, "ridge_flop_per_byte": ridge,
+                           "achieved": ach, "peak": hbm if b == "hbm" else peak, "unit": unit, "frac": frac,
+                           "frac_of_tensor_peak": ft, "frac_of_hbm": fh, "share_of_timed": g["ms"] / out["ms_sum"]}
         fl = sum(v["flop"] for v in gemms.values())
         ms = sum(v["ms"] for v in gemms.values())
+        at_roof = sum(max(v["flop"] / (peak * 1e12), v["bytes"] / (hbm * 1e9)) for v in gemms.values()) * 1e3
         out["all_gemms"] = {"launches": sum(v["launches"] for v in gemms.values()), "ms": ms,
-                            "achieved_tflops": fl / (ms / 1e3) / 1e12, "frac": fl / (ms / 1e3) / 1e12 / peak}
+                            "achieved_tflops": fl / (ms / 1e3) / 1e12, "frac": fl / (ms / 1e3) / 1e12 / peak,
+                            "roofline_ms": at_roof, "frac_of_roofline": at_roof / ms}
         top = sorted(gemms.items(), key=lambda kv: -kv[1]["ms"])[:6]
-        out["top_gemms"] = [{"kernel": k, "launches": v["launches"], "mean_ms": v["ms"] / v["launches"],
-                             "tflops": v["flop"] / (v["ms"] / 1e3) / 1e12} for k, v in top]
+        out["top_gemms"] = []
+        for k, v in top:
+            b, ach, unit, frac, ft, fh = bound(v)
+            out["top_gemms"].append({"kernel": k, "launches": v["launches"], "mean_ms": v["ms"] / v["launches"],
+                                     "tflops": v["flop"] / (v["ms"] / 1e3) / 1e12, "bound": b,
+                                     "achieved": ach, "unit": unit, "frac": frac})
     bw = {}
     for k, v in groups.items():
         if k.startswith("igemm_sm100") or v["bytes"] <= 0:
