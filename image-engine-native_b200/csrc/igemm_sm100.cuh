@@ -246,10 +246,6 @@ __device__ __forceinline__ float gemm_act(float v, int act) {
   return v;
 }
 
-// The OUT_MAP epilogue of one thread's row over accumulator columns
-// [c_begin, c_end) of its tile (output column = that - cb + the N tile's): in batches of 32 columns (two TMEM loads), the old values of the
-// batch's four 8-column groups are loaded together ahead of the
-// accumulators, so that their latencies overlap.
 // 16 accumulator columns from output column c0 (a multiple of 16) for the
 // warp's 32 rows. A_HALO: the sum over the kernel row's kw taps of the
 // products of tap dx held by the position dx to the right (lane + dx), which
@@ -285,6 +281,11 @@ __device__ __forceinline__ void acc_ld16(const GemmParams& p, uint32_t taddr, in
   }
 }
 
+// The OUT_MAP epilogue of one thread's row over accumulator columns
+// [c_begin, c_end) of its tile (output column = that - cb + the N tile's):
+// in batches of 32 columns (two TMEM loads), the old values of the batch's
+// four 8-column groups are loaded together ahead of the accumulators, so
+// that their latencies overlap.
 template <int BN, int AMODE>
 __device__ __forceinline__ void map_epilogue(const GemmParams& p, const float* bias, uint32_t taddr, int c_begin,
                                              int c_end, int cb, int nt, int m, const int* ry, const int* rx, int nry,

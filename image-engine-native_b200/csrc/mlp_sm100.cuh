@@ -63,24 +63,35 @@ struct MlpSmem {
   static constexpr int W1_BYTES = (C / 8) * NH * 16, W2_BYTES = (NH / 8) * C * 16;
   static constexpr int STAGE = W1_BYTES + W2_BYTES;
   static constexpr int H_BYTES = (NH / 8) * 128 * 16;
-  static constexpr int W_OFF = X_BYTES;
-  static constexpr int H_OFF = W_OFF + 2 * STAGE;
   static constexpr int PAR_FLOATS = 3 * C + HID;
+  static constexpr int NBAR = 24;
+  // Shared memory per CTA (two CTAs per SM share 228 KB). The weights stay
+  // resident (every chunk loaded once per CTA) where they fit beside two
+  // row tiles; else they stream through a ring of two chunks. The row tile
+  // is double-buffered where that fits, so the next tile's rows land while
+  // this one is in the hidden layer.
+  static constexpr int BUDGET = (CTAS == 2 ? 112 : 224) * 1024;
+  static constexpr int FIXED = 2 * H_BYTES + PAR_FLOATS * 4 + NBAR * 8 + 16;
+  static constexpr bool RES = CHUNKS * STAGE + 2 * X_BYTES + FIXED <= BUDGET;
+  static constexpr int WS = RES ? CHUNKS : 2;  // weight stages
+  static constexpr int XB = WS * STAGE + 2 * X_BYTES + FIXED <= BUDGET ? 2 : 1;
+  static constexpr int W_OFF = XB * X_BYTES;
+  static constexpr int H_OFF = W_OFF + WS * STAGE;
   static constexpr int PAR_OFF = H_OFF + 2 * H_BYTES;
   static constexpr int BAR_OFF = PAR_OFF + PAR_FLOATS * 4;
-  static constexpr int NBAR = 24;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16;
   // TMEM: fc2's accumulator at column 0 (C columns), fc1's two at D1 and D1 + NH.
   static constexpr int D1 = C <= 64 ? 64 : C <= 256 ? 256 : 384;
   static constexpr int N2_SPLIT = C > 256 ? 2 : 1, N2 = C / N2_SPLIT;  // fc2's MMA width
   static_assert(C % 32 == 0 && C <= 384, "MLP width");
-  static_assert(TOTAL <= 227 * 1024, "MLP shared memory");
+  static_assert(TOTAL <= 227 * 1024 && (CTAS == 1 || TOTAL <= 113 * 1024), "MLP shared memory");
   static_assert(D1 + 2 * NH <= TMEM_COLS, "MLP tensor memory");
 };
 
 // Barrier slots.
 enum : int {
-  MB_X_FULL = 0, MB_X_READY, MB_X_EMPTY, MB_W_FULL, MB_W_EMPTY = MB_W_FULL + 2, MB_D1_FULL = MB_W_EMPTY + 2,
+  MB_X_FULL = 0, MB_X_READY = 2, MB_X_EMPTY = 4,  // per row-tile buffer
+  MB_W_FULL = 6, MB_W_EMPTY = MB_W_FULL + 2, MB_D1_FULL = MB_W_EMPTY + 2,
   MB_H_FULL = MB_D1_FULL + 2, MB_H_EMPTY = MB_H_FULL + 2, MB_D2_FULL = MB_H_EMPTY + 2, MB_D2_EMPTY,
   MB_LN_READ,  // four: the warps of one lane quarter have read their rows
   MB_COUNT = MB_LN_READ + 4
@@ -107,12 +118,12 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(&bar[MB_X_FULL], 1);
-    mbar_init(&bar[MB_X_READY], L::EW);
-    mbar_init(&bar[MB_X_EMPTY], 1);
     mbar_init(&bar[MB_D2_FULL], 1);
     mbar_init(&bar[MB_D2_EMPTY], L::EW);
     for (int b = 0; b < 2; b++) {
+      mbar_init(&bar[MB_X_FULL + b], 1);
+      mbar_init(&bar[MB_X_READY + b], L::EW);
+      mbar_init(&bar[MB_X_EMPTY + b], 1);
       mbar_init(&bar[MB_W_FULL + b], 1);
       mbar_init(&bar[MB_W_EMPTY + b], 1);
       mbar_init(&bar[MB_D1_FULL + b], 1);
@@ -143,11 +154,18 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       prefetch_tensor_map(&x_map);
       bool ok = true;
       int i = 0;
+      if (L::RES) {  // every chunk once, on the first weight barrier
+        mbar_arrive_expect_tx(&bar[MB_W_FULL], (uint32_t)(CHUNKS * L::STAGE));
+        for (int j = 0; j < CHUNKS; j++)
+          bulk_load(Wst + j * L::STAGE, p.w + (size_t)j * L::STAGE, (uint32_t)L::STAGE, &bar[MB_W_FULL]);
+      }
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
-        if (!mbar_wait(&bar[MB_X_EMPTY], (uint32_t)(i & 1) ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) break;
-        mbar_arrive_expect_tx(&bar[MB_X_FULL], (uint32_t)L::X_BYTES);
-        tma_load_3d(X, &x_map, &bar[MB_X_FULL], 0, tile * 8, 0);
-        for (int j = 0; j < CHUNKS; j++) {
+        const int xb = i % L::XB;
+        const uint32_t xph = (uint32_t)(i / L::XB) & 1;
+        if (!mbar_wait(&bar[MB_X_EMPTY + xb], xph ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&bar[MB_X_FULL + xb], (uint32_t)L::X_BYTES);
+        tma_load_3d(X + xb * L::X_BYTES, &x_map, &bar[MB_X_FULL + xb], 0, tile * 8, 0);
+        for (int j = 0; j < CHUNKS && !L::RES; j++) {
           const int c = i * CHUNKS + j, b = c & 1;
           const uint32_t ph = (uint32_t)(c >> 1) & 1;
           if (!mbar_wait(&bar[MB_W_EMPTY + b], ph ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_WEIGHTS)) {
@@ -159,8 +177,10 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
         }
       }
       // let the copies in flight land before the CTA may leave
-      const int n = i * CHUNKS;
-      if (i > 0) mbar_wait(&bar[MB_X_FULL], (uint32_t)((i - 1) & 1), abort_flag, p.dev_err, 0);
+      const int n = L::RES ? 0 : i * CHUNKS;
+      for (int t = i - L::XB; t < i; t++)
+        if (t >= 0) mbar_wait(&bar[MB_X_FULL + t % L::XB], (uint32_t)(t / L::XB) & 1, abort_flag, p.dev_err, 0);
+      if (L::RES) mbar_wait(&bar[MB_W_FULL], 0, abort_flag, p.dev_err, 0);
       for (int c = n - 2; c < n; c++)
         if (c >= 0) mbar_wait(&bar[MB_W_FULL + (c & 1)], (uint32_t)(c >> 1) & 1, abort_flag, p.dev_err, 0);
     }
@@ -169,7 +189,7 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc1 = idesc_f16_f32(128, NH);
       constexpr uint32_t idesc2 = idesc_f16_f32(128, L::N2);
-      const uint32_t xa = smem_u32(X), wa = smem_u32(Wst), ha = smem_u32(Hb);
+      const uint32_t xa0 = smem_u32(X), wa = smem_u32(Wst), ha = smem_u32(Hb);
       bool ok = true;
       int i = 0;
       // fc2 of chunk c (global chunk count), accumulating over the tile's chunks
@@ -181,7 +201,8 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
                                  DEV_ERR_WAIT_ACC_EMPTY))
           return false;
         tc_fence_after();
-        const uint32_t hb = ha + (uint32_t)(b * L::H_BYTES), w2 = wa + (uint32_t)(b * L::STAGE + L::W1_BYTES);
+        const uint32_t hb = ha + (uint32_t)(b * L::H_BYTES);
+        const uint32_t w2 = wa + (uint32_t)((L::RES ? j : b) * L::STAGE + L::W1_BYTES);
 #pragma unroll
         for (int k = 0; k < NH / 16; k++)
 #pragma unroll
@@ -191,24 +212,33 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
             umma_f16(tmem + (uint32_t)(s * L::N2), ad, bd, idesc2, (j > 0 || k > 0) ? 1u : 0u);
           }
         umma_commit(&bar[MB_H_EMPTY + b]);
-        umma_commit(&bar[MB_W_EMPTY + b]);
+        if (!L::RES) umma_commit(&bar[MB_W_EMPTY + b]);
         return true;
       };
-      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
-        if (!mbar_wait(&bar[MB_X_READY], (uint32_t)(i & 1), abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) break;
+      if (L::RES) {
+        ok = mbar_wait(&bar[MB_W_FULL], 0, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL);
         tc_fence_after();
+      }
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
+        const int xb = i % L::XB;
+        if (!mbar_wait(&bar[MB_X_READY + xb], (uint32_t)(i / L::XB) & 1, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL))
+          break;
+        tc_fence_after();
+        const uint32_t xa = xa0 + (uint32_t)(xb * L::X_BYTES);
         for (int j = 0; j < CHUNKS && ok; j++) {
           const int c = i * CHUNKS + j, b = c & 1;
           const uint32_t ph = (uint32_t)(c >> 1) & 1;
-          if (!mbar_wait(&bar[MB_W_FULL + b], ph, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
-            ok = false;
-            break;
+          if (!L::RES) {
+            if (!mbar_wait(&bar[MB_W_FULL + b], ph, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
           // fc1 of chunk c: D1[b] = X (128 x C) x W1 chunk (C x NH). D1[b]
           // was last read by the epilogue of chunk c - 2, whose h_full this
           // thread waited for before issuing fc2 of c - 2.
-          const uint32_t w1 = wa + (uint32_t)(b * L::STAGE);
+          const uint32_t w1 = wa + (uint32_t)((L::RES ? j : b) * L::STAGE);
 #pragma unroll
           for (int k = 0; k < C / 16; k++) {
             const uint64_t ad = smem_desc(xa + (uint32_t)(2 * k * 128 * 16), 128 * 16, 128);
@@ -216,7 +246,7 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
             umma_f16(tmem + (uint32_t)(L::D1 + b * NH), ad, bd, idesc1, k > 0 ? 1u : 0u);
           }
           umma_commit(&bar[MB_D1_FULL + b]);
-          if (j == CHUNKS - 1) umma_commit(&bar[MB_X_EMPTY]);  // every fc1 of the tile has read X
+          if (j == CHUNKS - 1) umma_commit(&bar[MB_X_EMPTY + xb]);  // every fc1 of the tile has read X
           if (j > 0 && !fc2(c - 1, j - 1, i)) ok = false;
         }
         if (!ok) break;
@@ -235,7 +265,10 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
     constexpr int G = C / 8 / L::PARTS;  // channel groups this part normalises (part, part + PARTS, ...)
     int i = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
-      if (!mbar_wait(&bar[MB_X_FULL], (uint32_t)(i & 1), abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) break;
+      const int xb = i % L::XB;
+      uint8_t* Xt = X + xb * L::X_BYTES;
+      if (!mbar_wait(&bar[MB_X_FULL + xb], (uint32_t)(i / L::XB) & 1, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL))
+        break;
       // LayerNorm of the row in place (gemm.cu layer_norm_rows' formula:
       // mean, the mean squared deviation, (v - mean) / sqrt(var + 1e-5)).
       // Every part computes its row's statistics over all C channels itself
@@ -244,7 +277,7 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       float sum = 0.0f;
 #pragma unroll 4
       for (int g = 0; g < C / 8; g++) {
-        const uint4 u = *reinterpret_cast<const uint4*>(X + (g * 128 + row) * 16);
+        const uint4 u = *reinterpret_cast<const uint4*>(Xt + (g * 128 + row) * 16);
         const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
         for (int e = 0; e < 4; e++) {
@@ -256,7 +289,7 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       float var = 0.0f;
 #pragma unroll 4
       for (int g = 0; g < C / 8; g++) {
-        const uint4 u = *reinterpret_cast<const uint4*>(X + (g * 128 + row) * 16);
+        const uint4 u = *reinterpret_cast<const uint4*>(Xt + (g * 128 + row) * 16);
         const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
         for (int e = 0; e < 4; e++) {
@@ -273,7 +306,7 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
 #pragma unroll
       for (int k = 0; k < G; k++) {
         const int g = part + L::PARTS * k;
-        uint4* at = reinterpret_cast<uint4*>(X + (g * 128 + row) * 16);
+        uint4* at = reinterpret_cast<uint4*>(Xt + (g * 128 + row) * 16);
         const uint4 u = *at;
         const __half2* h = reinterpret_cast<const __half2*>(&u);
         float v[8];
@@ -287,7 +320,7 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       }
       fence_proxy_async_shared();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[MB_X_READY]);
+      if (lane == 0) mbar_arrive(&bar[MB_X_READY + xb]);
 
       // The hidden layer, chunk by chunk: bias, GELU, f16 into H[b].
       bool ok = true;
@@ -334,19 +367,39 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       }
       if (!ok) break;
 
-      // x += fc2 + b2 over this part's C / PARTS columns.
-      if (!mbar_wait(&bar[MB_D2_FULL], (uint32_t)(i & 1), abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
-      tc_fence_after();
+      // x += fc2 + b2 over this part's C / PARTS columns. Their old values
+      // are read before the wait for fc2 (into registers for up to four
+      // groups, else towards L1), so that the read overlaps the MMAs.
+      constexpr int PG = C / 8 / L::PARTS;  // this part's channel groups
+      constexpr bool HOLD = PG <= 4;
       const int m = tile * 128 + row;
       const bool live = m < p.M;
-#pragma unroll 1
-      for (int c0 = part * (C / L::PARTS); c0 < (part + 1) * (C / L::PARTS); c0 += 8) {
+      __half* row_at = p.x + (long long)(part * PG) * p.plane_elems + (long long)m * 8;
+      uint4 olds[HOLD ? PG : 1];
+      if (live) {
+#pragma unroll
+        for (int q = 0; q < PG; q++) {
+          if constexpr (HOLD)
+            olds[q] = *reinterpret_cast<const uint4*>(row_at + (long long)q * p.plane_elems);
+          else
+            prefetch_l1(row_at + (long long)q * p.plane_elems);
+        }
+      }
+      if (!mbar_wait(&bar[MB_D2_FULL], (uint32_t)(i & 1), abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_FULL)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < PG; q++) {
+        const int c0 = (part * PG + q) * 8;
         uint32_t r[8];
         tmem_ld8(tmem + lanes + (uint32_t)c0, r);
         tmem_wait_ld();
         if (!live) continue;
-        __half* at = p.x + (long long)(c0 / 8) * p.plane_elems + (long long)m * 8;
-        const uint4 old = *reinterpret_cast<const uint4*>(at);
+        __half* at = row_at + (long long)q * p.plane_elems;
+        uint4 old;
+        if constexpr (HOLD)
+          old = olds[q];
+        else
+          old = *reinterpret_cast<const uint4*>(at);
         float w[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) w[e] = __uint_as_float(r[e]) + b2[c0 + e];
