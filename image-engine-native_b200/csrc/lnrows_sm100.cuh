@@ -10,7 +10,8 @@
 // not normalised). Row r of the output is token r % 64 of window r / 64 in
 // the order layer_norm_planar's window mode writes (gemm.h WindowMap).
 // Per tile of 128 output rows:
-//   * four loader warps, one row per thread, gather the row's C channels
+//   * two groups of four loader warps (each group every other tile), one
+//     row per thread, gather the row's C channels
 //     (16-byte pixel groups of the planar map; consecutive tokens of a window
 //     row are consecutive pixels), take its mean and mean squared deviation,
 //     and write the normalised f16 row into one of two shared-memory A tiles
@@ -18,7 +19,7 @@
 //   * one thread issues the MMAs (M 128 x N x K C; N above 256 as two halves)
 //     into one of two TMEM accumulators (one when 2 N exceeds 512 columns),
 //     the weights resident in shared memory for the whole launch;
-//   * twelve epilogue warps add the bias and store the f16 rows, planar
+//   * eight epilogue warps add the bias and store the f16 rows, planar
 //     [N / 8][rows][8], while the next tile is gathered and multiplied.
 // Every wait is bounded (sm100.cuh).
 #pragma once
@@ -48,7 +49,10 @@ struct LnRowsParams {
 
 template <int C, int N>
 struct LnRowsSmem {
-  static constexpr int LOADERS = 4, EPI = 12, THREADS = 32 * (2 + LOADERS + EPI);
+  // Eight loader warps in two groups of four (one row per thread), each
+  // group owning every other tile and one of the two A tiles, so that two
+  // tiles' gathers and LayerNorms are in flight; eight epilogue warps.
+  static constexpr int LOADERS = 8, GROUP = 4, EPI = 8, THREADS = 32 * (2 + LOADERS + EPI);
   static constexpr int ACCS = 2 * N <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = ACCS * N <= 256 ? 256 : 512;
   static constexpr int NSPLIT = N > 256 ? 2 : 1, NPART = N / NSPLIT;
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(LnRowsSmem<C, N>::THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bar[LB_W], 1);
     for (int b = 0; b < 2; b++) {
-      mbar_init(&bar[LB_A_FULL + b], L::LOADERS);
+      mbar_init(&bar[LB_A_FULL + b], L::GROUP);
       mbar_init(&bar[LB_A_EMPTY + b], 1);
       mbar_init(&bar[LB_ACC_FULL + b], 1);
       mbar_init(&bar[LB_ACC_EMPTY + b], L::EPI);
@@ -140,36 +144,60 @@ __global__ void __launch_bounds__(LnRowsSmem<C, N>::THREADS, 1)
     }
   } else if (warp >= 2 && warp < 2 + L::LOADERS) {
     // ------------------------------------------------ gather + LayerNorm
-    const int row = (warp - 2) * 32 + lane;  // row of the tile
+    const int group = (warp - 2) / L::GROUP;            // tiles i = group, group + 2, ...
+    const int row = ((warp - 2) % L::GROUP) * 32 + lane;  // row of the tile
     const WindowMap wm = p.wm;
     const int cols = wm.pad_w / wm.ws;
-    int i = 0;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
-      const int b = i & 1;
-      const uint32_t ph = (uint32_t)(i >> 1) & 1;
-      if (!mbar_wait(&bar[LB_A_EMPTY + b], ph ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) break;
-      // the token this row holds (layer_norm_rows' window order)
+    // The token row `row` of a tile holds (layer_norm_rows' window order):
+    // whether it is a zero row, and its pixel.
+    auto locate = [&](int tile, bool& zero, long long& pix) {
       const int r = tile * 128 + row;
       const int win = r >> 6, t = r & 63;
       const int wy = win / cols, wx = win - wy * cols;
       const int y = (wy * wm.ws + t / wm.ws + wm.shift) % wm.pad_h, x = (wx * wm.ws + t % wm.ws + wm.shift) % wm.pad_w;
-      const bool zero = r >= p.rows || t >= wm.ws * wm.ws || y >= wm.map_h || x >= wm.map_w;
-      const long long pix = zero ? 0 : (long long)y * wm.map_w + x;
-      // Narrow rows stay in registers across the three passes; wide ones
-      // are read again (L1 hits) in each, which keeps the loaders unspilled.
-      constexpr bool HOLD = C <= 32;
-      uint4 v[HOLD ? C / 8 : 1];
+      zero = r >= p.rows || t >= wm.ws * wm.ws || y >= wm.map_h || x >= wm.map_w;
+      pix = zero ? 0 : (long long)y * wm.map_w + x;
+    };
+    // Narrow rows stay in registers across the three passes, and the next
+    // tile's row is loaded before this one is normalised; wide ones are read
+    // again (L1 hits) in each pass, the next tile's row prefetched towards
+    // L1, which keeps the loaders unspilled. Either way the row's global
+    // latency overlaps the previous tile's work.
+    constexpr bool HOLD = C <= 32;
+    uint4 v[HOLD ? C / 8 : 1], vn[HOLD ? C / 8 : 1];
+    auto fetch = [&](bool z, long long px, uint4* dst) {
+#pragma unroll
+      for (int g = 0; g < C / 8; g++) {
+        const __half* at = p.src + (long long)g * p.src_plane + px * 8;
+        if constexpr (HOLD)
+          dst[g] = z ? make_uint4(0u, 0u, 0u, 0u) : *reinterpret_cast<const uint4*>(at);
+        else if (!z)
+          prefetch_l1(at);
+      }
+    };
+    bool zero = true;
+    long long pix = 0;
+    const int first = (int)blockIdx.x + group * (int)gridDim.x, step = 2 * (int)gridDim.x;
+    if (first < p.tiles) {
+      locate(first, zero, pix);
+      fetch(zero, pix, v);
+    }
+    // the CTA's tile sequence i = group, group + 2, ...: A tile b = group
+    for (int tile = first, i = group; tile < p.tiles; tile += step, i += 2) {
+      const int b = i & 1;
+      const uint32_t ph = (uint32_t)(i >> 1) & 1;
+      bool zero_n = true;
+      long long pix_n = 0;
+      if (tile + step < p.tiles) {
+        locate(tile + step, zero_n, pix_n);
+        fetch(zero_n, pix_n, vn);
+      }
+      if (!mbar_wait(&bar[LB_A_EMPTY + b], ph ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) break;
       auto group = [&](int g) -> uint4 {
         if (zero) return make_uint4(0u, 0u, 0u, 0u);
         if constexpr (HOLD) return v[g];
         return *reinterpret_cast<const uint4*>(p.src + (long long)g * p.src_plane + pix * 8);
       };
-      if constexpr (HOLD) {
-#pragma unroll
-        for (int g = 0; g < C / 8; g++)
-          v[g] = zero ? make_uint4(0u, 0u, 0u, 0u)
-                      : *reinterpret_cast<const uint4*>(p.src + (long long)g * p.src_plane + pix * 8);
-      }
       float sum = 0.0f;
 #pragma unroll
       for (int g = 0; g < C / 8; g++) {
@@ -211,14 +239,21 @@ __global__ void __launch_bounds__(LnRowsSmem<C, N>::THREADS, 1)
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar[LB_A_FULL + b]);
+      zero = zero_n;
+      pix = pix_n;
+      if constexpr (HOLD) {
+#pragma unroll
+        for (int g = 0; g < C / 8; g++) v[g] = vn[g];
+      }
     }
   } else if (warp >= 2 + L::LOADERS) {
     // ------------------------------------------------------------- epilogue
-    const int e = warp - 2 - L::LOADERS;  // 0 .. 11
-    const int quarter = warp & 3, part = e >> 2;  // three column parts per lane quarter
+    const int e = warp - 2 - L::LOADERS;  // 0 .. EPI - 1
+    const int quarter = warp & 3, part = e >> 2;  // EPI / 4 column parts per lane quarter
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
-    constexpr int COLS = N / 3;
+    constexpr int COLS = N / (L::EPI / 4);
+    static_assert(COLS % 16 == 0, "epilogue columns");
     int i = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
       const int a = i % L::ACCS;
