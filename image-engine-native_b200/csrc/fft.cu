@@ -35,7 +35,7 @@ namespace {
 
 constexpr int FFT_THREADS = 256;
 constexpr int FFT_SMALL_THREADS = 1024;  // the one-launch transforms: a stage's butterflies at once
-constexpr int FFT_POINTS = 512;   // points per CTA when lines are short
+constexpr int FFT_POINTS = 256;   // points per CTA when lines are short (measured: 512 and 128 slower)
 constexpr int FFT_MAX_N = 1536;   // longest line (shared memory: 2 x 64 n bytes)
 
 __device__ __forceinline__ float4 cmul2(float4 v, float wr, float wi) {
