@@ -487,11 +487,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Programmatic dependent launch: let the next kernel's CTAs start their
-  // own set-up as SMs free up, and wait for the previous kernel's results
-  // (and for its reads of what this one overwrites) before any global
-  // memory access. Without the launch attribute both are no-ops.
+  // own set-up as SMs free up. The producer and the epilogue wait for the
+  // previous kernel's results (and for its reads of what this one
+  // overwrites) before they touch activations; the weights and the bias,
+  // which no kernel writes, are fetched before that wait, so the ring's
+  // first weight stages fill while the previous kernel drains. The MMA
+  // issuer touches no global memory. Without the launch attribute the
+  // waits are no-ops.
   griddep_launch_dependents();
-  griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -514,6 +517,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             bulk_load(smem + p.b_off + blk * p.b_stage, reinterpret_cast<const uint8_t*>(p.b) + (size_t)blk * p.b_stage,
                       (uint32_t)p.b_stage, &full[0]);
         }
+        griddep_wait();
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
           const int mt = (int)p.div_tiles_n.div((uint32_t)tile), nt = tile - mt * p.tiles_n;
           const int ty = (int)p.div_tiles_w.div((uint32_t)mt), tx = mt - ty * p.tiles_w;
@@ -561,18 +565,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int issued[L::NSTAGE];
       for (int i = 0; i < L::NSTAGE; i++) issued[i] = -1;
       bool ok = true;
+      // The first NSTAGE stages (fresh, so free) get their weights and their
+      // whole transaction count now; their A boxes follow after the wait.
+      int pre = 0;
+      for (int tile = blockIdx.x; tile < p.tiles && pre < L::NSTAGE; tile += gridDim.x) {
+        const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
+        const int nt = tmn - (int)p.div_tiles_n.div((uint32_t)tmn) * p.tiles_n;
+        const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
+        const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
+        for (int ks = ks0; ks < ks1 && pre < L::NSTAGE; ks++, pre++) {
+          mbar_arrive_expect_tx(&full[pre], (uint32_t)L::MSUB * a_bytes + (uint32_t)L::B_BYTES);
+          bulk_load(smem + pre * L::STAGE + L::A_BYTES, bsrc + (size_t)ks * L::B_BYTES, L::B_BYTES, &full[pre]);
+        }
+      }
+      griddep_wait();
+      int n_issue = 0;
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
         const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
         const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
         const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
         const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
-        for (int ks = ks0; ks < ks1; ks++) {
-          if (!mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
+        for (int ks = ks0; ks < ks1; ks++, n_issue++) {
+          const bool early = n_issue < pre;  // weights already in flight
+          if (!early && !mbar_wait(&empty[s], phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_EMPTY)) {
             ok = false;
             break;
           }
           uint8_t* st = smem + s * L::STAGE;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)L::MSUB * a_bytes + (uint32_t)L::B_BYTES);
+          if (!early) mbar_arrive_expect_tx(&full[s], (uint32_t)L::MSUB * a_bytes + (uint32_t)L::B_BYTES);
 #pragma unroll
           for (int sb = 0; sb < L::MSUB; sb++) {
             const int blk = mt * L::MSUB + sb;
@@ -587,7 +607,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               tma_load_5d(sa, &a_map, &full[s], (bx0 + p.dx[tap]) * 8, by0 + p.dy[tap], p.phase[tap], kb * KG, 0);
             }
           }
-          bulk_load(st + L::A_BYTES, bsrc + (size_t)ks * L::B_BYTES, L::B_BYTES, &full[s]);
+          if (!early) bulk_load(st + L::A_BYTES, bsrc + (size_t)ks * L::B_BYTES, L::B_BYTES, &full[s]);
           issued[s] = (int)phase;
           if (++s == L::NSTAGE) {
             s = 0;
@@ -685,6 +705,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int j = (int)threadIdx.x - 64; j < n_pad; j += 32 * GEMM_EPI_WARPS) sbias[j] = j < p.N ? p.bias[j] : 0.0f;
     asm volatile("bar.sync 1, %0;" ::"n"(32 * GEMM_EPI_WARPS) : "memory");
     const float* bias = bias_staged ? sbias : p.bias;
+    griddep_wait();
     int i = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
       const int a = i & 1;
