@@ -263,64 +263,73 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
     constexpr int G = C / 8 / L::PARTS;  // channel groups this part normalises (part, part + PARTS, ...)
+    // LayerNorm of tile `tile` (the CTA's i-th) in place, then X_READY; false
+    // when a bounded wait gave up.
+    auto layer_norm = [&](int tile, int i) -> bool {
+        const int xb = i % L::XB;
+        uint8_t* Xt = X + xb * L::X_BYTES;
+        if (!mbar_wait(&bar[MB_X_FULL + xb], (uint32_t)(i / L::XB) & 1, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL))
+          return false;
+        // LayerNorm of the row in place (gemm.cu layer_norm_rows' formula:
+        // mean, the mean squared deviation, (v - mean) / sqrt(var + 1e-5)).
+        // Every part computes its row's statistics over all C channels itself
+        // (no exchange between warps, so no barrier an aborted warp could
+        // leave waiting), then normalises its own groups.
+        float sum = 0.0f;
+#pragma unroll 4
+        for (int g = 0; g < C / 8; g++) {
+          const uint4 u = *reinterpret_cast<const uint4*>(Xt + (g * 128 + row) * 16);
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(h[e]);
+            sum += f.x + f.y;
+          }
+        }
+        const float mean = sum / (float)C;
+        float var = 0.0f;
+#pragma unroll 4
+        for (int g = 0; g < C / 8; g++) {
+          const uint4 u = *reinterpret_cast<const uint4*>(Xt + (g * 128 + row) * 16);
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(h[e]);
+            var += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
+          }
+        }
+        // every part has read the whole row before any part overwrites its
+        // groups: the four warps of a quarter meet on an mbarrier (bounded)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[MB_LN_READ + quarter]);
+        if (!mbar_wait(&bar[MB_LN_READ + quarter], (uint32_t)(i & 1), abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) return false;
+        const float inv = 1.0f / sqrtf(var / (float)C + 1e-5f);
+#pragma unroll
+        for (int k = 0; k < G; k++) {
+          const int g = part + L::PARTS * k;
+          uint4* at = reinterpret_cast<uint4*>(Xt + (g * 128 + row) * 16);
+          const uint4 u = *at;
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(h[e]);
+            v[2 * e] = (f.x - mean) * inv * gamma[8 * g + 2 * e] + beta[8 * g + 2 * e];
+            v[2 * e + 1] = (f.y - mean) * inv * gamma[8 * g + 2 * e + 1] + beta[8 * g + 2 * e + 1];
+          }
+          *at = pack_half8(v);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[MB_X_READY + xb]);
+      return true;
+    };
+    // Per tile: the hidden layer; then the next tile's LayerNorm, which
+    // fills the wait for this tile's last fc2 and lets the next fc1 run
+    // under this tile's final epilogue; then the final epilogue.
+    bool ln_ok = (int)blockIdx.x >= p.tiles || layer_norm(blockIdx.x, 0);
     int i = 0;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
-      const int xb = i % L::XB;
-      uint8_t* Xt = X + xb * L::X_BYTES;
-      if (!mbar_wait(&bar[MB_X_FULL + xb], (uint32_t)(i / L::XB) & 1, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL))
-        break;
-      // LayerNorm of the row in place (gemm.cu layer_norm_rows' formula:
-      // mean, the mean squared deviation, (v - mean) / sqrt(var + 1e-5)).
-      // Every part computes its row's statistics over all C channels itself
-      // (no exchange between warps, so no barrier an aborted warp could
-      // leave waiting), then normalises its own groups.
-      float sum = 0.0f;
-#pragma unroll 4
-      for (int g = 0; g < C / 8; g++) {
-        const uint4 u = *reinterpret_cast<const uint4*>(Xt + (g * 128 + row) * 16);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float2 f = __half22float2(h[e]);
-          sum += f.x + f.y;
-        }
-      }
-      const float mean = sum / (float)C;
-      float var = 0.0f;
-#pragma unroll 4
-      for (int g = 0; g < C / 8; g++) {
-        const uint4 u = *reinterpret_cast<const uint4*>(Xt + (g * 128 + row) * 16);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float2 f = __half22float2(h[e]);
-          var += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
-        }
-      }
-      // every part has read the whole row before any part overwrites its
-      // groups: the four warps of a quarter meet on an mbarrier (bounded)
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[MB_LN_READ + quarter]);
-      if (!mbar_wait(&bar[MB_LN_READ + quarter], (uint32_t)(i & 1), abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) break;
-      const float inv = 1.0f / sqrtf(var / (float)C + 1e-5f);
-#pragma unroll
-      for (int k = 0; k < G; k++) {
-        const int g = part + L::PARTS * k;
-        uint4* at = reinterpret_cast<uint4*>(Xt + (g * 128 + row) * 16);
-        const uint4 u = *at;
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float2 f = __half22float2(h[e]);
-          v[2 * e] = (f.x - mean) * inv * gamma[8 * g + 2 * e] + beta[8 * g + 2 * e];
-          v[2 * e + 1] = (f.y - mean) * inv * gamma[8 * g + 2 * e + 1] + beta[8 * g + 2 * e + 1];
-        }
-        *at = pack_half8(v);
-      }
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[MB_X_READY + xb]);
+    for (int tile = blockIdx.x; tile < p.tiles && ln_ok; tile += gridDim.x, i++) {
 
       // The hidden layer, chunk by chunk: bias, GELU, f16 into H[b].
       bool ok = true;
@@ -366,6 +375,8 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
         if (lane == 0) mbar_arrive(&bar[MB_H_FULL + b]);
       }
       if (!ok) break;
+
+      if (tile + (int)gridDim.x < p.tiles && !layer_norm(tile + gridDim.x, i + 1)) break;
 
       // x += fc2 + b2 over this part's C / PARTS columns. Their old values
       // are read before the wait for fc2 (into registers for up to four
