@@ -232,8 +232,13 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
       int last_acc = -1, cur = -1, nw = 0, wb = 0;
       uint32_t last_parity = 0, phase = 0;
       int s = 0, i = 0;
+      // The item's layer from its packed word, read one item ahead: the
+      // single issuing thread pays for any arithmetic or load latency
+      // between its MMAs.
+      uint32_t next = (int)blockIdx.x < p.items ? __ldg(p.item_words + blockIdx.x) : 0u;
       for (int k = blockIdx.x; k < p.items; k += gridDim.x, i++) {
-        const int layer = body_item(p, k).layer;
+        const int layer = (int)(next >> 27);
+        if (k + (int)gridDim.x < p.items) next = __ldg(p.item_words + k + gridDim.x);
         if (layer != cur) {
           if (cur >= 0) umma_commit(&wempty[wb]);  // the old layer's weights, once its MMAs are done
           wb = nw & 1;
@@ -263,10 +268,9 @@ __global__ void __launch_bounds__(BODY_THREADS, 1)
         umma_commit(&acc_full[a]);
         last_acc = a;
         last_parity = acc_phase;
-        if (++s == BODY_NSTAGE) {
-          s = 0;
-          phase ^= 1;
-        }
+        const bool wrap = s + 1 == BODY_NSTAGE;
+        s = wrap ? 0 : s + 1;
+        phase ^= wrap ? 1u : 0u;
       }
       // The accumulators must be written before TMEM is released.
       if (last_acc >= 0) mbar_wait(&acc_full[last_acc], last_parity, abort_flag, p.dev_err, 0);
