@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // whole transaction count now; their A boxes follow after the wait.
       int pre = 0;
       for (int tile = blockIdx.x; tile < p.tiles && pre < L::NSTAGE; tile += gridDim.x) {
-        const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
+        const int split = p.ksplit > 1 ? tile / p.tiles_mn : 0, tmn = tile - split * p.tiles_mn;
         const int nt = tmn - (int)p.div_tiles_n.div((uint32_t)tmn) * p.tiles_n;
         const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
         const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       griddep_wait();
       int n_issue = 0;
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
-        const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
+        const int split = p.ksplit > 1 ? tile / p.tiles_mn : 0, tmn = tile - split * p.tiles_mn;
         const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
         const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
         const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(p.b) + (size_t)nt * p.ksteps * L::B_BYTES;
@@ -653,7 +653,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&acc_empty[a], acc_phase ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_EMPTY)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(a * L::ACC_COLS);
-        const int split = tile / p.tiles_mn;
+        const int split = p.ksplit > 1 ? tile / p.tiles_mn : 0;  // no division without split-K
         const int ks0 = split * p.kslice, ks1 = min(ks0 + p.kslice, p.ksteps);
         for (int ks = ks0; ks < ks1; ks++) {
           if (!mbar_wait(&full[s], phase, abort_flag, p.dev_err, DEV_ERR_WAIT_FULL)) {
@@ -671,10 +671,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               umma_f16(d + (uint32_t)(sb * BN), adesc, bdesc, idesc, (ks != ks0) || (j != 0));
             }
           umma_commit(&empty[s]);
-          if (++s == L::NSTAGE) {
-            s = 0;
-            phase ^= 1;
-          }
+          const bool wrap = s + 1 == L::NSTAGE;
+          s = wrap ? 0 : s + 1;
+          phase ^= wrap ? 1u : 0u;
         }
         if (!ok) break;
         umma_commit(&acc_full[a]);
@@ -710,7 +709,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, i++) {
       const int a = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1;
-      const int split = tile / p.tiles_mn, tmn = tile - split * p.tiles_mn;
+      const int split = p.ksplit > 1 ? tile / p.tiles_mn : 0, tmn = tile - split * p.tiles_mn;
       const int mt = (int)p.div_tiles_n.div((uint32_t)tmn), nt = tmn - mt * p.tiles_n;
       // This thread's output row, and for A_TAPS its pixel.
       int m = -1, oy = 0, ox = 0;
