@@ -145,6 +145,13 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Resident weights do not depend on the previous kernel: every chunk
+  // once, on the first weight barrier, before the wait.
+  if (L::RES && threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar[MB_W_FULL], (uint32_t)(CHUNKS * L::STAGE));
+    for (int j = 0; j < CHUNKS; j++)
+      bulk_load(Wst + j * L::STAGE, p.w + (size_t)j * L::STAGE, (uint32_t)L::STAGE, &bar[MB_W_FULL]);
+  }
   griddep_launch_dependents();
   griddep_wait();
 
@@ -154,11 +161,6 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
       prefetch_tensor_map(&x_map);
       bool ok = true;
       int i = 0;
-      if (L::RES) {  // every chunk once, on the first weight barrier
-        mbar_arrive_expect_tx(&bar[MB_W_FULL], (uint32_t)(CHUNKS * L::STAGE));
-        for (int j = 0; j < CHUNKS; j++)
-          bulk_load(Wst + j * L::STAGE, p.w + (size_t)j * L::STAGE, (uint32_t)L::STAGE, &bar[MB_W_FULL]);
-      }
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, i++) {
         const int xb = i % L::XB;
         const uint32_t xph = (uint32_t)(i / L::XB) & 1;
