@@ -56,10 +56,24 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// The window projection fused after P V (one head, c = 32): the output's
+// rows times W (32 x 32, f16, pre-packed as each lane's mma.sync B
+// fragments) plus the bias, added onto the map's pixels the window's tokens
+// came from (swin.rs:176-181), as the separate projection's window-scatter
+// epilogue adds them.
+struct AttnProjArgs {
+  const uint4* frag;   // [lane][2 k steps][4 n tiles][2] u32: 4 uint4 per lane
+  const float* bias;   // [32]
+  __half* y;           // planar map, the head's channels from plane plane0
+  long long y_plane;
+  int plane0;
+  WindowMap wm;
+};
+
 __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __restrict__ qkv, long long qkv_plane,
                                                                int c, const float* __restrict__ bias, int shifted,
                                                                int rows_w, int cols_w, __half* __restrict__ out,
-                                                               long long out_plane, int* dev_err) {
+                                                               long long out_plane, int* dev_err, AttnProjArgs pj) {
   // Q, K, V of this head as 12 planes of [64 tokens][8]: plane 4 w + g is
   // channel group g of q (w 0), k (1) or v (2). Each is a contiguous 1 KB
   // run of the planar qkv map, brought by one bulk copy (the 8 x 8 blocks
@@ -171,6 +185,54 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
     }
   }
   const float inv[2] = {1.0f / sum[0], 1.0f / sum[1]};
+  if (pj.frag) {
+    // O as f16 A fragments (rounded where the separate launch stores it),
+    // the head's 32 dims the reduction: two k steps of 16.
+    uint32_t oa[2][4];
+#pragma unroll
+    for (int kk = 0; kk < 2; kk++) {
+      oa[kk][0] = pack_half2(o[2 * kk][0] * inv[0], o[2 * kk][1] * inv[0]);
+      oa[kk][1] = pack_half2(o[2 * kk][2] * inv[1], o[2 * kk][3] * inv[1]);
+      oa[kk][2] = pack_half2(o[2 * kk + 1][0] * inv[0], o[2 * kk + 1][1] * inv[0]);
+      oa[kk][3] = pack_half2(o[2 * kk + 1][2] * inv[1], o[2 * kk + 1][3] * inv[1]);
+    }
+    uint32_t bw[16];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint4 u = __ldg(pj.frag + lane * 4 + q);
+      bw[4 * q] = u.x;
+      bw[4 * q + 1] = u.y;
+      bw[4 * q + 2] = u.z;
+      bw[4 * q + 3] = u.w;
+    }
+    float pr[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      pr[j][0] = pr[j][1] = pr[j][2] = pr[j][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 2; kk++)
+        mma16816(pr[j], oa[kk][0], oa[kk][1], oa[kk][2], oa[kk][3], bw[(kk * 4 + j) * 2], bw[(kk * 4 + j) * 2 + 1]);
+    }
+    // rows g and g + 8 of the warp's 16: window tokens q0 + g + 8 h
+    const WindowMap& wm = pj.wm;
+    const int ws = wm.ws, cols = wm.pad_w / ws, wy = win / cols, wx = win - wy * cols;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int tk = q0 + g + 8 * h;
+      const int py = (wy * ws + tk / ws + wm.shift) % wm.pad_h, px = (wx * ws + tk % ws + wm.shift) % wm.pad_w;
+      if (tk >= ws * ws || py >= wm.map_h || px >= wm.map_w) continue;
+      const long long dest = (long long)py * wm.map_w + px;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int n = 8 * j + 2 * t;
+        __half2* at = reinterpret_cast<__half2*>(pj.y + (pj.plane0 + j) * pj.y_plane + dest * 8 + 2 * t);
+        const float2 old = __half22float2(*at);
+        *at = __floats2half2_rn((pr[j][2 * h] + __ldg(pj.bias + n)) + old.x,
+                                (pr[j][2 * h + 1] + __ldg(pj.bias + n + 1)) + old.y);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 4; j++)
 #pragma unroll
@@ -214,9 +276,53 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
   const double heads = (double)windows * (c / 32);
   timed_launch("window_attention_kernel", heads * 4.0 * 64 * 64 * 32, (double)windows * 64 * 4 * c * 2, s, [&] {
     launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w,
-               out, out_plane_elems, dev_err);
+               out, out_plane_elems, dev_err, AttnProjArgs{});
     IEC_CUDA(cudaGetLastError());
   });
+}
+
+void pack_attn_proj(AttnProj& ap, const std::vector<float>& w, const std::vector<float>& b) {
+  if (w.size() != 32 * 32 || b.size() != 32) throw Error(ERR_WEIGHTS, "fused window projection: 32 x 32 weights");
+  // lane l = 4 g + t, k step kk, n tile j: b0 = W[16 kk + 2 t (+1)][8 j + g],
+  // b1 = W[16 kk + 2 t + 8 (+9)][8 j + g], each a pair of f16 (low = lower k)
+  std::vector<uint16_t> frag(32 * 2 * 4 * 2 * 2);
+  for (int l = 0; l < 32; l++)
+    for (int kk = 0; kk < 2; kk++)
+      for (int j = 0; j < 4; j++)
+        for (int r = 0; r < 2; r++) {
+          const int g = l >> 2, t = l & 3, k = 16 * kk + 2 * t + 8 * r, n = 8 * j + g;
+          const size_t at = ((((size_t)l * 2 + kk) * 4 + j) * 2 + r) * 2;
+          frag[at] = f32_to_half(w[(size_t)k * 32 + n]);
+          frag[at + 1] = f32_to_half(w[(size_t)(k + 1) * 32 + n]);
+        }
+  ap.frag.reserve(frag.size() * 2);
+  IEC_CUDA(cudaMemcpy(ap.frag.get(), frag.data(), frag.size() * 2, cudaMemcpyHostToDevice));
+  ap.bias.reserve(32 * 4);
+  IEC_CUDA(cudaMemcpy(ap.bias.get(), b.data(), 32 * 4, cudaMemcpyHostToDevice));
+}
+
+void window_attention_proj(const __half* qkv, long long qkv_plane_elems, int windows, const float* bias, bool shifted,
+                           int rows_w, int cols_w, const AttnProj& ap, __half* y, long long y_plane_elems, int plane0,
+                           const WindowMap& wm, int* dev_err, cudaStream_t s) {
+  if ((qkv_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "attention planes must be 16-byte multiples");
+  if (wm.ws < 1 || wm.ws > 8 || wm.pad_w % wm.ws || wm.pad_h % wm.ws || windows != (wm.pad_h / wm.ws) * (wm.pad_w / wm.ws))
+    throw Error(ERR_INPUT, "window partition geometry is inconsistent");
+  AttnProjArgs pj;
+  pj.frag = ap.frag.as<uint4>();
+  pj.bias = ap.bias.as<float>();
+  pj.y = y;
+  pj.y_plane = y_plane_elems;
+  pj.plane0 = plane0;
+  pj.wm = wm;
+  dim3 grid(windows, 1);
+  // attention as above, then the 64 x 32 x 32 projection per window; bytes:
+  // q, k, v read once, the map's old values read and written (f16)
+  timed_launch("window_attention_proj", (double)windows * (4.0 * 64 * 64 * 32 + 2.0 * 64 * 32 * 32),
+               (double)windows * 64 * (3 * 32 + 2 * 32) * 2, s, [&] {
+                 launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, 32, bias, shifted ? 1 : 0,
+                            rows_w, cols_w, static_cast<__half*>(nullptr), 0LL, dev_err, pj);
+                 IEC_CUDA(cudaGetLastError());
+               });
 }
 
 }  // namespace iec

@@ -19,6 +19,7 @@ struct Scunet::Block {
   int c = 0, h = 0;
   bool shifted = false;
   PackedWeights split, conv1, conv2, join, qkv, proj, fc1, fc2;
+  AttnProj proj_fused;  // the projection for the fused attention (one head only)
   MlpWeights mlp;  // LN2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
   LnRowsWeights lnqkv;  // LN1 + window partition + qkv (lnrows_sm100.cuh), where the width fits
   DeviceBuffer ln1g, ln1b, ln2g, ln2b, bias;  // LN params f32; attention bias tables f32
@@ -190,7 +191,12 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
       if (lnrows_fits(h, 3 * h)) pack_lnrows(b.lnqkv, h, 3 * h, wq.values, bq, g1, be1);
     }
     upload(b.bias, attention_bias_layout(bias_tables(f.take(t + ".msa.position_bias", {(size_t)(h / 32), 64, 64}), shifted)));
-    linear(f, b.proj, t + ".msa.linear", h, h, true);
+    {
+      HostTensor w = f.take_tensor(t + ".msa.linear.weight", {(size_t)h, (size_t)h});
+      const std::vector<float> pb = f.take(t + ".msa.linear.bias", {(size_t)h});
+      pack_weights(b.proj, w.values, 1, h, h, pb.data());
+      if (h == 32) pack_attn_proj(b.proj_fused, w.values, pb);
+    }
     {
       // LN2 and the MLP: the separate launches' weights, and the same values
       // packed for the fused MLP kernel.
@@ -379,14 +385,19 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
         o.plane0 = 0;
         gemm_rows(dev_, B.qkv, tok, pl, Pl, ACT_NONE, o, s);
       }
-      window_attention(qkv, pl, h, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, att, pl, dev_.dev_err(), s);
-      o.mode = OUT_WINDOW_ACCUM;
-      o.out = y;
-      o.plane0 = h / 8;
-      o.map_h = H;
-      o.map_w = W;
-      o.shift = shift;
-      gemm_rows(dev_, B.proj, att, pl, Pl, ACT_NONE, o, s);
+      if (fused_mlp_ && h == 32) {
+        window_attention_proj(qkv, pl, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, B.proj_fused, y, pl, h / 8,
+                              wm, dev_.dev_err(), s);
+      } else {
+        window_attention(qkv, pl, h, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, att, pl, dev_.dev_err(), s);
+        o.mode = OUT_WINDOW_ACCUM;
+        o.out = y;
+        o.plane0 = h / 8;
+        o.map_h = H;
+        o.map_w = W;
+        o.shift = shift;
+        gemm_rows(dev_, B.proj, att, pl, Pl, ACT_NONE, o, s);
+      }
       // MLP (swin.rs:222-254): y[h:] += fc2(gelu(fc1(LN2(y[h:])))).
       if (fused_mlp_ && B.mlp.c == h && mlp_preferred(h)) {
         mlp_planar(dev_, B.mlp, y + (long long)(h / 8) * pl, pl, Pl, s);

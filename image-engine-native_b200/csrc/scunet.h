@@ -46,9 +46,10 @@ class Scunet {
 
   DeviceBuffer host_in, host_out;
 
-  // Each transformer MLP runs fused (the default: LayerNorm, fc1, GELU and
-  // fc2 in one kernel, mlp_sm100.cuh) or as a LayerNorm launch and two GEMMs
-  // (for comparisons).
+  // Each transformer block runs fused (the default: LN1 folded into the qkv
+  // product, the one-head window projection inside the attention kernel,
+  // LayerNorm, fc1, GELU and fc2 in one kernel) or as LayerNorm launches and
+  // GEMMs (for comparisons).
   void set_fused(bool on) {
     fused_mlp_ = on;
     alloc_gen_++;  // no captured pass of the other path replays
