@@ -5,6 +5,7 @@
 #include <algorithm>
 
 #include "igemm_sm100.cuh"
+#include "joinsplit_sm100.cuh"
 #include "mlp_sm100.cuh"
 #include "lnrows_sm100.cuh"
 
@@ -373,6 +374,80 @@ void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_el
       case 256: return launch_mlp<256>(dev, map, p, s);
       default: return launch_mlp<384>(dev, map, p, s);
     }
+  });
+}
+
+bool joinsplit_fits(int c) { return c == 64 || c == 128; }
+
+void pack_joinsplit(JoinSplitWeights& jw, int c, const std::vector<float>& wj, const std::vector<float>& bj,
+                    const std::vector<float>& ws, const std::vector<float>& bs) {
+  if (!joinsplit_fits(c)) throw Error(ERR_INPUT, "fused join and split of " + std::to_string(c) + " channels");
+  const size_t cc = (size_t)c * c;
+  if (wj.size() != cc || ws.size() != cc || bj.size() != (size_t)c || bs.size() != (size_t)c)
+    throw Error(ERR_WEIGHTS, "join and split weights of the wrong size");
+  // each matrix as [c / 8][c][8]: the core-matrix image of a B operand of K c
+  std::vector<uint16_t> w(2 * cc);
+  size_t at = 0;
+  for (const std::vector<float>* m : {&wj, &ws})
+    for (int g = 0; g < c / 8; g++)
+      for (int n = 0; n < c; n++)
+        for (int e = 0; e < 8; e++) w[at++] = f32_to_half((*m)[(size_t)(8 * g + e) * c + n]);
+  std::vector<float> b(bj);
+  b.insert(b.end(), bs.begin(), bs.end());
+  jw.c = c;
+  jw.w.reserve(w.size() * 2);
+  jw.bias.reserve(b.size() * 4);
+  IEC_CUDA(cudaMemcpy(jw.w.get(), w.data(), w.size() * 2, cudaMemcpyHostToDevice));
+  IEC_CUDA(cudaMemcpy(jw.bias.get(), b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+}
+
+namespace {
+
+template <int C>
+void launch_joinsplit(Device& dev, const CUtensorMap& ymap, const CUtensorMap& xmap, const JoinSplitParams& p,
+                      cudaStream_t s) {
+  using L = JoinSplitSmem<C>;
+  static bool prepared[64] = {};
+  if (!prepared[dev.ordinal() & 63]) {
+    IEC_CUDA(cudaFuncSetAttribute(joinsplit_sm100<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    prepared[dev.ordinal() & 63] = true;
+  }
+  launch_pdl(joinsplit_sm100<C>, std::min(p.tiles, dev.sms() * L::CTAS), L::THREADS, (size_t)L::TOTAL, s, ymap,
+             xmap, p);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+void joinsplit_planar(Device& dev, const JoinSplitWeights& jw, __half* x, __half* y, long long plane_elems, int rows,
+                      cudaStream_t s) {
+  const int c = jw.c;
+  if (!joinsplit_fits(c) || rows <= 0) throw Error(ERR_INPUT, "fused join and split shape");
+  const int alloc = gemm_rows_alloc(rows);
+  if (plane_elems < (long long)alloc * 8) throw Error(ERR_INPUT, "join and split planes too short");
+  // the A_ROWS box of gemm_rows with every channel group in one box, for
+  // both maps
+  CUtensorMap ymap, xmap;
+  const uint64_t dims[3] = {128, (uint64_t)alloc / 16, (uint64_t)c / 8};
+  const uint64_t strides[2] = {256, (uint64_t)plane_elems * 2};
+  const uint32_t box[3] = {128, 8, (uint32_t)c / 8};
+  encode_tensor_map(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, y, dims, strides, box);
+  encode_tensor_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, x, dims, strides, box);
+  JoinSplitParams p{};
+  p.M = rows;
+  p.tiles = (rows + 127) / 128;
+  p.x = x;
+  p.y = y;
+  p.plane_elems = plane_elems;
+  p.w = jw.w.as<uint8_t>();
+  p.bias = jw.bias.as<float>();
+  p.dev_err = dev.dev_err();
+  char name[64];
+  snprintf(name, sizeof name, "joinsplit_sm100<%d> %dx%d", c, rows, c);
+  // FLOPs of both products; bytes: y and x read and written, the weights
+  timed_launch(name, 4.0 * rows * c * c, (double)rows * c * 8 + 4.0 * c * c, s, [&] {
+    if (c == 64) return launch_joinsplit<64>(dev, ymap, xmap, p, s);
+    return launch_joinsplit<128>(dev, ymap, xmap, p, s);
   });
 }
 

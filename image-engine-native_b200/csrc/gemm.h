@@ -143,6 +143,22 @@ void pack_mlp(MlpWeights& mw, int c, const std::vector<float>& w1, const std::ve
               const std::vector<float>& beta);
 void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_elems, int rows, cudaStream_t s);
 
+// SCUNet's block boundary in one kernel (joinsplit_sm100.cuh): x += y Wj +
+// bj, then y = x Ws + bs (the rounded f16 x, as separate launches read it
+// back), over `rows` rows of the C channels at `x` and `y` (planar, plane
+// stride plane_elems, planes of at least gemm_rows_alloc(rows) rows), C in
+// {64, 128}.
+struct JoinSplitWeights {
+  int c = 0;
+  DeviceBuffer w, bias;
+};
+bool joinsplit_fits(int c);
+// wj, ws: c x c (row k, column n); bj, bs: c.
+void pack_joinsplit(JoinSplitWeights& jw, int c, const std::vector<float>& wj, const std::vector<float>& bj,
+                    const std::vector<float>& ws, const std::vector<float>& bs);
+void joinsplit_planar(Device& dev, const JoinSplitWeights& jw, __half* x, __half* y, long long plane_elems, int rows,
+                      cudaStream_t s);
+
 // LayerNorm and the window partition folded into one product
 // (lnrows_sm100.cuh): out row r (window order, as layer_norm_planar's
 // window mode writes) = LN(src[pixel(r)]) x W + b over `rows` rows, for the

@@ -20,6 +20,7 @@ struct Scunet::Block {
   bool shifted = false;
   PackedWeights split, conv1, conv2, join, qkv, proj, fc1, fc2;
   AttnProj proj_fused;  // the projection for the fused attention (one head only)
+  JoinSplitWeights joinsplit;  // this block's join and the next one's split in one kernel, where the width fits
   MlpWeights mlp;  // LN2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
   LnRowsWeights lnqkv;  // LN1 + window partition + qkv (lnrows_sm100.cuh), where the width fits
   DeviceBuffer ln1g, ln1b, ln2g, ln2b, bias;  // LN params f32; attention bias tables f32
@@ -43,11 +44,21 @@ void upload(DeviceBuffer& b, const std::vector<float>& v) {
   IEC_CUDA(cudaMemcpy(b.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
 }
 
-void linear(WeightFile& f, PackedWeights& pw, const std::string& name, int k, int n, bool bias) {
+// A 1x1 layer's host values, kept where another kernel packs them again.
+struct Linear {
+  std::vector<float> w, b;
+};
+
+void linear(WeightFile& f, PackedWeights& pw, const std::string& name, int k, int n, bool bias,
+            Linear* keep = nullptr) {
   HostTensor w = f.take_tensor(name + ".weight", {(size_t)k, (size_t)n});
   std::vector<float> b;
   if (bias) b = f.take(name + ".bias", {(size_t)n});
   pack_weights(pw, w.values, 1, k, n, bias ? b.data() : nullptr);
+  if (keep) {
+    keep->w = std::move(w.values);
+    keep->b = std::move(b);
+  }
 }
 
 void conv3(WeightFile& f, PackedWeights& pw, const std::string& name, int cin, int cout, int cin_pad) {
@@ -169,12 +180,12 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
   WeightFile f = WeightFile::read(path, std::string("SCUNET\0\0", 8).c_str());
   DeviceScope scope(dev_);
   conv3(f, head_, "m_head.0", 3, DIM, 16);
-  auto load_block = [&](Block& b, const std::string& name, int c, bool shifted) {
+  auto load_block = [&](Block& b, const std::string& name, int c, bool shifted, Linear* split, Linear* join) {
     b.c = c;
     b.h = c / 2;
     b.shifted = shifted;
     const int h = b.h;
-    linear(f, b.split, name + ".conv1_1", c, c, true);
+    linear(f, b.split, name + ".conv1_1", c, c, true, split);
     conv3(f, b.conv1, name + ".conv_block.0", h, h, h);
     conv3(f, b.conv2, name + ".conv_block.2", h, h, h);
     const std::string t = name + ".trans_block";
@@ -211,12 +222,18 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
       pack_weights(b.fc2, w2.values, 1, 4 * h, h, bb2.data());
       if (mlp_fits(h)) pack_mlp(b.mlp, h, w1.values, bb1, w2.values, bb2, g2, be2);
     }
-    linear(f, b.join, name + ".conv1_2", c, c, true);
+    linear(f, b.join, name + ".conv1_2", c, c, true, join);
   };
   auto load_level = [&](Level& L, const std::string& name, int first, int c) {
     L.c = c;
     L.blocks.resize(BLOCKS);
-    for (int b = 0; b < BLOCKS; b++) load_block(L.blocks[b], name + "." + std::to_string(first + b), c, b % 2 == 1);
+    std::vector<Linear> splits(BLOCKS), joins(BLOCKS);
+    for (int b = 0; b < BLOCKS; b++)
+      load_block(L.blocks[b], name + "." + std::to_string(first + b), c, b % 2 == 1, &splits[b], &joins[b]);
+    // a block's join with the next block's split, for the fused boundary
+    if (joinsplit_fits(c))
+      for (int b = 0; b + 1 < BLOCKS; b++)
+        pack_joinsplit(L.blocks[b].joinsplit, c, joins[b].w, joins[b].b, splits[b + 1].w, splits[b + 1].b);
   };
   const int widths[3] = {DIM, 2 * DIM, 4 * DIM};
   for (int i = 0; i < 3; i++) {
@@ -414,14 +431,18 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       }
       // x += join(y); y = next split(x) (network.rs:190-212).
       IEC_CUDA(cudaStreamWaitEvent(s, ev_conv_, 0));
-      o.mode = OUT_ACCUM;
-      o.out = x;
-      o.plane0 = 0;
-      gemm_rows(dev_, B.join, y, pl, Pl, ACT_NONE, o, s);
-      if (b + 1 < BLOCKS) {
-        o.mode = OUT_STORE;
-        o.out = y;
-        gemm_rows(dev_, L.blocks[b + 1].split, x, pl, Pl, ACT_NONE, o, s);
+      if (fused_mlp_ && b + 1 < BLOCKS && B.joinsplit.c == c) {
+        joinsplit_planar(dev_, B.joinsplit, x, y, pl, Pl, s);
+      } else {
+        o.mode = OUT_ACCUM;
+        o.out = x;
+        o.plane0 = 0;
+        gemm_rows(dev_, B.join, y, pl, Pl, ACT_NONE, o, s);
+        if (b + 1 < BLOCKS) {
+          o.mode = OUT_STORE;
+          o.out = y;
+          gemm_rows(dev_, L.blocks[b + 1].split, x, pl, Pl, ACT_NONE, o, s);
+        }
       }
       block_done();
     }

@@ -64,6 +64,72 @@ extern "C" iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int
   }
 }
 
+extern "C" iec_status iec_selftest_joinsplit(int device, int rows, int c, const float* wj, const float* bj,
+                                             const float* ws, const float* bs, int fused, float* x, float* y,
+                                             int iters, float* us) {
+  try {
+    Options opt;
+    opt.device = device;
+    Device dev(opt);
+    DeviceScope scope(dev);
+    const size_t cc = (size_t)c * c;
+    const std::vector<float> vwj(wj, wj + cc), vws(ws, ws + cc), vbj(bj, bj + c), vbs(bs, bs + c);
+    PackedWeights pj, ps;
+    pack_weights(pj, vwj, 1, c, c, bj);
+    pack_weights(ps, vws, 1, c, c, bs);
+    JoinSplitWeights jw;
+    if (fused) pack_joinsplit(jw, c, vwj, vbj, vws, vbs);
+    const long long plane = (long long)gemm_rows_alloc(rows) * 8;
+    DeviceBuffer d32, dx, dy;
+    d32.reserve((size_t)rows * c * 4);
+    dx.reserve((size_t)plane * c / 8 * 2);
+    dy.reserve((size_t)plane * c / 8 * 2);
+    cudaStream_t s = dev.stream();
+    for (int v = 0; v < 2; v++) {
+      IEC_CUDA(cudaMemcpyAsync(d32.get(), v ? y : x, (size_t)rows * c * 4, cudaMemcpyHostToDevice, s));
+      rows_to_planar(d32.as<float>(), rows, c, (v ? dy : dx).as<__half>(), plane, s);
+    }
+    auto run = [&] {
+      if (fused) {
+        joinsplit_planar(dev, jw, dx.as<__half>(), dy.as<__half>(), plane, rows, s);
+        return;
+      }
+      GemmOutSpec o;
+      o.plane_elems = plane;
+      o.mode = OUT_ACCUM;
+      o.out = dx.as<__half>();
+      gemm_rows(dev, pj, dy.as<__half>(), plane, rows, ACT_NONE, o, s);
+      o.mode = OUT_STORE;
+      o.out = dy.as<__half>();
+      gemm_rows(dev, ps, dx.as<__half>(), plane, rows, ACT_NONE, o, s);
+    };
+    run();
+    for (int v = 0; v < 2; v++) {
+      planar_to_rows((v ? dy : dx).as<__half>(), plane, rows, c, d32.as<float>(), s);
+      IEC_CUDA(cudaMemcpyAsync(v ? y : x, d32.get(), (size_t)rows * c * 4, cudaMemcpyDeviceToHost, s));
+    }
+    dev.sync(s);
+    if (iters > 0 && us) {
+      // the timed launches keep rewriting the buffers; their values are not read
+      cudaEvent_t e0, e1;
+      IEC_CUDA(cudaEventCreate(&e0));
+      IEC_CUDA(cudaEventCreate(&e1));
+      IEC_CUDA(cudaEventRecord(e0, s));
+      for (int i = 0; i < iters; i++) run();
+      IEC_CUDA(cudaEventRecord(e1, s));
+      IEC_CUDA(cudaEventSynchronize(e1));
+      float ms = 0.0f;
+      IEC_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+      us[0] = ms * 1000.0f / (float)iters;
+      IEC_CUDA(cudaEventDestroy(e0));
+      IEC_CUDA(cudaEventDestroy(e1));
+    }
+    return IEC_OK;
+  } catch (const Error& e) {
+    return (iec_status)e.code;
+  }
+}
+
 extern "C" iec_status iec_selftest_conv(int device, int h, int w, int k, int n, int size, int halo, const float* a,
                                         const float* weights, const float* bias, int act, float* out, int iters,
                                         float* us) {

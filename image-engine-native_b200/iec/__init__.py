@@ -93,6 +93,7 @@ def lib():
         L.iec_realesrgan_launches.restype = sz
         i32 = ctypes.c_int
         L.iec_selftest_gemm.argtypes = [i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, i32, f32p]
+        L.iec_selftest_joinsplit.argtypes = [i32, i32, i32, f32p, f32p, f32p, f32p, i32, f32p, f32p, i32, f32p]
         L.iec_selftest_mma_rate.argtypes = [i32, i32, i32, f32p]
         L.iec_selftest_conv.argtypes = [i32, i32, i32, i32, i32, i32, i32, f32p, f32p, f32p, i32, f32p, i32, f32p]
         L.iec_selftest_rfft2.argtypes = [ctypes.c_int, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -296,6 +297,21 @@ def selftest_gemm(a, w, bias=None, *, conv=False, shape=None, act=0, accumulate_
                                  _f32(b) if b is not None else None, act, int(accumulate_onto is not None), _f32(out))
     _check(st)
     return out
+
+
+def selftest_joinsplit(x, y, wj, bj, ws, bs, *, fused=True, iters=0, device=0):
+    """Diagnostics: SCUNet's block boundary x += y wj + bj; y = x ws + bs on
+    host arrays (rows x c, c x c, c). fused runs the one-kernel form (c 64 or
+    128), else two GEMM launches. Returns (x, y, microseconds per pass or
+    None)."""
+    x = np.ascontiguousarray(x, np.float32).copy()
+    y = np.ascontiguousarray(y, np.float32).copy()
+    rows, c = x.shape
+    us = np.zeros(1, np.float32)
+    args = [np.ascontiguousarray(v, np.float32) for v in (wj, bj, ws, bs)]
+    _check(lib().iec_selftest_joinsplit(device, rows, c, *[_f32(v) for v in args], int(fused), _f32(x), _f32(y),
+                                        iters, _f32(us) if iters > 0 else None))
+    return x, y, (float(us[0]) if iters > 0 else None)
 
 
 def selftest_conv(a, w, bias=None, *, size=3, halo=-1, act=0, iters=0, device=0):

@@ -351,6 +351,15 @@ iec_status iec_selftest_gemm(int device, int conv, int rows_or_h, int w, int k, 
 iec_status iec_selftest_conv(int device, int h, int w, int k, int n, int size, int halo, const float* a,
                              const float* weights, const float* bias, int act, float* out, int iters, float* us);
 
+/* Diagnostics: SCUNet's block boundary on host arrays `x` and `y` (rows x c
+ * each, rounded to f16 on the way in, overwritten with the results): x += y wj
+ * + bj, then y = x ws + bs (wj, ws c x c row-major, row k column n). fused
+ * non-zero runs the one-kernel form (c 64 or 128), 0 two GEMM launches. With
+ * iters > 0 and `us` non-null, us[0] gets the device microseconds per pass
+ * over `iters` passes after the checked one. */
+iec_status iec_selftest_joinsplit(int device, int rows, int c, const float* wj, const float* bj, const float* ws,
+                                  const float* bs, int fused, float* x, float* y, int iters, float* us);
+
 /* Diagnostics: the issue rate of tcgen05.mma kind::f16 128 x n x 16 (n 32,
  * 64, 96, 128, 192, 224 or 256) on zeroed no-swizzle operands, one CTA per
  * SM: *cycles_per_mma = SM cycles per MMA. variant 0 issues unrolled MMAs

@@ -101,3 +101,31 @@ def test_mma_rate_diagnostic_runs():
         for variant in (0, 1):
             c = iec.selftest_mma_rate(n, variant)
             assert np.isfinite(c) and c > 0
+
+
+@pytest.mark.parametrize("rows,c", [(1000, 64), (128 * 37, 64), (300, 128), (128 * 41 + 7, 128), (49152, 64)])
+def test_joinsplit_matches_separate_launches_and_oracle(rows, c):
+    """SCUNet's fused block boundary (x += y Wj + bj; y = x Ws + bs in one
+    kernel) equals the join and split as two GEMM launches bit for bit, and
+    both follow the oracle's multiply (network.rs:190-212: conv1_2, the
+    residual add, conv1_1 of the next block; f16 between the steps)."""
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(rows + c)
+    x = f16(rng.standard_normal((rows, c)))
+    y = f16(rng.standard_normal((rows, c)))
+    wj = f16(rng.standard_normal((c, c)) / np.sqrt(c))
+    ws = f16(rng.standard_normal((c, c)) / np.sqrt(c))
+    bj = rng.uniform(-0.5, 0.5, c).astype(np.float32)
+    bs = rng.uniform(-0.5, 0.5, c).astype(np.float32)
+    fx, fy, _ = iec.selftest_joinsplit(x, y, wj, bj, ws, bs, fused=True)
+    sx, sy, _ = iec.selftest_joinsplit(x, y, wj, bj, ws, bs, fused=False)
+    assert np.array_equal(fx.view(np.uint32), sx.view(np.uint32)), float(np.abs(fx - sx).max())
+    assert np.array_equal(fy.view(np.uint32), sy.view(np.uint32)), float(np.abs(fy - sy).max())
+    if rows <= 5000:
+        want_x = f16(refcpu.multiply(y.ravel(), wj, bj, kind="rows", out=x.ravel().copy(),
+                                     accumulate=True).reshape(rows, c))
+        want_y = refcpu.multiply(fx.ravel(), ws, bs, kind="rows").reshape(rows, c)
+        close(fx, want_x)
+        close(fy, want_y)
