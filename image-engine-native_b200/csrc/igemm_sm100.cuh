@@ -182,17 +182,24 @@ __device__ __forceinline__ uint4 pack_half8(const float* w) {
 // Sigmoid stays out of line (and GELU compact): inlined into every element of
 // the unrolled epilogue they made its loop body too large for the
 // instruction cache, and the common ReLU / identity path would pay for them.
-// erf by Abramowitz & Stegun 7.1.28: erf(a) = 1 - (1 + a1 a + ... + a6 a^6)^-16
-// for a >= 0, |error| <= 3e-7 in exact arithmetic, 1.8e-6 in f32 (the 16th
-// power multiplies the polynomial's rounding; f16 outputs round at 4.9e-4
-// relative). One MUFU operation per value, where 7.1.26 needs two (a reciprocal and an
-// exponential): the fused MLP's hidden layer, 16,384 GELUs per 128-row tile,
-// is bound by those. |x| is clamped at 4, where erf already rounds to 1 in
-// f32, so the 16th power cannot overflow. Compact enough to stay inline in
-// the epilogue (an IEEE division here cost more than the rest of the
-// activation).
-__device__ __forceinline__ float gemm_erf(float x) {
-  const float a = fminf(fabsf(x), 4.0f);
+// GELU(v) = v Phi(v) = max(v, 0) - |v| (1 - erf(|v| / sqrt 2)) / 2, with erf
+// by Abramowitz & Stegun 7.1.28: 1 - erf(a) = P(a)^-16 for a >= 0, P(a) = 1 +
+// a1 a + ... + a6 a^6 (|error| <= 3e-7 in exact arithmetic). So
+//   GELU(v) = max(v, 0) - |v| / (2 P(a)^16),  a = |v| / sqrt 2:
+// one MUFU reciprocal per value (7.1.26 needs a reciprocal and an
+// exponential; the fused MLP's hidden layer, 16,384 GELUs per 128-row tile,
+// is bound by this arithmetic), and for negative v no cancellation between
+// 1 and erf. Past a of about 13 the 16th power overflows to +inf, whose
+// approximate reciprocal is +0 (PTX rcp.approx), which is the limit: GELU(v)
+// = max(v, 0). Compact enough to stay inline in the epilogue (an IEEE
+// division here cost more than the rest of the activation).
+__device__ __forceinline__ float gelu_rcp(float q) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(q));
+  return r;
+}
+__device__ __forceinline__ float gemm_gelu(float v) {
+  const float av = fabsf(v), a = av * 0.70710678118654752f;
   float q = fmaf(fmaf(fmaf(fmaf(fmaf(fmaf(4.30638e-5f, a, 2.765672e-4f), a, 1.520143e-4f), a, 9.2705272e-3f), a,
                           4.22820123e-2f),
                      a, 7.05230784e-2f),
@@ -201,17 +208,16 @@ __device__ __forceinline__ float gemm_erf(float x) {
   q *= q;
   q *= q;
   q *= q;
-  return copysignf(1.0f - __fdividef(1.0f, q), x);
+  return fmaf(-0.5f * av, gelu_rcp(q), fmaxf(v, 0.0f));
 }
-__device__ __forceinline__ float gemm_gelu(float v) { return 0.5f * v * (1.0f + gemm_erf(v * 0.70710678118654752f)); }
 
 // The same GELU for two values, its multiplies and fused multiply-adds on
-// packed f32 pairs (each lane the scalar operation), half the FP32
-// instructions of two calls; the reciprocal stays per value.
+// packed f32 pairs (each lane the scalar operation, so the results equal two
+// gemm_gelu calls), half the FP32 instructions; the reciprocal stays per value.
 __device__ __forceinline__ float2 gemm_gelu2(float2 v) {
   auto both = [](float c) { return make_float2(c, c); };
-  const float2 z = fmul2(v, both(0.70710678118654752f));
-  const float2 a = make_float2(fminf(fabsf(z.x), 4.0f), fminf(fabsf(z.y), 4.0f));
+  const float2 av = make_float2(fabsf(v.x), fabsf(v.y));
+  const float2 a = fmul2(av, both(0.70710678118654752f));
   float2 q = ffma2(both(4.30638e-5f), a, both(2.765672e-4f));
   q = ffma2(q, a, both(1.520143e-4f));
   q = ffma2(q, a, both(9.2705272e-3f));
@@ -222,9 +228,8 @@ __device__ __forceinline__ float2 gemm_gelu2(float2 v) {
   q = fmul2(q, q);
   q = fmul2(q, q);
   q = fmul2(q, q);
-  const float2 r = make_float2(1.0f - __fdividef(1.0f, q.x), 1.0f - __fdividef(1.0f, q.y));
-  const float2 erf = make_float2(copysignf(r.x, z.x), copysignf(r.y, z.y));
-  return fmul2(fmul2(both(0.5f), v), fadd2(both(1.0f), erf));
+  return ffma2(fmul2(both(-0.5f), av), make_float2(gelu_rcp(q.x), gelu_rcp(q.y)),
+               make_float2(fmaxf(v.x, 0.0f), fmaxf(v.y, 0.0f)));
 }
 
 static __device__ __noinline__ float gemm_sigmoid(float v) {

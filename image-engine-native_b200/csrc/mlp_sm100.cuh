@@ -356,12 +356,18 @@ __global__ void __launch_bounds__(MlpSmem<C>::THREADS, MlpSmem<C>::CTAS)
         }
         tmem_wait_ld();
         float v[COLS];
+        const float4* bias4 = reinterpret_cast<const float4*>(b1 + j * NH + part * COLS);
 #pragma unroll
-        for (int e = 0; e < COLS; e += 2) {
-          const float2 g2 = gemm_gelu2(make_float2(__uint_as_float(r[e]) + b1[j * NH + part * COLS + e],
-                                                   __uint_as_float(r[e + 1]) + b1[j * NH + part * COLS + e + 1]));
-          v[e] = g2.x;
-          v[e + 1] = g2.y;
+        for (int e = 0; e < COLS; e += 4) {
+          const float4 b = bias4[e / 4];
+          const float2 g0 = gemm_gelu2(
+              fadd2(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), make_float2(b.x, b.y)));
+          const float2 g1 = gemm_gelu2(
+              fadd2(make_float2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])), make_float2(b.z, b.w)));
+          v[e] = g0.x;
+          v[e + 1] = g0.y;
+          v[e + 2] = g1.x;
+          v[e + 3] = g1.y;
         }
         if (!mbar_wait(&bar[MB_H_EMPTY + b], ph ^ 1, abort_flag, p.dev_err, DEV_ERR_WAIT_ACC_EMPTY)) {
           ok = false;
