@@ -22,6 +22,7 @@
 #include "gemm.h"
 #include "sm100.cuh"
 
+#include <algorithm>
 #include <vector>
 
 namespace iec {
@@ -56,24 +57,115 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The window projection fused after P V (one head, c = 32): the output's
-// rows times W (32 x 32, f16, pre-packed as each lane's mma.sync B
-// fragments) plus the bias, added onto the map's pixels the window's tokens
-// came from (swin.rs:176-181), as the separate projection's window-scatter
-// epilogue adds them.
-struct AttnProjArgs {
-  const uint4* frag;   // [lane][2 k steps][4 n tiles][2] u32: 4 uint4 per lane
-  const float* bias;   // [32]
-  __half* y;           // planar map, the head's channels from plane plane0
-  long long y_plane;
-  int plane0;
-  WindowMap wm;
-};
+// One warp's 16 query rows (q0 .. q0 + 15) of one head over the window's 64
+// keys: S = Q K^T (Q as the A fragments of its two k steps of 16 dims),
+// scaled by 1 / sqrt(32), plus the bias (tb: the warp's entries of the
+// window class's table, attention_bias_layout), softmax with quad shuffles
+// for the row max and sum, O = P V (the accumulator fragments of S are the A
+// fragments of P). sk, sv: keys and values as [4 dim groups][64][8]. o is
+// unnormalised; inv holds the reciprocal sums of rows g and g + 8.
+__device__ __forceinline__ void attend16(const uint32_t (&qa)[2][4], const __half* sk, const __half* sv,
+                                         const float4* tb, int lane, float (&o)[4][4], float (&inv)[2]) {
+  // S = Q K^T: 8 key tiles of 8.
+  float s[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 2; kk++) {
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      // keys 8j .. 8j + 15, dims 16 kk .. 16 kk + 15: two B fragments
+      uint32_t b0, b1, b2, b3;
+      const int key = 8 * j + (lane & 7) + ((lane >> 4) << 3);
+      const int grp = kk * 2 + ((lane >> 3) & 1);  // dims 8 grp .. 8 grp + 7
+      ldsm_x4((uint32_t)__cvta_generic_to_shared(sk + grp * TOK * 8 + key * 8), b0, b1, b2, b3);
+      mma16816(s[j], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+      mma16816(s[j + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+    }
+  }
+  // Scale, bias, softmax (rows g and g + 8 of the warp's 16).
+  const float scale = 0.17677669529663688f;  // 1 / sqrt(32)
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const float4 b4 = __ldg(tb + j * 32);
+    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      s[j][e] = s[j][e] * scale + bv[e];
+      mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+  }
+  float sum[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      s[j][e] = __expf(s[j][e] - mx[e >> 1]);
+      sum[e >> 1] += s[j][e];
+    }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+  }
+  // O = P V: tokens are the reduction, 4 dim tiles of 8.
+#pragma unroll
+  for (int j = 0; j < 4; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    const uint32_t a0 = pack_half2(s[2 * kk][0], s[2 * kk][1]);
+    const uint32_t a1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
+    const uint32_t a2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    const uint32_t a3 = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      // tokens 16 kk .. 16 kk + 15, dims 8 j .. 8 j + 15, transposed
+      uint32_t b0, b1, b2, b3;
+      const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int grp = j + (lane >> 4);  // dims 8 grp .. 8 grp + 7
+      ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv + grp * TOK * 8 + tok * 8), b0, b1, b2, b3);
+      mma16816(o[j], a0, a1, a2, a3, b0, b1);
+      mma16816(o[j + 1], a0, a1, a2, a3, b2, b3);
+    }
+  }
+  inv[0] = 1.0f / sum[0];
+  inv[1] = 1.0f / sum[1];
+}
+
+// The window projection (32 x 32) of one warp's 16 rows: O normalised and
+// rounded to f16 (as the separate projection reads the attention output),
+// as A fragments over the head's 32 dims (two k steps), times W (bw: the
+// lane's B fragments from pack_attn_proj); pr rows g and g + 8, columns
+// 8 j + 2 t and 8 j + 2 t + 1.
+__device__ __forceinline__ void project16(const float (&o)[4][4], const float (&inv)[2], const uint32_t (&bw)[16],
+                                          float (&pr)[4][4]) {
+  uint32_t oa[2][4];
+#pragma unroll
+  for (int kk = 0; kk < 2; kk++) {
+    oa[kk][0] = pack_half2(o[2 * kk][0] * inv[0], o[2 * kk][1] * inv[0]);
+    oa[kk][1] = pack_half2(o[2 * kk][2] * inv[1], o[2 * kk][3] * inv[1]);
+    oa[kk][2] = pack_half2(o[2 * kk + 1][0] * inv[0], o[2 * kk + 1][1] * inv[0]);
+    oa[kk][3] = pack_half2(o[2 * kk + 1][2] * inv[1], o[2 * kk + 1][3] * inv[1]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    pr[j][0] = pr[j][1] = pr[j][2] = pr[j][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 2; kk++)
+      mma16816(pr[j], oa[kk][0], oa[kk][1], oa[kk][2], oa[kk][3], bw[(kk * 4 + j) * 2], bw[(kk * 4 + j) * 2 + 1]);
+  }
+}
 
 __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __restrict__ qkv, long long qkv_plane,
                                                                int c, const float* __restrict__ bias, int shifted,
                                                                int rows_w, int cols_w, __half* __restrict__ out,
-                                                               long long out_plane, int* dev_err, AttnProjArgs pj) {
+                                                               long long out_plane, int* dev_err) {
   // Q, K, V of this head as 12 planes of [64 tokens][8]: plane 4 w + g is
   // channel group g of q (w 0), k (1) or v (2). Each is a contiguous 1 KB
   // run of the planar qkv map, brought by one bulk copy (the 8 x 8 blocks
@@ -112,127 +204,14 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
 
   const int g = lane >> 2, t = lane & 3;
   const int q0 = warp * 16;
-  // S = Q K^T for this warp's 16 rows: 8 key tiles of 8.
-  float s[8][4];
+  // This warp's 16 query rows as the A fragments of two k steps.
+  uint32_t qa[2][4];
 #pragma unroll
-  for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
-#pragma unroll
-  for (int kk = 0; kk < 2; kk++) {
-    uint32_t a0, a1, a2, a3;
-    ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8), a0,
-            a1, a2, a3);
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      // keys 8j .. 8j + 15, dims 16 kk .. 16 kk + 15: two B fragments
-      uint32_t b0, b1, b2, b3;
-      const int key = 8 * j + (lane & 7) + ((lane >> 4) << 3);
-      const int grp = kk * 2 + ((lane >> 3) & 1);  // dims 8 grp .. 8 grp + 7
-      ldsm_x4((uint32_t)__cvta_generic_to_shared(sk + grp * TOK * 8 + key * 8), b0, b1, b2, b3);
-      mma16816(s[j], a0, a1, a2, a3, b0, b1);
-      mma16816(s[j + 1], a0, a1, a2, a3, b2, b3);
-    }
-  }
-  // Scale, bias, softmax (rows g and g + 8 of the warp's 16).
-  const float scale = 0.17677669529663688f;  // 1 / sqrt(32)
-  float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const float4 b4 = __ldg(tb + j * 32);
-    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      s[j][e] = s[j][e] * scale + bv[e];
-      mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-  }
-  float sum[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int j = 0; j < 8; j++)
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      s[j][e] = __expf(s[j][e] - mx[e >> 1]);
-      sum[e >> 1] += s[j][e];
-    }
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
-    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
-  }
-  // O = P V: tokens are the reduction, 4 dim tiles of 8.
-  float o[4][4];
-#pragma unroll
-  for (int j = 0; j < 4; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
-#pragma unroll
-  for (int kk = 0; kk < 4; kk++) {
-    const uint32_t a0 = pack_half2(s[2 * kk][0], s[2 * kk][1]);
-    const uint32_t a1 = pack_half2(s[2 * kk][2], s[2 * kk][3]);
-    const uint32_t a2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-    const uint32_t a3 = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-    for (int j = 0; j < 4; j += 2) {
-      // tokens 16 kk .. 16 kk + 15, dims 8 j .. 8 j + 15, transposed
-      uint32_t b0, b1, b2, b3;
-      const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int grp = j + (lane >> 4);  // dims 8 grp .. 8 grp + 7
-      ldsm_x4_t((uint32_t)__cvta_generic_to_shared(sv + grp * TOK * 8 + tok * 8), b0, b1, b2, b3);
-      mma16816(o[j], a0, a1, a2, a3, b0, b1);
-      mma16816(o[j + 1], a0, a1, a2, a3, b2, b3);
-    }
-  }
-  const float inv[2] = {1.0f / sum[0], 1.0f / sum[1]};
-  if (pj.frag) {
-    // O as f16 A fragments (rounded where the separate launch stores it),
-    // the head's 32 dims the reduction: two k steps of 16.
-    uint32_t oa[2][4];
-#pragma unroll
-    for (int kk = 0; kk < 2; kk++) {
-      oa[kk][0] = pack_half2(o[2 * kk][0] * inv[0], o[2 * kk][1] * inv[0]);
-      oa[kk][1] = pack_half2(o[2 * kk][2] * inv[1], o[2 * kk][3] * inv[1]);
-      oa[kk][2] = pack_half2(o[2 * kk + 1][0] * inv[0], o[2 * kk + 1][1] * inv[0]);
-      oa[kk][3] = pack_half2(o[2 * kk + 1][2] * inv[1], o[2 * kk + 1][3] * inv[1]);
-    }
-    uint32_t bw[16];
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const uint4 u = __ldg(pj.frag + lane * 4 + q);
-      bw[4 * q] = u.x;
-      bw[4 * q + 1] = u.y;
-      bw[4 * q + 2] = u.z;
-      bw[4 * q + 3] = u.w;
-    }
-    float pr[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      pr[j][0] = pr[j][1] = pr[j][2] = pr[j][3] = 0.0f;
-#pragma unroll
-      for (int kk = 0; kk < 2; kk++)
-        mma16816(pr[j], oa[kk][0], oa[kk][1], oa[kk][2], oa[kk][3], bw[(kk * 4 + j) * 2], bw[(kk * 4 + j) * 2 + 1]);
-    }
-    // rows g and g + 8 of the warp's 16: window tokens q0 + g + 8 h
-    const WindowMap& wm = pj.wm;
-    const int ws = wm.ws, cols = wm.pad_w / ws, wy = win / cols, wx = win - wy * cols;
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int tk = q0 + g + 8 * h;
-      const int py = (wy * ws + tk / ws + wm.shift) % wm.pad_h, px = (wx * ws + tk % ws + wm.shift) % wm.pad_w;
-      if (tk >= ws * ws || py >= wm.map_h || px >= wm.map_w) continue;
-      const long long dest = (long long)py * wm.map_w + px;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int n = 8 * j + 2 * t;
-        __half2* at = reinterpret_cast<__half2*>(pj.y + (pj.plane0 + j) * pj.y_plane + dest * 8 + 2 * t);
-        const float2 old = __half22float2(*at);
-        *at = __floats2half2_rn((pr[j][2 * h] + __ldg(pj.bias + n)) + old.x,
-                                (pr[j][2 * h + 1] + __ldg(pj.bias + n + 1)) + old.y);
-      }
-    }
-    return;
-  }
+  for (int kk = 0; kk < 2; kk++)
+    ldsm_x4((uint32_t)__cvta_generic_to_shared(sq + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8),
+            qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+  float o[4][4], inv[2];
+  attend16(qa, sk, sv, tb, lane, o, inv);
 #pragma unroll
   for (int j = 0; j < 4; j++)
 #pragma unroll
@@ -242,6 +221,216 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
       *reinterpret_cast<uint32_t*>(out + plane * out_plane + tok * 8 + 2 * t) =
           pack_half2(o[j][2 * h] * inv[h], o[j][2 * h + 1] * inv[h]);
     }
+}
+
+// A whole one-head window attention half in one persistent kernel (c = 32):
+//
+//   y[tokens] += proj(attention(qkv(LayerNorm(y[tokens]))))
+//
+// (crates/scunet-native/src/swin.rs:124-220: LN1, the shifted-window
+// partition, the qkv layer, attention with the position bias and shift
+// mask, the projection and the residual add, for one head of 32 channels).
+// Each CTA takes windows in turn; warp w owns tokens 16 w .. 16 w + 15 of
+// the window, two lanes per token:
+//   * the token's 32 channels arrive from its pixel (four 16-byte groups of
+//     the planar map; a window row's tokens are consecutive pixels), the
+//     next window's already in registers while this one is computed;
+//   * LayerNorm (eps 1e-5; mean, then the mean squared deviation) over the
+//     lane pair, the normalised f16 row and the raw row into shared memory
+//     (the warp's own rows: only __syncwarp between the steps); tokens past
+//     the map or the window's ws x ws are zero rows and are not stored;
+//   * qkv = row x Wqkv + b on mma.sync m16n8k16 (Wqkv resident in shared
+//     memory, [4][96][8]), rounded to f16 where the separate launches store
+//     it: Q stays in registers as the attention's A fragments, K and V go to
+//     one of two shared-memory buffers, one barrier per window;
+//   * attention, the projection and bias (attend16, project16), plus the
+//     raw row, stored to the token's pixel.
+// The qkv rows never reach global memory: per window 64 tokens x 32 channels
+// are read and written once.
+struct WindowBlockArgs {
+  __half* y;              // planar map, the head's channels in planes plane0 .. plane0 + 3
+  long long y_plane;
+  int plane0;
+  WindowMap wm;
+  int windows, rows_w, cols_w, shifted;
+  const uint8_t* wqkv;    // [4][96][8] f16 (the B operand of lnrows_sm100)
+  const float* params;    // gamma [32], beta [32], qkv bias [96]
+  const float* bias;      // attention bias tables (attention_bias_layout), one head
+  const uint4* pfrag;     // projection B fragments (pack_attn_proj)
+  const float* pbias;     // projection bias [32]
+};
+
+constexpr int WB_THREADS = 128;
+
+__global__ void __launch_bounds__(WB_THREADS, 4) window_block_kernel(const WindowBlockArgs a) {
+  __shared__ __align__(128) __half sw[4 * 96 * 8];        // Wqkv
+  __shared__ __align__(128) __half skv[2][8 * TOK * 8];   // K (groups 0..3) and V (4..7), two buffers
+  __shared__ __align__(128) __half sx[4 * TOK * 8];       // normalised rows [4][64][8]
+  __shared__ __align__(128) __half sraw[4 * TOK * 8];     // the rows as read
+  __shared__ __align__(16) float spar[32 + 32 + 96 + 32];  // gamma, beta, qkv bias, projection bias
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3, q0 = warp * 16;
+  // Weights first: no kernel writes them.
+  for (int i = (int)threadIdx.x; i < 4 * 96; i += WB_THREADS)
+    reinterpret_cast<uint4*>(sw)[i] = __ldg(reinterpret_cast<const uint4*>(a.wqkv) + i);
+  for (int i = (int)threadIdx.x; i < 160; i += WB_THREADS) spar[i] = __ldg(a.params + i);
+  if (threadIdx.x < 32) spar[160 + threadIdx.x] = __ldg(a.pbias + threadIdx.x);
+  uint32_t bw[16];
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const uint4 u = __ldg(a.pfrag + lane * 4 + q);
+    bw[4 * q] = u.x;
+    bw[4 * q + 1] = u.y;
+    bw[4 * q + 2] = u.z;
+    bw[4 * q + 3] = u.w;
+  }
+  __syncthreads();
+  griddep_wait();
+  griddep_launch_dependents();
+  const float* gamma = spar;
+  const float* beta = spar + 32;
+  const float* bqkv = spar + 64;
+  const float* bproj = spar + 160;
+  const WindowMap& wm = a.wm;
+  const int ws = wm.ws, cols = wm.pad_w / ws;
+  // This lane's token and channel half: token 16 w + lane / 2, channels
+  // 16 hp .. 16 hp + 15 (planes 2 hp, 2 hp + 1).
+  const int tk_own = q0 + (lane >> 1), hp = lane & 1;
+  // The pixel of token tk of window win, or -1 when the token is padding.
+  auto pixel = [&](int win, int tk) -> long long {
+    const int wy = win / cols, wx = win - wy * cols;
+    const int py = (wy * ws + tk / ws + wm.shift) % wm.pad_h, px = (wx * ws + tk % ws + wm.shift) % wm.pad_w;
+    if (tk >= ws * ws || py >= wm.map_h || px >= wm.map_w) return -1;
+    return (long long)py * wm.map_w + px;
+  };
+  auto fetch = [&](int win, uint4& u0, uint4& u1) {
+    u0 = u1 = make_uint4(0u, 0u, 0u, 0u);
+    if (win >= a.windows) return;
+    const long long px = pixel(win, tk_own);
+    if (px < 0) return;
+    const __half* at = a.y + (long long)(a.plane0 + 2 * hp) * a.y_plane + px * 8;
+    u0 = *reinterpret_cast<const uint4*>(at);
+    u1 = *reinterpret_cast<const uint4*>(at + a.y_plane);
+  };
+  uint4 u0, u1;
+  fetch(blockIdx.x, u0, u1);
+  int it = 0;
+  for (int win = blockIdx.x; win < a.windows; win += gridDim.x, it++) {
+    const bool valid = pixel(win, tk_own) >= 0;
+    // the next window's rows, in flight while this one is computed
+    uint4 n0, n1;
+    fetch(win + gridDim.x, n0, n1);
+    // LayerNorm over the lane pair's 32 channels (gemm.cu layer_norm_rows'
+    // formula), then the normalised and the raw row into shared memory.
+    {
+      float v[16];
+      const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
+      const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float2 f0 = __half22float2(h0[e]), f1 = __half22float2(h1[e]);
+        v[2 * e] = f0.x;
+        v[2 * e + 1] = f0.y;
+        v[8 + 2 * e] = f1.x;
+        v[8 + 2 * e + 1] = f1.y;
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 16; e++) sum += v[e];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      const float mean = sum / 32.0f;
+      float var = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 16; e++) var += (v[e] - mean) * (v[e] - mean);
+      var += __shfl_xor_sync(0xffffffffu, var, 1);
+      const float inv = 1.0f / sqrtf(var / 32.0f + 1e-5f);
+      float nv[16];
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        const int ch = 16 * hp + e;
+        nv[e] = valid ? (v[e] - mean) * inv * gamma[ch] + beta[ch] : 0.0f;
+      }
+      uint4* xr = reinterpret_cast<uint4*>(sx);
+      uint4* rr = reinterpret_cast<uint4*>(sraw);
+      xr[(2 * hp) * TOK + tk_own] = make_uint4(pack_half2(nv[0], nv[1]), pack_half2(nv[2], nv[3]),
+                                               pack_half2(nv[4], nv[5]), pack_half2(nv[6], nv[7]));
+      xr[(2 * hp + 1) * TOK + tk_own] = make_uint4(pack_half2(nv[8], nv[9]), pack_half2(nv[10], nv[11]),
+                                                   pack_half2(nv[12], nv[13]), pack_half2(nv[14], nv[15]));
+      rr[(2 * hp) * TOK + tk_own] = u0;
+      rr[(2 * hp + 1) * TOK + tk_own] = u1;
+    }
+    __syncwarp();
+    // qkv for the warp's 16 rows: 12 column tiles of 8, two k steps.
+    float acc[12][4];
+#pragma unroll
+    for (int j = 0; j < 12; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 2; kk++) {
+      uint32_t x0, x1, x2, x3;
+      ldsm_x4((uint32_t)__cvta_generic_to_shared(sx + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8), x0,
+              x1, x2, x3);
+#pragma unroll
+      for (int j = 0; j < 12; j += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int n = 8 * j + (lane & 7) + ((lane >> 4) << 3);
+        const int grp = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4((uint32_t)__cvta_generic_to_shared(sw + grp * 96 * 8 + n * 8), b0, b1, b2, b3);
+        mma16816(acc[j], x0, x1, x2, x3, b0, b1);
+        mma16816(acc[j + 1], x0, x1, x2, x3, b2, b3);
+      }
+    }
+    // + bias, rounded to f16: Q as A fragments, K and V into the buffer.
+    uint32_t hq[12][2];
+#pragma unroll
+    for (int j = 0; j < 12; j++) {
+      const float2 b = *reinterpret_cast<const float2*>(bqkv + 8 * j + 2 * t);
+      hq[j][0] = pack_half2(acc[j][0] + b.x, acc[j][1] + b.y);
+      hq[j][1] = pack_half2(acc[j][2] + b.x, acc[j][3] + b.y);
+    }
+    uint32_t qa[2][4];
+#pragma unroll
+    for (int kk = 0; kk < 2; kk++) {
+      qa[kk][0] = hq[2 * kk][0];
+      qa[kk][1] = hq[2 * kk][1];
+      qa[kk][2] = hq[2 * kk + 1][0];
+      qa[kk][3] = hq[2 * kk + 1][1];
+    }
+    __half* kv = skv[it & 1];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+      for (int h = 0; h < 2; h++)
+        *reinterpret_cast<uint32_t*>(kv + (j * TOK + q0 + g + 8 * h) * 8 + 2 * t) = hq[4 + j][h];
+    // Every warp's keys and values are in. A warp can be one window ahead
+    // of another only into the other buffer: it stores window it + 1's
+    // keys and values before this barrier's next round, which no warp
+    // passes before all have finished window it.
+    __syncthreads();
+    int cls = 0;
+    if (a.shifted) cls = (win % a.cols_w == a.cols_w - 1 ? 1 : 0) + 2 * (win / a.cols_w == a.rows_w - 1 ? 1 : 0);
+    const float4* tb = reinterpret_cast<const float4*>(a.bias + (long long)cls * TOK * TOK) + warp * 8 * 32 + lane;
+    float o[4][4], inv[2];
+    attend16(qa, kv, kv + 4 * TOK * 8, tb, lane, o, inv);
+    float pr[4][4];
+    project16(o, inv, bw, pr);
+    // rows g and g + 8 of the warp's 16: + bias + the raw row, to the pixel
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int tk = q0 + g + 8 * h;
+      const long long dest = pixel(win, tk);
+      if (dest < 0) continue;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int n = 8 * j + 2 * t;
+        const float2 old = __half22float2(*reinterpret_cast<const __half2*>(sraw + (j * TOK + tk) * 8 + 2 * t));
+        *reinterpret_cast<__half2*>(a.y + (a.plane0 + j) * a.y_plane + dest * 8 + 2 * t) =
+            __floats2half2_rn((pr[j][2 * h] + bproj[n]) + old.x, (pr[j][2 * h + 1] + bproj[n + 1]) + old.y);
+      }
+    }
+    u0 = n0;
+    u1 = n1;
+    __syncwarp();
+  }
 }
 
 }  // namespace
@@ -276,7 +465,7 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
   const double heads = (double)windows * (c / 32);
   timed_launch("window_attention_kernel", heads * 4.0 * 64 * 64 * 32, (double)windows * 64 * 4 * c * 2, s, [&] {
     launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, c, bias, shifted ? 1 : 0, rows_w, cols_w,
-               out, out_plane_elems, dev_err, AttnProjArgs{});
+               out, out_plane_elems, dev_err);
     IEC_CUDA(cudaGetLastError());
   });
 }
@@ -301,26 +490,33 @@ void pack_attn_proj(AttnProj& ap, const std::vector<float>& w, const std::vector
   IEC_CUDA(cudaMemcpy(ap.bias.get(), b.data(), 32 * 4, cudaMemcpyHostToDevice));
 }
 
-void window_attention_proj(const __half* qkv, long long qkv_plane_elems, int windows, const float* bias, bool shifted,
-                           int rows_w, int cols_w, const AttnProj& ap, __half* y, long long y_plane_elems, int plane0,
-                           const WindowMap& wm, int* dev_err, cudaStream_t s) {
-  if ((qkv_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "attention planes must be 16-byte multiples");
-  if (wm.ws < 1 || wm.ws > 8 || wm.pad_w % wm.ws || wm.pad_h % wm.ws || windows != (wm.pad_h / wm.ws) * (wm.pad_w / wm.ws))
+void window_block(const LnRowsWeights& lw, const float* bias, bool shifted, int rows_w, int cols_w,
+                  const AttnProj& ap, __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, int sms,
+                  cudaStream_t s) {
+  if (lw.c != 32 || lw.n != 96) throw Error(ERR_INPUT, "the fused window block takes one head of 32 channels");
+  if (wm.ws < 1 || wm.ws > 8 || wm.pad_w % wm.ws || wm.pad_h % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w)
     throw Error(ERR_INPUT, "window partition geometry is inconsistent");
-  AttnProjArgs pj;
-  pj.frag = ap.frag.as<uint4>();
-  pj.bias = ap.bias.as<float>();
-  pj.y = y;
-  pj.y_plane = y_plane_elems;
-  pj.plane0 = plane0;
-  pj.wm = wm;
-  dim3 grid(windows, 1);
-  // attention as above, then the 64 x 32 x 32 projection per window; bytes:
-  // q, k, v read once, the map's old values read and written (f16)
-  timed_launch("window_attention_proj", (double)windows * (4.0 * 64 * 64 * 32 + 2.0 * 64 * 32 * 32),
-               (double)windows * 64 * (3 * 32 + 2 * 32) * 2, s, [&] {
-                 launch_pdl(window_attention_kernel, grid, 128, 0, s, qkv, qkv_plane_elems, 32, bias, shifted ? 1 : 0,
-                            rows_w, cols_w, static_cast<__half*>(nullptr), 0LL, dev_err, pj);
+  if ((y_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "map planes must be 16-byte multiples");
+  WindowBlockArgs a{};
+  a.y = y;
+  a.y_plane = y_plane_elems;
+  a.plane0 = plane0;
+  a.wm = wm;
+  a.windows = (wm.pad_h / wm.ws) * (wm.pad_w / wm.ws);
+  a.rows_w = rows_w;
+  a.cols_w = cols_w;
+  a.shifted = shifted ? 1 : 0;
+  a.wqkv = lw.w.as<uint8_t>();
+  a.params = lw.params.as<float>();
+  a.bias = bias;
+  a.pfrag = ap.frag.as<uint4>();
+  a.pbias = ap.bias.as<float>();
+  const int grid = std::min(a.windows, sms * 4);
+  // per window: qkv (64 x 96 x 32), attention (2 x 64 x 64 x 32) and the
+  // projection (64 x 32 x 32); bytes: the tokens' rows read and written
+  timed_launch("window_block", (double)a.windows * (2.0 * 64 * 96 * 32 + 4.0 * 64 * 64 * 32 + 2.0 * 64 * 32 * 32),
+               (double)a.windows * 64 * 32 * 2 * 2, s, [&] {
+                 launch_pdl(window_block_kernel, grid, WB_THREADS, 0, s, a);
                  IEC_CUDA(cudaGetLastError());
                });
 }

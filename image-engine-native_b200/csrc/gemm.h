@@ -187,19 +187,20 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
                       cudaStream_t s);
 
 // The window projection (c = 32, one head: a 32 x 32 linear layer with bias)
-// packed for the fused kernel: `w` row-major k x n, as pack_weights takes it.
+// packed for window_block: `w` row-major k x n, as pack_weights takes it.
 struct AttnProj {
   DeviceBuffer frag, bias;
 };
 void pack_attn_proj(AttnProj& ap, const std::vector<float>& w, const std::vector<float>& b);
 
-// Attention of one head (c = 32) followed by the window projection, added
-// onto `y` (planar, planes plane0 .. plane0 + 3) at each token's pixel under
-// `wm` (the window-scatter of gemm_rows' OUT_WINDOW_ACCUM): one launch in
-// place of window_attention and the projection GEMM, and the attention
-// output never leaves the SM.
-void window_attention_proj(const __half* qkv, long long qkv_plane_elems, int windows, const float* bias, bool shifted,
-                           int rows_w, int cols_w, const AttnProj& ap, __half* y, long long y_plane_elems, int plane0,
-                           const WindowMap& wm, int* dev_err, cudaStream_t s);
+// The one-head window attention half in one kernel (c = 32): LN1 and the
+// qkv layer (lw: the lnrows_planar weights of (32, 96)), attention with the
+// bias tables of one head, the projection (ap) and the residual add onto `y`
+// (planar, planes plane0 .. plane0 + 3) at each token's pixel under `wm`. In
+// place of lnrows_planar, window_attention and the projection GEMM; the qkv
+// rows and the attention output stay on the SM.
+void window_block(const LnRowsWeights& lw, const float* bias, bool shifted, int rows_w, int cols_w,
+                  const AttnProj& ap, __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, int sms,
+                  cudaStream_t s);
 
 }  // namespace iec

@@ -393,19 +393,19 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       // Attention (swin.rs:124-220) on y[h:]: LN1 + window partition, qkv,
       // attention, projection added back at the tokens' pixels.
       const WindowMap wm{8, H, W, H, W, shift};
-      if (fused_mlp_ && B.lnqkv.c == h) {
-        lnrows_planar(dev_, B.lnqkv, y + (long long)(h / 8) * pl, pl, Pl, wm, qkv, pl, s);
+      if (fused_mlp_ && h == 32 && B.lnqkv.c == h) {
+        // LN1, qkv, attention, projection and the residual add in one kernel
+        window_block(B.lnqkv, B.bias.as<float>(), B.shifted, H / 8, W / 8, B.proj_fused, y, pl, h / 8, wm, sms, s);
       } else {
-        layer_norm_planar(y, pl, h / 8, Pl, h, B.ln1g.as<float>(), B.ln1b.as<float>(), tok, pl, &wm, s);
-        o.mode = OUT_STORE;
-        o.out = qkv;
-        o.plane0 = 0;
-        gemm_rows(dev_, B.qkv, tok, pl, Pl, ACT_NONE, o, s);
-      }
-      if (fused_mlp_ && h == 32) {
-        window_attention_proj(qkv, pl, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, B.proj_fused, y, pl, h / 8,
-                              wm, dev_.dev_err(), s);
-      } else {
+        if (fused_mlp_ && B.lnqkv.c == h) {
+          lnrows_planar(dev_, B.lnqkv, y + (long long)(h / 8) * pl, pl, Pl, wm, qkv, pl, s);
+        } else {
+          layer_norm_planar(y, pl, h / 8, Pl, h, B.ln1g.as<float>(), B.ln1b.as<float>(), tok, pl, &wm, s);
+          o.mode = OUT_STORE;
+          o.out = qkv;
+          o.plane0 = 0;
+          gemm_rows(dev_, B.qkv, tok, pl, Pl, ACT_NONE, o, s);
+        }
         window_attention(qkv, pl, h, Pl / 64, B.bias.as<float>(), B.shifted, H / 8, W / 8, att, pl, dev_.dev_err(), s);
         o.mode = OUT_WINDOW_ACCUM;
         o.out = y;

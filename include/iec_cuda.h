@@ -224,8 +224,9 @@ iec_status iec_scunet_run_batch(iec_scunet* model, const float* images, size_t c
 /* Each transformer block runs its LayerNorms fused (the default, `on` = 1:
  * LN1 and the window partition folded into the qkv product's staged rows;
  * LN2, fc1, GELU and fc2 in one kernel with the hidden layer kept in shared
- * memory, for the widths those kernels take; with one head, the window
- * projection in the attention kernel) or, with `on` = 0, as LayerNorm
+ * memory, for the widths those kernels take; with one head, LN1, qkv,
+ * attention, the projection and the residual add in one kernel; a block's
+ * join with the next block's split in one kernel) or, with `on` = 0, as LayerNorm
  * launches and GEMM launches through device buffers (for comparisons; no
  * counterpart in the reference). The two agree to f16 rounding (the
  * LayerNorm and product sums run in another order). */
