@@ -138,30 +138,6 @@ __device__ __forceinline__ void attend16(const uint32_t (&qa)[2][4], const __hal
   inv[1] = 1.0f / sum[1];
 }
 
-// The window projection (32 x 32) of one warp's 16 rows: O normalised and
-// rounded to f16 (as the separate projection reads the attention output),
-// as A fragments over the head's 32 dims (two k steps), times W (bw: the
-// lane's B fragments from pack_attn_proj); pr rows g and g + 8, columns
-// 8 j + 2 t and 8 j + 2 t + 1.
-__device__ __forceinline__ void project16(const float (&o)[4][4], const float (&inv)[2], const uint32_t (&bw)[16],
-                                          float (&pr)[4][4]) {
-  uint32_t oa[2][4];
-#pragma unroll
-  for (int kk = 0; kk < 2; kk++) {
-    oa[kk][0] = pack_half2(o[2 * kk][0] * inv[0], o[2 * kk][1] * inv[0]);
-    oa[kk][1] = pack_half2(o[2 * kk][2] * inv[1], o[2 * kk][3] * inv[1]);
-    oa[kk][2] = pack_half2(o[2 * kk + 1][0] * inv[0], o[2 * kk + 1][1] * inv[0]);
-    oa[kk][3] = pack_half2(o[2 * kk + 1][2] * inv[1], o[2 * kk + 1][3] * inv[1]);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    pr[j][0] = pr[j][1] = pr[j][2] = pr[j][3] = 0.0f;
-#pragma unroll
-    for (int kk = 0; kk < 2; kk++)
-      mma16816(pr[j], oa[kk][0], oa[kk][1], oa[kk][2], oa[kk][3], bw[(kk * 4 + j) * 2], bw[(kk * 4 + j) * 2 + 1]);
-  }
-}
-
 __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __restrict__ qkv, long long qkv_plane,
                                                                int c, const float* __restrict__ bias, int shifted,
                                                                int rows_w, int cols_w, __half* __restrict__ out,
@@ -223,78 +199,101 @@ __global__ void __launch_bounds__(128) window_attention_kernel(const __half* __r
     }
 }
 
-// A whole one-head window attention half in one persistent kernel (c = 32):
+// A whole window attention half in one persistent kernel, for one or two
+// heads of 32 channels (C = 32 HEADS):
 //
 //   y[tokens] += proj(attention(qkv(LayerNorm(y[tokens]))))
 //
 // (crates/scunet-native/src/swin.rs:124-220: LN1, the shifted-window
-// partition, the qkv layer, attention with the position bias and shift
-// mask, the projection and the residual add, for one head of 32 channels).
-// Each CTA takes windows in turn; warp w owns tokens 16 w .. 16 w + 15 of
-// the window, two lanes per token:
-//   * the token's 32 channels arrive from its pixel (four 16-byte groups of
-//     the planar map; a window row's tokens are consecutive pixels), the
-//     next window's already in registers while this one is computed;
+// partition, the qkv layer, attention per head with the position bias and
+// shift mask, the projection and the residual add). Each CTA takes windows
+// in turn with four warps per head; warp (hd, tb) owns tokens 16 tb .. 16 tb
+// + 15 of the window for head hd, two lanes per token:
+//   * the token's C channels arrive from its pixel (16-byte groups of the
+//     planar map; a window row's tokens are consecutive pixels), the next
+//     window's already in registers while this one is computed;
 //   * LayerNorm (eps 1e-5; mean, then the mean squared deviation) over the
-//     lane pair, the normalised f16 row and the raw row into shared memory
-//     (the warp's own rows: only __syncwarp between the steps); tokens past
-//     the map or the window's ws x ws are zero rows and are not stored;
-//   * qkv = row x Wqkv + b on mma.sync m16n8k16 (Wqkv resident in shared
-//     memory, [4][96][8]), rounded to f16 where the separate launches store
-//     it: Q stays in registers as the attention's A fragments, K and V go to
-//     one of two shared-memory buffers, one barrier per window;
-//   * attention, the projection and bias (attend16, project16), plus the
-//     raw row, stored to the token's pixel.
-// The qkv rows never reach global memory: per window 64 tokens x 32 channels
-// are read and written once.
+//     lane pair; the normalised f16 row into the head's own copy of the A
+//     tile and the raw row (the head's channels) into shared memory, both
+//     rows of this warp only (__syncwarp between the steps); tokens past the
+//     map or the window's ws x ws are zero rows and are not stored;
+//   * the head's q, k and v = row x Wqkv + b on mma.sync m16n8k16, rounded to
+//     f16 where the separate launches store them: Q stays in registers as
+//     the attention's A fragments, K and V go to one of two shared-memory
+//     buffers (one barrier);
+//   * attention (attend16); with one head the f16 output is the
+//     projection's A operand in registers, with two each warp writes its
+//     head's output to one of two shared-memory buffers (a second barrier)
+//     and projects its 16 rows over both heads into its head's 32 output
+//     columns;
+//   * plus the projection bias and the raw row, stored to the token's pixel.
+// A warp is at most one window ahead of another, and only into the other
+// buffer of each pair: it writes window i + 1's keys before the barrier that
+// no warp passes before all have finished window i.
+// The qkv rows and the attention output never reach global memory: per
+// window 64 tokens x C channels are read and written once. Weights (qkv and
+// projection as [C / 8][N][8] f16, the B operands' core-matrix images) stay
+// in shared memory.
 struct WindowBlockArgs {
-  __half* y;              // planar map, the head's channels in planes plane0 .. plane0 + 3
+  __half* y;              // planar map, the block's channels in planes plane0 .. plane0 + C / 8 - 1
   long long y_plane;
   int plane0;
   WindowMap wm;
   int windows, rows_w, cols_w, shifted;
-  const uint8_t* wqkv;    // [4][96][8] f16 (the B operand of lnrows_sm100)
-  const float* params;    // gamma [32], beta [32], qkv bias [96]
-  const float* bias;      // attention bias tables (attention_bias_layout), one head
-  const uint4* pfrag;     // projection B fragments (pack_attn_proj)
-  const float* pbias;     // projection bias [32]
+  const uint8_t* w;       // Wqkv [C / 8][3 C][8] f16, then Wproj [C / 8][C][8] f16
+  const float* params;    // gamma [C], beta [C], qkv bias [3 C], projection bias [C]
+  const float* bias;      // attention bias tables (attention_bias_layout), [class][head]
 };
 
-constexpr int WB_THREADS = 128;
+template <int HEADS>
+struct WindowBlockSmem {
+  static constexpr int C = 32 * HEADS, NQ = 3 * C, WARPS = 4 * HEADS, THREADS = 32 * WARPS;
+  static constexpr int CTAS = HEADS == 1 ? 4 : 2;  // per SM (registers: 128 per thread)
+  static constexpr int WQ_BYTES = C * NQ * 2, WP_BYTES = C * C * 2, PAR_FLOATS = 6 * C;
+  static constexpr int TILE = C * TOK * 2;         // [C / 8][64][8] f16
+  static constexpr int KV = 8 * TOK * 16;          // one head's K and V
+  static constexpr int WQ_OFF = 0, WP_OFF = WQ_BYTES, PAR_OFF = WP_OFF + WP_BYTES;
+  static constexpr int X_OFF = PAR_OFF + PAR_FLOATS * 4;       // HEADS copies of the normalised rows
+  static constexpr int RAW_OFF = X_OFF + HEADS * TILE;         // the rows as read
+  static constexpr int KV_OFF = RAW_OFF + TILE;                // [2][HEADS] K and V
+  static constexpr int O_OFF = KV_OFF + 2 * HEADS * KV;        // [2] attention outputs (two heads)
+  static constexpr int TOTAL = O_OFF + (HEADS > 1 ? 2 * TILE : 0);
+  static_assert(TOTAL * CTAS <= 220 * 1024, "window block shared memory");
+};
 
-__global__ void __launch_bounds__(WB_THREADS, 4) window_block_kernel(const WindowBlockArgs a) {
-  __shared__ __align__(128) __half sw[4 * 96 * 8];        // Wqkv
-  __shared__ __align__(128) __half skv[2][8 * TOK * 8];   // K (groups 0..3) and V (4..7), two buffers
-  __shared__ __align__(128) __half sx[4 * TOK * 8];       // normalised rows [4][64][8]
-  __shared__ __align__(128) __half sraw[4 * TOK * 8];     // the rows as read
-  __shared__ __align__(16) float spar[32 + 32 + 96 + 32];  // gamma, beta, qkv bias, projection bias
+template <int HEADS>
+__global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSmem<HEADS>::CTAS)
+    window_block_kernel(const WindowBlockArgs a) {
+  using L = WindowBlockSmem<HEADS>;
+  constexpr int C = L::C, NQ = L::NQ, G = C / 8;  // G: channel groups (planes)
+  extern __shared__ __align__(128) uint8_t wb_smem[];
+  __half* sw = reinterpret_cast<__half*>(wb_smem + L::WQ_OFF);
+  __half* swp = reinterpret_cast<__half*>(wb_smem + L::WP_OFF);
+  float* spar = reinterpret_cast<float*>(wb_smem + L::PAR_OFF);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3, q0 = warp * 16;
+  const int hd = warp >> 2, tb = warp & 3;  // head, token block
+  const int g = lane >> 2, t = lane & 3, q0 = tb * 16;
+  __half* sx = reinterpret_cast<__half*>(wb_smem + L::X_OFF + hd * L::TILE);
+  __half* sraw = reinterpret_cast<__half*>(wb_smem + L::RAW_OFF);
   // Weights first: no kernel writes them.
-  for (int i = (int)threadIdx.x; i < 4 * 96; i += WB_THREADS)
-    reinterpret_cast<uint4*>(sw)[i] = __ldg(reinterpret_cast<const uint4*>(a.wqkv) + i);
-  for (int i = (int)threadIdx.x; i < 160; i += WB_THREADS) spar[i] = __ldg(a.params + i);
-  if (threadIdx.x < 32) spar[160 + threadIdx.x] = __ldg(a.pbias + threadIdx.x);
-  uint32_t bw[16];
-#pragma unroll
-  for (int q = 0; q < 4; q++) {
-    const uint4 u = __ldg(a.pfrag + lane * 4 + q);
-    bw[4 * q] = u.x;
-    bw[4 * q + 1] = u.y;
-    bw[4 * q + 2] = u.z;
-    bw[4 * q + 3] = u.w;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(a.w);
+    uint4* dst = reinterpret_cast<uint4*>(wb_smem + L::WQ_OFF);
+    for (int i = (int)threadIdx.x; i < (L::WQ_BYTES + L::WP_BYTES) / 16; i += L::THREADS) dst[i] = __ldg(src + i);
+    for (int i = (int)threadIdx.x; i < L::PAR_FLOATS; i += L::THREADS) spar[i] = __ldg(a.params + i);
   }
   __syncthreads();
   griddep_wait();
   griddep_launch_dependents();
   const float* gamma = spar;
-  const float* beta = spar + 32;
-  const float* bqkv = spar + 64;
-  const float* bproj = spar + 160;
+  const float* beta = spar + C;
+  const float* bqkv = spar + 2 * C;
+  const float* bproj = spar + 5 * C;
   const WindowMap& wm = a.wm;
   const int ws = wm.ws, cols = wm.pad_w / ws;
-  // This lane's token and channel half: token 16 w + lane / 2, channels
-  // 16 hp .. 16 hp + 15 (planes 2 hp, 2 hp + 1).
+  // This lane's token and channel half: token q0 + lane / 2, channel groups
+  // [GH hp, GH hp + GH).
+  constexpr int GH = G / 2;
   const int tk_own = q0 + (lane >> 1), hp = lane & 1;
   // The pixel of token tk of window win, or -1 when the token is padding.
   auto pixel = [&](int win, int tk) -> long long {
@@ -303,89 +302,91 @@ __global__ void __launch_bounds__(WB_THREADS, 4) window_block_kernel(const Windo
     if (tk >= ws * ws || py >= wm.map_h || px >= wm.map_w) return -1;
     return (long long)py * wm.map_w + px;
   };
-  auto fetch = [&](int win, uint4& u0, uint4& u1) {
-    u0 = u1 = make_uint4(0u, 0u, 0u, 0u);
+  auto fetch = [&](int win, uint4 (&u)[GH]) {
+#pragma unroll
+    for (int q = 0; q < GH; q++) u[q] = make_uint4(0u, 0u, 0u, 0u);
     if (win >= a.windows) return;
     const long long px = pixel(win, tk_own);
     if (px < 0) return;
-    const __half* at = a.y + (long long)(a.plane0 + 2 * hp) * a.y_plane + px * 8;
-    u0 = *reinterpret_cast<const uint4*>(at);
-    u1 = *reinterpret_cast<const uint4*>(at + a.y_plane);
+    const __half* at = a.y + (long long)(a.plane0 + GH * hp) * a.y_plane + px * 8;
+#pragma unroll
+    for (int q = 0; q < GH; q++) u[q] = *reinterpret_cast<const uint4*>(at + q * a.y_plane);
   };
-  uint4 u0, u1;
-  fetch(blockIdx.x, u0, u1);
+  uint4 u[GH];
+  fetch(blockIdx.x, u);
   int it = 0;
   for (int win = blockIdx.x; win < a.windows; win += gridDim.x, it++) {
     const bool valid = pixel(win, tk_own) >= 0;
     // the next window's rows, in flight while this one is computed
-    uint4 n0, n1;
-    fetch(win + gridDim.x, n0, n1);
-    // LayerNorm over the lane pair's 32 channels (gemm.cu layer_norm_rows'
-    // formula), then the normalised and the raw row into shared memory.
+    uint4 nu[GH];
+    fetch(win + gridDim.x, nu);
+    // LayerNorm over the lane pair's C channels (gemm.cu layer_norm_rows'
+    // formula), then the normalised and the raw rows into shared memory.
     {
-      float v[16];
-      const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
-      const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
+      float v[8 * GH];
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float2 f0 = __half22float2(h0[e]), f1 = __half22float2(h1[e]);
-        v[2 * e] = f0.x;
-        v[2 * e + 1] = f0.y;
-        v[8 + 2 * e] = f1.x;
-        v[8 + 2 * e + 1] = f1.y;
+      for (int q = 0; q < GH; q++) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&u[q]);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float2 f = __half22float2(h2[e]);
+          v[8 * q + 2 * e] = f.x;
+          v[8 * q + 2 * e + 1] = f.y;
+        }
       }
       float sum = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 16; e++) sum += v[e];
+      for (int e = 0; e < 8 * GH; e++) sum += v[e];
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      const float mean = sum / 32.0f;
+      const float mean = sum / (float)C;
       float var = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 16; e++) var += (v[e] - mean) * (v[e] - mean);
+      for (int e = 0; e < 8 * GH; e++) var += (v[e] - mean) * (v[e] - mean);
       var += __shfl_xor_sync(0xffffffffu, var, 1);
-      const float inv = 1.0f / sqrtf(var / 32.0f + 1e-5f);
-      float nv[16];
-#pragma unroll
-      for (int e = 0; e < 16; e++) {
-        const int ch = 16 * hp + e;
-        nv[e] = valid ? (v[e] - mean) * inv * gamma[ch] + beta[ch] : 0.0f;
-      }
+      const float inv = 1.0f / sqrtf(var / (float)C + 1e-5f);
       uint4* xr = reinterpret_cast<uint4*>(sx);
       uint4* rr = reinterpret_cast<uint4*>(sraw);
-      xr[(2 * hp) * TOK + tk_own] = make_uint4(pack_half2(nv[0], nv[1]), pack_half2(nv[2], nv[3]),
-                                               pack_half2(nv[4], nv[5]), pack_half2(nv[6], nv[7]));
-      xr[(2 * hp + 1) * TOK + tk_own] = make_uint4(pack_half2(nv[8], nv[9]), pack_half2(nv[10], nv[11]),
-                                                   pack_half2(nv[12], nv[13]), pack_half2(nv[14], nv[15]));
-      rr[(2 * hp) * TOK + tk_own] = u0;
-      rr[(2 * hp + 1) * TOK + tk_own] = u1;
+#pragma unroll
+      for (int q = 0; q < GH; q++) {
+        const int grp = GH * hp + q;
+        float nv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) nv[e] = valid ? (v[8 * q + e] - mean) * inv * gamma[8 * grp + e] + beta[8 * grp + e] : 0.0f;
+        xr[grp * TOK + tk_own] = make_uint4(pack_half2(nv[0], nv[1]), pack_half2(nv[2], nv[3]),
+                                            pack_half2(nv[4], nv[5]), pack_half2(nv[6], nv[7]));
+        if (grp / 4 == hd) rr[grp * TOK + tk_own] = u[q];  // this head's channels
+      }
     }
     __syncwarp();
-    // qkv for the warp's 16 rows: 12 column tiles of 8, two k steps.
+    // This head's q, k and v for the warp's 16 rows: 12 column tiles of 8
+    // (local tile jl: q, k or v by jl / 4, the head's dims 8 (jl % 4) ..).
     float acc[12][4];
 #pragma unroll
     for (int j = 0; j < 12; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < 2; kk++) {
+    for (int kk = 0; kk < C / 16; kk++) {
       uint32_t x0, x1, x2, x3;
       ldsm_x4((uint32_t)__cvta_generic_to_shared(sx + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8), x0,
               x1, x2, x3);
 #pragma unroll
-      for (int j = 0; j < 12; j += 2) {
+      for (int jl = 0; jl < 12; jl += 2) {
         uint32_t b0, b1, b2, b3;
-        const int n = 8 * j + (lane & 7) + ((lane >> 4) << 3);
+        const int nt = (jl / 4) * G + 4 * hd + (jl % 4);  // global column tile
+        const int n = 8 * nt + (lane & 7) + ((lane >> 4) << 3);
         const int grp = kk * 2 + ((lane >> 3) & 1);
-        ldsm_x4((uint32_t)__cvta_generic_to_shared(sw + grp * 96 * 8 + n * 8), b0, b1, b2, b3);
-        mma16816(acc[j], x0, x1, x2, x3, b0, b1);
-        mma16816(acc[j + 1], x0, x1, x2, x3, b2, b3);
+        ldsm_x4((uint32_t)__cvta_generic_to_shared(sw + grp * NQ * 8 + n * 8), b0, b1, b2, b3);
+        mma16816(acc[jl], x0, x1, x2, x3, b0, b1);
+        mma16816(acc[jl + 1], x0, x1, x2, x3, b2, b3);
       }
     }
     // + bias, rounded to f16: Q as A fragments, K and V into the buffer.
     uint32_t hq[12][2];
 #pragma unroll
-    for (int j = 0; j < 12; j++) {
-      const float2 b = *reinterpret_cast<const float2*>(bqkv + 8 * j + 2 * t);
-      hq[j][0] = pack_half2(acc[j][0] + b.x, acc[j][1] + b.y);
-      hq[j][1] = pack_half2(acc[j][2] + b.x, acc[j][3] + b.y);
+    for (int jl = 0; jl < 12; jl++) {
+      const int nt = (jl / 4) * G + 4 * hd + (jl % 4);
+      const float2 b = *reinterpret_cast<const float2*>(bqkv + 8 * nt + 2 * t);
+      hq[jl][0] = pack_half2(acc[jl][0] + b.x, acc[jl][1] + b.y);
+      hq[jl][1] = pack_half2(acc[jl][2] + b.x, acc[jl][3] + b.y);
     }
     uint32_t qa[2][4];
 #pragma unroll
@@ -395,24 +396,60 @@ __global__ void __launch_bounds__(WB_THREADS, 4) window_block_kernel(const Windo
       qa[kk][2] = hq[2 * kk + 1][0];
       qa[kk][3] = hq[2 * kk + 1][1];
     }
-    __half* kv = skv[it & 1];
+    __half* kv = reinterpret_cast<__half*>(wb_smem + L::KV_OFF + ((it & 1) * HEADS + hd) * L::KV);
 #pragma unroll
     for (int j = 0; j < 8; j++)
 #pragma unroll
       for (int h = 0; h < 2; h++)
         *reinterpret_cast<uint32_t*>(kv + (j * TOK + q0 + g + 8 * h) * 8 + 2 * t) = hq[4 + j][h];
-    // Every warp's keys and values are in. A warp can be one window ahead
-    // of another only into the other buffer: it stores window it + 1's
-    // keys and values before this barrier's next round, which no warp
-    // passes before all have finished window it.
     __syncthreads();
     int cls = 0;
     if (a.shifted) cls = (win % a.cols_w == a.cols_w - 1 ? 1 : 0) + 2 * (win / a.cols_w == a.rows_w - 1 ? 1 : 0);
-    const float4* tb = reinterpret_cast<const float4*>(a.bias + (long long)cls * TOK * TOK) + warp * 8 * 32 + lane;
+    const float4* tbl =
+        reinterpret_cast<const float4*>(a.bias + ((long long)cls * HEADS + hd) * TOK * TOK) + tb * 8 * 32 + lane;
     float o[4][4], inv[2];
-    attend16(qa, kv, kv + 4 * TOK * 8, tb, lane, o, inv);
+    attend16(qa, kv, kv + 4 * TOK * 8, tbl, lane, o, inv);
+    // The projection of the warp's 16 rows into this head's 32 output
+    // columns (column tiles 4 hd .. 4 hd + 3), the attention output rounded
+    // to f16 as the separate projection reads it.
     float pr[4][4];
-    project16(o, inv, bw, pr);
+#pragma unroll
+    for (int j = 0; j < 4; j++) pr[j][0] = pr[j][1] = pr[j][2] = pr[j][3] = 0.0f;
+    auto project = [&](int kk, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int n = 8 * (4 * hd + j) + (lane & 7) + ((lane >> 4) << 3);
+        const int grp = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4((uint32_t)__cvta_generic_to_shared(swp + grp * C * 8 + n * 8), b0, b1, b2, b3);
+        mma16816(pr[j], a0, a1, a2, a3, b0, b1);
+        mma16816(pr[j + 1], a0, a1, a2, a3, b2, b3);
+      }
+    };
+    if constexpr (HEADS == 1) {
+#pragma unroll
+      for (int kk = 0; kk < 2; kk++)
+        project(kk, pack_half2(o[2 * kk][0] * inv[0], o[2 * kk][1] * inv[0]),
+                pack_half2(o[2 * kk][2] * inv[1], o[2 * kk][3] * inv[1]),
+                pack_half2(o[2 * kk + 1][0] * inv[0], o[2 * kk + 1][1] * inv[0]),
+                pack_half2(o[2 * kk + 1][2] * inv[1], o[2 * kk + 1][3] * inv[1]));
+    } else {
+      __half* so = reinterpret_cast<__half*>(wb_smem + L::O_OFF + (it & 1) * L::TILE);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+          *reinterpret_cast<uint32_t*>(so + ((4 * hd + j) * TOK + q0 + g + 8 * h) * 8 + 2 * t) =
+              pack_half2(o[j][2 * h] * inv[h], o[j][2 * h + 1] * inv[h]);
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < C / 16; kk++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4((uint32_t)__cvta_generic_to_shared(so + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8),
+                a0, a1, a2, a3);
+        project(kk, a0, a1, a2, a3);
+      }
+    }
     // rows g and g + 8 of the warp's 16: + bias + the raw row, to the pixel
 #pragma unroll
     for (int h = 0; h < 2; h++) {
@@ -421,14 +458,14 @@ __global__ void __launch_bounds__(WB_THREADS, 4) window_block_kernel(const Windo
       if (dest < 0) continue;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const int n = 8 * j + 2 * t;
-        const float2 old = __half22float2(*reinterpret_cast<const __half2*>(sraw + (j * TOK + tk) * 8 + 2 * t));
-        *reinterpret_cast<__half2*>(a.y + (a.plane0 + j) * a.y_plane + dest * 8 + 2 * t) =
+        const int grp = 4 * hd + j, n = 8 * grp + 2 * t;
+        const float2 old = __half22float2(*reinterpret_cast<const __half2*>(sraw + (grp * TOK + tk) * 8 + 2 * t));
+        *reinterpret_cast<__half2*>(a.y + (a.plane0 + grp) * a.y_plane + dest * 8 + 2 * t) =
             __floats2half2_rn((pr[j][2 * h] + bproj[n]) + old.x, (pr[j][2 * h + 1] + bproj[n + 1]) + old.y);
       }
     }
-    u0 = n0;
-    u1 = n1;
+#pragma unroll
+    for (int q = 0; q < GH; q++) u[q] = nu[q];
     __syncwarp();
   }
 }
@@ -470,30 +507,55 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
   });
 }
 
-void pack_attn_proj(AttnProj& ap, const std::vector<float>& w, const std::vector<float>& b) {
-  if (w.size() != 32 * 32 || b.size() != 32) throw Error(ERR_WEIGHTS, "fused window projection: 32 x 32 weights");
-  // lane l = 4 g + t, k step kk, n tile j: b0 = W[16 kk + 2 t (+1)][8 j + g],
-  // b1 = W[16 kk + 2 t + 8 (+9)][8 j + g], each a pair of f16 (low = lower k)
-  std::vector<uint16_t> frag(32 * 2 * 4 * 2 * 2);
-  for (int l = 0; l < 32; l++)
-    for (int kk = 0; kk < 2; kk++)
-      for (int j = 0; j < 4; j++)
-        for (int r = 0; r < 2; r++) {
-          const int g = l >> 2, t = l & 3, k = 16 * kk + 2 * t + 8 * r, n = 8 * j + g;
-          const size_t at = ((((size_t)l * 2 + kk) * 4 + j) * 2 + r) * 2;
-          frag[at] = f32_to_half(w[(size_t)k * 32 + n]);
-          frag[at + 1] = f32_to_half(w[(size_t)(k + 1) * 32 + n]);
-        }
-  ap.frag.reserve(frag.size() * 2);
-  IEC_CUDA(cudaMemcpy(ap.frag.get(), frag.data(), frag.size() * 2, cudaMemcpyHostToDevice));
-  ap.bias.reserve(32 * 4);
-  IEC_CUDA(cudaMemcpy(ap.bias.get(), b.data(), 32 * 4, cudaMemcpyHostToDevice));
+bool window_block_fits(int c) { return c == 32 || c == 64; }
+
+void pack_window_block(WindowBlockWeights& wb, int c, const std::vector<float>& wq, const std::vector<float>& bq,
+                       const std::vector<float>& wp, const std::vector<float>& bp, const std::vector<float>& gamma,
+                       const std::vector<float>& beta) {
+  if (!window_block_fits(c)) throw Error(ERR_INPUT, "fused window block of " + std::to_string(c) + " channels");
+  const size_t nq = (size_t)3 * c;
+  if (wq.size() != (size_t)c * nq || bq.size() != nq || wp.size() != (size_t)c * c || bp.size() != (size_t)c ||
+      gamma.size() != (size_t)c || beta.size() != (size_t)c)
+    throw Error(ERR_WEIGHTS, "window block weights of the wrong size");
+  // Wqkv as [c / 8][3c][8], then Wproj as [c / 8][c][8]: the B operands'
+  // core-matrix images, which ldmatrix reads as mma.sync B fragments
+  std::vector<uint16_t> w((size_t)c * nq + (size_t)c * c);
+  size_t at = 0;
+  for (int g = 0; g < c / 8; g++)
+    for (size_t n = 0; n < nq; n++)
+      for (int e = 0; e < 8; e++) w[at++] = f32_to_half(wq[(size_t)(8 * g + e) * nq + n]);
+  for (int g = 0; g < c / 8; g++)
+    for (int n = 0; n < c; n++)
+      for (int e = 0; e < 8; e++) w[at++] = f32_to_half(wp[(size_t)(8 * g + e) * c + n]);
+  std::vector<float> par;
+  for (const std::vector<float>* v : {&gamma, &beta, &bq, &bp}) par.insert(par.end(), v->begin(), v->end());
+  wb.c = c;
+  wb.w.reserve(w.size() * 2);
+  wb.params.reserve(par.size() * 4);
+  IEC_CUDA(cudaMemcpy(wb.w.get(), w.data(), w.size() * 2, cudaMemcpyHostToDevice));
+  IEC_CUDA(cudaMemcpy(wb.params.get(), par.data(), par.size() * 4, cudaMemcpyHostToDevice));
 }
 
-void window_block(const LnRowsWeights& lw, const float* bias, bool shifted, int rows_w, int cols_w,
-                  const AttnProj& ap, __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, int sms,
-                  cudaStream_t s) {
-  if (lw.c != 32 || lw.n != 96) throw Error(ERR_INPUT, "the fused window block takes one head of 32 channels");
+namespace {
+
+template <int HEADS>
+void launch_window_block(int device, int sms, const WindowBlockArgs& a, cudaStream_t s) {
+  using L = WindowBlockSmem<HEADS>;
+  static bool prepared[64] = {};
+  if (!prepared[device & 63]) {
+    IEC_CUDA(cudaFuncSetAttribute(window_block_kernel<HEADS>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    prepared[device & 63] = true;
+  }
+  launch_pdl(window_block_kernel<HEADS>, std::min(a.windows, sms * L::CTAS), L::THREADS, (size_t)L::TOTAL, s, a);
+  IEC_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+void window_block(Device& dev, const WindowBlockWeights& wb, const float* bias, bool shifted, int rows_w, int cols_w,
+                  __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, cudaStream_t s) {
+  const int c = wb.c;
+  if (!window_block_fits(c)) throw Error(ERR_INPUT, "fused window block shape");
   if (wm.ws < 1 || wm.ws > 8 || wm.pad_w % wm.ws || wm.pad_h % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w)
     throw Error(ERR_INPUT, "window partition geometry is inconsistent");
   if ((y_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "map planes must be 16-byte multiples");
@@ -506,18 +568,18 @@ void window_block(const LnRowsWeights& lw, const float* bias, bool shifted, int 
   a.rows_w = rows_w;
   a.cols_w = cols_w;
   a.shifted = shifted ? 1 : 0;
-  a.wqkv = lw.w.as<uint8_t>();
-  a.params = lw.params.as<float>();
+  a.w = wb.w.as<uint8_t>();
+  a.params = wb.params.as<float>();
   a.bias = bias;
-  a.pfrag = ap.frag.as<uint4>();
-  a.pbias = ap.bias.as<float>();
-  const int grid = std::min(a.windows, sms * 4);
-  // per window: qkv (64 x 96 x 32), attention (2 x 64 x 64 x 32) and the
-  // projection (64 x 32 x 32); bytes: the tokens' rows read and written
-  timed_launch("window_block", (double)a.windows * (2.0 * 64 * 96 * 32 + 4.0 * 64 * 64 * 32 + 2.0 * 64 * 32 * 32),
-               (double)a.windows * 64 * 32 * 2 * 2, s, [&] {
-                 launch_pdl(window_block_kernel, grid, WB_THREADS, 0, s, a);
-                 IEC_CUDA(cudaGetLastError());
+  const double heads = c / 32;
+  char name[48];
+  snprintf(name, sizeof name, "window_block<%d>", c / 32);
+  // per window: qkv (64 x 3c x c), attention (2 x 64 x 64 x 32 per head) and
+  // the projection (64 x c x c); bytes: the tokens' rows read and written
+  timed_launch(name, (double)a.windows * (2.0 * 64 * 3 * c * c + heads * 4.0 * 64 * 64 * 32 + 2.0 * 64 * c * c),
+               (double)a.windows * 64 * c * 2 * 2, s, [&] {
+                 if (c == 32) return launch_window_block<1>(dev.ordinal(), dev.sms(), a, s);
+                 return launch_window_block<2>(dev.ordinal(), dev.sms(), a, s);
                });
 }
 

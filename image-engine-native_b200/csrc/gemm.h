@@ -186,21 +186,22 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
                       bool shifted, int rows_w, int cols_w, __half* out, long long out_plane_elems, int* dev_err,
                       cudaStream_t s);
 
-// The window projection (c = 32, one head: a 32 x 32 linear layer with bias)
-// packed for window_block: `w` row-major k x n, as pack_weights takes it.
-struct AttnProj {
-  DeviceBuffer frag, bias;
+// A whole window attention half in one kernel, for one or two heads of 32
+// channels (c 32 or 64): LN1, the qkv layer, attention with the bias tables
+// of the heads (attention_bias_layout), the projection and the residual add
+// onto `y` (planar, planes plane0 .. plane0 + c / 8 - 1) at each token's
+// pixel under `wm`. In place of lnrows_planar, window_attention and the
+// projection GEMM; the qkv rows and the attention output stay on the SM.
+struct WindowBlockWeights {
+  int c = 0;
+  DeviceBuffer w, params;
 };
-void pack_attn_proj(AttnProj& ap, const std::vector<float>& w, const std::vector<float>& b);
-
-// The one-head window attention half in one kernel (c = 32): LN1 and the
-// qkv layer (lw: the lnrows_planar weights of (32, 96)), attention with the
-// bias tables of one head, the projection (ap) and the residual add onto `y`
-// (planar, planes plane0 .. plane0 + 3) at each token's pixel under `wm`. In
-// place of lnrows_planar, window_attention and the projection GEMM; the qkv
-// rows and the attention output stay on the SM.
-void window_block(const LnRowsWeights& lw, const float* bias, bool shifted, int rows_w, int cols_w,
-                  const AttnProj& ap, __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, int sms,
-                  cudaStream_t s);
+bool window_block_fits(int c);
+// wq: c x 3c (q, k, v columns), wp: c x c (row k, column n); biases, gamma, beta f32.
+void pack_window_block(WindowBlockWeights& wb, int c, const std::vector<float>& wq, const std::vector<float>& bq,
+                       const std::vector<float>& wp, const std::vector<float>& bp, const std::vector<float>& gamma,
+                       const std::vector<float>& beta);
+void window_block(Device& dev, const WindowBlockWeights& wb, const float* bias, bool shifted, int rows_w, int cols_w,
+                  __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, cudaStream_t s);
 
 }  // namespace iec

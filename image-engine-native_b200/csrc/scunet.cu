@@ -19,7 +19,7 @@ struct Scunet::Block {
   int c = 0, h = 0;
   bool shifted = false;
   PackedWeights split, conv1, conv2, join, qkv, proj, fc1, fc2;
-  AttnProj proj_fused;  // the projection for the fused attention (one head only)
+  WindowBlockWeights wblock;  // LN1, qkv, attention and projection in one kernel, where the width fits
   JoinSplitWeights joinsplit;  // this block's join and the next one's split in one kernel, where the width fits
   MlpWeights mlp;  // LN2, fc1, GELU and fc2 fused (mlp_sm100.cuh), where the width fits
   LnRowsWeights lnqkv;  // LN1 + window partition + qkv (lnrows_sm100.cuh), where the width fits
@@ -189,6 +189,7 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
     conv3(f, b.conv1, name + ".conv_block.0", h, h, h);
     conv3(f, b.conv2, name + ".conv_block.2", h, h, h);
     const std::string t = name + ".trans_block";
+    std::vector<float> wq_keep, bq_keep, g1_keep, be1_keep;  // LN1 and qkv again for the fused window block
     {
       // LN1 and the qkv layer: the separate launches' weights, and the same
       // values for the kernel that folds LN1 and the window partition into
@@ -200,13 +201,17 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
       upload(b.ln1b, be1);
       pack_weights(b.qkv, wq.values, 1, h, 3 * h, bq.data());
       if (lnrows_fits(h, 3 * h)) pack_lnrows(b.lnqkv, h, 3 * h, wq.values, bq, g1, be1);
+      wq_keep = std::move(wq.values);
+      bq_keep = bq;
+      g1_keep = g1;
+      be1_keep = be1;
     }
     upload(b.bias, attention_bias_layout(bias_tables(f.take(t + ".msa.position_bias", {(size_t)(h / 32), 64, 64}), shifted)));
     {
       HostTensor w = f.take_tensor(t + ".msa.linear.weight", {(size_t)h, (size_t)h});
       const std::vector<float> pb = f.take(t + ".msa.linear.bias", {(size_t)h});
       pack_weights(b.proj, w.values, 1, h, h, pb.data());
-      if (h == 32) pack_attn_proj(b.proj_fused, w.values, pb);
+      if (window_block_fits(h)) pack_window_block(b.wblock, h, wq_keep, bq_keep, w.values, pb, g1_keep, be1_keep);
     }
     {
       // LN2 and the MLP: the separate launches' weights, and the same values
@@ -393,9 +398,9 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
       // Attention (swin.rs:124-220) on y[h:]: LN1 + window partition, qkv,
       // attention, projection added back at the tokens' pixels.
       const WindowMap wm{8, H, W, H, W, shift};
-      if (fused_mlp_ && h == 32 && B.lnqkv.c == h) {
+      if (fused_mlp_ && B.wblock.c == h) {
         // LN1, qkv, attention, projection and the residual add in one kernel
-        window_block(B.lnqkv, B.bias.as<float>(), B.shifted, H / 8, W / 8, B.proj_fused, y, pl, h / 8, wm, sms, s);
+        window_block(dev_, B.wblock, B.bias.as<float>(), B.shifted, H / 8, W / 8, y, pl, h / 8, wm, s);
       } else {
         if (fused_mlp_ && B.lnqkv.c == h) {
           lnrows_planar(dev_, B.lnqkv, y + (long long)(h / 8) * pl, pl, Pl, wm, qkv, pl, s);
