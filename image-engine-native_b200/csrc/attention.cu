@@ -29,7 +29,7 @@ namespace iec {
 
 namespace {
 
-constexpr int TOK = 64, HD = 32;
+constexpr int TOK = 64;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -295,18 +295,41 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSm
   // [GH hp, GH hp + GH).
   constexpr int GH = G / 2;
   const int tk_own = q0 + (lane >> 1), hp = lane & 1;
-  // The pixel of token tk of window win, or -1 when the token is padding.
-  auto pixel = [&](int win, int tk) -> long long {
-    const int wy = win / cols, wx = win - wy * cols;
-    const int py = (wy * ws + tk / ws + wm.shift) % wm.pad_h, px = (wx * ws + tk % ws + wm.shift) % wm.pad_w;
-    if (tk >= ws * ws || py >= wm.map_h || px >= wm.map_w) return -1;
+  // A lane's tokens are the same in every window: their rows and columns
+  // within the window once per launch (ty = -1 for the slot's padding
+  // tokens past ws x ws); per window only its origin, shifted. The shifted
+  // coordinate is below twice the padded size (shift < ws), so one
+  // subtraction wraps it.
+  struct Tok {
+    int ty, tx;
+  };
+  auto tok = [&](int tk) -> Tok {
+    if (tk >= ws * ws) return Tok{-1, 0};
+    const int ty = tk / ws;
+    return Tok{ty, tk - ty * ws};
+  };
+  const Tok t_own = tok(tk_own), t_out[2] = {tok(q0 + g), tok(q0 + g + 8)};
+  // The pixel of a token of the window with shifted origin (oy, ox), or -1
+  // when the token is padding.
+  auto pixel = [&](int oy, int ox, Tok k) -> long long {
+    int py = oy + k.ty, px = ox + k.tx;
+    if (py >= wm.pad_h) py -= wm.pad_h;
+    if (px >= wm.pad_w) px -= wm.pad_w;
+    if (k.ty < 0 || py >= wm.map_h || px >= wm.map_w) return -1;
     return (long long)py * wm.map_w + px;
+  };
+  auto origin = [&](int win, int& oy, int& ox) {
+    const int wy = win / cols;
+    oy = wy * ws + wm.shift;
+    ox = (win - wy * cols) * ws + wm.shift;
   };
   auto fetch = [&](int win, uint4 (&u)[GH]) {
 #pragma unroll
     for (int q = 0; q < GH; q++) u[q] = make_uint4(0u, 0u, 0u, 0u);
     if (win >= a.windows) return;
-    const long long px = pixel(win, tk_own);
+    int oy, ox;
+    origin(win, oy, ox);
+    const long long px = pixel(oy, ox, t_own);
     if (px < 0) return;
     const __half* at = a.y + (long long)(a.plane0 + GH * hp) * a.y_plane + px * 8;
 #pragma unroll
@@ -316,7 +339,9 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSm
   fetch(blockIdx.x, u);
   int it = 0;
   for (int win = blockIdx.x; win < a.windows; win += gridDim.x, it++) {
-    const bool valid = pixel(win, tk_own) >= 0;
+    int oy, ox;
+    origin(win, oy, ox);
+    const bool valid = pixel(oy, ox, t_own) >= 0;
     // the next window's rows, in flight while this one is computed
     uint4 nu[GH];
     fetch(win + gridDim.x, nu);
@@ -358,50 +383,65 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSm
       }
     }
     __syncwarp();
-    // This head's q, k and v for the warp's 16 rows: 12 column tiles of 8
-    // (local tile jl: q, k or v by jl / 4, the head's dims 8 (jl % 4) ..).
-    float acc[12][4];
+    // This head's k and v, then its q, for the warp's 16 rows (local column
+    // tile jl: q, k or v by jl / 4, the head's dims 8 (jl % 4) ..), the A
+    // fragments loaded once: 32 accumulators live at a time, not 48.
+    uint32_t xa[C / 16][4];
 #pragma unroll
-    for (int j = 0; j < 12; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    for (int kk = 0; kk < C / 16; kk++)
+      ldsm_x4((uint32_t)__cvta_generic_to_shared(sx + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8),
+              xa[kk][0], xa[kk][1], xa[kk][2], xa[kk][3]);
+    // local tiles j0 .. j0 + NT - 1 into acc, then + bias, rounded to f16
+    auto qkv_tiles = [&](auto& acc, auto& hq, int j0) {
+      constexpr int NT = sizeof(acc) / sizeof(acc[0]);
 #pragma unroll
-    for (int kk = 0; kk < C / 16; kk++) {
-      uint32_t x0, x1, x2, x3;
-      ldsm_x4((uint32_t)__cvta_generic_to_shared(sx + (kk * 2 + (lane >> 4)) * TOK * 8 + (q0 + (lane & 15)) * 8), x0,
-              x1, x2, x3);
+      for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 #pragma unroll
-      for (int jl = 0; jl < 12; jl += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int nt = (jl / 4) * G + 4 * hd + (jl % 4);  // global column tile
-        const int n = 8 * nt + (lane & 7) + ((lane >> 4) << 3);
-        const int grp = kk * 2 + ((lane >> 3) & 1);
-        ldsm_x4((uint32_t)__cvta_generic_to_shared(sw + grp * NQ * 8 + n * 8), b0, b1, b2, b3);
-        mma16816(acc[jl], x0, x1, x2, x3, b0, b1);
-        mma16816(acc[jl + 1], x0, x1, x2, x3, b2, b3);
+      for (int kk = 0; kk < C / 16; kk++)
+#pragma unroll
+        for (int j = 0; j < NT; j += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int jl = j0 + j, nt = (jl / 4) * G + 4 * hd + (jl % 4);  // global column tile
+          const int n = 8 * nt + (lane & 7) + ((lane >> 4) << 3);
+          const int grp = kk * 2 + ((lane >> 3) & 1);
+          ldsm_x4((uint32_t)__cvta_generic_to_shared(sw + grp * NQ * 8 + n * 8), b0, b1, b2, b3);
+          mma16816(acc[j], xa[kk][0], xa[kk][1], xa[kk][2], xa[kk][3], b0, b1);
+          mma16816(acc[j + 1], xa[kk][0], xa[kk][1], xa[kk][2], xa[kk][3], b2, b3);
+        }
+#pragma unroll
+      for (int j = 0; j < NT; j++) {
+        const int jl = j0 + j, nt = (jl / 4) * G + 4 * hd + (jl % 4);
+        const float2 b = *reinterpret_cast<const float2*>(bqkv + 8 * nt + 2 * t);
+        hq[j][0] = pack_half2(acc[j][0] + b.x, acc[j][1] + b.y);
+        hq[j][1] = pack_half2(acc[j][2] + b.x, acc[j][3] + b.y);
+      }
+    };
+    // K and V into the buffer.
+    __half* kv = reinterpret_cast<__half*>(wb_smem + L::KV_OFF + ((it & 1) * HEADS + hd) * L::KV);
+    {
+      float acc[8][4];
+      uint32_t hkv[8][2];
+      qkv_tiles(acc, hkv, 4);
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+          *reinterpret_cast<uint32_t*>(kv + (j * TOK + q0 + g + 8 * h) * 8 + 2 * t) = hkv[j][h];
+    }
+    // Q as the attention's A fragments.
+    uint32_t qa[2][4];
+    {
+      float acc[4][4];
+      uint32_t hq[4][2];
+      qkv_tiles(acc, hq, 0);
+#pragma unroll
+      for (int kk = 0; kk < 2; kk++) {
+        qa[kk][0] = hq[2 * kk][0];
+        qa[kk][1] = hq[2 * kk][1];
+        qa[kk][2] = hq[2 * kk + 1][0];
+        qa[kk][3] = hq[2 * kk + 1][1];
       }
     }
-    // + bias, rounded to f16: Q as A fragments, K and V into the buffer.
-    uint32_t hq[12][2];
-#pragma unroll
-    for (int jl = 0; jl < 12; jl++) {
-      const int nt = (jl / 4) * G + 4 * hd + (jl % 4);
-      const float2 b = *reinterpret_cast<const float2*>(bqkv + 8 * nt + 2 * t);
-      hq[jl][0] = pack_half2(acc[jl][0] + b.x, acc[jl][1] + b.y);
-      hq[jl][1] = pack_half2(acc[jl][2] + b.x, acc[jl][3] + b.y);
-    }
-    uint32_t qa[2][4];
-#pragma unroll
-    for (int kk = 0; kk < 2; kk++) {
-      qa[kk][0] = hq[2 * kk][0];
-      qa[kk][1] = hq[2 * kk][1];
-      qa[kk][2] = hq[2 * kk + 1][0];
-      qa[kk][3] = hq[2 * kk + 1][1];
-    }
-    __half* kv = reinterpret_cast<__half*>(wb_smem + L::KV_OFF + ((it & 1) * HEADS + hd) * L::KV);
-#pragma unroll
-    for (int j = 0; j < 8; j++)
-#pragma unroll
-      for (int h = 0; h < 2; h++)
-        *reinterpret_cast<uint32_t*>(kv + (j * TOK + q0 + g + 8 * h) * 8 + 2 * t) = hq[4 + j][h];
     __syncthreads();
     int cls = 0;
     if (a.shifted) cls = (win % a.cols_w == a.cols_w - 1 ? 1 : 0) + 2 * (win / a.cols_w == a.rows_w - 1 ? 1 : 0);
@@ -454,7 +494,7 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSm
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const int tk = q0 + g + 8 * h;
-      const long long dest = pixel(win, tk);
+      const long long dest = pixel(oy, ox, t_out[h]);
       if (dest < 0) continue;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
@@ -556,7 +596,8 @@ void window_block(Device& dev, const WindowBlockWeights& wb, const float* bias, 
                   __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, cudaStream_t s) {
   const int c = wb.c;
   if (!window_block_fits(c)) throw Error(ERR_INPUT, "fused window block shape");
-  if (wm.ws < 1 || wm.ws > 8 || wm.pad_w % wm.ws || wm.pad_h % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w)
+  if (wm.ws < 1 || wm.ws > 8 || wm.pad_w % wm.ws || wm.pad_h % wm.ws || wm.pad_h < wm.map_h || wm.pad_w < wm.map_w ||
+      wm.shift < 0 || wm.shift >= wm.ws)
     throw Error(ERR_INPUT, "window partition geometry is inconsistent");
   if ((y_plane_elems * 2) % 16 != 0) throw Error(ERR_INPUT, "map planes must be 16-byte multiples");
   WindowBlockArgs a{};
