@@ -377,7 +377,7 @@ void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_el
   });
 }
 
-bool joinsplit_fits(int c) { return c == 64 || c == 128; }
+bool joinsplit_fits(int c) { return c == 64 || c == 128 || c == 256; }
 
 void pack_joinsplit(JoinSplitWeights& jw, int c, const std::vector<float>& wj, const std::vector<float>& bj,
                     const std::vector<float>& ws, const std::vector<float>& bs) {
@@ -447,7 +447,8 @@ void joinsplit_planar(Device& dev, const JoinSplitWeights& jw, __half* x, __half
   // FLOPs of both products; bytes: y and x read and written, the weights
   timed_launch(name, 4.0 * rows * c * c, (double)rows * c * 8 + 4.0 * c * c, s, [&] {
     if (c == 64) return launch_joinsplit<64>(dev, ymap, xmap, p, s);
-    return launch_joinsplit<128>(dev, ymap, xmap, p, s);
+    if (c == 128) return launch_joinsplit<128>(dev, ymap, xmap, p, s);
+    return launch_joinsplit<256>(dev, ymap, xmap, p, s);
   });
 }
 

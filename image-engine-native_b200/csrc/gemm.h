@@ -147,7 +147,7 @@ void mlp_planar(Device& dev, const MlpWeights& mw, __half* x, long long plane_el
 // bj, then y = x Ws + bs (the rounded f16 x, as separate launches read it
 // back), over `rows` rows of the C channels at `x` and `y` (planar, plane
 // stride plane_elems, planes of at least gemm_rows_alloc(rows) rows), C in
-// {64, 128}.
+// {64, 128, 256}.
 struct JoinSplitWeights {
   int c = 0;
   DeviceBuffer w, bias;

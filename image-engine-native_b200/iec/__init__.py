@@ -301,8 +301,8 @@ def selftest_gemm(a, w, bias=None, *, conv=False, shape=None, act=0, accumulate_
 
 def selftest_joinsplit(x, y, wj, bj, ws, bs, *, fused=True, iters=0, device=0):
     """Diagnostics: SCUNet's block boundary x += y wj + bj; y = x ws + bs on
-    host arrays (rows x c, c x c, c). fused runs the one-kernel form (c 64 or
-    128), else two GEMM launches. Returns (x, y, microseconds per pass or
+    host arrays (rows x c, c x c, c). fused runs the one-kernel form (c 64,
+    128 or 256), else two GEMM launches. Returns (x, y, microseconds per pass or
     None)."""
     x = np.ascontiguousarray(x, np.float32).copy()
     y = np.ascontiguousarray(y, np.float32).copy()

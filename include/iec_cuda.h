@@ -355,7 +355,7 @@ iec_status iec_selftest_conv(int device, int h, int w, int k, int n, int size, i
 /* Diagnostics: SCUNet's block boundary on host arrays `x` and `y` (rows x c
  * each, rounded to f16 on the way in, overwritten with the results): x += y wj
  * + bj, then y = x ws + bs (wj, ws c x c row-major, row k column n). fused
- * non-zero runs the one-kernel form (c 64 or 128), 0 two GEMM launches. With
+ * non-zero runs the one-kernel form (c 64, 128 or 256), 0 two GEMM launches. With
  * iters > 0 and `us` non-null, us[0] gets the device microseconds per pass
  * over `iters` passes after the checked one. */
 iec_status iec_selftest_joinsplit(int device, int rows, int c, const float* wj, const float* bj, const float* ws,

@@ -103,7 +103,8 @@ def test_mma_rate_diagnostic_runs():
             assert np.isfinite(c) and c > 0
 
 
-@pytest.mark.parametrize("rows,c", [(1000, 64), (128 * 37, 64), (300, 128), (128 * 41 + 7, 128), (49152, 64)])
+@pytest.mark.parametrize("rows,c", [(1000, 64), (128 * 37, 64), (300, 128), (128 * 41 + 7, 128), (49152, 64),
+                                    (200, 256), (128 * 150 + 33, 256), (24576, 256)])
 def test_joinsplit_matches_separate_launches_and_oracle(rows, c):
     """SCUNet's fused block boundary (x += y Wj + bj; y = x Ws + bs in one
     kernel) equals the join and split as two GEMM launches bit for bit, and
