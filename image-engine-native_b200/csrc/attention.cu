@@ -20,6 +20,7 @@
 #include <cuda_fp16.h>
 
 #include "gemm.h"
+#include "igemm_sm100.cuh"
 #include "sm100.cuh"
 
 #include <algorithm>
@@ -243,9 +244,14 @@ struct WindowBlockArgs {
   const uint8_t* w;       // Wqkv [C / 8][3 C][8] f16, then Wproj [C / 8][C][8] f16
   const float* params;    // gamma [C], beta [C], qkv bias [3 C], projection bias [C]
   const float* bias;      // attention bias tables (attention_bias_layout), [class][head]
+  // One head only, optional: the block's MLP after the attention
+  // (mlp_w: W1 [4][128][8] f16, then W2 [16][32][8] f16; mlp_params: gamma2
+  // [32], beta2 [32], b1 [128], b2 [32]).
+  const uint8_t* mlp_w;
+  const float* mlp_params;
 };
 
-template <int HEADS>
+template <int HEADS, bool MLP>
 struct WindowBlockSmem {
   static constexpr int C = 32 * HEADS, NQ = 3 * C, WARPS = 4 * HEADS, THREADS = 32 * WARPS;
   static constexpr int CTAS = HEADS == 1 ? 4 : 2;  // per SM (registers: 128 per thread)
@@ -257,14 +263,18 @@ struct WindowBlockSmem {
   static constexpr int RAW_OFF = X_OFF + HEADS * TILE;         // the rows as read
   static constexpr int KV_OFF = RAW_OFF + TILE;                // [2][HEADS] K and V
   static constexpr int O_OFF = KV_OFF + 2 * HEADS * KV;        // [2] attention outputs (two heads)
-  static constexpr int TOTAL = O_OFF + (HEADS > 1 ? 2 * TILE : 0);
+  static constexpr int MW_OFF = O_OFF + (HEADS > 1 ? 2 * TILE : 0);  // the MLP's W1, W2 and parameters
+  static constexpr int MW_BYTES = MLP ? 2 * C * 4 * C * 2 : 0, MPAR_FLOATS = MLP ? 7 * C : 0;
+  static constexpr int MPAR_OFF = MW_OFF + MW_BYTES;
+  static constexpr int TOTAL = MPAR_OFF + MPAR_FLOATS * 4;
+  static_assert(!MLP || HEADS == 1, "the MLP folds into one-head blocks");
   static_assert(TOTAL * CTAS <= 220 * 1024, "window block shared memory");
 };
 
-template <int HEADS>
-__global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSmem<HEADS>::CTAS)
+template <int HEADS, bool MLP>
+__global__ void __launch_bounds__(WindowBlockSmem<HEADS, MLP>::THREADS, WindowBlockSmem<HEADS, MLP>::CTAS)
     window_block_kernel(const WindowBlockArgs a) {
-  using L = WindowBlockSmem<HEADS>;
+  using L = WindowBlockSmem<HEADS, MLP>;
   constexpr int C = L::C, NQ = L::NQ, G = C / 8;  // G: channel groups (planes)
   extern __shared__ __align__(128) uint8_t wb_smem[];
   __half* sw = reinterpret_cast<__half*>(wb_smem + L::WQ_OFF);
@@ -281,6 +291,13 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSm
     uint4* dst = reinterpret_cast<uint4*>(wb_smem + L::WQ_OFF);
     for (int i = (int)threadIdx.x; i < (L::WQ_BYTES + L::WP_BYTES) / 16; i += L::THREADS) dst[i] = __ldg(src + i);
     for (int i = (int)threadIdx.x; i < L::PAR_FLOATS; i += L::THREADS) spar[i] = __ldg(a.params + i);
+    if constexpr (MLP) {
+      const uint4* msrc = reinterpret_cast<const uint4*>(a.mlp_w);
+      uint4* mdst = reinterpret_cast<uint4*>(wb_smem + L::MW_OFF);
+      for (int i = (int)threadIdx.x; i < L::MW_BYTES / 16; i += L::THREADS) mdst[i] = __ldg(msrc + i);
+      float* mpar = reinterpret_cast<float*>(wb_smem + L::MPAR_OFF);
+      for (int i = (int)threadIdx.x; i < L::MPAR_FLOATS; i += L::THREADS) mpar[i] = __ldg(a.mlp_params + i);
+    }
   }
   __syncthreads();
   griddep_wait();
@@ -490,18 +507,132 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS>::THREADS, WindowBlockSm
         project(kk, a0, a1, a2, a3);
       }
     }
-    // rows g and g + 8 of the warp's 16: + bias + the raw row, to the pixel
+    if constexpr (MLP) {
+      // The block's MLP on the warp's 16 rows (swin.rs:222-254), all in
+      // registers: the rows after the attention, rounded to f16 as the
+      // separate launches store them; LN2 over each row's 32 channels (the
+      // four lanes of a quad); fc1 in four chunks of 32 hidden columns,
+      // + b1, GELU, f16, which are the A fragments of fc2's k steps; fc2
+      // accumulated; + b2 + the rows, stored to the pixels. Rounded where
+      // mlp_sm100 rounds (normalised rows, hidden layer, sums).
+      const __half* mw1 = reinterpret_cast<const __half*>(wb_smem + L::MW_OFF);
+      const __half* mw2 = mw1 + 4 * 128 * 8;
+      const float* mpar = reinterpret_cast<const float*>(wb_smem + L::MPAR_OFF);
+      const float *g2 = mpar, *be2 = mpar + 32, *b1 = mpar + 64, *b2 = mpar + 192;
+      float ya[4][4];
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int tk = q0 + g + 8 * h;
-      const long long dest = pixel(oy, ox, t_out[h]);
-      if (dest < 0) continue;
+      for (int h = 0; h < 2; h++) {
+        const int tk = q0 + g + 8 * h;
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int grp = 4 * hd + j, n = 8 * grp + 2 * t;
-        const float2 old = __half22float2(*reinterpret_cast<const __half2*>(sraw + (grp * TOK + tk) * 8 + 2 * t));
-        *reinterpret_cast<__half2*>(a.y + (a.plane0 + grp) * a.y_plane + dest * 8 + 2 * t) =
-            __floats2half2_rn((pr[j][2 * h] + bproj[n]) + old.x, (pr[j][2 * h + 1] + bproj[n + 1]) + old.y);
+        for (int j = 0; j < 4; j++) {
+          const int n = 8 * j + 2 * t;
+          const float2 old = __half22float2(*reinterpret_cast<const __half2*>(sraw + (j * TOK + tk) * 8 + 2 * t));
+          const float2 r = __half22float2(
+              __floats2half2_rn((pr[j][2 * h] + bproj[n]) + old.x, (pr[j][2 * h + 1] + bproj[n + 1]) + old.y));
+          ya[j][2 * h] = r.x;
+          ya[j][2 * h + 1] = r.y;
+        }
+      }
+      // LN2 (mlp_sm100's formula: mean, the mean squared deviation) of rows g
+      // (h 0) and g + 8 (h 1)
+      float mean[2], inv2[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; j++) sum += ya[j][2 * h] + ya[j][2 * h + 1];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        mean[h] = sum / 32.0f;
+        float var = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          var += (ya[j][2 * h] - mean[h]) * (ya[j][2 * h] - mean[h]) +
+                 (ya[j][2 * h + 1] - mean[h]) * (ya[j][2 * h + 1] - mean[h]);
+        var += __shfl_xor_sync(0xffffffffu, var, 1);
+        var += __shfl_xor_sync(0xffffffffu, var, 2);
+        inv2[h] = 1.0f / sqrtf(var / 32.0f + 1e-5f);
+      }
+      auto norm2 = [&](int j, int h) -> uint32_t {
+        const int n = 8 * j + 2 * t;
+        return pack_half2((ya[j][2 * h] - mean[h]) * inv2[h] * g2[n] + be2[n],
+                          (ya[j][2 * h + 1] - mean[h]) * inv2[h] * g2[n + 1] + be2[n + 1]);
+      };
+      uint32_t la[2][4];
+#pragma unroll
+      for (int kk = 0; kk < 2; kk++) {
+        la[kk][0] = norm2(2 * kk, 0);
+        la[kk][1] = norm2(2 * kk, 1);
+        la[kk][2] = norm2(2 * kk + 1, 0);
+        la[kk][3] = norm2(2 * kk + 1, 1);
+      }
+      float p2[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) p2[j][0] = p2[j][1] = p2[j][2] = p2[j][3] = 0.0f;
+#pragma unroll 1
+      for (int hc = 0; hc < 4; hc++) {
+        float a1[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) a1[j][0] = a1[j][1] = a1[j][2] = a1[j][3] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 2; kk++)
+#pragma unroll
+          for (int jj = 0; jj < 4; jj += 2) {
+            uint32_t b0, b1r, b2r, b3;
+            const int n = 8 * (4 * hc + jj) + (lane & 7) + ((lane >> 4) << 3);
+            const int grp = kk * 2 + ((lane >> 3) & 1);
+            ldsm_x4((uint32_t)__cvta_generic_to_shared(mw1 + grp * 128 * 8 + n * 8), b0, b1r, b2r, b3);
+            mma16816(a1[jj], la[kk][0], la[kk][1], la[kk][2], la[kk][3], b0, b1r);
+            mma16816(a1[jj + 1], la[kk][0], la[kk][1], la[kk][2], la[kk][3], b2r, b3);
+          }
+        uint32_t hv[4][2];
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const float2 bb = *reinterpret_cast<const float2*>(b1 + 32 * hc + 8 * jj + 2 * t);
+          const float2 h0 = gemm_gelu2(fadd2(make_float2(a1[jj][0], a1[jj][1]), bb));
+          const float2 h1 = gemm_gelu2(fadd2(make_float2(a1[jj][2], a1[jj][3]), bb));
+          hv[jj][0] = pack_half2(h0.x, h0.y);
+          hv[jj][1] = pack_half2(h1.x, h1.y);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 2; kk++) {
+          const int ks = 2 * hc + kk;  // fc2's k step (hidden 16 ks ..)
+#pragma unroll
+          for (int j = 0; j < 4; j += 2) {
+            uint32_t b0, b1r, b2r, b3;
+            const int n = 8 * j + (lane & 7) + ((lane >> 4) << 3);
+            const int grp = ks * 2 + ((lane >> 3) & 1);
+            ldsm_x4((uint32_t)__cvta_generic_to_shared(mw2 + grp * 32 * 8 + n * 8), b0, b1r, b2r, b3);
+            mma16816(p2[j], hv[2 * kk][0], hv[2 * kk][1], hv[2 * kk + 1][0], hv[2 * kk + 1][1], b0, b1r);
+            mma16816(p2[j + 1], hv[2 * kk][0], hv[2 * kk][1], hv[2 * kk + 1][0], hv[2 * kk + 1][1], b2r, b3);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const long long dest = pixel(oy, ox, t_out[h]);
+        if (dest < 0) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int n = 8 * j + 2 * t;
+          *reinterpret_cast<__half2*>(a.y + (a.plane0 + j) * a.y_plane + dest * 8 + 2 * t) =
+              __floats2half2_rn((p2[j][2 * h] + b2[n]) + ya[j][2 * h], (p2[j][2 * h + 1] + b2[n + 1]) + ya[j][2 * h + 1]);
+        }
+      }
+    } else {
+      // rows g and g + 8 of the warp's 16: + bias + the raw row, to the pixel
+  #pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int tk = q0 + g + 8 * h;
+        const long long dest = pixel(oy, ox, t_out[h]);
+        if (dest < 0) continue;
+  #pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int grp = 4 * hd + j, n = 8 * grp + 2 * t;
+          const float2 old = __half22float2(*reinterpret_cast<const __half2*>(sraw + (grp * TOK + tk) * 8 + 2 * t));
+          *reinterpret_cast<__half2*>(a.y + (a.plane0 + grp) * a.y_plane + dest * 8 + 2 * t) =
+              __floats2half2_rn((pr[j][2 * h] + bproj[n]) + old.x, (pr[j][2 * h + 1] + bproj[n + 1]) + old.y);
+        }
       }
     }
 #pragma unroll
@@ -576,17 +707,44 @@ void pack_window_block(WindowBlockWeights& wb, int c, const std::vector<float>& 
   IEC_CUDA(cudaMemcpy(wb.params.get(), par.data(), par.size() * 4, cudaMemcpyHostToDevice));
 }
 
+void pack_window_block_mlp(WindowBlockWeights& wb, const std::vector<float>& w1, const std::vector<float>& b1,
+                           const std::vector<float>& w2, const std::vector<float>& b2, const std::vector<float>& gamma,
+                           const std::vector<float>& beta) {
+  const int c = wb.c, hid = 4 * c;
+  if (c != 32) throw Error(ERR_INPUT, "the MLP folds into one-head window blocks only");
+  if (w1.size() != (size_t)c * hid || w2.size() != (size_t)hid * c || b1.size() != (size_t)hid ||
+      b2.size() != (size_t)c || gamma.size() != (size_t)c || beta.size() != (size_t)c)
+    throw Error(ERR_WEIGHTS, "window block MLP weights of the wrong size");
+  // W1 as [c / 8][4c][8], then W2 as [4c / 8][c][8]: B operands' core-matrix images
+  std::vector<uint16_t> w((size_t)2 * c * hid);
+  size_t at = 0;
+  for (int g = 0; g < c / 8; g++)
+    for (int n = 0; n < hid; n++)
+      for (int e = 0; e < 8; e++) w[at++] = f32_to_half(w1[(size_t)(8 * g + e) * hid + n]);
+  for (int g = 0; g < hid / 8; g++)
+    for (int n = 0; n < c; n++)
+      for (int e = 0; e < 8; e++) w[at++] = f32_to_half(w2[(size_t)(8 * g + e) * c + n]);
+  std::vector<float> par;
+  for (const std::vector<float>* v : {&gamma, &beta, &b1, &b2}) par.insert(par.end(), v->begin(), v->end());
+  wb.mlp_w.reserve(w.size() * 2);
+  wb.mlp_params.reserve(par.size() * 4);
+  IEC_CUDA(cudaMemcpy(wb.mlp_w.get(), w.data(), w.size() * 2, cudaMemcpyHostToDevice));
+  IEC_CUDA(cudaMemcpy(wb.mlp_params.get(), par.data(), par.size() * 4, cudaMemcpyHostToDevice));
+  wb.mlp = true;
+}
+
 namespace {
 
-template <int HEADS>
+template <int HEADS, bool MLP>
 void launch_window_block(int device, int sms, const WindowBlockArgs& a, cudaStream_t s) {
-  using L = WindowBlockSmem<HEADS>;
+  using L = WindowBlockSmem<HEADS, MLP>;
   static bool prepared[64] = {};
   if (!prepared[device & 63]) {
-    IEC_CUDA(cudaFuncSetAttribute(window_block_kernel<HEADS>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    IEC_CUDA(cudaFuncSetAttribute(window_block_kernel<HEADS, MLP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  L::TOTAL));
     prepared[device & 63] = true;
   }
-  launch_pdl(window_block_kernel<HEADS>, std::min(a.windows, sms * L::CTAS), L::THREADS, (size_t)L::TOTAL, s, a);
+  launch_pdl(window_block_kernel<HEADS, MLP>, std::min(a.windows, sms * L::CTAS), L::THREADS, (size_t)L::TOTAL, s, a);
   IEC_CUDA(cudaGetLastError());
 }
 
@@ -612,15 +770,23 @@ void window_block(Device& dev, const WindowBlockWeights& wb, const float* bias, 
   a.w = wb.w.as<uint8_t>();
   a.params = wb.params.as<float>();
   a.bias = bias;
+  if (wb.mlp) {
+    a.mlp_w = wb.mlp_w.as<uint8_t>();
+    a.mlp_params = wb.mlp_params.as<float>();
+  }
   const double heads = c / 32;
   char name[48];
-  snprintf(name, sizeof name, "window_block<%d>", c / 32);
-  // per window: qkv (64 x 3c x c), attention (2 x 64 x 64 x 32 per head) and
-  // the projection (64 x c x c); bytes: the tokens' rows read and written
-  timed_launch(name, (double)a.windows * (2.0 * 64 * 3 * c * c + heads * 4.0 * 64 * 64 * 32 + 2.0 * 64 * c * c),
+  snprintf(name, sizeof name, wb.mlp ? "window_block<%d>+mlp" : "window_block<%d>", c / 32);
+  // per window: qkv (64 x 3c x c), attention (2 x 64 x 64 x 32 per head),
+  // the projection (64 x c x c) and with the MLP fc1 and fc2 (2 x 64 x c x
+  // 4c); bytes: the tokens' rows read and written
+  timed_launch(name,
+               (double)a.windows * (2.0 * 64 * 3 * c * c + heads * 4.0 * 64 * 64 * 32 + 2.0 * 64 * c * c +
+                                    (wb.mlp ? 4.0 * 64 * c * 4 * c : 0.0)),
                (double)a.windows * 64 * c * 2 * 2, s, [&] {
-                 if (c == 32) return launch_window_block<1>(dev.ordinal(), dev.sms(), a, s);
-                 return launch_window_block<2>(dev.ordinal(), dev.sms(), a, s);
+                 if (c == 32 && wb.mlp) return launch_window_block<1, true>(dev.ordinal(), dev.sms(), a, s);
+                 if (c == 32) return launch_window_block<1, false>(dev.ordinal(), dev.sms(), a, s);
+                 return launch_window_block<2, false>(dev.ordinal(), dev.sms(), a, s);
                });
 }
 

@@ -195,12 +195,19 @@ void window_attention(const __half* qkv, long long qkv_plane_elems, int c, int w
 struct WindowBlockWeights {
   int c = 0;
   DeviceBuffer w, params;
+  bool mlp = false;  // with one head: the block's MLP (LN2, fc1, GELU, fc2, residual) in the same kernel
+  DeviceBuffer mlp_w, mlp_params;
 };
 bool window_block_fits(int c);
 // wq: c x 3c (q, k, v columns), wp: c x c (row k, column n); biases, gamma, beta f32.
 void pack_window_block(WindowBlockWeights& wb, int c, const std::vector<float>& wq, const std::vector<float>& bq,
                        const std::vector<float>& wp, const std::vector<float>& bp, const std::vector<float>& gamma,
                        const std::vector<float>& beta);
+// The block's MLP folded in after the attention (c = 32 only): w1 c x 4c,
+// w2 4c x c (row k, column n); biases, gamma, beta (LN2, eps 1e-5) f32.
+void pack_window_block_mlp(WindowBlockWeights& wb, const std::vector<float>& w1, const std::vector<float>& b1,
+                           const std::vector<float>& w2, const std::vector<float>& b2, const std::vector<float>& gamma,
+                           const std::vector<float>& beta);
 void window_block(Device& dev, const WindowBlockWeights& wb, const float* bias, bool shifted, int rows_w, int cols_w,
                   __half* y, long long y_plane_elems, int plane0, const WindowMap& wm, cudaStream_t s);
 

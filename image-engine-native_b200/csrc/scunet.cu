@@ -226,6 +226,7 @@ Scunet::Scunet(const std::string& path, const Options& opt) : dev_(opt) {
       pack_weights(b.fc1, w1.values, 1, h, 4 * h, bb1.data());
       pack_weights(b.fc2, w2.values, 1, 4 * h, h, bb2.data());
       if (mlp_fits(h)) pack_mlp(b.mlp, h, w1.values, bb1, w2.values, bb2, g2, be2);
+      if (b.wblock.c == 32) pack_window_block_mlp(b.wblock, w1.values, bb1, w2.values, bb2, g2, be2);
     }
     linear(f, b.join, name + ".conv1_2", c, c, true, join);
   };
@@ -421,7 +422,9 @@ bool Scunet::run_region(const void* src, bool src_u8, void* dst, bool dst_u8, in
         gemm_rows(dev_, B.proj, att, pl, Pl, ACT_NONE, o, s);
       }
       // MLP (swin.rs:222-254): y[h:] += fc2(gelu(fc1(LN2(y[h:])))).
-      if (fused_mlp_ && B.mlp.c == h && mlp_preferred(h)) {
+      if (fused_mlp_ && B.wblock.c == h && B.wblock.mlp) {
+        // folded into the window block above
+      } else if (fused_mlp_ && B.mlp.c == h && mlp_preferred(h)) {
         mlp_planar(dev_, B.mlp, y + (long long)(h / 8) * pl, pl, Pl, s);
       } else {
         layer_norm_planar(y, pl, h / 8, Pl, h, B.ln2g.as<float>(), B.ln2b.as<float>(), ln2, pl, nullptr, s);
