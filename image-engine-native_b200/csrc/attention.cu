@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(WindowBlockSmem<HEADS, MLP>::THREADS, WindowBl
       float p2[4][4];
 #pragma unroll
       for (int j = 0; j < 4; j++) p2[j][0] = p2[j][1] = p2[j][2] = p2[j][3] = 0.0f;
-#pragma unroll 1
+#pragma unroll 2
       for (int hc = 0; hc < 4; hc++) {
         float a1[4][4];
 #pragma unroll

@@ -130,3 +130,43 @@ def test_joinsplit_matches_separate_launches_and_oracle(rows, c):
         want_y = refcpu.multiply(fx.ravel(), ws, bs, kind="rows").reshape(rows, c)
         close(fx, want_x)
         close(fy, want_y)
+
+
+@pytest.mark.parametrize("m,k,n,act,accumulate", [
+    (256, 4096, 64, 0, False), (304, 2048, 96, 2, False), (256, 4096, 32, 0, True), (640, 2048, 128, 1, False),
+])
+def test_split_k_rows_match_oracle(m, k, n, act, accumulate):
+    """Products with few row tiles and at least 32 K steps run their K steps
+    in slices on more CTAs; the CTA that completes a tile's last slice adds
+    the slices in order and applies the epilogue (bias, activation, the
+    accumulated output)."""
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(m + k + n + act)
+    a = f16(rng.standard_normal((m, k)))
+    w = f16(rng.standard_normal((k, n)) / np.sqrt(k))
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    old = f16(rng.standard_normal((m, n))) if accumulate else None
+    want = refcpu.multiply(a.ravel(), w, bias, kind="rows", act=act,
+                           out=None if old is None else old.ravel().copy(), accumulate=accumulate).reshape(m, n)
+    for _ in range(2):  # the tile counters are left at zero for the next launch
+        got = iec.selftest_gemm(a, w, bias, act=act, accumulate_onto=old)
+        close(got, want)
+
+
+def test_split_k_conv_matches_oracle():
+    """A 3x3 convolution over 512 channels of a small map (72 K steps, few
+    tiles) through the split-K path."""
+    import iec
+    from oracle import refcpu
+
+    rng = np.random.default_rng(11)
+    h, w, k, n = 12, 20, 512, 128
+    a = f16(rng.standard_normal((h, w, k)))
+    wt = f16(rng.standard_normal((9 * k, n)) / np.sqrt(9 * k))
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    want = refcpu.multiply(a.ravel(), wt, bias, kind="conv", shape=(h, w, k), size=3, act=1).reshape(h * w, n)
+    for _ in range(2):
+        got = iec.selftest_gemm(a, wt, bias, conv=True, shape=(h, w), act=1)
+        close(got, want)
